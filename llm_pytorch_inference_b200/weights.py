@@ -1,0 +1,74 @@
+"""Canonical random-init weights with HuggingFace key names.
+
+Every Linear / Embedding weight is drawn N(0, 0.02) in sorted-key order from one
+seeded generator, in fp32, then cast; norm weights keep their constructor values
+(ones, or zeros for the (1+w) form, ``mini_vllm/models/model.py:10-17``).  The
+same seed therefore gives the same tensors to the oracle, the golden-fixture
+script and the CUDA path.  The reference's ``Embedding.reset_parameters``
+(``mini_vllm/ops/embedding.py:47``) uses the same N(0, 0.02) law.
+
+For the full-size benchmark the draw can run on the GPU instead (``device="cuda"``):
+same law, different values, no 33 GB fp32 staging on the host.
+"""
+from __future__ import annotations
+
+import torch
+
+from .configs import head_dim, num_kv_heads
+
+
+def weight_shapes(cfg: dict) -> dict[str, tuple[int, ...]]:
+    """HF key -> shape for a Llama/Qwen-family decoder (``model.py:120-424``)."""
+    H = cfg["hidden_size"]
+    hd = head_dim(cfg)
+    nq = cfg["num_attention_heads"]
+    nkv = num_kv_heads(cfg)
+    inter = cfg["intermediate_size"]
+    V = cfg["vocab_size"]
+    shapes: dict[str, tuple[int, ...]] = {"model.embed_tokens.weight": (V, H), "model.norm.weight": (H,)}
+    if not cfg.get("tie_word_embeddings", False):
+        shapes["lm_head.weight"] = (V, H)
+    for i in range(cfg["num_hidden_layers"]):
+        p = f"model.layers.{i}."
+        shapes[p + "self_attn.q_proj.weight"] = (nq * hd, H)
+        shapes[p + "self_attn.k_proj.weight"] = (nkv * hd, H)
+        shapes[p + "self_attn.v_proj.weight"] = (nkv * hd, H)
+        shapes[p + "self_attn.o_proj.weight"] = (H, nq * hd)
+        if cfg.get("_qk_norm", False):
+            shapes[p + "self_attn.q_norm.weight"] = (hd,)
+            shapes[p + "self_attn.k_norm.weight"] = (hd,)
+        shapes[p + "mlp.gate_proj.weight"] = (inter, H)
+        shapes[p + "mlp.up_proj.weight"] = (inter, H)
+        shapes[p + "mlp.down_proj.weight"] = (H, inter)
+        shapes[p + "input_layernorm.weight"] = (H,)
+        shapes[p + "post_attention_layernorm.weight"] = (H,)
+    return shapes
+
+
+def _is_norm(key: str) -> bool:
+    return key.endswith("norm.weight")
+
+
+def canonical_state_dict(cfg: dict, seed: int = 0, dtype: torch.dtype = torch.float32,
+                         device: str | torch.device = "cpu") -> dict[str, torch.Tensor]:
+    """Seeded random-init state dict (sorted keys, N(0, 0.02), norms at ones)."""
+    plus_one = cfg.get("_rms_norm_plus_one", False)
+    shapes = weight_shapes(cfg)
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    out: dict[str, torch.Tensor] = {}
+    for key in sorted(shapes):
+        shape = shapes[key]
+        if _is_norm(key):
+            t = torch.zeros(shape, device=dev) if plus_one else torch.ones(shape, device=dev)
+            out[key] = t.to(dtype)
+        elif dev.type == "cpu":
+            t = torch.empty(shape, dtype=torch.float32)
+            t.normal_(0.0, 0.02, generator=gen)
+            out[key] = t.to(dtype)
+        else:
+            # GPU draw straight into the target dtype: avoids an fp32 copy of 8B params.
+            t = torch.empty(shape, dtype=dtype, device=dev)
+            t.normal_(0.0, 0.02, generator=gen)
+            out[key] = t
+    return out

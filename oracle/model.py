@@ -1,0 +1,224 @@
+"""Oracle restatement of the reference's decoder math (pure PyTorch, CPU).
+
+Follows ``mini_vllm/models/model.py`` (the PyTorch-path model the reference runs
+with ``MINI_VLLM_BACKEND=pytorch``) operation by operation, in the same dtype and
+with the same intermediate roundings, so that the CUDA path can be compared with
+it at bf16 tolerance and its KV-cache indexing bit for bit.
+
+Weights come in as an HF-keyed state dict; ``gate_proj``/``up_proj`` stay separate
+as in ``model.py:106-117``.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+
+# ----------------------------------------------------------------- primitives
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, plus_one: bool = False) -> torch.Tensor:
+    """RMSNorm as ``model.py:19-25``: variance in fp32, then ``(w * x_hat)`` cast back."""
+    orig = x.dtype
+    var = x.float().pow(2).mean(-1, keepdim=True)
+    xh = x * torch.rsqrt(var + eps)
+    if plus_one:
+        return (xh * (1.0 + w.float())).to(orig)
+    return (w * xh).to(orig)
+
+
+def ops_rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """The ops-API fallback ``ops/rmsnorm.py:12-20``: ``(w * x)`` rounds to the input dtype first."""
+    w = w if w.dtype == x.dtype else w.to(x.dtype)
+    var = x.float().pow(2).mean(-1, keepdim=True)
+    return (w * x * torch.rsqrt(var + eps)).to(x.dtype)
+
+
+def ops_rmsnorm_plus_one(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """``ops/rmsnorm.py:23-31``."""
+    w = w if w.dtype == x.dtype else w.to(x.dtype)
+    var = x.float().pow(2).mean(-1, keepdim=True)
+    return ((1.0 + w.float()) * (x * torch.rsqrt(var + eps))).to(x.dtype)
+
+
+def ops_fused_add_rmsnorm(residual, x, w, eps, plus_one=False):
+    """``ops/rmsnorm.py:34-53``: returns ``(out, residual + x)``.
+
+    The plus-one variant associates as ``((1 + w) * r) * rsqrt`` (``:51``), unlike
+    the unfused ``rmsnorm_plus_one``.
+    """
+    r = residual + x
+    if not plus_one:
+        return ops_rmsnorm(r, w, eps), r
+    w = w if w.dtype == x.dtype else w.to(x.dtype)
+    var = r.float().pow(2).mean(-1, keepdim=True)
+    return ((1.0 + w.float()) * r * torch.rsqrt(var + eps)).to(x.dtype), r
+
+
+def inv_freq(head_dim: int, theta: float) -> torch.Tensor:
+    """``model.py:31``: fp32 inverse frequencies (no rope_scaling for Qwen3/Llama-3 cfgs here)."""
+    return 1.0 / (theta ** (torch.arange(0, head_dim, 2).float() / head_dim))
+
+
+def rope_tables(head_dim: int, theta: float, length: int, dtype: torch.dtype,
+                device: str | torch.device = "cpu") -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin cache as ``RotaryEmbedding.forward`` builds it (``model.py:74-81``).
+
+    After ``model.to(dtype)`` (``loader.py:297``) the ``inv_freq`` buffer is in the
+    model dtype, and the position ramp is ``arange(..., dtype=inv_freq.dtype)``:
+    in bf16 the positions themselves are rounded (2049 -> 2048).  The table rows
+    depend only on the position, not on the grown cache length.
+    """
+    f = inv_freq(head_dim, theta).to(dtype).to(device)
+    t = torch.arange(length, device=device, dtype=f.dtype)
+    freqs = torch.outer(t, f)
+    emb = torch.cat((freqs, freqs), dim=-1)
+    return emb.cos(), emb.sin()
+
+
+def rotate_half(x: torch.Tensor) -> torch.Tensor:
+    """``model.py:94-97``."""
+    h = x.shape[-1] // 2
+    return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """``model.py:100-103``: ``x*cos + rotate_half(x)*sin`` in the tensors' dtype."""
+    return (x * cos) + (rotate_half(x) * sin)
+
+
+# ----------------------------------------------------------------------- model
+class OracleDecoder:
+    """The reference's ``ForCausalLM`` forward (``model.py:412-424``) over a paged KV pool.
+
+    ``kv_pool`` has the reference layout ``[L, 2, num_blocks, block_size, n_kv, head_dim]``
+    (``kv_cache.py:24-29``).
+    """
+
+    def __init__(self, cfg: dict, state_dict: dict[str, torch.Tensor], dtype: torch.dtype,
+                 device: str | torch.device = "cpu"):
+        self.cfg = cfg
+        self.dtype = dtype
+        self.device = torch.device(device)
+        self.L = cfg["num_hidden_layers"]
+        self.H = cfg["hidden_size"]
+        self.nq = cfg["num_attention_heads"]
+        self.nkv = cfg.get("num_key_value_heads", self.nq)
+        self.hd = cfg.get("head_dim", self.H // self.nq)
+        self.eps = cfg.get("rms_norm_eps", 1e-6)
+        self.theta = cfg.get("rope_theta", 10000.0)
+        self.qk_norm = cfg.get("_qk_norm", False)
+        self.plus_one = cfg.get("_rms_norm_plus_one", False)
+        self.scale = cfg.get("query_pre_attn_scalar") or self.hd    # model.py:139
+        act = cfg.get("hidden_act", "silu")
+        self.act = {"silu": F.silu, "gelu": F.gelu, "gelu_new": lambda t: F.gelu(t, approximate="tanh"),
+                    "relu": F.relu}[act]                                  # model.py:85-90
+        self.w = {k: v.to(device=self.device, dtype=dtype) for k, v in state_dict.items()}
+        if "lm_head.weight" not in self.w:                                # tied (model.py:417-418)
+            self.w["lm_head.weight"] = self.w["model.embed_tokens.weight"]
+        self._cos = self._sin = None
+        self._cache_len = 0
+
+    # model.py:60-81 -- grow like the reference: max(seq_len, 2*cache_len, 256)
+    def rope(self, positions: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        seq_len = int(positions.max().item()) + 1
+        if self._cos is None or self._cache_len < seq_len:
+            grow_to = max(seq_len, self._cache_len * 2, 256)
+            self._cos, self._sin = rope_tables(self.hd, self.theta, grow_to, self.dtype, self.device)
+            self._cache_len = grow_to
+        return self._cos[:seq_len], self._sin[:seq_len]
+
+    # model.py:226-243
+    @staticmethod
+    def write_kv(kv_pool, k, v, block_tables, slot_idx, layer):
+        bs = kv_pool.shape[3]
+        is_batch = isinstance(block_tables[0], list)
+        for i in range(k.shape[2]):
+            if is_batch:
+                for b in range(k.shape[0]):
+                    pos = slot_idx[b] + i
+                    blk = block_tables[b][pos // bs]
+                    kv_pool[layer, 0, blk, pos % bs] = k[b, :, i]
+                    kv_pool[layer, 1, blk, pos % bs] = v[b, :, i]
+            else:
+                pos = slot_idx + i
+                blk = block_tables[pos // bs]
+                kv_pool[layer, 0, blk, pos % bs] = k[0, :, i]
+                kv_pool[layer, 1, blk, pos % bs] = v[0, :, i]
+
+    # model.py:245-279
+    @staticmethod
+    def read_kv_batch(kv_pool, block_tables, layer, num_cached):
+        max_cached = max(n + 1 for n in num_cached)
+        ks, vs = [], []
+        for b, bt in enumerate(block_tables):
+            k = torch.cat([kv_pool[layer, 0, blk] for blk in bt], 0)[: num_cached[b] + 1]
+            v = torch.cat([kv_pool[layer, 1, blk] for blk in bt], 0)[: num_cached[b] + 1]
+            if k.shape[0] < max_cached:
+                pad = torch.zeros(max_cached - k.shape[0], *k.shape[1:], dtype=k.dtype, device=k.device)
+                k, v = torch.cat([k, pad]), torch.cat([v, pad])
+            ks.append(k)
+            vs.append(v)
+        return torch.stack(ks).transpose(1, 2), torch.stack(vs).transpose(1, 2)
+
+    def attention(self, i, x, cos, sin, kv_pool, block_tables, slot_idx, use_cache, num_cached, attn_mask):
+        """``Attention.forward`` (``model.py:154-224``)."""
+        w, p = self.w, f"model.layers.{i}.self_attn."
+        B, S, _ = x.shape
+        q = F.linear(x, w[p + "q_proj.weight"], w.get(p + "q_proj.bias")).view(B, S, self.nq, self.hd)
+        k = F.linear(x, w[p + "k_proj.weight"], w.get(p + "k_proj.bias")).view(B, S, self.nkv, self.hd)
+        v = F.linear(x, w[p + "v_proj.weight"], w.get(p + "v_proj.bias")).view(B, S, self.nkv, self.hd)
+        v = v.transpose(1, 2)
+        if self.qk_norm:
+            q = rms_norm(q, w[p + "q_norm.weight"], self.eps)
+            k = rms_norm(k, w[p + "k_norm.weight"], self.eps)
+        q, k = q.transpose(1, 2), k.transpose(1, 2)
+        q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+        if kv_pool is not None and block_tables is not None and slot_idx is not None:
+            self.write_kv(kv_pool, k, v, block_tables, slot_idx, i)
+            if use_cache:
+                k, v = self.read_kv_batch(kv_pool, block_tables, i, num_cached)
+        g = self.nq // self.nkv
+        if g > 1:
+            k = k.repeat_interleave(g, dim=1)
+            v = v.repeat_interleave(g, dim=1)
+        sc = 1.0 / math.sqrt(self.scale)
+        if attn_mask is not None:
+            o = F.scaled_dot_product_attention(q, k, v, scale=sc, attn_mask=attn_mask)
+        elif use_cache:
+            o = F.scaled_dot_product_attention(q, k, v, scale=sc)
+        else:
+            o = F.scaled_dot_product_attention(q, k, v, scale=sc, is_causal=True)
+        o = o.transpose(1, 2).contiguous().view(B, S, -1)
+        return F.linear(o, w[p + "o_proj.weight"], w.get(p + "o_proj.bias"))
+
+    def mlp(self, i, x):
+        """``MLP.forward`` (``model.py:116-117``): ``down(act(gate(x)) * up(x))``."""
+        w, p = self.w, f"model.layers.{i}.mlp."
+        return F.linear(self.act(F.linear(x, w[p + "gate_proj.weight"])) * F.linear(x, w[p + "up_proj.weight"]),
+                        w[p + "down_proj.weight"])
+
+    def forward(self, input_ids, positions, kv_pool=None, block_tables=None, slot_idx=None, use_cache=False,
+                num_cached=None, attn_mask=None, return_hidden=False):
+        """``ForCausalLM.forward`` -> logits ``[B, S, V]`` in the model dtype (``model.py:369-424``)."""
+        w = self.w
+        h = F.embedding(input_ids, w["model.embed_tokens.weight"])
+        cos, sin = self.rope(positions)
+        cos, sin = cos[positions], sin[positions]
+        if cos.dim() == 3:
+            cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
+        else:
+            cos, sin = cos.unsqueeze(0).unsqueeze(0), sin.unsqueeze(0).unsqueeze(0)
+        for i in range(self.L):
+            p = f"model.layers.{i}."
+            r = h
+            h = rms_norm(h, w[p + "input_layernorm.weight"], self.eps, self.plus_one)
+            h = self.attention(i, h, cos, sin, kv_pool, block_tables, slot_idx, use_cache, num_cached, attn_mask)
+            h = r + h
+            r = h
+            h = rms_norm(h, w[p + "post_attention_layernorm.weight"], self.eps, self.plus_one)
+            h = self.mlp(i, h)
+            h = r + h
+        h = rms_norm(h, w["model.norm.weight"], self.eps, self.plus_one)
+        logits = F.linear(h, w["lm_head.weight"])
+        return (logits, h) if return_hidden else logits

@@ -1,0 +1,123 @@
+"""Pin the CPU oracle to fixtures the reference itself produced (tests/golden/make_golden.py)."""
+import json
+import random
+
+import numpy as np
+import pytest
+import torch
+
+from llm_pytorch_inference_b200.configs import get_config
+from llm_pytorch_inference_b200.weights import canonical_state_dict
+from oracle import model as om
+from oracle import sampling as osamp
+from oracle.engine import BlockManager, OracleEngine
+
+
+@pytest.fixture(scope="module")
+def ops(golden_dir):
+    return torch.load(golden_dir / "ops_golden.pt")
+
+
+@pytest.mark.parametrize("tag", ["bf16", "f32"])
+def test_rmsnorm_family(ops, tag):
+    x, w, res = ops[f"rms_x_{tag}"], ops[f"rms_w_{tag}"], ops[f"rms_res_{tag}"]
+    assert torch.equal(om.ops_rmsnorm(x, w, 1e-6), ops[f"rmsnorm_{tag}"])
+    assert torch.equal(om.ops_rmsnorm_plus_one(x, w, 1e-6), ops[f"rmsnorm_p1_{tag}"])
+    y, r = om.ops_fused_add_rmsnorm(res, x, w, 1e-6)
+    assert torch.equal(r, ops[f"fadd_r_{tag}"]) and torch.equal(y, ops[f"fadd_y_{tag}"])
+    y, r = om.ops_fused_add_rmsnorm(res, x, w, 1e-6, plus_one=True)
+    assert torch.equal(r, ops[f"fadd_p1_r_{tag}"]) and torch.equal(y, ops[f"fadd_p1_y_{tag}"])
+
+
+def test_rope_tables_and_apply(ops):
+    n = int(ops["rope_table_len"])
+    cos, sin = om.rope_tables(128, 1000000.0, n, torch.bfloat16)
+    rows = ops["rope_table_rows"]
+    assert torch.equal(cos[rows], ops["rope_cos_rows"])
+    assert torch.equal(sin[rows], ops["rope_sin_rows"])
+    pos = ops["rope_positions"]
+    c, s = cos[pos].unsqueeze(1), sin[pos].unsqueeze(1)
+    assert torch.equal(om.apply_rope(ops["rope_q"], c, s), ops["rope_q_out"])
+    assert torch.equal(om.apply_rope(ops["rope_k"], c, s), ops["rope_k_out"])
+    # The bf16 position ramp rounds positions: 2049 -> 2048, 2300 -> 2304 (model.py:75).
+    assert torch.equal(cos[2049], cos[2048]) and torch.equal(cos[2300], cos[2304])
+
+
+def test_table_rows_independent_of_length():
+    a, _ = om.rope_tables(128, 1e6, 256, torch.bfloat16)
+    b, _ = om.rope_tables(128, 1e6, 8192, torch.bfloat16)
+    assert torch.equal(a, b[:256])
+
+
+def test_sampling_filters(ops):
+    logits = ops["samp_logits_bf16"].float()
+    assert torch.equal(osamp.greedy(logits), ops["greedy"])
+    assert int(osamp.greedy(logits)[2]) == 10  # first of the tied maxima
+    for k, p in ((50, 0.95), (50, 1.0), (0, 0.9), (1, 1.0), (5, 0.5)):
+        kept = torch.isfinite(osamp.top_k_top_p_filter(logits, k, p)).numpy()
+        bits = ops[f"filter_k{k}_p{int(p * 100)}_kept_bits"].numpy()
+        assert np.array_equal(np.packbits(kept, axis=-1), bits), (k, p)
+        # The stable (kernel) tie rule keeps the same number of tokens with the same values.
+        ks = torch.isfinite(osamp.top_k_top_p_filter(logits, k, p, stable=True))
+        for r in range(logits.shape[0]):
+            assert torch.equal(torch.sort(logits[r][ks[r]])[0], torch.sort(logits[r][torch.from_numpy(kept[r])])[0])
+    probs = osamp.tempered_probs(osamp.top_k_top_p_filter(logits, 50, 0.95), 0.8)
+    for r in range(logits.shape[0]):
+        idx = ops[f"probs_t08_k50_p95_row{r}_idx"]
+        assert torch.equal(probs[r].nonzero()[:, 0], idx)
+        torch.testing.assert_close(probs[r, idx], ops[f"probs_t08_k50_p95_row{r}_val"], rtol=1e-6, atol=0)
+
+
+def test_philox_known_answers():
+    # Random123 known-answer vectors for philox4x32 with 10 rounds.
+    assert osamp.philox4x32_10((0, 0, 0, 0), (0, 0)) == (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)
+    assert osamp.philox4x32_10((0xFFFFFFFF,) * 4, (0xFFFFFFFF,) * 2) == (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)
+    assert osamp.philox4x32_10((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0)) == \
+        (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1)
+
+
+def test_block_manager_trace(golden_dir):
+    tr = json.loads((golden_dir / "kv_golden.json").read_text())["shuffled_pool"]
+    bm = BlockManager(64, 16, tr["order"])
+    for ev in tr["log"]:
+        if ev[0] == "allocate":
+            assert bm.allocate(ev[1], ev[2]) == ev[3]
+        elif ev[0] == "append":
+            assert bm.append_token(ev[1]) == ev[2]
+            assert bm.get_block_table(ev[1]) == ev[3]
+        elif ev[0] == "free":
+            bm.free(ev[1])
+            assert list(bm.free_blocks) == ev[2]
+    assert list(bm.free_blocks) == tr["free_end"]
+
+
+def _engine_for(fx, dtype):
+    cfg = get_config(fx["arch"])
+    order = list(range(256))
+    random.Random(0).shuffle(order)
+    return OracleEngine(cfg, canonical_state_dict(cfg, 0, torch.float32), dtype, 256, 16, order)
+
+
+def test_decode_tiny_bf16_matches_reference(golden_dir):
+    fx = torch.load(golden_dir / "decode_tiny_bf16.pt")
+    eng = _engine_for(fx, torch.bfloat16)
+    prompts = [p.tolist() for p in fx["prompts"]]
+    out, step_logits = eng.generate_greedy(prompts, 24)
+    assert torch.equal(torch.tensor(out), fx["output_tokens"])
+    L = torch.stack(step_logits)
+    assert torch.equal(L.to(torch.bfloat16), fx["decode_logits"])
+
+
+@pytest.mark.slow
+def test_decode_cfg1_fp32_matches_reference(golden_dir):
+    fx = torch.load(golden_dir / "decode_cfg1.pt")
+    eng = _engine_for(fx, torch.float32)
+    prompts = [p.tolist() for p in fx["prompts"]]
+    out, step_logits = eng.generate_greedy(prompts, 64)
+    assert torch.equal(torch.tensor(out), fx["output_tokens"])
+    L = torch.stack(step_logits)
+    torch.testing.assert_close(torch.topk(L, 16, dim=-1).values, fx["decode_logits_top"], rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(L.double().sum(-1), fx["decode_logits_sum"], rtol=1e-6, atol=1e-3)
+    bts = json.loads(fx["decode_block_tables"])
+    # Block tables at the last decode step are bit-exact (FIFO allocation from the shuffled pool).
+    assert [eng.blocks.get_block_table(s) for s in range(4)] == bts[-1]
