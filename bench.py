@@ -1,0 +1,386 @@
+"""Decode throughput of the Qwen3-8B-architecture workload on the B200 decode path.
+
+Workload (one decode step = one new token for each of 64 sequences):
+  Qwen3-8B architecture (36 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128,
+  SwiGLU 12288, vocab 151936, QK-norm, RoPE theta 1e6), random-init bf16 weights,
+  batch 64, prompts of 2048 tokens whose K/V are pre-filled with seeded random values
+  in a shuffled paged pool (block 16, pool sized to the 180 GB per-GPU budget),
+  sampling T=0.8 / top-k 50 / top-p 0.95.
+
+Reported (one JSON line from rank 0):
+  value     tokens/s of the whole job: K graph replays of the full step (forward + sampling),
+            the per-step metadata already resident in HBM, CUDA events on the launching stream,
+            max over ranks.  Weights (15.1 GB) + KV (~20 GB) per step >> L2 (126 MB).
+  e2e       the same through DecodeEngine.step(): per step one host->device copy of the
+            step's metadata from pinned memory and one device->host read of the 64 sampled tokens.
+  roofline  the kernel with the largest share of the step, its algorithmic bytes / average
+            launch duration (CUDA events, launching stream) against the measured HBM peak.
+  cpu_baseline  the oracle (the reference's PyTorch decode path restated on the CPU) on this
+            host's cores, on a bounded sample of the same step, extrapolated to 36 layers.
+
+--impl reference runs only that CPU path (rank 0), as the reference arm.
+--gpus N (under torchrun): N independent replicas of the workload, one per GPU (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import random
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "decode tokens/s Qwen3-8B-arch bf16 at TP=1/2/4/8; paged-attn HBM GB/s % peak"
+ARCH = "qwen3-8b"
+BATCH = 64
+PROMPT = 2048
+SAMPLING = (0.8, 50, 0.95)
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--layers", type=int, default=None, help="override layer count (debug only; invalid bench)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--pdl", type=int, default=1)
+    return ap.parse_args(argv)
+
+
+# ------------------------------------------------------------------ distributed
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ----------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clock / throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"mvb_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "100"], stdout=self.fh,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.fh.close()
+        rows = [r.split(",") for r in self.path.read_text().strip().splitlines() if r.count(",") >= 8]
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        mx = max(float(r[2]) for r in rows)
+        under = [s for s in sm if s > 0.5 * mx] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(under), "sm_max_mhz": mx, "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows)}
+
+
+def peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def ncu_traffic() -> dict:
+    """Per-launch DRAM bytes from committed ncu summaries (lines 'traffic <kernel> <bytes>')."""
+    out = {}
+    for f in (REPO / "profiles").glob("*.md"):
+        for line in f.read_text().splitlines():
+            parts = line.strip().strip("|").split("|") if "|" in line else line.split()
+            parts = [p.strip() for p in parts]
+            if len(parts) >= 3 and parts[0] == "traffic":
+                try:
+                    out[parts[1]] = float(parts[2])
+                except ValueError:
+                    pass
+    return out
+
+
+# -------------------------------------------------------------------- CPU oracle
+def cpu_baseline(warmup: int = 1, steps: int = 1) -> dict:
+    """The oracle's decode step (the reference's PyTorch path restated, CPU, bf16) at batch 64 and
+    context 2048 through 1 and 2 Qwen3-8B layers + final norm + lm_head + sampling; the per-layer
+    and fixed costs are separated and extrapolated to 36 layers."""
+    from llm_pytorch_inference_b200.configs import get_config
+    from oracle import sampling as osamp
+    from oracle.model import OracleDecoder
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    times = {}
+    base_cfg = get_config(ARCH)
+    V, H = base_cfg["vocab_size"], base_cfg["hidden_size"]
+    shared = {
+        "model.embed_tokens.weight": torch.empty(V, H, dtype=torch.bfloat16).normal_(0, 0.02, generator=g),
+        "lm_head.weight": torch.empty(V, H, dtype=torch.bfloat16).normal_(0, 0.02, generator=g),
+        "model.norm.weight": torch.ones(H, dtype=torch.bfloat16),
+    }
+    nblk = (PROMPT + 16) // 16 + 1
+    for L in (1, 2):
+        cfg = get_config(ARCH, num_hidden_layers=L)
+        sd = dict(shared)
+        for i in range(L):
+            p = f"model.layers.{i}."
+            for k, shp in (("self_attn.q_proj.weight", (4096, 4096)), ("self_attn.k_proj.weight", (1024, 4096)),
+                           ("self_attn.v_proj.weight", (1024, 4096)), ("self_attn.o_proj.weight", (4096, 4096)),
+                           ("mlp.gate_proj.weight", (12288, 4096)), ("mlp.up_proj.weight", (12288, 4096)),
+                           ("mlp.down_proj.weight", (4096, 12288))):
+                sd[p + k] = torch.empty(shp, dtype=torch.bfloat16).normal_(0, 0.02, generator=g)
+            for k in ("self_attn.q_norm.weight", "self_attn.k_norm.weight"):
+                sd[p + k] = torch.ones(128, dtype=torch.bfloat16)
+            for k in ("input_layernorm.weight", "post_attention_layernorm.weight"):
+                sd[p + k] = torch.ones(H, dtype=torch.bfloat16)
+        model = OracleDecoder(cfg, sd, torch.bfloat16)
+        pool = torch.empty(L, 2, BATCH * nblk, 16, 8, 128, dtype=torch.bfloat16).normal_(0, 1, generator=g)
+        bts = [list(range(b * nblk, (b + 1) * nblk)) for b in range(BATCH)]
+        ids = torch.randint(0, V, (BATCH, 1), generator=g)
+        pos = [PROMPT] * BATCH
+        mask = torch.zeros(BATCH, 1, 1, PROMPT + 1, dtype=torch.bfloat16)
+        samples = []
+        for it in range(warmup + steps):
+            t0 = time.perf_counter()
+            with torch.no_grad(), torch.autocast("cpu", dtype=torch.bfloat16):
+                logits = model.forward(ids, torch.tensor(pos).view(BATCH, 1), pool, bts, pos, use_cache=True,
+                                       num_cached=pos, attn_mask=mask)[:, -1].float()
+            for b in range(BATCH):
+                osamp.sample_row(logits[b], *SAMPLING, seed=0, row=b, offset=it)
+            if it >= warmup:
+                samples.append(time.perf_counter() - t0)
+        times[L] = min(samples)
+        del model, pool, sd
+    per_layer = max(times[2] - times[1], 0.0)
+    fixed = max(times[1] - per_layer, 0.0)
+    step_s = fixed + 36 * per_layer
+    return {"value": BATCH / step_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": (f"one batch-{BATCH} decode step at context {PROMPT} through 1 and 2 Qwen3-8B layers + norm + "
+                       f"lm_head + T/top-k/top-p sampling (oracle, bf16, CPU); per-layer {per_layer:.3f} s, fixed "
+                       f"{fixed:.3f} s, extrapolated to 36 layers = {step_s:.2f} s/step"),
+            "cpu_model": _cpu_model()}
+
+
+def _cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    vals = []
+    last = None
+    for it in range(args.warmup + args.steps):
+        last = cpu_baseline(warmup=0, steps=1)
+        if it >= args.warmup:
+            vals.append(last["value"])
+    v = statistics.median(vals) if vals else last["value"]
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": BATCH / v * 1000.0, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{ARCH} decode, batch {BATCH}, context {PROMPT}", "model": ARCH,
+                       "global_batch": BATCH, "seq_len": PROMPT, "parallelism": "cpu"},
+            "cpu_baseline": {k: last[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- GPU path
+def run_gpu(args, rank: int, world: int, local: int) -> None:
+    from llm_pytorch_inference_b200 import _native as N
+    from llm_pytorch_inference_b200.configs import get_config
+    from llm_pytorch_inference_b200.engine import DecodeEngine
+    from llm_pytorch_inference_b200.weights import canonical_state_dict
+
+    dev = torch.device("cuda", local)
+    N.set_pdl(bool(args.pdl))
+    overrides = {} if args.layers is None else {"num_hidden_layers": args.layers}
+    cfg = get_config(ARCH, **overrides)
+    sd = canonical_state_dict(cfg, seed=rank, dtype=torch.bfloat16, device=dev)
+    W, K = args.warmup, args.steps
+    max_len = PROMPT + 1 + W + 2 * K + 16
+    free_order_seed = 0
+    eng = DecodeEngine(cfg, sd, max_batch=BATCH, max_model_len=max_len, device=dev)
+    del sd
+    order = list(range(eng.kv.num_blocks))
+    random.Random(free_order_seed).shuffle(order)
+    from collections import deque
+
+    eng.kv.free_blocks = deque(order)
+    g = torch.Generator().manual_seed(1 + rank)
+    for s in range(BATCH):
+        eng.add_sequence(s, torch.randint(0, cfg["vocab_size"], (PROMPT,), generator=g).tolist())
+        eng.append_first_token(s, int(torch.randint(0, cfg["vocab_size"], (1,), generator=g)))
+    eng.prefill_synthetic(seed=rank)
+    eng.set_sampling(*SAMPLING, seed=1234)
+    eng.prepare_first_step()
+    r = eng.runner
+    stream = torch.cuda.current_stream(dev)
+
+    # warm-up through the public API (captures the graph on the first call)
+    for _ in range(W):
+        eng.step()
+    torch.cuda.synchronize(dev)
+
+    # ---- value: K replays with each step's metadata already in HBM
+    metas = torch.stack([eng.plan_step(eng.runner.tokens_host[:BATCH].tolist()) for _ in range(K)]).to(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(K):
+        r.meta.copy_(metas[k], non_blocking=True)
+        r.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    dev_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    barrier(world)
+
+    # ---- e2e: K steps through DecodeEngine.step() (H2D metadata, replay, D2H tokens)
+    torch.cuda.synchronize(dev)
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(K):
+        eng.step()
+    e3.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e2.elapsed_time(e3), world)
+    clk = clocks.stop()
+    status = N.device_status(clear=True)
+
+    # ---- per-kernel timing for the roofline
+    kinds = r.time_kernels(iters=36 if cfg["num_hidden_layers"] >= 36 else cfg["num_hidden_layers"] * 4)
+    step_ms = dev_ms / K
+    for v in kinds.values():
+        v["share"] = v["avg_ms"] * v["launches_per_step"] / step_ms
+    top_name, top = max(kinds.items(), key=lambda kv: kv[1]["share"])
+    pk = peaks()
+    traffic = ncu_traffic().get(top_name)
+    achieved = top["bytes_per_launch"] / (top["avg_ms"] * 1e-3) / 1e9
+    roof = {"kernel": top_name, "bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": pk["source"],
+            "traffic": traffic, "algorithmic_bytes_per_launch": top["bytes_per_launch"],
+            "avg_launch_ms": round(top["avg_ms"], 5), "share_of_step": round(top["share"], 3)}
+    # whole-step roofline: algorithmic bytes of every launch in one step / step time
+    step_bytes = sum(v["bytes_per_launch"] * v["launches_per_step"] for v in kinds.values())
+    step_roof = {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (step_ms * 1e-3) / 1e9, 1),
+                 "frac": round(step_bytes / (step_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline()
+    if rank != 0:
+        return
+    h2d = r.meta_host.numel() * r.meta_host.element_size()
+    value = BATCH * world * K / (dev_ms * 1e-3)
+    e2e = BATCH * world * K / (e2e_ms * 1e-3)
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{ARCH} decode, batch {BATCH} per GPU, prompt {PROMPT}, T/top-k/top-p "
+                               f"{SAMPLING[0]}/{SAMPLING[1]}/{SAMPLING[2]}",
+                   "model": ARCH, "layers": cfg["num_hidden_layers"], "global_batch": BATCH * world,
+                   "seq_len": PROMPT, "context_during_timing": [PROMPT + 1 + W, PROMPT + 1 + W + 2 * K],
+                   "parallelism": f"replica{world}" if world > 1 else "tp1",
+                   "l2": "inputs larger than L2: 15.1 GB weights + ~20 GB KV read per step",
+                   "kv_pool_blocks": eng.kv.num_blocks, "pdl": bool(args.pdl)},
+        "roofline": roof, "step_roofline": step_roof,
+        "kernels": {k: {"avg_us": round(v["avg_ms"] * 1e3, 2), "per_step": v["launches_per_step"],
+                        "share": round(v["share"], 3), "gbs": round(v["gbs"], 1)} for k, v in kinds.items()},
+        "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": BATCH * 8},
+        "gpu_launches": r.launches_per_step() * K,
+        "clocks": clk, "device_status": status,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    rank, world, local = (0, 1, 0)
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, rank, world)
+        return 0
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        run_gpu(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,199 @@
+/*
+ * mvb200.h -- C ABI of the B200 (sm_100a) mini_vllm decode-path kernels.
+ *
+ * Every entry point takes caller-owned device pointers, plain sizes and a
+ * cudaStream_t, launches on that stream, never allocates, never synchronises,
+ * and returns an int status (MVB_OK or an MVB_ERR_* code; the message is in
+ * mvb_last_error()).  Device-side conditions that a kernel detects instead of
+ * faulting (a bounded wait that gave up, a block id or position out of range)
+ * are ORed into a device status word read back with mvb_device_status().
+ *
+ * Reference interface replaced by each entry point: the torch dispatcher schema
+ * in csrc/bindings/ops_binding.cpp:10-26 (TORCH_LIBRARY(mini_vllm_ops)) and the
+ * host wrappers in csrc/kernels/<op>/<op>_kernel.cu, plus the model/engine code
+ * for the entry points that the reference implements in Python/cuBLAS.
+ *
+ * Layouts are row-major.  dtype codes: MVB_F32, MVB_F16, MVB_BF16.
+ */
+#ifndef MVB200_H_
+#define MVB200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* mvb_stream_t; /* == cudaStream_t */
+
+/* ---- status codes -------------------------------------------------------- */
+#define MVB_OK 0
+#define MVB_ERR_INVALID_ARG 1 /* a size, pointer, alignment or dtype the kernel does not take */
+#define MVB_ERR_UNSUPPORTED 2 /* a shape outside what this build was compiled for */
+#define MVB_ERR_CUDA 3        /* launch / runtime error (message names it) */
+#define MVB_ERR_DRIVER 4      /* driver entry point (tensor-map encoder) unavailable */
+
+/* ---- device status bits (mvb_device_status) ------------------------------ */
+#define MVB_DEV_WAIT_TIMEOUT 0x1u /* a bounded wait expired; the kernel unwound */
+#define MVB_DEV_BAD_BLOCK 0x2u    /* a block-table entry was outside [0, num_blocks) */
+#define MVB_DEV_BAD_POSITION 0x4u /* a position was outside its block table / table */
+#define MVB_DEV_BAD_TOKEN 0x8u    /* a token id was outside [0, vocab) */
+
+/* ---- dtype codes ---------------------------------------------------------- */
+#define MVB_F32 0
+#define MVB_F16 1
+#define MVB_BF16 2
+#define MVB_I32 3
+#define MVB_I64 4
+
+/* ---- activation codes (mlp_kernel.cu:12-13: 0 = silu, 1 = gelu) ---------- */
+#define MVB_ACT_SILU 0
+#define MVB_ACT_GELU_TANH 1
+
+/* ---- library / status ------------------------------------------------------ */
+const char* mvb_last_error(void);   /* message of the last failing call on this thread */
+int mvb_version(void);               /* ABI version */
+int mvb_num_sms(int device);         /* SM count of `device` (148 on B200) */
+/* Read (and with clear != 0, reset) the device status word of the current device.
+ * Synchronises `stream`.  *status receives the OR of MVB_DEV_* bits. */
+int mvb_device_status(unsigned int* status, int clear, mvb_stream_t stream);
+
+/* ---- RMSNorm family -------------------------------------------------------
+ * Replaces rmsnorm_forward / rmsnorm_plus_one_forward (ops_binding.cpp:11-12,
+ * rmsnorm_kernel.cu:153-185).  out/in: [rows, hidden], weight: [hidden].
+ * semantics: MVB_NORM_OPS reproduces the ops-API formula of ops/rmsnorm.py:12-31
+ * (w*x rounded to the dtype before the 1/rms scale); MVB_NORM_MODEL reproduces
+ * RMSNorm.forward of models/model.py:19-25 (x*(1/rms) in fp32, then w*, one rounding).
+ * in_stride / out_stride: elements between rows (>= hidden). */
+#define MVB_NORM_OPS 0
+#define MVB_NORM_MODEL 1
+int mvb_rmsnorm(void* out, int64_t out_stride, const void* in, int64_t in_stride, const void* weight, int64_t rows,
+                int64_t hidden, float eps, int plus_one, int semantics, int dtype, mvb_stream_t stream);
+
+/* Replaces fused_add_rmsnorm_forward / ..._plus_one_forward (ops_binding.cpp:13-14,
+ * rmsnorm_kernel.cu:187-223): residual += in (in place, rounded to the dtype);
+ * out = norm(residual).  Same `semantics` switch as mvb_rmsnorm
+ * (ops/rmsnorm.py:34-53 vs. the model's add-then-RMSNorm, model.py:319-322). */
+int mvb_fused_add_rmsnorm(void* out, void* residual, const void* in, const void* weight, int64_t rows,
+                          int64_t hidden, float eps, int plus_one, int semantics, int dtype, mvb_stream_t stream);
+
+/* ---- RoPE ------------------------------------------------------------------
+ * Replaces rotary_pos_emb_forward (ops_binding.cpp:15, rope_kernel.cu:44-61):
+ * NeoX rotate-half RoPE, out = x*cos + rotate_half(x)*sin, each product and the
+ * sum rounded to the dtype as the PyTorch path does (ops/rope.py:74-76).
+ * in/out/cos/sin: [rows, head_dim]. */
+int mvb_rotary_pos_emb(void* out, const void* in, const void* cos, const void* sin, int64_t rows,
+                       int64_t head_dim, int dtype, mvb_stream_t stream);
+
+/* ---- activations -------------------------------------------------------------
+ * silu_forward / gelu_forward (ops_binding.cpp:16-17, activation_kernel.cu:82-114),
+ * swiglu_forward / geglu_forward (:18-19, :116-146), fused_mlp_forward
+ * (:25, mlp_kernel.cu:61-93: out[r, j] = act(gate_up[r, j]) * gate_up[r, I + j]).
+ * gelu is the tanh approximation (ops/activation.py:28). */
+int mvb_activation(void* out, const void* in, int64_t n, int act, int dtype, mvb_stream_t stream);
+int mvb_gated_activation(void* out, const void* gate, const void* up, int64_t n, int act, int dtype,
+                         mvb_stream_t stream);
+int mvb_fused_mlp(void* out, const void* gate_up, int64_t rows, int64_t intermediate, int act, int dtype,
+                  mvb_stream_t stream);
+
+/* ---- embedding / softmax -------------------------------------------------------
+ * embedding_forward (ops_binding.cpp:23, embedding_kernel.cu:41-65): out[t] = W[ids[t]] * scale.
+ * ids: int32 or int64 (ids_dtype); an id outside [0, vocab) yields a zero row and MVB_DEV_BAD_TOKEN.
+ * softmax_forward (:24, softmax_kernel.cu:83-100): last-dim softmax, fp32 math. */
+int mvb_embedding(void* out, const void* ids, int ids_dtype, const void* weight, int64_t tokens, int64_t hidden,
+                  int64_t vocab, float scale, int dtype, mvb_stream_t stream);
+int mvb_softmax(void* out, const void* in, int64_t rows, int64_t n, int dtype, mvb_stream_t stream);
+
+/* ---- sampling ------------------------------------------------------------------
+ * greedy_sample (ops_binding.cpp:20, sampling_kernel.cu:195-215): row argmax,
+ * lowest index among equal maxima (torch.argmax semantics).  out: int64 [rows].
+ * top_k_top_p_filter (:21, :218-231): in place; logits outside the top-k
+ * (ties at the k-th value kept) and outside the top-p nucleus of the untempered
+ * distribution become -inf (ops/sampling.py:26-50).  top_k <= 0 / top_p >= 1 disable.
+ * softmax_multinomial_sample (:22, :236-254): temperature-scaled softmax and one
+ * draw per row.  The draw is an inverse CDF in vocabulary order with one
+ * Philox4x32-10 uniform per row, counter (row, offset, 'SAMP'), key = seed. */
+int mvb_greedy_sample(int64_t* out, const void* logits, int64_t rows, int64_t vocab, int64_t row_stride,
+                      int dtype, mvb_stream_t stream);
+int mvb_top_k_top_p_filter(void* logits, int64_t rows, int64_t vocab, int top_k, float top_p, int dtype,
+                           mvb_stream_t stream);
+int mvb_softmax_multinomial_sample(int64_t* out, const void* logits, int64_t rows, int64_t vocab,
+                                   float temperature, uint64_t seed, uint64_t offset, int dtype,
+                                   mvb_stream_t stream);
+
+/* Fused decode sampler (replaces Sampler.sample's per-sequence loop, engine.py:352-356 +
+ * sampler.py:21-48): per row, temperature == 0 -> greedy; otherwise top-k, top-p on the
+ * untempered logits, /T, softmax, Philox inverse-CDF draw.  Per-row parameters (arrays of
+ * `rows`; any may be NULL for "use scalar default": T=1, top_k=-1, top_p=1).
+ * probs_out (nullable, fp32 [rows, vocab]): the filtered tempered distribution, for callers
+ * that draw with their own generator.  offset_dev (nullable): a device int64 added to
+ * `offset` at run time, so a captured CUDA graph draws fresh uniforms on every replay.
+ * top_k is limited to 1024; rows with top_k <= 0 and top_p < 1 take the full-vocabulary
+ * nucleus path. */
+int mvb_sample(int64_t* out, float* probs_out, const void* logits, int64_t rows, int64_t vocab,
+               int64_t row_stride, const float* temperature, const int32_t* top_k, const float* top_p,
+               uint64_t seed, uint64_t offset, const int64_t* offset_dev, int dtype, mvb_stream_t stream);
+
+/* ---- fused QK-norm + RoPE + paged KV write ---------------------------------
+ * Replaces, for one decode step of one layer, the q_norm/k_norm RMSNorm
+ * (model.py:174-178), apply_rotary_pos_emb (:184) and Attention._write_kv_cache
+ * (:226-243; model_cuda.py:182-207).  qkv: [B, (Hq + 2*Hkv) * D] bf16 (row stride
+ * qkv_stride) -- the fused q|k|v projection.  q_norm_w / k_norm_w: [D] bf16 or NULL
+ * (no QK-norm).  cos/sin: the model's bf16 tables [table_len, D].  positions: int32 [B]
+ * (token position = slot index = cached tokens, engine.py:316/326).  block_tables:
+ * int32 [B, max_blocks].  kv_cache: the KVCacheManager tensor
+ * [L, 2, num_blocks, block_size, Hkv, D] bf16 (kv_cache.py:24-29).
+ * q_out: [B, Hq, D] bf16.  Writes K (normed, roped) and V of each token to
+ * (layer, block_tables[b][pos / block_size], pos % block_size). */
+int mvb_qk_norm_rope_kv_write(void* q_out, void* kv_cache, const void* qkv, int64_t qkv_stride,
+                              const void* q_norm_w, const void* k_norm_w, const void* cos, const void* sin,
+                              int64_t table_len, const int32_t* positions, const int32_t* block_tables,
+                              int64_t max_blocks, int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+                              int64_t head_dim, int64_t num_layers, int64_t layer, int64_t num_blocks,
+                              int64_t block_size, float eps, mvb_stream_t stream);
+
+/* ---- paged attention decode --------------------------------------------------
+ * Replaces Attention._read_kv_cache_batch + GQA expand + SDPA for one query token per
+ * sequence (model.py:191-221, model_cuda.py:145-177): out[b, h] =
+ * softmax(q[b,h] . K[b, :ctx_lens[b]]^T * scale) V, reading K/V straight out of the
+ * paged pool through block_tables.  q/out: [B, Hq, D] bf16 (row stride in elements
+ * q_stride / out_stride between sequences).  Split-KV across the whole GPU with a
+ * deterministic merge.  workspace: >= mvb_paged_attention_workspace_bytes(); its
+ * counter region must be zero before the first call (the kernel leaves it zero). */
+int64_t mvb_paged_attention_workspace_bytes(int64_t batch, int64_t num_q_heads, int64_t head_dim, int device);
+int mvb_paged_attention_decode(void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                               const void* kv_cache, const int32_t* block_tables, int64_t max_blocks,
+                               const int32_t* ctx_lens, int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+                               int64_t head_dim, int64_t num_layers, int64_t layer, int64_t num_blocks,
+                               int64_t block_size, float scale, void* workspace, int64_t workspace_bytes,
+                               mvb_stream_t stream);
+
+/* ---- dense GEMM on tcgen05 --------------------------------------------------------
+ * Replaces the nn.Linear (cuBLAS) projections of the decode step (model_cuda.py:124-126,
+ * :180, ops/mlp.py:66/84, model_cuda.py:413): Y[m, n] = sum_k X[m, k] * W[n, k] (bf16 in,
+ * fp32 accumulate in TMEM).  Stream-K over all SMs; partial tiles merged in a fixed order.
+ * epilogue: MVB_EPI_STORE  Y = bf16(acc)
+ *           MVB_EPI_SWIGLU W is the reference's cat([gate, up]) of 2*inter rows; Y[m, j] =
+ *                          bf16(bf16(silu(bf16(gate))) * bf16(up)), j < inter (model.py:116-117)
+ *           MVB_EPI_RESADD Y = bf16(aux[m, n] + bf16(acc)) (residual add, model.py:319/328)
+ * Requires k % 64 == 0, ldx/ldw/ldy multiples of 8, 16-byte aligned pointers, m <= 256.
+ * workspace: >= mvb_gemm_workspace_bytes(m, n, k, device); zero before the first call. */
+#define MVB_EPI_STORE 0
+#define MVB_EPI_SWIGLU 1
+#define MVB_EPI_RESADD 2
+int64_t mvb_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int device);
+int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t m,
+                  int64_t n, int64_t k, int epilogue, const void* aux, int64_t ld_aux, void* workspace,
+                  int64_t workspace_bytes, mvb_stream_t stream);
+
+/* ---- programmatic dependent launch -------------------------------------------
+ * When enabled (default off), kernels of this library are launched with the PDL
+ * attribute so that, inside a stream or CUDA graph, a kernel's prologue overlaps the
+ * tail of the previous one.  Returns the previous setting. */
+int mvb_set_pdl(int enable);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MVB200_H_ */

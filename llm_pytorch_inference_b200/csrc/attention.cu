@@ -1,0 +1,503 @@
+// Paged-attention decode: one query token per sequence, K/V read straight out of the
+// reference's paged pool through the block table.
+//
+// Replaces, for decode, Attention._read_kv_cache_batch + GQA expand + SDPA with a
+// padding mask (models/model.py:191-221; models/model_cuda.py:145-177):
+//   out[b, h] = softmax(q[b, h] . K[b, 0:ctx_b]^T * scale) V[b, 0:ctx_b]
+// Pool layout (engine/kv_cache.py:24-29): [L, 2, num_blocks, block_size=16, Hkv, D].
+//
+// Work split: the (sequence, block) pairs of the whole batch are laid end to end and
+// divided evenly over the persistent CTAs (split-KV across the GPU).  A sequence that
+// spans several CTAs is merged by the last CTA to finish it, combining the partial
+// (max, sum, output) triples in CTA order, so results are deterministic.
+//
+// CTA = Hkv consumer warps (one per KV head, its GROUP query heads as the rows of a
+// 16-row mma tile) + 1 producer warp that streams each block's K and V (all heads)
+// through TMA into a 128-byte-swizzled [head][token][64] image, 2 halves of head_dim.
+// QK^T and PV use mma.sync m16n8k16 (bf16 in, fp32 accumulate); softmax is the online
+// (running max / running sum) form in the exp2 domain.
+#include "common.cuh"
+#include "host.h"
+
+namespace mvb {
+namespace {
+
+constexpr int D = 128;       // head_dim handled by this kernel
+constexpr int BS = 16;       // tokens per block (the reference's block_size)
+constexpr int HALF_BYTES_PER_HEAD = BS * 64 * 2;  // 2 KB: 16 tokens x 64 dims
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct AttnArgs {
+  __nv_bfloat16* out;
+  int64_t out_stride;
+  const __nv_bfloat16* q;
+  int64_t q_stride;
+  const int32_t* block_tables;
+  int64_t max_blocks;
+  const int32_t* ctx_lens;
+  int batch;
+  int num_q_heads;
+  int64_t layer;
+  int64_t num_blocks;
+  float scale_log2;  // scale * log2(e)
+  float* partial_o;  // [2*G][Hq][D]
+  float2* partial_ml;  // [2*G][Hq]  (running max in log2 units, running sum)
+  int* counters;     // [batch]
+  unsigned* err;
+  int per_head_tma;
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ int64_t range_start(int c, int64_t total, int grid) {
+  return static_cast<int64_t>(c) * total / grid;
+}
+__device__ __forceinline__ int cta_of(int64_t x, int64_t total, int grid) {
+  return static_cast<int>(((x + 1) * grid + total - 1) / total - 1);
+}
+
+template <int HKV>
+__device__ __forceinline__ void consumer_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(HKV * 32) : "memory");
+}
+
+template <int GROUP, int HKV, int STAGES>
+__global__ void __launch_bounds__((HKV + 1) * 32, 1)
+    paged_attention_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs a) {
+  constexpr int STAGE_BYTES = 4 * HKV * HALF_BYTES_PER_HEAD;  // K lo, K hi, V lo, V hi
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + STAGES);
+  volatile int* last_flag = abort_flag + 1;
+  int* cu = const_cast<int*>(abort_flag + 2);  // [batch + 1] block prefix sums
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], HKV);
+    }
+    *abort_flag = 0;
+    *last_flag = 0;
+    fence_barrier_init();
+  }
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  pdl_wait();
+  // Per-sequence block counts -> prefix sums (warp 0, 32 sequences at a time).
+  if (warp == 0) {
+    int carry = 0;
+    for (int base = 0; base < a.batch; base += 32) {
+      const int b = base + lane;
+      int n = 0;
+      if (b < a.batch) {
+        const int ctx = a.ctx_lens[b];
+        n = ctx > 0 ? (ctx + BS - 1) / BS : 0;
+        if (n > a.max_blocks) {
+          report(a.err, kDevBadPosition);
+          n = static_cast<int>(a.max_blocks);
+        }
+      }
+      int incl = n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (b < a.batch) cu[b + 1] = carry + incl;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) cu[0] = 0;
+  }
+  __syncthreads();
+  const int64_t total = cu[a.batch];
+  // Effective grid: never more CTAs than blocks, so every CTA in [0, G) owns at least
+  // one block and the contributor count of a sequence is exact.
+  const int G = static_cast<int>(total < gridDim.x ? total : gridDim.x);
+  if (static_cast<int>(blockIdx.x) >= G) return;
+  const int64_t g_begin = range_start(blockIdx.x, total, G);
+  const int64_t g_end = range_start(blockIdx.x + 1, total, G);
+  int b0 = 0;
+  {  // first sequence with cu[b+1] > g_begin
+    int lo = 0, hi = a.batch - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (cu[mid + 1] > g_begin) hi = mid; else lo = mid + 1;
+    }
+    b0 = lo;
+  }
+
+  int issued = 0;
+  if (warp == HKV) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0 && g_end > g_begin) {
+      prefetch_tmap(&tm);
+      const uint64_t pol = l2_policy_evict_first();
+      int b = b0;
+      const int64_t P = a.num_blocks;
+      for (int64_t g = g_begin; g < g_end; ++g) {
+        while (g >= cu[b + 1]) ++b;
+        const int j = static_cast<int>(g - cu[b]);
+        int blk = a.block_tables[static_cast<int64_t>(b) * a.max_blocks + j];
+        if (blk < 0 || blk >= P) {
+          report(a.err, kDevBadBlock);
+          blk = 0;  // stay in bounds; the sequence's output is not trusted (status word set)
+        }
+        const int it = static_cast<int>(g - g_begin);
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err)) break;
+        mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+        uint8_t* st = smem + s * STAGE_BYTES;
+        for (int kv = 0; kv < 2; ++kv) {
+          const int row = static_cast<int>((a.layer * 2 + kv) * P + blk);
+          for (int half = 0; half < 2; ++half) {
+            uint8_t* dst = st + (kv * 2 + half) * HKV * HALF_BYTES_PER_HEAD;
+            if (a.per_head_tma) {
+              for (int h = 0; h < HKV; ++h)
+                tma_load_4d(dst + h * HALF_BYTES_PER_HEAD, &tm, &full[s], half * 64, h, 0, row, pol);
+            } else {
+              tma_load_4d(dst, &tm, &full[s], half * 64, 0, 0, row, pol);
+            }
+          }
+        }
+        issued = it + 1;
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- consumers
+    const int h = warp;  // KV head
+    const int g = lane >> 2, t = lane & 3;
+    const bool row_valid = g < GROUP;
+    const uint32_t sbase = smem_u32(smem);
+    int b = b0;
+    int64_t gpos = g_begin;
+    int it = 0;
+    bool ok = true;
+    while (ok && gpos < g_end) {
+      while (gpos >= cu[b + 1]) ++b;
+      const int64_t seq_lo = cu[b], seq_hi = cu[b + 1];
+      const int64_t seg_end = min(g_end, seq_hi);
+      const int ctx = a.ctx_lens[b];
+      const int hq0 = h * GROUP;
+      // Q fragments (rows = the GROUP query heads of this KV head; rows >= GROUP are zero).
+      uint32_t qa[8][2];
+      {
+        const __nv_bfloat16* qp = a.q + static_cast<int64_t>(b) * a.q_stride + static_cast<int64_t>(hq0 + g) * D;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          if (row_valid) {
+            qa[kk][0] = *reinterpret_cast<const uint32_t*>(qp + kk * 16 + 2 * t);
+            qa[kk][1] = *reinterpret_cast<const uint32_t*>(qp + kk * 16 + 8 + 2 * t);
+          } else {
+            qa[kk][0] = qa[kk][1] = 0u;
+          }
+        }
+      }
+      float o[16][4];
+#pragma unroll
+      for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+      float m_run = -INFINITY, l_run = 0.0f;
+
+      for (int64_t gg = gpos; gg < seg_end; ++gg, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&full[s], ph, nullptr, a.err)) {
+          ok = false;
+          break;
+        }
+        const int j = static_cast<int>(gg - seq_lo);  // block index within the sequence
+        const uint32_t kbase = sbase + s * STAGE_BYTES + h * HALF_BYTES_PER_HEAD;
+        const uint32_t vbase = kbase + 2 * HKV * HALF_BYTES_PER_HEAD;
+        // S = Q K^T for 16 tokens: two n-tiles of 8 tokens.
+        float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const int half = kk >> 2;
+          const int mi = lane >> 3;
+          const int tok = (mi >> 1) * 8 + (lane & 7);
+          const int chunk = (kk & 3) * 2 + (mi & 1);
+          const uint32_t addr = kbase + half * HKV * HALF_BYTES_PER_HEAD + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+          uint32_t k0, k1, k2, k3;
+          ldsm_x4(addr, k0, k1, k2, k3);
+          mma_bf16_16816(sacc[0], qa[kk][0], 0u, qa[kk][1], 0u, k0, k1);
+          mma_bf16_16816(sacc[1], qa[kk][0], 0u, qa[kk][1], 0u, k2, k3);
+        }
+        // Scale into the log2 domain and mask tokens past the context.
+        float sv[4];
+        const int tok0 = j * BS;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int tok = tok0 + nt * 8 + 2 * t + c;
+            sv[nt * 2 + c] = tok < ctx ? sacc[nt][c] * a.scale_log2 : -INFINITY;
+          }
+        }
+        float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run, mx);
+        const float alpha = exp2f(m_run - m_new);
+        float p[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p[i] = exp2f(sv[i] - m_new);
+        l_run = l_run * alpha + (p[0] + p[1] + p[2] + p[3]);
+        m_run = m_new;
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          o[n][0] *= alpha;
+          o[n][1] *= alpha;
+        }
+        const uint32_t pa0 = pack_bf16(p[0], p[1]);  // row g, tokens 2t, 2t+1
+        const uint32_t pa2 = pack_bf16(p[2], p[3]);  // row g, tokens 8+2t, 9+2t
+        // O += P V: 16 n-tiles of 8 dims, two per transposed ldmatrix.
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {
+          const int half = np >> 2;
+          const int mi = lane >> 3;
+          const int tok = (mi & 1) * 8 + (lane & 7);
+          const int chunk = (np & 3) * 2 + (mi >> 1);
+          const uint32_t addr = vbase + half * HKV * HALF_BYTES_PER_HEAD + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+          uint32_t v0, v1, v2, v3;
+          ldsm_x4_t(addr, v0, v1, v2, v3);
+          mma_bf16_16816(o[2 * np], pa0, 0u, pa2, 0u, v0, v1);
+          mma_bf16_16816(o[2 * np + 1], pa0, 0u, pa2, 0u, v2, v3);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+      if (!ok) break;
+
+      // Segment done: finish this warp's GROUP heads.
+      l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+      l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+      const bool whole = (gpos == seq_lo) && (seg_end == seq_hi);
+      const int hq = hq0 + g;
+      if (whole) {
+        if (row_valid) {
+          const float inv = 1.0f / l_run;
+          __nv_bfloat16* op = a.out + static_cast<int64_t>(b) * a.out_stride + static_cast<int64_t>(hq) * D;
+#pragma unroll
+          for (int n = 0; n < 16; ++n)
+            *reinterpret_cast<__nv_bfloat162*>(op + n * 8 + 2 * t) = __floats2bfloat162_rn(o[n][0] * inv, o[n][1] * inv);
+        }
+      } else {
+        const int slot = (g_begin >= seq_lo) ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
+        if (row_valid) {
+          const float inv = 1.0f / l_run;
+          float* po = a.partial_o + (static_cast<int64_t>(slot) * a.num_q_heads + hq) * D;
+#pragma unroll
+          for (int n = 0; n < 16; ++n) __stcg(reinterpret_cast<float2*>(po + n * 8 + 2 * t), make_float2(o[n][0] * inv, o[n][1] * inv));
+          if (t == 0) __stcg(a.partial_ml + static_cast<int64_t>(slot) * a.num_q_heads + hq, make_float2(m_run, l_run));
+        }
+        __threadfence();
+        consumer_bar<HKV>();
+        if (threadIdx.x == 0) {
+          const int c_first = cta_of(seq_lo, total, G);
+          const int c_last = cta_of(seq_hi - 1, total, G);
+          const int old = atomicAdd(&a.counters[b], 1);
+          const int last = old == c_last - c_first;
+          if (last) __threadfence();
+          *last_flag = last;
+        }
+        consumer_bar<HKV>();
+        if (*last_flag) {
+          const int c_first = cta_of(seq_lo, total, G);
+          const int c_last = cta_of(seq_hi - 1, total, G);
+          const int n_out = a.num_q_heads * D;
+          for (int i = threadIdx.x; i < n_out; i += HKV * 32) {
+            const int hh = i / D;
+            float mmax = -INFINITY;
+            for (int c = c_first; c <= c_last; ++c) {
+              const int sl = range_start(c, total, G) >= seq_lo ? 2 * c : 2 * c + 1;
+              mmax = fmaxf(mmax, __ldcg(a.partial_ml + static_cast<int64_t>(sl) * a.num_q_heads + hh).x);
+            }
+            float num = 0.0f, den = 0.0f;
+            for (int c = c_first; c <= c_last; ++c) {
+              const int sl = range_start(c, total, G) >= seq_lo ? 2 * c : 2 * c + 1;
+              const float2 ml = __ldcg(a.partial_ml + static_cast<int64_t>(sl) * a.num_q_heads + hh);
+              const float wgt = ml.y * exp2f(ml.x - mmax);
+              num += wgt * __ldcg(a.partial_o + static_cast<int64_t>(sl) * a.num_q_heads * D + i);
+              den += wgt;
+            }
+            a.out[static_cast<int64_t>(b) * a.out_stride + i] = __float2bfloat16_rn(num / den);
+          }
+          if (threadIdx.x == 0) a.counters[b] = 0;
+        }
+        consumer_bar<HKV>();
+      }
+      gpos = seg_end;
+    }
+  }
+
+  __syncthreads();
+  if (warp == HKV && lane == 0) {
+    const int first = issued > STAGES ? issued - STAGES : 0;
+    for (int it = first; it < issued; ++it) mbar_wait(&full[it % STAGES], (it / STAGES) & 1, nullptr, a.err);
+  }
+}
+
+template <int HKV>
+constexpr int attn_stages() {
+  return HKV >= 8 ? 3 : (HKV == 4 ? 6 : 8);
+}
+
+template <int HKV>
+size_t attn_smem(int batch) {
+  return static_cast<size_t>(attn_stages<HKV>()) * 4 * HKV * HALF_BYTES_PER_HEAD + 2 * 8 * attn_stages<HKV>() + 16 +
+         4 * (batch + 1) + 1024;
+}
+
+template <int GROUP, int HKV>
+int launch_attn(const CUtensorMap& tm, const AttnArgs& a, int grid, cudaStream_t st) {
+  constexpr int S = attn_stages<HKV>();
+  const size_t smem = attn_smem<HKV>(a.batch);
+  // Raise the kernel's dynamic-smem limit once per device (to the 4096-sequence maximum),
+  // so no attribute call happens while a stream is being captured into a graph.
+  static unsigned long long done_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !(done_mask & (1ull << dev))) {
+    MVB_TRY(set_smem(paged_attention_kernel<GROUP, HKV, S>, attn_smem<HKV>(4096), "paged_attention: smem attribute"));
+    if (dev < 64) done_mask |= 1ull << dev;
+  }
+  return launch("paged_attention_decode", paged_attention_kernel<GROUP, HKV, S>, dim3(grid), dim3((HKV + 1) * 32),
+                smem, st, tm, a);
+}
+
+template <int HKV>
+int dispatch_group(int group, const CUtensorMap& tm, const AttnArgs& a, int grid, cudaStream_t st) {
+  switch (group) {
+    case 1: return launch_attn<1, HKV>(tm, a, grid, st);
+    case 2: return launch_attn<2, HKV>(tm, a, grid, st);
+    case 4: return launch_attn<4, HKV>(tm, a, grid, st);
+    case 8: return launch_attn<8, HKV>(tm, a, grid, st);
+    default: return fail(MVB_ERR_UNSUPPORTED, "paged attention: %d query heads per KV head", group);
+  }
+}
+
+int64_t attn_counters_bytes(int64_t batch) { return (batch * 4 + 255) / 256 * 256; }
+
+// Encodes the KV-pool tensor map.  Tries the one-box-per-half view (dims ordered
+// {dim, token, head, block}, which permutes the token/head strides) and falls back
+// to one box per head in natural stride order; both give the same shared-memory image.
+int encode_kv_map(CUtensorMap* m, const void* kv, int64_t hkv, int64_t rows, int* per_head) {
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(BS), static_cast<uint64_t>(hkv),
+                              static_cast<uint64_t>(rows)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(hkv * D * 2), static_cast<uint64_t>(D * 2),
+                                 static_cast<uint64_t>(BS * hkv * D * 2)};
+    const uint32_t box[4] = {64, BS, static_cast<uint32_t>(hkv), 1};
+    if (encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, kv, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) ==
+        MVB_OK) {
+      *per_head = 0;
+      return MVB_OK;
+    }
+  }
+  const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(hkv), static_cast<uint64_t>(BS),
+                            static_cast<uint64_t>(rows)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(D * 2), static_cast<uint64_t>(hkv * D * 2),
+                               static_cast<uint64_t>(BS * hkv * D * 2)};
+  const uint32_t box[4] = {64, 1, BS, 1};
+  *per_head = 1;
+  return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, kv, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace
+}  // namespace mvb
+
+using namespace mvb;
+
+extern "C" int64_t mvb_paged_attention_workspace_bytes(int64_t batch, int64_t num_q_heads, int64_t head_dim,
+                                                       int device) {
+  int sms = mvb_num_sms(device);
+  if (sms <= 0) sms = 148;
+  return attn_counters_bytes(batch) + 2LL * sms * num_q_heads * 8 + 2LL * sms * num_q_heads * head_dim * 4 + 256;
+}
+
+extern "C" int mvb_paged_attention_decode(void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                                          const void* kv_cache, const int32_t* block_tables, int64_t max_blocks,
+                                          const int32_t* ctx_lens, int64_t batch, int64_t num_q_heads,
+                                          int64_t num_kv_heads, int64_t head_dim, int64_t num_layers, int64_t layer,
+                                          int64_t num_blocks, int64_t block_size, float scale, void* workspace,
+                                          int64_t workspace_bytes, mvb_stream_t stream) {
+  MVB_REQUIRE(out && q && kv_cache && block_tables && ctx_lens && workspace,
+              "mvb_paged_attention_decode: null pointer");
+  MVB_REQUIRE(head_dim == D, "mvb_paged_attention_decode: head_dim %lld (this build: 128)", (long long)head_dim);
+  MVB_REQUIRE(block_size == BS, "mvb_paged_attention_decode: block_size %lld (this build: 16)",
+              (long long)block_size);
+  MVB_REQUIRE(batch >= 0 && batch <= 4096, "mvb_paged_attention_decode: batch %lld", (long long)batch);
+  MVB_REQUIRE(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0, "mvb_paged_attention_decode: head counts");
+  MVB_REQUIRE(layer >= 0 && layer < num_layers && num_blocks > 0 && max_blocks > 0,
+              "mvb_paged_attention_decode: cache geometry");
+  MVB_REQUIRE(q_stride % 2 == 0 && aligned(q, 4) && out_stride % 2 == 0 && aligned(out, 4),
+              "mvb_paged_attention_decode: q/out must be 4-byte aligned with even strides");
+  MVB_REQUIRE(aligned(kv_cache, 16) && aligned(workspace, 256), "mvb_paged_attention_decode: alignment");
+  if (batch == 0) return MVB_OK;
+  const int64_t group = num_q_heads / num_kv_heads;
+  const int sms = current_sm_count();
+  MVB_REQUIRE(sms > 0, "mvb_paged_attention_decode: no device");
+  const int64_t need = attn_counters_bytes(batch) + 2LL * sms * num_q_heads * 8 + 2LL * sms * num_q_heads * D * 4;
+  MVB_REQUIRE(workspace_bytes >= need, "mvb_paged_attention_decode: workspace %lld < %lld",
+              (long long)workspace_bytes, (long long)need);
+
+  CUtensorMap tm;
+  int per_head = 0;
+  MVB_TRY(encode_kv_map(&tm, kv_cache, num_kv_heads, num_layers * 2 * num_blocks, &per_head));
+
+  AttnArgs a;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.out_stride = out_stride;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_stride = q_stride;
+  a.block_tables = block_tables;
+  a.max_blocks = max_blocks;
+  a.ctx_lens = ctx_lens;
+  a.batch = static_cast<int>(batch);
+  a.num_q_heads = static_cast<int>(num_q_heads);
+  a.layer = layer;
+  a.num_blocks = num_blocks;
+  a.scale_log2 = scale * kLog2e;
+  char* ws = static_cast<char*>(workspace);
+  a.counters = reinterpret_cast<int*>(ws);
+  a.partial_ml = reinterpret_cast<float2*>(ws + attn_counters_bytes(batch));
+  a.partial_o = reinterpret_cast<float*>(ws + attn_counters_bytes(batch) + 2LL * sms * num_q_heads * 8);
+  a.err = device_status_ptr();
+  a.per_head_tma = per_head;
+  // Grid: one persistent CTA per SM (192 KB of stages each); never more CTAs than blocks.
+  // The block total is only known on the device, so the grid is the SM count and CTAs
+  // with an empty range exit after the prologue.
+  const int grid = sms;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (num_kv_heads) {
+    case 1: return dispatch_group<1>(static_cast<int>(group), tm, a, grid, st);
+    case 2: return dispatch_group<2>(static_cast<int>(group), tm, a, grid, st);
+    case 4: return dispatch_group<4>(static_cast<int>(group), tm, a, grid, st);
+    case 8: return dispatch_group<8>(static_cast<int>(group), tm, a, grid, st);
+    default: return fail(MVB_ERR_UNSUPPORTED, "mvb_paged_attention_decode: %lld KV heads", (long long)num_kv_heads);
+  }
+}

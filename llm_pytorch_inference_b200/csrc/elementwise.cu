@@ -1,0 +1,213 @@
+// Elementwise / row ops of the mini_vllm ops API: activations, gated activations,
+// fused MLP activation, embedding gather, row softmax, standalone RoPE.
+//
+// Each reproduces the rounding sequence of the PyTorch expression it replaces:
+//   silu / gelu(tanh)            ops/activation.py:10-30       y = T(act(x))
+//   swiglu / geglu               ops/activation.py:33-66       y = T(T(act(g)) * u)
+//   fused_mlp (FusedMLP fallback) ops/mlp.py:73-82             y = T(T(act(g)) * u)
+//   embedding                    ops/embedding.py:11-35        y = W[id] (* scale, rounded)
+//   softmax                      ops/softmax.py:5-25           fp32 exp/sum, one rounding
+//   rotary                       ops/rope.py:74-76             y = T(T(x*cos) + T(rot(x)*sin))
+#include "common.cuh"
+#include "host.h"
+
+namespace mvb {
+namespace {
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  const float kBeta = 0.7978845608028654f;  // sqrt(2/pi)
+  const float kKappa = 0.044715f;
+  return 0.5f * x * (1.0f + tanhf(kBeta * (x + kKappa * x * x * x)));
+}
+
+__device__ __forceinline__ float act_f(float x, int act) { return act == MVB_ACT_SILU ? silu_f(x) : gelu_tanh_f(x); }
+
+template <typename T>
+__global__ void activation_kernel(T* __restrict__ out, const T* __restrict__ in, int64_t n, int act) {
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = from_f<T>(act_f(to_f<T>(in[i]), act));
+}
+
+template <typename T>
+__global__ void gated_kernel(T* __restrict__ out, const T* __restrict__ gate, const T* __restrict__ up, int64_t n,
+                             int act) {
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = from_f<T>(rnd<T>(act_f(to_f<T>(gate[i]), act)) * to_f<T>(up[i]));
+}
+
+template <typename T>
+__global__ void fused_mlp_kernel(T* __restrict__ out, const T* __restrict__ gate_up, int64_t rows, int64_t inter,
+                                 int act) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t n = rows * inter;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / inter, j = i - r * inter;
+    const T* row = gate_up + r * 2 * inter;
+    out[i] = from_f<T>(rnd<T>(act_f(to_f<T>(row[j]), act)) * to_f<T>(row[inter + j]));
+  }
+}
+
+template <typename T, typename I>
+__global__ void embedding_kernel(T* __restrict__ out, const I* __restrict__ ids, const T* __restrict__ w,
+                                 int64_t hidden, int64_t vocab, float scale, unsigned* err) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t t = blockIdx.x;
+  const int64_t id = static_cast<int64_t>(ids[t]);
+  T* y = out + t * hidden;
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) report(err, kDevBadToken);
+    for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) y[i] = from_f<T>(0.0f);
+    return;
+  }
+  const T* src = w + id * hidden;
+  if (scale == 1.0f) {
+    for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) y[i] = src[i];
+  } else {
+    for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) y[i] = from_f<T>(to_f<T>(src[i]) * scale);
+  }
+}
+
+template <typename T>
+__global__ void softmax_kernel(T* __restrict__ out, const T* __restrict__ in, int64_t n) {
+  __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait();
+  const T* x = in + blockIdx.x * n;
+  T* y = out + blockIdx.x * n;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  float m = -INFINITY;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, to_f<T>(x[i]));
+  m = warp_max(m);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  m = warp_max(lane < nw ? red[lane] : -INFINITY);
+  __syncthreads();
+  float s = 0.0f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += expf(to_f<T>(x[i]) - m);
+  s = warp_sum(s);
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  s = warp_sum(lane < nw ? red[lane] : 0.0f);
+  const float inv = 1.0f / s;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) y[i] = from_f<T>(expf(to_f<T>(x[i]) - m) * inv);
+}
+
+template <typename T>
+__global__ void rope_kernel(T* __restrict__ out, const T* __restrict__ in, const T* __restrict__ cos,
+                            const T* __restrict__ sin, int64_t rows, int hd) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int half = hd / 2;
+  const int64_t n = rows * hd;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / hd;
+    const int d = static_cast<int>(i - r * hd);
+    const T* x = in + r * hd;
+    const float xv = to_f<T>(x[d]);
+    const float rot = d < half ? -to_f<T>(x[d + half]) : to_f<T>(x[d - half]);
+    const float a = rnd<T>(xv * to_f<T>(cos[i]));
+    const float b = rnd<T>(rot * to_f<T>(sin[i]));
+    out[i] = from_f<T>(a + b);
+  }
+}
+
+dim3 grid_for(int64_t n, int threads) {
+  int64_t b = (n + threads - 1) / threads;
+  if (b > 148 * 32) b = 148 * 32;
+  if (b < 1) b = 1;
+  return dim3(static_cast<unsigned>(b));
+}
+
+}  // namespace
+}  // namespace mvb
+
+using namespace mvb;
+
+#define MVB_DISPATCH_FLOAT(dtype, NAME, ...)                                            \
+  switch (dtype) {                                                                      \
+    case MVB_F32: { using T = float; __VA_ARGS__; }                                     \
+    case MVB_F16: { using T = __half; __VA_ARGS__; }                                    \
+    case MVB_BF16: { using T = __nv_bfloat16; __VA_ARGS__; }                            \
+    default: return fail(MVB_ERR_INVALID_ARG, NAME ": unsupported dtype %d", dtype);  \
+  }
+
+extern "C" int mvb_activation(void* out, const void* in, int64_t n, int act, int dtype, mvb_stream_t stream) {
+  MVB_REQUIRE(out && in && n >= 0, "mvb_activation: bad arguments");
+  MVB_REQUIRE(act == MVB_ACT_SILU || act == MVB_ACT_GELU_TANH, "mvb_activation: bad act %d", act);
+  if (n == 0) return MVB_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  MVB_DISPATCH_FLOAT(dtype, "mvb_activation",
+                     return launch("activation", activation_kernel<T>, grid_for(n, 256), dim3(256), 0, st, (T*)out,
+                                   (const T*)in, n, act));
+}
+
+extern "C" int mvb_gated_activation(void* out, const void* gate, const void* up, int64_t n, int act, int dtype,
+                                    mvb_stream_t stream) {
+  MVB_REQUIRE(out && gate && up && n >= 0, "mvb_gated_activation: bad arguments");
+  MVB_REQUIRE(act == MVB_ACT_SILU || act == MVB_ACT_GELU_TANH, "mvb_gated_activation: bad act %d", act);
+  if (n == 0) return MVB_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  MVB_DISPATCH_FLOAT(dtype, "mvb_gated_activation",
+                     return launch("gated_activation", gated_kernel<T>, grid_for(n, 256), dim3(256), 0, st, (T*)out,
+                                   (const T*)gate, (const T*)up, n, act));
+}
+
+extern "C" int mvb_fused_mlp(void* out, const void* gate_up, int64_t rows, int64_t inter, int act, int dtype,
+                             mvb_stream_t stream) {
+  MVB_REQUIRE(out && gate_up && rows >= 0 && inter > 0, "mvb_fused_mlp: bad arguments");
+  MVB_REQUIRE(act == MVB_ACT_SILU || act == MVB_ACT_GELU_TANH, "mvb_fused_mlp: bad act %d", act);
+  if (rows == 0) return MVB_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  MVB_DISPATCH_FLOAT(dtype, "mvb_fused_mlp",
+                     return launch("fused_mlp", fused_mlp_kernel<T>, grid_for(rows * inter, 256), dim3(256), 0, st,
+                                   (T*)out, (const T*)gate_up, rows, inter, act));
+}
+
+extern "C" int mvb_embedding(void* out, const void* ids, int ids_dtype, const void* weight, int64_t tokens,
+                             int64_t hidden, int64_t vocab, float scale, int dtype, mvb_stream_t stream) {
+  MVB_REQUIRE(out && ids && weight && tokens >= 0 && hidden > 0 && vocab > 0, "mvb_embedding: bad arguments");
+  MVB_REQUIRE(ids_dtype == MVB_I32 || ids_dtype == MVB_I64, "mvb_embedding: ids must be int32 or int64");
+  if (tokens == 0) return MVB_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  unsigned* err = device_status_ptr();
+  const int threads = hidden >= 1024 ? 256 : 128;
+  dim3 grid(static_cast<unsigned>(tokens));
+  if (ids_dtype == MVB_I64) {
+    MVB_DISPATCH_FLOAT(dtype, "mvb_embedding",
+                       return launch("embedding", embedding_kernel<T, int64_t>, grid, dim3(threads), 0, st, (T*)out,
+                                     (const int64_t*)ids, (const T*)weight, hidden, vocab, scale, err));
+  }
+  MVB_DISPATCH_FLOAT(dtype, "mvb_embedding",
+                     return launch("embedding", embedding_kernel<T, int32_t>, grid, dim3(threads), 0, st, (T*)out,
+                                   (const int32_t*)ids, (const T*)weight, hidden, vocab, scale, err));
+}
+
+extern "C" int mvb_softmax(void* out, const void* in, int64_t rows, int64_t n, int dtype, mvb_stream_t stream) {
+  MVB_REQUIRE(out && in && rows >= 0 && n > 0, "mvb_softmax: bad arguments");
+  if (rows == 0) return MVB_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int threads = n >= 4096 ? 1024 : (n >= 512 ? 256 : 64);
+  MVB_DISPATCH_FLOAT(dtype, "mvb_softmax",
+                     return launch("softmax", softmax_kernel<T>, dim3(static_cast<unsigned>(rows)), dim3(threads), 0,
+                                   st, (T*)out, (const T*)in, n));
+}
+
+extern "C" int mvb_rotary_pos_emb(void* out, const void* in, const void* cos, const void* sin, int64_t rows,
+                                  int64_t head_dim, int dtype, mvb_stream_t stream) {
+  MVB_REQUIRE(out && in && cos && sin && rows >= 0, "mvb_rotary_pos_emb: bad arguments");
+  MVB_REQUIRE(head_dim > 0 && head_dim % 2 == 0 && head_dim <= 1024, "mvb_rotary_pos_emb: bad head_dim %lld",
+              (long long)head_dim);
+  if (rows == 0) return MVB_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  MVB_DISPATCH_FLOAT(dtype, "mvb_rotary_pos_emb",
+                     return launch("rotary_pos_emb", rope_kernel<T>, grid_for(rows * head_dim, 256), dim3(256), 0,
+                                   st, (T*)out, (const T*)in, (const T*)cos, (const T*)sin, rows, (int)head_dim));
+}

@@ -1,0 +1,443 @@
+// Dense bf16 GEMM for the decode-step projections on 5th-generation tensor cores.
+//
+//   Y[m, n] = sum_k X[m, k] * W[n, k]      (X: activations, m = batch <= 256; W: nn.Linear weight)
+//
+// Replaces the nn.Linear / cuBLAS calls of the reference decode step: q/k/v
+// (models/model_cuda.py:124-126), o_proj (:180), gate_up / down (ops/mlp.py:66, :84)
+// and lm_head (model_cuda.py:413).
+//
+// Decode GEMMs have a tiny m, so the kernel computes D^T = W X^T ("swap AB"): a
+// 128-row slab of W is the UMMA M=128 operand, the whole batch is UMMA N=BN.  Both
+// operands are K-major and arrive through TMA in the 128-byte swizzle layout.  The
+// weight stream (the only large traffic) is split evenly over all SMs by
+// stream-K: CTA c owns k-blocks [c*T/G, (c+1)*T/G) of the linearised (tile, k-block)
+// space.  A tile covered by several CTAs is merged by the last CTA to finish it,
+// summing the fp32 partials in CTA order (deterministic).
+//
+// Warp roles (192 threads):  warp 0 TMA producer, warp 1 TMEM alloc + MMA issue,
+// warps 2-5 epilogue (TMEM -> registers -> global).  Accumulators are double
+// buffered in TMEM so the next tile's MMAs overlap the previous tile's epilogue.
+#include "common.cuh"
+#include "host.h"
+
+namespace mvb {
+namespace {
+
+constexpr int BM = 128;               // UMMA M: weight rows (output features) per tile
+constexpr int BK = 64;                // k per stage: one 128-byte swizzle row of bf16
+constexpr int A_STAGE = BM * BK * 2;  // 16 KB
+constexpr int kThreads = 192;
+
+struct GemmArgs {
+  __nv_bfloat16* y;
+  int64_t ldy;
+  const __nv_bfloat16* aux;
+  int64_t ld_aux;
+  int m, n, k;
+  int tiles;     // output tiles
+  int kblocks;   // k / BK
+  int epilogue;  // MVB_EPI_*
+  int inter;     // SWIGLU: rows of the gate half of W
+  float* partials;
+  int* counters;
+  unsigned* err;
+};
+
+__device__ __forceinline__ int64_t range_start(int c, int64_t total, int grid) {
+  return static_cast<int64_t>(c) * total / grid;
+}
+// CTA whose k-block range holds linear k-block x.
+__device__ __forceinline__ int cta_of(int64_t x, int64_t total, int grid) {
+  return static_cast<int>(((x + 1) * grid + total - 1) / total - 1);
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+// Final epilogue for 32 batch columns [c0, c0+32) of feature `row` of tile t.
+template <int BN>
+__device__ __forceinline__ void epilogue_store(const GemmArgs& a, const float (&v)[32], int t, int row, int c0,
+                                               float* xbuf) {
+  if (a.epilogue == MVB_EPI_SWIGLU) {
+    // TMEM lanes 0-63 hold gate features 64t + r, lanes 64-127 the matching up features.
+    const bool is_up = row >= 64;
+    const int r = row & 63;
+    if (is_up) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) xbuf[r * 33 + j] = bf16_round(v[j]);
+    }
+    epi_bar();
+    if (!is_up) {
+      const int f = 64 * t + r;
+      if (f < a.inter) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int b = c0 + j;
+          if (b < a.m) {
+            const float g = bf16_round(v[j]);
+            const float s = bf16_round(silu_f(g));
+            a.y[static_cast<int64_t>(b) * a.ldy + f] = __float2bfloat16_rn(s * xbuf[r * 33 + j]);
+          }
+        }
+      }
+    }
+    epi_bar();
+    return;
+  }
+  const int nn = t * BM + row;
+  if (nn >= a.n) return;
+  if (a.epilogue == MVB_EPI_RESADD) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int b = c0 + j;
+      if (b < a.m) {
+        const float r = __bfloat162float(a.aux[static_cast<int64_t>(b) * a.ld_aux + nn]);
+        a.y[static_cast<int64_t>(b) * a.ldy + nn] = __float2bfloat16_rn(r + bf16_round(v[j]));
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int b = c0 + j;
+    if (b < a.m) a.y[static_cast<int64_t>(b) * a.ldy + nn] = __float2bfloat16_rn(v[j]);
+  }
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                     const GemmArgs a) {
+  constexpr int B_STAGE = BN * BK * 2;
+  constexpr uint32_t STAGE_BYTES = A_STAGE + B_STAGE;
+  constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
+  constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * A_STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;  // [2]
+  uint64_t* acce = accf + 2;        // [2]
+  uint64_t* drain = acce + 2;       // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = abort_flag + 1;
+  float* xbuf = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 256);  // 64 x 33 floats (SWIGLU)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const int64_t total = static_cast<int64_t>(a.tiles) * a.kblocks;
+  const int64_t kb_begin = range_start(blockIdx.x, total, G);
+  const int64_t kb_end = range_start(blockIdx.x + 1, total, G);
+  const int my_kb = static_cast<int>(kb_end - kb_begin);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf[i], 1);
+      mbar_init(&acce[i], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *last_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
+  int issued = 0;  // producer: loads issued
+  if (warp == 0) {
+    if (lane == 0 && my_kb > 0) {
+      prefetch_tmap(&tmW);
+      prefetch_tmap(&tmX);
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      const bool swiglu = a.epilogue == MVB_EPI_SWIGLU;
+      auto load_w = [&](int it) {
+        const int s = it % STAGES;
+        const int64_t g = kb_begin + it;
+        const int t = static_cast<int>(g / a.kblocks);
+        const int kb = static_cast<int>(g - static_cast<int64_t>(t) * a.kblocks);
+        if (swiglu) {
+          tma_load_2d(sA + s * A_STAGE, &tmW, &full[s], kb * BK, 64 * t, pol_w);
+          tma_load_2d(sA + s * A_STAGE + A_STAGE / 2, &tmW, &full[s], kb * BK, a.inter + 64 * t, pol_w);
+        } else {
+          tma_load_2d(sA + s * A_STAGE, &tmW, &full[s], kb * BK, BM * t, pol_w);
+        }
+      };
+      auto load_x = [&](int it) {
+        const int s = it % STAGES;
+        const int64_t g = kb_begin + it;
+        const int t = static_cast<int>(g / a.kblocks);
+        const int kb = static_cast<int>(g - static_cast<int64_t>(t) * a.kblocks);
+        tma_load_2d(sB + s * B_STAGE, &tmX, &full[s], kb * BK, 0, pol_x);
+      };
+      // Weights do not depend on the previous kernel: start streaming them before the
+      // grid-dependency wait, then add the activation tiles to the same stages.
+      const int pro = my_kb < STAGES ? my_kb : STAGES;
+      for (int it = 0; it < pro; ++it) {
+        mbar_arrive_expect_tx(&full[it], STAGE_BYTES);
+        load_w(it);
+      }
+      pdl_wait();
+      for (int it = 0; it < pro; ++it) load_x(it);
+      issued = pro;
+      for (int it = pro; it < my_kb; ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err)) break;
+        mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+        load_w(it);
+        load_x(it);
+        issued = it + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && my_kb > 0) {
+      int it = 0, seg = 0;
+      int64_t kb = kb_begin;
+      bool ok = true;
+      while (ok && kb < kb_end) {
+        const int t = static_cast<int>(kb / a.kblocks);
+        const int64_t seg_end = min(kb_end, static_cast<int64_t>(t + 1) * a.kblocks);
+        const int ab = seg & 1;
+        if (!mbar_wait(&acce[ab], ((seg >> 1) & 1) ^ 1, abort_flag, a.err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(ab * BN);
+        for (int64_t g = kb; g < seg_end; ++g, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag, a.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = umma_desc_sw128(smem_u32(sA + s * A_STAGE));
+          const uint64_t bd = umma_desc_sw128(smem_u32(sB + s * B_STAGE));
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_bf16(d, ad + 2 * kk, bd + 2 * kk, IDESC, (g > kb || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&accf[ab]);
+        kb = seg_end;
+        ++seg;
+      }
+      // Drain: every MMA issued above has completed before TMEM is released.
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, a.err);
+    }
+  } else {
+    // Epilogue warps 2..5: warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31.
+    pdl_wait();
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int e = threadIdx.x - 64;
+    int seg = 0;
+    int64_t kb = kb_begin;
+    while (kb < kb_end) {
+      const int t = static_cast<int>(kb / a.kblocks);
+      const int64_t tile_lo = static_cast<int64_t>(t) * a.kblocks;
+      const int64_t seg_end = min(kb_end, tile_lo + a.kblocks);
+      const int ab = seg & 1;
+      if (!mbar_wait(&accf[ab], (seg >> 1) & 1, abort_flag, a.err)) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(ab * BN);
+      const bool full_tile = (kb == tile_lo) && (seg_end == tile_lo + a.kblocks);
+      if (full_tile) {
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld_x32(tb + c0, r);
+          tmem_ld_wait();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          epilogue_store<BN>(a, v, t, row, c0, xbuf);
+        }
+      } else {
+        const int slot = seg == 0 ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
+        float* part = a.partials + static_cast<int64_t>(slot) * BN * BM;
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld_x32(tb + c0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) __stcg(part + (c0 + j) * BM + row, __uint_as_float(r[j]));
+        }
+        __threadfence();
+        epi_bar();
+        if (e == 0) {
+          const int c_first = cta_of(tile_lo, total, G);
+          const int c_last = cta_of(tile_lo + a.kblocks - 1, total, G);
+          const int old = atomicAdd(&a.counters[t], 1);
+          const int last = (old == c_last - c_first);
+          if (last) __threadfence();
+          *last_flag = last;
+        }
+        epi_bar();
+        if (*last_flag) {
+          const int c_first = cta_of(tile_lo, total, G);
+          const int c_last = cta_of(tile_lo + a.kblocks - 1, total, G);
+          for (int c0 = 0; c0 < BN; c0 += 32) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+            for (int c = c_first; c <= c_last; ++c) {
+              const int sl = range_start(c, total, G) >= tile_lo ? 2 * c : 2 * c + 1;
+              const float* p = a.partials + static_cast<int64_t>(sl) * BN * BM;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += __ldcg(p + (c0 + j) * BM + row);
+            }
+            epilogue_store<BN>(a, v, t, row, c0, xbuf);
+          }
+          if (e == 0) a.counters[t] = 0;
+        }
+        epi_bar();
+      }
+      tc_fence_before();
+      mbar_arrive(&acce[ab]);
+      kb = seg_end;
+      ++seg;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 0 && lane == 0) {
+    // Wait (bounded) for the copies still in flight when a wait gave up.
+    const int first = issued > STAGES ? issued - STAGES : 0;
+    for (int it = first; it < issued; ++it) mbar_wait(&full[it % STAGES], (it / STAGES) & 1, nullptr, a.err);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+template <int BN>
+constexpr int stages_for() {
+  return BN == 64 ? 8 : (BN == 128 ? 6 : 4);
+}
+
+template <int BN>
+size_t smem_for() {
+  return static_cast<size_t>(stages_for<BN>()) * (A_STAGE + BN * BK * 2) + 256 + 64 * 33 * 4 + 1024;
+}
+
+int bn_for(int64_t m) { return m <= 64 ? 64 : (m <= 128 ? 128 : 256); }
+
+int64_t tiles_for(int64_t n, int epilogue) {
+  return epilogue == MVB_EPI_SWIGLU ? (n / 2 + 63) / 64 : (n + BM - 1) / BM;
+}
+
+int64_t counters_bytes(int64_t tiles) { return (tiles * 4 + 255) / 256 * 256; }
+
+template <int BN>
+int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, int grid, cudaStream_t st) {
+  constexpr int S = stages_for<BN>();
+  const size_t smem = smem_for<BN>();
+  // Once per device and instantiation, so no attribute call happens during graph capture.
+  static unsigned long long done_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !(done_mask & (1ull << dev))) {
+    MVB_TRY(set_smem(gemm_bf16_kernel<BN, S>, smem, "gemm: smem attribute"));
+    if (dev < 64) done_mask |= 1ull << dev;
+  }
+  return launch("gemm_bf16", gemm_bf16_kernel<BN, S>, dim3(grid), dim3(kThreads), smem, st, tw, tx, a);
+}
+
+}  // namespace
+}  // namespace mvb
+
+using namespace mvb;
+
+extern "C" int64_t mvb_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int device) {
+  (void)k;
+  int sms = mvb_num_sms(device);
+  if (sms <= 0) sms = 148;
+  const int64_t bn = bn_for(m);
+  // Counters sized for the larger of the two tilings (plain / SWIGLU pairs).
+  const int64_t tiles = (n + 63) / 64;
+  return counters_bytes(tiles) + 2LL * sms * bn * BM * 4;
+}
+
+extern "C" int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                             int64_t m, int64_t n, int64_t k, int epilogue, const void* aux, int64_t ld_aux,
+                             void* workspace, int64_t workspace_bytes, mvb_stream_t stream) {
+  MVB_REQUIRE(y && x && w && workspace, "mvb_gemm_bf16: null pointer");
+  MVB_REQUIRE(m > 0 && m <= 256, "mvb_gemm_bf16: m=%lld outside [1, 256]", (long long)m);
+  MVB_REQUIRE(n > 0 && n < (1LL << 31) && k > 0 && k % BK == 0, "mvb_gemm_bf16: need k %% 64 == 0 (k=%lld)",
+              (long long)k);
+  MVB_REQUIRE(ldx >= k && ldw >= k && ldx % 8 == 0 && ldw % 8 == 0, "mvb_gemm_bf16: ldx/ldw must be >= k, %% 8");
+  MVB_REQUIRE(aligned(x, 16) && aligned(w, 16), "mvb_gemm_bf16: x and w must be 16-byte aligned");
+  MVB_REQUIRE(epilogue == MVB_EPI_STORE || epilogue == MVB_EPI_SWIGLU || epilogue == MVB_EPI_RESADD,
+              "mvb_gemm_bf16: bad epilogue %d", epilogue);
+  MVB_REQUIRE(epilogue != MVB_EPI_RESADD || (aux != nullptr && ld_aux >= n), "mvb_gemm_bf16: RESADD needs aux");
+  MVB_REQUIRE(epilogue != MVB_EPI_SWIGLU || n % 2 == 0, "mvb_gemm_bf16: SWIGLU needs an even n (= 2*inter)");
+  const int64_t out_cols = epilogue == MVB_EPI_SWIGLU ? n / 2 : n;
+  MVB_REQUIRE(ldy >= out_cols, "mvb_gemm_bf16: ldy < output columns");
+  const int sms = current_sm_count();
+  MVB_REQUIRE(sms > 0, "mvb_gemm_bf16: no device");
+  const int bn = bn_for(m);
+  const int64_t tiles = tiles_for(n, epilogue);
+  const int64_t kblocks = k / BK;
+  const int64_t total = tiles * kblocks;
+  const int grid = static_cast<int>(total < sms ? total : sms);
+  const int64_t need = counters_bytes((n + 63) / 64) + 2LL * grid * bn * BM * 4;
+  MVB_REQUIRE(workspace_bytes >= need, "mvb_gemm_bf16: workspace %lld < %lld bytes", (long long)workspace_bytes,
+              (long long)need);
+  MVB_REQUIRE(aligned(workspace, 256), "mvb_gemm_bf16: workspace must be 256-byte aligned");
+
+  CUtensorMap tw, tx;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldw) * 2};
+    const uint32_t box[2] = {BK, static_cast<uint32_t>(epilogue == MVB_EPI_SWIGLU ? 64 : BM)};
+    MVB_TRY(encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldx) * 2};
+    const uint32_t box[2] = {BK, static_cast<uint32_t>(bn)};
+    MVB_TRY(encode_tiled(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  GemmArgs a;
+  a.y = static_cast<__nv_bfloat16*>(y);
+  a.ldy = ldy;
+  a.aux = static_cast<const __nv_bfloat16*>(aux);
+  a.ld_aux = ld_aux;
+  a.m = static_cast<int>(m);
+  a.n = static_cast<int>(n);
+  a.k = static_cast<int>(k);
+  a.tiles = static_cast<int>(tiles);
+  a.kblocks = static_cast<int>(kblocks);
+  a.epilogue = epilogue;
+  a.inter = static_cast<int>(n / 2);
+  a.counters = static_cast<int*>(workspace);
+  a.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + counters_bytes((n + 63) / 64));
+  a.err = device_status_ptr();
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (bn) {
+    case 64: return launch_gemm<64>(tw, tx, a, grid, st);
+    case 128: return launch_gemm<128>(tw, tx, a, grid, st);
+    default: return launch_gemm<256>(tw, tx, a, grid, st);
+  }
+}

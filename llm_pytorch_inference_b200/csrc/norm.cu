@@ -1,0 +1,144 @@
+// RMSNorm family: rmsnorm, rmsnorm_plus_one, fused residual-add + RMSNorm.
+//
+// One CTA per row; fp32 sum of squares reduced across the whole CTA and broadcast
+// to every warp (the reference's block_reduce_sum leaves the result in warp 0
+// only, csrc/include/mini_vllm/utils.cuh:27-30).  The rounding sequence of each
+// variant reproduces the PyTorch expression it replaces:
+//   ops      (ops/rmsnorm.py:12-20)  y = T( T(w*x) * r )
+//   ops +1   (ops/rmsnorm.py:23-31)  y = T( (1+w) * (x*r) )
+//   ops +1 fused (ops/rmsnorm.py:51) y = T( ((1+w)*x) * r )
+//   model    (models/model.py:19-25) y = T( w * (x*r) )       model +1: T( (x*r) * (1+w) )
+// with r = 1/sqrt(mean(x^2) + eps) in fp32 and T() rounding to the storage type.
+#include "common.cuh"
+#include "host.h"
+
+namespace mvb {
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float norm_out(float x, float w, float r, int plus_one, int semantics, bool fused) {
+  if (semantics == MVB_NORM_OPS) {
+    if (!plus_one) return rnd<T>(rnd<T>(w * x) * r);
+    if (fused) return rnd<T>(((1.0f + w) * x) * r);
+    return rnd<T>((1.0f + w) * (x * r));
+  }
+  if (!plus_one) return rnd<T>(w * (x * r));
+  return rnd<T>((x * r) * (1.0f + w));
+}
+
+// CTA-wide sum broadcast to all threads.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = (blockDim.x + 31) >> 5;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : 0.0f;
+  t = warp_sum(t);
+  __syncthreads();
+  return t;
+}
+
+template <typename T>
+__global__ void rmsnorm_kernel(T* __restrict__ out, int64_t out_stride, const T* __restrict__ in, int64_t in_stride,
+                               const T* __restrict__ w, int hidden, float eps, int plus_one, int semantics) {
+  __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait();
+  const T* x = in + blockIdx.x * in_stride;
+  T* y = out + blockIdx.x * out_stride;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    float v = to_f<T>(x[i]);
+    ss += v * v;
+  }
+  ss = block_sum(ss, red);
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(hidden) + eps);
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x)
+    y[i] = from_f<T>(norm_out<T>(to_f<T>(x[i]), to_f<T>(w[i]), r, plus_one, semantics, false));
+}
+
+template <typename T>
+__global__ void fused_add_rmsnorm_kernel(T* __restrict__ out, T* __restrict__ residual, const T* __restrict__ in,
+                                         const T* __restrict__ w, int hidden, float eps, int plus_one,
+                                         int semantics) {
+  __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait();
+  T* res = residual + static_cast<int64_t>(blockIdx.x) * hidden;
+  const T* x = in + static_cast<int64_t>(blockIdx.x) * hidden;
+  T* y = out + static_cast<int64_t>(blockIdx.x) * hidden;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    float v = rnd<T>(to_f<T>(res[i]) + to_f<T>(x[i]));
+    res[i] = from_f<T>(v);
+    ss += v * v;
+  }
+  ss = block_sum(ss, red);
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(hidden) + eps);
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x)
+    y[i] = from_f<T>(norm_out<T>(to_f<T>(res[i]), to_f<T>(w[i]), r, plus_one, semantics, true));
+}
+
+int threads_for(int64_t hidden) {
+  int t = static_cast<int>(((hidden + 3) / 4 + 31) / 32 * 32);
+  return t < 64 ? 64 : (t > 1024 ? 1024 : t);
+}
+
+}  // namespace
+}  // namespace mvb
+
+using namespace mvb;
+
+extern "C" int mvb_rmsnorm(void* out, int64_t out_stride, const void* in, int64_t in_stride, const void* weight,
+                           int64_t rows, int64_t hidden, float eps, int plus_one, int semantics, int dtype,
+                           mvb_stream_t stream) {
+  MVB_REQUIRE(out && in && weight, "mvb_rmsnorm: null pointer");
+  MVB_REQUIRE(rows >= 0 && hidden > 0 && hidden <= (1 << 20), "mvb_rmsnorm: bad shape rows=%lld hidden=%lld",
+              (long long)rows, (long long)hidden);
+  MVB_REQUIRE(out_stride >= hidden && in_stride >= hidden, "mvb_rmsnorm: stride < hidden");
+  MVB_REQUIRE(semantics == MVB_NORM_OPS || semantics == MVB_NORM_MODEL, "mvb_rmsnorm: bad semantics %d", semantics);
+  if (rows == 0) return MVB_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  dim3 grid(static_cast<unsigned>(rows)), block(threads_for(hidden));
+  switch (dtype) {
+    case MVB_F32:
+      return launch("rmsnorm", rmsnorm_kernel<float>, grid, block, 0, st, (float*)out, out_stride, (const float*)in,
+                    in_stride, (const float*)weight, (int)hidden, eps, plus_one, semantics);
+    case MVB_F16:
+      return launch("rmsnorm", rmsnorm_kernel<__half>, grid, block, 0, st, (__half*)out, out_stride,
+                    (const __half*)in, in_stride, (const __half*)weight, (int)hidden, eps, plus_one, semantics);
+    case MVB_BF16:
+      return launch("rmsnorm", rmsnorm_kernel<__nv_bfloat16>, grid, block, 0, st, (__nv_bfloat16*)out, out_stride,
+                    (const __nv_bfloat16*)in, in_stride, (const __nv_bfloat16*)weight, (int)hidden, eps, plus_one,
+                    semantics);
+    default:
+      return fail(MVB_ERR_INVALID_ARG, "mvb_rmsnorm: unsupported dtype %d", dtype);
+  }
+}
+
+extern "C" int mvb_fused_add_rmsnorm(void* out, void* residual, const void* in, const void* weight, int64_t rows,
+                                     int64_t hidden, float eps, int plus_one, int semantics, int dtype,
+                                     mvb_stream_t stream) {
+  MVB_REQUIRE(out && residual && in && weight, "mvb_fused_add_rmsnorm: null pointer");
+  MVB_REQUIRE(rows >= 0 && hidden > 0 && hidden <= (1 << 20), "mvb_fused_add_rmsnorm: bad shape");
+  MVB_REQUIRE(semantics == MVB_NORM_OPS || semantics == MVB_NORM_MODEL, "mvb_fused_add_rmsnorm: bad semantics");
+  if (rows == 0) return MVB_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  dim3 grid(static_cast<unsigned>(rows)), block(threads_for(hidden));
+  switch (dtype) {
+    case MVB_F32:
+      return launch("fused_add_rmsnorm", fused_add_rmsnorm_kernel<float>, grid, block, 0, st, (float*)out,
+                    (float*)residual, (const float*)in, (const float*)weight, (int)hidden, eps, plus_one, semantics);
+    case MVB_F16:
+      return launch("fused_add_rmsnorm", fused_add_rmsnorm_kernel<__half>, grid, block, 0, st, (__half*)out,
+                    (__half*)residual, (const __half*)in, (const __half*)weight, (int)hidden, eps, plus_one,
+                    semantics);
+    case MVB_BF16:
+      return launch("fused_add_rmsnorm", fused_add_rmsnorm_kernel<__nv_bfloat16>, grid, block, 0, st,
+                    (__nv_bfloat16*)out, (__nv_bfloat16*)residual, (const __nv_bfloat16*)in,
+                    (const __nv_bfloat16*)weight, (int)hidden, eps, plus_one, semantics);
+    default:
+      return fail(MVB_ERR_INVALID_ARG, "mvb_fused_add_rmsnorm: unsupported dtype %d", dtype);
+  }
+}

@@ -1,0 +1,152 @@
+// Fused per-head QK RMSNorm + NeoX RoPE + paged KV-cache write for one decode step.
+//
+// Replaces, for a single new token per sequence, the chain
+//   q_norm / k_norm            models/model.py:174-178   (RMSNorm.forward, model.py:19-25)
+//   apply_rotary_pos_emb       models/model.py:184       (q*cos + rotate_half(q)*sin, bf16 ops)
+//   Attention._write_kv_cache  models/model.py:226-243   (kv[l, 0|1, bt[pos//bs], pos%bs] = k|v)
+// One warp per (sequence, head) of the fused q|k|v projection row.  Lane l owns
+// head_dim/32 consecutive elements; its rotate_half partner sits 16 lanes away.
+// The slot of a token is (block_tables[b][pos / bs], pos % bs) exactly as the
+// reference computes it; an out-of-range table index or block id is reported in
+// the device status word and nothing is written for that token.
+#include "common.cuh"
+#include "host.h"
+
+namespace mvb {
+namespace {
+
+template <int D>
+__global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
+    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ kv, const __nv_bfloat16* __restrict__ qkv,
+    int64_t qkv_stride, const __nv_bfloat16* __restrict__ qnw, const __nv_bfloat16* __restrict__ knw,
+    const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t, int64_t table_len,
+    const int32_t* __restrict__ positions, const int32_t* __restrict__ block_tables, int64_t max_blocks, int batch,
+    int nq, int nkv, int64_t layer, int64_t num_blocks, int bs, float eps, unsigned* err) {
+  constexpr int E = D / 32;
+  pdl_launch_dependents();
+  const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int heads = nq + 2 * nkv;
+  if (warp_global >= batch * heads) {
+    pdl_wait();
+    return;
+  }
+  const int b = warp_global / heads;
+  const int h = warp_global - b * heads;
+  const int d0 = lane * E;
+
+  pdl_wait();
+  const __nv_bfloat16* src = qkv + static_cast<int64_t>(b) * qkv_stride + static_cast<int64_t>(h) * D + d0;
+  float x[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) x[e] = __bfloat162float(src[e]);
+
+  const int pos = positions[b];
+  const bool is_q = h < nq, is_k = !is_q && h < nq + nkv;
+
+  // Slot of this token in the paged pool (only K/V heads need it).
+  int64_t dst_off = -1;
+  if (!is_q) {
+    const int64_t bidx = pos / bs;
+    if (pos < 0 || bidx >= max_blocks) {
+      if (lane == 0) report(err, kDevBadPosition);
+      return;
+    }
+    const int64_t blk = block_tables[static_cast<int64_t>(b) * max_blocks + bidx];
+    if (blk < 0 || blk >= num_blocks) {
+      if (lane == 0) report(err, kDevBadBlock);
+      return;
+    }
+    const int kvh = is_k ? h - nq : h - nq - nkv;
+    const int64_t which = is_k ? 0 : 1;
+    dst_off = ((((layer * 2 + which) * num_blocks + blk) * bs + (pos % bs)) * nkv + kvh) * D + d0;
+  }
+
+  if (!is_q && !is_k) {  // V: plain copy into the cache
+#pragma unroll
+    for (int e = 0; e < E; ++e) kv[dst_off + e] = __float2bfloat16_rn(x[e]);
+    return;
+  }
+
+  // Per-head RMSNorm (model semantics: T(w * (x * r))).
+  const __nv_bfloat16* nw = is_q ? qnw : knw;
+  if (nw != nullptr) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss += x[e] * x[e];
+    ss = warp_sum(ss);
+    const float r = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = bf16_round(__bfloat162float(nw[d0 + e]) * (x[e] * r));
+  }
+
+  // RoPE with the model's bf16 cos/sin rows: T(T(x*cos) + T(rot(x)*sin)).
+  float out[E];
+  if (pos < 0 || pos >= table_len) {
+    if (lane == 0) report(err, kDevBadPosition);
+#pragma unroll
+    for (int e = 0; e < E; ++e) out[e] = 0.0f;
+  } else {
+    const __nv_bfloat16* c = cos_t + static_cast<int64_t>(pos) * D + d0;
+    const __nv_bfloat16* s = sin_t + static_cast<int64_t>(pos) * D + d0;
+    const bool low = lane < 16;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
+      const float rot = low ? -partner : partner;
+      const float a = bf16_round(x[e] * __bfloat162float(c[e]));
+      const float bb = bf16_round(rot * __bfloat162float(s[e]));
+      out[e] = a + bb;
+    }
+  }
+
+  if (is_q) {
+    __nv_bfloat16* q = q_out + (static_cast<int64_t>(b) * nq + h) * D + d0;
+#pragma unroll
+    for (int e = 0; e < E; ++e) q[e] = __float2bfloat16_rn(out[e]);
+  } else if (dst_off >= 0) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) kv[dst_off + e] = __float2bfloat16_rn(out[e]);
+  }
+}
+
+}  // namespace
+}  // namespace mvb
+
+using namespace mvb;
+
+extern "C" int mvb_qk_norm_rope_kv_write(void* q_out, void* kv_cache, const void* qkv, int64_t qkv_stride,
+                                         const void* q_norm_w, const void* k_norm_w, const void* cos,
+                                         const void* sin, int64_t table_len, const int32_t* positions,
+                                         const int32_t* block_tables, int64_t max_blocks, int64_t batch,
+                                         int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                                         int64_t num_layers, int64_t layer, int64_t num_blocks, int64_t block_size,
+                                         float eps, mvb_stream_t stream) {
+  MVB_REQUIRE(q_out && kv_cache && qkv && cos && sin && positions && block_tables,
+              "mvb_qk_norm_rope_kv_write: null pointer");
+  MVB_REQUIRE((q_norm_w == nullptr) == (k_norm_w == nullptr),
+              "mvb_qk_norm_rope_kv_write: pass both norm weights or neither");
+  MVB_REQUIRE(batch >= 0 && num_q_heads > 0 && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
+              "mvb_qk_norm_rope_kv_write: bad head counts");
+  MVB_REQUIRE(layer >= 0 && layer < num_layers && num_blocks > 0 && block_size > 0 && max_blocks > 0,
+              "mvb_qk_norm_rope_kv_write: bad cache geometry");
+  MVB_REQUIRE(qkv_stride >= (num_q_heads + 2 * num_kv_heads) * head_dim, "mvb_qk_norm_rope_kv_write: qkv_stride");
+  if (batch == 0) return MVB_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  unsigned* err = device_status_ptr();
+  const int64_t warps = batch * (num_q_heads + 2 * num_kv_heads);
+  dim3 grid(static_cast<unsigned>((warps + 7) / 8)), block(256);
+#define MVB_QKR_LAUNCH(D)                                                                                        \
+  return launch("qk_norm_rope_kv_write", qk_norm_rope_kv_kernel<D>, grid, block, 0, st, (__nv_bfloat16*)q_out,  \
+                (__nv_bfloat16*)kv_cache, (const __nv_bfloat16*)qkv, qkv_stride, (const __nv_bfloat16*)q_norm_w, \
+                (const __nv_bfloat16*)k_norm_w, (const __nv_bfloat16*)cos, (const __nv_bfloat16*)sin, table_len,  \
+                positions, block_tables, max_blocks, (int)batch, (int)num_q_heads, (int)num_kv_heads, layer,     \
+                num_blocks, (int)block_size, eps, err)
+  switch (head_dim) {
+    case 64: MVB_QKR_LAUNCH(64);
+    case 128: MVB_QKR_LAUNCH(128);
+    case 256: MVB_QKR_LAUNCH(256);
+    default: return fail(MVB_ERR_UNSUPPORTED, "mvb_qk_norm_rope_kv_write: head_dim %lld", (long long)head_dim);
+  }
+#undef MVB_QKR_LAUNCH
+}

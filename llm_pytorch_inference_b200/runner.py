@@ -1,0 +1,347 @@
+"""Decode-step runner: one batched decode forward + sampling on the sm_100a kernels.
+
+Replaces the per-step body of ``LLMEngine._run_decode`` (``mini_vllm/engine/engine.py:297-360``):
+the model forward of ``ForCausalLM`` (``models/model.py:412-424``) for one new token
+per sequence over the paged KV pool, then ``Sampler.sample`` for every row.
+
+Everything the step touches is resident on the device and laid out once:
+
+* weights in bf16, the q/k/v projections concatenated into one ``[(Hq+2Hkv)*D, H]``
+  matrix per layer and gate/up into the reference's fused ``cat([gate, up])``
+  (``ops/mlp.py:87-121``);
+* the model's bf16 cos/sin tables, built once exactly as ``RotaryEmbedding`` builds
+  them after ``model.to(bf16)`` (``models/model.py:28-81``);
+* activations, logits and sampled tokens in fixed buffers;
+* per-step metadata (token ids, positions, context lengths, block tables, sampling
+  offset) in one int32 device buffer filled by one host->device copy per step;
+* stream-K / split-KV workspaces (zero-initialised once; the kernels leave them zero).
+
+A step is ~9 kernels per layer.  ``capture()`` records the whole step in one CUDA
+graph; ``replay()`` re-runs it (the host only refreshes the metadata buffer).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _native as N
+from .configs import head_dim, num_kv_heads
+from .kv_cache import KVCacheManager
+
+
+def rope_tables(head_dim_: int, theta: float, length: int, dtype: torch.dtype, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin ``[length, D]`` as the reference's ``RotaryEmbedding`` holds them after
+    ``model.to(dtype)``: fp32 ``inv_freq`` rounded to ``dtype``, position ramp in ``dtype``
+    (``models/model.py:31``, ``:75-80``).  Built on the host, then copied."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim_, 2).float() / head_dim_))
+    inv = inv.to(dtype)
+    t = torch.arange(length, dtype=inv.dtype)
+    freqs = torch.outer(t, inv)
+    emb = torch.cat((freqs, freqs), dim=-1)
+    return emb.cos().to(device).contiguous(), emb.sin().to(device).contiguous()
+
+
+class DecodeWeights:
+    """Per-layer device weights in the layout the decode kernels read."""
+
+    def __init__(self, cfg: dict, sd: dict[str, torch.Tensor], device, dtype=torch.bfloat16):
+        L = cfg["num_hidden_layers"]
+        dev = torch.device(device)
+
+        def get(k):
+            return sd[k].to(device=dev, dtype=dtype).contiguous()
+
+        self.embed = get("model.embed_tokens.weight")
+        self.lm_head = get("lm_head.weight") if "lm_head.weight" in sd else self.embed
+        self.final_norm = get("model.norm.weight")
+        self.qk_norm = cfg.get("_qk_norm", False)
+        self.wqkv, self.wo, self.wgu, self.wdown, self.ln1, self.ln2, self.qn, self.kn = ([] for _ in range(8))
+        for i in range(L):
+            p = f"model.layers.{i}."
+            a = p + "self_attn."
+            self.wqkv.append(torch.cat([get(a + "q_proj.weight"), get(a + "k_proj.weight"),
+                                        get(a + "v_proj.weight")], 0).contiguous())
+            self.wo.append(get(a + "o_proj.weight"))
+            self.wgu.append(torch.cat([get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight")], 0).contiguous())
+            self.wdown.append(get(p + "mlp.down_proj.weight"))
+            self.ln1.append(get(p + "input_layernorm.weight"))
+            self.ln2.append(get(p + "post_attention_layernorm.weight"))
+            if self.qk_norm:
+                self.qn.append(get(a + "q_norm.weight"))
+                self.kn.append(get(a + "k_norm.weight"))
+
+    def nbytes(self) -> int:
+        ts = [self.embed, self.final_norm, *self.wqkv, *self.wo, *self.wgu, *self.wdown, *self.ln1, *self.ln2,
+              *self.qn, *self.kn]
+        if self.lm_head is not self.embed:
+            ts.append(self.lm_head)
+        return sum(t.numel() * t.element_size() for t in ts)
+
+
+class DecodeRunner:
+    def __init__(self, cfg: dict, weights: DecodeWeights, kv: KVCacheManager, max_batch: int, max_model_len: int,
+                 device="cuda", rope_len: int | None = None):
+        self.cfg = cfg
+        self.w = weights
+        self.kv = kv
+        self.dev = torch.device(device)
+        self.B = max_batch
+        self.L = cfg["num_hidden_layers"]
+        self.H = cfg["hidden_size"]
+        self.Hq = cfg["num_attention_heads"]
+        self.Hkv = num_kv_heads(cfg)
+        self.D = head_dim(cfg)
+        self.I = cfg["intermediate_size"]
+        self.V = cfg["vocab_size"]
+        self.eps = float(cfg.get("rms_norm_eps", 1e-6))
+        self.scale = 1.0 / math.sqrt(cfg.get("query_pre_attn_scalar") or self.D)
+        if kv.kv_cache is None or kv.kv_cache.device != self.dev or kv.kv_cache.dtype != torch.bfloat16:
+            raise RuntimeError("DecodeRunner needs a bf16 KV pool on the runner's device")
+        if kv.block_size != 16 or kv.head_dim != self.D or kv.num_heads != self.Hkv or kv.num_layers != self.L:
+            raise RuntimeError("KV pool geometry does not match the model")
+        self.max_blocks = (max_model_len + kv.block_size - 1) // kv.block_size
+        self.P = kv.kv_cache.shape[2]  # includes the scratch block
+        rope_len = rope_len or max(max_model_len, 256)
+        self.cos, self.sin = rope_tables(self.D, float(cfg.get("rope_theta", 10000.0)), rope_len, torch.bfloat16,
+                                         self.dev)
+
+        B, H, dev, bf = self.B, self.H, self.dev, torch.bfloat16
+        qkv_n = (self.Hq + 2 * self.Hkv) * self.D
+        self.residual = torch.zeros(B, H, dtype=bf, device=dev)
+        self.xn = torch.zeros(B, H, dtype=bf, device=dev)
+        self.qkv = torch.zeros(B, qkv_n, dtype=bf, device=dev)
+        self.q = torch.zeros(B, self.Hq, self.D, dtype=bf, device=dev)
+        self.attn = torch.zeros(B, self.Hq * self.D, dtype=bf, device=dev)
+        self.o = torch.zeros(B, H, dtype=bf, device=dev)
+        self.h = torch.zeros(B, self.I, dtype=bf, device=dev)
+        self.mlp = torch.zeros(B, H, dtype=bf, device=dev)
+        self.logits = torch.zeros(B, self.V, dtype=bf, device=dev)
+        self.tokens = torch.zeros(B, dtype=torch.int64, device=dev)
+        # per-row sampling parameters (greedy by default)
+        self.temperature = torch.zeros(B, dtype=torch.float32, device=dev)
+        self.top_k = torch.full((B,), -1, dtype=torch.int32, device=dev)
+        self.top_p = torch.ones(B, dtype=torch.float32, device=dev)
+        self.seed = 0
+
+        # metadata: ids | pos | ctx | offset(int64) | block tables
+        self._o_pos = B
+        self._o_ctx = 2 * B
+        self._o_off = (3 * B + 1) // 2 * 2
+        self._o_bt = self._o_off + 2
+        n_meta = self._o_bt + B * self.max_blocks
+        self.meta = torch.zeros(n_meta, dtype=torch.int32, device=dev)
+        self.meta_host = torch.zeros(n_meta, dtype=torch.int32, pin_memory=True)
+        self.ids = self.meta[0:B]
+        self.pos = self.meta[self._o_pos:self._o_pos + B]
+        self.ctx = self.meta[self._o_ctx:self._o_ctx + B]
+        self.offset = self.meta[self._o_off:self._o_off + 2].view(torch.int64)
+        self.block_tables = self.meta[self._o_bt:].view(B, self.max_blocks)
+        self.tokens_host = torch.zeros(B, dtype=torch.int64, pin_memory=True)
+
+        didx = dev.index if dev.index is not None else torch.cuda.current_device()
+        gemm_ws = max(N.lib().mvb_gemm_workspace_bytes(B, n, k, didx) for n, k in
+                      ((qkv_n, H), (H, self.Hq * self.D), (2 * self.I, H), (H, self.I), (self.V, H)))
+        attn_ws = N.lib().mvb_paged_attention_workspace_bytes(B, self.Hq, self.D, didx)
+        self.gemm_ws = torch.zeros(gemm_ws, dtype=torch.uint8, device=dev)
+        self.attn_ws = torch.zeros(attn_ws, dtype=torch.uint8, device=dev)
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.graph_stream: torch.cuda.Stream | None = None
+
+    # ----------------------------------------------------------------- metadata
+    def set_metadata(self, ids: list[int], positions: list[int], block_tables: list[list[int]], offset: int = 0,
+                     ctx_lens: list[int] | None = None) -> None:
+        """Fills the pinned host mirror for the rows given; the rest are padded rows that
+        write into the pool's scratch block and attend to one token there."""
+        n = len(ids)
+        if n > self.B:
+            raise ValueError(f"batch {n} exceeds the runner's max_batch {self.B}")
+        m = self.meta_host
+        m.zero_()
+        B, mb = self.B, self.max_blocks
+        m[0:n] = torch.tensor(ids, dtype=torch.int32)
+        m[self._o_pos:self._o_pos + n] = torch.tensor(positions, dtype=torch.int32)
+        ctx = ctx_lens if ctx_lens is not None else [p + 1 for p in positions]
+        m[self._o_ctx:self._o_ctx + n] = torch.tensor(ctx, dtype=torch.int32)
+        if n < B:
+            m[self._o_ctx + n:self._o_ctx + B] = 1
+        m[self._o_off:self._o_off + 2] = torch.tensor([offset], dtype=torch.int64).view(torch.int32)
+        bt = m[self._o_bt:].view(B, mb)
+        bt.fill_(self.kv.scratch_block)
+        for i, t in enumerate(block_tables):
+            if len(t) > mb:
+                raise ValueError(f"sequence needs {len(t)} blocks > max_blocks {mb}")
+            bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+
+    def upload_metadata(self) -> None:
+        self.meta.copy_(self.meta_host, non_blocking=True)
+
+    def set_sampling(self, temperature, top_k, top_p, seed: int = 0) -> None:
+        """Per-row (or scalar) sampling parameters; T == 0 rows decode greedily."""
+        self.temperature.copy_(torch.as_tensor(temperature, dtype=torch.float32).expand(self.B))
+        self.top_k.copy_(torch.as_tensor(top_k, dtype=torch.int32).expand(self.B))
+        self.top_p.copy_(torch.as_tensor(top_p, dtype=torch.float32).expand(self.B))
+        self.seed = int(seed)
+        self.graph = None  # the seed is a kernel argument: re-capture
+
+    # ------------------------------------------------------------------- step
+    def _gemm(self, y, x, w, epilogue=N.EPI_STORE, aux=None):
+        lib = N.lib()
+        B = self.B
+        N.check(lib.mvb_gemm_bf16(y.data_ptr(), y.stride(0), x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), B,
+                                  w.shape[0], w.shape[1], epilogue, N.ptr(aux), 0 if aux is None else aux.stride(0),
+                                  self.gemm_ws.data_ptr(), self.gemm_ws.numel(), self._st), "gemm_bf16")
+
+    def forward(self) -> None:
+        """Launches one decode step on the current stream (metadata must be on the device)."""
+        lib, w, B, H = N.lib(), self.w, self.B, self.H
+        self._st = N.stream_handle(self.dev)
+        st, eps, bf = self._st, self.eps, N.BF16
+        kvc = self.kv.kv_cache
+        N.check(lib.mvb_embedding(self.residual.data_ptr(), self.ids.data_ptr(), N.I32, w.embed.data_ptr(), B, H,
+                                  self.V, 1.0, bf, st), "embedding")
+        N.check(lib.mvb_rmsnorm(self.xn.data_ptr(), H, self.residual.data_ptr(), H, w.ln1[0].data_ptr(), B, H, eps, 0,
+                                N.NORM_MODEL, bf, st), "rmsnorm")
+        for i in range(self.L):
+            if i > 0:
+                N.check(lib.mvb_fused_add_rmsnorm(self.xn.data_ptr(), self.residual.data_ptr(), self.mlp.data_ptr(),
+                                                  w.ln1[i].data_ptr(), B, H, eps, 0, N.NORM_MODEL, bf, st),
+                        "fused_add_rmsnorm")
+            self._gemm(self.qkv, self.xn, w.wqkv[i])
+            N.check(lib.mvb_qk_norm_rope_kv_write(
+                self.q.data_ptr(), kvc.data_ptr(), self.qkv.data_ptr(), self.qkv.stride(0),
+                w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
+                self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0], self.pos.data_ptr(),
+                self.block_tables.data_ptr(), self.max_blocks, B, self.Hq, self.Hkv, self.D, self.L, i, self.P,
+                self.kv.block_size, eps, st), "qk_norm_rope_kv_write")
+            N.check(lib.mvb_paged_attention_decode(
+                self.attn.data_ptr(), self.attn.stride(0), self.q.data_ptr(), self.Hq * self.D, kvc.data_ptr(),
+                self.block_tables.data_ptr(), self.max_blocks, self.ctx.data_ptr(), B, self.Hq, self.Hkv, self.D,
+                self.L, i, self.P, self.kv.block_size, self.scale, self.attn_ws.data_ptr(), self.attn_ws.numel(), st),
+                "paged_attention_decode")
+            self._gemm(self.o, self.attn, w.wo[i])
+            N.check(lib.mvb_fused_add_rmsnorm(self.xn.data_ptr(), self.residual.data_ptr(), self.o.data_ptr(),
+                                              w.ln2[i].data_ptr(), B, H, eps, 0, N.NORM_MODEL, bf, st),
+                    "fused_add_rmsnorm")
+            self._gemm(self.h, self.xn, w.wgu[i], N.EPI_SWIGLU)
+            self._gemm(self.mlp, self.h, w.wdown[i])
+        N.check(lib.mvb_fused_add_rmsnorm(self.xn.data_ptr(), self.residual.data_ptr(), self.mlp.data_ptr(),
+                                          w.final_norm.data_ptr(), B, H, eps, 0, N.NORM_MODEL, bf, st),
+                "fused_add_rmsnorm")
+        self._gemm(self.logits, self.xn, w.lm_head)
+        N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
+                               self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
+                               0, self.offset.data_ptr(), bf, st), "sample")
+
+    def kernel_kinds(self) -> dict:
+        """kind -> (launch(layer), launches per step, algorithmic bytes per launch, flops per launch)."""
+        lib, w, B, H, D = N.lib(), self.w, self.B, self.H, self.D
+        st, eps, bf = self._st, self.eps, N.BF16
+        kvc = self.kv.kv_cache
+        ctx = self.ctx.cpu()
+        kv_bytes = int(ctx.sum()) * self.Hkv * D * 2 * 2          # K and V of every attended token
+        qkv_n = (self.Hq + 2 * self.Hkv) * D
+
+        def gemm_bytes(n, k, out_cols):
+            return n * k * 2 + B * k * 2 + B * out_cols * 2
+
+        def qk(i):
+            N.check(lib.mvb_qk_norm_rope_kv_write(
+                self.q.data_ptr(), kvc.data_ptr(), self.qkv.data_ptr(), self.qkv.stride(0),
+                w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
+                self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0], self.pos.data_ptr(),
+                self.block_tables.data_ptr(), self.max_blocks, B, self.Hq, self.Hkv, D, self.L, i, self.P,
+                self.kv.block_size, eps, st), "qk_norm_rope_kv_write")
+
+        def attn(i):
+            N.check(lib.mvb_paged_attention_decode(
+                self.attn.data_ptr(), self.attn.stride(0), self.q.data_ptr(), self.Hq * D, kvc.data_ptr(),
+                self.block_tables.data_ptr(), self.max_blocks, self.ctx.data_ptr(), B, self.Hq, self.Hkv, D,
+                self.L, i, self.P, self.kv.block_size, self.scale, self.attn_ws.data_ptr(), self.attn_ws.numel(),
+                st), "paged_attention_decode")
+
+        def fadd(i):
+            N.check(lib.mvb_fused_add_rmsnorm(self.xn.data_ptr(), self.residual.data_ptr(), self.o.data_ptr(),
+                                              w.ln2[i].data_ptr(), B, H, eps, 0, N.NORM_MODEL, bf, st),
+                    "fused_add_rmsnorm")
+
+        def samp(i):
+            N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
+                                   self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(),
+                                   self.seed, 0, self.offset.data_ptr(), bf, st), "sample")
+
+        return {
+            "paged_attention_decode": (attn, self.L, kv_bytes + 2 * B * self.Hq * D * 2, 4 * int(ctx.sum()) * self.Hq * D),
+            "gemm_qkv": (lambda i: self._gemm(self.qkv, self.xn, w.wqkv[i]), self.L, gemm_bytes(qkv_n, H, qkv_n),
+                         2 * B * qkv_n * H),
+            "gemm_o_proj": (lambda i: self._gemm(self.o, self.attn, w.wo[i]), self.L,
+                            gemm_bytes(H, self.Hq * D, H), 2 * B * H * self.Hq * D),
+            "gemm_gate_up_swiglu": (lambda i: self._gemm(self.h, self.xn, w.wgu[i], N.EPI_SWIGLU), self.L,
+                                    gemm_bytes(2 * self.I, H, self.I), 2 * B * 2 * self.I * H),
+            "gemm_down": (lambda i: self._gemm(self.mlp, self.h, w.wdown[i]), self.L, gemm_bytes(H, self.I, H),
+                          2 * B * H * self.I),
+            "gemm_lm_head": (lambda i: self._gemm(self.logits, self.xn, w.lm_head), 1,
+                             gemm_bytes(self.V, H, self.V), 2 * B * self.V * H),
+            "qk_norm_rope_kv_write": (qk, self.L, B * qkv_n * 2 + B * self.Hq * D * 2 + 2 * B * self.Hkv * D * 2, 0),
+            "fused_add_rmsnorm": (fadd, 2 * self.L, 5 * B * H * 2, 0),
+            "sample": (samp, 1, B * self.V * 2, 0),
+        }
+
+    def time_kernels(self, iters: int = 36) -> dict[str, dict]:
+        """Average device time of each kernel kind: every launch bracketed by CUDA events on
+        the launching stream, rotating over the layers (a working set far larger than L2)."""
+        self._st = N.stream_handle(self.dev)
+        stream = torch.cuda.current_stream(self.dev)
+        out = {}
+        for name, (fn, per_step, nbytes, flops) in self.kernel_kinds().items():
+            fn(0)
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+            torch.cuda.synchronize(self.dev)
+            for it in range(iters):
+                ev[it][0].record(stream)
+                fn(it % self.L)
+                ev[it][1].record(stream)
+            torch.cuda.synchronize(self.dev)
+            ms = sorted(a.elapsed_time(b) for a, b in ev)
+            avg = sum(ms) / len(ms)
+            out[name] = {"avg_ms": avg, "median_ms": ms[len(ms) // 2], "launches_per_step": per_step,
+                         "bytes_per_launch": nbytes, "flops_per_launch": flops,
+                         "gbs": nbytes / (avg * 1e-3) / 1e9}
+        return out
+
+    def launches_per_step(self) -> int:
+        """Kernels one step launches (embedding, rmsnorm, 8 per layer + 1 between layers, norm, lm_head, sample)."""
+        return 2 + self.L * 8 + (self.L - 1) + 3
+
+    # ------------------------------------------------------------------ graphs
+    def capture(self) -> None:
+        """Records one full step in a CUDA graph (metadata and sampling buffers are read at replay)."""
+        torch.cuda.synchronize(self.dev)
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            self.forward()  # warm-up outside the graph: sets function attributes, loads modules
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self.forward()
+        torch.cuda.synchronize(self.dev)
+        self.graph, self.graph_stream = g, s
+
+    def replay(self) -> None:
+        if self.graph is None:
+            self.capture()
+        self.graph.replay()
+
+    def step(self, use_graph: bool = True) -> None:
+        """Metadata upload + one step on the current stream (no host sync)."""
+        self.upload_metadata()
+        if use_graph:
+            self.replay()
+        else:
+            self.forward()
+
+    def fetch_tokens(self) -> torch.Tensor:
+        self.tokens_host.copy_(self.tokens, non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        return self.tokens_host

@@ -1,0 +1,312 @@
+"""Kernel-level parity on the GPU: each sm_100a kernel against the oracle (the reference's
+algorithm restated on the CPU) or a plain fp32 PyTorch reference, at small sizes."""
+import math
+import random
+
+import numpy as np
+import pytest
+import torch
+
+from llm_pytorch_inference_b200 import _native as N
+from llm_pytorch_inference_b200 import ops
+from oracle import model as om
+from oracle import sampling as osamp
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def golden(golden_dir):
+    return torch.load(golden_dir / "ops_golden.pt")
+
+
+@pytest.fixture(autouse=True)
+def _status_clean():
+    N.device_status(clear=True)
+    yield
+    assert N.device_status(clear=True) == 0, "a kernel reported a device-side error"
+
+
+def bf16_ulps(a: torch.Tensor, b: torch.Tensor) -> int:
+    """Max distance in bf16 units in the last place between two bf16 tensors."""
+    ia = a.contiguous().view(torch.int16).to(torch.int32)
+    ib = b.contiguous().view(torch.int16).to(torch.int32)
+    ia = torch.where(ia < 0, -(ia & 0x7FFF), ia)
+    ib = torch.where(ib < 0, -(ib & 0x7FFF), ib)
+    return int((ia - ib).abs().max())
+
+
+# ------------------------------------------------------------------------ norms
+@pytest.mark.parametrize("tag", ["bf16", "f32"])
+def test_rmsnorm_ops_semantics_match_reference_fallback(golden, tag):
+    x, w, res = golden[f"rms_x_{tag}"], golden[f"rms_w_{tag}"], golden[f"rms_res_{tag}"]
+    out = ops.rmsnorm(x.to(DEV), w.to(DEV)).cpu()
+    ref = golden[f"rmsnorm_{tag}"]
+    if tag == "bf16":
+        assert bf16_ulps(out, ref) <= 1
+    else:
+        torch.testing.assert_close(out, ref, rtol=1e-6, atol=1e-6)
+    out = ops.rmsnorm_plus_one(x.to(DEV), w.to(DEV)).cpu()
+    torch.testing.assert_close(out.float(), golden[f"rmsnorm_p1_{tag}"].float(), rtol=1e-2, atol=2e-2)
+    r = res.to(DEV).clone()
+    y, r2 = ops.fused_add_rmsnorm(r, x.to(DEV), w.to(DEV))
+    assert r2.data_ptr() == r.data_ptr()  # residual updated in place (rmsnorm_kernel.cu:187-204)
+    assert torch.equal(r.cpu(), golden[f"fadd_r_{tag}"])
+    torch.testing.assert_close(y.cpu().float(), golden[f"fadd_y_{tag}"].float(), rtol=1e-2, atol=2e-2)
+
+
+def test_rmsnorm_model_semantics_match_oracle():
+    torch.manual_seed(0)
+    x = torch.randn(64, 4096).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(4096)).to(torch.bfloat16)
+    out = torch.empty(64, 4096, dtype=torch.bfloat16, device=DEV)
+    xd, wd = x.to(DEV), w.to(DEV)
+    N.check(N.lib().mvb_rmsnorm(out.data_ptr(), 4096, xd.data_ptr(), 4096, wd.data_ptr(), 64, 4096, 1e-6, 0,
+                                N.NORM_MODEL, N.BF16, N.stream_handle()), "rmsnorm")
+    assert bf16_ulps(out.cpu(), om.rms_norm(x, w, 1e-6)) <= 1
+
+
+# ------------------------------------------------------------------ elementwise
+def test_rope_op_matches_reference(golden):
+    q, k = golden["rope_q"], golden["rope_k"]
+    cos, sin = om.rope_tables(128, 1e6, int(golden["rope_table_len"]), torch.bfloat16)
+    pos = golden["rope_positions"]
+    c, s = cos[pos].unsqueeze(1), sin[pos].unsqueeze(1)
+    qe, ke = ops.apply_rotary_pos_emb(q.to(DEV), k.to(DEV), c.to(DEV), s.to(DEV))
+    assert torch.equal(qe.cpu(), golden["rope_q_out"])
+    assert torch.equal(ke.cpu(), golden["rope_k_out"])
+
+
+def test_activations_embedding_softmax(golden):
+    ax, ay = golden["act_x"].to(DEV), golden["act_y"].to(DEV)
+    for fn, key in ((ops.silu, "silu"), (ops.gelu, "gelu")):
+        assert bf16_ulps(fn(ax).cpu(), golden[key]) <= 1
+    assert bf16_ulps(ops.swiglu(ax, ay).cpu(), golden["swiglu"]) <= 1
+    assert bf16_ulps(ops.geglu(ax, ay).cpu(), golden["geglu"]) <= 1
+    e = ops.embedding(golden["emb_ids"].to(DEV), golden["emb_w"].to(DEV), 1.0).cpu()
+    assert torch.equal(e, golden["emb_out"])
+    e = ops.embedding(golden["emb_ids"].to(DEV), golden["emb_w"].to(DEV), 2.5).cpu()
+    assert torch.equal(e, golden["emb_out_scaled"])
+    sm = ops.softmax(golden["softmax_x"].to(DEV)).cpu()
+    torch.testing.assert_close(sm, golden["softmax_out"], rtol=1e-5, atol=1e-7)
+
+
+def test_embedding_bad_id_is_reported_not_faulted():
+    w = torch.randn(10, 64, device=DEV).to(torch.bfloat16)
+    out = ops.embedding(torch.tensor([3, 11], device=DEV), w)
+    assert torch.equal(out[0], w[3]) and torch.count_nonzero(out[1]) == 0
+    assert N.device_status(clear=True) & N.DEV_BAD_TOKEN
+
+
+def test_fused_mlp_module_matches_reference(golden):
+    mlp = ops.FusedMLP(256, 384, "silu").to(DEV, torch.bfloat16)
+    with torch.no_grad():
+        mlp.gate_up_proj.weight.copy_(golden["mlp_gate_up_w"])
+        mlp.down_proj.weight.copy_(golden["mlp_down_w"])
+    out = mlp(golden["mlp_x"].to(DEV)).cpu()
+    torch.testing.assert_close(out.float(), golden["mlp_out"].float(), rtol=2e-2, atol=2e-2)
+    gu = golden["mlp_x"].float() @ golden["mlp_gate_up_w"].float().T
+    h = ops.fused_mlp_forward(gu.to(torch.bfloat16).to(DEV), 384, 0).cpu()
+    g, u = gu.to(torch.bfloat16).chunk(2, -1)
+    assert bf16_ulps(h, torch.nn.functional.silu(g) * u) <= 1
+
+
+# ------------------------------------------------------------------------- GEMM
+@pytest.mark.parametrize("m,n,k", [(64, 4096, 4096), (64, 6144, 4096), (1, 512, 512), (37, 1000, 128),
+                                   (128, 2048, 1024), (256, 256, 8192), (64, 151936, 256)])
+def test_gemm_store_matches_fp32(m, n, k):
+    g = torch.Generator(device=DEV).manual_seed(m * 7 + n + k)
+    x = (torch.randn(m, k, device=DEV, generator=g) / math.sqrt(k)).to(torch.bfloat16)
+    w = torch.randn(n, k, device=DEV, generator=g).to(torch.bfloat16)
+    y = ops.linear(x, w)
+    ref = x.float() @ w.float().T
+    torch.testing.assert_close(y.float(), ref, rtol=1e-2, atol=1e-2)
+    assert torch.equal(ops.linear(x, w), y)  # deterministic split-K merge
+
+
+def test_gemm_swiglu_and_resadd_epilogues():
+    g = torch.Generator(device=DEV).manual_seed(3)
+    m, inter, k = 64, 1536, 2048
+    x = (torch.randn(m, k, device=DEV, generator=g) / math.sqrt(k)).to(torch.bfloat16)
+    w = torch.randn(2 * inter, k, device=DEV, generator=g).to(torch.bfloat16)
+    h = ops.linear(x, w, N.EPI_SWIGLU)
+    gu = (x.float() @ w.float().T).to(torch.bfloat16)
+    gate, up = gu[:, :inter], gu[:, inter:]
+    ref = (torch.nn.functional.silu(gate.float()).to(torch.bfloat16).float() * up.float())
+    torch.testing.assert_close(h.float(), ref, rtol=2e-2, atol=2e-2)
+    aux = torch.randn(m, 1024, device=DEV, generator=g).to(torch.bfloat16)
+    w2 = torch.randn(1024, k, device=DEV, generator=g).to(torch.bfloat16)
+    y = ops.linear(x, w2, N.EPI_RESADD, aux=aux)
+    ref = aux.float() + (x.float() @ w2.float().T).to(torch.bfloat16).float()
+    torch.testing.assert_close(y.float(), ref, rtol=1e-2, atol=2e-2)
+
+
+# ------------------------------------------------- QK-norm + RoPE + paged KV write
+def _pool(L, P, nkv, D, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(L, 2, P + 1, 16, nkv, D, generator=g).to(torch.bfloat16)
+
+
+def test_qk_norm_rope_kv_write_indexing_is_bit_exact():
+    B, Hq, Hkv, D, L, P, layer = 6, 8, 4, 128, 3, 40, 1
+    rng = random.Random(0)
+    order = list(range(P))
+    rng.shuffle(order)
+    lens = [1, 15, 16, 17, 100, 33]       # positions cross block boundaries
+    bts, it = [], iter(order)
+    for n in lens:
+        bts.append([next(it) for _ in range((n + 15) // 16)])
+    mb = max(len(b) for b in bts)
+    bt = torch.full((B, mb), P, dtype=torch.int32)
+    for i, b in enumerate(bts):
+        bt[i, :len(b)] = torch.tensor(b)
+    pos = torch.tensor([n - 1 for n in lens], dtype=torch.int32)
+    g = torch.Generator().manual_seed(1)
+    qkv = torch.randn(B, (Hq + 2 * Hkv) * D, generator=g).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16)
+    cos, sin = om.rope_tables(D, 1e6, 256, torch.bfloat16)
+    pool = _pool(L, P, Hkv, D, 2)
+    pool_d = pool.to(DEV)
+    q = ops.qk_norm_rope_kv_write(qkv.to(DEV), pool_d, layer, pos.to(DEV), bt.to(DEV), cos.to(DEV), sin.to(DEV),
+                                  Hq, Hkv, qn.to(DEV), kn.to(DEV), 1e-6)
+    # oracle: model.py:170-184 then _write_kv_cache (model.py:226-243)
+    qo = qkv[:, :Hq * D].view(B, 1, Hq, D)
+    ko = qkv[:, Hq * D:(Hq + Hkv) * D].view(B, 1, Hkv, D)
+    vo = qkv[:, (Hq + Hkv) * D:].view(B, 1, Hkv, D).transpose(1, 2)
+    qo = om.rms_norm(qo, qn, 1e-6).transpose(1, 2)
+    ko = om.rms_norm(ko, kn, 1e-6).transpose(1, 2)
+    c, s = cos[pos.long()].unsqueeze(1).unsqueeze(1), sin[pos.long()].unsqueeze(1).unsqueeze(1)
+    qo, ko = om.apply_rope(qo, c, s), om.apply_rope(ko, c, s)
+    expect = pool.clone()
+    om.OracleDecoder.write_kv(expect, ko, vo, bts, pos.tolist(), layer)
+    got = pool_d.cpu()
+    changed_got = (got != pool).flatten(4).any(-1)
+    changed_exp = (expect != pool).flatten(4).any(-1)
+    assert torch.equal(changed_got, changed_exp)          # exactly the same slots written
+    assert bf16_ulps(got, expect) <= 1
+    assert bf16_ulps(q.cpu(), qo[:, :, 0]) <= 1
+
+
+def test_kv_write_bad_block_is_reported_not_faulted():
+    B, Hq, Hkv, D, L, P = 2, 4, 2, 128, 1, 8
+    pool = torch.zeros(L, 2, P + 1, 16, Hkv, D, dtype=torch.bfloat16, device=DEV)
+    bt = torch.tensor([[3], [P + 5]], dtype=torch.int32, device=DEV)   # second row: block id out of range
+    pos = torch.tensor([0, 0], dtype=torch.int32, device=DEV)
+    qkv = torch.randn(B, (Hq + 2 * Hkv) * D, device=DEV).to(torch.bfloat16)
+    cos, sin = om.rope_tables(D, 1e6, 256, torch.bfloat16)
+    ops.qk_norm_rope_kv_write(qkv, pool, 0, pos, bt, cos.to(DEV), sin.to(DEV), Hq, Hkv)
+    assert N.device_status(clear=True) & N.DEV_BAD_BLOCK
+    assert torch.count_nonzero(pool[0, :, 3]) > 0
+
+
+# ------------------------------------------------------------ paged attention
+def _attention_ref(q, pool, layer, bts, ctx, scale):
+    """fp32 restatement of _read_kv_cache_batch + SDPA (model.py:191-221)."""
+    B, Hq, D = q.shape
+    Hkv = pool.shape[4]
+    out = torch.empty(B, Hq, D)
+    for b in range(B):
+        k = torch.cat([pool[layer, 0, blk] for blk in bts[b]], 0)[:ctx[b]].float()   # [ctx, Hkv, D]
+        v = torch.cat([pool[layer, 1, blk] for blk in bts[b]], 0)[:ctx[b]].float()
+        k = k.repeat_interleave(Hq // Hkv, dim=1)
+        v = v.repeat_interleave(Hq // Hkv, dim=1)
+        s = torch.einsum("hd,thd->ht", q[b].float(), k) * scale
+        p = torch.softmax(s, -1)
+        out[b] = torch.einsum("ht,thd->hd", p, v)
+    return out
+
+
+@pytest.mark.parametrize("Hq,Hkv,lens", [
+    (32, 8, [2049] * 4 + [1, 16, 17, 300]),     # Qwen3-8B heads, mixed lengths incl. 1 token
+    (16, 8, [129, 5, 64]),                      # Qwen3-0.6B heads
+    (8, 4, [37, 50, 16, 64]),
+    (32, 4, [700, 33]),                         # group 8 (Qwen3-30B-A3B heads)
+    (4, 1, [513, 2, 31]),                       # one KV head per rank (TP=8 shard)
+])
+def test_paged_attention_matches_fp32_reference(Hq, Hkv, lens):
+    D, L, layer = 128, 2, 1
+    total_blocks = sum((n + 15) // 16 for n in lens)
+    P = total_blocks + 7
+    order = list(range(P))
+    random.Random(5).shuffle(order)
+    it = iter(order)
+    bts = [[next(it) for _ in range((n + 15) // 16)] for n in lens]
+    mb = max(len(b) for b in bts)
+    bt = torch.full((len(lens), mb), P, dtype=torch.int32)
+    for i, b in enumerate(bts):
+        bt[i, :len(b)] = torch.tensor(b)
+    pool = _pool(L, P, Hkv, D, 9)
+    g = torch.Generator().manual_seed(4)
+    q = torch.randn(len(lens), Hq, D, generator=g).to(torch.bfloat16)
+    scale = 1.0 / math.sqrt(D)
+    out = ops.paged_attention_decode(q.to(DEV), pool.to(DEV), layer, bt.to(DEV),
+                                     torch.tensor(lens, dtype=torch.int32, device=DEV), scale)
+    ref = _attention_ref(q, pool, layer, bts, lens, scale)
+    torch.testing.assert_close(out.cpu().float(), ref, rtol=2e-2, atol=1e-2)
+    out2 = ops.paged_attention_decode(q.to(DEV), pool.to(DEV), layer, bt.to(DEV),
+                                      torch.tensor(lens, dtype=torch.int32, device=DEV), scale)
+    assert torch.equal(out, out2)  # deterministic split-KV merge
+
+
+# --------------------------------------------------------------------- sampling
+def test_greedy_matches_torch_argmax(golden):
+    logits = golden["samp_logits_bf16"]
+    for t in (logits, logits.float()):
+        assert torch.equal(ops.greedy_sample(t.to(DEV)).cpu(), golden["greedy"])
+
+
+@pytest.mark.parametrize("k,p", [(50, 0.95), (50, 1.0), (1, 1.0), (5, 0.5), (0, 0.9)])
+def test_filter_matches_oracle(golden, k, p):
+    logits = golden["samp_logits_bf16"].float()
+    got = torch.isfinite(ops.top_k_top_p_filter(logits.to(DEV), k, p).cpu())
+    exp = torch.isfinite(osamp.top_k_top_p_filter(logits, k, p, stable=True))
+    for r in range(logits.shape[0]):
+        if not torch.equal(got[r], exp[r]):
+            # only a cutoff within float rounding of top_p may differ: same values kept up to one token
+            assert abs(int(got[r].sum()) - int(exp[r].sum())) <= 1, (r, k, p)
+    ref_keep = np.unpackbits(golden[f"filter_k{k}_p{int(p * 100)}_kept_bits"].numpy(), axis=-1)[:, :logits.shape[1]]
+    assert np.array_equal(got.sum(-1).numpy(), ref_keep.sum(-1))  # same count as the reference itself
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_sample_matches_oracle_draw(golden, dt):
+    logits = golden["samp_logits_bf16"].float()
+    V = logits.shape[1]
+    x = logits.to(dt).to(DEV)
+    mismatches = 0
+    for seed in range(6):
+        for (T, k, p) in ((0.8, 50, 0.95), (1.0, -1, 1.0), (0.7, -1, 0.9), (0.0, 50, 0.95), (1.3, 5, 1.0)):
+            probs = torch.empty(4, V, device=DEV)
+            tok = ops.sample(x, T, k, p, seed, 17, probs_out=probs).cpu()
+            for r in range(4):
+                exp, margin = osamp.sample_row(logits[r], T, k, p, seed, r, 17)
+                if int(tok[r]) != exp:
+                    assert margin < 1e-5, (seed, T, k, p, r, int(tok[r]), exp, margin)
+                    mismatches += 1
+            if T > 0:
+                ref = osamp.gpu_semantics_probs(logits.double(), T, k, p)
+                torch.testing.assert_close(probs.cpu().double(), ref, rtol=1e-4, atol=1e-7)
+    assert mismatches <= 1
+
+
+def test_softmax_multinomial_follows_torch_seed(golden):
+    logits = golden["samp_logits_bf16"].float().to(DEV)
+    torch.manual_seed(123)
+    a = ops.softmax_multinomial_sample(logits, 0.8)
+    b = ops.softmax_multinomial_sample(logits, 0.8)
+    torch.manual_seed(123)
+    c = ops.softmax_multinomial_sample(logits, 0.8)
+    assert torch.equal(a, c)
+    assert 0 <= int(a.min()) and int(a.max()) < logits.shape[1]
+    del b
+
+
+def test_sample_distribution_is_statistically_right():
+    V, rows = 8, 4096
+    logits = torch.tensor([2.0, 1.0, 0.5, 0.0, -1.0, 0.3, 1.7, -0.2]).repeat(rows, 1).to(DEV)
+    tok = ops.sample(logits, 1.0, -1, 1.0, seed=11, offset=0)
+    freq = torch.bincount(tok.cpu(), minlength=V).double() / rows
+    p = torch.softmax(logits[0].double().cpu(), -1)
+    assert float((freq - p).abs().max()) < 0.03
