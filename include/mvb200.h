@@ -158,8 +158,8 @@ int mvb_qk_norm_rope_kv_write(void* q_out, void* kv_cache, const void* qkv, int6
  * softmax(q[b,h] . K[b, :ctx_lens[b]]^T * scale) V, reading K/V straight out of the
  * paged pool through block_tables.  q/out: [B, Hq, D] bf16 (row stride in elements
  * q_stride / out_stride between sequences).  Split-KV across the whole GPU with a
- * deterministic merge.  workspace: >= mvb_paged_attention_workspace_bytes(); its
- * counter region must be zero before the first call (the kernel leaves it zero). */
+ * deterministic merge.  workspace: >= mvb_paged_attention_workspace_bytes(), zero before
+ * the first call (partials at its head, per-sequence counters at its tail, left zero). */
 int64_t mvb_paged_attention_workspace_bytes(int64_t batch, int64_t num_q_heads, int64_t head_dim, int device);
 int mvb_paged_attention_decode(void* out, int64_t out_stride, const void* q, int64_t q_stride,
                                const void* kv_cache, const int32_t* block_tables, int64_t max_blocks,
@@ -177,7 +177,10 @@ int mvb_paged_attention_decode(void* out, int64_t out_stride, const void* q, int
  *                          bf16(bf16(silu(bf16(gate))) * bf16(up)), j < inter (model.py:116-117)
  *           MVB_EPI_RESADD Y = bf16(aux[m, n] + bf16(acc)) (residual add, model.py:319/328)
  * Requires k % 64 == 0, ldx/ldw/ldy multiples of 8, 16-byte aligned pointers, m <= 256.
- * workspace: >= mvb_gemm_workspace_bytes(m, n, k, device); zero before the first call. */
+ * workspace: >= mvb_gemm_workspace_bytes(m, n, k, device); zero before the first call.  fp32
+ * partials use its head, per-tile counters its tail; the kernel leaves the counters zero, so
+ * one buffer serves any number of calls on one stream.  Calls of different shapes may share
+ * a buffer sized for the largest partial area plus the largest counter area among them. */
 #define MVB_EPI_STORE 0
 #define MVB_EPI_SWIGLU 1
 #define MVB_EPI_RESADD 2

@@ -461,9 +461,13 @@ extern "C" int mvb_paged_attention_decode(void* out, int64_t out_stride, const v
   const int64_t group = num_q_heads / num_kv_heads;
   const int sms = current_sm_count();
   MVB_REQUIRE(sms > 0, "mvb_paged_attention_decode: no device");
-  const int64_t need = attn_counters_bytes(batch) + 2LL * sms * num_q_heads * 8 + 2LL * sms * num_q_heads * D * 4;
-  MVB_REQUIRE(workspace_bytes >= need, "mvb_paged_attention_decode: workspace %lld < %lld",
-              (long long)workspace_bytes, (long long)need);
+  // Partials at the head, per-sequence counters at the tail (nested suffixes across calls
+  // of different batch sizes sharing one buffer; the kernel leaves them zero).
+  const int64_t ws_end = workspace_bytes / 256 * 256;
+  const int64_t cbytes = attn_counters_bytes(batch);
+  const int64_t need = cbytes + 2LL * sms * num_q_heads * 8 + 2LL * sms * num_q_heads * D * 4;
+  MVB_REQUIRE(ws_end >= need, "mvb_paged_attention_decode: workspace %lld < %lld", (long long)workspace_bytes,
+              (long long)need);
 
   CUtensorMap tm;
   int per_head = 0;
@@ -483,9 +487,9 @@ extern "C" int mvb_paged_attention_decode(void* out, int64_t out_stride, const v
   a.num_blocks = num_blocks;
   a.scale_log2 = scale * kLog2e;
   char* ws = static_cast<char*>(workspace);
-  a.counters = reinterpret_cast<int*>(ws);
-  a.partial_ml = reinterpret_cast<float2*>(ws + attn_counters_bytes(batch));
-  a.partial_o = reinterpret_cast<float*>(ws + attn_counters_bytes(batch) + 2LL * sms * num_q_heads * 8);
+  a.partial_ml = reinterpret_cast<float2*>(ws);
+  a.partial_o = reinterpret_cast<float*>(ws + 2LL * sms * num_q_heads * 8);
+  a.counters = reinterpret_cast<int*>(ws + ws_end - cbytes);
   a.err = device_status_ptr();
   a.per_head_tma = per_head;
   // Grid: one persistent CTA per SM (192 KB of stages each); never more CTAs than blocks.

@@ -374,7 +374,7 @@ extern "C" int64_t mvb_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int
   const int64_t bn = bn_for(m);
   // Counters sized for the larger of the two tilings (plain / SWIGLU pairs).
   const int64_t tiles = (n + 63) / 64;
-  return counters_bytes(tiles) + 2LL * sms * bn * BM * 4;
+  return counters_bytes(tiles) + 2LL * sms * bn * BM * 4 + 256;
 }
 
 extern "C" int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t ldw,
@@ -399,8 +399,13 @@ extern "C" int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, c
   const int64_t kblocks = k / BK;
   const int64_t total = tiles * kblocks;
   const int grid = static_cast<int>(total < sms ? total : sms);
-  const int64_t need = counters_bytes((n + 63) / 64) + 2LL * grid * bn * BM * 4;
-  MVB_REQUIRE(workspace_bytes >= need, "mvb_gemm_bf16: workspace %lld < %lld bytes", (long long)workspace_bytes,
+  // Partials at the head, tile counters at the tail of the workspace: calls of any shape
+  // that share one buffer then use nested suffixes of the same (self-zeroing) counter area,
+  // never bytes that another call used for partials.
+  const int64_t ws_end = workspace_bytes / 256 * 256;
+  const int64_t cbytes = counters_bytes((n + 63) / 64);
+  const int64_t need = cbytes + 2LL * grid * bn * BM * 4;
+  MVB_REQUIRE(ws_end >= need, "mvb_gemm_bf16: workspace %lld < %lld bytes", (long long)workspace_bytes,
               (long long)need);
   MVB_REQUIRE(aligned(workspace, 256), "mvb_gemm_bf16: workspace must be 256-byte aligned");
 
@@ -431,8 +436,8 @@ extern "C" int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, c
   a.kblocks = static_cast<int>(kblocks);
   a.epilogue = epilogue;
   a.inter = static_cast<int>(n / 2);
-  a.counters = static_cast<int*>(workspace);
-  a.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + counters_bytes((n + 63) / 64));
+  a.partials = static_cast<float*>(workspace);
+  a.counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + ws_end - cbytes);
   a.err = device_status_ptr();
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (bn) {

@@ -355,7 +355,9 @@ def linear(x: torch.Tensor, weight: torch.Tensor, epilogue: int = N.EPI_STORE, a
     with torch.cuda.device(dev):
         for m0 in range(0, M, 256):
             m = min(256, M - m0)
-            need = N.lib().mvb_gemm_workspace_bytes(m, Nn, K, dev.index if dev.index is not None else 0)
+            # + a fixed 1 MiB counter reserve: shapes sharing the cached buffer keep their
+            # partials clear of every other shape's counters (up to 256K output tiles)
+            need = N.lib().mvb_gemm_workspace_bytes(m, Nn, K, dev.index if dev.index is not None else 0) + (1 << 20)
             ws = workspace if workspace is not None else WORKSPACES.get(dev, "gemm", need)
             N.check(N.lib().mvb_gemm_bf16(out[m0:].data_ptr(), out.stride(0), xf[m0:].data_ptr(), xf.stride(0),
                                           w.data_ptr(), w.stride(0), m, Nn, K, epilogue,
@@ -439,7 +441,7 @@ def paged_attention_decode(q: torch.Tensor, kv_cache: torch.Tensor, layer: int, 
         out = torch.empty_like(q)
     dev = q.device
     with torch.cuda.device(dev):
-        need = N.lib().mvb_paged_attention_workspace_bytes(B, Hq, D, dev.index if dev.index is not None else 0)
+        need = N.lib().mvb_paged_attention_workspace_bytes(B, Hq, D, dev.index if dev.index is not None else 0) + (1 << 16)
         ws = workspace if workspace is not None else WORKSPACES.get(dev, "attention", need)
         N.check(N.lib().mvb_paged_attention_decode(
             out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), kv_cache.data_ptr(), block_tables.data_ptr(),

@@ -125,6 +125,21 @@ def test_gemm_store_matches_fp32(m, n, k):
     assert torch.equal(ops.linear(x, w), y)  # deterministic split-K merge
 
 
+def test_gemm_shapes_sharing_one_workspace():
+    # the decode step's five GEMM shapes back to back on one buffer, twice, as the runner does
+    from llm_pytorch_inference_b200 import _native
+    shapes = [(6144, 4096), (4096, 4096), (2 * 12288, 4096), (4096, 12288), (151936, 4096)]
+    need = max(_native.lib().mvb_gemm_workspace_bytes(64, n, k, 0) for n, k in shapes)
+    ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
+    g = torch.Generator(device=DEV).manual_seed(8)
+    xs = {k: (torch.randn(64, k, device=DEV, generator=g) / math.sqrt(k)).to(torch.bfloat16) for _, k in shapes}
+    ws_ = {s: torch.randn(*s, device=DEV, generator=g).to(torch.bfloat16) for s in shapes}
+    for _ in range(2):
+        for n, k in shapes:
+            y = ops.linear(xs[k], ws_[(n, k)], workspace=ws)
+            torch.testing.assert_close(y.float(), xs[k].float() @ ws_[(n, k)].float().T, rtol=1e-2, atol=1e-2)
+
+
 def test_gemm_swiglu_and_resadd_epilogues():
     g = torch.Generator(device=DEV).manual_seed(3)
     m, inter, k = 64, 1536, 2048
