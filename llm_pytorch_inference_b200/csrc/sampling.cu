@@ -362,26 +362,44 @@ struct Nucleus {
 
 template <typename T>
 __device__ Nucleus nucleus_threshold(const T* x, int64_t n, float top_p, Shared& s) {
+  // Masses accumulate in fp64: at 152k tokens a boundary token carries ~1e-5 of the mass,
+  // below what fp32 sums of the whole row resolve.
   constexpr int kBits = KeyOf<T>::kBits;
   float m = -INFINITY;
   for (int64_t i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, to_f<T>(x[i]));
   m = block_max(m, s);
-  float z = 0.0f;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) z += expf(to_f<T>(x[i]) - m);
-  z = block_sum_f(z, s);
-  const float target = top_p * z;
-  float* hmass = s.scan;  // 256 bins
+  double zl = 0.0;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) zl += static_cast<double>(expf(to_f<T>(x[i]) - m));
+  double* red = reinterpret_cast<double*>(s.scan);       // [0, 32): reduction, [32, 288): bins
+  double* hmass = red + 32;
+  {
+    zl += __shfl_xor_sync(0xffffffffu, zl, 16);
+    zl += __shfl_xor_sync(0xffffffffu, zl, 8);
+    zl += __shfl_xor_sync(0xffffffffu, zl, 4);
+    zl += __shfl_xor_sync(0xffffffffu, zl, 2);
+    zl += __shfl_xor_sync(0xffffffffu, zl, 1);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = zl;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double z = 0.0;
+      for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) z += red[w];
+      red[0] = z;
+    }
+    __syncthreads();
+  }
+  const double target = static_cast<double>(top_p) * red[0];
+  __syncthreads();
   if (threadIdx.x == 0) {
     s.prefix = 0;
-    s.redf[0] = 0.0f;  // mass above the current prefix range
+    red[1] = 0.0;  // mass above the current prefix range
   }
   __syncthreads();
-  float mass_above = 0.0f;
+  double mass_above = 0.0;
   unsigned ties = 0;
   for (int shift = kBits - 8; shift >= 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) {
       s.hist[i] = 0;
-      hmass[i] = 0.0f;
+      hmass[i] = 0.0;
     }
     __syncthreads();
     const uint32_t prefix = s.prefix;
@@ -392,12 +410,12 @@ __device__ Nucleus nucleus_threshold(const T* x, int64_t n, float top_p, Shared&
       if ((key & mask_hi) == (prefix & mask_hi)) {
         const int d = (key >> shift) & 0xFF;
         atomicAdd(&s.hist[d], 1u);
-        atomicAdd(&hmass[d], expf(to_f<T>(v) - m));
+        atomicAdd(&hmass[d], static_cast<double>(expf(to_f<T>(v) - m)));
       }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-      float above = s.redf[0];
+      double above = red[1];
       int d = 255, last_nonempty = -1;
       for (; d >= 0; --d) {
         if (s.hist[d] == 0) continue;
@@ -410,24 +428,24 @@ __device__ Nucleus nucleus_threshold(const T* x, int64_t n, float top_p, Shared&
         above -= hmass[d];
       }
       s.prefix = prefix | (static_cast<uint32_t>(d) << shift);
-      s.redf[0] = above;
+      red[1] = above;
       s.ncand = static_cast<int>(s.hist[d]);
     }
     __syncthreads();
-    mass_above = s.redf[0];
+    mass_above = red[1];
     ties = static_cast<unsigned>(s.ncand);
     __syncthreads();
   }
   Nucleus r;
   r.tau = s.prefix;
   r.xmax = m;
-  const float e_tau = expf(key_value<T>(r.tau) - m);
+  const double e_tau = static_cast<double>(expf(key_value<T>(r.tau) - m));
   int kept = 0;
-  if (target > mass_above && e_tau > 0.0f) {
-    const float q = ceilf((target - mass_above) / e_tau);
-    kept = q >= static_cast<float>(ties) ? static_cast<int>(ties) : static_cast<int>(q);
+  if (target > mass_above && e_tau > 0.0) {
+    const double q = ceil((target - mass_above) / e_tau);
+    kept = q >= static_cast<double>(ties) ? static_cast<int>(ties) : static_cast<int>(q);
   }
-  if (kept < 1 && mass_above == 0.0f) kept = 1;  // the top token always survives
+  if (kept < 1 && mass_above == 0.0) kept = 1;  // the top token always survives
   r.kept_ties = kept;
   return r;
 }

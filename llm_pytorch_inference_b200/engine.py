@@ -25,7 +25,7 @@ import torch
 
 from .configs import head_dim, num_kv_heads
 from .kv_cache import KVCacheManager, num_blocks_for_budget
-from .runner import DecodeRunner, DecodeWeights
+from .runner import DecodeRunner, DecodeWeights, resolve_device
 
 
 class DecodeEngine:
@@ -33,7 +33,7 @@ class DecodeEngine:
                  num_blocks: int | None = None, device="cuda", free_order: list[int] | None = None,
                  hbm_budget_bytes: int | None = None):
         self.cfg = cfg
-        self.dev = torch.device(device)
+        self.dev = resolve_device(device)
         self.weights = DecodeWeights(cfg, state_dict, self.dev)
         L, nkv, D = cfg["num_hidden_layers"], num_kv_heads(cfg), head_dim(cfg)
         if num_blocks is None:

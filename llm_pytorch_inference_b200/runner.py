@@ -30,6 +30,14 @@ from .configs import head_dim, num_kv_heads
 from .kv_cache import KVCacheManager
 
 
+def resolve_device(device) -> torch.device:
+    """``cuda`` -> ``cuda:<current>`` so device comparisons are exact."""
+    dev = torch.device(device)
+    if dev.type == "cuda" and dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    return dev
+
+
 def rope_tables(head_dim_: int, theta: float, length: int, dtype: torch.dtype, device) -> tuple[torch.Tensor, torch.Tensor]:
     """cos/sin ``[length, D]`` as the reference's ``RotaryEmbedding`` holds them after
     ``model.to(dtype)``: fp32 ``inv_freq`` rounded to ``dtype``, position ramp in ``dtype``
@@ -47,7 +55,7 @@ class DecodeWeights:
 
     def __init__(self, cfg: dict, sd: dict[str, torch.Tensor], device, dtype=torch.bfloat16):
         L = cfg["num_hidden_layers"]
-        dev = torch.device(device)
+        dev = resolve_device(device)
 
         def get(k):
             return sd[k].to(device=dev, dtype=dtype).contiguous()
@@ -85,7 +93,7 @@ class DecodeRunner:
         self.cfg = cfg
         self.w = weights
         self.kv = kv
-        self.dev = torch.device(device)
+        self.dev = resolve_device(device)
         self.B = max_batch
         self.L = cfg["num_hidden_layers"]
         self.H = cfg["hidden_size"]
