@@ -67,8 +67,14 @@ class OracleEngine:
     """Greedy / sampled generation through the reference's step structure."""
 
     def __init__(self, cfg: dict, state_dict: dict, dtype: torch.dtype, num_blocks: int = 256,
-                 block_size: int = 16, free_order: list[int] | None = None, device="cpu"):
+                 block_size: int = 16, free_order: list[int] | None = None, device="cpu",
+                 sdpa_backend=None, prefill_last_only: bool = False):
+        """``sdpa_backend`` (a ``torch.nn.attention.SDPBackend``) pins PyTorch's attention
+        implementation -- the reference leaves the choice to PyTorch, so two backends are two
+        equally valid executions of the reference (used to measure its own rounding noise)."""
         self.model = OracleDecoder(cfg, state_dict, dtype, device)
+        self.sdpa_backend = sdpa_backend
+        self.prefill_last_only = prefill_last_only
         self.dtype = dtype
         self.device = torch.device(device)
         self.blocks = BlockManager(num_blocks, block_size, free_order)
@@ -80,9 +86,18 @@ class OracleEngine:
         self.prompt_len: dict[int, int] = {}
 
     def _autocast(self):
+        import contextlib
+
+        stack = contextlib.ExitStack()
+        if self.sdpa_backend is not None:
+            from torch.nn.attention import sdpa_kernel
+
+            stack.enter_context(sdpa_kernel([self.sdpa_backend]))
         if self.dtype == torch.float32:
-            return torch.autocast(device_type=self.device.type, enabled=False)
-        return torch.autocast(device_type=self.device.type, dtype=self.dtype)
+            stack.enter_context(torch.autocast(device_type=self.device.type, enabled=False))
+        else:
+            stack.enter_context(torch.autocast(device_type=self.device.type, dtype=self.dtype))
+        return stack
 
     def prefill(self, seq_id: int, prompt: list[int]) -> torch.Tensor:
         """``engine.py:253-290``; returns the fp32 logits row of the last prompt token."""
@@ -94,7 +109,8 @@ class OracleEngine:
         ids = torch.tensor([prompt], dtype=torch.long, device=self.device)
         pos = torch.arange(len(prompt), dtype=torch.long, device=self.device)
         with torch.no_grad(), self._autocast():
-            logits = self.model.forward(ids, pos, self.kv_pool, bt, 0, use_cache=False)
+            logits = self.model.forward(ids, pos, self.kv_pool, bt, 0, use_cache=False,
+                                        last_only=self.prefill_last_only)
         return logits[:, -1, :].float()[0]
 
     def decode_inputs(self, seq_ids: list[int]):

@@ -199,8 +199,11 @@ class OracleDecoder:
                         w[p + "down_proj.weight"])
 
     def forward(self, input_ids, positions, kv_pool=None, block_tables=None, slot_idx=None, use_cache=False,
-                num_cached=None, attn_mask=None, return_hidden=False):
-        """``ForCausalLM.forward`` -> logits ``[B, S, V]`` in the model dtype (``model.py:369-424``)."""
+                num_cached=None, attn_mask=None, return_hidden=False, last_only=False):
+        """``ForCausalLM.forward`` -> logits ``[B, S, V]`` in the model dtype (``model.py:369-424``).
+
+        ``last_only`` projects only the last position through the final norm and lm_head
+        (rows are independent there; it saves the ``S x V`` prefill projection)."""
         w = self.w
         h = F.embedding(input_ids, w["model.embed_tokens.weight"])
         cos, sin = self.rope(positions)
@@ -219,6 +222,8 @@ class OracleDecoder:
             h = rms_norm(h, w[p + "post_attention_layernorm.weight"], self.eps, self.plus_one)
             h = self.mlp(i, h)
             h = r + h
+        if last_only:
+            h = h[:, -1:]
         h = rms_norm(h, w["model.norm.weight"], self.eps, self.plus_one)
         logits = F.linear(h, w["lm_head.weight"])
         return (logits, h) if return_hidden else logits

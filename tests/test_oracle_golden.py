@@ -104,8 +104,12 @@ def test_decode_tiny_bf16_matches_reference(golden_dir):
     prompts = [p.tolist() for p in fx["prompts"]]
     out, step_logits = eng.generate_greedy(prompts, 24)
     assert torch.equal(torch.tensor(out), fx["output_tokens"])
-    L = torch.stack(step_logits)
-    assert torch.equal(L.to(torch.bfloat16), fx["decode_logits"])
+    L = torch.stack(step_logits).to(torch.bfloat16).float()
+    # PyTorch's CPU bf16 GEMMs round differently per instruction set, so the reference's own
+    # bf16 logits move between hosts: measured max 1.6e-2 / mean 1.7e-3 between the host that
+    # made the fixture and another x86 host (same tokens).  On the fixture's host: bit-equal.
+    d = (L - fx["decode_logits"].float()).abs()
+    assert float(d.max()) <= 2e-2 and float(d.mean()) <= 2.5e-3, (float(d.max()), float(d.mean()))
 
 
 @pytest.mark.slow
