@@ -168,6 +168,22 @@ int mvb_paged_attention_decode(void* out, int64_t out_stride, const void* q, int
                                int64_t block_size, float scale, void* workspace, int64_t workspace_bytes,
                                mvb_stream_t stream);
 
+/* Allocation-free paged attention (no counterpart in the reference).  Same arguments and
+ * result as mvb_paged_attention_decode, minus the workspace: the split-KV scratch is a
+ * 6 MiB area built into the library, for callers that cannot allocate device memory (a host
+ * runtime binding this C ABI without a device allocator of its own, or a server whose HBM is
+ * all committed to the KV pool and that cannot take cudaMalloc's device-wide sync).
+ * Limit: the scratch covers up to 32 query heads of 128 dims on a 148-SM GPU and up to 4096
+ * sequences; larger shapes return MVB_ERR_UNSUPPORTED.  The first call on a device looks up
+ * the area's device address (cudaGetSymbolAddress), so make that first call before any
+ * stream capture.  All calls on a device share the area: each call clears its counters
+ * itself, and calls that overlap on the GPU (e.g. on two streams) race. */
+int mvb_paged_attention_decode_noalloc(void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                                       const void* kv_cache, const int32_t* block_tables, int64_t max_blocks,
+                                       const int32_t* ctx_lens, int64_t batch, int64_t num_q_heads,
+                                       int64_t num_kv_heads, int64_t head_dim, int64_t num_layers, int64_t layer,
+                                       int64_t num_blocks, int64_t block_size, float scale, mvb_stream_t stream);
+
 /* ---- dense GEMM on tcgen05 --------------------------------------------------------
  * Replaces the nn.Linear (cuBLAS) projections of the decode step (model_cuda.py:124-126,
  * :180, ops/mlp.py:66/84, model_cuda.py:413): Y[m, n] = sum_k X[m, k] * W[n, k] (bf16 in,

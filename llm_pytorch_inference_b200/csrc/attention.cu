@@ -16,6 +16,8 @@
 // through TMA into a 128-byte-swizzled [head][token][64] image, 2 halves of head_dim.
 // QK^T and PV use mma.sync m16n8k16 (bf16 in, fp32 accumulate); softmax is the online
 // (running max / running sum) form in the exp2 domain.
+#include <mutex>
+
 #include "common.cuh"
 #include "host.h"
 
@@ -504,4 +506,67 @@ extern "C" int mvb_paged_attention_decode(void* out, int64_t out_stride, const v
     case 8: return dispatch_group<8>(static_cast<int>(group), tm, a, grid, st);
     default: return fail(MVB_ERR_UNSUPPORTED, "mvb_paged_attention_decode: %lld KV heads", (long long)num_kv_heads);
   }
+}
+
+// ---------------------------------------------------------------------------------
+// Allocation-free variant.  Some callers cannot allocate device memory: a host runtime
+// that reaches this library only through its C ABI and owns no device allocator, or a
+// server that has already handed all of HBM to the KV pool and cannot afford cudaMalloc's
+// implicit device-wide synchronisation on the decode path.  For them the split-KV scratch
+// lives in a fixed area compiled into the library instead of a caller-provided workspace.
+namespace {
+
+// 6 MiB: partials for up to 32 query heads of 128 dims on a 148-SM B200 (~4.9 MB) plus the
+// per-sequence counters of up to 4096 sequences.  Every GPU that loads the library holds
+// this area until the process exits.
+constexpr int64_t kNoAllocScratchBytes = 6LL << 20;
+static __device__ __align__(256) unsigned char g_attn_scratch[kNoAllocScratchBytes];
+
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[64] = {};  // device address of g_attn_scratch, per device
+
+}  // namespace
+
+extern "C" int mvb_paged_attention_decode_noalloc(void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                                                  const void* kv_cache, const int32_t* block_tables,
+                                                  int64_t max_blocks, const int32_t* ctx_lens, int64_t batch,
+                                                  int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                                                  int64_t num_layers, int64_t layer, int64_t num_blocks,
+                                                  int64_t block_size, float scale, mvb_stream_t stream) {
+  int dev = 0;
+  MVB_TRY(cuda_status(cudaGetDevice(&dev), "mvb_paged_attention_decode_noalloc: cudaGetDevice"));
+  MVB_REQUIRE(dev >= 0 && dev < 64, "mvb_paged_attention_decode_noalloc: device %d out of range", dev);
+  void* scratch = nullptr;
+  {
+    // Set-up on the first call on each device (the current one): host code cannot use the
+    // array's name as a device address, so look the address up and keep it.
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (g_scratch_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      MVB_TRY(cuda_status(cudaGetSymbolAddress(&p, g_attn_scratch),
+                          "mvb_paged_attention_decode_noalloc: cudaGetSymbolAddress"));
+      g_scratch_ptr[dev] = p;
+    }
+    scratch = g_scratch_ptr[dev];
+  }
+  const int sms = current_sm_count();
+  MVB_REQUIRE(sms > 0, "mvb_paged_attention_decode_noalloc: no device");
+  MVB_REQUIRE(num_q_heads > 0 && head_dim > 0 && batch >= 0 && batch <= 4096,
+              "mvb_paged_attention_decode_noalloc: bad shape");
+  const int64_t cbytes = attn_counters_bytes(batch);
+  const int64_t need = cbytes + 2LL * sms * num_q_heads * 8 + 2LL * sms * num_q_heads * head_dim * 4;
+  if (need > kNoAllocScratchBytes)
+    return fail(MVB_ERR_UNSUPPORTED,
+                "mvb_paged_attention_decode_noalloc: %lld query heads x %lld dims on %d SMs need %lld bytes of "
+                "scratch; the built-in area holds %lld (use mvb_paged_attention_decode with a workspace)",
+                (long long)num_q_heads, (long long)head_dim, sms, (long long)need, (long long)kNoAllocScratchBytes);
+  if (batch == 0) return MVB_OK;
+  // The area keeps whatever the previous call left; the per-sequence counters must start at
+  // zero, so clear them (they sit at the tail) in stream order before the kernel.
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  MVB_TRY(cuda_status(cudaMemsetAsync(static_cast<char*>(scratch) + kNoAllocScratchBytes - cbytes, 0, cbytes, st),
+                      "mvb_paged_attention_decode_noalloc: clear counters"));
+  return mvb_paged_attention_decode(out, out_stride, q, q_stride, kv_cache, block_tables, max_blocks, ctx_lens, batch,
+                                    num_q_heads, num_kv_heads, head_dim, num_layers, layer, num_blocks, block_size,
+                                    scale, scratch, kNoAllocScratchBytes, stream);
 }
