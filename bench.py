@@ -54,6 +54,9 @@ def parse_args(argv=None):
     ap.add_argument("--layers", type=int, default=None, help="override layer count (debug only; invalid bench)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pdl", type=int, default=1)
+    ap.add_argument("--case", default=None, choices=["kernels"],
+                    help="kernels: small profiling case (2 layers of the workload's dims), each kernel kind "
+                         "launched a few times; prints per-kernel timings only")
     return ap.parse_args(argv)
 
 
@@ -363,8 +366,44 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_kernel_case(args) -> None:
+    """Profiling case: Qwen3-8B layer dims with 2 layers, batch 64, context 2048 (537 MB of KV per
+    layer, above the 126 MB L2), ~4.5 GB on the device; every kernel kind of the step is launched
+    1 + 3 times (first launch = warm-up), in the order of DecodeRunner.kernel_kinds()."""
+    from llm_pytorch_inference_b200 import _native as N
+    from llm_pytorch_inference_b200.configs import get_config
+    from llm_pytorch_inference_b200.engine import DecodeEngine
+    from llm_pytorch_inference_b200.weights import canonical_state_dict
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    N.set_pdl(bool(args.pdl))
+    cfg = get_config(ARCH, num_hidden_layers=2)
+    sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev)
+    nblk = BATCH * ((PROMPT + 2 + 15) // 16) + 64
+    eng = DecodeEngine(cfg, sd, max_batch=BATCH, max_model_len=PROMPT + 64, num_blocks=nblk, device=dev)
+    del sd
+    g = torch.Generator().manual_seed(1)
+    for s in range(BATCH):
+        eng.add_sequence(s, torch.randint(0, cfg["vocab_size"], (PROMPT,), generator=g).tolist())
+        eng.append_first_token(s, 1)
+    eng.prefill_synthetic(seed=0)
+    eng.set_sampling(*SAMPLING, seed=1234)
+    eng.prepare_first_step()
+    eng._grow_blocks()
+    eng.runner.upload_metadata()
+    torch.cuda.synchronize(dev)
+    res = eng.runner.time_kernels(iters=3)
+    print(json.dumps({k: {"avg_us": round(v["avg_ms"] * 1e3, 2), "gbs": round(v["gbs"], 1),
+                          "bytes_per_launch": v["bytes_per_launch"]} for k, v in res.items()}), flush=True)
+    assert N.device_status(clear=True) == 0
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
+    if args.case == "kernels":
+        run_kernel_case(args)
+        return 0
     rank, world, local = (0, 1, 0)
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
