@@ -368,8 +368,9 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
 
 def run_kernel_case(args) -> None:
     """Profiling case: Qwen3-8B layer dims with 2 layers, batch 64, context 2048 (537 MB of KV per
-    layer, above the 126 MB L2), ~4.5 GB on the device; every kernel kind of the step is launched
-    1 + 3 times (first launch = warm-up), in the order of DecodeRunner.kernel_kinds()."""
+    layer, above the 126 MB L2), ~4.5 GB on the device.  One full decode step runs first (2 attention
+    and 9 GEMM launches), then every kernel kind of the step is launched 1 + 3 times (first launch
+    = warm-up), in the order of DecodeRunner.kernel_kinds()."""
     from llm_pytorch_inference_b200 import _native as N
     from llm_pytorch_inference_b200.configs import get_config
     from llm_pytorch_inference_b200.engine import DecodeEngine
@@ -392,6 +393,7 @@ def run_kernel_case(args) -> None:
     eng.prepare_first_step()
     eng._grow_blocks()
     eng.runner.upload_metadata()
+    eng.runner.forward()          # one real step first, so every buffer holds realistic values
     torch.cuda.synchronize(dev)
     res = eng.runner.time_kernels(iters=3)
     print(json.dumps({k: {"avg_us": round(v["avg_ms"] * 1e3, 2), "gbs": round(v["gbs"], 1),

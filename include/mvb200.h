@@ -38,6 +38,7 @@ typedef struct CUstream_st* mvb_stream_t; /* == cudaStream_t */
 #define MVB_DEV_BAD_BLOCK 0x2u    /* a block-table entry was outside [0, num_blocks) */
 #define MVB_DEV_BAD_POSITION 0x4u /* a position was outside its block table / table */
 #define MVB_DEV_BAD_TOKEN 0x8u    /* a token id was outside [0, vocab) */
+#define MVB_DEV_SAMPLER_TIES 0x10u /* > 2048 logits tied at the top-k cutoff; ties past 2048 were dropped */
 
 /* ---- dtype codes ---------------------------------------------------------- */
 #define MVB_F32 0

@@ -19,7 +19,7 @@ F32, F16, BF16, I32, I64 = 0, 1, 2, 3, 4
 NORM_OPS, NORM_MODEL = 0, 1
 ACT_SILU, ACT_GELU_TANH = 0, 1
 EPI_STORE, EPI_SWIGLU, EPI_RESADD = 0, 1, 2
-DEV_WAIT_TIMEOUT, DEV_BAD_BLOCK, DEV_BAD_POSITION, DEV_BAD_TOKEN = 0x1, 0x2, 0x4, 0x8
+DEV_WAIT_TIMEOUT, DEV_BAD_BLOCK, DEV_BAD_POSITION, DEV_BAD_TOKEN, DEV_SAMPLER_TIES = 0x1, 0x2, 0x4, 0x8, 0x10
 
 _vp, _i64, _i32, _f32, _u64, _u32p = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_uint64, C.POINTER(C.c_uint)
 

@@ -23,6 +23,7 @@ constexpr unsigned kDevWaitTimeout = MVB_DEV_WAIT_TIMEOUT;
 constexpr unsigned kDevBadBlock = MVB_DEV_BAD_BLOCK;
 constexpr unsigned kDevBadPosition = MVB_DEV_BAD_POSITION;
 constexpr unsigned kDevBadToken = MVB_DEV_BAD_TOKEN;
+constexpr unsigned kDevSamplerTies = MVB_DEV_SAMPLER_TIES;
 
 __device__ __forceinline__ void report(unsigned* err, unsigned code) {
   if (err) atomicOr(err, code);

@@ -287,7 +287,7 @@ __device__ int gather_sorted_candidates(const T* x, int64_t n, uint32_t kth, Sha
   __syncthreads();
   int nc = s.ncand;
   if (nc > kCandMax) {
-    if (threadIdx.x == 0) report(err, kDevBadToken);
+    if (threadIdx.x == 0) report(err, kDevSamplerTies);
     nc = kCandMax;
   }
   int n2 = 1;
