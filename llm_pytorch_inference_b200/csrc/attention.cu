@@ -28,6 +28,7 @@ constexpr int D = 128;       // head_dim handled by this kernel
 constexpr int BS = 16;       // tokens per block (the reference's block_size)
 constexpr int HALF_BYTES_PER_HEAD = BS * 64 * 2;  // 2 KB: 16 tokens x 64 dims
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kMergeC = 32;  // contributors merged per round
 
 struct AttnArgs {
   __nv_bfloat16* out;
@@ -95,6 +96,7 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + STAGES);
   volatile int* last_flag = abort_flag + 1;
   int* cu = const_cast<int*>(abort_flag + 2);  // [batch + 1] block prefix sums
+  float* merge_smem = reinterpret_cast<float*>(cu + a.batch + 1);  // split-sequence merge scratch
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -155,38 +157,59 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
   int issued = 0;
   if (warp == HKV) {
     // ---------------------------------------------------------------- producer
-    if (lane == 0 && g_end > g_begin) {
-      prefetch_tmap(&tm);
+    // The whole warp fetches the next 32 block ids at once (one per lane, one round trip of
+    // latency per 32 blocks); lane 0 then issues the TMA copies from the shuffled ids.
+    if (g_end > g_begin) {
+      if (lane == 0) prefetch_tmap(&tm);
       const uint64_t pol = l2_policy_evict_first();
-      int b = b0;
       const int64_t P = a.num_blocks;
-      for (int64_t g = g_begin; g < g_end; ++g) {
-        while (g >= cu[b + 1]) ++b;
-        const int j = static_cast<int>(g - cu[b]);
-        int blk = a.block_tables[static_cast<int64_t>(b) * a.max_blocks + j];
-        if (blk < 0 || blk >= P) {
-          report(a.err, kDevBadBlock);
-          blk = 0;  // stay in bounds; the sequence's output is not trusted (status word set)
-        }
-        const int it = static_cast<int>(g - g_begin);
-        const int s = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err)) break;
-        mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-        uint8_t* st = smem + s * STAGE_BYTES;
-        for (int kv = 0; kv < 2; ++kv) {
-          const int row = static_cast<int>((a.layer * 2 + kv) * P + blk);
-          for (int half = 0; half < 2; ++half) {
-            uint8_t* dst = st + (kv * 2 + half) * HKV * HALF_BYTES_PER_HEAD;
-            if (a.per_head_tma) {
-              for (int h = 0; h < HKV; ++h)
-                tma_load_4d(dst + h * HALF_BYTES_PER_HEAD, &tm, &full[s], half * 64, h, 0, row, pol);
-            } else {
-              tma_load_4d(dst, &tm, &full[s], half * 64, 0, 0, row, pol);
-            }
+      int b_lane = b0;
+      bool ok = true;
+      for (int64_t g0 = g_begin; ok && g0 < g_end; g0 += 32) {
+        const int64_t g = g0 + lane;
+        int blk = 0;
+        if (g < g_end) {
+          while (g >= cu[b_lane + 1]) ++b_lane;
+          const int j = static_cast<int>(g - cu[b_lane]);
+          blk = a.block_tables[static_cast<int64_t>(b_lane) * a.max_blocks + j];
+          if (blk < 0 || blk >= P) {
+            report(a.err, kDevBadBlock);
+            blk = 0;  // stay in bounds; the sequence's output is not trusted (status word set)
           }
         }
-        issued = it + 1;
+        const int n = static_cast<int>(g_end - g0 < 32 ? g_end - g0 : 32);
+        for (int i = 0; i < n; ++i) {
+          const int bi = __shfl_sync(0xffffffffu, blk, i);
+          int good = 1;
+          if (lane == 0) {
+            const int it = static_cast<int>(g0 - g_begin) + i;
+            const int s = it % STAGES;
+            const uint32_t ph = (it / STAGES) & 1;
+            if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err)) {
+              good = 0;
+            } else {
+              mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+              uint8_t* st = smem + s * STAGE_BYTES;
+              for (int kv = 0; kv < 2; ++kv) {
+                const int row = static_cast<int>((a.layer * 2 + kv) * P + bi);
+                for (int half = 0; half < 2; ++half) {
+                  uint8_t* dst = st + (kv * 2 + half) * HKV * HALF_BYTES_PER_HEAD;
+                  if (a.per_head_tma) {
+                    for (int h = 0; h < HKV; ++h)
+                      tma_load_4d(dst + h * HALF_BYTES_PER_HEAD, &tm, &full[s], half * 64, h, 0, row, pol);
+                  } else {
+                    tma_load_4d(dst, &tm, &full[s], half * 64, 0, 0, row, pol);
+                  }
+                }
+              }
+              issued = it + 1;
+            }
+          }
+          if (!__shfl_sync(0xffffffffu, good, 0)) {
+            ok = false;
+            break;
+          }
+        }
       }
     }
   } else {
@@ -328,26 +351,62 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
         }
         consumer_bar<HKV>();
         if (*last_flag) {
+          // Merge the sequence's partials (deterministic, contributor order).  Per-head max and
+          // denominator first, then normalised weights staged in shared memory 32 contributors at a
+          // time, and every thread accumulates its GROUP*4 outputs with all loads independent.
+          constexpr int HQ = GROUP * HKV;
+          constexpr int NT = HKV * 32;
+          constexpr int PER = HQ * D / NT;
+          float* s_w = merge_smem;                       // [kMergeC][HQ]
+          float* s_M = s_w + kMergeC * HQ;               // [HQ]
+          float* s_den = s_M + HQ;                       // [HQ]
+          int* s_slot = reinterpret_cast<int*>(s_den + HQ);  // [kMergeC]
           const int c_first = cta_of(seq_lo, total, G);
-          const int c_last = cta_of(seq_hi - 1, total, G);
-          const int n_out = a.num_q_heads * D;
-          for (int i = threadIdx.x; i < n_out; i += HKV * 32) {
-            const int hh = i / D;
-            float mmax = -INFINITY;
-            for (int c = c_first; c <= c_last; ++c) {
+          const int nc = cta_of(seq_hi - 1, total, G) - c_first + 1;
+          for (int hh = threadIdx.x; hh < HQ; hh += NT) {
+            float M = -INFINITY;
+            for (int j = 0; j < nc; ++j) {
+              const int c = c_first + j;
               const int sl = range_start(c, total, G) >= seq_lo ? 2 * c : 2 * c + 1;
-              mmax = fmaxf(mmax, __ldcg(a.partial_ml + static_cast<int64_t>(sl) * a.num_q_heads + hh).x);
+              M = fmaxf(M, __ldcg(a.partial_ml + static_cast<int64_t>(sl) * HQ + hh).x);
             }
-            float num = 0.0f, den = 0.0f;
-            for (int c = c_first; c <= c_last; ++c) {
+            float den = 0.0f;
+            for (int j = 0; j < nc; ++j) {
+              const int c = c_first + j;
               const int sl = range_start(c, total, G) >= seq_lo ? 2 * c : 2 * c + 1;
-              const float2 ml = __ldcg(a.partial_ml + static_cast<int64_t>(sl) * a.num_q_heads + hh);
-              const float wgt = ml.y * exp2f(ml.x - mmax);
-              num += wgt * __ldcg(a.partial_o + static_cast<int64_t>(sl) * a.num_q_heads * D + i);
-              den += wgt;
+              const float2 ml = __ldcg(a.partial_ml + static_cast<int64_t>(sl) * HQ + hh);
+              den += ml.y * exp2f(ml.x - M);
             }
-            a.out[static_cast<int64_t>(b) * a.out_stride + i] = __float2bfloat16_rn(num / den);
+            s_M[hh] = M;
+            s_den[hh] = den;
           }
+          float acc[PER];
+#pragma unroll
+          for (int k = 0; k < PER; ++k) acc[k] = 0.0f;
+          for (int j0 = 0; j0 < nc; j0 += kMergeC) {
+            const int cn = nc - j0 < kMergeC ? nc - j0 : kMergeC;
+            consumer_bar<HKV>();
+            for (int e = threadIdx.x; e < cn * HQ; e += NT) {
+              const int j = e / HQ, hh = e - j * HQ;
+              const int c = c_first + j0 + j;
+              const int sl = range_start(c, total, G) >= seq_lo ? 2 * c : 2 * c + 1;
+              const float2 ml = __ldcg(a.partial_ml + static_cast<int64_t>(sl) * HQ + hh);
+              s_w[j * HQ + hh] = ml.y * exp2f(ml.x - s_M[hh]) / s_den[hh];
+              if (hh == 0) s_slot[j] = sl;
+            }
+            consumer_bar<HKV>();
+            for (int j = 0; j < cn; ++j) {
+              const float* po = a.partial_o + static_cast<int64_t>(s_slot[j]) * HQ * D;
+#pragma unroll
+              for (int k = 0; k < PER; ++k) {
+                const int i = threadIdx.x + k * NT;
+                acc[k] += s_w[j * HQ + i / D] * __ldcg(po + i);
+              }
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < PER; ++k)
+            a.out[static_cast<int64_t>(b) * a.out_stride + threadIdx.x + k * NT] = __float2bfloat16_rn(acc[k]);
           if (threadIdx.x == 0) a.counters[b] = 0;
         }
         consumer_bar<HKV>();
@@ -368,23 +427,23 @@ constexpr int attn_stages() {
   return HKV >= 8 ? 3 : (HKV == 4 ? 6 : 8);
 }
 
-template <int HKV>
+template <int GROUP, int HKV>
 size_t attn_smem(int batch) {
   return static_cast<size_t>(attn_stages<HKV>()) * 4 * HKV * HALF_BYTES_PER_HEAD + 2 * 8 * attn_stages<HKV>() + 16 +
-         4 * (batch + 1) + 1024;
+         4 * (batch + 1) + 4 * ((kMergeC + 2) * GROUP * HKV + kMergeC) + 1024;
 }
 
 template <int GROUP, int HKV>
 int launch_attn(const CUtensorMap& tm, const AttnArgs& a, int grid, cudaStream_t st) {
   constexpr int S = attn_stages<HKV>();
-  const size_t smem = attn_smem<HKV>(a.batch);
+  const size_t smem = attn_smem<GROUP, HKV>(a.batch);
   // Raise the kernel's dynamic-smem limit once per device (to the 4096-sequence maximum),
   // so no attribute call happens while a stream is being captured into a graph.
   static unsigned long long done_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !(done_mask & (1ull << dev))) {
-    MVB_TRY(set_smem(paged_attention_kernel<GROUP, HKV, S>, attn_smem<HKV>(4096), "paged_attention: smem attribute"));
+    MVB_TRY(set_smem(paged_attention_kernel<GROUP, HKV, S>, attn_smem<GROUP, HKV>(4096), "paged_attention: smem attribute"));
     if (dev < 64) done_mask |= 1ull << dev;
   }
   return launch("paged_attention_decode", paged_attention_kernel<GROUP, HKV, S>, dim3(grid), dim3((HKV + 1) * 32),

@@ -105,8 +105,11 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs& a, const float (&
   }
 }
 
+// BN=64 (decode batches) keeps ~106 KB of shared memory and <= 168 registers so that two CTAs
+// fit on one SM: under programmatic dependent launch the next GEMM's CTAs become resident while
+// this one drains and stream their first weight tiles before the grid-dependency wait.
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                      const GemmArgs a) {
   constexpr int B_STAGE = BN * BK * 2;
@@ -331,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int BN>
 constexpr int stages_for() {
-  return BN == 64 ? 8 : (BN == 128 ? 6 : 4);
+  return BN == 64 ? 4 : (BN == 128 ? 6 : 4);
 }
 
 template <int BN>

@@ -318,8 +318,9 @@ class DecodeRunner:
         return out
 
     def launches_per_step(self) -> int:
-        """Kernels one step launches (embedding, rmsnorm, 8 per layer + 1 between layers, norm, lm_head, sample)."""
-        return 2 + self.L * 8 + (self.L - 1) + 3
+        """Kernels one step launches: embedding, rmsnorm, 7 per layer (qkv, qk-norm/rope/kv, attention,
+        o_proj, add+norm, gate_up, down), an add+norm between layers, final add+norm, lm_head, sample."""
+        return 2 + self.L * 7 + (self.L - 1) + 3
 
     # ------------------------------------------------------------------ graphs
     def capture(self) -> None:
