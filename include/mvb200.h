@@ -78,6 +78,13 @@ int mvb_rmsnorm(void* out, int64_t out_stride, const void* in, int64_t in_stride
 int mvb_fused_add_rmsnorm(void* out, void* residual, const void* in, const void* weight, int64_t rows,
                           int64_t hidden, float eps, int plus_one, int semantics, int dtype, mvb_stream_t stream);
 
+/* Residual add + RMSNorm (model semantics) of a linear layer's output still in split-K partial
+ * form (models/model.py:319-322, :328 + the next RMSNorm): `gemm_workspace` is the workspace of
+ * the preceding mvb_gemm_bf16(MVB_EPI_PARTIALS) call of shape [rows, hidden, gemm_k];
+ * residual += bf16(sum of partials) (in place, bf16), out = RMSNorm(residual).  bf16 only. */
+int mvb_fused_add_rmsnorm_gemm(void* out, void* residual, const void* gemm_workspace, int64_t rows, int64_t hidden,
+                               int64_t gemm_k, const void* weight, float eps, int plus_one, mvb_stream_t stream);
+
 /* ---- RoPE ------------------------------------------------------------------
  * Replaces rotary_pos_emb_forward (ops_binding.cpp:15, rope_kernel.cu:44-61):
  * NeoX rotate-half RoPE, out = x*cos + rotate_half(x)*sin, each product and the
@@ -153,6 +160,17 @@ int mvb_qk_norm_rope_kv_write(void* q_out, void* kv_cache, const void* qkv, int6
                               int64_t head_dim, int64_t num_layers, int64_t layer, int64_t num_blocks,
                               int64_t block_size, float eps, mvb_stream_t stream);
 
+/* The same, with the fused q|k|v projection still in split-K partial form: `gemm_workspace`
+ * is the workspace of the preceding mvb_gemm_bf16(MVB_EPI_PARTIALS) call of shape
+ * [batch, (Hq + 2*Hkv) * head_dim, gemm_k]; each element is taken as bf16(sum of its tile's
+ * partials), i.e. exactly the projection's bf16 output (model.py:170-172). */
+int mvb_qk_norm_rope_kv_write_gemm(void* q_out, void* kv_cache, const void* gemm_workspace, int64_t gemm_k,
+                                   const void* q_norm_w, const void* k_norm_w, const void* cos, const void* sin,
+                                   int64_t table_len, const int32_t* positions, const int32_t* block_tables,
+                                   int64_t max_blocks, int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+                                   int64_t head_dim, int64_t num_layers, int64_t layer, int64_t num_blocks,
+                                   int64_t block_size, float eps, mvb_stream_t stream);
+
 /* ---- paged attention decode --------------------------------------------------
  * Replaces Attention._read_kv_cache_batch + GQA expand + SDPA for one query token per
  * sequence (model.py:191-221, model_cuda.py:145-177): out[b, h] =
@@ -193,6 +211,9 @@ int mvb_paged_attention_decode_noalloc(void* out, int64_t out_stride, const void
  *           MVB_EPI_SWIGLU W is the reference's cat([gate, up]) of 2*inter rows; Y[m, j] =
  *                          bf16(bf16(silu(bf16(gate))) * bf16(up)), j < inter (model.py:116-117)
  *           MVB_EPI_RESADD Y = bf16(aux[m, n] + bf16(acc)) (residual add, model.py:319/328)
+ *           MVB_EPI_PARTIALS  no Y (y may be NULL): every stream-K segment leaves its fp32 partial in
+ *                          the workspace for a consuming kernel to sum (mvb_fused_add_rmsnorm_gemm,
+ *                          mvb_qk_norm_rope_kv_write_gemm); the GEMM then ends without a merge
  * Requires k % 64 == 0, ldx/ldw/ldy multiples of 8, 16-byte aligned pointers, m <= 256.
  * workspace: >= mvb_gemm_workspace_bytes(m, n, k, device); zero before the first call.  fp32
  * partials use its head, per-tile counters its tail; the kernel leaves the counters zero, so
@@ -201,6 +222,7 @@ int mvb_paged_attention_decode_noalloc(void* out, int64_t out_stride, const void
 #define MVB_EPI_STORE 0
 #define MVB_EPI_SWIGLU 1
 #define MVB_EPI_RESADD 2
+#define MVB_EPI_PARTIALS 3
 int64_t mvb_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int device);
 int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t m,
                   int64_t n, int64_t k, int epilogue, const void* aux, int64_t ld_aux, void* workspace,

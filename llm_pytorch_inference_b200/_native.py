@@ -18,7 +18,7 @@ MVB_OK = 0
 F32, F16, BF16, I32, I64 = 0, 1, 2, 3, 4
 NORM_OPS, NORM_MODEL = 0, 1
 ACT_SILU, ACT_GELU_TANH = 0, 1
-EPI_STORE, EPI_SWIGLU, EPI_RESADD = 0, 1, 2
+EPI_STORE, EPI_SWIGLU, EPI_RESADD, EPI_PARTIALS = 0, 1, 2, 3
 DEV_WAIT_TIMEOUT, DEV_BAD_BLOCK, DEV_BAD_POSITION, DEV_BAD_TOKEN, DEV_SAMPLER_TIES = 0x1, 0x2, 0x4, 0x8, 0x10
 
 _vp, _i64, _i32, _f32, _u64, _u32p = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_uint64, C.POINTER(C.c_uint)
@@ -32,6 +32,7 @@ SIGNATURES: dict[str, tuple] = {
     "mvb_set_pdl": (_i32, [_i32]),
     "mvb_rmsnorm": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _f32, _i32, _i32, _i32, _vp]),
     "mvb_fused_add_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _i32, _i32, _i32, _vp]),
+    "mvb_fused_add_rmsnorm_gemm": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _f32, _i32, _vp]),
     "mvb_rotary_pos_emb": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _vp]),
     "mvb_activation": (_i32, [_vp, _vp, _i64, _i32, _i32, _vp]),
     "mvb_gated_activation": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _vp]),
@@ -44,6 +45,8 @@ SIGNATURES: dict[str, tuple] = {
     "mvb_sample": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _u64, _u64, _vp, _i32, _vp]),
     "mvb_qk_norm_rope_kv_write": (_i32, [_vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64,
                                          _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp]),
+    "mvb_qk_norm_rope_kv_write_gemm": (_i32, [_vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64,
+                                              _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp]),
     "mvb_paged_attention_workspace_bytes": (_i64, [_i64, _i64, _i64, _i32]),
     "mvb_paged_attention_decode": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64,
                                           _i64, _i64, _i64, _i64, _f32, _vp, _i64, _vp]),

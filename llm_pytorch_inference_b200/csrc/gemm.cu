@@ -19,6 +19,7 @@
 // buffered in TMEM so the next tile's MMAs overlap the previous tile's epilogue.
 #include "common.cuh"
 #include "host.h"
+#include "splitk.cuh"
 
 namespace mvb {
 namespace {
@@ -38,6 +39,7 @@ struct GemmArgs {
   int kblocks;   // k / BK
   int epilogue;  // MVB_EPI_*
   int inter;     // SWIGLU: rows of the gate half of W
+  int maxc;      // PARTIALS: slots per tile (most contributors of any tile)
   float* partials;
   int* counters;
   unsigned* err;
@@ -262,7 +264,19 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
       tc_fence_after();
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(ab * BN);
       const bool full_tile = (kb == tile_lo) && (seg_end == tile_lo + a.kblocks);
-      if (full_tile) {
+      if (a.epilogue == MVB_EPI_PARTIALS) {
+        // Every segment's fp32 accumulator goes to its (tile, contributor) slot; the consuming
+        // kernel sums the slots (no fence, counter or merge here).
+        const int j = static_cast<int>(blockIdx.x) - cta_of(tile_lo, total, G);
+        float* part = a.partials + (static_cast<int64_t>(t) * a.maxc + j) * BN * BM;
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld_x32(tb + c0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) part[(c0 + jj) * BM + row] = __uint_as_float(r[jj]);
+        }
+      } else if (full_tile) {
         for (int c0 = 0; c0 < BN; c0 += 32) {
           uint32_t r[32];
           tmem_ld_x32(tb + c0, r);
@@ -377,24 +391,27 @@ extern "C" int64_t mvb_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int
   const int64_t bn = bn_for(m);
   // Counters sized for the larger of the two tilings (plain / SWIGLU pairs).
   const int64_t tiles = (n + 63) / 64;
-  return counters_bytes(tiles) + 2LL * sms * bn * BM * 4 + 256;
+  const int64_t merge = counters_bytes(tiles) + 2LL * sms * bn * BM * 4 + 256;
+  const int64_t part = splitk_partials_bytes(splitk_plan(m, n, k, sms)) + 256;
+  return merge > part ? merge : part;
 }
 
 extern "C" int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t ldw,
                              int64_t m, int64_t n, int64_t k, int epilogue, const void* aux, int64_t ld_aux,
                              void* workspace, int64_t workspace_bytes, mvb_stream_t stream) {
-  MVB_REQUIRE(y && x && w && workspace, "mvb_gemm_bf16: null pointer");
+  MVB_REQUIRE(x && w && workspace && (y || epilogue == MVB_EPI_PARTIALS), "mvb_gemm_bf16: null pointer");
   MVB_REQUIRE(m > 0 && m <= 256, "mvb_gemm_bf16: m=%lld outside [1, 256]", (long long)m);
   MVB_REQUIRE(n > 0 && n < (1LL << 31) && k > 0 && k % BK == 0, "mvb_gemm_bf16: need k %% 64 == 0 (k=%lld)",
               (long long)k);
   MVB_REQUIRE(ldx >= k && ldw >= k && ldx % 8 == 0 && ldw % 8 == 0, "mvb_gemm_bf16: ldx/ldw must be >= k, %% 8");
   MVB_REQUIRE(aligned(x, 16) && aligned(w, 16), "mvb_gemm_bf16: x and w must be 16-byte aligned");
-  MVB_REQUIRE(epilogue == MVB_EPI_STORE || epilogue == MVB_EPI_SWIGLU || epilogue == MVB_EPI_RESADD,
+  MVB_REQUIRE(epilogue == MVB_EPI_STORE || epilogue == MVB_EPI_SWIGLU || epilogue == MVB_EPI_RESADD ||
+                  epilogue == MVB_EPI_PARTIALS,
               "mvb_gemm_bf16: bad epilogue %d", epilogue);
   MVB_REQUIRE(epilogue != MVB_EPI_RESADD || (aux != nullptr && ld_aux >= n), "mvb_gemm_bf16: RESADD needs aux");
   MVB_REQUIRE(epilogue != MVB_EPI_SWIGLU || n % 2 == 0, "mvb_gemm_bf16: SWIGLU needs an even n (= 2*inter)");
   const int64_t out_cols = epilogue == MVB_EPI_SWIGLU ? n / 2 : n;
-  MVB_REQUIRE(ldy >= out_cols, "mvb_gemm_bf16: ldy < output columns");
+  MVB_REQUIRE(epilogue == MVB_EPI_PARTIALS || ldy >= out_cols, "mvb_gemm_bf16: ldy < output columns");
   const int sms = current_sm_count();
   MVB_REQUIRE(sms > 0, "mvb_gemm_bf16: no device");
   const int bn = bn_for(m);
@@ -407,7 +424,9 @@ extern "C" int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, c
   // never bytes that another call used for partials.
   const int64_t ws_end = workspace_bytes / 256 * 256;
   const int64_t cbytes = counters_bytes((n + 63) / 64);
-  const int64_t need = cbytes + 2LL * grid * bn * BM * 4;
+  SplitKPlan plan{};
+  if (epilogue == MVB_EPI_PARTIALS) plan = splitk_plan(m, n, k, sms);
+  const int64_t need = epilogue == MVB_EPI_PARTIALS ? splitk_partials_bytes(plan) : cbytes + 2LL * grid * bn * BM * 4;
   MVB_REQUIRE(ws_end >= need, "mvb_gemm_bf16: workspace %lld < %lld bytes", (long long)workspace_bytes,
               (long long)need);
   MVB_REQUIRE(aligned(workspace, 256), "mvb_gemm_bf16: workspace must be 256-byte aligned");
@@ -439,6 +458,7 @@ extern "C" int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, c
   a.kblocks = static_cast<int>(kblocks);
   a.epilogue = epilogue;
   a.inter = static_cast<int>(n / 2);
+  a.maxc = plan.maxc;
   a.partials = static_cast<float*>(workspace);
   a.counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + ws_end - cbytes);
   a.err = device_status_ptr();

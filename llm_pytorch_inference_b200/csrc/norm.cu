@@ -11,6 +11,7 @@
 // with r = 1/sqrt(mean(x^2) + eps) in fp32 and T() rounding to the storage type.
 #include "common.cuh"
 #include "host.h"
+#include "splitk.cuh"
 
 namespace mvb {
 namespace {
@@ -80,6 +81,36 @@ __global__ void fused_add_rmsnorm_kernel(T* __restrict__ out, T* __restrict__ re
     y[i] = from_f<T>(norm_out<T>(to_f<T>(res[i]), to_f<T>(w[i]), r, plus_one, semantics, true));
 }
 
+// Residual add + RMSNorm whose input is a GEMM's output still in split-K partial form: the
+// linear layer's bf16 output is formed here as bf16(sum of the tile's partial slots), then
+// residual += it and out = RMSNorm(residual) (model semantics, models/model.py:19-25, :319).
+__global__ void fused_add_rmsnorm_gemm_kernel(__nv_bfloat16* __restrict__ out, __nv_bfloat16* __restrict__ residual,
+                                              const float* __restrict__ partials, SplitKPlan p,
+                                              const __nv_bfloat16* __restrict__ w, int hidden, float eps,
+                                              int plus_one) {
+  __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.x;
+  __nv_bfloat16* res = residual + static_cast<int64_t>(b) * hidden;
+  __nv_bfloat16* y = out + static_cast<int64_t>(b) * hidden;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    const int t = i / kSplitBM, r = i - t * kSplitBM;
+    const int nc = sk_count(p, t);
+    float acc = 0.0f;
+    for (int j = 0; j < nc; ++j) acc += __ldcg(partials + sk_offset(p, t, j, b, r));
+    const float v = bf16_round(__bfloat162float(res[i]) + bf16_round(acc));
+    res[i] = __float2bfloat16_rn(v);
+    ss += v * v;
+  }
+  ss = block_sum(ss, red);
+  const float rr = 1.0f / sqrtf(ss / static_cast<float>(hidden) + eps);
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x)
+    y[i] = __float2bfloat16_rn(norm_out<__nv_bfloat16>(__bfloat162float(res[i]), __bfloat162float(w[i]), rr,
+                                                       plus_one, MVB_NORM_MODEL, true));
+}
+
 int threads_for(int64_t hidden) {
   int t = static_cast<int>(((hidden + 3) / 4 + 31) / 32 * 32);
   return t < 64 ? 64 : (t > 1024 ? 1024 : t);
@@ -141,4 +172,19 @@ extern "C" int mvb_fused_add_rmsnorm(void* out, void* residual, const void* in, 
     default:
       return fail(MVB_ERR_INVALID_ARG, "mvb_fused_add_rmsnorm: unsupported dtype %d", dtype);
   }
+}
+
+extern "C" int mvb_fused_add_rmsnorm_gemm(void* out, void* residual, const void* gemm_workspace, int64_t rows,
+                                          int64_t hidden, int64_t gemm_k, const void* weight, float eps,
+                                          int plus_one, mvb_stream_t stream) {
+  MVB_REQUIRE(out && residual && gemm_workspace && weight, "mvb_fused_add_rmsnorm_gemm: null pointer");
+  MVB_REQUIRE(rows > 0 && rows <= 256 && hidden > 0 && gemm_k > 0 && gemm_k % kSplitBK == 0,
+              "mvb_fused_add_rmsnorm_gemm: bad shape");
+  const int sms = current_sm_count();
+  MVB_REQUIRE(sms > 0, "mvb_fused_add_rmsnorm_gemm: no device");
+  const SplitKPlan p = splitk_plan(rows, hidden, gemm_k, sms);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return launch("fused_add_rmsnorm_gemm", fused_add_rmsnorm_gemm_kernel, dim3(static_cast<unsigned>(rows)),
+                dim3(threads_for(hidden)), 0, st, (__nv_bfloat16*)out, (__nv_bfloat16*)residual,
+                (const float*)gemm_workspace, p, (const __nv_bfloat16*)weight, (int)hidden, eps, plus_one);
 }

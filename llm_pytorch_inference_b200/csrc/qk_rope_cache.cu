@@ -11,6 +11,7 @@
 // the device status word and nothing is written for that token.
 #include "common.cuh"
 #include "host.h"
+#include "splitk.cuh"
 
 namespace mvb {
 namespace {
@@ -21,7 +22,8 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     int64_t qkv_stride, const __nv_bfloat16* __restrict__ qnw, const __nv_bfloat16* __restrict__ knw,
     const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t, int64_t table_len,
     const int32_t* __restrict__ positions, const int32_t* __restrict__ block_tables, int64_t max_blocks, int batch,
-    int nq, int nkv, int64_t layer, int64_t num_blocks, int bs, float eps, unsigned* err) {
+    int nq, int nkv, int64_t layer, int64_t num_blocks, int bs, float eps, unsigned* err,
+    const float* __restrict__ partials, SplitKPlan plan) {
   constexpr int E = D / 32;
   pdl_launch_dependents();
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -36,10 +38,24 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
   const int d0 = lane * E;
 
   pdl_wait();
-  const __nv_bfloat16* src = qkv + static_cast<int64_t>(b) * qkv_stride + static_cast<int64_t>(h) * D + d0;
+  const __nv_bfloat16* src =
+      partials ? nullptr : qkv + static_cast<int64_t>(b) * qkv_stride + static_cast<int64_t>(h) * D + d0;
   float x[E];
+  if (partials == nullptr) {
 #pragma unroll
-  for (int e = 0; e < E; ++e) x[e] = __bfloat162float(src[e]);
+    for (int e = 0; e < E; ++e) x[e] = __bfloat162float(src[e]);
+  } else {
+    // The projection's bf16 output, formed from the GEMM's split-K partial slots.
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const int n = h * D + d0 + e;
+      const int t = n / kSplitBM, r = n - t * kSplitBM;
+      const int nc = sk_count(plan, t);
+      float acc = 0.0f;
+      for (int j = 0; j < nc; ++j) acc += __ldcg(partials + sk_offset(plan, t, j, b, r));
+      x[e] = bf16_round(acc);
+    }
+  }
 
   const int pos = positions[b];
   const bool is_q = h < nq, is_k = !is_q && h < nq + nkv;
@@ -115,14 +131,14 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
 
 using namespace mvb;
 
-extern "C" int mvb_qk_norm_rope_kv_write(void* q_out, void* kv_cache, const void* qkv, int64_t qkv_stride,
-                                         const void* q_norm_w, const void* k_norm_w, const void* cos,
-                                         const void* sin, int64_t table_len, const int32_t* positions,
-                                         const int32_t* block_tables, int64_t max_blocks, int64_t batch,
-                                         int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
-                                         int64_t num_layers, int64_t layer, int64_t num_blocks, int64_t block_size,
-                                         float eps, mvb_stream_t stream) {
-  MVB_REQUIRE(q_out && kv_cache && qkv && cos && sin && positions && block_tables,
+static int qk_norm_rope_kv_write_impl(void* q_out, void* kv_cache, const void* qkv, int64_t qkv_stride,
+                                      const void* q_norm_w, const void* k_norm_w, const void* cos, const void* sin,
+                                      int64_t table_len, const int32_t* positions, const int32_t* block_tables,
+                                      int64_t max_blocks, int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+                                      int64_t head_dim, int64_t num_layers, int64_t layer, int64_t num_blocks,
+                                      int64_t block_size, float eps, const float* partials, SplitKPlan plan,
+                                      mvb_stream_t stream) {
+  MVB_REQUIRE(q_out && kv_cache && (qkv || partials) && cos && sin && positions && block_tables,
               "mvb_qk_norm_rope_kv_write: null pointer");
   MVB_REQUIRE((q_norm_w == nullptr) == (k_norm_w == nullptr),
               "mvb_qk_norm_rope_kv_write: pass both norm weights or neither");
@@ -130,7 +146,8 @@ extern "C" int mvb_qk_norm_rope_kv_write(void* q_out, void* kv_cache, const void
               "mvb_qk_norm_rope_kv_write: bad head counts");
   MVB_REQUIRE(layer >= 0 && layer < num_layers && num_blocks > 0 && block_size > 0 && max_blocks > 0,
               "mvb_qk_norm_rope_kv_write: bad cache geometry");
-  MVB_REQUIRE(qkv_stride >= (num_q_heads + 2 * num_kv_heads) * head_dim, "mvb_qk_norm_rope_kv_write: qkv_stride");
+  MVB_REQUIRE(partials || qkv_stride >= (num_q_heads + 2 * num_kv_heads) * head_dim,
+              "mvb_qk_norm_rope_kv_write: qkv_stride");
   if (batch == 0) return MVB_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   unsigned* err = device_status_ptr();
@@ -141,7 +158,7 @@ extern "C" int mvb_qk_norm_rope_kv_write(void* q_out, void* kv_cache, const void
                 (__nv_bfloat16*)kv_cache, (const __nv_bfloat16*)qkv, qkv_stride, (const __nv_bfloat16*)q_norm_w, \
                 (const __nv_bfloat16*)k_norm_w, (const __nv_bfloat16*)cos, (const __nv_bfloat16*)sin, table_len,  \
                 positions, block_tables, max_blocks, (int)batch, (int)num_q_heads, (int)num_kv_heads, layer,     \
-                num_blocks, (int)block_size, eps, err)
+                num_blocks, (int)block_size, eps, err, partials, plan)
   switch (head_dim) {
     case 64: MVB_QKR_LAUNCH(64);
     case 128: MVB_QKR_LAUNCH(128);
@@ -149,4 +166,35 @@ extern "C" int mvb_qk_norm_rope_kv_write(void* q_out, void* kv_cache, const void
     default: return fail(MVB_ERR_UNSUPPORTED, "mvb_qk_norm_rope_kv_write: head_dim %lld", (long long)head_dim);
   }
 #undef MVB_QKR_LAUNCH
+}
+
+extern "C" int mvb_qk_norm_rope_kv_write(void* q_out, void* kv_cache, const void* qkv, int64_t qkv_stride,
+                                         const void* q_norm_w, const void* k_norm_w, const void* cos,
+                                         const void* sin, int64_t table_len, const int32_t* positions,
+                                         const int32_t* block_tables, int64_t max_blocks, int64_t batch,
+                                         int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                                         int64_t num_layers, int64_t layer, int64_t num_blocks, int64_t block_size,
+                                         float eps, mvb_stream_t stream) {
+  return qk_norm_rope_kv_write_impl(q_out, kv_cache, qkv, qkv_stride, q_norm_w, k_norm_w, cos, sin, table_len,
+                                    positions, block_tables, max_blocks, batch, num_q_heads, num_kv_heads, head_dim,
+                                    num_layers, layer, num_blocks, block_size, eps, nullptr, SplitKPlan{}, stream);
+}
+
+extern "C" int mvb_qk_norm_rope_kv_write_gemm(void* q_out, void* kv_cache, const void* gemm_workspace,
+                                              int64_t gemm_k, const void* q_norm_w, const void* k_norm_w,
+                                              const void* cos, const void* sin, int64_t table_len,
+                                              const int32_t* positions, const int32_t* block_tables,
+                                              int64_t max_blocks, int64_t batch, int64_t num_q_heads,
+                                              int64_t num_kv_heads, int64_t head_dim, int64_t num_layers,
+                                              int64_t layer, int64_t num_blocks, int64_t block_size, float eps,
+                                              mvb_stream_t stream) {
+  MVB_REQUIRE(gemm_workspace && batch > 0 && batch <= 256 && gemm_k > 0 && gemm_k % kSplitBK == 0,
+              "mvb_qk_norm_rope_kv_write_gemm: bad arguments");
+  const int sms = current_sm_count();
+  MVB_REQUIRE(sms > 0, "mvb_qk_norm_rope_kv_write_gemm: no device");
+  const SplitKPlan plan = splitk_plan(batch, (num_q_heads + 2 * num_kv_heads) * head_dim, gemm_k, sms);
+  return qk_norm_rope_kv_write_impl(q_out, kv_cache, nullptr, 0, q_norm_w, k_norm_w, cos, sin, table_len,
+                                    positions, block_tables, max_blocks, batch, num_q_heads, num_kv_heads, head_dim,
+                                    num_layers, layer, num_blocks, block_size, eps,
+                                    static_cast<const float*>(gemm_workspace), plan, stream);
 }

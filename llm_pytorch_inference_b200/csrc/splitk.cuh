@@ -1,0 +1,72 @@
+// Stream-K work split of the decode GEMMs, shared by the GEMM and by the kernels that
+// consume its fp32 partials directly (MVB_EPI_PARTIALS).
+//
+// The linearised (output tile, k-block) space of T = tiles * kblocks k-blocks is cut into
+// `grid` contiguous ranges, CTA c owning [c*T/grid, (c+1)*T/grid).  The CTAs whose range meets
+// tile t are its contributors c_first(t)..c_last(t); contributor j = c - c_first(t) stores
+// its fp32 partial of the tile in slot t*maxc + j, laid out [bn batch columns][128 rows].
+// A consumer reads element (b, n) as the sum over j in contributor order (deterministic).
+#pragma once
+
+#include <stdint.h>
+
+namespace mvb {
+
+constexpr int kSplitBM = 128;  // output features per tile
+constexpr int kSplitBK = 64;   // k per k-block
+
+struct SplitKPlan {
+  int grid;     // CTAs
+  int tiles;    // output tiles of 128 features
+  int kblocks;  // k / 64
+  int bn;       // batch columns per tile (64, 128 or 256)
+  int maxc;     // most contributors of any tile
+};
+
+__host__ __device__ __forceinline__ int64_t sk_range_start(int c, int64_t total, int grid) {
+  return static_cast<int64_t>(c) * total / grid;
+}
+
+// CTA whose range holds linear k-block x.
+__host__ __device__ __forceinline__ int sk_cta_of(int64_t x, int64_t total, int grid) {
+  return static_cast<int>(((x + 1) * grid + total - 1) / total - 1);
+}
+
+__host__ __device__ __forceinline__ int sk_first(const SplitKPlan& p, int t) {
+  return sk_cta_of(static_cast<int64_t>(t) * p.kblocks, static_cast<int64_t>(p.tiles) * p.kblocks, p.grid);
+}
+
+__host__ __device__ __forceinline__ int sk_count(const SplitKPlan& p, int t) {
+  const int64_t total = static_cast<int64_t>(p.tiles) * p.kblocks;
+  return sk_cta_of(static_cast<int64_t>(t + 1) * p.kblocks - 1, total, p.grid) -
+         sk_cta_of(static_cast<int64_t>(t) * p.kblocks, total, p.grid) + 1;
+}
+
+// Offset (floats) of element (column b, row r) of contributor j of tile t.
+__host__ __device__ __forceinline__ int64_t sk_offset(const SplitKPlan& p, int t, int j, int b, int r) {
+  return ((static_cast<int64_t>(t) * p.maxc + j) * p.bn + b) * kSplitBM + r;
+}
+
+inline int sk_bn_for(int64_t m) { return m <= 64 ? 64 : (m <= 128 ? 128 : 256); }
+
+// The plan the GEMM uses for a plain (non-SwiGLU) m x n x k product on `sms` SMs.
+inline SplitKPlan splitk_plan(int64_t m, int64_t n, int64_t k, int sms) {
+  SplitKPlan p;
+  p.tiles = static_cast<int>((n + kSplitBM - 1) / kSplitBM);
+  p.kblocks = static_cast<int>(k / kSplitBK);
+  const int64_t total = static_cast<int64_t>(p.tiles) * p.kblocks;
+  p.grid = static_cast<int>(total < sms ? total : sms);
+  p.bn = sk_bn_for(m);
+  p.maxc = 1;
+  for (int t = 0; t < p.tiles; ++t) {
+    const int c = sk_count(p, t);
+    if (c > p.maxc) p.maxc = c;
+  }
+  return p;
+}
+
+inline int64_t splitk_partials_bytes(const SplitKPlan& p) {
+  return static_cast<int64_t>(p.tiles) * p.maxc * p.bn * kSplitBM * 4;
+}
+
+}  // namespace mvb

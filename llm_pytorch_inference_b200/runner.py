@@ -194,9 +194,12 @@ class DecodeRunner:
 
     # ------------------------------------------------------------------- step
     def _gemm(self, y, x, w, epilogue=N.EPI_STORE, aux=None):
+        """y = x @ w.T on the tcgen05 GEMM; with EPI_PARTIALS (y None) the result stays in the
+        workspace as split-K partials for the next kernel to reduce."""
         lib = N.lib()
         B = self.B
-        N.check(lib.mvb_gemm_bf16(y.data_ptr(), y.stride(0), x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), B,
+        N.check(lib.mvb_gemm_bf16(N.ptr(y), 0 if y is None else y.stride(0), x.data_ptr(), x.stride(0),
+                                  w.data_ptr(), w.stride(0), B,
                                   w.shape[0], w.shape[1], epilogue, N.ptr(aux), 0 if aux is None else aux.stride(0),
                                   self.gemm_ws.data_ptr(), self.gemm_ws.numel(), self._st), "gemm_bf16")
 
@@ -210,32 +213,32 @@ class DecodeRunner:
                                   self.V, 1.0, bf, st), "embedding")
         N.check(lib.mvb_rmsnorm(self.xn.data_ptr(), H, self.residual.data_ptr(), H, w.ln1[0].data_ptr(), B, H, eps, 0,
                                 N.NORM_MODEL, bf, st), "rmsnorm")
+        ws = self.gemm_ws.data_ptr()
         for i in range(self.L):
-            if i > 0:
-                N.check(lib.mvb_fused_add_rmsnorm(self.xn.data_ptr(), self.residual.data_ptr(), self.mlp.data_ptr(),
-                                                  w.ln1[i].data_ptr(), B, H, eps, 0, N.NORM_MODEL, bf, st),
-                        "fused_add_rmsnorm")
-            self._gemm(self.qkv, self.xn, w.wqkv[i])
-            N.check(lib.mvb_qk_norm_rope_kv_write(
-                self.q.data_ptr(), kvc.data_ptr(), self.qkv.data_ptr(), self.qkv.stride(0),
+            if i > 0:   # residual += down_proj output (split-K partials), then input_layernorm
+                N.check(lib.mvb_fused_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(), ws, B, H,
+                                                       self.I, w.ln1[i].data_ptr(), eps, 0, st),
+                        "fused_add_rmsnorm_gemm")
+            self._gemm(None, self.xn, w.wqkv[i], N.EPI_PARTIALS)
+            N.check(lib.mvb_qk_norm_rope_kv_write_gemm(
+                self.q.data_ptr(), kvc.data_ptr(), ws, H,
                 w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
                 self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0], self.pos.data_ptr(),
                 self.block_tables.data_ptr(), self.max_blocks, B, self.Hq, self.Hkv, self.D, self.L, i, self.P,
-                self.kv.block_size, eps, st), "qk_norm_rope_kv_write")
+                self.kv.block_size, eps, st), "qk_norm_rope_kv_write_gemm")
             N.check(lib.mvb_paged_attention_decode(
                 self.attn.data_ptr(), self.attn.stride(0), self.q.data_ptr(), self.Hq * self.D, kvc.data_ptr(),
                 self.block_tables.data_ptr(), self.max_blocks, self.ctx.data_ptr(), B, self.Hq, self.Hkv, self.D,
                 self.L, i, self.P, self.kv.block_size, self.scale, self.attn_ws.data_ptr(), self.attn_ws.numel(), st),
                 "paged_attention_decode")
-            self._gemm(self.o, self.attn, w.wo[i])
-            N.check(lib.mvb_fused_add_rmsnorm(self.xn.data_ptr(), self.residual.data_ptr(), self.o.data_ptr(),
-                                              w.ln2[i].data_ptr(), B, H, eps, 0, N.NORM_MODEL, bf, st),
-                    "fused_add_rmsnorm")
+            self._gemm(None, self.attn, w.wo[i], N.EPI_PARTIALS)
+            N.check(lib.mvb_fused_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(), ws, B, H,
+                                                   self.Hq * self.D, w.ln2[i].data_ptr(), eps, 0, st),
+                    "fused_add_rmsnorm_gemm")
             self._gemm(self.h, self.xn, w.wgu[i], N.EPI_SWIGLU)
-            self._gemm(self.mlp, self.h, w.wdown[i])
-        N.check(lib.mvb_fused_add_rmsnorm(self.xn.data_ptr(), self.residual.data_ptr(), self.mlp.data_ptr(),
-                                          w.final_norm.data_ptr(), B, H, eps, 0, N.NORM_MODEL, bf, st),
-                "fused_add_rmsnorm")
+            self._gemm(None, self.h, w.wdown[i], N.EPI_PARTIALS)
+        N.check(lib.mvb_fused_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(), ws, B, H, self.I,
+                                               w.final_norm.data_ptr(), eps, 0, st), "fused_add_rmsnorm_gemm")
         self._gemm(self.logits, self.xn, w.lm_head)
         N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
                                self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
@@ -254,8 +257,8 @@ class DecodeRunner:
             return n * k * 2 + B * k * 2 + B * out_cols * 2
 
         def qk(i):
-            N.check(lib.mvb_qk_norm_rope_kv_write(
-                self.q.data_ptr(), kvc.data_ptr(), self.qkv.data_ptr(), self.qkv.stride(0),
+            N.check(lib.mvb_qk_norm_rope_kv_write_gemm(
+                self.q.data_ptr(), kvc.data_ptr(), self.gemm_ws.data_ptr(), H,
                 w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
                 self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0], self.pos.data_ptr(),
                 self.block_tables.data_ptr(), self.max_blocks, B, self.Hq, self.Hkv, D, self.L, i, self.P,
@@ -269,9 +272,9 @@ class DecodeRunner:
                 st), "paged_attention_decode")
 
         def fadd(i):
-            N.check(lib.mvb_fused_add_rmsnorm(self.xn.data_ptr(), self.residual.data_ptr(), self.o.data_ptr(),
-                                              w.ln2[i].data_ptr(), B, H, eps, 0, N.NORM_MODEL, bf, st),
-                    "fused_add_rmsnorm")
+            N.check(lib.mvb_fused_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(),
+                                                   self.gemm_ws.data_ptr(), B, H, self.Hq * D, w.ln2[i].data_ptr(),
+                                                   eps, 0, st), "fused_add_rmsnorm_gemm")
 
         def samp(i):
             N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
@@ -280,14 +283,14 @@ class DecodeRunner:
 
         return {
             "paged_attention_decode": (attn, self.L, kv_bytes + 2 * B * self.Hq * D * 2, 4 * int(ctx.sum()) * self.Hq * D),
-            "gemm_qkv": (lambda i: self._gemm(self.qkv, self.xn, w.wqkv[i]), self.L, gemm_bytes(qkv_n, H, qkv_n),
-                         2 * B * qkv_n * H),
-            "gemm_o_proj": (lambda i: self._gemm(self.o, self.attn, w.wo[i]), self.L,
-                            gemm_bytes(H, self.Hq * D, H), 2 * B * H * self.Hq * D),
+            "gemm_qkv": (lambda i: self._gemm(None, self.xn, w.wqkv[i], N.EPI_PARTIALS), self.L,
+                         gemm_bytes(qkv_n, H, 0), 2 * B * qkv_n * H),
+            "gemm_o_proj": (lambda i: self._gemm(None, self.attn, w.wo[i], N.EPI_PARTIALS), self.L,
+                            gemm_bytes(H, self.Hq * D, 0), 2 * B * H * self.Hq * D),
             "gemm_gate_up_swiglu": (lambda i: self._gemm(self.h, self.xn, w.wgu[i], N.EPI_SWIGLU), self.L,
                                     gemm_bytes(2 * self.I, H, self.I), 2 * B * 2 * self.I * H),
-            "gemm_down": (lambda i: self._gemm(self.mlp, self.h, w.wdown[i]), self.L, gemm_bytes(H, self.I, H),
-                          2 * B * H * self.I),
+            "gemm_down": (lambda i: self._gemm(None, self.h, w.wdown[i], N.EPI_PARTIALS), self.L,
+                          gemm_bytes(H, self.I, 0), 2 * B * H * self.I),
             "gemm_lm_head": (lambda i: self._gemm(self.logits, self.xn, w.lm_head), 1,
                              gemm_bytes(self.V, H, self.V), 2 * B * self.V * H),
             "qk_norm_rope_kv_write": (qk, self.L, B * qkv_n * 2 + B * self.Hq * D * 2 + 2 * B * self.Hkv * D * 2, 0),

@@ -157,6 +157,33 @@ def test_gemm_swiglu_and_resadd_epilogues():
     torch.testing.assert_close(y.float(), ref, rtol=1e-2, atol=2e-2)
 
 
+def _gemm_partials(x, w, ws):
+    N.check(N.lib().mvb_gemm_bf16(None, 0, x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), x.shape[0],
+                                  w.shape[0], w.shape[1], N.EPI_PARTIALS, None, 0, ws.data_ptr(), ws.numel(),
+                                  N.stream_handle()), "gemm partials")
+
+
+@pytest.mark.parametrize("m,n,k", [(64, 4096, 4096), (64, 4096, 12288), (13, 1024, 512)])
+def test_split_k_partials_feed_fused_add_rmsnorm_bit_exactly(m, n, k):
+    """GEMM(MVB_EPI_PARTIALS) + mvb_fused_add_rmsnorm_gemm == GEMM(STORE) + fused_add_rmsnorm (model
+    semantics): the consumer sums the same partials in the same order."""
+    g = torch.Generator(device=DEV).manual_seed(n + k)
+    x = (torch.randn(m, k, device=DEV, generator=g) / math.sqrt(k)).to(torch.bfloat16)
+    w = torch.randn(n, k, device=DEV, generator=g).to(torch.bfloat16)
+    ln = (1 + 0.1 * torch.randn(n, device=DEV, generator=g)).to(torch.bfloat16)
+    res0 = torch.randn(m, n, device=DEV, generator=g).to(torch.bfloat16)
+    y = ops.linear(x, w)
+    res_a, xn_a = res0.clone(), torch.empty_like(res0)
+    N.check(N.lib().mvb_fused_add_rmsnorm(xn_a.data_ptr(), res_a.data_ptr(), y.data_ptr(), ln.data_ptr(), m, n, 1e-6,
+                                          0, N.NORM_MODEL, N.BF16, N.stream_handle()), "fadd")
+    ws = torch.zeros(N.lib().mvb_gemm_workspace_bytes(m, n, k, 0), dtype=torch.uint8, device=DEV)
+    _gemm_partials(x, w, ws)
+    res_b, xn_b = res0.clone(), torch.empty_like(res0)
+    N.check(N.lib().mvb_fused_add_rmsnorm_gemm(xn_b.data_ptr(), res_b.data_ptr(), ws.data_ptr(), m, n, k,
+                                               ln.data_ptr(), 1e-6, 0, N.stream_handle()), "fadd gemm")
+    assert torch.equal(res_a, res_b) and torch.equal(xn_a, xn_b)
+
+
 # ------------------------------------------------- QK-norm + RoPE + paged KV write
 def _pool(L, P, nkv, D, seed):
     g = torch.Generator().manual_seed(seed)
@@ -202,6 +229,31 @@ def test_qk_norm_rope_kv_write_indexing_is_bit_exact():
     assert torch.equal(changed_got, changed_exp)          # exactly the same slots written
     assert bf16_ulps(got, expect) <= 1
     assert bf16_ulps(q.cpu(), qo[:, :, 0]) <= 1
+
+
+def test_qk_norm_rope_kv_write_from_split_k_partials_bit_exact():
+    B, Hq, Hkv, D, L, P, H = 64, 32, 8, 128, 2, 300, 4096
+    g = torch.Generator(device=DEV).manual_seed(5)
+    x = (torch.randn(B, H, device=DEV, generator=g) / math.sqrt(H)).to(torch.bfloat16)
+    wqkv = torch.randn((Hq + 2 * Hkv) * D, H, device=DEV, generator=g).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(D, device=DEV, generator=g)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(D, device=DEV, generator=g)).to(torch.bfloat16)
+    cos, sin = om.rope_tables(D, 1e6, 256, torch.bfloat16)
+    cos, sin = cos.to(DEV), sin.to(DEV)
+    pos = torch.randint(0, 64, (B,), device=DEV, dtype=torch.int32)
+    bt = torch.randperm(P, device=DEV)[:B * 4].to(torch.int32).view(B, 4)
+    pool_a = torch.zeros(L, 2, P + 1, 16, Hkv, D, dtype=torch.bfloat16, device=DEV)
+    pool_b = pool_a.clone()
+    qkv = ops.linear(x, wqkv)
+    q_a = ops.qk_norm_rope_kv_write(qkv, pool_a, 1, pos, bt, cos, sin, Hq, Hkv, qn, kn, 1e-6)
+    ws = torch.zeros(N.lib().mvb_gemm_workspace_bytes(B, wqkv.shape[0], H, 0), dtype=torch.uint8, device=DEV)
+    _gemm_partials(x, wqkv, ws)
+    q_b = torch.empty_like(q_a)
+    N.check(N.lib().mvb_qk_norm_rope_kv_write_gemm(
+        q_b.data_ptr(), pool_b.data_ptr(), ws.data_ptr(), H, qn.data_ptr(), kn.data_ptr(), cos.data_ptr(),
+        sin.data_ptr(), cos.shape[0], pos.data_ptr(), bt.data_ptr(), 4, B, Hq, Hkv, D, L, 1, P + 1, 16, 1e-6,
+        N.stream_handle()), "qk gemm")
+    assert torch.equal(q_a, q_b) and torch.equal(pool_a, pool_b)
 
 
 def test_kv_write_bad_block_is_reported_not_faulted():
