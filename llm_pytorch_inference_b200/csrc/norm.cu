@@ -82,33 +82,78 @@ __global__ void fused_add_rmsnorm_kernel(T* __restrict__ out, T* __restrict__ re
 }
 
 // Residual add + RMSNorm whose input is a GEMM's output still in split-K partial form: the
-// linear layer's bf16 output is formed here as bf16(sum of the tile's partial slots), then
-// residual += it and out = RMSNorm(residual) (model semantics, models/model.py:19-25, :319).
+// linear layer's bf16 output is formed here as bf16(sum of the tile's partial slots, contributor
+// order), then residual += it and out = RMSNorm(residual) (model semantics, models/model.py:19-25,
+// :319).  Each thread owns runs of 4 consecutive features (float4 partial loads, 8-byte residual
+// loads) and keeps its values in registers between the two passes; per-tile contributor counts
+// are computed once per CTA.  Supports hidden % 4 == 0 and hidden <= 16 * blockDim.
+constexpr int kFaddMaxRuns = 4;
+constexpr int kFaddMaxTiles = 256;
+
 __global__ void fused_add_rmsnorm_gemm_kernel(__nv_bfloat16* __restrict__ out, __nv_bfloat16* __restrict__ residual,
                                               const float* __restrict__ partials, SplitKPlan p,
                                               const __nv_bfloat16* __restrict__ w, int hidden, float eps,
                                               int plus_one) {
   __shared__ float red[32];
+  __shared__ unsigned char s_nc[kFaddMaxTiles];
   pdl_launch_dependents();
+  const int tiles = (hidden + kSplitBM - 1) / kSplitBM;
+  for (int t = threadIdx.x; t < tiles; t += blockDim.x) s_nc[t] = static_cast<unsigned char>(sk_count(p, t));
   pdl_wait();
+  __syncthreads();
   const int b = blockIdx.x;
   __nv_bfloat16* res = residual + static_cast<int64_t>(b) * hidden;
   __nv_bfloat16* y = out + static_cast<int64_t>(b) * hidden;
+  float v[kFaddMaxRuns][4];
   float ss = 0.0f;
-  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
-    const int t = i / kSplitBM, r = i - t * kSplitBM;
-    const int nc = sk_count(p, t);
-    float acc = 0.0f;
-    for (int j = 0; j < nc; ++j) acc += __ldcg(partials + sk_offset(p, t, j, b, r));
-    const float v = bf16_round(__bfloat162float(res[i]) + bf16_round(acc));
-    res[i] = __float2bfloat16_rn(v);
-    ss += v * v;
+#pragma unroll
+  for (int k = 0; k < kFaddMaxRuns; ++k) {
+    const int i = (threadIdx.x + k * blockDim.x) * 4;
+    if (i < hidden) {
+      const int t = i / kSplitBM, r = i - t * kSplitBM;
+      const int nc = s_nc[t];
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < nc; ++j) {
+        const float4 q = __ldcg(reinterpret_cast<const float4*>(partials + sk_offset(p, t, j, b, r)));
+        acc.x += q.x;
+        acc.y += q.y;
+        acc.z += q.z;
+        acc.w += q.w;
+      }
+      const uint2 rr = *reinterpret_cast<const uint2*>(res + i);
+      const __nv_bfloat162 r01 = *reinterpret_cast<const __nv_bfloat162*>(&rr.x);
+      const __nv_bfloat162 r23 = *reinterpret_cast<const __nv_bfloat162*>(&rr.y);
+      v[k][0] = bf16_round(__low2float(r01) + bf16_round(acc.x));
+      v[k][1] = bf16_round(__high2float(r01) + bf16_round(acc.y));
+      v[k][2] = bf16_round(__low2float(r23) + bf16_round(acc.z));
+      v[k][3] = bf16_round(__high2float(r23) + bf16_round(acc.w));
+      __nv_bfloat162 o01 = __floats2bfloat162_rn(v[k][0], v[k][1]);
+      __nv_bfloat162 o23 = __floats2bfloat162_rn(v[k][2], v[k][3]);
+      uint2 ov;
+      ov.x = *reinterpret_cast<uint32_t*>(&o01);
+      ov.y = *reinterpret_cast<uint32_t*>(&o23);
+      *reinterpret_cast<uint2*>(res + i) = ov;
+      ss += v[k][0] * v[k][0] + v[k][1] * v[k][1] + v[k][2] * v[k][2] + v[k][3] * v[k][3];
+    }
   }
   ss = block_sum(ss, red);
   const float rr = 1.0f / sqrtf(ss / static_cast<float>(hidden) + eps);
-  for (int i = threadIdx.x; i < hidden; i += blockDim.x)
-    y[i] = __float2bfloat16_rn(norm_out<__nv_bfloat16>(__bfloat162float(res[i]), __bfloat162float(w[i]), rr,
-                                                       plus_one, MVB_NORM_MODEL, true));
+#pragma unroll
+  for (int k = 0; k < kFaddMaxRuns; ++k) {
+    const int i = (threadIdx.x + k * blockDim.x) * 4;
+    if (i < hidden) {
+      float o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        o[e] = norm_out<__nv_bfloat16>(v[k][e], __bfloat162float(w[i + e]), rr, plus_one, MVB_NORM_MODEL, true);
+      __nv_bfloat162 o01 = __floats2bfloat162_rn(o[0], o[1]);
+      __nv_bfloat162 o23 = __floats2bfloat162_rn(o[2], o[3]);
+      uint2 ov;
+      ov.x = *reinterpret_cast<uint32_t*>(&o01);
+      ov.y = *reinterpret_cast<uint32_t*>(&o23);
+      *reinterpret_cast<uint2*>(y + i) = ov;
+    }
+  }
 }
 
 int threads_for(int64_t hidden) {
@@ -182,9 +227,16 @@ extern "C" int mvb_fused_add_rmsnorm_gemm(void* out, void* residual, const void*
               "mvb_fused_add_rmsnorm_gemm: bad shape");
   const int sms = current_sm_count();
   MVB_REQUIRE(sms > 0, "mvb_fused_add_rmsnorm_gemm: no device");
+  MVB_REQUIRE(hidden % 4 == 0 && hidden <= 4 * 1024 * kFaddMaxRuns && (hidden + 127) / 128 <= kFaddMaxTiles,
+              "mvb_fused_add_rmsnorm_gemm: hidden %lld must be a multiple of 4 and <= 16384", (long long)hidden);
+  MVB_REQUIRE(aligned(residual, 8) && aligned(out, 8), "mvb_fused_add_rmsnorm_gemm: 8-byte alignment");
   const SplitKPlan p = splitk_plan(rows, hidden, gemm_k, sms);
+  MVB_REQUIRE(p.maxc <= 255, "mvb_fused_add_rmsnorm_gemm: too many split-K contributors");
+  int threads = static_cast<int>((hidden / 4 + kFaddMaxRuns - 1) / kFaddMaxRuns);
+  threads = (threads + 31) / 32 * 32;
+  if (threads < 128) threads = 128;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return launch("fused_add_rmsnorm_gemm", fused_add_rmsnorm_gemm_kernel, dim3(static_cast<unsigned>(rows)),
-                dim3(threads_for(hidden)), 0, st, (__nv_bfloat16*)out, (__nv_bfloat16*)residual,
+                dim3(threads), 0, st, (__nv_bfloat16*)out, (__nv_bfloat16*)residual,
                 (const float*)gemm_workspace, p, (const __nv_bfloat16*)weight, (int)hidden, eps, plus_one);
 }

@@ -45,16 +45,32 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
 #pragma unroll
     for (int e = 0; e < E; ++e) x[e] = __bfloat162float(src[e]);
   } else {
-    // The projection's bf16 output, formed from the GEMM's split-K partial slots.
+    // The projection's bf16 output, formed from the GEMM's split-K partial slots: the lane's E
+    // consecutive features sit in one 128-feature tile, read as float4 per contributor.
+    const int n0 = h * D + d0;
+    const int t = n0 / kSplitBM, r = n0 - t * kSplitBM;
+    const int nc = sk_count(plan, t);
+    float acc[E];
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const int n = h * D + d0 + e;
-      const int t = n / kSplitBM, r = n - t * kSplitBM;
-      const int nc = sk_count(plan, t);
-      float acc = 0.0f;
-      for (int j = 0; j < nc; ++j) acc += __ldcg(partials + sk_offset(plan, t, j, b, r));
-      x[e] = bf16_round(acc);
+    for (int e = 0; e < E; ++e) acc[e] = 0.0f;
+    for (int j = 0; j < nc; ++j) {
+      const float* src_p = partials + sk_offset(plan, t, j, b, r);
+      if constexpr (E % 4 == 0) {
+#pragma unroll
+        for (int e4 = 0; e4 < E; e4 += 4) {
+          const float4 q = __ldcg(reinterpret_cast<const float4*>(src_p + e4));
+          acc[e4] += q.x;
+          acc[e4 + 1] += q.y;
+          acc[e4 + 2] += q.z;
+          acc[e4 + 3] += q.w;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] += __ldcg(src_p + e);
+      }
     }
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = bf16_round(acc[e]);
   }
 
   const int pos = positions[b];
