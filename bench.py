@@ -71,7 +71,7 @@ def dist_setup(n_gpus: int):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return rank, world, local
@@ -257,28 +257,32 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
     from llm_pytorch_inference_b200 import _native as N
     from llm_pytorch_inference_b200.configs import get_config
     from llm_pytorch_inference_b200.engine import DecodeEngine
+    from llm_pytorch_inference_b200.tensor_parallel import TensorParallelConfig
     from llm_pytorch_inference_b200.weights import canonical_state_dict
 
     dev = torch.device("cuda", local)
     N.set_pdl(bool(args.pdl))
     overrides = {} if args.layers is None else {"num_hidden_layers": args.layers}
     cfg = get_config(ARCH, **overrides)
-    sd = canonical_state_dict(cfg, seed=rank, dtype=torch.bfloat16, device=dev)
+    # N GPUs = one tensor-parallel group over the same batch-64 workload (strong scaling): every
+    # rank builds the same model and sequences and keeps its shard.
+    tp = TensorParallelConfig(world, rank)
+    sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev)
     W, K = args.warmup, args.steps
     max_len = PROMPT + 1 + W + 2 * K + 16
     free_order_seed = 0
-    eng = DecodeEngine(cfg, sd, max_batch=BATCH, max_model_len=max_len, device=dev)
+    eng = DecodeEngine(cfg, sd, max_batch=BATCH, max_model_len=max_len, device=dev, tp=tp)
     del sd
     order = list(range(eng.kv.num_blocks))
     random.Random(free_order_seed).shuffle(order)
     from collections import deque
 
     eng.kv.free_blocks = deque(order)
-    g = torch.Generator().manual_seed(1 + rank)
+    g = torch.Generator().manual_seed(1)
     for s in range(BATCH):
         eng.add_sequence(s, torch.randint(0, cfg["vocab_size"], (PROMPT,), generator=g).tolist())
         eng.append_first_token(s, int(torch.randint(0, cfg["vocab_size"], (1,), generator=g)))
-    eng.prefill_synthetic(seed=rank)
+    eng.prefill_synthetic(seed=rank)   # each rank fills its own KV heads
     eng.set_sampling(*SAMPLING, seed=1234)
     eng.prepare_first_step()
     r = eng.runner
@@ -330,28 +334,30 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
             "frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": pk["source"],
             "traffic": traffic, "algorithmic_bytes_per_launch": top["bytes_per_launch"],
             "avg_launch_ms": round(top["avg_ms"], 5), "share_of_step": round(top["share"], 3)}
-    # whole-step roofline: algorithmic bytes of every launch in one step / step time
-    step_bytes = sum(v["bytes_per_launch"] * v["launches_per_step"] for v in kinds.values())
+    # whole-step roofline: weights + KV read + KV write of one step / step time
+    step_bytes = r.algorithmic_step_bytes()
     step_roof = {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (step_ms * 1e-3) / 1e9, 1),
                  "frac": round(step_bytes / (step_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
 
+    barrier(world)
+    r.close()   # graph, then the symmetric heap (every rank, before the process group goes)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline()
     if rank != 0:
         return
     h2d = r.meta_host.numel() * r.meta_host.element_size()
-    value = BATCH * world * K / (dev_ms * 1e-3)
-    e2e = BATCH * world * K / (e2e_ms * 1e-3)
+    value = BATCH * K / (dev_ms * 1e-3)
+    e2e = BATCH * K / (e2e_ms * 1e-3)
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{ARCH} decode, batch {BATCH} per GPU, prompt {PROMPT}, T/top-k/top-p "
+        "config": {"workload": f"{ARCH} decode, batch {BATCH}, prompt {PROMPT}, T/top-k/top-p "
                                f"{SAMPLING[0]}/{SAMPLING[1]}/{SAMPLING[2]}",
-                   "model": ARCH, "layers": cfg["num_hidden_layers"], "global_batch": BATCH * world,
+                   "model": ARCH, "layers": cfg["num_hidden_layers"], "global_batch": BATCH,
                    "seq_len": PROMPT, "context_during_timing": [PROMPT + 1 + W, PROMPT + 1 + W + 2 * K],
-                   "parallelism": f"replica{world}" if world > 1 else "tp1",
+                   "parallelism": f"tp{world}",
                    "l2": "inputs larger than L2: 15.1 GB weights + ~20 GB KV read per step",
                    "kv_pool_blocks": eng.kv.num_blocks, "pdl": bool(args.pdl)},
         "roofline": roof, "step_roofline": step_roof,

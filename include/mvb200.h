@@ -214,6 +214,8 @@ int mvb_paged_attention_decode_noalloc(void* out, int64_t out_stride, const void
  *           MVB_EPI_PARTIALS  no Y (y may be NULL): every stream-K segment leaves its fp32 partial in
  *                          the workspace for a consuming kernel to sum (mvb_fused_add_rmsnorm_gemm,
  *                          mvb_qk_norm_rope_kv_write_gemm); the GEMM then ends without a merge
+ *           MVB_EPI_SWIGLU_PARTIALS  the SWIGLU pairing of W's rows with MVB_EPI_PARTIALS' output:
+ *                          fp32 partials of gate and up features, finished by mvb_swiglu_gemm
  * Requires k % 64 == 0, ldx/ldw/ldy multiples of 8, 16-byte aligned pointers, m <= 256.
  * workspace: >= mvb_gemm_workspace_bytes(m, n, k, device); zero before the first call.  fp32
  * partials use its head, per-tile counters its tail; the kernel leaves the counters zero, so
@@ -223,10 +225,72 @@ int mvb_paged_attention_decode_noalloc(void* out, int64_t out_stride, const void
 #define MVB_EPI_SWIGLU 1
 #define MVB_EPI_RESADD 2
 #define MVB_EPI_PARTIALS 3
+#define MVB_EPI_SWIGLU_PARTIALS 4
 int64_t mvb_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int device);
 int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t m,
                   int64_t n, int64_t k, int epilogue, const void* aux, int64_t ld_aux, void* workspace,
                   int64_t workspace_bytes, mvb_stream_t stream);
+
+/* The activation of FusedMLP (ops/mlp.py:65-84; mlp_kernel.cu:17-36 with SiLU) applied to a
+ * gate_up product still in split-K partial form: `gemm_workspace` is the workspace of the
+ * preceding mvb_gemm_bf16(MVB_EPI_SWIGLU_PARTIALS) call of shape [rows, 2 * inter, gemm_k];
+ * out[r, j] = bf16(bf16(silu(bf16(gate))) * bf16(up)) for j < inter, the same values
+ * MVB_EPI_SWIGLU writes.  Requires inter % 4 == 0, out_stride % 4 == 0, 8-byte aligned out. */
+int mvb_swiglu_gemm(void* out, int64_t out_stride, const void* gemm_workspace, int64_t rows, int64_t inter,
+                    int64_t gemm_k, mvb_stream_t stream);
+
+/* ---- tensor parallelism (one process per GPU, NVLink peer memory) ----------------------
+ * No counterpart in the reference beyond its stub (distributed/tensor_parallel.py:14-35,
+ * tp_size > 1 raises).  These replace the NCCL all-reduce a Megatron-style split of the decode
+ * step would need after each row-parallel GEMM, and the all-gather of vocab-parallel logits.
+ *
+ * Symmetric heap: every rank calls mvb_tp_heap_alloc with the same size (one cudaMalloc,
+ * zeroed; the first mvb_tp_signal_bytes() bytes are signal counters), exchanges the 64-byte
+ * IPC handles (e.g. with torch.distributed.all_gather_object), then calls mvb_tp_comm_init with
+ * all handles in rank order.  Buffers inside the heap are named by byte offset, the same on
+ * every rank.  Each step starts with mvb_tp_begin_step (a one-thread kernel that advances
+ * this rank's step counter on the device, so a CUDA graph of a step can be replayed), and
+ * every rank issues the same sequence of mvb_tp_* calls per step.  A wait for a peer gives up
+ * after 2 s and sets MVB_DEV_WAIT_TIMEOUT (the kernel then completes with whatever data
+ * arrived).
+ *
+ * Signal points are small integers (< 1024) chosen by the caller, one per exchange site in a
+ * step; a call that waits on a point must come after the call that signals it. */
+#define MVB_TP_IPC_HANDLE_BYTES 64
+typedef struct mvb_tp_comm mvb_tp_comm;
+int64_t mvb_tp_signal_bytes(void);
+int mvb_tp_heap_alloc(int64_t bytes, void** base, void* ipc_handle);
+int mvb_tp_heap_free(void* base);
+int mvb_tp_comm_init(int rank, int nranks, void* local_base, const void* ipc_handles, int64_t heap_bytes,
+                     mvb_tp_comm** comm);
+int mvb_tp_comm_destroy(mvb_tp_comm* comm);
+int mvb_tp_begin_step(mvb_tp_comm* comm, mvb_stream_t stream);
+/* Bytes of the receive area of a row-parallel (push) GEMM of shape [m, n, k_local]. */
+int64_t mvb_tp_recv_bytes(int64_t m, int64_t n, int64_t k, int nranks, int device);
+/* The tcgen05 GEMM of mvb_gemm_bf16 with the exchanges of a tensor-parallel step:
+ *   wait_point >= 0       X (a local buffer, e.g. inside the heap) is only read after every
+ *                         rank signalled wait_point this step;
+ *   MVB_EPI_PARTIALS with out_offset >= 0  (row-parallel o_proj / down_proj, model.py:180, :328)
+ *                         push: the fp32 split-K partials of batch row b go to the receive area
+ *                         at out_offset in the heap of rank b / (m / nranks); then signal_point;
+ *   MVB_EPI_STORE with out_offset >= 0  (vocab-parallel lm_head, model_cuda.py:413)
+ *                         all-gather: Y (this rank's n columns, row stride ldy) is stored at
+ *                         out_offset in every rank's heap; then signal_point;
+ *   MVB_EPI_PARTIALS / MVB_EPI_SWIGLU_PARTIALS with out_offset < 0  local partials in
+ *                         `workspace`, as mvb_gemm_bf16 (column-parallel q/k/v, gate/up). */
+int mvb_tp_gemm_bf16(mvb_tp_comm* comm, const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t m, int64_t n,
+                     int64_t k, int epilogue, void* workspace, int64_t workspace_bytes, int64_t out_offset,
+                     int64_t ldy, int wait_point, int signal_point, mvb_stream_t stream);
+/* The all-reduce + residual add + RMSNorm after a push GEMM of shape [rows, hidden, gemm_k]
+ * (model.py:319-322, :328 + the next RMSNorm): for the rows this rank owns, waits for
+ * wait_point, sums the pushed partials over ranks, residual += bf16(sum) (the residual of a row
+ * is kept by its owner only), and writes RMSNorm(residual) into every rank's [rows, hidden]
+ * bf16 buffer at out_offset; then signal_point. */
+int mvb_tp_fused_add_rmsnorm_gemm(mvb_tp_comm* comm, void* residual, int64_t rows, int64_t hidden, int64_t gemm_k,
+                                  const void* weight, float eps, int plus_one, int64_t recv_offset, int wait_point,
+                                  int64_t out_offset, int signal_point, mvb_stream_t stream);
+/* Stream-ordered wait (one tiny kernel) until every rank signalled `point` this step. */
+int mvb_tp_wait(mvb_tp_comm* comm, int point, mvb_stream_t stream);
 
 /* ---- programmatic dependent launch -------------------------------------------
  * When enabled (default off), kernels of this library are launched with the PDL

@@ -18,10 +18,11 @@ MVB_OK = 0
 F32, F16, BF16, I32, I64 = 0, 1, 2, 3, 4
 NORM_OPS, NORM_MODEL = 0, 1
 ACT_SILU, ACT_GELU_TANH = 0, 1
-EPI_STORE, EPI_SWIGLU, EPI_RESADD, EPI_PARTIALS = 0, 1, 2, 3
+EPI_STORE, EPI_SWIGLU, EPI_RESADD, EPI_PARTIALS, EPI_SWIGLU_PARTIALS = 0, 1, 2, 3, 4
 DEV_WAIT_TIMEOUT, DEV_BAD_BLOCK, DEV_BAD_POSITION, DEV_BAD_TOKEN, DEV_SAMPLER_TIES = 0x1, 0x2, 0x4, 0x8, 0x10
 
 _vp, _i64, _i32, _f32, _u64, _u32p = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_uint64, C.POINTER(C.c_uint)
+_vpp = C.POINTER(C.c_void_p)
 
 # name -> (restype, argtypes); the exact list of entry points the header declares.
 SIGNATURES: dict[str, tuple] = {
@@ -54,6 +55,19 @@ SIGNATURES: dict[str, tuple] = {
                                                   _i64, _i64, _i64, _i64, _i64, _f32, _vp]),
     "mvb_gemm_workspace_bytes": (_i64, [_i64, _i64, _i64, _i32]),
     "mvb_gemm_bf16": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i32, _vp, _i64, _vp, _i64, _vp]),
+    "mvb_swiglu_gemm": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _vp]),
+    "mvb_tp_signal_bytes": (_i64, []),
+    "mvb_tp_heap_alloc": (_i32, [_i64, _vpp, C.c_char_p]),
+    "mvb_tp_heap_free": (_i32, [_vp]),
+    "mvb_tp_comm_init": (_i32, [_i32, _i32, _vp, C.c_char_p, _i64, _vpp]),
+    "mvb_tp_comm_destroy": (_i32, [_vp]),
+    "mvb_tp_begin_step": (_i32, [_vp, _vp]),
+    "mvb_tp_recv_bytes": (_i64, [_i64, _i64, _i64, _i32, _i32]),
+    "mvb_tp_gemm_bf16": (_i32, [_vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i32, _vp, _i64, _i64, _i64, _i32, _i32,
+                                _vp]),
+    "mvb_tp_fused_add_rmsnorm_gemm": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _f32, _i32, _i64, _i32, _i64, _i32,
+                                             _vp]),
+    "mvb_tp_wait": (_i32, [_vp, _i32, _vp]),
 }
 
 _lock = threading.Lock()

@@ -223,6 +223,60 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ------------------------------------------------------------------ cross-GPU signals
+// Tensor-parallel kernels exchange data through peer (CUDA IPC) memory and announce it with
+// monotonically increasing 32-bit counters: every signalling CTA adds 1 to a counter in each
+// rank's memory after its stores, so after step e (e >= 1) a point that `count` CTAs per rank
+// signal holds e * count (mod 2^32) for every source rank.
+__device__ __forceinline__ void signal_add_release_sys(uint32_t* counter) {
+  asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Orders this thread's earlier generic-proxy accesses (e.g. an acquire of a peer's signal)
+// before its later async-proxy (TMA) accesses of global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Bounded wait until counters[0..n) all reach `target` (wrap-around compare).  Gives up after
+// kWaitLimitNs, reports kDevWaitTimeout and returns false; the caller carries on with whatever
+// the buffers hold, so a missing peer costs time and a status bit, never a hang.
+__device__ __forceinline__ bool wait_counters(const uint32_t* counters, int n, uint32_t target, unsigned* err) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (int s = 0; s < n; ++s) {
+    unsigned polls = 0;
+    while (static_cast<int32_t>(ld_acquire_sys(counters + s) - target) < 0) {
+      if ((++polls & 15u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+        report(err, kDevWaitTimeout);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// ------------------------------------------------------------------ clusters
+// Full cluster barrier: shared-memory writes before it are visible to every CTA of the
+// cluster after it.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Reads a float at the same shared-memory offset as `p` in CTA `rank` of this cluster.
+__device__ __forceinline__ float dsmem_ld_f32(const float* p, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(p)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
 // ------------------------------------------------------------------ numerics
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 

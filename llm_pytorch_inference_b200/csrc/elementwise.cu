@@ -5,11 +5,13 @@
 //   silu / gelu(tanh)            ops/activation.py:10-30       y = T(act(x))
 //   swiglu / geglu               ops/activation.py:33-66       y = T(T(act(g)) * u)
 //   fused_mlp (FusedMLP fallback) ops/mlp.py:73-82             y = T(T(act(g)) * u)
+//   swiglu of split-K partials   models/model.py:116-117       y = T(T(silu(T(g))) * T(u))
 //   embedding                    ops/embedding.py:11-35        y = W[id] (* scale, rounded)
 //   softmax                      ops/softmax.py:5-25           fp32 exp/sum, one rounding
 //   rotary                       ops/rope.py:74-76             y = T(T(x*cos) + T(rot(x)*sin))
 #include "common.cuh"
 #include "host.h"
+#include "splitk.cuh"
 
 namespace mvb {
 namespace {
@@ -52,6 +54,43 @@ __global__ void fused_mlp_kernel(T* __restrict__ out, const T* __restrict__ gate
     const T* row = gate_up + r * 2 * inter;
     out[i] = from_f<T>(rnd<T>(act_f(to_f<T>(row[j]), act)) * to_f<T>(row[inter + j]));
   }
+}
+
+// SiLU(gate) * up of a SwiGLU-paired GEMM still in split-K partial form
+// (MVB_EPI_SWIGLU_PARTIALS): tile t = j / 64 holds gate feature j in row j % 64 and up feature
+// j in row 64 + j % 64 of each contributor slot.  Both sums run in contributor order; the
+// rounding sequence is that of the GEMM's SWIGLU epilogue.  Thread = 4 consecutive features
+// of one batch row (blockIdx.y).
+__global__ void swiglu_gemm_kernel(__nv_bfloat16* __restrict__ out, int64_t out_stride,
+                                   const float* __restrict__ partials, SplitKPlan p, int inter) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.y;
+  const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (j >= inter) return;
+  const int t = j >> 6, r = j & 63;
+  const int nc = sk_count(p, t);
+  float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
+  for (int c = 0; c < nc; ++c) {
+    const float* base = partials + sk_offset(p, t, c, b, r);
+    const float4 pg = __ldcg(reinterpret_cast<const float4*>(base));
+    const float4 pu = __ldcg(reinterpret_cast<const float4*>(base + 64));
+    g.x += pg.x;
+    g.y += pg.y;
+    g.z += pg.z;
+    g.w += pg.w;
+    u.x += pu.x;
+    u.y += pu.y;
+    u.z += pu.z;
+    u.w += pu.w;
+  }
+  auto h = [](float gv, float uv) { return bf16_round(silu_f(bf16_round(gv))) * bf16_round(uv); };
+  __nv_bfloat162 o01 = __floats2bfloat162_rn(h(g.x, u.x), h(g.y, u.y));
+  __nv_bfloat162 o23 = __floats2bfloat162_rn(h(g.z, u.z), h(g.w, u.w));
+  uint2 ov;
+  ov.x = *reinterpret_cast<uint32_t*>(&o01);
+  ov.y = *reinterpret_cast<uint32_t*>(&o23);
+  *reinterpret_cast<uint2*>(out + static_cast<int64_t>(b) * out_stride + j) = ov;
 }
 
 template <typename T, typename I>
@@ -210,4 +249,22 @@ extern "C" int mvb_rotary_pos_emb(void* out, const void* in, const void* cos, co
   MVB_DISPATCH_FLOAT(dtype, "mvb_rotary_pos_emb",
                      return launch("rotary_pos_emb", rope_kernel<T>, grid_for(rows * head_dim, 256), dim3(256), 0,
                                    st, (T*)out, (const T*)in, (const T*)cos, (const T*)sin, rows, (int)head_dim));
+}
+
+extern "C" int mvb_swiglu_gemm(void* out, int64_t out_stride, const void* gemm_workspace, int64_t rows, int64_t inter,
+                               int64_t gemm_k, mvb_stream_t stream) {
+  MVB_REQUIRE(out && gemm_workspace, "mvb_swiglu_gemm: null pointer");
+  MVB_REQUIRE(rows > 0 && rows <= 256 && inter > 0 && inter % 4 == 0 && inter < (1LL << 30) && gemm_k > 0 &&
+                  gemm_k % kSplitBK == 0,
+              "mvb_swiglu_gemm: bad shape rows=%lld inter=%lld k=%lld", (long long)rows, (long long)inter,
+              (long long)gemm_k);
+  MVB_REQUIRE(out_stride >= inter && out_stride % 4 == 0 && aligned(out, 8),
+              "mvb_swiglu_gemm: out_stride must be >= inter and a multiple of 4, out 8-byte aligned");
+  const int sms = current_sm_count();
+  MVB_REQUIRE(sms > 0, "mvb_swiglu_gemm: no device");
+  const SplitKPlan p = splitk_plan_swiglu(rows, inter, gemm_k, sms);
+  const unsigned bx = static_cast<unsigned>((inter / 4 + 255) / 256);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return launch("swiglu_gemm", swiglu_gemm_kernel, dim3(bx, static_cast<unsigned>(rows)), dim3(256), 0, st,
+                (__nv_bfloat16*)out, out_stride, (const float*)gemm_workspace, p, (int)inter);
 }

@@ -20,6 +20,7 @@
 #include "common.cuh"
 #include "host.h"
 #include "splitk.cuh"
+#include "tp.cuh"
 
 namespace mvb {
 namespace {
@@ -59,8 +60,8 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x));
 
 // Final epilogue for 32 batch columns [c0, c0+32) of feature `row` of tile t.
 template <int BN>
-__device__ __forceinline__ void epilogue_store(const GemmArgs& a, const float (&v)[32], int t, int row, int c0,
-                                               float* xbuf) {
+__device__ __forceinline__ void epilogue_store(const GemmArgs& a, const TpGemm& tp, const float (&v)[32], int t,
+                                               int row, int c0, float* xbuf) {
   if (a.epilogue == MVB_EPI_SWIGLU) {
     // TMEM lanes 0-63 hold gate features 64t + r, lanes 64-127 the matching up features.
     const bool is_up = row >= 64;
@@ -100,6 +101,18 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs& a, const float (&
     }
     return;
   }
+  if (tp.nranks > 0 && tp.y[0] != nullptr) {
+    // all-gather: this rank's output columns land in every rank's copy of the full output
+    for (int q = 0; q < tp.nranks; ++q) {
+      __nv_bfloat16* yq = tp.y[q];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int b = c0 + j;
+        if (b < a.m) yq[static_cast<int64_t>(b) * a.ldy + nn] = __float2bfloat16_rn(v[j]);
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const int b = c0 + j;
@@ -113,7 +126,7 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs& a, const float (&
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-                     const GemmArgs a) {
+                     const GemmArgs a, const __grid_constant__ TpGemm tp) {
   constexpr int B_STAGE = BN * BK * 2;
   constexpr uint32_t STAGE_BYTES = A_STAGE + B_STAGE;
   constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
@@ -171,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
       prefetch_tmap(&tmX);
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
-      const bool swiglu = a.epilogue == MVB_EPI_SWIGLU;
+      const bool swiglu = a.epilogue == MVB_EPI_SWIGLU || a.epilogue == MVB_EPI_SWIGLU_PARTIALS;
       auto load_w = [&](int it) {
         const int s = it % STAGES;
         const int64_t g = kb_begin + it;
@@ -199,6 +212,12 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
         load_w(it);
       }
       pdl_wait();
+      if (tp.wait != nullptr) {
+        // X is written by every rank (all-gathered rows): wait for all of them, then make the
+        // acquired data visible to the TMA (async proxy) reads below.
+        wait_counters(tp.wait, tp.nranks, static_cast<uint32_t>(*tp.epoch) * tp.wait_count, a.err);
+        fence_proxy_async_global();
+      }
       for (int it = 0; it < pro; ++it) load_x(it);
       issued = pro;
       for (int it = pro; it < my_kb; ++it) {
@@ -264,17 +283,36 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
       tc_fence_after();
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(ab * BN);
       const bool full_tile = (kb == tile_lo) && (seg_end == tile_lo + a.kblocks);
-      if (a.epilogue == MVB_EPI_PARTIALS) {
+      if (a.epilogue == MVB_EPI_PARTIALS || a.epilogue == MVB_EPI_SWIGLU_PARTIALS) {
         // Every segment's fp32 accumulator goes to its (tile, contributor) slot; the consuming
         // kernel sums the slots (no fence, counter or merge here).
         const int j = static_cast<int>(blockIdx.x) - cta_of(tile_lo, total, G);
-        float* part = a.partials + (static_cast<int64_t>(t) * a.maxc + j) * BN * BM;
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld_x32(tb + c0, r);
-          tmem_ld_wait();
+        if (tp.nranks > 0 && tp.recv[0] != nullptr) {
+          // push: batch row b goes to the receive area of the rank that owns it
+          const int rpr = tp.rows_per_rank;
+          const int64_t base = ((static_cast<int64_t>(tp.rank) * a.tiles + t) * a.maxc + j) * rpr;
+          for (int c0 = 0; c0 < BN && c0 < a.m; c0 += 32) {
+            uint32_t r[32];
+            tmem_ld_x32(tb + c0, r);
+            tmem_ld_wait();
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) part[(c0 + jj) * BM + row] = __uint_as_float(r[jj]);
+            for (int jj = 0; jj < 32; ++jj) {
+              const int b = c0 + jj;
+              if (b < a.m) {
+                const int q = b / rpr;
+                tp.recv[q][(base + (b - q * rpr)) * BM + row] = __uint_as_float(r[jj]);
+              }
+            }
+          }
+        } else {
+          float* part = a.partials + (static_cast<int64_t>(t) * a.maxc + j) * BN * BM;
+          for (int c0 = 0; c0 < BN; c0 += 32) {
+            uint32_t r[32];
+            tmem_ld_x32(tb + c0, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) part[(c0 + jj) * BM + row] = __uint_as_float(r[jj]);
+          }
         }
       } else if (full_tile) {
         for (int c0 = 0; c0 < BN; c0 += 32) {
@@ -284,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          epilogue_store<BN>(a, v, t, row, c0, xbuf);
+          epilogue_store<BN>(a, tp, v, t, row, c0, xbuf);
         }
       } else {
         const int slot = seg == 0 ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
@@ -320,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] += __ldcg(p + (c0 + j) * BM + row);
             }
-            epilogue_store<BN>(a, v, t, row, c0, xbuf);
+            epilogue_store<BN>(a, tp, v, t, row, c0, xbuf);
           }
           if (e == 0) a.counters[t] = 0;
         }
@@ -330,6 +368,10 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
       mbar_arrive(&acce[ab]);
       kb = seg_end;
       ++seg;
+    }
+    if (tp.nranks > 0 && tp.signal[0] != nullptr) {
+      epi_bar();  // every store of this CTA's epilogue threads
+      if (e == 0) signal_ranks_once(tp.arrive, tp.arrive_total, tp.signal, tp.nranks);
     }
   }
 
@@ -358,14 +400,16 @@ size_t smem_for() {
 
 int bn_for(int64_t m) { return m <= 64 ? 64 : (m <= 128 ? 128 : 256); }
 
-int64_t tiles_for(int64_t n, int epilogue) {
-  return epilogue == MVB_EPI_SWIGLU ? (n / 2 + 63) / 64 : (n + BM - 1) / BM;
-}
+bool swiglu_tiling(int epilogue) { return epilogue == MVB_EPI_SWIGLU || epilogue == MVB_EPI_SWIGLU_PARTIALS; }
+bool partials_out(int epilogue) { return epilogue == MVB_EPI_PARTIALS || epilogue == MVB_EPI_SWIGLU_PARTIALS; }
+
+int64_t tiles_for(int64_t n, int epilogue) { return swiglu_tiling(epilogue) ? (n / 2 + 63) / 64 : (n + BM - 1) / BM; }
 
 int64_t counters_bytes(int64_t tiles) { return (tiles * 4 + 255) / 256 * 256; }
 
 template <int BN>
-int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, int grid, cudaStream_t st) {
+int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, const TpGemm& tp, int grid,
+                cudaStream_t st) {
   constexpr int S = stages_for<BN>();
   const size_t smem = smem_for<BN>();
   // Once per device and instantiation, so no attribute call happens during graph capture.
@@ -376,7 +420,7 @@ int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a,
     MVB_TRY(set_smem(gemm_bf16_kernel<BN, S>, smem, "gemm: smem attribute"));
     if (dev < 64) done_mask |= 1ull << dev;
   }
-  return launch("gemm_bf16", gemm_bf16_kernel<BN, S>, dim3(grid), dim3(kThreads), smem, st, tw, tx, a);
+  return launch("gemm_bf16", gemm_bf16_kernel<BN, S>, dim3(grid), dim3(kThreads), smem, st, tw, tx, a, tp);
 }
 
 }  // namespace
@@ -392,26 +436,34 @@ extern "C" int64_t mvb_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int
   // Counters sized for the larger of the two tilings (plain / SWIGLU pairs).
   const int64_t tiles = (n + 63) / 64;
   const int64_t merge = counters_bytes(tiles) + 2LL * sms * bn * BM * 4 + 256;
-  const int64_t part = splitk_partials_bytes(splitk_plan(m, n, k, sms)) + 256;
+  int64_t part = splitk_partials_bytes(splitk_plan(m, n, k, sms)) + 256;
+  if (n % 2 == 0) {
+    const int64_t sw = splitk_partials_bytes(splitk_plan_swiglu(m, n / 2, k, sms)) + 256;
+    if (sw > part) part = sw;
+  }
   return merge > part ? merge : part;
 }
 
-extern "C" int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t ldw,
-                             int64_t m, int64_t n, int64_t k, int epilogue, const void* aux, int64_t ld_aux,
-                             void* workspace, int64_t workspace_bytes, mvb_stream_t stream) {
-  MVB_REQUIRE(x && w && workspace && (y || epilogue == MVB_EPI_PARTIALS), "mvb_gemm_bf16: null pointer");
+namespace mvb {
+
+// Shared body of mvb_gemm_bf16 and mvb_tp_gemm_bf16; `grid_out` receives the CTA count.
+int gemm_launch(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t m, int64_t n,
+                int64_t k, int epilogue, const void* aux, int64_t ld_aux, void* workspace, int64_t workspace_bytes,
+                const TpGemm& tp, int* grid_out, mvb_stream_t stream) {
+  MVB_REQUIRE(x && w && workspace && (y || partials_out(epilogue) || (tp.nranks > 0 && tp.y[0])),
+              "mvb_gemm_bf16: null pointer");
   MVB_REQUIRE(m > 0 && m <= 256, "mvb_gemm_bf16: m=%lld outside [1, 256]", (long long)m);
   MVB_REQUIRE(n > 0 && n < (1LL << 31) && k > 0 && k % BK == 0, "mvb_gemm_bf16: need k %% 64 == 0 (k=%lld)",
               (long long)k);
   MVB_REQUIRE(ldx >= k && ldw >= k && ldx % 8 == 0 && ldw % 8 == 0, "mvb_gemm_bf16: ldx/ldw must be >= k, %% 8");
   MVB_REQUIRE(aligned(x, 16) && aligned(w, 16), "mvb_gemm_bf16: x and w must be 16-byte aligned");
   MVB_REQUIRE(epilogue == MVB_EPI_STORE || epilogue == MVB_EPI_SWIGLU || epilogue == MVB_EPI_RESADD ||
-                  epilogue == MVB_EPI_PARTIALS,
+                  partials_out(epilogue),
               "mvb_gemm_bf16: bad epilogue %d", epilogue);
   MVB_REQUIRE(epilogue != MVB_EPI_RESADD || (aux != nullptr && ld_aux >= n), "mvb_gemm_bf16: RESADD needs aux");
-  MVB_REQUIRE(epilogue != MVB_EPI_SWIGLU || n % 2 == 0, "mvb_gemm_bf16: SWIGLU needs an even n (= 2*inter)");
+  MVB_REQUIRE(!swiglu_tiling(epilogue) || n % 2 == 0, "mvb_gemm_bf16: SWIGLU needs an even n (= 2*inter)");
   const int64_t out_cols = epilogue == MVB_EPI_SWIGLU ? n / 2 : n;
-  MVB_REQUIRE(epilogue == MVB_EPI_PARTIALS || ldy >= out_cols, "mvb_gemm_bf16: ldy < output columns");
+  MVB_REQUIRE(partials_out(epilogue) || ldy >= out_cols, "mvb_gemm_bf16: ldy < output columns");
   const int sms = current_sm_count();
   MVB_REQUIRE(sms > 0, "mvb_gemm_bf16: no device");
   const int bn = bn_for(m);
@@ -426,7 +478,8 @@ extern "C" int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, c
   const int64_t cbytes = counters_bytes((n + 63) / 64);
   SplitKPlan plan{};
   if (epilogue == MVB_EPI_PARTIALS) plan = splitk_plan(m, n, k, sms);
-  const int64_t need = epilogue == MVB_EPI_PARTIALS ? splitk_partials_bytes(plan) : cbytes + 2LL * grid * bn * BM * 4;
+  if (epilogue == MVB_EPI_SWIGLU_PARTIALS) plan = splitk_plan_swiglu(m, n / 2, k, sms);
+  const int64_t need = partials_out(epilogue) ? splitk_partials_bytes(plan) : cbytes + 2LL * grid * bn * BM * 4;
   MVB_REQUIRE(ws_end >= need, "mvb_gemm_bf16: workspace %lld < %lld bytes", (long long)workspace_bytes,
               (long long)need);
   MVB_REQUIRE(aligned(workspace, 256), "mvb_gemm_bf16: workspace must be 256-byte aligned");
@@ -435,7 +488,7 @@ extern "C" int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, c
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
     const uint64_t strides[1] = {static_cast<uint64_t>(ldw) * 2};
-    const uint32_t box[2] = {BK, static_cast<uint32_t>(epilogue == MVB_EPI_SWIGLU ? 64 : BM)};
+    const uint32_t box[2] = {BK, static_cast<uint32_t>(swiglu_tiling(epilogue) ? 64 : BM)};
     MVB_TRY(encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B));
   }
@@ -462,10 +515,21 @@ extern "C" int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, c
   a.partials = static_cast<float*>(workspace);
   a.counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + ws_end - cbytes);
   a.err = device_status_ptr();
+  if (grid_out) *grid_out = grid;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (bn) {
-    case 64: return launch_gemm<64>(tw, tx, a, grid, st);
-    case 128: return launch_gemm<128>(tw, tx, a, grid, st);
-    default: return launch_gemm<256>(tw, tx, a, grid, st);
+    case 64: return launch_gemm<64>(tw, tx, a, tp, grid, st);
+    case 128: return launch_gemm<128>(tw, tx, a, tp, grid, st);
+    default: return launch_gemm<256>(tw, tx, a, tp, grid, st);
   }
+}
+
+}  // namespace mvb
+
+extern "C" int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                             int64_t m, int64_t n, int64_t k, int epilogue, const void* aux, int64_t ld_aux,
+                             void* workspace, int64_t workspace_bytes, mvb_stream_t stream) {
+  TpGemm tp{};
+  return gemm_launch(y, ldy, x, ldx, w, ldw, m, n, k, epilogue, aux, ld_aux, workspace, workspace_bytes, tp, nullptr,
+                     stream);
 }

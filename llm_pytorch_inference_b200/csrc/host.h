@@ -66,6 +66,31 @@ int launch(const char* name, void (*kernel)(KArgs...), dim3 grid, dim3 block, si
   return cuda_status(e, name);
 }
 
+// Launch with a (cluster_x, 1, 1) thread-block cluster, plus the PDL attribute when enabled.
+template <typename... KArgs, typename... Args>
+int launch_cluster(const char* name, void (*kernel)(KArgs...), dim3 grid, dim3 block, unsigned cluster_x,
+                   size_t smem, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (pdl_enabled()) {
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  return cuda_status(e, name);
+}
+
 // Opt a kernel into more than 48 KB of dynamic shared memory (idempotent).
 template <typename... KArgs>
 int set_smem(void (*kernel)(KArgs...), size_t bytes, const char* name) {

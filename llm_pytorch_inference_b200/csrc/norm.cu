@@ -12,6 +12,7 @@
 #include "common.cuh"
 #include "host.h"
 #include "splitk.cuh"
+#include "tp.cuh"
 
 namespace mvb {
 namespace {
@@ -84,41 +85,75 @@ __global__ void fused_add_rmsnorm_kernel(T* __restrict__ out, T* __restrict__ re
 // Residual add + RMSNorm whose input is a GEMM's output still in split-K partial form: the
 // linear layer's bf16 output is formed here as bf16(sum of the tile's partial slots, contributor
 // order), then residual += it and out = RMSNorm(residual) (model semantics, models/model.py:19-25,
-// :319).  Each thread owns runs of 4 consecutive features (float4 partial loads, 8-byte residual
-// loads) and keeps its values in registers between the two passes; per-tile contributor counts
-// are computed once per CTA.  Supports hidden % 4 == 0 and hidden <= 16 * blockDim.
+// :319).
+//
+// Row b (blockIdx.y) is split over a cluster of gridDim.x CTAs: CTA c owns the runs of 4
+// consecutive features [c * runs_per_cta, (c + 1) * runs_per_cta), each thread up to
+// kFaddMaxRuns of them, kept in registers between the two passes (float4 partial loads,
+// 8-byte residual accesses).  Each CTA reduces its share of the sum of squares, publishes it
+// in shared memory, and every CTA of the cluster sums the published shares in CTA order
+// through distributed shared memory, so all chunks of a row scale by the same 1/rms.
+//
+// Tensor-parallel form (TP = true): the partials were pushed by every rank's row-parallel GEMM
+// into this rank's receive area (layout sk_push_offset) for the rows this rank owns
+// (blockIdx.y indexes them); the sum runs over source ranks, then contributors.  The
+// normalised row is written into every rank's copy of the activations (all-gather), and each
+// CTA then signals every rank.  The residual stream of a row lives on its owner only.
 constexpr int kFaddMaxRuns = 4;
-constexpr int kFaddMaxTiles = 256;
+constexpr int kFaddMaxCluster = 8;
 
+struct TpFadd {
+  int nranks, rank, rows_per_rank;
+  const float* recv;                       // this rank's receive area
+  __nv_bfloat16* out[kTpMaxRanks];         // every rank's copy of the normalised activations
+  uint32_t* signal[kTpMaxRanks];           // every rank's counter [point][this rank]
+  uint32_t* arrive;                        // this rank's arrival counter of the signal point
+  const uint32_t* wait;                    // this rank's counters of the GEMM's push point
+  uint32_t wait_count;
+  const int32_t* epoch;
+};
+
+template <bool TP>
 __global__ void fused_add_rmsnorm_gemm_kernel(__nv_bfloat16* __restrict__ out, __nv_bfloat16* __restrict__ residual,
                                               const float* __restrict__ partials, SplitKPlan p,
-                                              const __nv_bfloat16* __restrict__ w, int hidden, float eps,
-                                              int plus_one) {
+                                              const __nv_bfloat16* __restrict__ w, int hidden, int runs_per_cta,
+                                              float eps, int plus_one, const __grid_constant__ TpFadd tp,
+                                              unsigned* err) {
   __shared__ float red[32];
-  __shared__ unsigned char s_nc[kFaddMaxTiles];
+  __shared__ float cta_ss;
   pdl_launch_dependents();
-  const int tiles = (hidden + kSplitBM - 1) / kSplitBM;
-  for (int t = threadIdx.x; t < tiles; t += blockDim.x) s_nc[t] = static_cast<unsigned char>(sk_count(p, t));
   pdl_wait();
-  __syncthreads();
-  const int b = blockIdx.x;
+  if (TP) {
+    if (threadIdx.x == 0)
+      wait_counters(tp.wait, tp.nranks, static_cast<uint32_t>(*tp.epoch) * tp.wait_count, err);
+    __syncthreads();
+  }
+  const int bl = blockIdx.y;
+  const int b = TP ? tp.rank * tp.rows_per_rank + bl : bl;
+  const int run0 = blockIdx.x * runs_per_cta;
+  const int run_end = min(run0 + runs_per_cta, hidden / 4);
   __nv_bfloat16* res = residual + static_cast<int64_t>(b) * hidden;
-  __nv_bfloat16* y = out + static_cast<int64_t>(b) * hidden;
   float v[kFaddMaxRuns][4];
   float ss = 0.0f;
 #pragma unroll
   for (int k = 0; k < kFaddMaxRuns; ++k) {
-    const int i = (threadIdx.x + k * blockDim.x) * 4;
-    if (i < hidden) {
+    const int run = run0 + threadIdx.x + k * blockDim.x;
+    if (run < run_end) {
+      const int i = run * 4;
       const int t = i / kSplitBM, r = i - t * kSplitBM;
-      const int nc = s_nc[t];
+      const int nc = sk_count(p, t);
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int j = 0; j < nc; ++j) {
-        const float4 q = __ldcg(reinterpret_cast<const float4*>(partials + sk_offset(p, t, j, b, r)));
-        acc.x += q.x;
-        acc.y += q.y;
-        acc.z += q.z;
-        acc.w += q.w;
+      const int nsrc = TP ? tp.nranks : 1;
+      for (int src = 0; src < nsrc; ++src) {
+        for (int j = 0; j < nc; ++j) {
+          const float* q = TP ? tp.recv + sk_push_offset(p, src, t, j, tp.rows_per_rank, bl, r)
+                              : partials + sk_offset(p, t, j, b, r);
+          const float4 qv = __ldcg(reinterpret_cast<const float4*>(q));
+          acc.x += qv.x;
+          acc.y += qv.y;
+          acc.z += qv.z;
+          acc.w += qv.w;
+        }
       }
       const uint2 rr = *reinterpret_cast<const uint2*>(res + i);
       const __nv_bfloat162 r01 = *reinterpret_cast<const __nv_bfloat162*>(&rr.x);
@@ -137,23 +172,58 @@ __global__ void fused_add_rmsnorm_gemm_kernel(__nv_bfloat16* __restrict__ out, _
     }
   }
   ss = block_sum(ss, red);
-  const float rr = 1.0f / sqrtf(ss / static_cast<float>(hidden) + eps);
+  if (threadIdx.x == 0) cta_ss = ss;
+  cluster_sync();
+  float total = 0.0f;
+  for (unsigned c = 0; c < gridDim.x; ++c) total += dsmem_ld_f32(&cta_ss, c);
+  cluster_sync();  // no CTA leaves while another may still read its share
+  const float rr = 1.0f / sqrtf(total / static_cast<float>(hidden) + eps);
 #pragma unroll
   for (int k = 0; k < kFaddMaxRuns; ++k) {
-    const int i = (threadIdx.x + k * blockDim.x) * 4;
-    if (i < hidden) {
+    const int run = run0 + threadIdx.x + k * blockDim.x;
+    if (run < run_end) {
+      const int i = run * 4;
+      const uint2 wr = *reinterpret_cast<const uint2*>(w + i);
+      const __nv_bfloat162 w01 = *reinterpret_cast<const __nv_bfloat162*>(&wr.x);
+      const __nv_bfloat162 w23 = *reinterpret_cast<const __nv_bfloat162*>(&wr.y);
+      const float wf[4] = {__low2float(w01), __high2float(w01), __low2float(w23), __high2float(w23)};
       float o[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e)
-        o[e] = norm_out<__nv_bfloat16>(v[k][e], __bfloat162float(w[i + e]), rr, plus_one, MVB_NORM_MODEL, true);
+        o[e] = norm_out<__nv_bfloat16>(v[k][e], wf[e], rr, plus_one, MVB_NORM_MODEL, true);
       __nv_bfloat162 o01 = __floats2bfloat162_rn(o[0], o[1]);
       __nv_bfloat162 o23 = __floats2bfloat162_rn(o[2], o[3]);
       uint2 ov;
       ov.x = *reinterpret_cast<uint32_t*>(&o01);
       ov.y = *reinterpret_cast<uint32_t*>(&o23);
-      *reinterpret_cast<uint2*>(y + i) = ov;
+      const int64_t off = static_cast<int64_t>(b) * hidden + i;
+      if (TP) {
+        for (int q = 0; q < tp.nranks; ++q) *reinterpret_cast<uint2*>(tp.out[q] + off) = ov;
+      } else {
+        *reinterpret_cast<uint2*>(out + off) = ov;
+      }
     }
   }
+  if (TP) {
+    __syncthreads();
+    if (threadIdx.x == 0) signal_ranks_once(tp.arrive, gridDim.x * gridDim.y, tp.signal, tp.nranks);
+  }
+}
+
+// Cluster split of a row of `hidden` features: CTAs per row, runs of 4 per CTA, threads per CTA.
+struct FaddSplit {
+  int ctas, runs_per_cta, threads;
+};
+inline FaddSplit fadd_split(int64_t hidden) {
+  FaddSplit s;
+  const int runs = static_cast<int>(hidden / 4);
+  s.ctas = static_cast<int>((hidden + 511) / 512);
+  if (s.ctas > kFaddMaxCluster) s.ctas = kFaddMaxCluster;
+  s.runs_per_cta = (runs + s.ctas - 1) / s.ctas;
+  const int per_thread = (s.runs_per_cta + 255) / 256;
+  s.threads = ((s.runs_per_cta + per_thread - 1) / per_thread + 31) / 32 * 32;
+  if (s.threads < 64) s.threads = 64;
+  return s;
 }
 
 int threads_for(int64_t hidden) {
@@ -227,16 +297,68 @@ extern "C" int mvb_fused_add_rmsnorm_gemm(void* out, void* residual, const void*
               "mvb_fused_add_rmsnorm_gemm: bad shape");
   const int sms = current_sm_count();
   MVB_REQUIRE(sms > 0, "mvb_fused_add_rmsnorm_gemm: no device");
-  MVB_REQUIRE(hidden % 4 == 0 && hidden <= 4 * 1024 * kFaddMaxRuns && (hidden + 127) / 128 <= kFaddMaxTiles,
+  MVB_REQUIRE(hidden % 4 == 0 && hidden <= 16384,
               "mvb_fused_add_rmsnorm_gemm: hidden %lld must be a multiple of 4 and <= 16384", (long long)hidden);
-  MVB_REQUIRE(aligned(residual, 8) && aligned(out, 8), "mvb_fused_add_rmsnorm_gemm: 8-byte alignment");
+  MVB_REQUIRE(aligned(residual, 8) && aligned(out, 8) && aligned(weight, 8),
+              "mvb_fused_add_rmsnorm_gemm: 8-byte alignment");
   const SplitKPlan p = splitk_plan(rows, hidden, gemm_k, sms);
-  MVB_REQUIRE(p.maxc <= 255, "mvb_fused_add_rmsnorm_gemm: too many split-K contributors");
-  int threads = static_cast<int>((hidden / 4 + kFaddMaxRuns - 1) / kFaddMaxRuns);
-  threads = (threads + 31) / 32 * 32;
-  if (threads < 128) threads = 128;
+  const FaddSplit sp = fadd_split(hidden);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  return launch("fused_add_rmsnorm_gemm", fused_add_rmsnorm_gemm_kernel, dim3(static_cast<unsigned>(rows)),
-                dim3(threads), 0, st, (__nv_bfloat16*)out, (__nv_bfloat16*)residual,
-                (const float*)gemm_workspace, p, (const __nv_bfloat16*)weight, (int)hidden, eps, plus_one);
+  const TpFadd none{};
+  return launch_cluster("fused_add_rmsnorm_gemm", fused_add_rmsnorm_gemm_kernel<false>,
+                        dim3(static_cast<unsigned>(sp.ctas), static_cast<unsigned>(rows)), dim3(sp.threads),
+                        static_cast<unsigned>(sp.ctas), 0, st, (__nv_bfloat16*)out, (__nv_bfloat16*)residual,
+                        (const float*)gemm_workspace, p, (const __nv_bfloat16*)weight, (int)hidden,
+                        sp.runs_per_cta, eps, plus_one, none, device_status_ptr());
+}
+
+extern "C" int mvb_tp_fused_add_rmsnorm_gemm(mvb_tp_comm* comm, void* residual, int64_t rows, int64_t hidden,
+                                             int64_t gemm_k, const void* weight, float eps, int plus_one,
+                                             int64_t recv_offset, int wait_point, int64_t out_offset,
+                                             int signal_point, mvb_stream_t stream) {
+  MVB_REQUIRE(comm && residual && weight, "mvb_tp_fused_add_rmsnorm_gemm: null pointer");
+  const int nr = comm->nranks;
+  MVB_REQUIRE(rows > 0 && rows <= 256 && rows % nr == 0 && gemm_k > 0 && gemm_k % kSplitBK == 0,
+              "mvb_tp_fused_add_rmsnorm_gemm: rows %lld must be in [1, 256] and a multiple of %d ranks",
+              (long long)rows, nr);
+  MVB_REQUIRE(hidden % 4 == 0 && hidden > 0 && hidden <= 16384,
+              "mvb_tp_fused_add_rmsnorm_gemm: hidden %lld must be a multiple of 4 and <= 16384", (long long)hidden);
+  MVB_REQUIRE(wait_point >= 0 && wait_point < kTpMaxPoints && signal_point >= 0 && signal_point < kTpMaxPoints &&
+                  wait_point != signal_point,
+              "mvb_tp_fused_add_rmsnorm_gemm: bad signal points");
+  MVB_REQUIRE(comm->point_count[wait_point] > 0, "mvb_tp_fused_add_rmsnorm_gemm: nothing signals point %d",
+              wait_point);
+  MVB_REQUIRE(aligned(residual, 8) && aligned(weight, 8), "mvb_tp_fused_add_rmsnorm_gemm: 8-byte alignment");
+  const int sms = current_sm_count();
+  MVB_REQUIRE(sms > 0, "mvb_tp_fused_add_rmsnorm_gemm: no device");
+  const int rpr = static_cast<int>(rows / nr);
+  const SplitKPlan p = splitk_plan(rows, hidden, gemm_k, sms);
+  MVB_REQUIRE(recv_offset >= kTpSignalBytes && recv_offset % 16 == 0 &&
+                  recv_offset + splitk_push_bytes(p, nr, rpr) <= comm->heap_bytes,
+              "mvb_tp_fused_add_rmsnorm_gemm: receive area outside the heap");
+  MVB_REQUIRE(out_offset >= kTpSignalBytes && out_offset % 16 == 0 &&
+                  out_offset + rows * hidden * 2 <= comm->heap_bytes,
+              "mvb_tp_fused_add_rmsnorm_gemm: output outside the heap");
+  TpFadd tp{};
+  tp.nranks = nr;
+  tp.rank = comm->rank;
+  tp.rows_per_rank = rpr;
+  tp.recv = reinterpret_cast<const float*>(comm->base[comm->rank] + recv_offset);
+  for (int q = 0; q < nr; ++q) {
+    tp.out[q] = reinterpret_cast<__nv_bfloat16*>(comm->base[q] + out_offset);
+    tp.signal[q] = comm->signal_slot(q, signal_point);
+  }
+  tp.arrive = comm->arrive_slot(signal_point);
+  tp.wait = comm->wait_row(wait_point);
+  tp.wait_count = comm->point_count[wait_point];
+  tp.epoch = comm->epoch;
+  const FaddSplit sp = fadd_split(hidden);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  MVB_TRY(launch_cluster("tp_fused_add_rmsnorm_gemm", fused_add_rmsnorm_gemm_kernel<true>,
+                         dim3(static_cast<unsigned>(sp.ctas), static_cast<unsigned>(rpr)), dim3(sp.threads),
+                         static_cast<unsigned>(sp.ctas), 0, st, (__nv_bfloat16*)nullptr, (__nv_bfloat16*)residual,
+                         (const float*)nullptr, p, (const __nv_bfloat16*)weight, (int)hidden, sp.runs_per_cta, eps,
+                         plus_one, tp, device_status_ptr()));
+  comm->point_count[signal_point] = 1;
+  return MVB_OK;
 }

@@ -49,10 +49,10 @@ __host__ __device__ __forceinline__ int64_t sk_offset(const SplitKPlan& p, int t
 
 inline int sk_bn_for(int64_t m) { return m <= 64 ? 64 : (m <= 128 ? 128 : 256); }
 
-// The plan the GEMM uses for a plain (non-SwiGLU) m x n x k product on `sms` SMs.
-inline SplitKPlan splitk_plan(int64_t m, int64_t n, int64_t k, int sms) {
+// The plan for `tiles` output tiles of a k-deep product over `m` batch rows on `sms` SMs.
+inline SplitKPlan splitk_plan_tiles(int64_t m, int tiles, int64_t k, int sms) {
   SplitKPlan p;
-  p.tiles = static_cast<int>((n + kSplitBM - 1) / kSplitBM);
+  p.tiles = tiles;
   p.kblocks = static_cast<int>(k / kSplitBK);
   const int64_t total = static_cast<int64_t>(p.tiles) * p.kblocks;
   p.grid = static_cast<int>(total < sms ? total : sms);
@@ -63,6 +63,17 @@ inline SplitKPlan splitk_plan(int64_t m, int64_t n, int64_t k, int sms) {
     if (c > p.maxc) p.maxc = c;
   }
   return p;
+}
+
+// The plan the GEMM uses for a plain (non-SwiGLU) m x n x k product on `sms` SMs.
+inline SplitKPlan splitk_plan(int64_t m, int64_t n, int64_t k, int sms) {
+  return splitk_plan_tiles(m, static_cast<int>((n + kSplitBM - 1) / kSplitBM), k, sms);
+}
+
+// The plan of a SwiGLU-paired product (W = [gate; up], 2 * inter rows): tile t holds gate
+// features 64t..64t+63 in rows 0-63 and the matching up features in rows 64-127.
+inline SplitKPlan splitk_plan_swiglu(int64_t m, int64_t inter, int64_t k, int sms) {
+  return splitk_plan_tiles(m, static_cast<int>((inter + 63) / 64), k, sms);
 }
 
 inline int64_t splitk_partials_bytes(const SplitKPlan& p) {

@@ -26,24 +26,38 @@ import torch
 from .configs import head_dim, num_kv_heads
 from .kv_cache import KVCacheManager, num_blocks_for_budget
 from .runner import DecodeRunner, DecodeWeights, resolve_device
+from .tensor_parallel import TensorParallelConfig, shard_state_dict
 
 
 class DecodeEngine:
+    """``tp``: this process's place in a tensor-parallel group (one engine per GPU, every rank
+    driven with the same calls); ``state_dict`` is the full model, sharded here."""
+
     def __init__(self, cfg: dict, state_dict: dict[str, torch.Tensor], max_batch: int, max_model_len: int,
                  num_blocks: int | None = None, device="cuda", free_order: list[int] | None = None,
-                 hbm_budget_bytes: int | None = None):
+                 hbm_budget_bytes: int | None = None, tp: TensorParallelConfig | None = None):
         self.cfg = cfg
         self.dev = resolve_device(device)
-        self.weights = DecodeWeights(cfg, state_dict, self.dev)
-        L, nkv, D = cfg["num_hidden_layers"], num_kv_heads(cfg), head_dim(cfg)
+        self.tp = tp or TensorParallelConfig()
+        T = self.tp.tp_size
+        sd = shard_state_dict(cfg, state_dict, T, self.tp.rank) if T > 1 else state_dict
+        self.weights = DecodeWeights(cfg, sd, self.dev)
+        del sd
+        L, nkv, D = cfg["num_hidden_layers"], num_kv_heads(cfg) // T, head_dim(cfg)
         if num_blocks is None:
             free, _ = torch.cuda.mem_get_info(self.dev)
             kw = {} if hbm_budget_bytes is None else {"budget_bytes": hbm_budget_bytes}
             num_blocks = num_blocks_for_budget(16, nkv, D, L, 2, self.weights.nbytes(), 1 << 30,
                                                device_free_bytes=free, **kw)
+            if T > 1:   # block ids are replicated: every rank needs the same pool size
+                import torch.distributed as dist
+
+                t = torch.tensor([num_blocks], dtype=torch.int64, device=self.dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MIN)
+                num_blocks = int(t.item())
         self.kv = KVCacheManager(num_blocks, 16, L, nkv, D, device=self.dev, dtype=torch.bfloat16,
                                  free_order=free_order)
-        self.runner = DecodeRunner(cfg, self.weights, self.kv, max_batch, max_model_len, self.dev)
+        self.runner = DecodeRunner(cfg, self.weights, self.kv, max_batch, max_model_len, self.dev, tp=self.tp)
         self.seqs: list[int] = []                     # active sequence ids, one per batch row
         self.tokens: dict[int, list[int]] = {}
         self.prompt_len: dict[int, int] = {}

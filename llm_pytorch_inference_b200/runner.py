@@ -16,8 +16,13 @@ Everything the step touches is resident on the device and laid out once:
   offset) in one int32 device buffer filled by one host->device copy per step;
 * stream-K / split-KV workspaces (zero-initialised once; the kernels leave them zero).
 
-A step is ~9 kernels per layer.  ``capture()`` records the whole step in one CUDA
+A step is 8 kernels per layer.  ``capture()`` records the whole step in one CUDA
 graph; ``replay()`` re-runs it (the host only refreshes the metadata buffer).
+
+With tensor parallelism (``tp.tp_size > 1``, one runner per GPU) the weights are the rank's
+shard (``tensor_parallel.shard_state_dict``), the KV pool holds the rank's KV heads, and the
+normalised activations and the logits live in the symmetric heap that the TP kernels write
+across GPUs (``tensor_parallel``).
 """
 from __future__ import annotations
 
@@ -28,6 +33,8 @@ import torch
 from . import _native as N
 from .configs import head_dim, num_kv_heads
 from .kv_cache import KVCacheManager
+from . import tensor_parallel as tpm
+from .tensor_parallel import TensorParallelConfig
 
 
 def resolve_device(device) -> torch.device:
@@ -86,22 +93,35 @@ class DecodeWeights:
             ts.append(self.lm_head)
         return sum(t.numel() * t.element_size() for t in ts)
 
+    def streamed_bytes(self) -> int:
+        """Weight bytes one decode step must read: every layer's matrices and norms, the final norm
+        and lm_head (the embedding table is only gathered, one row per sequence)."""
+        ts = [self.final_norm, self.lm_head, *self.wqkv, *self.wo, *self.wgu, *self.wdown, *self.ln1, *self.ln2,
+              *self.qn, *self.kn]
+        return sum(t.numel() * t.element_size() for t in ts)
+
 
 class DecodeRunner:
     def __init__(self, cfg: dict, weights: DecodeWeights, kv: KVCacheManager, max_batch: int, max_model_len: int,
-                 device="cuda", rope_len: int | None = None):
+                 device="cuda", rope_len: int | None = None, tp: TensorParallelConfig | None = None):
         self.cfg = cfg
         self.w = weights
         self.kv = kv
         self.dev = resolve_device(device)
+        self.tp = tp or TensorParallelConfig()
+        T = self.tp.tp_size
+        tpm.check_divisible(cfg, T)
+        if max_batch % T:
+            raise ValueError(f"max_batch {max_batch} must be a multiple of tp_size {T}")
         self.B = max_batch
         self.L = cfg["num_hidden_layers"]
         self.H = cfg["hidden_size"]
-        self.Hq = cfg["num_attention_heads"]
-        self.Hkv = num_kv_heads(cfg)
+        self.Hq = cfg["num_attention_heads"] // T       # this rank's heads / features
+        self.Hkv = num_kv_heads(cfg) // T
         self.D = head_dim(cfg)
-        self.I = cfg["intermediate_size"]
-        self.V = cfg["vocab_size"]
+        self.I = cfg["intermediate_size"] // T
+        self.V = cfg["vocab_size"]                       # full vocabulary (logits are all-gathered)
+        self.Vl = self.V // T
         self.eps = float(cfg.get("rms_norm_eps", 1e-6))
         self.scale = 1.0 / math.sqrt(cfg.get("query_pre_attn_scalar") or self.D)
         if kv.kv_cache is None or kv.kv_cache.device != self.dev or kv.kv_cache.dtype != torch.bfloat16:
@@ -116,15 +136,23 @@ class DecodeRunner:
 
         B, H, dev, bf = self.B, self.H, self.dev, torch.bfloat16
         qkv_n = (self.Hq + 2 * self.Hkv) * self.D
+        didx = dev.index if dev.index is not None else torch.cuda.current_device()
+        self.heap = None
         self.residual = torch.zeros(B, H, dtype=bf, device=dev)
-        self.xn = torch.zeros(B, H, dtype=bf, device=dev)
-        self.qkv = torch.zeros(B, qkv_n, dtype=bf, device=dev)
+        if self.tp.enabled:
+            lib = N.lib()
+            recv_o = lib.mvb_tp_recv_bytes(B, H, self.Hq * self.D, T, didx)
+            recv_d = lib.mvb_tp_recv_bytes(B, H, self.I, T, didx)
+            self.layout = tpm.plan_heap(lib.mvb_tp_signal_bytes(), B, H, self.V, recv_o, recv_d)
+            self.heap = tpm.SymmetricHeap(self.layout.total, self.tp.rank, T)
+            self.xn = self.heap.tensor(self.layout.xn, (B, H), bf, dev)
+            self.logits = self.heap.tensor(self.layout.logits, (B, self.V), bf, dev)
+        else:
+            self.xn = torch.zeros(B, H, dtype=bf, device=dev)
+            self.logits = torch.zeros(B, self.V, dtype=bf, device=dev)
         self.q = torch.zeros(B, self.Hq, self.D, dtype=bf, device=dev)
         self.attn = torch.zeros(B, self.Hq * self.D, dtype=bf, device=dev)
-        self.o = torch.zeros(B, H, dtype=bf, device=dev)
         self.h = torch.zeros(B, self.I, dtype=bf, device=dev)
-        self.mlp = torch.zeros(B, H, dtype=bf, device=dev)
-        self.logits = torch.zeros(B, self.V, dtype=bf, device=dev)
         self.tokens = torch.zeros(B, dtype=torch.int64, device=dev)
         # per-row sampling parameters (greedy by default)
         self.temperature = torch.zeros(B, dtype=torch.float32, device=dev)
@@ -147,9 +175,8 @@ class DecodeRunner:
         self.block_tables = self.meta[self._o_bt:].view(B, self.max_blocks)
         self.tokens_host = torch.zeros(B, dtype=torch.int64, pin_memory=True)
 
-        didx = dev.index if dev.index is not None else torch.cuda.current_device()
         gemm_ws = max(N.lib().mvb_gemm_workspace_bytes(B, n, k, didx) for n, k in
-                      ((qkv_n, H), (H, self.Hq * self.D), (2 * self.I, H), (H, self.I), (self.V, H)))
+                      ((qkv_n, H), (H, self.Hq * self.D), (2 * self.I, H), (H, self.I), (self.Vl, H)))
         attn_ws = N.lib().mvb_paged_attention_workspace_bytes(B, self.Hq, self.D, didx)
         self.gemm_ws = torch.zeros(gemm_ws, dtype=torch.uint8, device=dev)
         self.attn_ws = torch.zeros(attn_ws, dtype=torch.uint8, device=dev)
@@ -205,6 +232,9 @@ class DecodeRunner:
 
     def forward(self) -> None:
         """Launches one decode step on the current stream (metadata must be on the device)."""
+        if self.tp.enabled:
+            self._forward_tp()
+            return
         lib, w, B, H = N.lib(), self.w, self.B, self.H
         self._st = N.stream_handle(self.dev)
         st, eps, bf = self._st, self.eps, N.BF16
@@ -235,11 +265,68 @@ class DecodeRunner:
             N.check(lib.mvb_fused_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(), ws, B, H,
                                                    self.Hq * self.D, w.ln2[i].data_ptr(), eps, 0, st),
                     "fused_add_rmsnorm_gemm")
-            self._gemm(self.h, self.xn, w.wgu[i], N.EPI_SWIGLU)
+            self._gemm(None, self.xn, w.wgu[i], N.EPI_SWIGLU_PARTIALS)
+            N.check(lib.mvb_swiglu_gemm(self.h.data_ptr(), self.h.stride(0), ws, B, self.I, H, st), "swiglu_gemm")
             self._gemm(None, self.h, w.wdown[i], N.EPI_PARTIALS)
         N.check(lib.mvb_fused_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(), ws, B, H, self.I,
                                                w.final_norm.data_ptr(), eps, 0, st), "fused_add_rmsnorm_gemm")
         self._gemm(self.logits, self.xn, w.lm_head)
+        N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
+                               self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
+                               0, self.offset.data_ptr(), bf, st), "sample")
+
+    def _tp_gemm(self, x, w, epilogue, out_offset=-1, ldy=0, wait=-1, signal=-1):
+        N.check(N.lib().mvb_tp_gemm_bf16(self.heap.comm, x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), self.B,
+                                         w.shape[0], w.shape[1], epilogue, self.gemm_ws.data_ptr(),
+                                         self.gemm_ws.numel(), out_offset, ldy, wait, signal, self._st),
+                "tp_gemm_bf16")
+
+    def _tp_add_norm(self, gemm_k, weight, recv, wait, signal):
+        N.check(N.lib().mvb_tp_fused_add_rmsnorm_gemm(self.heap.comm, self.residual.data_ptr(), self.B, self.H, gemm_k,
+                                                      weight.data_ptr(), self.eps, 0, recv, wait, self.layout.xn,
+                                                      signal, self._st), "tp_fused_add_rmsnorm_gemm")
+
+    def _forward_tp(self) -> None:
+        """The step on one rank of a tensor-parallel group (see tensor_parallel): same kernels,
+        local head / feature counts, and the cross-GPU exchanges inside the row-parallel GEMMs,
+        the add+norm kernels, the lm_head GEMM and one wait before sampling."""
+        lib, w, B, H, D = N.lib(), self.w, self.B, self.H, self.D
+        self._st = N.stream_handle(self.dev)
+        st, eps, bf, lay = self._st, self.eps, N.BF16, self.layout
+        comm = self.heap.comm
+        kvc = self.kv.kv_cache
+        ws = self.gemm_ws.data_ptr()
+        N.check(lib.mvb_tp_begin_step(comm, st), "tp_begin_step")
+        N.check(lib.mvb_embedding(self.residual.data_ptr(), self.ids.data_ptr(), N.I32, w.embed.data_ptr(), B, H,
+                                  self.V, 1.0, bf, st), "embedding")
+        N.check(lib.mvb_rmsnorm(self.xn.data_ptr(), H, self.residual.data_ptr(), H, w.ln1[0].data_ptr(), B, H, eps, 0,
+                                N.NORM_MODEL, bf, st), "rmsnorm")
+        for i in range(self.L):
+            if i > 0:
+                self._tp_add_norm(self.I, w.ln1[i], lay.recv_down, tpm.point_down(i - 1), tpm.point_mlp_norm(i - 1))
+            self._tp_gemm(self.xn, w.wqkv[i], N.EPI_PARTIALS, wait=-1 if i == 0 else tpm.point_mlp_norm(i - 1))
+            N.check(lib.mvb_qk_norm_rope_kv_write_gemm(
+                self.q.data_ptr(), kvc.data_ptr(), ws, H,
+                w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
+                self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0], self.pos.data_ptr(),
+                self.block_tables.data_ptr(), self.max_blocks, B, self.Hq, self.Hkv, D, self.L, i, self.P,
+                self.kv.block_size, eps, st), "qk_norm_rope_kv_write_gemm")
+            N.check(lib.mvb_paged_attention_decode(
+                self.attn.data_ptr(), self.attn.stride(0), self.q.data_ptr(), self.Hq * D, kvc.data_ptr(),
+                self.block_tables.data_ptr(), self.max_blocks, self.ctx.data_ptr(), B, self.Hq, self.Hkv, D,
+                self.L, i, self.P, self.kv.block_size, self.scale, self.attn_ws.data_ptr(), self.attn_ws.numel(), st),
+                "paged_attention_decode")
+            self._tp_gemm(self.attn, w.wo[i], N.EPI_PARTIALS, out_offset=lay.recv_o, signal=tpm.point_o_proj(i))
+            self._tp_add_norm(self.Hq * D, w.ln2[i], lay.recv_o, tpm.point_o_proj(i), tpm.point_attn_norm(i))
+            self._tp_gemm(self.xn, w.wgu[i], N.EPI_SWIGLU_PARTIALS, wait=tpm.point_attn_norm(i))
+            N.check(lib.mvb_swiglu_gemm(self.h.data_ptr(), self.h.stride(0), ws, B, self.I, H, st), "swiglu_gemm")
+            self._tp_gemm(self.h, w.wdown[i], N.EPI_PARTIALS, out_offset=lay.recv_down, signal=tpm.point_down(i))
+        last = self.L - 1
+        self._tp_add_norm(self.I, w.final_norm, lay.recv_down, tpm.point_down(last), tpm.point_mlp_norm(last))
+        # vocab-parallel lm_head: this rank's columns into every rank's full logits
+        self._tp_gemm(self.xn, w.lm_head, N.EPI_STORE, out_offset=lay.logits + self.tp.rank * self.Vl * 2,
+                      ldy=self.V, wait=tpm.point_mlp_norm(last), signal=tpm.point_logits(self.L))
+        N.check(lib.mvb_tp_wait(comm, tpm.point_logits(self.L), st), "tp_wait")
         N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
                                self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
                                0, self.offset.data_ptr(), bf, st), "sample")
@@ -276,6 +363,10 @@ class DecodeRunner:
                                                    self.gemm_ws.data_ptr(), B, H, self.Hq * D, w.ln2[i].data_ptr(),
                                                    eps, 0, st), "fused_add_rmsnorm_gemm")
 
+        def swiglu(i):
+            N.check(lib.mvb_swiglu_gemm(self.h.data_ptr(), self.h.stride(0), self.gemm_ws.data_ptr(), B, self.I, H,
+                                        st), "swiglu_gemm")
+
         def samp(i):
             N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
                                    self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(),
@@ -287,12 +378,13 @@ class DecodeRunner:
                          gemm_bytes(qkv_n, H, 0), 2 * B * qkv_n * H),
             "gemm_o_proj": (lambda i: self._gemm(None, self.attn, w.wo[i], N.EPI_PARTIALS), self.L,
                             gemm_bytes(H, self.Hq * D, 0), 2 * B * H * self.Hq * D),
-            "gemm_gate_up_swiglu": (lambda i: self._gemm(self.h, self.xn, w.wgu[i], N.EPI_SWIGLU), self.L,
-                                    gemm_bytes(2 * self.I, H, self.I), 2 * B * 2 * self.I * H),
+            "gemm_gate_up": (lambda i: self._gemm(None, self.xn, w.wgu[i], N.EPI_SWIGLU_PARTIALS), self.L,
+                             gemm_bytes(2 * self.I, H, 0), 2 * B * 2 * self.I * H),
+            "swiglu_gemm": (swiglu, self.L, B * 2 * self.I * 4 + B * self.I * 2, 0),
             "gemm_down": (lambda i: self._gemm(None, self.h, w.wdown[i], N.EPI_PARTIALS), self.L,
                           gemm_bytes(H, self.I, 0), 2 * B * H * self.I),
             "gemm_lm_head": (lambda i: self._gemm(self.logits, self.xn, w.lm_head), 1,
-                             gemm_bytes(self.V, H, self.V), 2 * B * self.V * H),
+                             gemm_bytes(self.Vl, H, self.Vl), 2 * B * self.Vl * H),
             "qk_norm_rope_kv_write": (qk, self.L, B * qkv_n * 2 + B * self.Hq * D * 2 + 2 * B * self.Hkv * D * 2, 0),
             "fused_add_rmsnorm": (fadd, 2 * self.L, 5 * B * H * 2, 0),
             "sample": (samp, 1, B * self.V * 2, 0),
@@ -320,10 +412,20 @@ class DecodeRunner:
                          "gbs": nbytes / (avg * 1e-3) / 1e9}
         return out
 
+    def algorithmic_step_bytes(self) -> int:
+        """HBM bytes a decode step cannot avoid at the current context lengths: streamed weights,
+        K and V of every attended token in every layer, and the new token's K and V."""
+        ctx = int(self.ctx.cpu().sum())
+        kv_token = self.L * self.Hkv * self.D * 2 * 2
+        return self.w.streamed_bytes() + ctx * kv_token + self.B * kv_token
+
     def launches_per_step(self) -> int:
-        """Kernels one step launches: embedding, rmsnorm, 7 per layer (qkv, qk-norm/rope/kv, attention,
-        o_proj, add+norm, gate_up, down), an add+norm between layers, final add+norm, lm_head, sample."""
-        return 2 + self.L * 7 + (self.L - 1) + 3
+        """Kernels one step launches: embedding, rmsnorm, 8 per layer (qkv, qk-norm/rope/kv, attention,
+        o_proj, add+norm, gate_up, swiglu, down), an add+norm between layers, final add+norm, lm_head,
+        sample."""
+        if self.tp.enabled:   # + the step-counter kernel and the wait before sampling
+            return 2 + self.L * 8 + (self.L - 1) + 3 + 2
+        return 2 + self.L * 8 + (self.L - 1) + 3
 
     # ------------------------------------------------------------------ graphs
     def capture(self) -> None:
@@ -352,6 +454,15 @@ class DecodeRunner:
             self.replay()
         else:
             self.forward()
+
+    def close(self) -> None:
+        """Releases the graph, then the symmetric heap (tensor parallel)."""
+        self.graph = None
+        if self.heap is not None:
+            torch.cuda.synchronize(self.dev)
+            self.xn = self.logits = None
+            self.heap.close()
+            self.heap = None
 
     def fetch_tokens(self) -> torch.Tensor:
         self.tokens_host.copy_(self.tokens, non_blocking=True)

@@ -1,0 +1,160 @@
+"""Host side of tensor parallelism, on the CPU with the gloo backend (world size 2).
+
+The GPU path shards the weights with ``tensor_parallel.shard_state_dict`` and lets its kernels
+sum the row-parallel outputs across ranks and gather the vocab-parallel logits.  Here two gloo
+ranks run one decode step of a small Qwen3-family model in fp32 with exactly those shards,
+replacing the kernels' exchanges with ``all_reduce`` / ``all_gather``, and must reproduce the
+unsharded step: this pins the slicing (query heads <-> o_proj columns, KV heads <-> GQA groups,
+gate/up rows <-> down_proj columns, vocab slices in rank order).  Also checked: every rank
+plans the same heap layout, the signal points of one step are distinct, and the replicated FIFO
+block allocator hands every rank the same block ids.
+"""
+import math
+import os
+import random
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from llm_pytorch_inference_b200 import tensor_parallel as tpm
+from llm_pytorch_inference_b200.configs import get_config, head_dim, num_kv_heads
+from llm_pytorch_inference_b200.kv_cache import KVCacheManager
+from llm_pytorch_inference_b200.weights import canonical_state_dict
+
+CFG = dict(num_hidden_layers=2, hidden_size=256, num_attention_heads=8, num_key_value_heads=4,
+           intermediate_size=512, vocab_size=1000)
+
+
+def _rms(x, w, eps):
+    return w * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps))
+
+
+def _step(cfg, sd, x_ids, kcache, vcache, pos, reduce, gather, kv_heads, q_heads):
+    """One decode token per row in fp32; kcache/vcache [L, B, T, kv_heads, D] hold positions < pos."""
+    H, D, eps = cfg["hidden_size"], head_dim(cfg), cfg["rms_norm_eps"]
+    group = q_heads // kv_heads
+    B = x_ids.shape[0]
+    res = sd["model.embed_tokens.weight"][x_ids]
+    for i in range(cfg["num_hidden_layers"]):
+        p = f"model.layers.{i}."
+        xn = _rms(res, sd[p + "input_layernorm.weight"], eps)
+        q = (xn @ sd[p + "self_attn.q_proj.weight"].T).view(B, q_heads, D)
+        k = (xn @ sd[p + "self_attn.k_proj.weight"].T).view(B, kv_heads, D)
+        v = (xn @ sd[p + "self_attn.v_proj.weight"].T).view(B, kv_heads, D)
+        q = _rms(q, sd[p + "self_attn.q_norm.weight"], eps)
+        k = _rms(k, sd[p + "self_attn.k_norm.weight"], eps)
+        K = torch.cat([kcache[i], k[:, None]], 1)              # [B, T+1, kv, D] (RoPE omitted: slicing test)
+        V = torch.cat([vcache[i], v[:, None]], 1)
+        Kq = K.repeat_interleave(group, dim=2)                  # GQA: query head h reads KV head h // group
+        Vq = V.repeat_interleave(group, dim=2)
+        s = torch.einsum("bhd,bthd->bht", q, Kq) / math.sqrt(D)
+        o = torch.einsum("bht,bthd->bhd", s.softmax(-1), Vq).reshape(B, q_heads * D)
+        res = res + reduce(o @ sd[p + "self_attn.o_proj.weight"].T)
+        xn = _rms(res, sd[p + "post_attention_layernorm.weight"], eps)
+        h = torch.nn.functional.silu(xn @ sd[p + "mlp.gate_proj.weight"].T) * (xn @ sd[p + "mlp.up_proj.weight"].T)
+        res = res + reduce(h @ sd[p + "mlp.down_proj.weight"].T)
+    xn = _rms(res, sd["model.norm.weight"], eps)
+    return gather(xn @ sd["lm_head.weight"].T)
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = get_config("qwen3-tiny", **CFG)
+        sd = canonical_state_dict(cfg, seed=0, dtype=torch.float32)
+        for k in sd:
+            if k.endswith("norm.weight"):   # non-trivial norm weights
+                sd[k] = 1 + 0.1 * torch.randn(sd[k].shape, generator=torch.Generator().manual_seed(len(k)))
+        L, D = cfg["num_hidden_layers"], head_dim(cfg)
+        hq, hkv = cfg["num_attention_heads"], num_kv_heads(cfg)
+        B, T = 6, 5
+        g = torch.Generator().manual_seed(3)
+        ids = torch.randint(0, cfg["vocab_size"], (B,), generator=g)
+        kc = torch.randn(L, B, T, hkv, D, generator=g)
+        vc = torch.randn(L, B, T, hkv, D, generator=g)
+
+        shard = tpm.shard_state_dict(cfg, sd, world, rank)
+        lh = hkv // world
+
+        def reduce(t):
+            t = t.clone()
+            dist.all_reduce(t)
+            return t
+
+        def gather(t):
+            parts = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(parts, t.contiguous())
+            return torch.cat(parts, -1)
+
+        got = _step(cfg, shard, ids, kc[:, :, :, rank * lh:(rank + 1) * lh], vc[:, :, :, rank * lh:(rank + 1) * lh],
+                    T, reduce, gather, lh, hq // world)
+        want = _step(cfg, sd, ids, kc, vc, T, lambda t: t, lambda t: t, hkv, hq)
+        err = float((got - want).abs().max())
+
+        # heap plan, signal points, replicated allocator
+        layout = tpm.plan_heap(33024, 64, 4096, 151936, 3 << 20, 6 << 20)
+        layouts = [None] * world
+        dist.all_gather_object(layouts, layout)
+        pts = [f(i) for i in range(36) for f in (tpm.point_o_proj, tpm.point_attn_norm, tpm.point_down,
+                                                  tpm.point_mlp_norm)] + [tpm.point_logits(36)]
+        order = list(range(300))
+        random.Random(0).shuffle(order)
+        kv = KVCacheManager(300, 16, 2, 2, 128, device="cpu", free_order=order, allocate_pool=False)
+        tabs = [kv.allocate(s, 17 + 23 * s) for s in range(8)]
+        for _ in range(40):
+            for s in range(8):
+                kv.append_token(s)
+        tabs = [kv.get_block_table(s) for s in range(8)]
+        all_tabs = [None] * world
+        dist.all_gather_object(all_tabs, tabs)
+        results[rank] = {"err": err, "scale": float(want.abs().max()),
+                         "layouts_equal": all(x == layouts[0] for x in layouts),
+                         "points_distinct": len(set(pts)) == len(pts) and max(pts) < 1024,
+                         "tables_equal": all(t == all_tabs[0] for t in all_tabs)}
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_step_reproduces_the_unsharded_step_on_two_gloo_ranks():
+    world = 2
+    with mp.get_context("spawn").Manager() as m:
+        results = m.dict()
+        mp.spawn(_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+        res = dict(results)
+    for r in range(world):
+        assert res[r]["err"] <= 1e-4 * max(1.0, res[r]["scale"]), res[r]
+        assert res[r]["layouts_equal"] and res[r]["points_distinct"] and res[r]["tables_equal"], res[r]
+
+
+def test_shard_shapes_and_divisibility():
+    cfg = get_config("qwen3-8b", num_hidden_layers=1)
+    shapes = {"model.layers.0.self_attn.q_proj.weight": (4096, 4096), "model.layers.0.self_attn.k_proj.weight":
+              (1024, 4096), "model.layers.0.self_attn.v_proj.weight": (1024, 4096),
+              "model.layers.0.self_attn.o_proj.weight": (4096, 4096), "model.layers.0.mlp.gate_proj.weight":
+              (12288, 4096), "model.layers.0.mlp.up_proj.weight": (12288, 4096),
+              "model.layers.0.mlp.down_proj.weight": (4096, 12288), "lm_head.weight": (151936, 4096),
+              "model.embed_tokens.weight": (151936, 4096)}
+    sd = {k: torch.empty(s, dtype=torch.bfloat16, device="meta") for k, s in shapes.items()}
+    out = tpm.shard_state_dict(cfg, sd, 8, 3)
+    assert out["model.layers.0.self_attn.q_proj.weight"].shape == (512, 4096)
+    assert out["model.layers.0.self_attn.k_proj.weight"].shape == (128, 4096)
+    assert out["model.layers.0.self_attn.o_proj.weight"].shape == (4096, 512)
+    assert out["model.layers.0.mlp.gate_proj.weight"].shape == (1536, 4096)
+    assert out["model.layers.0.mlp.down_proj.weight"].shape == (4096, 1536)
+    assert out["lm_head.weight"].shape == (18992, 4096)
+    assert out["model.embed_tokens.weight"].shape == (151936, 4096)     # replicated
+    assert tpm.local_config(cfg, 8)["num_key_value_heads"] == 1
+    with pytest.raises(ValueError):
+        tpm.check_divisible(cfg, 3)

@@ -1,0 +1,117 @@
+"""One rank of the tensor-parallel parity run (launched by tests/test_tensor_parallel_gpu.py via
+torch.distributed.run, one process per GPU).
+
+Every rank builds the same 2-layer model at Qwen3-8B layer dims and the same batch of sequences
+on a shuffled block pool, and decodes with the tensor-parallel engine.  Rank 0 also decodes the
+same workload on one GPU (TP=1) and compares, step by step under teacher forcing, the full
+logits and the greedy tokens; it writes a JSON report to --out.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import random
+import sys
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+
+from llm_pytorch_inference_b200 import _native as N  # noqa: E402
+from llm_pytorch_inference_b200.configs import get_config  # noqa: E402
+from llm_pytorch_inference_b200.engine import DecodeEngine  # noqa: E402
+from llm_pytorch_inference_b200.tensor_parallel import TensorParallelConfig  # noqa: E402
+from llm_pytorch_inference_b200.weights import canonical_state_dict  # noqa: E402
+
+
+def build(cfg, tp, dev, batch, lens, num_blocks):
+    sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev)
+    order = list(range(num_blocks))
+    random.Random(0).shuffle(order)
+    eng = DecodeEngine(cfg, sd, max_batch=batch, max_model_len=max(lens) + 64, num_blocks=num_blocks, device=dev,
+                       free_order=order, tp=tp)
+    del sd
+    g = torch.Generator().manual_seed(1)
+    for s, n in enumerate(lens):
+        eng.add_sequence(s, torch.randint(0, cfg["vocab_size"], (n,), generator=g).tolist())
+        eng.append_first_token(s, int(torch.randint(0, cfg["vocab_size"], (1,), generator=g)))
+    # identical prompt K/V on every configuration: fill the full-head pool on the CPU, slice heads
+    T, r = tp.tp_size, tp.rank
+    hkv = eng.kv.num_heads
+    gk = torch.Generator().manual_seed(2)
+    for s in range(len(lens)):
+        for blk in eng.kv.get_block_table(s):
+            full = torch.randn(cfg["num_hidden_layers"], 2, 16, hkv * T, eng.kv.head_dim, generator=gk)
+            eng.kv.kv_cache[:, :, blk] = full[:, :, :, r * hkv:(r + 1) * hkv].to(dev, torch.bfloat16)
+    eng.set_sampling(0.0, -1, 1.0)
+    eng.prepare_first_step()
+    return eng
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", required=True)
+    ap.add_argument("--steps", type=int, default=4)
+    args = ap.parse_args()
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    N.set_pdl(True)
+    cfg = get_config("qwen3-8b", num_hidden_layers=2)
+    batch = 16
+    lens = [37 + 29 * i for i in range(batch)]          # ragged contexts, blocks cross boundaries
+    num_blocks = 512
+    eng = build(cfg, TensorParallelConfig(world, rank), dev, batch, lens, num_blocks)
+    ref = None
+    if rank == 0:
+        ref = build(cfg, TensorParallelConfig(1, 0), dev, batch, lens, num_blocks)
+    report = {"steps": [], "tables_equal": True}
+    for step in range(args.steps):
+        toks = eng.step(use_graph=step > 0)
+        tabs = [eng.kv.get_block_table(s) for s in range(batch)]
+        all_tabs = [None] * world
+        dist.all_gather_object(all_tabs, tabs)
+        report["tables_equal"] &= all(t == all_tabs[0] for t in all_tabs)
+        if rank == 0:
+            want = ref.step(use_graph=step > 0)
+            a = eng.runner.logits.float()
+            b = ref.runner.logits.float()
+            d = (a - b).abs()
+            top2 = b[:batch].topk(2, dim=-1).values
+            margin = (top2[:, 0] - top2[:, 1]).tolist()
+            # a greedy token may only differ where TP=1's own top-2 margin is within the logit noise
+            bad = [i for i in range(batch) if toks[i] != want[i] and margin[i] > 2 * float(d[i].max())]
+            report["steps"].append({"max_abs": float(d.max()), "mean_abs": float(d.mean()),
+                                    "tokens_tp": toks, "tokens_ref": want, "bad_token_rows": bad,
+                                    "tables_ref_equal": tabs == [ref.kv.get_block_table(s) for s in range(batch)]})
+            forced = want
+        else:
+            forced = None
+        obj = [forced]
+        dist.broadcast_object_list(obj, src=0)
+        eng.force_last_tokens(obj[0])            # teacher forcing: both continue from TP=1's tokens
+        if rank == 0:
+            ref.force_last_tokens(obj[0])
+    report["device_status"] = N.device_status(clear=True)
+    statuses = [None] * world
+    dist.all_gather_object(statuses, report["device_status"])
+    report["all_status"] = statuses
+    dist.barrier()
+    eng.runner.close()
+    if ref is not None:
+        ref.runner.close()
+    if rank == 0:
+        Path(args.out).write_text(json.dumps(report))
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
