@@ -145,15 +145,17 @@ def peaks() -> dict:
 
 
 def ncu_traffic() -> dict:
-    """Per-launch DRAM bytes from committed ncu summaries (lines 'traffic <kernel> <bytes>')."""
+    """DRAM bytes per launch from the committed ncu summaries: lines
+    ``traffic <kernel> <dram bytes per launch> <algorithmic bytes per launch of the captured case>``.
+    Returns kernel -> (traffic, case algorithmic bytes); the caller scales the traffic to its own
+    launch by the units processed (the ratio of algorithmic bytes)."""
     out = {}
-    for f in (REPO / "profiles").glob("*.md"):
+    for f in sorted((REPO / "profiles").glob("*.md")):
         for line in f.read_text().splitlines():
-            parts = line.strip().strip("|").split("|") if "|" in line else line.split()
-            parts = [p.strip() for p in parts]
-            if len(parts) >= 3 and parts[0] == "traffic":
+            parts = line.strip().strip("`").split()
+            if len(parts) == 4 and parts[0] == "traffic":
                 try:
-                    out[parts[1]] = float(parts[2])
+                    out[parts[1]] = (float(parts[2]), float(parts[3]))
                 except ValueError:
                     pass
     return out
@@ -244,9 +246,11 @@ def run_reference(args, rank: int, world: int) -> None:
     v = statistics.median(vals) if vals else last["value"]
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": BATCH / v * 1000.0, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"{ARCH} decode, batch {BATCH}, context {PROMPT}", "model": ARCH,
-                       "global_batch": BATCH, "seq_len": PROMPT, "parallelism": "cpu"},
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{ARCH} decode, batch {BATCH}, prompt {PROMPT}, T/top-k/top-p "
+                                   f"{SAMPLING[0]}/{SAMPLING[1]}/{SAMPLING[2]}",
+                       "model": ARCH, "layers": 36, "global_batch": BATCH, "seq_len": PROMPT,
+                       "parallelism": "cpu"},
             "cpu_baseline": {k: last[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -328,7 +332,8 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
         v["share"] = v["avg_ms"] * v["launches_per_step"] / step_ms
     top_name, top = max(kinds.items(), key=lambda kv: kv[1]["share"])
     pk = peaks()
-    traffic = ncu_traffic().get(top_name)
+    tr = ncu_traffic().get(top_name)
+    traffic = None if tr is None else round(tr[0] * top["bytes_per_launch"] / tr[1])
     achieved = top["bytes_per_launch"] / (top["avg_ms"] * 1e-3) / 1e9
     roof = {"kernel": top_name, "bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
             "frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": pk["source"],
