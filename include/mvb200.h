@@ -206,7 +206,8 @@ int mvb_paged_attention_decode_noalloc(void* out, int64_t out_stride, const void
 /* ---- dense GEMM on tcgen05 --------------------------------------------------------
  * Replaces the nn.Linear (cuBLAS) projections of the decode step (model_cuda.py:124-126,
  * :180, ops/mlp.py:66/84, model_cuda.py:413): Y[m, n] = sum_k X[m, k] * W[n, k] (bf16 in,
- * fp32 accumulate in TMEM).  Stream-K over all SMs; partial tiles merged in a fixed order.
+ * fp32 accumulate in TMEM).  Stream-K over all SMs (two CTAs per SM at m <= 64); partial tiles
+ * merged in a fixed order.
  * epilogue: MVB_EPI_STORE  Y = bf16(acc)
  *           MVB_EPI_SWIGLU W is the reference's cat([gate, up]) of 2*inter rows; Y[m, j] =
  *                          bf16(bf16(silu(bf16(gate))) * bf16(up)), j < inter (model.py:116-117)

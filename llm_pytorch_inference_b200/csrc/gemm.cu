@@ -9,8 +9,8 @@
 // Decode GEMMs have a tiny m, so the kernel computes D^T = W X^T ("swap AB"): a
 // 128-row slab of W is the UMMA M=128 operand, the whole batch is UMMA N=BN.  Both
 // operands are K-major and arrive through TMA in the 128-byte swizzle layout.  The
-// weight stream (the only large traffic) is split evenly over all SMs by
-// stream-K: CTA c owns k-blocks [c*T/G, (c+1)*T/G) of the linearised (tile, k-block)
+// weight stream (the only large traffic) is split evenly over G CTAs (two per SM at batch
+// <= 64, see splitk_ctas) by stream-K: CTA c owns k-blocks [c*T/G, (c+1)*T/G) of the linearised (tile, k-block)
 // space.  A tile covered by several CTAs is merged by the last CTA to finish it,
 // summing the fp32 partials in CTA order (deterministic).
 //
@@ -121,8 +121,7 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs& a, const TpGemm& 
 }
 
 // BN=64 (decode batches) keeps ~106 KB of shared memory and <= 168 registers so that two CTAs
-// fit on one SM: under programmatic dependent launch the next GEMM's CTAs become resident while
-// this one drains and stream their first weight tiles before the grid-dependency wait.
+// fit on one SM: the grid is two CTAs per SM, doubling the weight bytes in flight per SM.
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
@@ -435,7 +434,7 @@ extern "C" int64_t mvb_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int
   const int64_t bn = bn_for(m);
   // Counters sized for the larger of the two tilings (plain / SWIGLU pairs).
   const int64_t tiles = (n + 63) / 64;
-  const int64_t merge = counters_bytes(tiles) + 2LL * sms * bn * BM * 4 + 256;
+  const int64_t merge = counters_bytes(tiles) + 2LL * splitk_ctas(m, sms) * bn * BM * 4 + 256;
   int64_t part = splitk_partials_bytes(splitk_plan(m, n, k, sms)) + 256;
   if (n % 2 == 0) {
     const int64_t sw = splitk_partials_bytes(splitk_plan_swiglu(m, n / 2, k, sms)) + 256;
@@ -470,7 +469,8 @@ int gemm_launch(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
   const int64_t tiles = tiles_for(n, epilogue);
   const int64_t kblocks = k / BK;
   const int64_t total = tiles * kblocks;
-  const int grid = static_cast<int>(total < sms ? total : sms);
+  const int64_t ctas = splitk_ctas(m, sms);
+  const int grid = static_cast<int>(total < ctas ? total : ctas);
   // Partials at the head, tile counters at the tail of the workspace: calls of any shape
   // that share one buffer then use nested suffixes of the same (self-zeroing) counter area,
   // never bytes that another call used for partials.

@@ -49,13 +49,19 @@ __host__ __device__ __forceinline__ int64_t sk_offset(const SplitKPlan& p, int t
 
 inline int sk_bn_for(int64_t m) { return m <= 64 ? 64 : (m <= 128 ? 128 : 256); }
 
+// CTAs a decode GEMM of m batch rows may use on `sms` SMs.  At BN = 64 a CTA holds 4 x 24 KB
+// stages and 128 TMEM columns, so two fit on an SM; two CTAs per SM double the bytes in flight
+// per SM (4 stages x 16 KB of weights at ~1.8 us load latency sustain only ~5.4 TB/s).
+inline int64_t splitk_ctas(int64_t m, int sms) { return sk_bn_for(m) == 64 ? 2LL * sms : sms; }
+
 // The plan for `tiles` output tiles of a k-deep product over `m` batch rows on `sms` SMs.
 inline SplitKPlan splitk_plan_tiles(int64_t m, int tiles, int64_t k, int sms) {
   SplitKPlan p;
   p.tiles = tiles;
   p.kblocks = static_cast<int>(k / kSplitBK);
   const int64_t total = static_cast<int64_t>(p.tiles) * p.kblocks;
-  p.grid = static_cast<int>(total < sms ? total : sms);
+  const int64_t ctas = splitk_ctas(m, sms);
+  p.grid = static_cast<int>(total < ctas ? total : ctas);
   p.bn = sk_bn_for(m);
   p.maxc = 1;
   for (int t = 0; t < p.tiles; ++t) {

@@ -182,7 +182,8 @@ extern "C" int mvb_tp_gemm_bf16(mvb_tp_comm* comm, const void* x, int64_t ldx, c
     MVB_REQUIRE(sms > 0, "mvb_tp_gemm_bf16: no device");
     const int64_t tiles = epilogue == MVB_EPI_SWIGLU_PARTIALS ? (n / 2 + 63) / 64 : (n + kSplitBM - 1) / kSplitBM;
     const int64_t total = tiles * (k / kSplitBK);
-    tp.arrive_total = static_cast<uint32_t>(total < sms ? total : sms);   // the GEMM's grid
+    const int64_t ctas = splitk_ctas(m, sms);
+    tp.arrive_total = static_cast<uint32_t>(total < ctas ? total : ctas);   // the GEMM's grid
   }
   int grid = 0;
   MVB_TRY(gemm_launch(nullptr, gather ? ldy : 0, x, ldx, w, ldw, m, n, k, epilogue, nullptr, 0, workspace,
