@@ -11,9 +11,15 @@
 // spans several CTAs is merged by the last CTA to finish it, combining the partial
 // (max, sum, output) triples in CTA order, so results are deterministic.
 //
-// CTA = Hkv consumer warps (one per KV head, its GROUP query heads as the rows of a
-// 16-row mma tile) + 1 producer warp that streams each block's K and V (all heads)
-// through TMA into a 128-byte-swizzled [head][token][64] image, 2 halves of head_dim.
+// CTA = 8 consumer warps + 1 producer warp.  The producer streams each block's K and V
+// (all heads) through TMA into a 128-byte-swizzled image of 128-byte lines (head_dim split into
+// two halves of 64).  With >= 4 KV heads per GPU it issues 4 copies per block, one per (K|V,
+// half), image [kv][half][head][token][64]; with fewer heads (tensor-parallel shards, blocks of
+// 4-8 KB) the per-copy cost dominates and one 5-D copy per block is issued instead, image
+// [kv][token][head, half][64].  Consumer warp (h, w) serves KV head h -- its GROUP query heads are the rows of a
+// 16-row mma tile -- and with W = 8 / Hkv warps per head takes every W-th block of the CTA's
+// range, so a GPU holding few KV heads (tensor parallelism) still runs 8 warps per SM; the W
+// partial softmax states of a head are combined in shared memory at each sequence boundary.
 // QK^T and PV use mma.sync m16n8k16 (bf16 in, fp32 accumulate); softmax is the online
 // (running max / running sum) form in the exp2 domain.
 #include <mutex>
@@ -47,7 +53,6 @@ struct AttnArgs {
   float2* partial_ml;  // [2*G][Hq]  (running max in log2 units, running sum)
   int* counters;     // [batch]
   unsigned* err;
-  int per_head_tma;
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -80,15 +85,51 @@ __device__ __forceinline__ int cta_of(int64_t x, int64_t total, int grid) {
   return static_cast<int>(((x + 1) * grid + total - 1) / total - 1);
 }
 
-template <int HKV>
+template <int NCW>
 __device__ __forceinline__ void consumer_bar() {
-  asm volatile("bar.sync 1, %0;" ::"n"(HKV * 32) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
+}
+
+// Barrier of the W consumer warps of KV head h (named barriers 2 .. 2 + Hkv - 1).
+template <int W>
+__device__ __forceinline__ void head_bar(int h) {
+  asm volatile("bar.sync %0, %1;" ::"r"(2 + h), "n"(W * 32) : "memory");
+}
+
+// Consumer warps per KV head: 8 consumer warps per CTA in total, as long as the merge's
+// per-thread share (GROUP * D / (W * 32) outputs) stays whole.
+template <int GROUP, int HKV>
+__host__ __device__ constexpr int attn_wph() {
+  return (8 / HKV) < GROUP * (D / 32) ? (8 / HKV) : GROUP * (D / 32);
+}
+
+// One TMA copy per block (small blocks) or one per (K|V, half) (large blocks).
+__host__ __device__ constexpr bool attn_one_copy_for(int hkv) { return hkv <= 2; }
+template <int HKV>
+__host__ __device__ constexpr bool attn_one_copy() {
+  return attn_one_copy_for(HKV);
+}
+
+// 128-byte line of (kv, half, head, token) in a stage image of either layout.
+template <int HKV>
+__device__ __forceinline__ int attn_line(int kv, int half, int h, int tok) {
+  if constexpr (attn_one_copy<HKV>()) return (kv * BS + tok) * (2 * HKV) + 2 * h + half;
+  return ((kv * 2 + half) * HKV + h) * BS + tok;
+}
+
+// Shared memory of the per-head combine: every consumer warp's (m, l, o) for its GROUP rows.
+template <int GROUP, int HKV>
+__host__ __device__ constexpr int attn_combine_bytes() {
+  return attn_wph<GROUP, HKV>() > 1 ? HKV * attn_wph<GROUP, HKV>() * GROUP * (D + 2) * 4 : 0;
 }
 
 template <int GROUP, int HKV, int STAGES>
-__global__ void __launch_bounds__((HKV + 1) * 32, 1)
+__global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
     paged_attention_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs a) {
   constexpr int STAGE_BYTES = 4 * HKV * HALF_BYTES_PER_HEAD;  // K lo, K hi, V lo, V hi
+  constexpr int W = attn_wph<GROUP, HKV>();                  // consumer warps per KV head
+  constexpr int NCW = HKV * W;                                // consumer warps
+  static_assert(STAGES % W == 0, "a stage must always serve the same warp of each head");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -97,6 +138,9 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
   volatile int* last_flag = abort_flag + 1;
   int* cu = const_cast<int*>(abort_flag + 2);  // [batch + 1] block prefix sums
   float* merge_smem = reinterpret_cast<float*>(cu + a.batch + 1);  // split-sequence merge scratch
+  // per-head combine (W > 1), 16-byte aligned for its float2 accesses
+  float* combine_smem = reinterpret_cast<float*>(
+      (reinterpret_cast<uintptr_t>(merge_smem + (kMergeC + 2) * GROUP * HKV + kMergeC) + 15) & ~uintptr_t(15));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -155,7 +199,7 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
   }
 
   int issued = 0;
-  if (warp == HKV) {
+  if (warp == NCW) {
     // ---------------------------------------------------------------- producer
     // The whole warp fetches the next 32 block ids at once (one per lane, one round trip of
     // latency per 32 blocks); lane 0 then issues the TMA copies from the shuffled ids.
@@ -190,16 +234,14 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
             } else {
               mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
               uint8_t* st = smem + s * STAGE_BYTES;
-              for (int kv = 0; kv < 2; ++kv) {
-                const int row = static_cast<int>((a.layer * 2 + kv) * P + bi);
-                for (int half = 0; half < 2; ++half) {
-                  uint8_t* dst = st + (kv * 2 + half) * HKV * HALF_BYTES_PER_HEAD;
-                  if (a.per_head_tma) {
-                    for (int h = 0; h < HKV; ++h)
-                      tma_load_4d(dst + h * HALF_BYTES_PER_HEAD, &tm, &full[s], half * 64, h, 0, row, pol);
-                  } else {
-                    tma_load_4d(dst, &tm, &full[s], half * 64, 0, 0, row, pol);
-                  }
+              if constexpr (attn_one_copy<HKV>()) {
+                tma_load_5d(st, &tm, &full[s], 0, 0, 0, bi, static_cast<int>(a.layer * 2), pol);
+              } else {
+                for (int kv = 0; kv < 2; ++kv) {
+                  const int row = static_cast<int>((a.layer * 2 + kv) * P + bi);
+                  for (int half = 0; half < 2; ++half)
+                    tma_load_4d(st + (kv * 2 + half) * HKV * HALF_BYTES_PER_HEAD, &tm, &full[s], half * 64, 0, 0,
+                                row, pol);
                 }
               }
               issued = it + 1;
@@ -214,15 +256,13 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
     }
   } else {
     // ---------------------------------------------------------------- consumers
-    const int h = warp;  // KV head
+    const int h = warp / W, w = warp - (warp / W) * W;  // KV head, and this warp's turn among its W
     const int g = lane >> 2, t = lane & 3;
     const bool row_valid = g < GROUP;
     const uint32_t sbase = smem_u32(smem);
     int b = b0;
     int64_t gpos = g_begin;
-    int it = 0;
-    bool ok = true;
-    while (ok && gpos < g_end) {
+    while (gpos < g_end) {
       while (gpos >= cu[b + 1]) ++b;
       const int64_t seq_lo = cu[b], seq_hi = cu[b + 1];
       const int64_t seg_end = min(g_end, seq_hi);
@@ -247,16 +287,19 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
       for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
       float m_run = -INFINITY, l_run = 0.0f;
 
-      for (int64_t gg = gpos; gg < seg_end; ++gg, ++it) {
+      // This warp's blocks of the segment: iterations it = gg - g_begin with it % W == w.
+      const int64_t off = (gpos - g_begin) % W;
+      for (int64_t gg = gpos + (w - off + W) % W; gg < seg_end; gg += W) {
+        const int it = static_cast<int>(gg - g_begin);
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
-        if (!mbar_wait(&full[s], ph, nullptr, a.err)) {
-          ok = false;
-          break;
-        }
+        // A wait that gives up has reported the timeout and raised the abort flag; the warp
+        // carries on (on stale data) so that every warp still meets every barrier below.
+        mbar_wait(&full[s], ph, abort_flag, a.err);
         const int j = static_cast<int>(gg - seq_lo);  // block index within the sequence
-        const uint32_t kbase = sbase + s * STAGE_BYTES + h * HALF_BYTES_PER_HEAD;
-        const uint32_t vbase = kbase + 2 * HKV * HALF_BYTES_PER_HEAD;
+        // 128-byte lines of the stage image (attn_line); 16-byte chunks are XOR-swizzled with the
+        // line index mod 8 (the stage is 1024-byte aligned).
+        const uint32_t stage_base = sbase + s * STAGE_BYTES;
         // S = Q K^T for 16 tokens: two n-tiles of 8 tokens.
         float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
@@ -265,7 +308,8 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
           const int mi = lane >> 3;
           const int tok = (mi >> 1) * 8 + (lane & 7);
           const int chunk = (kk & 3) * 2 + (mi & 1);
-          const uint32_t addr = kbase + half * HKV * HALF_BYTES_PER_HEAD + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+          const int line = attn_line<HKV>(0, half, h, tok);
+          const uint32_t addr = stage_base + line * 128 + ((chunk ^ (line & 7)) << 4);
           uint32_t k0, k1, k2, k3;
           ldsm_x4(addr, k0, k1, k2, k3);
           mma_bf16_16816(sacc[0], qa[kk][0], 0u, qa[kk][1], 0u, k0, k1);
@@ -306,7 +350,8 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
           const int mi = lane >> 3;
           const int tok = (mi & 1) * 8 + (lane & 7);
           const int chunk = (np & 3) * 2 + (mi >> 1);
-          const uint32_t addr = vbase + half * HKV * HALF_BYTES_PER_HEAD + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+          const int line = attn_line<HKV>(1, half, h, tok);
+          const uint32_t addr = stage_base + line * 128 + ((chunk ^ (line & 7)) << 4);
           uint32_t v0, v1, v2, v3;
           ldsm_x4_t(addr, v0, v1, v2, v3);
           mma_bf16_16816(o[2 * np], pa0, 0u, pa2, 0u, v0, v1);
@@ -315,15 +360,53 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
       }
-      if (!ok) break;
 
       // Segment done: finish this warp's GROUP heads.
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+      if constexpr (W > 1) {
+        // Combine the W warps of head h: each publishes (m, l, o) of its rows; warp w == 0 merges
+        // them (a warp that had no block in the segment contributes m = -inf, l = 0, o = 0).
+        float* mine = combine_smem + static_cast<int64_t>(warp) * GROUP * (D + 2);
+        if (row_valid) {
+          float* r = mine + g * (D + 2);
+          if (t == 0) {
+            r[0] = m_run;
+            r[1] = l_run;
+          }
+#pragma unroll
+          for (int n = 0; n < 16; ++n) *reinterpret_cast<float2*>(r + 2 + n * 8 + 2 * t) = make_float2(o[n][0], o[n][1]);
+        }
+        head_bar<W>(h);
+        if (w == 0 && row_valid) {
+          const float* base = combine_smem + static_cast<int64_t>(h * W) * GROUP * (D + 2) + g * (D + 2);
+          float M = -INFINITY;
+#pragma unroll
+          for (int ww = 0; ww < W; ++ww) M = fmaxf(M, base[ww * GROUP * (D + 2)]);
+          float L = 0.0f;
+#pragma unroll
+          for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = 0.0f;
+#pragma unroll
+          for (int ww = 0; ww < W; ++ww) {
+            const float* r = base + ww * GROUP * (D + 2);
+            const float sc = r[0] == -INFINITY ? 0.0f : exp2f(r[0] - M);
+            L += r[1] * sc;
+#pragma unroll
+            for (int n = 0; n < 16; ++n) {
+              const float2 v = *reinterpret_cast<const float2*>(r + 2 + n * 8 + 2 * t);
+              o[n][0] += v.x * sc;
+              o[n][1] += v.y * sc;
+            }
+          }
+          m_run = M;
+          l_run = L;
+        }
+        head_bar<W>(h);  // the area is rewritten by the next segment
+      }
       const bool whole = (gpos == seq_lo) && (seg_end == seq_hi);
       const int hq = hq0 + g;
       if (whole) {
-        if (row_valid) {
+        if (w == 0 && row_valid) {
           const float inv = 1.0f / l_run;
           __nv_bfloat16* op = a.out + static_cast<int64_t>(b) * a.out_stride + static_cast<int64_t>(hq) * D;
 #pragma unroll
@@ -332,7 +415,7 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
         }
       } else {
         const int slot = (g_begin >= seq_lo) ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
-        if (row_valid) {
+        if (w == 0 && row_valid) {
           const float inv = 1.0f / l_run;
           float* po = a.partial_o + (static_cast<int64_t>(slot) * a.num_q_heads + hq) * D;
 #pragma unroll
@@ -340,7 +423,7 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
           if (t == 0) __stcg(a.partial_ml + static_cast<int64_t>(slot) * a.num_q_heads + hq, make_float2(m_run, l_run));
         }
         __threadfence();
-        consumer_bar<HKV>();
+        consumer_bar<NCW>();
         if (threadIdx.x == 0) {
           const int c_first = cta_of(seq_lo, total, G);
           const int c_last = cta_of(seq_hi - 1, total, G);
@@ -349,14 +432,15 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
           if (last) __threadfence();
           *last_flag = last;
         }
-        consumer_bar<HKV>();
+        consumer_bar<NCW>();
         if (*last_flag) {
           // Merge the sequence's partials (deterministic, contributor order).  Per-head max and
           // denominator first, then normalised weights staged in shared memory 32 contributors at a
           // time, and every thread accumulates its GROUP*4 outputs with all loads independent.
           constexpr int HQ = GROUP * HKV;
-          constexpr int NT = HKV * 32;
+          constexpr int NT = NCW * 32;
           constexpr int PER = HQ * D / NT;
+          static_assert(PER * NT == HQ * D, "merge share must be whole");
           float* s_w = merge_smem;                       // [kMergeC][HQ]
           float* s_M = s_w + kMergeC * HQ;               // [HQ]
           float* s_den = s_M + HQ;                       // [HQ]
@@ -385,7 +469,7 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
           for (int k = 0; k < PER; ++k) acc[k] = 0.0f;
           for (int j0 = 0; j0 < nc; j0 += kMergeC) {
             const int cn = nc - j0 < kMergeC ? nc - j0 : kMergeC;
-            consumer_bar<HKV>();
+            consumer_bar<NCW>();
             for (int e = threadIdx.x; e < cn * HQ; e += NT) {
               const int j = e / HQ, hh = e - j * HQ;
               const int c = c_first + j0 + j;
@@ -394,7 +478,7 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
               s_w[j * HQ + hh] = ml.y * exp2f(ml.x - s_M[hh]) / s_den[hh];
               if (hh == 0) s_slot[j] = sl;
             }
-            consumer_bar<HKV>();
+            consumer_bar<NCW>();
             for (int j = 0; j < cn; ++j) {
               const float* po = a.partial_o + static_cast<int64_t>(s_slot[j]) * HQ * D;
 #pragma unroll
@@ -409,33 +493,55 @@ __global__ void __launch_bounds__((HKV + 1) * 32, 1)
             a.out[static_cast<int64_t>(b) * a.out_stride + threadIdx.x + k * NT] = __float2bfloat16_rn(acc[k]);
           if (threadIdx.x == 0) a.counters[b] = 0;
         }
-        consumer_bar<HKV>();
+        consumer_bar<NCW>();
       }
       gpos = seg_end;
     }
   }
 
   __syncthreads();
-  if (warp == HKV && lane == 0) {
+  if (warp == NCW && lane == 0) {
     const int first = issued > STAGES ? issued - STAGES : 0;
     for (int it = first; it < issued; ++it) mbar_wait(&full[it % STAGES], (it / STAGES) & 1, nullptr, a.err);
   }
 }
 
-template <int HKV>
+constexpr int kAttnMaxBatch = 4096;
+
+// Shared memory other than the stages, at the largest batch: barriers, the block prefix sums,
+// the merge scratch, the per-head combine and the 1 KB alignment slack.
+template <int GROUP, int HKV>
+constexpr int attn_fixed_smem() {
+  return 2 * 8 * 32 + 16 + 4 * (kAttnMaxBatch + 1) + 4 * ((kMergeC + 2) * GROUP * HKV + kMergeC) + 16 +
+         attn_combine_bytes<GROUP, HKV>() + 1024;
+}
+
+// As many stages as fit in 227 KB next to the rest (at most 24), rounded down to a multiple of
+// the warps per head: iteration `it` uses stage it % STAGES and warp it % W of each head, so with
+// STAGES % W == 0 a stage only ever serves the same warp of each head, in iteration order.  A warp
+// therefore never waits on a stage more than one phase ahead of its last use, where the
+// mbarrier's parity would alias a stale phase as complete.
+template <int GROUP, int HKV>
 constexpr int attn_stages() {
-  return HKV >= 8 ? 3 : (HKV == 4 ? 6 : 8);
+  constexpr int stage = 4 * HKV * HALF_BYTES_PER_HEAD;
+  constexpr int W = attn_wph<GROUP, HKV>();
+  constexpr int n = (227 * 1024 - attn_fixed_smem<GROUP, HKV>()) / stage;
+  constexpr int c = n > 24 ? 24 : n;
+  return c / W * W;
 }
 
 template <int GROUP, int HKV>
 size_t attn_smem(int batch) {
-  return static_cast<size_t>(attn_stages<HKV>()) * 4 * HKV * HALF_BYTES_PER_HEAD + 2 * 8 * attn_stages<HKV>() + 16 +
-         4 * (batch + 1) + 4 * ((kMergeC + 2) * GROUP * HKV + kMergeC) + 1024;
+  return static_cast<size_t>(attn_stages<GROUP, HKV>()) * 4 * HKV * HALF_BYTES_PER_HEAD + 2 * 8 * 32 + 16 +
+         4 * (batch + 1) + 4 * ((kMergeC + 2) * GROUP * HKV + kMergeC) + 16 + attn_combine_bytes<GROUP, HKV>() +
+         1024;
 }
 
 template <int GROUP, int HKV>
 int launch_attn(const CUtensorMap& tm, const AttnArgs& a, int grid, cudaStream_t st) {
-  constexpr int S = attn_stages<HKV>();
+  constexpr int S = attn_stages<GROUP, HKV>();
+  static_assert(S >= 2, "two stages must fit");
+  constexpr int NT = (HKV * attn_wph<GROUP, HKV>() + 1) * 32;
   const size_t smem = attn_smem<GROUP, HKV>(a.batch);
   // Raise the kernel's dynamic-smem limit once per device (to the 4096-sequence maximum),
   // so no attribute call happens while a stream is being captured into a graph.
@@ -443,11 +549,12 @@ int launch_attn(const CUtensorMap& tm, const AttnArgs& a, int grid, cudaStream_t
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !(done_mask & (1ull << dev))) {
-    MVB_TRY(set_smem(paged_attention_kernel<GROUP, HKV, S>, attn_smem<GROUP, HKV>(4096), "paged_attention: smem attribute"));
+    MVB_TRY(set_smem(paged_attention_kernel<GROUP, HKV, S>, attn_smem<GROUP, HKV>(kAttnMaxBatch),
+                     "paged_attention: smem attribute"));
     if (dev < 64) done_mask |= 1ull << dev;
   }
-  return launch("paged_attention_decode", paged_attention_kernel<GROUP, HKV, S>, dim3(grid), dim3((HKV + 1) * 32),
-                smem, st, tm, a);
+  return launch("paged_attention_decode", paged_attention_kernel<GROUP, HKV, S>, dim3(grid), dim3(NT), smem, st, tm,
+                a);
 }
 
 template <int HKV>
@@ -466,25 +573,25 @@ int64_t attn_counters_bytes(int64_t batch) { return (batch * 4 + 255) / 256 * 25
 // Encodes the KV-pool tensor map.  Tries the one-box-per-half view (dims ordered
 // {dim, token, head, block}, which permutes the token/head strides) and falls back
 // to one box per head in natural stride order; both give the same shared-memory image.
-int encode_kv_map(CUtensorMap* m, const void* kv, int64_t hkv, int64_t rows, int* per_head) {
-  {
-    const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(BS), static_cast<uint64_t>(hkv),
-                              static_cast<uint64_t>(rows)};
-    const uint64_t strides[3] = {static_cast<uint64_t>(hkv * D * 2), static_cast<uint64_t>(D * 2),
-                                 static_cast<uint64_t>(BS * hkv * D * 2)};
-    const uint32_t box[4] = {64, BS, static_cast<uint32_t>(hkv), 1};
-    if (encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, kv, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) ==
-        MVB_OK) {
-      *per_head = 0;
-      return MVB_OK;
-    }
+// The KV-pool tensor map.  One-copy layout: dims (innermost first) 64 dims of a half, 2*Hkv
+// (head, half) lines of 128 bytes, 16 tokens, blocks, layer*2 + kv; one box = K and V of one
+// block, all heads.  Split layout: dims 128 dims, 16 tokens, Hkv heads (strides permuted so a
+// box lands as [head][token][64]), rows = (layer*2 + kv)*P + block; one box = one half of K or V.
+int encode_kv_map(CUtensorMap* m, const void* kv, int64_t hkv, int64_t num_blocks, int64_t num_layers,
+                  bool one_copy) {
+  const uint64_t block_bytes = static_cast<uint64_t>(BS * hkv * D * 2);
+  if (one_copy) {
+    const uint64_t dims[5] = {64, static_cast<uint64_t>(2 * hkv), static_cast<uint64_t>(BS),
+                              static_cast<uint64_t>(num_blocks), static_cast<uint64_t>(2 * num_layers)};
+    const uint64_t strides[4] = {128, static_cast<uint64_t>(hkv * D * 2), block_bytes,
+                                 block_bytes * static_cast<uint64_t>(num_blocks)};
+    const uint32_t box[5] = {64, static_cast<uint32_t>(2 * hkv), BS, 1, 2};
+    return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, kv, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   }
-  const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(hkv), static_cast<uint64_t>(BS),
-                            static_cast<uint64_t>(rows)};
-  const uint64_t strides[3] = {static_cast<uint64_t>(D * 2), static_cast<uint64_t>(hkv * D * 2),
-                               static_cast<uint64_t>(BS * hkv * D * 2)};
-  const uint32_t box[4] = {64, 1, BS, 1};
-  *per_head = 1;
+  const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(BS), static_cast<uint64_t>(hkv),
+                            static_cast<uint64_t>(2 * num_layers * num_blocks)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(hkv * D * 2), static_cast<uint64_t>(D * 2), block_bytes};
+  const uint32_t box[4] = {64, BS, static_cast<uint32_t>(hkv), 1};
   return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, kv, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
@@ -531,8 +638,7 @@ extern "C" int mvb_paged_attention_decode(void* out, int64_t out_stride, const v
               (long long)need);
 
   CUtensorMap tm;
-  int per_head = 0;
-  MVB_TRY(encode_kv_map(&tm, kv_cache, num_kv_heads, num_layers * 2 * num_blocks, &per_head));
+  MVB_TRY(encode_kv_map(&tm, kv_cache, num_kv_heads, num_blocks, num_layers, attn_one_copy_for(static_cast<int>(num_kv_heads))));
 
   AttnArgs a;
   a.out = static_cast<__nv_bfloat16*>(out);
@@ -552,7 +658,6 @@ extern "C" int mvb_paged_attention_decode(void* out, int64_t out_stride, const v
   a.partial_o = reinterpret_cast<float*>(ws + 2LL * sms * num_q_heads * 8);
   a.counters = reinterpret_cast<int*>(ws + ws_end - cbytes);
   a.err = device_status_ptr();
-  a.per_head_tma = per_head;
   // Grid: one persistent CTA per SM (192 KB of stages each); never more CTAs than blocks.
   // The block total is only known on the device, so the grid is the SM count and CTAs
   // with an empty range exit after the prologue.

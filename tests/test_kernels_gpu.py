@@ -315,6 +315,10 @@ def _attention_ref(q, pool, layer, bts, ctx, scale):
     (8, 4, [37, 50, 16, 64]),
     (32, 4, [700, 33]),                         # group 8 (Qwen3-30B-A3B heads)
     (4, 1, [513, 2, 31]),                       # one KV head per rank (TP=8 shard)
+    # many blocks per CTA with several consumer warps per KV head (tensor-parallel shards):
+    (16, 4, [2049] * 12 + [7, 300]),            # TP=2 shard of Qwen3-8B
+    (8, 2, [1200] * 16),                        # TP=4 shard
+    (4, 1, [2049] * 16),                        # TP=8 shard
 ])
 def test_paged_attention_matches_fp32_reference(Hq, Hkv, lens):
     D, L, layer = 128, 2, 1
