@@ -117,6 +117,13 @@ __device__ __forceinline__ int attn_line(int kv, int half, int h, int tok) {
   return ((kv * 2 + half) * HKV + h) * BS + tok;
 }
 
+// Floats of the split-sequence merge scratch: (m, l) pairs, weights, per-head max and
+// denominator, contributor slots.
+template <int GROUP, int HKV>
+__host__ __device__ constexpr int attn_merge_floats() {
+  return (3 * kMergeC + 2) * GROUP * HKV + kMergeC;
+}
+
 // Shared memory of the per-head combine: every consumer warp's (m, l, o) for its GROUP rows.
 template <int GROUP, int HKV>
 __host__ __device__ constexpr int attn_combine_bytes() {
@@ -137,10 +144,11 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + STAGES);
   volatile int* last_flag = abort_flag + 1;
   int* cu = const_cast<int*>(abort_flag + 2);  // [batch + 1] block prefix sums
-  float* merge_smem = reinterpret_cast<float*>(cu + a.batch + 1);  // split-sequence merge scratch
-  // per-head combine (W > 1), 16-byte aligned for its float2 accesses
+  // split-sequence merge scratch and per-head combine (W > 1), each 16-byte aligned (float2 use)
+  float* merge_smem =
+      reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(cu + a.batch + 1) + 15) & ~uintptr_t(15));
   float* combine_smem = reinterpret_cast<float*>(
-      (reinterpret_cast<uintptr_t>(merge_smem + (kMergeC + 2) * GROUP * HKV + kMergeC) + 15) & ~uintptr_t(15));
+      (reinterpret_cast<uintptr_t>(merge_smem + attn_merge_floats<GROUP, HKV>()) + 15) & ~uintptr_t(15));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -153,8 +161,11 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
     *last_flag = 0;
     fence_barrier_init();
   }
+  // Programmatic dependent launch: only q and the newest token's K/V (always in the last block of
+  // its sequence) come from the previous kernel.  Lengths and block tables are step metadata, so
+  // the prologue and the TMA copies of every other block run before the grid-dependency wait; the
+  // producer waits before issuing a sequence's last block, the consumers before reading q.
   if (threadIdx.x == 0) pdl_launch_dependents();
-  pdl_wait();
   // Per-sequence block counts -> prefix sums (warp 0, 32 sequences at a time).
   if (warp == 0) {
     int carry = 0;
@@ -209,12 +220,14 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
       const int64_t P = a.num_blocks;
       int b_lane = b0;
       bool ok = true;
+      bool waited = false;  // lane 0: grid-dependency wait done
       for (int64_t g0 = g_begin; ok && g0 < g_end; g0 += 32) {
         const int64_t g = g0 + lane;
-        int blk = 0;
+        int blk = 0, last = 0;
         if (g < g_end) {
           while (g >= cu[b_lane + 1]) ++b_lane;
           const int j = static_cast<int>(g - cu[b_lane]);
+          last = g == cu[b_lane + 1] - 1;
           blk = a.block_tables[static_cast<int64_t>(b_lane) * a.max_blocks + j];
           if (blk < 0 || blk >= P) {
             report(a.err, kDevBadBlock);
@@ -224,8 +237,13 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
         const int n = static_cast<int>(g_end - g0 < 32 ? g_end - g0 : 32);
         for (int i = 0; i < n; ++i) {
           const int bi = __shfl_sync(0xffffffffu, blk, i);
+          const int li = __shfl_sync(0xffffffffu, last, i);
           int good = 1;
           if (lane == 0) {
+            if (li && !waited) {  // this block holds the token the previous kernel wrote
+              pdl_wait();
+              waited = true;
+            }
             const int it = static_cast<int>(g0 - g_begin) + i;
             const int s = it % STAGES;
             const uint32_t ph = (it / STAGES) & 1;
@@ -256,6 +274,7 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
     }
   } else {
     // ---------------------------------------------------------------- consumers
+    pdl_wait();  // q, and the partial / counter workspace the previous launch may still use
     const int h = warp / W, w = warp - (warp / W) * W;  // KV head, and this warp's turn among its W
     const int g = lane >> 2, t = lane & 3;
     const bool row_valid = g < GROUP;
@@ -434,57 +453,90 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
         }
         consumer_bar<NCW>();
         if (*last_flag) {
-          // Merge the sequence's partials (deterministic, contributor order).  Per-head max and
-          // denominator first, then normalised weights staged in shared memory 32 contributors at a
-          // time, and every thread accumulates its GROUP*4 outputs with all loads independent.
+          // Merge the sequence's partials (deterministic, contributor order): per-head max and
+          // denominator, normalised weights staged in shared memory, then every thread accumulates
+          // its GROUP*4 outputs.  Up to kMergeC contributors (the usual case) take two rounds of
+          // global loads; more are merged kMergeC at a time.
           constexpr int HQ = GROUP * HKV;
           constexpr int NT = NCW * 32;
           constexpr int PER = HQ * D / NT;
           static_assert(PER * NT == HQ * D, "merge share must be whole");
-          float* s_w = merge_smem;                       // [kMergeC][HQ]
-          float* s_M = s_w + kMergeC * HQ;               // [HQ]
-          float* s_den = s_M + HQ;                       // [HQ]
-          int* s_slot = reinterpret_cast<int*>(s_den + HQ);  // [kMergeC]
+          float2* s_ml = reinterpret_cast<float2*>(merge_smem);  // [kMergeC][HQ]
+          float* s_w = merge_smem + 2 * kMergeC * HQ;            // [kMergeC][HQ]
+          float* s_M = s_w + kMergeC * HQ;                       // [HQ]
+          float* s_den = s_M + HQ;                               // [HQ]
+          int* s_slot = reinterpret_cast<int*>(s_den + HQ);      // [kMergeC]
           const int c_first = cta_of(seq_lo, total, G);
           const int nc = cta_of(seq_hi - 1, total, G) - c_first + 1;
-          for (int hh = threadIdx.x; hh < HQ; hh += NT) {
-            float M = -INFINITY;
-            for (int j = 0; j < nc; ++j) {
-              const int c = c_first + j;
-              const int sl = range_start(c, total, G) >= seq_lo ? 2 * c : 2 * c + 1;
-              M = fmaxf(M, __ldcg(a.partial_ml + static_cast<int64_t>(sl) * HQ + hh).x);
-            }
-            float den = 0.0f;
-            for (int j = 0; j < nc; ++j) {
-              const int c = c_first + j;
-              const int sl = range_start(c, total, G) >= seq_lo ? 2 * c : 2 * c + 1;
-              const float2 ml = __ldcg(a.partial_ml + static_cast<int64_t>(sl) * HQ + hh);
-              den += ml.y * exp2f(ml.x - M);
-            }
-            s_M[hh] = M;
-            s_den[hh] = den;
-          }
+          auto slot_of = [&](int j) {
+            const int c = c_first + j;
+            return range_start(c, total, G) >= seq_lo ? 2 * c : 2 * c + 1;
+          };
           float acc[PER];
 #pragma unroll
           for (int k = 0; k < PER; ++k) acc[k] = 0.0f;
-          for (int j0 = 0; j0 < nc; j0 += kMergeC) {
-            const int cn = nc - j0 < kMergeC ? nc - j0 : kMergeC;
-            consumer_bar<NCW>();
-            for (int e = threadIdx.x; e < cn * HQ; e += NT) {
+          if (nc <= kMergeC) {
+            for (int e = threadIdx.x; e < nc * HQ; e += NT) {
               const int j = e / HQ, hh = e - j * HQ;
-              const int c = c_first + j0 + j;
-              const int sl = range_start(c, total, G) >= seq_lo ? 2 * c : 2 * c + 1;
-              const float2 ml = __ldcg(a.partial_ml + static_cast<int64_t>(sl) * HQ + hh);
-              s_w[j * HQ + hh] = ml.y * exp2f(ml.x - s_M[hh]) / s_den[hh];
+              const int sl = slot_of(j);
+              s_ml[e] = __ldcg(a.partial_ml + static_cast<int64_t>(sl) * HQ + hh);
               if (hh == 0) s_slot[j] = sl;
             }
             consumer_bar<NCW>();
-            for (int j = 0; j < cn; ++j) {
+            for (int hh = threadIdx.x; hh < HQ; hh += NT) {
+              float M = -INFINITY;
+              for (int j = 0; j < nc; ++j) M = fmaxf(M, s_ml[j * HQ + hh].x);
+              float den = 0.0f;
+              for (int j = 0; j < nc; ++j) den += s_ml[j * HQ + hh].y * exp2f(s_ml[j * HQ + hh].x - M);
+              s_M[hh] = M;
+              s_den[hh] = den;
+            }
+            consumer_bar<NCW>();
+            for (int e = threadIdx.x; e < nc * HQ; e += NT) {
+              const int hh = e % HQ;
+              s_w[e] = s_ml[e].y * exp2f(s_ml[e].x - s_M[hh]) / s_den[hh];
+            }
+            consumer_bar<NCW>();
+#pragma unroll 4
+            for (int j = 0; j < nc; ++j) {
               const float* po = a.partial_o + static_cast<int64_t>(s_slot[j]) * HQ * D;
 #pragma unroll
               for (int k = 0; k < PER; ++k) {
                 const int i = threadIdx.x + k * NT;
                 acc[k] += s_w[j * HQ + i / D] * __ldcg(po + i);
+              }
+            }
+          } else {
+            for (int hh = threadIdx.x; hh < HQ; hh += NT) {
+              float M = -INFINITY;
+              for (int j = 0; j < nc; ++j)
+                M = fmaxf(M, __ldcg(a.partial_ml + static_cast<int64_t>(slot_of(j)) * HQ + hh).x);
+              float den = 0.0f;
+              for (int j = 0; j < nc; ++j) {
+                const float2 ml = __ldcg(a.partial_ml + static_cast<int64_t>(slot_of(j)) * HQ + hh);
+                den += ml.y * exp2f(ml.x - M);
+              }
+              s_M[hh] = M;
+              s_den[hh] = den;
+            }
+            for (int j0 = 0; j0 < nc; j0 += kMergeC) {
+              const int cn = nc - j0 < kMergeC ? nc - j0 : kMergeC;
+              consumer_bar<NCW>();
+              for (int e = threadIdx.x; e < cn * HQ; e += NT) {
+                const int j = e / HQ, hh = e - j * HQ;
+                const int sl = slot_of(j0 + j);
+                const float2 ml = __ldcg(a.partial_ml + static_cast<int64_t>(sl) * HQ + hh);
+                s_w[j * HQ + hh] = ml.y * exp2f(ml.x - s_M[hh]) / s_den[hh];
+                if (hh == 0) s_slot[j] = sl;
+              }
+              consumer_bar<NCW>();
+              for (int j = 0; j < cn; ++j) {
+                const float* po = a.partial_o + static_cast<int64_t>(s_slot[j]) * HQ * D;
+#pragma unroll
+                for (int k = 0; k < PER; ++k) {
+                  const int i = threadIdx.x + k * NT;
+                  acc[k] += s_w[j * HQ + i / D] * __ldcg(po + i);
+                }
               }
             }
           }
@@ -512,7 +564,7 @@ constexpr int kAttnMaxBatch = 4096;
 // the merge scratch, the per-head combine and the 1 KB alignment slack.
 template <int GROUP, int HKV>
 constexpr int attn_fixed_smem() {
-  return 2 * 8 * 32 + 16 + 4 * (kAttnMaxBatch + 1) + 4 * ((kMergeC + 2) * GROUP * HKV + kMergeC) + 16 +
+  return 2 * 8 * 32 + 16 + 4 * (kAttnMaxBatch + 1) + 16 + 4 * attn_merge_floats<GROUP, HKV>() + 16 +
          attn_combine_bytes<GROUP, HKV>() + 1024;
 }
 
@@ -533,8 +585,7 @@ constexpr int attn_stages() {
 template <int GROUP, int HKV>
 size_t attn_smem(int batch) {
   return static_cast<size_t>(attn_stages<GROUP, HKV>()) * 4 * HKV * HALF_BYTES_PER_HEAD + 2 * 8 * 32 + 16 +
-         4 * (batch + 1) + 4 * ((kMergeC + 2) * GROUP * HKV + kMergeC) + 16 + attn_combine_bytes<GROUP, HKV>() +
-         1024;
+         4 * (batch + 1) + 16 + 4 * attn_merge_floats<GROUP, HKV>() + 16 + attn_combine_bytes<GROUP, HKV>() + 1024;
 }
 
 template <int GROUP, int HKV>

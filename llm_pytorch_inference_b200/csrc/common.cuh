@@ -243,6 +243,13 @@ __device__ __forceinline__ void signal_add_release_sys(uint32_t* counter) {
   asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
 }
 
+// Release fence at system scope, then plain (relaxed) increments: one fence orders this thread's
+// earlier accesses, and what it acquired, before all of the increments.
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void signal_add_relaxed_sys(uint32_t* counter) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -445,10 +445,11 @@ extern "C" int64_t mvb_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int
 
 namespace mvb {
 
-// Shared body of mvb_gemm_bf16 and mvb_tp_gemm_bf16; `grid_out` receives the CTA count.
+// Shared body of mvb_gemm_bf16 and mvb_tp_gemm_bf16; `max_ctas` > 0 caps the CTA count (the
+// split-K plan follows), `grid_out` receives the CTA count.
 int gemm_launch(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t m, int64_t n,
                 int64_t k, int epilogue, const void* aux, int64_t ld_aux, void* workspace, int64_t workspace_bytes,
-                const TpGemm& tp, int* grid_out, mvb_stream_t stream) {
+                const TpGemm& tp, int64_t max_ctas, int* grid_out, mvb_stream_t stream) {
   MVB_REQUIRE(x && w && workspace && (y || partials_out(epilogue) || (tp.nranks > 0 && tp.y[0])),
               "mvb_gemm_bf16: null pointer");
   MVB_REQUIRE(m > 0 && m <= 256, "mvb_gemm_bf16: m=%lld outside [1, 256]", (long long)m);
@@ -469,7 +470,8 @@ int gemm_launch(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
   const int64_t tiles = tiles_for(n, epilogue);
   const int64_t kblocks = k / BK;
   const int64_t total = tiles * kblocks;
-  const int64_t ctas = splitk_ctas(m, sms);
+  int64_t ctas = splitk_ctas(m, sms);
+  if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
   const int grid = static_cast<int>(total < ctas ? total : ctas);
   // Partials at the head, tile counters at the tail of the workspace: calls of any shape
   // that share one buffer then use nested suffixes of the same (self-zeroing) counter area,
@@ -477,8 +479,7 @@ int gemm_launch(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
   const int64_t ws_end = workspace_bytes / 256 * 256;
   const int64_t cbytes = counters_bytes((n + 63) / 64);
   SplitKPlan plan{};
-  if (epilogue == MVB_EPI_PARTIALS) plan = splitk_plan(m, n, k, sms);
-  if (epilogue == MVB_EPI_SWIGLU_PARTIALS) plan = splitk_plan_swiglu(m, n / 2, k, sms);
+  if (partials_out(epilogue)) plan = splitk_plan_ctas(m, static_cast<int>(tiles), k, ctas);
   const int64_t need = partials_out(epilogue) ? splitk_partials_bytes(plan) : cbytes + 2LL * grid * bn * BM * 4;
   MVB_REQUIRE(ws_end >= need, "mvb_gemm_bf16: workspace %lld < %lld bytes", (long long)workspace_bytes,
               (long long)need);
@@ -530,6 +531,6 @@ extern "C" int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, c
                              int64_t m, int64_t n, int64_t k, int epilogue, const void* aux, int64_t ld_aux,
                              void* workspace, int64_t workspace_bytes, mvb_stream_t stream) {
   TpGemm tp{};
-  return gemm_launch(y, ldy, x, ldx, w, ldw, m, n, k, epilogue, aux, ld_aux, workspace, workspace_bytes, tp, nullptr,
-                     stream);
+  return gemm_launch(y, ldy, x, ldx, w, ldw, m, n, k, epilogue, aux, ld_aux, workspace, workspace_bytes, tp, 0,
+                     nullptr, stream);
 }

@@ -332,7 +332,7 @@ extern "C" int mvb_tp_fused_add_rmsnorm_gemm(mvb_tp_comm* comm, void* residual, 
   const int sms = current_sm_count();
   MVB_REQUIRE(sms > 0, "mvb_tp_fused_add_rmsnorm_gemm: no device");
   const int rpr = static_cast<int>(rows / nr);
-  const SplitKPlan p = splitk_plan(rows, hidden, gemm_k, sms);
+  const SplitKPlan p = splitk_plan_push(rows, hidden, gemm_k, sms, nr);
   MVB_REQUIRE(recv_offset >= kTpSignalBytes && recv_offset % 16 == 0 &&
                   recv_offset + splitk_push_bytes(p, nr, rpr) <= comm->heap_bytes,
               "mvb_tp_fused_add_rmsnorm_gemm: receive area outside the heap");

@@ -54,13 +54,12 @@ inline int sk_bn_for(int64_t m) { return m <= 64 ? 64 : (m <= 128 ? 128 : 256); 
 // per SM (4 stages x 16 KB of weights at ~1.8 us load latency sustain only ~5.4 TB/s).
 inline int64_t splitk_ctas(int64_t m, int sms) { return sk_bn_for(m) == 64 ? 2LL * sms : sms; }
 
-// The plan for `tiles` output tiles of a k-deep product over `m` batch rows on `sms` SMs.
-inline SplitKPlan splitk_plan_tiles(int64_t m, int tiles, int64_t k, int sms) {
+// The plan for `tiles` output tiles of a k-deep product over `m` batch rows on at most `ctas` CTAs.
+inline SplitKPlan splitk_plan_ctas(int64_t m, int tiles, int64_t k, int64_t ctas) {
   SplitKPlan p;
   p.tiles = tiles;
   p.kblocks = static_cast<int>(k / kSplitBK);
   const int64_t total = static_cast<int64_t>(p.tiles) * p.kblocks;
-  const int64_t ctas = splitk_ctas(m, sms);
   p.grid = static_cast<int>(total < ctas ? total : ctas);
   p.bn = sk_bn_for(m);
   p.maxc = 1;
@@ -69,6 +68,11 @@ inline SplitKPlan splitk_plan_tiles(int64_t m, int tiles, int64_t k, int sms) {
     if (c > p.maxc) p.maxc = c;
   }
   return p;
+}
+
+// The plan for `tiles` output tiles of a k-deep product over `m` batch rows on `sms` SMs.
+inline SplitKPlan splitk_plan_tiles(int64_t m, int tiles, int64_t k, int sms) {
+  return splitk_plan_ctas(m, tiles, k, splitk_ctas(m, sms));
 }
 
 // The plan the GEMM uses for a plain (non-SwiGLU) m x n x k product on `sms` SMs.
@@ -80,6 +84,22 @@ inline SplitKPlan splitk_plan(int64_t m, int64_t n, int64_t k, int sms) {
 // features 64t..64t+63 in rows 0-63 and the matching up features in rows 64-127.
 inline SplitKPlan splitk_plan_swiglu(int64_t m, int64_t inter, int64_t k, int sms) {
   return splitk_plan_tiles(m, static_cast<int>((inter + 63) / 64), k, sms);
+}
+
+// CTAs of a row-parallel GEMM in a tensor-parallel group of `nranks` > 1.  Such a GEMM pushes
+// every contributor's fp32 partial tile over NVLink to the rows' owners, so a tile is split over
+// at most one CTA per 16 k-blocks: at 8 ranks (k = 512 for o_proj) the stream-K split would put
+// ~9 contributors on every tile and push ~9x the bytes of the tile itself.
+inline int64_t splitk_push_ctas(int64_t m, int64_t n, int64_t k, int sms, int nranks) {
+  const int64_t full = splitk_ctas(m, sms);
+  if (nranks <= 1) return full;
+  const int64_t c = (n + kSplitBM - 1) / kSplitBM * ((k / kSplitBK + 15) / 16);
+  return c < full ? c : full;
+}
+
+inline SplitKPlan splitk_plan_push(int64_t m, int64_t n, int64_t k, int sms, int nranks) {
+  return splitk_plan_ctas(m, static_cast<int>((n + kSplitBM - 1) / kSplitBM), k,
+                          splitk_push_ctas(m, n, k, sms, nranks));
 }
 
 inline int64_t splitk_partials_bytes(const SplitKPlan& p) {

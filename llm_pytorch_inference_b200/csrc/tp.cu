@@ -30,7 +30,7 @@ namespace mvb {
 
 int gemm_launch(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t m, int64_t n,
                 int64_t k, int epilogue, const void* aux, int64_t ld_aux, void* workspace, int64_t workspace_bytes,
-                const TpGemm& tp, int* grid_out, mvb_stream_t stream);
+                const TpGemm& tp, int64_t max_ctas, int* grid_out, mvb_stream_t stream);
 
 namespace {
 
@@ -132,7 +132,7 @@ extern "C" int64_t mvb_tp_recv_bytes(int64_t m, int64_t n, int64_t k, int nranks
   int sms = mvb_num_sms(device);
   if (sms <= 0) sms = 148;
   if (nranks <= 0 || m % nranks != 0 || k % kSplitBK != 0) return -1;
-  return splitk_push_bytes(splitk_plan(m, n, k, sms), nranks, static_cast<int>(m / nranks));
+  return splitk_push_bytes(splitk_plan_push(m, n, k, sms, nranks), nranks, static_cast<int>(m / nranks));
 }
 
 extern "C" int mvb_tp_gemm_bf16(mvb_tp_comm* comm, const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t m,
@@ -164,7 +164,7 @@ extern "C" int mvb_tp_gemm_bf16(mvb_tp_comm* comm, const void* x, int64_t ldx, c
     const int sms = current_sm_count();
     MVB_REQUIRE(sms > 0, "mvb_tp_gemm_bf16: no device");
     tp.rows_per_rank = static_cast<int>(m / nr);
-    const int64_t need = splitk_push_bytes(splitk_plan(m, n, k, sms), nr, tp.rows_per_rank);
+    const int64_t need = splitk_push_bytes(splitk_plan_push(m, n, k, sms, nr), nr, tp.rows_per_rank);
     MVB_REQUIRE(out_offset >= kTpSignalBytes && out_offset % 16 == 0 && out_offset + need <= comm->heap_bytes,
                 "mvb_tp_gemm_bf16: receive area outside the heap");
     for (int q = 0; q < nr; ++q) tp.recv[q] = reinterpret_cast<float*>(comm->base[q] + out_offset);
@@ -182,12 +182,13 @@ extern "C" int mvb_tp_gemm_bf16(mvb_tp_comm* comm, const void* x, int64_t ldx, c
     MVB_REQUIRE(sms > 0, "mvb_tp_gemm_bf16: no device");
     const int64_t tiles = epilogue == MVB_EPI_SWIGLU_PARTIALS ? (n / 2 + 63) / 64 : (n + kSplitBM - 1) / kSplitBM;
     const int64_t total = tiles * (k / kSplitBK);
-    const int64_t ctas = splitk_ctas(m, sms);
+    const int64_t ctas = push ? splitk_push_ctas(m, n, k, sms, nr) : splitk_ctas(m, sms);
     tp.arrive_total = static_cast<uint32_t>(total < ctas ? total : ctas);   // the GEMM's grid
   }
   int grid = 0;
+  const int64_t max_ctas = push ? splitk_push_ctas(m, n, k, current_sm_count(), nr) : 0;
   MVB_TRY(gemm_launch(nullptr, gather ? ldy : 0, x, ldx, w, ldw, m, n, k, epilogue, nullptr, 0, workspace,
-                      workspace_bytes, tp, &grid, stream));
+                      workspace_bytes, tp, max_ctas, &grid, stream));
   if (signal_point >= 0) {
     MVB_REQUIRE(static_cast<uint32_t>(grid) == tp.arrive_total, "mvb_tp_gemm_bf16: grid mismatch");
     comm->point_count[signal_point] = 1;

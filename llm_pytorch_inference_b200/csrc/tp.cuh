@@ -27,15 +27,16 @@ constexpr int64_t kTpSignalBytes = kTpArriveOffset + static_cast<int64_t>(kTpMax
 // Called by one thread of each CTA of a signalling kernel, after a barrier over the CTA's
 // stores.  The CTAs meet on a local (GPU-scope, acquire-release) arrival counter; the last of
 // the `ctas` re-arms it and releases, at system scope, the stores of all of them to every rank
-// (one increment of each rank's counter per launch).  Release is cumulative over what the last
-// CTA acquired, so no separate system fence is needed.
+// (one increment of each rank's counter per launch): one system-scope release fence, cumulative
+// over what the last CTA acquired, then a relaxed increment per rank.
 __device__ __forceinline__ void signal_ranks_once(uint32_t* arrive, uint32_t ctas, uint32_t* const* signal,
                                                   int nranks) {
   uint32_t old;
   asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(arrive) : "memory");
   if (old == ctas - 1) {
     asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(arrive) : "memory");
-    for (int q = 0; q < nranks; ++q) signal_add_release_sys(signal[q]);
+    fence_acq_rel_sys();
+    for (int q = 0; q < nranks; ++q) signal_add_relaxed_sys(signal[q]);
   }
 }
 
