@@ -74,6 +74,38 @@ ARCHS: dict[str, dict] = {
         "tie_word_embeddings": False,
     },
     "qwen3-8b-2l": None,  # filled below: Qwen3-8B dims with 2 layers
+    # Qwen3-30B-A3B architecture: sparse MoE MLP (qwen3_moe_model.py), 128 experts, top-8.
+    "qwen3-30b-a3b": {
+        **_QWEN3_COMMON,
+        "model_type": "qwen3_moe",
+        "num_hidden_layers": 48,
+        "hidden_size": 2048,
+        "num_attention_heads": 32,
+        "num_key_value_heads": 4,
+        "intermediate_size": 6144,
+        "moe_intermediate_size": 768,
+        "num_experts": 128,
+        "num_experts_per_tok": 8,
+        "norm_topk_prob": True,
+        "vocab_size": 151936,
+        "tie_word_embeddings": False,
+    },
+    # Small MoE shapes for the parity tests.
+    "qwen3-moe-tiny": {
+        **_QWEN3_COMMON,
+        "model_type": "qwen3_moe",
+        "num_hidden_layers": 2,
+        "hidden_size": 512,
+        "num_attention_heads": 8,
+        "num_key_value_heads": 2,
+        "intermediate_size": 1024,
+        "moe_intermediate_size": 128,
+        "num_experts": 16,
+        "num_experts_per_tok": 4,
+        "norm_topk_prob": True,
+        "vocab_size": 4096,
+        "tie_word_embeddings": False,
+    },
 }
 
 ARCHS["qwen3-8b-2l"] = {**ARCHS["qwen3-8b"], "num_hidden_layers": 2}

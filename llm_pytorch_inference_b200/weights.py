@@ -37,9 +37,18 @@ def weight_shapes(cfg: dict) -> dict[str, tuple[int, ...]]:
         if cfg.get("_qk_norm", False):
             shapes[p + "self_attn.q_norm.weight"] = (hd,)
             shapes[p + "self_attn.k_norm.weight"] = (hd,)
-        shapes[p + "mlp.gate_proj.weight"] = (inter, H)
-        shapes[p + "mlp.up_proj.weight"] = (inter, H)
-        shapes[p + "mlp.down_proj.weight"] = (H, inter)
+        if cfg.get("num_experts"):   # sparse MoE block (qwen3_moe_model.py:23-65)
+            E, mi = cfg["num_experts"], cfg["moe_intermediate_size"]
+            shapes[p + "mlp.gate.weight"] = (E, H)
+            for e in range(E):
+                q = f"{p}mlp.experts.{e}."
+                shapes[q + "gate_proj.weight"] = (mi, H)
+                shapes[q + "up_proj.weight"] = (mi, H)
+                shapes[q + "down_proj.weight"] = (H, mi)
+        else:
+            shapes[p + "mlp.gate_proj.weight"] = (inter, H)
+            shapes[p + "mlp.up_proj.weight"] = (inter, H)
+            shapes[p + "mlp.down_proj.weight"] = (H, inter)
         shapes[p + "input_layernorm.weight"] = (H,)
         shapes[p + "post_attention_layernorm.weight"] = (H,)
     return shapes

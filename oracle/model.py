@@ -194,9 +194,54 @@ class OracleDecoder:
 
     def mlp(self, i, x):
         """``MLP.forward`` (``model.py:116-117``): ``down(act(gate(x)) * up(x))``."""
+        if self.cfg.get("num_experts"):
+            return self.moe(i, x)
         w, p = self.w, f"model.layers.{i}.mlp."
         return F.linear(self.act(F.linear(x, w[p + "gate_proj.weight"])) * F.linear(x, w[p + "up_proj.weight"]),
                         w[p + "down_proj.weight"])
+
+    def route(self, i, flat):
+        """Router of ``Qwen3MoeSparseMoe.forward`` (``qwen3_moe_model.py:45-53``): softmax over the
+        expert logits, top-k, optional renormalisation.  The reference's GPU decode runs under CUDA
+        autocast, where softmax computes and returns fp32 from the bf16 logits; that is the
+        semantics stated here for every dtype.  Ties among equal probabilities go to the lower
+        expert index."""
+        w, p = self.w, f"model.layers.{i}.mlp."
+        logits = F.linear(flat, w[p + "gate.weight"])
+        probs = F.softmax(logits.float(), dim=-1)
+        k = self.cfg["num_experts_per_tok"]
+        # stable descending order: equal probabilities keep ascending expert index
+        order = torch.sort(probs, dim=-1, descending=True, stable=True)
+        topw, topi = order.values[:, :k], order.indices[:, :k]
+        if self.cfg.get("norm_topk_prob", True):
+            topw = topw / topw.sum(dim=-1, keepdim=True)
+        return topw, topi
+
+    def moe(self, i, x):
+        """``Qwen3MoeSparseMoe.forward`` (``qwen3_moe_model.py:39-65``): each expert's
+        ``down(silu(gate(x)) * up(x))`` on its tokens; the weighted outputs are added into a zero
+        tensor of the model dtype expert by expert in ascending index (``final += w * out``: the
+        product in the routing weights' dtype, each addition rounded to the model dtype)."""
+        w, p = self.w, f"model.layers.{i}.mlp."
+        B, S, H = x.shape
+        flat = x.reshape(-1, H)
+        topw, topi = self.route(i, flat)
+        final = torch.zeros_like(flat)
+        for e in range(self.cfg["num_experts"]):
+            mask = topi == e
+            if not bool(mask.any()):
+                continue
+            tok = mask.any(dim=-1).nonzero(as_tuple=True)[0]
+            q = f"{p}experts.{e}."
+            xe = flat[tok]
+            out = F.linear(F.silu(F.linear(xe, w[q + "gate_proj.weight"])) * F.linear(xe, w[q + "up_proj.weight"]),
+                           w[q + "down_proj.weight"])
+            for k in range(topi.shape[1]):
+                km = mask[tok, k]
+                if bool(km.any()):
+                    rows = tok[km]
+                    final[rows] = (final[rows] + topw[rows, k].unsqueeze(-1) * out[km]).to(final.dtype)
+        return final.view(B, S, H)
 
     def forward(self, input_ids, positions, kv_pool=None, block_tables=None, slot_idx=None, use_cache=False,
                 num_cached=None, attn_mask=None, return_hidden=False, last_only=False):

@@ -13,6 +13,8 @@ PyTorch path (``MINI_VLLM_BACKEND=pytorch``, ``mini_vllm/ops/_utils.py:74``):
   ``LLMEngine._step`` (``engine/engine.py:241-360``): 4 prompts x 128 ids, 64 tokens.
 * ``decode_tiny_bf16.pt`` -- a 2-layer Qwen3-family bf16 model, ragged prompts,
   greedy 24 tokens, full per-step logits.
+* ``decode_moe_tiny_f32.pt`` -- a 2-layer Qwen3-MoE model (``models/qwen3_moe_model.py``,
+  16 experts, top-4) in fp32: its MoE block alone, and greedy decoding with full logits.
 
 Usage (only where the reference is mounted):
     python tests/golden/make_golden.py [--reference /root/reference]
@@ -252,6 +254,31 @@ def _decode_fixture(cfg, dtype, prompts, max_tokens, keep_full_logits):
     return fx
 
 
+def make_moe_golden() -> dict:
+    """The reference's sparse-MoE model (``models/qwen3_moe_model.py``) in fp32: the MoE block of
+    layer 0 on seeded hidden states, and greedy decoding through ``LLMEngine._step`` (the engine
+    picks the model class by ``model_type`` = ``qwen3_moe``)."""
+    from mini_vllm.models.qwen3_moe_model import Qwen3MoeSparseMoe
+
+    cfg = get_config("qwen3-moe-tiny")
+    sd = canonical_state_dict(cfg, seed=0, dtype=torch.float32)
+    block = Qwen3MoeSparseMoe(dict(cfg))
+    pre = "model.layers.0.mlp."
+    block.load_state_dict({k[len(pre):]: v for k, v in sd.items() if k.startswith(pre)}, strict=True)
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(1, 6, cfg["hidden_size"], generator=g)
+    with torch.no_grad():
+        y = block(x)
+    g = torch.Generator().manual_seed(11)
+    lens = [21, 40, 9, 33]
+    prompts = [torch.randint(0, cfg["vocab_size"], (n,), generator=g).tolist() for n in lens]
+    fx = _decode_fixture(cfg, torch.float32, prompts, 12, keep_full_logits=True)
+    fx["arch"] = "qwen3-moe-tiny"
+    fx["block_x"] = x
+    fx["block_y"] = y
+    return fx
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -279,6 +306,9 @@ def main() -> None:
         fx["arch"] = "qwen3-tiny"
         torch.save(fx, HERE / "decode_tiny_bf16.pt")
         print("decode_tiny_bf16.pt written")
+    if want("moe"):
+        torch.save(make_moe_golden(), HERE / "decode_moe_tiny_f32.pt")
+        print("decode_moe_tiny_f32.pt written")
     if want("cfg1"):
         cfg = get_config("qwen3-0.6b")
         g = torch.Generator().manual_seed(0)

@@ -125,3 +125,26 @@ def test_decode_cfg1_fp32_matches_reference(golden_dir):
     bts = json.loads(fx["decode_block_tables"])
     # Block tables at the last decode step are bit-exact (FIFO allocation from the shuffled pool).
     assert [eng.blocks.get_block_table(s) for s in range(4)] == bts[-1]
+
+
+def test_moe_block_matches_reference(golden_dir):
+    """``Qwen3MoeSparseMoe.forward`` of the reference (fp32) on seeded hidden states."""
+    fx = torch.load(golden_dir / "decode_moe_tiny_f32.pt")
+    cfg = get_config(fx["arch"])
+    from oracle.model import OracleDecoder
+
+    dec = OracleDecoder(cfg, canonical_state_dict(cfg, 0, torch.float32), torch.float32)
+    y = dec.moe(0, fx["block_x"])
+    torch.testing.assert_close(y, fx["block_y"], rtol=1e-6, atol=1e-7)
+
+
+def test_decode_moe_tiny_fp32_matches_reference(golden_dir):
+    """Greedy decoding of the reference's own sparse-MoE model through ``LLMEngine._step``."""
+    fx = torch.load(golden_dir / "decode_moe_tiny_f32.pt")
+    eng = _engine_for(fx, torch.float32)
+    prompts = [p.tolist() for p in fx["prompts"]]
+    out, step_logits = eng.generate_greedy(prompts, 12)
+    assert torch.equal(torch.tensor(out), fx["output_tokens"])
+    torch.testing.assert_close(torch.stack(step_logits), fx["decode_logits"], rtol=1e-5, atol=1e-5)
+    bts = json.loads(fx["decode_block_tables"])
+    assert [eng.blocks.get_block_table(s) for s in range(4)] == bts[-1]
