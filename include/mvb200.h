@@ -240,6 +240,37 @@ int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, const void* 
 int mvb_swiglu_gemm(void* out, int64_t out_stride, const void* gemm_workspace, int64_t rows, int64_t inter,
                     int64_t gemm_k, mvb_stream_t stream);
 
+/* ---- sparse mixture of experts (Qwen3-MoE) ---------------------------------------------
+ * Replace Qwen3MoeSparseMoe.forward (models/qwen3_moe_model.py:39-65) for one decode step.
+ *
+ * mvb_moe_route: router logits [rows, E] (bf16, the gate GEMM's output) -> fp32 softmax (the
+ * reference's GPU decode runs under CUDA autocast, where softmax computes in fp32), top_k experts
+ * per row (ties to the lower expert index), weights renormalised over the top_k when norm_topk.
+ * Outputs: topk_ids / topk_w [rows, top_k] (slots in descending probability); the dispatch order
+ * of the (row, slot) pairs -- by expert, rows ascending within an expert: pair_row [rows, top_k]
+ * (position of each pair), row_token [rows * top_k] (row of each position), expert_off [E + 1]
+ * (first position of each expert), active [1 + E] (count of experts with rows, then their ids
+ * ascending).  rows <= 256, E <= 256, top_k <= 16.  One CTA. */
+int mvb_moe_route(const void* logits, int64_t rows, int64_t num_experts, int64_t top_k, int norm_topk,
+                  int32_t* topk_ids, float* topk_w, int32_t* pair_row, int32_t* row_token, int32_t* expert_off,
+                  int32_t* active, mvb_stream_t stream);
+/* out[r] = x[row_token[r]] for r < nrows (bf16 rows of `hidden`, hidden % 8 == 0). */
+int mvb_moe_gather(void* out, const void* x, int64_t hidden, const int32_t* row_token, int64_t nrows,
+                   mvb_stream_t stream);
+/* Grouped GEMM over the active experts (tcgen05): w = [num_experts, n_per_expert, k] bf16; rows
+ * expert_off[e] .. expert_off[e+1]-1 of x (dispatch order, at most max_rows_per_expert <= 256 per
+ * expert) are multiplied by expert e's matrix:
+ *   MVB_EPI_STORE   y[r, j] = bf16(sum_k x[r, k] w[e, j, k]), j < n_per_expert   (down_proj)
+ *   MVB_EPI_SWIGLU  w[e] = cat(gate, up) of 2*inter rows (inter % 64 == 0):
+ *                   y[r, j] = bf16(bf16(silu(bf16(gate))) * bf16(up)), j < inter  (gate/up_proj) */
+int mvb_moe_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t n_per_expert,
+                      int64_t k, int64_t num_experts, int64_t nrows, int64_t max_rows_per_expert, int epilogue,
+                      const int32_t* expert_off, const int32_t* active, mvb_stream_t stream);
+/* out[row] = the reference's accumulation of the row's expert outputs y[pair_row] (bf16 rows of
+ * `hidden`): experts in ascending index, acc = bf16(acc + w * y) from acc = 0. */
+int mvb_moe_combine(void* out, const void* y, const float* topk_w, const int32_t* topk_ids, const int32_t* pair_row,
+                    int64_t rows, int64_t top_k, int64_t hidden, mvb_stream_t stream);
+
 /* ---- tensor parallelism (one process per GPU, NVLink peer memory) ----------------------
  * No counterpart in the reference beyond its stub (distributed/tensor_parallel.py:14-35,
  * tp_size > 1 raises).  These replace the NCCL all-reduce a Megatron-style split of the decode

@@ -72,14 +72,29 @@ class DecodeWeights:
         self.final_norm = get("model.norm.weight")
         self.qk_norm = cfg.get("_qk_norm", False)
         self.wqkv, self.wo, self.wgu, self.wdown, self.ln1, self.ln2, self.qn, self.kn = ([] for _ in range(8))
+        self.moe = bool(cfg.get("num_experts"))
+        self.router, self.egu, self.edown = [], [], []    # MoE: [E, H], [E, 2I, H], [E, H, I]
         for i in range(L):
             p = f"model.layers.{i}."
             a = p + "self_attn."
             self.wqkv.append(torch.cat([get(a + "q_proj.weight"), get(a + "k_proj.weight"),
                                         get(a + "v_proj.weight")], 0).contiguous())
             self.wo.append(get(a + "o_proj.weight"))
-            self.wgu.append(torch.cat([get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight")], 0).contiguous())
-            self.wdown.append(get(p + "mlp.down_proj.weight"))
+            if self.moe:
+                self.router.append(get(p + "mlp.gate.weight"))
+                e = p + "mlp.experts."
+                if e + "gate_up_proj.weight" in sd:
+                    self.egu.append(get(e + "gate_up_proj.weight"))
+                    self.edown.append(get(e + "down_proj.weight"))
+                else:
+                    E = cfg["num_experts"]
+                    self.egu.append(torch.stack([torch.cat([get(f"{e}{j}.gate_proj.weight"), get(f"{e}{j}.up_proj.weight")],
+                                                           0) for j in range(E)]).contiguous())
+                    self.edown.append(torch.stack([get(f"{e}{j}.down_proj.weight") for j in range(E)]).contiguous())
+            else:
+                self.wgu.append(torch.cat([get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight")],
+                                          0).contiguous())
+                self.wdown.append(get(p + "mlp.down_proj.weight"))
             self.ln1.append(get(p + "input_layernorm.weight"))
             self.ln2.append(get(p + "post_attention_layernorm.weight"))
             if self.qk_norm:
@@ -88,7 +103,7 @@ class DecodeWeights:
 
     def nbytes(self) -> int:
         ts = [self.embed, self.final_norm, *self.wqkv, *self.wo, *self.wgu, *self.wdown, *self.ln1, *self.ln2,
-              *self.qn, *self.kn]
+              *self.qn, *self.kn, *self.router, *self.egu, *self.edown]
         if self.lm_head is not self.embed:
             ts.append(self.lm_head)
         return sum(t.numel() * t.element_size() for t in ts)
@@ -97,7 +112,7 @@ class DecodeWeights:
         """Weight bytes one decode step must read: every layer's matrices and norms, the final norm
         and lm_head (the embedding table is only gathered, one row per sequence)."""
         ts = [self.final_norm, self.lm_head, *self.wqkv, *self.wo, *self.wgu, *self.wdown, *self.ln1, *self.ln2,
-              *self.qn, *self.kn]
+              *self.qn, *self.kn, *self.router, *self.egu, *self.edown]
         return sum(t.numel() * t.element_size() for t in ts)
 
 
@@ -153,6 +168,25 @@ class DecodeRunner:
         self.q = torch.zeros(B, self.Hq, self.D, dtype=bf, device=dev)
         self.attn = torch.zeros(B, self.Hq * self.D, dtype=bf, device=dev)
         self.h = torch.zeros(B, self.I, dtype=bf, device=dev)
+        self.moe = bool(cfg.get("num_experts"))
+        if self.moe:
+            if self.tp.enabled:
+                raise NotImplementedError("tensor parallelism of the MoE layers is not built")
+            self.E, self.K = cfg["num_experts"], cfg["num_experts_per_tok"]
+            self.Im = cfg["moe_intermediate_size"]
+            self.norm_topk = 1 if cfg.get("norm_topk_prob", True) else 0
+            i32 = torch.int32
+            self.router_logits = torch.zeros(B, self.E, dtype=bf, device=dev)
+            self.topk_ids = torch.zeros(B, self.K, dtype=i32, device=dev)
+            self.topk_w = torch.zeros(B, self.K, dtype=torch.float32, device=dev)
+            self.pair_row = torch.zeros(B, self.K, dtype=i32, device=dev)
+            self.row_token = torch.zeros(B * self.K, dtype=i32, device=dev)
+            self.expert_off = torch.zeros(self.E + 1, dtype=i32, device=dev)
+            self.active = torch.zeros(self.E + 1, dtype=i32, device=dev)
+            self.x_sorted = torch.zeros(B * self.K, H, dtype=bf, device=dev)
+            self.h_sorted = torch.zeros(B * self.K, self.Im, dtype=bf, device=dev)
+            self.y_sorted = torch.zeros(B * self.K, H, dtype=bf, device=dev)
+            self.mlp_out = torch.zeros(B, H, dtype=bf, device=dev)
         self.tokens = torch.zeros(B, dtype=torch.int64, device=dev)
         # per-row sampling parameters (greedy by default)
         self.temperature = torch.zeros(B, dtype=torch.float32, device=dev)
@@ -175,8 +209,10 @@ class DecodeRunner:
         self.block_tables = self.meta[self._o_bt:].view(B, self.max_blocks)
         self.tokens_host = torch.zeros(B, dtype=torch.int64, pin_memory=True)
 
-        gemm_ws = max(N.lib().mvb_gemm_workspace_bytes(B, n, k, didx) for n, k in
-                      ((qkv_n, H), (H, self.Hq * self.D), (2 * self.I, H), (H, self.I), (self.Vl, H)))
+        gemm_shapes = [(qkv_n, H), (H, self.Hq * self.D), (2 * self.I, H), (H, self.I), (self.Vl, H)]
+        if self.moe:
+            gemm_shapes.append((self.E, H))
+        gemm_ws = max(N.lib().mvb_gemm_workspace_bytes(B, n, k, didx) for n, k in gemm_shapes)
         attn_ws = N.lib().mvb_paged_attention_workspace_bytes(B, self.Hq, self.D, didx)
         self.gemm_ws = torch.zeros(gemm_ws, dtype=torch.uint8, device=dev)
         self.attn_ws = torch.zeros(attn_ws, dtype=torch.uint8, device=dev)
@@ -235,6 +271,9 @@ class DecodeRunner:
         if self.tp.enabled:
             self._forward_tp()
             return
+        if self.moe:
+            self._forward_moe()
+            return
         lib, w, B, H = N.lib(), self.w, self.B, self.H
         self._st = N.stream_handle(self.dev)
         st, eps, bf = self._st, self.eps, N.BF16
@@ -270,6 +309,71 @@ class DecodeRunner:
             self._gemm(None, self.h, w.wdown[i], N.EPI_PARTIALS)
         N.check(lib.mvb_fused_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(), ws, B, H, self.I,
                                                w.final_norm.data_ptr(), eps, 0, st), "fused_add_rmsnorm_gemm")
+        self._gemm(self.logits, self.xn, w.lm_head)
+        N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
+                               self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
+                               0, self.offset.data_ptr(), bf, st), "sample")
+
+    def _moe_mlp(self, i) -> None:
+        """The sparse MoE block on ``self.xn`` into ``self.mlp_out`` (``qwen3_moe_model.py:39-65``):
+        router GEMM, routing + dispatch order, gather, grouped gate/up (SwiGLU) and down GEMMs over
+        the active experts, expert-ordered weighted combine."""
+        lib, w, B, H, st = N.lib(), self.w, self.B, self.H, self._st
+        self._gemm(self.router_logits, self.xn, w.router[i])
+        N.check(lib.mvb_moe_route(self.router_logits.data_ptr(), B, self.E, self.K, self.norm_topk,
+                                  self.topk_ids.data_ptr(), self.topk_w.data_ptr(), self.pair_row.data_ptr(),
+                                  self.row_token.data_ptr(), self.expert_off.data_ptr(), self.active.data_ptr(), st),
+                "moe_route")
+        n = B * self.K
+        N.check(lib.mvb_moe_gather(self.x_sorted.data_ptr(), self.xn.data_ptr(), H, self.row_token.data_ptr(), n, st),
+                "moe_gather")
+        N.check(lib.mvb_moe_gemm_bf16(self.h_sorted.data_ptr(), self.Im, self.x_sorted.data_ptr(), H,
+                                      w.egu[i].data_ptr(), 2 * self.Im, H, self.E, n, B, N.EPI_SWIGLU,
+                                      self.expert_off.data_ptr(), self.active.data_ptr(), st), "moe_gemm gate_up")
+        N.check(lib.mvb_moe_gemm_bf16(self.y_sorted.data_ptr(), H, self.h_sorted.data_ptr(), self.Im,
+                                      w.edown[i].data_ptr(), H, self.Im, self.E, n, B, N.EPI_STORE,
+                                      self.expert_off.data_ptr(), self.active.data_ptr(), st), "moe_gemm down")
+        N.check(lib.mvb_moe_combine(self.mlp_out.data_ptr(), self.y_sorted.data_ptr(), self.topk_w.data_ptr(),
+                                    self.topk_ids.data_ptr(), self.pair_row.data_ptr(), B, self.K, H, st),
+                "moe_combine")
+
+    def _forward_moe(self) -> None:
+        """The step of a sparse-MoE model: the dense attention half as ``forward``, the MoE block
+        in place of the MLP, and a plain residual add + RMSNorm after it."""
+        lib, w, B, H, D = N.lib(), self.w, self.B, self.H, self.D
+        self._st = N.stream_handle(self.dev)
+        st, eps, bf = self._st, self.eps, N.BF16
+        kvc = self.kv.kv_cache
+        ws = self.gemm_ws.data_ptr()
+        N.check(lib.mvb_embedding(self.residual.data_ptr(), self.ids.data_ptr(), N.I32, w.embed.data_ptr(), B, H,
+                                  self.V, 1.0, bf, st), "embedding")
+        N.check(lib.mvb_rmsnorm(self.xn.data_ptr(), H, self.residual.data_ptr(), H, w.ln1[0].data_ptr(), B, H, eps, 0,
+                                N.NORM_MODEL, bf, st), "rmsnorm")
+        for i in range(self.L):
+            if i > 0:   # residual += MoE output, then input_layernorm
+                N.check(lib.mvb_fused_add_rmsnorm(self.xn.data_ptr(), self.residual.data_ptr(), self.mlp_out.data_ptr(),
+                                                  w.ln1[i].data_ptr(), B, H, eps, 0, N.NORM_MODEL, bf, st),
+                        "fused_add_rmsnorm")
+            self._gemm(None, self.xn, w.wqkv[i], N.EPI_PARTIALS)
+            N.check(lib.mvb_qk_norm_rope_kv_write_gemm(
+                self.q.data_ptr(), kvc.data_ptr(), ws, H,
+                w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
+                self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0], self.pos.data_ptr(),
+                self.block_tables.data_ptr(), self.max_blocks, B, self.Hq, self.Hkv, D, self.L, i, self.P,
+                self.kv.block_size, eps, st), "qk_norm_rope_kv_write_gemm")
+            N.check(lib.mvb_paged_attention_decode(
+                self.attn.data_ptr(), self.attn.stride(0), self.q.data_ptr(), self.Hq * D, kvc.data_ptr(),
+                self.block_tables.data_ptr(), self.max_blocks, self.ctx.data_ptr(), B, self.Hq, self.Hkv, D,
+                self.L, i, self.P, self.kv.block_size, self.scale, self.attn_ws.data_ptr(), self.attn_ws.numel(), st),
+                "paged_attention_decode")
+            self._gemm(None, self.attn, w.wo[i], N.EPI_PARTIALS)
+            N.check(lib.mvb_fused_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(), ws, B, H,
+                                                   self.Hq * D, w.ln2[i].data_ptr(), eps, 0, st),
+                    "fused_add_rmsnorm_gemm")
+            self._moe_mlp(i)
+        N.check(lib.mvb_fused_add_rmsnorm(self.xn.data_ptr(), self.residual.data_ptr(), self.mlp_out.data_ptr(),
+                                          w.final_norm.data_ptr(), B, H, eps, 0, N.NORM_MODEL, bf, st),
+                "fused_add_rmsnorm")
         self._gemm(self.logits, self.xn, w.lm_head)
         N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
                                self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
@@ -423,6 +527,8 @@ class DecodeRunner:
         """Kernels one step launches: embedding, rmsnorm, 8 per layer (qkv, qk-norm/rope/kv, attention,
         o_proj, add+norm, gate_up, swiglu, down), an add+norm between layers, final add+norm, lm_head,
         sample."""
+        if self.moe:   # 11 per layer: qkv, qk, attention, o_proj, add+norm, router, route, gather, 2 GEMMs, combine
+            return 2 + self.L * 11 + (self.L - 1) + 3
         if self.tp.enabled:   # + the step-counter kernel and the wait before sampling
             return 2 + self.L * 8 + (self.L - 1) + 3 + 2
         return 2 + self.L * 8 + (self.L - 1) + 3

@@ -58,11 +58,25 @@ def _is_norm(key: str) -> bool:
     return key.endswith("norm.weight")
 
 
+def stacked_expert_shapes(cfg: dict) -> dict[str, tuple[int, ...]]:
+    """``weight_shapes`` with each MoE layer's experts stacked: ``mlp.experts.gate_up_proj.weight``
+    ``[E, 2I, H]`` (per expert ``cat(gate, up)``) and ``mlp.experts.down_proj.weight`` ``[E, H, I]``."""
+    shapes = {k: v for k, v in weight_shapes(cfg).items() if ".mlp.experts." not in k}
+    E, mi, H = cfg["num_experts"], cfg["moe_intermediate_size"], cfg["hidden_size"]
+    for i in range(cfg["num_hidden_layers"]):
+        p = f"model.layers.{i}.mlp.experts."
+        shapes[p + "gate_up_proj.weight"] = (E, 2 * mi, H)
+        shapes[p + "down_proj.weight"] = (E, H, mi)
+    return shapes
+
+
 def canonical_state_dict(cfg: dict, seed: int = 0, dtype: torch.dtype = torch.float32,
-                         device: str | torch.device = "cpu") -> dict[str, torch.Tensor]:
-    """Seeded random-init state dict (sorted keys, N(0, 0.02), norms at ones)."""
+                         device: str | torch.device = "cpu", stacked_experts: bool = False) -> dict[str, torch.Tensor]:
+    """Seeded random-init state dict (sorted keys, N(0, 0.02), norms at ones).  With
+    ``stacked_experts`` (MoE only) the experts come pre-stacked (``stacked_expert_shapes``): same
+    law, different values, and no second copy of the experts when the decode weights are built."""
     plus_one = cfg.get("_rms_norm_plus_one", False)
-    shapes = weight_shapes(cfg)
+    shapes = stacked_expert_shapes(cfg) if stacked_experts and cfg.get("num_experts") else weight_shapes(cfg)
     dev = torch.device(device)
     gen = torch.Generator(device=dev).manual_seed(seed)
     out: dict[str, torch.Tensor] = {}

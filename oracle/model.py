@@ -88,6 +88,32 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
 
 
 # ----------------------------------------------------------------------- model
+def moe_route(logits: torch.Tensor, top_k: int, norm_topk: bool = True):
+    """``qwen3_moe_model.py:45-53``: softmax over the expert logits, top-k, optional
+    renormalisation.  The reference's GPU decode runs under CUDA autocast, where softmax computes
+    and returns fp32 from the bf16 logits; that is the semantics stated here for every dtype.
+    Ties among equal probabilities go to the lower expert index."""
+    probs = F.softmax(logits.float(), dim=-1)
+    order = torch.sort(probs, dim=-1, descending=True, stable=True)   # equal values: ascending index
+    topw, topi = order.values[:, :top_k], order.indices[:, :top_k]
+    if norm_topk:
+        topw = topw / topw.sum(dim=-1, keepdim=True)
+    return topw, topi
+
+
+def moe_combine(outs: torch.Tensor, topw: torch.Tensor, topi: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """``qwen3_moe_model.py:55-63`` for one token per row: ``outs[b, k]`` is expert ``topi[b, k]``'s
+    output for row b; the weighted outputs are added into zeros of ``dtype`` in ascending expert
+    order, each addition rounded to ``dtype``."""
+    B, K, H = outs.shape
+    final = torch.zeros(B, H, dtype=dtype)
+    for b in range(B):
+        for k in sorted(range(K), key=lambda j: int(topi[b, j])):
+            # the reference's weights are an [n, 1] fp32 tensor: the product and the sum are fp32
+            final[b] = (final[b].float() + topw[b, k].float() * outs[b, k].float()).to(dtype)
+    return final
+
+
 class OracleDecoder:
     """The reference's ``ForCausalLM`` forward (``model.py:412-424``) over a paged KV pool.
 
@@ -201,21 +227,9 @@ class OracleDecoder:
                         w[p + "down_proj.weight"])
 
     def route(self, i, flat):
-        """Router of ``Qwen3MoeSparseMoe.forward`` (``qwen3_moe_model.py:45-53``): softmax over the
-        expert logits, top-k, optional renormalisation.  The reference's GPU decode runs under CUDA
-        autocast, where softmax computes and returns fp32 from the bf16 logits; that is the
-        semantics stated here for every dtype.  Ties among equal probabilities go to the lower
-        expert index."""
-        w, p = self.w, f"model.layers.{i}.mlp."
-        logits = F.linear(flat, w[p + "gate.weight"])
-        probs = F.softmax(logits.float(), dim=-1)
-        k = self.cfg["num_experts_per_tok"]
-        # stable descending order: equal probabilities keep ascending expert index
-        order = torch.sort(probs, dim=-1, descending=True, stable=True)
-        topw, topi = order.values[:, :k], order.indices[:, :k]
-        if self.cfg.get("norm_topk_prob", True):
-            topw = topw / topw.sum(dim=-1, keepdim=True)
-        return topw, topi
+        """Router of ``Qwen3MoeSparseMoe.forward`` (``qwen3_moe_model.py:45-53``) for layer i."""
+        logits = F.linear(flat, self.w[f"model.layers.{i}.mlp.gate.weight"])
+        return moe_route(logits, self.cfg["num_experts_per_tok"], self.cfg.get("norm_topk_prob", True))
 
     def moe(self, i, x):
         """``Qwen3MoeSparseMoe.forward`` (``qwen3_moe_model.py:39-65``): each expert's
