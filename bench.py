@@ -54,9 +54,10 @@ def parse_args(argv=None):
     ap.add_argument("--layers", type=int, default=None, help="override layer count (debug only; invalid bench)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pdl", type=int, default=1)
-    ap.add_argument("--case", default=None, choices=["kernels"],
+    ap.add_argument("--case", default=None, choices=["kernels", "moe"],
                     help="kernels: small profiling case (2 layers of the workload's dims), each kernel kind "
-                         "launched a few times; prints per-kernel timings only")
+                         "launched a few times; prints per-kernel timings only.  moe: the sparse-MoE decode "
+                         "workload (Qwen3-30B-A3B arch, batch 32, prompt 4096, greedy), 1 GPU")
     return ap.parse_args(argv)
 
 
@@ -412,10 +413,89 @@ def run_kernel_case(args) -> None:
     assert N.device_status(clear=True) == 0
 
 
+def run_moe_case(args) -> None:
+    """Sparse-MoE decode (Qwen3-30B-A3B architecture: 48 layers, hidden 2048, 32/4 heads, 128
+    experts of 768, top-8), batch 32, 4096-token prompts with seeded synthetic K/V, greedy.  Same
+    timing rules as the headline line (CUDA events over K graph replays, inputs far above L2)."""
+    from llm_pytorch_inference_b200 import _native as N
+    from llm_pytorch_inference_b200.configs import get_config
+    from llm_pytorch_inference_b200.engine import DecodeEngine
+    from llm_pytorch_inference_b200.weights import canonical_state_dict
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    N.set_pdl(bool(args.pdl))
+    cfg = get_config("qwen3-30b-a3b")
+    B, prompt = 32, 4096
+    W, K = args.warmup, args.steps
+    sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev, stacked_experts=True)
+    eng = DecodeEngine(cfg, sd, max_batch=B, max_model_len=prompt + 2 * (W + 2 * K) + 32, device=dev)
+    del sd
+    order = list(range(eng.kv.num_blocks))
+    random.Random(0).shuffle(order)
+    from collections import deque
+
+    eng.kv.free_blocks = deque(order)
+    g = torch.Generator().manual_seed(1)
+    for s in range(B):
+        eng.add_sequence(s, torch.randint(0, cfg["vocab_size"], (prompt,), generator=g).tolist())
+        eng.append_first_token(s, int(torch.randint(0, cfg["vocab_size"], (1,), generator=g)))
+    eng.prefill_synthetic(seed=0)
+    eng.set_sampling(0.0, -1, 1.0)
+    eng.prepare_first_step()
+    r = eng.runner
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(W):
+        eng.step()
+    torch.cuda.synchronize(dev)
+    metas = torch.stack([eng.plan_step(eng.runner.tokens_host[:B].tolist()) for _ in range(K)]).to(dev)
+    clocks = ClockSampler(0)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(K):
+        r.meta.copy_(metas[k], non_blocking=True)
+        r.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / K
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(K):
+        eng.step()
+    e3.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e2.elapsed_time(e3) / K
+    clk = clocks.stop()
+    # algorithmic bytes: attention/norm/lm_head weights, the experts the step's routing touched in
+    # each layer (counted on the device after the last step), K/V of every attended token
+    act = int(r.active[0])
+    L, H, E, Im = cfg["num_hidden_layers"], cfg["hidden_size"], cfg["num_experts"], cfg["moe_intermediate_size"]
+    w = r.w
+    dense = sum(t.numel() * 2 for t in [w.final_norm, w.lm_head, *w.wqkv, *w.wo, *w.ln1, *w.ln2, *w.qn, *w.kn,
+                                          *w.router])
+    expert_bytes = 3 * Im * H * 2
+    kv_token = L * r.Hkv * r.D * 2 * 2
+    step_bytes = dense + L * act * expert_bytes + int(r.ctx.cpu().sum()) * kv_token
+    pk = peaks()
+    line = {"case": "moe", "metric": "decode tokens/s Qwen3-30B-A3B-arch bf16 batch 32 ctx 4096 greedy",
+            "value": round(B / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 4), "steps": K,
+            "warmup": W, "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tokens/s"},
+            "active_experts_last_layer": act, "step_bytes": step_bytes,
+            "step_roofline": {"achieved_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),
+                              "frac": round(step_bytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)},
+            "launches_per_step": r.launches_per_step(), "clocks": clk,
+            "device_status": N.device_status(clear=True)}
+    print(json.dumps(line), flush=True)
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
     if args.case == "kernels":
         run_kernel_case(args)
+        return 0
+    if args.case == "moe":
+        run_moe_case(args)
         return 0
     rank, world, local = (0, 1, 0)
     if args.impl == "reference":
