@@ -472,6 +472,10 @@ int gemm_launch(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
   const int64_t total = tiles * kblocks;
   int64_t ctas = splitk_ctas(m, sms);
   if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
+  // The merge path's last-arriving CTA sums a tile's contributors one after another: a GEMM with
+  // so few tiles that each would have more than 16 contributors (a 128-expert router: 32) is
+  // spread over 8 CTAs per tile instead.
+  if (!partials_out(epilogue) && ctas > tiles * 16) ctas = tiles * 8;
   const int grid = static_cast<int>(total < ctas ? total : ctas);
   // Partials at the head, tile counters at the tail of the workspace: calls of any shape
   // that share one buffer then use nested suffixes of the same (self-zeroing) counter area,

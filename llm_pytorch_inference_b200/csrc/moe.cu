@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
 // ---------------------------------------------------------------------------- routing
 // One CTA: every warp routes tokens (softmax, top-k, renormalisation), then the dispatch order is
 // built from per-expert counts (thread e lists expert e's tokens in ascending token order).
-__global__ void __launch_bounds__(256) moe_route_kernel(const __nv_bfloat16* __restrict__ logits, int rows, int E,
+__global__ void __launch_bounds__(1024) moe_route_kernel(const __nv_bfloat16* __restrict__ logits, int rows, int E,
                                                         int K, int norm, int32_t* topk_ids, float* topk_w,
                                                         int32_t* pair_row, int32_t* row_token, int32_t* expert_off,
                                                         int32_t* active) {
@@ -306,17 +306,43 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const __nv_bfloat16* __r
   __syncthreads();
   for (int i = threadIdx.x; i < rows * K; i += blockDim.x) atomicAdd(&s_cnt[s_ids[i]], 1);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int off = 0, n = 0;
-    for (int e = 0; e < E; ++e) {
-      s_off[e] = off;
-      expert_off[e] = off;
-      if (s_cnt[e] > 0) active[1 + n++] = e;
-      off += s_cnt[e];
+  if (warp == 0) {
+    // Prefix sums of the counts (row offsets) and of the active flags (active list), PER experts
+    // per lane, then across the warp.
+    int cnt[PER], run = 0, act = 0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = lane * PER + i;
+      cnt[i] = e < E ? s_cnt[e] : 0;
+      run += cnt[i];
+      act += cnt[i] > 0;
     }
-    s_off[E] = off;
-    expert_off[E] = off;
-    active[0] = n;
+    int incl = run, iact = act;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      const int va = __shfl_up_sync(0xffffffffu, iact, o);
+      if (lane >= o) {
+        incl += v;
+        iact += va;
+      }
+    }
+    int off = incl - run, n = iact - act;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = lane * PER + i;
+      if (e < E) {
+        s_off[e] = off;
+        expert_off[e] = off;
+        if (cnt[i] > 0) active[1 + n++] = e;
+        off += cnt[i];
+      }
+    }
+    if (lane == 31) {
+      s_off[E] = incl;
+      expert_off[E] = incl;
+      active[0] = iact;
+    }
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -421,7 +447,9 @@ extern "C" int mvb_moe_route(const void* logits, int64_t rows, int64_t num_exper
               "mvb_moe_route: rows %lld (<= %d), experts %lld (<= %d), top_k %lld (<= %d)", (long long)rows, kMaxRows,
               (long long)num_experts, kMaxExperts, (long long)top_k, kMaxTopK);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  return launch("moe_route", moe_route_kernel, dim3(1), dim3(256), 0, st, (const __nv_bfloat16*)logits, (int)rows,
+  // one warp per row, up to 32 warps
+  const int threads = static_cast<int>((rows < 32 ? rows : 32) * 32 < 256 ? 256 : (rows < 32 ? rows : 32) * 32);
+  return launch("moe_route", moe_route_kernel, dim3(1), dim3(threads), 0, st, (const __nv_bfloat16*)logits, (int)rows,
                 (int)num_experts, (int)top_k, norm_topk, topk_ids, topk_w, pair_row, row_token, expert_off, active);
 }
 

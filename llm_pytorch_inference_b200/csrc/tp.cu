@@ -182,7 +182,8 @@ extern "C" int mvb_tp_gemm_bf16(mvb_tp_comm* comm, const void* x, int64_t ldx, c
     MVB_REQUIRE(sms > 0, "mvb_tp_gemm_bf16: no device");
     const int64_t tiles = epilogue == MVB_EPI_SWIGLU_PARTIALS ? (n / 2 + 63) / 64 : (n + kSplitBM - 1) / kSplitBM;
     const int64_t total = tiles * (k / kSplitBK);
-    const int64_t ctas = push ? splitk_push_ctas(m, n, k, sms, nr) : splitk_ctas(m, sms);
+    int64_t ctas = push ? splitk_push_ctas(m, n, k, sms, nr) : splitk_ctas(m, sms);
+    if (gather && ctas > tiles * 16) ctas = tiles * 8;  // the merge path's contributor cap (gemm_launch)
     tp.arrive_total = static_cast<uint32_t>(total < ctas ? total : ctas);   // the GEMM's grid
   }
   int grid = 0;
