@@ -147,7 +147,8 @@ int mvb_sample(int64_t* out, float* probs_out, const void* logits, int64_t rows,
  * (model.py:174-178), apply_rotary_pos_emb (:184) and Attention._write_kv_cache
  * (:226-243; model_cuda.py:182-207).  qkv: [B, (Hq + 2*Hkv) * D] bf16 (row stride
  * qkv_stride) -- the fused q|k|v projection.  q_norm_w / k_norm_w: [D] bf16 or NULL
- * (no QK-norm).  cos/sin: the model's bf16 tables [table_len, D].  positions: int32 [B]
+ * (no QK-norm); plus_one != 0 scales by (1 + w) in fp32 as Gemma's RMSNorm does
+ * (models/gemma3_model.py:14-25).  cos/sin: the model's bf16 tables [table_len, D].  positions: int32 [B]
  * (token position = slot index = cached tokens, engine.py:316/326).  block_tables:
  * int32 [B, max_blocks].  kv_cache: the KVCacheManager tensor
  * [L, 2, num_blocks, block_size, Hkv, D] bf16 (kv_cache.py:24-29).
@@ -158,7 +159,7 @@ int mvb_qk_norm_rope_kv_write(void* q_out, void* kv_cache, const void* qkv, int6
                               int64_t table_len, const int32_t* positions, const int32_t* block_tables,
                               int64_t max_blocks, int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
                               int64_t head_dim, int64_t num_layers, int64_t layer, int64_t num_blocks,
-                              int64_t block_size, float eps, mvb_stream_t stream);
+                              int64_t block_size, float eps, int plus_one, mvb_stream_t stream);
 
 /* The same, with the fused q|k|v projection still in split-K partial form: `gemm_workspace`
  * is the workspace of the preceding mvb_gemm_bf16(MVB_EPI_PARTIALS) call of shape
@@ -169,7 +170,7 @@ int mvb_qk_norm_rope_kv_write_gemm(void* q_out, void* kv_cache, const void* gemm
                                    int64_t table_len, const int32_t* positions, const int32_t* block_tables,
                                    int64_t max_blocks, int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
                                    int64_t head_dim, int64_t num_layers, int64_t layer, int64_t num_blocks,
-                                   int64_t block_size, float eps, mvb_stream_t stream);
+                                   int64_t block_size, float eps, int plus_one, mvb_stream_t stream);
 
 /* ---- paged attention decode --------------------------------------------------
  * Replaces Attention._read_kv_cache_batch + GQA expand + SDPA for one query token per
@@ -186,6 +187,20 @@ int mvb_paged_attention_decode(void* out, int64_t out_stride, const void* q, int
                                int64_t head_dim, int64_t num_layers, int64_t layer, int64_t num_blocks,
                                int64_t block_size, float scale, void* workspace, int64_t workspace_bytes,
                                mvb_stream_t stream);
+
+/* mvb_paged_attention_decode with the Gemma attention variants (Gemma-2/3 decode,
+ * models/gemma3_model.py:169-195 for head_dim 256 and the query_pre_attn_scalar scale).
+ * softcap > 0: every scaled score s becomes softcap * tanh(s / softcap) before the softmax
+ * (Gemma-2's attention logit soft-capping; 0 = off).  window > 0: sequence b attends to its
+ * newest `window` keys only, positions [ctx_b - window, ctx_b) (a sliding-window layer;
+ * 0 = all keys).  head_dim 128 or 256.  mvb_paged_attention_decode is this call with
+ * softcap = 0 and window = 0. */
+int mvb_paged_attention_decode_ex(void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                                  const void* kv_cache, const int32_t* block_tables, int64_t max_blocks,
+                                  const int32_t* ctx_lens, int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+                                  int64_t head_dim, int64_t num_layers, int64_t layer, int64_t num_blocks,
+                                  int64_t block_size, float scale, float softcap, int64_t window, void* workspace,
+                                  int64_t workspace_bytes, mvb_stream_t stream);
 
 /* Allocation-free paged attention (no counterpart in the reference).  Same arguments and
  * result as mvb_paged_attention_decode, minus the workspace: the split-KV scratch is a
@@ -239,6 +254,26 @@ int mvb_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, const void* 
  * MVB_EPI_SWIGLU writes.  Requires inter % 4 == 0, out_stride % 4 == 0, 8-byte aligned out. */
 int mvb_swiglu_gemm(void* out, int64_t out_stride, const void* gemm_workspace, int64_t rows, int64_t inter,
                     int64_t gemm_k, mvb_stream_t stream);
+
+/* mvb_swiglu_gemm with the activation chosen: MVB_ACT_SILU (SwiGLU) or MVB_ACT_GELU_TANH
+ * (GeGLU: Gemma's down(gelu_tanh(gate(x)) * up(x)), models/gemma3_model.py:104-105;
+ * mlp_kernel.cu:17-36 with GELU): out = bf16(bf16(act(bf16(gate))) * bf16(up)). */
+int mvb_gated_gemm(void* out, int64_t out_stride, const void* gemm_workspace, int64_t rows, int64_t inter,
+                   int64_t gemm_k, int act, mvb_stream_t stream);
+
+/* Post-norm, residual add and RMSNorm of a linear layer's output still in split-K partial
+ * form (Gemma's sandwich norms, models/gemma3_model.py:270-283): y = bf16(sum of partials),
+ * residual = bf16(residual + RMSNorm(y; post_weight)), out = RMSNorm(residual; weight), both
+ * norms in the model's form (plus_one: T((x * r) * (1 + w)), models/gemma3_model.py:21-25).
+ * Same arguments and requirements as mvb_fused_add_rmsnorm_gemm plus post_weight [hidden]. */
+int mvb_fused_norm_add_rmsnorm_gemm(void* out, void* residual, const void* gemm_workspace, int64_t rows,
+                                    int64_t hidden, int64_t gemm_k, const void* post_weight, const void* weight,
+                                    float eps, int plus_one, mvb_stream_t stream);
+
+/* Logit soft-capping in place (Gemma-2's final_logit_softcapping): x = T(T(tanh(T(x / cap))) * cap),
+ * the rounding sequence of `logits / cap; tanh; * cap` in the logits' dtype.  n elements of
+ * dtype MVB_BF16 or MVB_F32; cap > 0. */
+int mvb_softcap(void* x, int64_t n, float cap, int dtype, mvb_stream_t stream);
 
 /* ---- sparse mixture of experts (Qwen3-MoE) ---------------------------------------------
  * Replace Qwen3MoeSparseMoe.forward (models/qwen3_moe_model.py:39-65) for one decode step.

@@ -34,6 +34,7 @@ SIGNATURES: dict[str, tuple] = {
     "mvb_rmsnorm": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _f32, _i32, _i32, _i32, _vp]),
     "mvb_fused_add_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _i32, _i32, _i32, _vp]),
     "mvb_fused_add_rmsnorm_gemm": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _f32, _i32, _vp]),
+    "mvb_fused_norm_add_rmsnorm_gemm": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _f32, _i32, _vp]),
     "mvb_rotary_pos_emb": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _vp]),
     "mvb_activation": (_i32, [_vp, _vp, _i64, _i32, _i32, _vp]),
     "mvb_gated_activation": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _vp]),
@@ -45,17 +46,21 @@ SIGNATURES: dict[str, tuple] = {
     "mvb_softmax_multinomial_sample": (_i32, [_vp, _vp, _i64, _i64, _f32, _u64, _u64, _i32, _vp]),
     "mvb_sample": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _u64, _u64, _vp, _i32, _vp]),
     "mvb_qk_norm_rope_kv_write": (_i32, [_vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64,
-                                         _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp]),
+                                         _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _vp]),
     "mvb_qk_norm_rope_kv_write_gemm": (_i32, [_vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64,
-                                              _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp]),
+                                              _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _vp]),
     "mvb_paged_attention_workspace_bytes": (_i64, [_i64, _i64, _i64, _i32]),
     "mvb_paged_attention_decode": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64,
                                           _i64, _i64, _i64, _i64, _f32, _vp, _i64, _vp]),
+    "mvb_paged_attention_decode_ex": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64,
+                                             _i64, _i64, _i64, _i64, _f32, _f32, _i64, _vp, _i64, _vp]),
     "mvb_paged_attention_decode_noalloc": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64,
                                                   _i64, _i64, _i64, _i64, _i64, _f32, _vp]),
     "mvb_gemm_workspace_bytes": (_i64, [_i64, _i64, _i64, _i32]),
     "mvb_gemm_bf16": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i32, _vp, _i64, _vp, _i64, _vp]),
     "mvb_swiglu_gemm": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _vp]),
+    "mvb_gated_gemm": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _i32, _vp]),
+    "mvb_softcap": (_i32, [_vp, _i64, _f32, _i32, _vp]),
     "mvb_moe_route": (_i32, [_vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mvb_moe_gather": (_i32, [_vp, _vp, _i64, _vp, _i64, _vp]),
     "mvb_moe_gemm_bf16": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _vp, _vp]),

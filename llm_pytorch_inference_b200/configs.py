@@ -108,7 +108,68 @@ ARCHS: dict[str, dict] = {
     },
 }
 
+_GEMMA_COMMON = {
+    "hidden_act": "gelu_new",                  # tanh GELU (loader.py:149-157 maps gelu_pytorch_tanh)
+    "hidden_activation": "gelu_pytorch_tanh",
+    "rms_norm_eps": 1e-6,
+    "head_dim": 256,
+    "query_pre_attn_scalar": 256,
+    "_rms_norm_plus_one": True,               # (1 + w) norms, zero-initialised
+    "_has_feedforward_layernorms": True,      # pre/post feed-forward norms (loader.py:143-147)
+}
+
+# Gemma-2-9B architecture: alternating 4096-token sliding-window / global layers (even layers
+# slide), attention logits soft-capped at 50 and final logits at 30, no QK-norm, one RoPE theta.
+ARCHS["gemma2-9b"] = {
+    **_GEMMA_COMMON,
+    "model_type": "gemma2",
+    "num_hidden_layers": 42,
+    "hidden_size": 3584,
+    "num_attention_heads": 16,
+    "num_key_value_heads": 8,
+    "intermediate_size": 14336,
+    "vocab_size": 256000,
+    "rope_theta": 10000.0,
+    "max_position_embeddings": 8192,
+    "sliding_window": 4096,
+    "attn_logit_softcapping": 50.0,
+    "final_logit_softcapping": 30.0,
+    "tie_word_embeddings": True,
+    "_qk_norm": False,
+}
+# Small Gemma-2 shapes for the parity tests: 4 layers (2 sliding, 2 global), a 32-token window,
+# an untied lm_head (tied random weights mostly echo the input token).
+ARCHS["gemma2-tiny"] = {
+    **ARCHS["gemma2-9b"],
+    "num_hidden_layers": 4,
+    "hidden_size": 512,
+    "num_attention_heads": 4,
+    "num_key_value_heads": 2,
+    "intermediate_size": 1024,
+    "vocab_size": 4096,
+    "sliding_window": 32,
+    "tie_word_embeddings": False,
+}
+# The reference's own Gemma 3 model (models/gemma3_model.py, model_type gemma3_text): QK-norm,
+# local/global RoPE theta every `sliding_window_pattern` layers, no soft-capping and no window.
+ARCHS["gemma3-tiny"] = {
+    **_GEMMA_COMMON,
+    "model_type": "gemma3_text",
+    "num_hidden_layers": 2,
+    "hidden_size": 512,
+    "num_attention_heads": 4,
+    "num_key_value_heads": 2,
+    "intermediate_size": 1024,
+    "vocab_size": 4096,
+    "rope_theta": 1000000.0,
+    "rope_local_base_freq": 10000.0,
+    "sliding_window_pattern": 2,
+    "max_position_embeddings": 32768,
+    "tie_word_embeddings": False,
+    "_qk_norm": True,
+}
 ARCHS["qwen3-8b-2l"] = {**ARCHS["qwen3-8b"], "num_hidden_layers": 2}
+ARCHS["gemma2-9b-2l"] = {**ARCHS["gemma2-9b"], "num_hidden_layers": 2}
 
 
 def get_config(name: str, **overrides) -> dict:
@@ -118,6 +179,39 @@ def get_config(name: str, **overrides) -> dict:
     cfg = copy.deepcopy(ARCHS[name])
     cfg.update(overrides)
     return cfg
+
+
+def is_gemma(cfg: dict) -> bool:
+    """Gemma-family decoder: (1 + w) sandwich norms, GeGLU, sqrt(hidden) embedding scale."""
+    return cfg.get("model_type") in ("gemma2", "gemma3_text")
+
+
+def layer_rope_theta(cfg: dict, i: int) -> float:
+    """RoPE base of layer i: Gemma 3 uses the global theta on every ``sliding_window_pattern``-th
+    layer and the local one elsewhere (models/gemma3_model.py:307-320); the rest use one theta."""
+    if cfg.get("model_type") == "gemma3_text":
+        pattern = cfg.get("sliding_window_pattern", 6)
+        glob = i % pattern == pattern - 1
+        return float(cfg.get("rope_theta", 1000000.0)) if glob else float(cfg.get("rope_local_base_freq", 10000.0))
+    return float(cfg.get("rope_theta", 10000.0))
+
+
+def layer_window(cfg: dict, i: int) -> int:
+    """Sliding window of layer i (0 = global): Gemma-2 alternates, even layers sliding."""
+    if cfg.get("model_type") == "gemma2" and cfg.get("sliding_window"):
+        return int(cfg["sliding_window"]) if i % 2 == 0 else 0
+    return 0
+
+
+def embed_scale(cfg: dict) -> float:
+    """Embedding multiplier: sqrt(hidden) for Gemma (models/gemma3_model.py:295-299), else 1.  The
+    reference keeps it in a buffer that ``model.to(dtype)`` casts, so a bf16 model multiplies by
+    bf16(sqrt(hidden)); the value returned here is that bf16-rounded one."""
+    if not is_gemma(cfg):
+        return 1.0
+    import torch
+
+    return float(torch.tensor(float(cfg["hidden_size"]) ** 0.5).to(torch.bfloat16))
 
 
 def head_dim(cfg: dict) -> int:

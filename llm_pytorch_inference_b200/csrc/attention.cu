@@ -2,26 +2,34 @@
 // reference's paged pool through the block table.
 //
 // Replaces, for decode, Attention._read_kv_cache_batch + GQA expand + SDPA with a
-// padding mask (models/model.py:191-221; models/model_cuda.py:145-177):
-//   out[b, h] = softmax(q[b, h] . K[b, 0:ctx_b]^T * scale) V[b, 0:ctx_b]
-// Pool layout (engine/kv_cache.py:24-29): [L, 2, num_blocks, block_size=16, Hkv, D].
+// padding mask (models/model.py:191-221; models/model_cuda.py:145-177;
+// models/gemma3_model.py:169-195 for head_dim 256):
+//   out[b, h] = softmax(q[b, h] . K[b, lo_b:ctx_b]^T * scale) V[b, lo_b:ctx_b]
+// with lo_b = 0, or ctx_b - window under a sliding window of the newest `window` keys, and
+// optionally soft-capped scores s -> cap * tanh(s / cap) (Gemma-2's attention softcap).
+// Pool layout (engine/kv_cache.py:24-29): [L, 2, num_blocks, block_size=16, Hkv, D], D 128 or 256.
 //
-// Work split: the (sequence, block) pairs of the whole batch are laid end to end and
-// divided evenly over the persistent CTAs (split-KV across the GPU).  A sequence that
-// spans several CTAs is merged by the last CTA to finish it, combining the partial
-// (max, sum, output) triples in CTA order, so results are deterministic.
+// Work split: the KV heads are cut into head groups of HKV heads (all of them at D = 128; two
+// at D = 256, whose blocks are twice as large).  The (sequence x head group, block) pairs of the
+// whole batch are laid end to end and divided evenly over the persistent CTAs (split-KV across
+// the GPU).  A sequence that spans several CTAs is merged by the last CTA to finish it,
+// combining the partial (max, sum, output) triples in CTA order, so results are deterministic.
 //
-// CTA = 8 consumer warps + 1 producer warp.  The producer streams each block's K and V
-// (all heads) through TMA into a 128-byte-swizzled image of 128-byte lines (head_dim split into
-// two halves of 64).  With >= 4 KV heads per GPU it issues 4 copies per block, one per (K|V,
-// half), image [kv][half][head][token][64]; with fewer heads (tensor-parallel shards, blocks of
-// 4-8 KB) the per-copy cost dominates and one 5-D copy per block is issued instead, image
-// [kv][token][head, half][64].  Consumer warp (h, w) serves KV head h -- its GROUP query heads are the rows of a
-// 16-row mma tile -- and with W = 8 / Hkv warps per head takes every W-th block of the CTA's
-// range, so a GPU holding few KV heads (tensor parallelism) still runs 8 warps per SM; the W
-// partial softmax states of a head are combined in shared memory at each sequence boundary.
-// QK^T and PV use mma.sync m16n8k16 (bf16 in, fp32 accumulate); softmax is the online
-// (running max / running sum) form in the exp2 domain.
+// CTA = 8 consumer warps (4 at D = 256) + 1 producer warp.  The producer streams each block's
+// K and V (the head group's heads) through TMA into a 128-byte-swizzled image of 128-byte lines
+// (head_dim split into parts of 64).  It issues one copy per (K|V, part), image
+// [kv][part][head][token][64]; only for D = 128 blocks of one or two heads (tensor-parallel
+// shards, 4-8 KB) is the per-copy cost worth saving, with one 5-D copy per block, image
+// [kv][token][head, part][64].  Consumer warp (h, w) serves KV head h -- its GROUP query heads
+// are the columns of an m16n8 tile -- and with W = 8 / HKV (4 / HKV) warps per head takes every
+// W-th block of the CTA's range, so a GPU holding few KV heads (tensor parallelism) still runs
+// every consumer warp; the W partial softmax states of a head are combined in shared memory at
+// each sequence boundary.
+// Both products run transposed on mma.sync m16n8k16 (bf16 in, fp32 accumulate) so that the
+// query heads fill the n = 8 side instead of wasting 16-row tiles: S^T = K Q^T (tokens x heads),
+// then O^T = V^T P^T (dims x heads), P^T reaching the B operand through one 8x8 transpose
+// (movmatrix) per 8 tokens.  The softmax is the online (running max / running sum) form in the
+// exp2 domain, kept per head column.
 #include <mutex>
 
 #include "common.cuh"
@@ -30,9 +38,8 @@
 namespace mvb {
 namespace {
 
-constexpr int D = 128;       // head_dim handled by this kernel
 constexpr int BS = 16;       // tokens per block (the reference's block_size)
-constexpr int HALF_BYTES_PER_HEAD = BS * 64 * 2;  // 2 KB: 16 tokens x 64 dims
+constexpr int HALF_BYTES_PER_HEAD = BS * 64 * 2;  // 2 KB: 16 tokens x 64 dims (one part of a head)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kMergeC = 32;  // contributors merged per round
 
@@ -45,15 +52,23 @@ struct AttnArgs {
   int64_t max_blocks;
   const int32_t* ctx_lens;
   int batch;
-  int num_q_heads;
+  int nhg;           // head groups per sequence (KV heads / HKV)
+  int window;        // > 0: attend to the newest `window` keys only
   int64_t layer;
   int64_t num_blocks;
   float scale_log2;  // scale * log2(e)
-  float* partial_o;  // [2*G][Hq][D]
-  float2* partial_ml;  // [2*G][Hq]  (running max in log2 units, running sum)
-  int* counters;     // [batch]
+  float cap_scale;   // softcap > 0: scale / softcap
+  float cap_log2;    // softcap * log2(e); 0 = no soft-capping
+  float* partial_o;  // [2*G][GROUP*HKV][D]
+  float2* partial_ml;  // [2*G][GROUP*HKV]  (running max in log2 units, running sum)
+  int* counters;     // [batch * nhg]
   unsigned* err;
 };
+
+// First block of a sequence of ctx keys that the window reaches.
+__device__ __forceinline__ int window_first_block(int ctx, int window) {
+  return (window > 0 && ctx > window) ? (ctx - window) / 16 : 0;
+}
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -72,6 +87,11 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
       "{%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Transpose of an 8x8 b16 matrix held as the warp's standard fragment (thread T: row T / 4,
+// columns 2 (T % 4) and 2 (T % 4) + 1).
+__device__ __forceinline__ void movmatrix_trans(uint32_t a, uint32_t& d) {
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
 }
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -96,25 +116,36 @@ __device__ __forceinline__ void head_bar(int h) {
   asm volatile("bar.sync %0, %1;" ::"r"(2 + h), "n"(W * 32) : "memory");
 }
 
-// Consumer warps per KV head: 8 consumer warps per CTA in total, as long as the merge's
-// per-thread share (GROUP * D / (W * 32) outputs) stays whole.
-template <int GROUP, int HKV>
+// Consumer warps per CTA: 8 at D = 128.  At D = 256 the bandwidth is set by the bytes the
+// stages keep in flight, and 4 warps (2 per KV head of a two-head group) let the stage count be
+// a multiple of 2 instead of 4: 6 stages of 32 KB instead of 4.
+template <int D>
+__host__ __device__ constexpr int attn_consumer_warps() {
+  return D == 128 ? 8 : 4;
+}
+
+// Consumer warps per KV head: all consumer warps of the CTA shared by its HKV heads, as long as
+// the merge's per-thread share (GROUP * D / (W * 32) outputs) stays whole.
+template <int GROUP, int HKV, int D>
 __host__ __device__ constexpr int attn_wph() {
-  return (8 / HKV) < GROUP * (D / 32) ? (8 / HKV) : GROUP * (D / 32);
+  return (attn_consumer_warps<D>() / HKV) < GROUP * (D / 32) ? (attn_consumer_warps<D>() / HKV) : GROUP * (D / 32);
 }
 
-// One TMA copy per block (small blocks) or one per (K|V, half) (large blocks).
-__host__ __device__ constexpr bool attn_one_copy_for(int hkv) { return hkv <= 2; }
-template <int HKV>
+// One TMA copy per block (D = 128 blocks of <= 2 heads) or one per (K|V, part).  Several small
+// copies keep more requests in flight than one large multi-dimensional box: at D = 256 the split
+// form streams at 6.7 TB/s where one 32 KB box per stage reached 3.9 TB/s.
+__host__ __device__ constexpr bool attn_one_copy_for(int hkv, int d) { return d == 128 && hkv <= 2; }
+template <int HKV, int D>
 __host__ __device__ constexpr bool attn_one_copy() {
-  return attn_one_copy_for(HKV);
+  return attn_one_copy_for(HKV, D);
 }
 
-// 128-byte line of (kv, half, head, token) in a stage image of either layout.
-template <int HKV>
-__device__ __forceinline__ int attn_line(int kv, int half, int h, int tok) {
-  if constexpr (attn_one_copy<HKV>()) return (kv * BS + tok) * (2 * HKV) + 2 * h + half;
-  return ((kv * 2 + half) * HKV + h) * BS + tok;
+// 128-byte line of (kv, part, head, token) in a stage image of either layout.
+template <int HKV, int D>
+__device__ __forceinline__ int attn_line(int kv, int part, int h, int tok) {
+  constexpr int NP = D / 64;
+  if constexpr (attn_one_copy<HKV, D>()) return (kv * BS + tok) * (NP * HKV) + h * NP + part;
+  return ((kv * NP + part) * HKV + h) * BS + tok;
 }
 
 // Floats of the split-sequence merge scratch: (m, l) pairs, weights, per-head max and
@@ -125,16 +156,18 @@ __host__ __device__ constexpr int attn_merge_floats() {
 }
 
 // Shared memory of the per-head combine: every consumer warp's (m, l, o) for its GROUP rows.
-template <int GROUP, int HKV>
+template <int GROUP, int HKV, int D>
 __host__ __device__ constexpr int attn_combine_bytes() {
-  return attn_wph<GROUP, HKV>() > 1 ? HKV * attn_wph<GROUP, HKV>() * GROUP * (D + 2) * 4 : 0;
+  return attn_wph<GROUP, HKV, D>() > 1 ? HKV * attn_wph<GROUP, HKV, D>() * GROUP * (D + 2) * 4 : 0;
 }
 
-template <int GROUP, int HKV, int STAGES>
-__global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
+template <int GROUP, int HKV, int STAGES, int D>
+__global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, 1)
     paged_attention_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs a) {
-  constexpr int STAGE_BYTES = 4 * HKV * HALF_BYTES_PER_HEAD;  // K lo, K hi, V lo, V hi
-  constexpr int W = attn_wph<GROUP, HKV>();                  // consumer warps per KV head
+  constexpr int NP = D / 64;                                      // 64-dim parts of a head
+  constexpr int STAGE_BYTES = 2 * NP * HKV * HALF_BYTES_PER_HEAD;  // K and V parts of HKV heads
+  constexpr int W = attn_wph<GROUP, HKV, D>();                    // consumer warps per KV head
+  constexpr int HQ = GROUP * HKV;                                 // query heads of a head group
   constexpr int NCW = HKV * W;                                // consumer warps
   static_assert(STAGES % W == 0, "a stage must always serve the same warp of each head");
   extern __shared__ uint8_t smem_raw[];
@@ -149,6 +182,7 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
       reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(cu + a.batch + 1) + 15) & ~uintptr_t(15));
   float* combine_smem = reinterpret_cast<float*>(
       (reinterpret_cast<uintptr_t>(merge_smem + attn_merge_floats<GROUP, HKV>()) + 15) & ~uintptr_t(15));
+  const int nv = a.batch * a.nhg;  // virtual sequences: (sequence, head group), head groups adjacent
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -166,33 +200,35 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
   // the prologue and the TMA copies of every other block run before the grid-dependency wait; the
   // producer waits before issuing a sequence's last block, the consumers before reading q.
   if (threadIdx.x == 0) pdl_launch_dependents();
-  // Per-sequence block counts -> prefix sums (warp 0, 32 sequences at a time).
+  // Per-(sequence, head group) block counts -> prefix sums (warp 0, 32 at a time).
   if (warp == 0) {
     int carry = 0;
-    for (int base = 0; base < a.batch; base += 32) {
-      const int b = base + lane;
+    for (int base = 0; base < nv; base += 32) {
+      const int v = base + lane;
       int n = 0;
-      if (b < a.batch) {
-        const int ctx = a.ctx_lens[b];
+      if (v < nv) {
+        const int ctx = a.ctx_lens[v / a.nhg];
         n = ctx > 0 ? (ctx + BS - 1) / BS : 0;
         if (n > a.max_blocks) {
           report(a.err, kDevBadPosition);
           n = static_cast<int>(a.max_blocks);
         }
+        n -= window_first_block(ctx, a.window);
+        if (n < 0) n = 0;
       }
       int incl = n;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += v;
+        const int x = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += x;
       }
-      if (b < a.batch) cu[b + 1] = carry + incl;
+      if (v < nv) cu[v + 1] = carry + incl;
       carry += __shfl_sync(0xffffffffu, incl, 31);
     }
     if (lane == 0) cu[0] = 0;
   }
   __syncthreads();
-  const int64_t total = cu[a.batch];
+  const int64_t total = cu[nv];
   // Effective grid: never more CTAs than blocks, so every CTA in [0, G) owns at least
   // one block and the contributor count of a sequence is exact.
   const int G = static_cast<int>(total < gridDim.x ? total : gridDim.x);
@@ -200,8 +236,8 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
   const int64_t g_begin = range_start(blockIdx.x, total, G);
   const int64_t g_end = range_start(blockIdx.x + 1, total, G);
   int b0 = 0;
-  {  // first sequence with cu[b+1] > g_begin
-    int lo = 0, hi = a.batch - 1;
+  {  // first virtual sequence with cu[v+1] > g_begin
+    int lo = 0, hi = nv - 1;
     while (lo < hi) {
       const int mid = (lo + hi) >> 1;
       if (cu[mid + 1] > g_begin) hi = mid; else lo = mid + 1;
@@ -226,9 +262,10 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
         int blk = 0, last = 0;
         if (g < g_end) {
           while (g >= cu[b_lane + 1]) ++b_lane;
-          const int j = static_cast<int>(g - cu[b_lane]);
+          const int bs = b_lane / a.nhg;
+          const int j = static_cast<int>(g - cu[b_lane]) + window_first_block(a.ctx_lens[bs], a.window);
           last = g == cu[b_lane + 1] - 1;
-          blk = a.block_tables[static_cast<int64_t>(b_lane) * a.max_blocks + j];
+          blk = a.block_tables[static_cast<int64_t>(bs) * a.max_blocks + j];
           if (blk < 0 || blk >= P) {
             report(a.err, kDevBadBlock);
             blk = 0;  // stay in bounds; the sequence's output is not trusted (status word set)
@@ -238,6 +275,7 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
         for (int i = 0; i < n; ++i) {
           const int bi = __shfl_sync(0xffffffffu, blk, i);
           const int li = __shfl_sync(0xffffffffu, last, i);
+          const int hg = __shfl_sync(0xffffffffu, b_lane, i) % a.nhg;  // head group of the block
           int good = 1;
           if (lane == 0) {
             if (li && !waited) {  // this block holds the token the previous kernel wrote
@@ -252,14 +290,14 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
             } else {
               mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
               uint8_t* st = smem + s * STAGE_BYTES;
-              if constexpr (attn_one_copy<HKV>()) {
-                tma_load_5d(st, &tm, &full[s], 0, 0, 0, bi, static_cast<int>(a.layer * 2), pol);
+              if constexpr (attn_one_copy<HKV, D>()) {
+                tma_load_5d(st, &tm, &full[s], 0, hg * HKV * NP, 0, bi, static_cast<int>(a.layer * 2), pol);
               } else {
                 for (int kv = 0; kv < 2; ++kv) {
                   const int row = static_cast<int>((a.layer * 2 + kv) * P + bi);
-                  for (int half = 0; half < 2; ++half)
-                    tma_load_4d(st + (kv * 2 + half) * HKV * HALF_BYTES_PER_HEAD, &tm, &full[s], half * 64, 0, 0,
-                                row, pol);
+                  for (int part = 0; part < NP; ++part)
+                    tma_load_4d(st + (kv * NP + part) * HKV * HALF_BYTES_PER_HEAD, &tm, &full[s], part * 64, 0,
+                                hg * HKV, row, pol);
                 }
               }
               issued = it + 1;
@@ -279,20 +317,23 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
     const int g = lane >> 2, t = lane & 3;
     const bool row_valid = g < GROUP;
     const uint32_t sbase = smem_u32(smem);
-    int b = b0;
+    int vs = b0;  // virtual sequence: (sequence b, head group hg)
     int64_t gpos = g_begin;
     while (gpos < g_end) {
-      while (gpos >= cu[b + 1]) ++b;
-      const int64_t seq_lo = cu[b], seq_hi = cu[b + 1];
+      while (gpos >= cu[vs + 1]) ++vs;
+      const int b = vs / a.nhg, hg = vs - (vs / a.nhg) * a.nhg;
+      const int64_t seq_lo = cu[vs], seq_hi = cu[vs + 1];
       const int64_t seg_end = min(g_end, seq_hi);
       const int ctx = a.ctx_lens[b];
-      const int hq0 = h * GROUP;
+      const int blk0 = window_first_block(ctx, a.window);
+      const int lo_tok = a.window > 0 ? ctx - a.window : 0;
+      const int hq0 = (hg * HKV + h) * GROUP;  // first query head of KV head h (global index)
       // Q fragments (rows = the GROUP query heads of this KV head; rows >= GROUP are zero).
-      uint32_t qa[8][2];
+      uint32_t qa[D / 16][2];
       {
         const __nv_bfloat16* qp = a.q + static_cast<int64_t>(b) * a.q_stride + static_cast<int64_t>(hq0 + g) * D;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
+        for (int kk = 0; kk < D / 16; ++kk) {
           if (row_valid) {
             qa[kk][0] = *reinterpret_cast<const uint32_t*>(qp + kk * 16 + 2 * t);
             qa[kk][1] = *reinterpret_cast<const uint32_t*>(qp + kk * 16 + 8 + 2 * t);
@@ -301,10 +342,14 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
           }
         }
       }
-      float o[16][4];
+      // O^T accumulators, one m16n8 tile per 16 dims: o[mt] = {O^T[dim 16mt+g][head 2t],
+      // [16mt+g][2t+1], [16mt+g+8][2t], [16mt+g+8][2t+1]} (heads = this KV head's GROUP query heads).
+      float o[D / 16][4];
 #pragma unroll
-      for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
-      float m_run = -INFINITY, l_run = 0.0f;
+      for (int n = 0; n < D / 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+      // Softmax state of this thread's two query heads 2t and 2t+1 (the S^T / O^T columns): running
+      // max (log2 units, equal across the g lanes) and this thread's share of the denominator.
+      float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;
 
       // This warp's blocks of the segment: iterations it = gg - g_begin with it % W == w.
       const int64_t off = (gpos - g_begin) % W;
@@ -315,138 +360,216 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
         // A wait that gives up has reported the timeout and raised the abort flag; the warp
         // carries on (on stale data) so that every warp still meets every barrier below.
         mbar_wait(&full[s], ph, abort_flag, a.err);
-        const int j = static_cast<int>(gg - seq_lo);  // block index within the sequence
+        const int j = blk0 + static_cast<int>(gg - seq_lo);  // block index within the sequence
         // 128-byte lines of the stage image (attn_line); 16-byte chunks are XOR-swizzled with the
         // line index mod 8 (the stage is 1024-byte aligned).
         const uint32_t stage_base = sbase + s * STAGE_BYTES;
-        // S = Q K^T for 16 tokens: two n-tiles of 8 tokens.
-        float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        // S^T = K Q^T for 16 tokens (m = 16 tokens, n = 8 query heads, k = 16 dims per step), in four
+        // independent accumulator chains.  A = K from a plain ldmatrix.x4: matrices (tokens 0-7 |
+        // 8-15) x (dims 0-7 | 8-15) in the fragment order a0 a1 a2 a3; B = Q^T is the q fragment.
+        float sacc[4][4];
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const int half = kk >> 2;
+        for (int c = 0; c < 4; ++c) sacc[c][0] = sacc[c][1] = sacc[c][2] = sacc[c][3] = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int part = kk >> 2;
           const int mi = lane >> 3;
-          const int tok = (mi >> 1) * 8 + (lane & 7);
-          const int chunk = (kk & 3) * 2 + (mi & 1);
-          const int line = attn_line<HKV>(0, half, h, tok);
+          const int tok = (mi & 1) * 8 + (lane & 7);
+          const int chunk = (kk & 3) * 2 + (mi >> 1);
+          const int line = attn_line<HKV, D>(0, part, h, tok);
           const uint32_t addr = stage_base + line * 128 + ((chunk ^ (line & 7)) << 4);
           uint32_t k0, k1, k2, k3;
           ldsm_x4(addr, k0, k1, k2, k3);
-          mma_bf16_16816(sacc[0], qa[kk][0], 0u, qa[kk][1], 0u, k0, k1);
-          mma_bf16_16816(sacc[1], qa[kk][0], 0u, qa[kk][1], 0u, k2, k3);
+          mma_bf16_16816(sacc[kk & 3], k0, k1, k2, k3, qa[kk][0], qa[kk][1]);
         }
-        // Scale into the log2 domain and mask tokens past the context.
-        float sv[4];
+        // x = S^T[token g][head 2t], [g][2t+1], [g+8][2t], [g+8][2t+1]: scaled (and soft-capped)
+        // into the log2 domain; tokens past the context or before the window masked.
         const int tok0 = j * BS;
+        const int tka = tok0 + g, tkb = tok0 + g + 8;
+        const bool ka = tka < ctx && tka >= lo_tok, kb = tkb < ctx && tkb >= lo_tok;
+        float x[4];
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const int tok = tok0 + nt * 8 + 2 * t + c;
-            sv[nt * 2 + c] = tok < ctx ? sacc[nt][c] * a.scale_log2 : -INFINITY;
-          }
+        for (int c = 0; c < 4; ++c) {
+          const float raw = sacc[0][c] + sacc[1][c] + sacc[2][c] + sacc[3][c];
+          const float sc = a.cap_log2 > 0.0f ? a.cap_log2 * tanhf(raw * a.cap_scale) : raw * a.scale_log2;
+          x[c] = (c < 2 ? ka : kb) ? sc : -INFINITY;
         }
-        float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float m_new = fmaxf(m_run, mx);
-        const float alpha = exp2f(m_run - m_new);
+        // Column (head) maxima over the 16 tokens: this thread's two rows, then the 8 g lanes.
+        float mxa = fmaxf(x[0], x[2]), mxb = fmaxf(x[1], x[3]);
+#pragma unroll
+        for (int o_ = 4; o_ < 32; o_ <<= 1) {
+          mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, o_));
+          mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, o_));
+        }
+        const float mna = fmaxf(m_a, mxa), mnb = fmaxf(m_b, mxb);
+        const float alpha_a = exp2f(m_a - mna), alpha_b = exp2f(m_b - mnb);
         float p[4];
+        p[0] = exp2f(x[0] - mna);
+        p[1] = exp2f(x[1] - mnb);
+        p[2] = exp2f(x[2] - mna);
+        p[3] = exp2f(x[3] - mnb);
+        l_a = l_a * alpha_a + (p[0] + p[2]);
+        l_b = l_b * alpha_b + (p[1] + p[3]);
+        m_a = mna;
+        m_b = mnb;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) p[i] = exp2f(sv[i] - m_new);
-        l_run = l_run * alpha + (p[0] + p[1] + p[2] + p[3]);
-        m_run = m_new;
-#pragma unroll
-        for (int n = 0; n < 16; ++n) {
-          o[n][0] *= alpha;
-          o[n][1] *= alpha;
+        for (int n = 0; n < D / 16; ++n) {
+          o[n][0] *= alpha_a;
+          o[n][1] *= alpha_b;
+          o[n][2] *= alpha_a;
+          o[n][3] *= alpha_b;
         }
-        const uint32_t pa0 = pack_bf16(p[0], p[1]);  // row g, tokens 2t, 2t+1
-        const uint32_t pa2 = pack_bf16(p[2], p[3]);  // row g, tokens 8+2t, 9+2t
-        // O += P V: 16 n-tiles of 8 dims, two per transposed ldmatrix.
+        // O^T += V^T P^T (m = 16 dims, n = 8 heads, k = 16 tokens).  The P^T values of this thread
+        // are [token g | g+8][heads 2t, 2t+1], the layout of an 8x8 fragment; one transpose per 8
+        // tokens turns them into the B fragment P[head g][tokens 2t, 2t+1 | 8+2t, 9+2t].
+        uint32_t pb0, pb1;
+        movmatrix_trans(pack_bf16(p[0], p[1]), pb0);
+        movmatrix_trans(pack_bf16(p[2], p[3]), pb1);
+        // A = V^T, one transposed ldmatrix.x4 per 16 dims: matrices (dims 0-7 | 8-15) x
+        // (tokens 0-7 | 8-15) in the fragment order a0 a1 a2 a3.
 #pragma unroll
-        for (int np = 0; np < 8; ++np) {
-          const int half = np >> 2;
+        for (int mt = 0; mt < D / 16; ++mt) {
+          const int part = mt >> 2;
           const int mi = lane >> 3;
-          const int tok = (mi & 1) * 8 + (lane & 7);
-          const int chunk = (np & 3) * 2 + (mi >> 1);
-          const int line = attn_line<HKV>(1, half, h, tok);
+          const int tok = (mi >> 1) * 8 + (lane & 7);
+          const int chunk = (mt & 3) * 2 + (mi & 1);
+          const int line = attn_line<HKV, D>(1, part, h, tok);
           const uint32_t addr = stage_base + line * 128 + ((chunk ^ (line & 7)) << 4);
           uint32_t v0, v1, v2, v3;
           ldsm_x4_t(addr, v0, v1, v2, v3);
-          mma_bf16_16816(o[2 * np], pa0, 0u, pa2, 0u, v0, v1);
-          mma_bf16_16816(o[2 * np + 1], pa0, 0u, pa2, 0u, v2, v3);
+          mma_bf16_16816(o[mt], v0, v1, v2, v3, pb0, pb1);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
       }
 
-      // Segment done: finish this warp's GROUP heads.
-      l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
-      l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
-      if constexpr (W > 1) {
-        // Combine the W warps of head h: each publishes (m, l, o) of its rows; warp w == 0 merges
-        // them (a warp that had no block in the segment contributes m = -inf, l = 0, o = 0).
-        float* mine = combine_smem + static_cast<int64_t>(warp) * GROUP * (D + 2);
-        if (row_valid) {
-          float* r = mine + g * (D + 2);
-          if (t == 0) {
-            r[0] = m_run;
-            r[1] = l_run;
-          }
+      // Segment done: finish this warp's GROUP heads.  This thread's O^T columns are heads 2t and
+      // 2t+1; their denominators are summed over the 8 g lanes.
 #pragma unroll
-          for (int n = 0; n < 16; ++n) *reinterpret_cast<float2*>(r + 2 + n * 8 + 2 * t) = make_float2(o[n][0], o[n][1]);
+      for (int o_ = 4; o_ < 32; o_ <<= 1) {
+        l_a += __shfl_xor_sync(0xffffffffu, l_a, o_);
+        l_b += __shfl_xor_sync(0xffffffffu, l_b, o_);
+      }
+      const int ha = 2 * t, hb = 2 * t + 1;
+      const bool va = ha < GROUP, vb = hb < GROUP;
+      float ma = m_a, la = l_a, mb = m_b, lb = l_b;
+      if constexpr (W > 1) {
+        // Combine the W warps of head h: each publishes (m, l, o) of its GROUP heads as rows of
+        // D + 2 floats; warp w == 0 merges them (a warp that had no block in the segment
+        // contributes m = -inf, l = 0, o = 0).
+        constexpr int RS = D + 2;
+        float* mine = combine_smem + static_cast<int64_t>(warp) * GROUP * RS;
+        if (g == 0) {
+          if (va) {
+            mine[ha * RS] = ma;
+            mine[ha * RS + 1] = la;
+          }
+          if (vb) {
+            mine[hb * RS] = mb;
+            mine[hb * RS + 1] = lb;
+          }
+        }
+#pragma unroll
+        for (int n = 0; n < D / 16; ++n) {
+          const int d0 = 16 * n + g;
+          if (va) {
+            mine[ha * RS + 2 + d0] = o[n][0];
+            mine[ha * RS + 2 + d0 + 8] = o[n][2];
+          }
+          if (vb) {
+            mine[hb * RS + 2 + d0] = o[n][1];
+            mine[hb * RS + 2 + d0 + 8] = o[n][3];
+          }
         }
         head_bar<W>(h);
-        if (w == 0 && row_valid) {
-          const float* base = combine_smem + static_cast<int64_t>(h * W) * GROUP * (D + 2) + g * (D + 2);
-          float M = -INFINITY;
-#pragma unroll
-          for (int ww = 0; ww < W; ++ww) M = fmaxf(M, base[ww * GROUP * (D + 2)]);
-          float L = 0.0f;
-#pragma unroll
-          for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = 0.0f;
+        if (w == 0) {
+          const float* base = combine_smem + static_cast<int64_t>(h * W) * GROUP * RS;
+          float Ma = -INFINITY, Mb = -INFINITY;
 #pragma unroll
           for (int ww = 0; ww < W; ++ww) {
-            const float* r = base + ww * GROUP * (D + 2);
-            const float sc = r[0] == -INFINITY ? 0.0f : exp2f(r[0] - M);
-            L += r[1] * sc;
+            if (va) Ma = fmaxf(Ma, base[ww * GROUP * RS + ha * RS]);
+            if (vb) Mb = fmaxf(Mb, base[ww * GROUP * RS + hb * RS]);
+          }
+          float La = 0.0f, Lb = 0.0f;
 #pragma unroll
-            for (int n = 0; n < 16; ++n) {
-              const float2 v = *reinterpret_cast<const float2*>(r + 2 + n * 8 + 2 * t);
-              o[n][0] += v.x * sc;
-              o[n][1] += v.y * sc;
+          for (int n = 0; n < D / 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+#pragma unroll
+          for (int ww = 0; ww < W; ++ww) {
+            const float* r = base + ww * GROUP * RS;
+            if (va) {
+              const float sc = r[ha * RS] == -INFINITY ? 0.0f : exp2f(r[ha * RS] - Ma);
+              La += r[ha * RS + 1] * sc;
+#pragma unroll
+              for (int n = 0; n < D / 16; ++n) {
+                o[n][0] += r[ha * RS + 2 + 16 * n + g] * sc;
+                o[n][2] += r[ha * RS + 2 + 16 * n + g + 8] * sc;
+              }
+            }
+            if (vb) {
+              const float sc = r[hb * RS] == -INFINITY ? 0.0f : exp2f(r[hb * RS] - Mb);
+              Lb += r[hb * RS + 1] * sc;
+#pragma unroll
+              for (int n = 0; n < D / 16; ++n) {
+                o[n][1] += r[hb * RS + 2 + 16 * n + g] * sc;
+                o[n][3] += r[hb * RS + 2 + 16 * n + g + 8] * sc;
+              }
             }
           }
-          m_run = M;
-          l_run = L;
+          ma = Ma;
+          la = La;
+          mb = Mb;
+          lb = Lb;
         }
         head_bar<W>(h);  // the area is rewritten by the next segment
       }
       const bool whole = (gpos == seq_lo) && (seg_end == seq_hi);
-      const int hq = hq0 + g;
       if (whole) {
-        if (w == 0 && row_valid) {
-          const float inv = 1.0f / l_run;
-          __nv_bfloat16* op = a.out + static_cast<int64_t>(b) * a.out_stride + static_cast<int64_t>(hq) * D;
+        if (w == 0) {
+          __nv_bfloat16* op = a.out + static_cast<int64_t>(b) * a.out_stride + static_cast<int64_t>(hq0) * D;
+          const float ia = va ? 1.0f / la : 0.0f, ib = vb ? 1.0f / lb : 0.0f;
 #pragma unroll
-          for (int n = 0; n < 16; ++n)
-            *reinterpret_cast<__nv_bfloat162*>(op + n * 8 + 2 * t) = __floats2bfloat162_rn(o[n][0] * inv, o[n][1] * inv);
+          for (int n = 0; n < D / 16; ++n) {
+            const int d0 = 16 * n + g;
+            if (va) {
+              op[ha * D + d0] = __float2bfloat16_rn(o[n][0] * ia);
+              op[ha * D + d0 + 8] = __float2bfloat16_rn(o[n][2] * ia);
+            }
+            if (vb) {
+              op[hb * D + d0] = __float2bfloat16_rn(o[n][1] * ib);
+              op[hb * D + d0 + 8] = __float2bfloat16_rn(o[n][3] * ib);
+            }
+          }
         }
       } else {
         const int slot = (g_begin >= seq_lo) ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
-        if (w == 0 && row_valid) {
-          const float inv = 1.0f / l_run;
-          float* po = a.partial_o + (static_cast<int64_t>(slot) * a.num_q_heads + hq) * D;
+        if (w == 0) {
+          // query heads h*GROUP + ha / hb within the head group
+          float* po = a.partial_o + (static_cast<int64_t>(slot) * HQ + h * GROUP) * D;
+          const float ia = va ? 1.0f / la : 0.0f, ib = vb ? 1.0f / lb : 0.0f;
 #pragma unroll
-          for (int n = 0; n < 16; ++n) __stcg(reinterpret_cast<float2*>(po + n * 8 + 2 * t), make_float2(o[n][0] * inv, o[n][1] * inv));
-          if (t == 0) __stcg(a.partial_ml + static_cast<int64_t>(slot) * a.num_q_heads + hq, make_float2(m_run, l_run));
+          for (int n = 0; n < D / 16; ++n) {
+            const int d0 = 16 * n + g;
+            if (va) {
+              __stcg(po + ha * D + d0, o[n][0] * ia);
+              __stcg(po + ha * D + d0 + 8, o[n][2] * ia);
+            }
+            if (vb) {
+              __stcg(po + hb * D + d0, o[n][1] * ib);
+              __stcg(po + hb * D + d0 + 8, o[n][3] * ib);
+            }
+          }
+          float2* pml = a.partial_ml + static_cast<int64_t>(slot) * HQ + h * GROUP;
+          if (g == 0) {
+            if (va) __stcg(pml + ha, make_float2(ma, la));
+            if (vb) __stcg(pml + hb, make_float2(mb, lb));
+          }
         }
         __threadfence();
         consumer_bar<NCW>();
         if (threadIdx.x == 0) {
           const int c_first = cta_of(seq_lo, total, G);
           const int c_last = cta_of(seq_hi - 1, total, G);
-          const int old = atomicAdd(&a.counters[b], 1);
+          const int old = atomicAdd(&a.counters[vs], 1);
           const int last = old == c_last - c_first;
           if (last) __threadfence();
           *last_flag = last;
@@ -457,7 +580,6 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
           // denominator, normalised weights staged in shared memory, then every thread accumulates
           // its GROUP*4 outputs.  Up to kMergeC contributors (the usual case) take two rounds of
           // global loads; more are merged kMergeC at a time.
-          constexpr int HQ = GROUP * HKV;
           constexpr int NT = NCW * 32;
           constexpr int PER = HQ * D / NT;
           static_assert(PER * NT == HQ * D, "merge share must be whole");
@@ -540,10 +662,10 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
               }
             }
           }
+          __nv_bfloat16* og = a.out + static_cast<int64_t>(b) * a.out_stride + static_cast<int64_t>(hg) * HQ * D;
 #pragma unroll
-          for (int k = 0; k < PER; ++k)
-            a.out[static_cast<int64_t>(b) * a.out_stride + threadIdx.x + k * NT] = __float2bfloat16_rn(acc[k]);
-          if (threadIdx.x == 0) a.counters[b] = 0;
+          for (int k = 0; k < PER; ++k) og[threadIdx.x + k * NT] = __float2bfloat16_rn(acc[k]);
+          if (threadIdx.x == 0) a.counters[vs] = 0;
         }
         consumer_bar<NCW>();
       }
@@ -558,14 +680,20 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV>() + 1) * 32, 1)
   }
 }
 
+// Most (sequence, head group) pairs one launch takes: their block prefix sums live in shared
+// memory, so at D = 256 (32 KB stages) the bound is lower to leave room for a sixth stage.
+template <int D>
+constexpr int attn_max_pairs() {
+  return D == 128 ? 4096 : 1024;
+}
 constexpr int kAttnMaxBatch = 4096;
 
 // Shared memory other than the stages, at the largest batch: barriers, the block prefix sums,
 // the merge scratch, the per-head combine and the 1 KB alignment slack.
-template <int GROUP, int HKV>
+template <int GROUP, int HKV, int D>
 constexpr int attn_fixed_smem() {
-  return 2 * 8 * 32 + 16 + 4 * (kAttnMaxBatch + 1) + 16 + 4 * attn_merge_floats<GROUP, HKV>() + 16 +
-         attn_combine_bytes<GROUP, HKV>() + 1024;
+  return 2 * 8 * 32 + 16 + 4 * (attn_max_pairs<D>() + 1) + 16 + 4 * attn_merge_floats<GROUP, HKV>() + 16 +
+         attn_combine_bytes<GROUP, HKV, D>() + 1024;
 }
 
 // As many stages as fit in 227 KB next to the rest (at most 24), rounded down to a multiple of
@@ -573,76 +701,78 @@ constexpr int attn_fixed_smem() {
 // STAGES % W == 0 a stage only ever serves the same warp of each head, in iteration order.  A warp
 // therefore never waits on a stage more than one phase ahead of its last use, where the
 // mbarrier's parity would alias a stale phase as complete.
-template <int GROUP, int HKV>
+template <int GROUP, int HKV, int D>
 constexpr int attn_stages() {
-  constexpr int stage = 4 * HKV * HALF_BYTES_PER_HEAD;
-  constexpr int W = attn_wph<GROUP, HKV>();
-  constexpr int n = (227 * 1024 - attn_fixed_smem<GROUP, HKV>()) / stage;
+  constexpr int stage = 2 * (D / 64) * HKV * HALF_BYTES_PER_HEAD;
+  constexpr int W = attn_wph<GROUP, HKV, D>();
+  constexpr int n = (227 * 1024 - attn_fixed_smem<GROUP, HKV, D>()) / stage;
   constexpr int c = n > 24 ? 24 : n;
   return c / W * W;
 }
 
-template <int GROUP, int HKV>
-size_t attn_smem(int batch) {
-  return static_cast<size_t>(attn_stages<GROUP, HKV>()) * 4 * HKV * HALF_BYTES_PER_HEAD + 2 * 8 * 32 + 16 +
-         4 * (batch + 1) + 16 + 4 * attn_merge_floats<GROUP, HKV>() + 16 + attn_combine_bytes<GROUP, HKV>() + 1024;
+template <int GROUP, int HKV, int D>
+size_t attn_smem(int nv) {
+  return static_cast<size_t>(attn_stages<GROUP, HKV, D>()) * 2 * (D / 64) * HKV * HALF_BYTES_PER_HEAD + 2 * 8 * 32 +
+         16 + 4 * (nv + 1) + 16 + 4 * attn_merge_floats<GROUP, HKV>() + 16 + attn_combine_bytes<GROUP, HKV, D>() +
+         1024;
 }
 
-template <int GROUP, int HKV>
+template <int GROUP, int HKV, int D>
 int launch_attn(const CUtensorMap& tm, const AttnArgs& a, int grid, cudaStream_t st) {
-  constexpr int S = attn_stages<GROUP, HKV>();
+  constexpr int S = attn_stages<GROUP, HKV, D>();
   static_assert(S >= 2, "two stages must fit");
-  constexpr int NT = (HKV * attn_wph<GROUP, HKV>() + 1) * 32;
-  const size_t smem = attn_smem<GROUP, HKV>(a.batch);
+  constexpr int NT = (HKV * attn_wph<GROUP, HKV, D>() + 1) * 32;
+  const size_t smem = attn_smem<GROUP, HKV, D>(a.batch * a.nhg);
   // Raise the kernel's dynamic-smem limit once per device (to the 4096-sequence maximum),
   // so no attribute call happens while a stream is being captured into a graph.
   static unsigned long long done_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !(done_mask & (1ull << dev))) {
-    MVB_TRY(set_smem(paged_attention_kernel<GROUP, HKV, S>, attn_smem<GROUP, HKV>(kAttnMaxBatch),
+    MVB_TRY(set_smem(paged_attention_kernel<GROUP, HKV, S, D>, attn_smem<GROUP, HKV, D>(attn_max_pairs<D>()),
                      "paged_attention: smem attribute"));
     if (dev < 64) done_mask |= 1ull << dev;
   }
-  return launch("paged_attention_decode", paged_attention_kernel<GROUP, HKV, S>, dim3(grid), dim3(NT), smem, st, tm,
-                a);
+  return launch("paged_attention_decode", paged_attention_kernel<GROUP, HKV, S, D>, dim3(grid), dim3(NT), smem, st,
+                tm, a);
 }
 
-template <int HKV>
+template <int HKV, int D>
 int dispatch_group(int group, const CUtensorMap& tm, const AttnArgs& a, int grid, cudaStream_t st) {
   switch (group) {
-    case 1: return launch_attn<1, HKV>(tm, a, grid, st);
-    case 2: return launch_attn<2, HKV>(tm, a, grid, st);
-    case 4: return launch_attn<4, HKV>(tm, a, grid, st);
-    case 8: return launch_attn<8, HKV>(tm, a, grid, st);
+    case 1: return launch_attn<1, HKV, D>(tm, a, grid, st);
+    case 2: return launch_attn<2, HKV, D>(tm, a, grid, st);
+    case 4: return launch_attn<4, HKV, D>(tm, a, grid, st);
+    case 8: return launch_attn<8, HKV, D>(tm, a, grid, st);
     default: return fail(MVB_ERR_UNSUPPORTED, "paged attention: %d query heads per KV head", group);
   }
 }
 
 int64_t attn_counters_bytes(int64_t batch) { return (batch * 4 + 255) / 256 * 256; }
 
-// Encodes the KV-pool tensor map.  Tries the one-box-per-half view (dims ordered
-// {dim, token, head, block}, which permutes the token/head strides) and falls back
-// to one box per head in natural stride order; both give the same shared-memory image.
-// The KV-pool tensor map.  One-copy layout: dims (innermost first) 64 dims of a half, 2*Hkv
-// (head, half) lines of 128 bytes, 16 tokens, blocks, layer*2 + kv; one box = K and V of one
-// block, all heads.  Split layout: dims 128 dims, 16 tokens, Hkv heads (strides permuted so a
-// box lands as [head][token][64]), rows = (layer*2 + kv)*P + block; one box = one half of K or V.
-int encode_kv_map(CUtensorMap* m, const void* kv, int64_t hkv, int64_t num_blocks, int64_t num_layers,
-                  bool one_copy) {
-  const uint64_t block_bytes = static_cast<uint64_t>(BS * hkv * D * 2);
+// KV heads one CTA stage holds (a head group): all of them at D = 128, two (or one) at D = 256.
+int64_t attn_heads_per_group(int64_t hkv, int64_t d) { return d == 128 ? hkv : (hkv % 2 == 0 ? 2 : 1); }
+
+// The KV-pool tensor map.  One-copy layout: dims (innermost first) 64 dims of a part, NP*Hkv
+// (head, part) lines of 128 bytes, 16 tokens, blocks, layer*2 + kv; one box = K and V of one
+// block for the hs heads of a head group.  Split layout (D = 128): dims 128 dims, 16 tokens,
+// Hkv heads (strides permuted so a box lands as [head][token][64]), rows = (layer*2 + kv)*P +
+// block; one box = one part of K or V of hs heads.
+int encode_kv_map(CUtensorMap* m, const void* kv, int64_t hkv, int64_t d, int64_t hs, int64_t num_blocks,
+                  int64_t num_layers, bool one_copy) {
+  const uint64_t block_bytes = static_cast<uint64_t>(BS * hkv * d * 2);
   if (one_copy) {
-    const uint64_t dims[5] = {64, static_cast<uint64_t>(2 * hkv), static_cast<uint64_t>(BS),
+    const uint64_t dims[5] = {64, static_cast<uint64_t>(d / 64 * hkv), static_cast<uint64_t>(BS),
                               static_cast<uint64_t>(num_blocks), static_cast<uint64_t>(2 * num_layers)};
-    const uint64_t strides[4] = {128, static_cast<uint64_t>(hkv * D * 2), block_bytes,
+    const uint64_t strides[4] = {128, static_cast<uint64_t>(hkv * d * 2), block_bytes,
                                  block_bytes * static_cast<uint64_t>(num_blocks)};
-    const uint32_t box[5] = {64, static_cast<uint32_t>(2 * hkv), BS, 1, 2};
+    const uint32_t box[5] = {64, static_cast<uint32_t>(d / 64 * hs), BS, 1, 2};
     return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, kv, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   }
-  const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(BS), static_cast<uint64_t>(hkv),
+  const uint64_t dims[4] = {static_cast<uint64_t>(d), static_cast<uint64_t>(BS), static_cast<uint64_t>(hkv),
                             static_cast<uint64_t>(2 * num_layers * num_blocks)};
-  const uint64_t strides[3] = {static_cast<uint64_t>(hkv * D * 2), static_cast<uint64_t>(D * 2), block_bytes};
-  const uint32_t box[4] = {64, BS, static_cast<uint32_t>(hkv), 1};
+  const uint64_t strides[3] = {static_cast<uint64_t>(hkv * d * 2), static_cast<uint64_t>(d * 2), block_bytes};
+  const uint32_t box[4] = {64, BS, static_cast<uint32_t>(hs), 1};
   return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, kv, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
@@ -655,22 +785,33 @@ extern "C" int64_t mvb_paged_attention_workspace_bytes(int64_t batch, int64_t nu
                                                        int device) {
   int sms = mvb_num_sms(device);
   if (sms <= 0) sms = 148;
-  return attn_counters_bytes(batch) + 2LL * sms * num_q_heads * 8 + 2LL * sms * num_q_heads * head_dim * 4 + 256;
+  // counters: one per (sequence, head group); head groups <= KV heads <= query heads
+  return attn_counters_bytes(batch * num_q_heads) + 2LL * sms * num_q_heads * 8 +
+         2LL * sms * num_q_heads * head_dim * 4 + 256;
 }
 
-extern "C" int mvb_paged_attention_decode(void* out, int64_t out_stride, const void* q, int64_t q_stride,
-                                          const void* kv_cache, const int32_t* block_tables, int64_t max_blocks,
-                                          const int32_t* ctx_lens, int64_t batch, int64_t num_q_heads,
-                                          int64_t num_kv_heads, int64_t head_dim, int64_t num_layers, int64_t layer,
-                                          int64_t num_blocks, int64_t block_size, float scale, void* workspace,
-                                          int64_t workspace_bytes, mvb_stream_t stream) {
+extern "C" int mvb_paged_attention_decode_ex(void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                                             const void* kv_cache, const int32_t* block_tables, int64_t max_blocks,
+                                             const int32_t* ctx_lens, int64_t batch, int64_t num_q_heads,
+                                             int64_t num_kv_heads, int64_t head_dim, int64_t num_layers,
+                                             int64_t layer, int64_t num_blocks, int64_t block_size, float scale,
+                                             float softcap, int64_t window, void* workspace,
+                                             int64_t workspace_bytes, mvb_stream_t stream) {
   MVB_REQUIRE(out && q && kv_cache && block_tables && ctx_lens && workspace,
               "mvb_paged_attention_decode: null pointer");
-  MVB_REQUIRE(head_dim == D, "mvb_paged_attention_decode: head_dim %lld (this build: 128)", (long long)head_dim);
+  MVB_REQUIRE(head_dim == 128 || head_dim == 256, "mvb_paged_attention_decode: head_dim %lld (128 or 256)",
+              (long long)head_dim);
   MVB_REQUIRE(block_size == BS, "mvb_paged_attention_decode: block_size %lld (this build: 16)",
               (long long)block_size);
-  MVB_REQUIRE(batch >= 0 && batch <= 4096, "mvb_paged_attention_decode: batch %lld", (long long)batch);
   MVB_REQUIRE(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0, "mvb_paged_attention_decode: head counts");
+  MVB_REQUIRE(softcap >= 0.0f && window >= 0 && window <= (1LL << 30),
+              "mvb_paged_attention_decode: softcap and window must be >= 0");
+  const int64_t hs = attn_heads_per_group(num_kv_heads, head_dim);
+  const int64_t nhg = num_kv_heads / hs;
+  const int max_pairs = head_dim == 128 ? attn_max_pairs<128>() : attn_max_pairs<256>();
+  MVB_REQUIRE(batch >= 0 && batch * nhg <= max_pairs,
+              "mvb_paged_attention_decode: batch %lld x %lld head groups > %d", (long long)batch, (long long)nhg,
+              max_pairs);
   MVB_REQUIRE(layer >= 0 && layer < num_layers && num_blocks > 0 && max_blocks > 0,
               "mvb_paged_attention_decode: cache geometry");
   MVB_REQUIRE(q_stride % 2 == 0 && aligned(q, 4) && out_stride % 2 == 0 && aligned(out, 4),
@@ -680,16 +821,17 @@ extern "C" int mvb_paged_attention_decode(void* out, int64_t out_stride, const v
   const int64_t group = num_q_heads / num_kv_heads;
   const int sms = current_sm_count();
   MVB_REQUIRE(sms > 0, "mvb_paged_attention_decode: no device");
-  // Partials at the head, per-sequence counters at the tail (nested suffixes across calls
-  // of different batch sizes sharing one buffer; the kernel leaves them zero).
+  // Partials at the head, per-(sequence, head group) counters at the tail (nested suffixes
+  // across calls of different batch sizes sharing one buffer; the kernel leaves them zero).
   const int64_t ws_end = workspace_bytes / 256 * 256;
-  const int64_t cbytes = attn_counters_bytes(batch);
-  const int64_t need = cbytes + 2LL * sms * num_q_heads * 8 + 2LL * sms * num_q_heads * D * 4;
+  const int64_t cbytes = attn_counters_bytes(batch * nhg);
+  const int64_t need = cbytes + 2LL * sms * num_q_heads * 8 + 2LL * sms * num_q_heads * head_dim * 4;
   MVB_REQUIRE(ws_end >= need, "mvb_paged_attention_decode: workspace %lld < %lld", (long long)workspace_bytes,
               (long long)need);
 
   CUtensorMap tm;
-  MVB_TRY(encode_kv_map(&tm, kv_cache, num_kv_heads, num_blocks, num_layers, attn_one_copy_for(static_cast<int>(num_kv_heads))));
+  MVB_TRY(encode_kv_map(&tm, kv_cache, num_kv_heads, head_dim, hs, num_blocks, num_layers,
+                        attn_one_copy_for(static_cast<int>(hs), static_cast<int>(head_dim))));
 
   AttnArgs a;
   a.out = static_cast<__nv_bfloat16*>(out);
@@ -700,10 +842,13 @@ extern "C" int mvb_paged_attention_decode(void* out, int64_t out_stride, const v
   a.max_blocks = max_blocks;
   a.ctx_lens = ctx_lens;
   a.batch = static_cast<int>(batch);
-  a.num_q_heads = static_cast<int>(num_q_heads);
+  a.nhg = static_cast<int>(nhg);
+  a.window = static_cast<int>(window);
   a.layer = layer;
   a.num_blocks = num_blocks;
   a.scale_log2 = scale * kLog2e;
+  a.cap_scale = softcap > 0.0f ? scale / softcap : 0.0f;
+  a.cap_log2 = softcap > 0.0f ? softcap * kLog2e : 0.0f;
   char* ws = static_cast<char*>(workspace);
   a.partial_ml = reinterpret_cast<float2*>(ws);
   a.partial_o = reinterpret_cast<float*>(ws + 2LL * sms * num_q_heads * 8);
@@ -714,13 +859,29 @@ extern "C" int mvb_paged_attention_decode(void* out, int64_t out_stride, const v
   // with an empty range exit after the prologue.
   const int grid = sms;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int g = static_cast<int>(group);
+  if (head_dim == 256) {
+    if (hs == 2) return dispatch_group<2, 256>(g, tm, a, grid, st);
+    return dispatch_group<1, 256>(g, tm, a, grid, st);
+  }
   switch (num_kv_heads) {
-    case 1: return dispatch_group<1>(static_cast<int>(group), tm, a, grid, st);
-    case 2: return dispatch_group<2>(static_cast<int>(group), tm, a, grid, st);
-    case 4: return dispatch_group<4>(static_cast<int>(group), tm, a, grid, st);
-    case 8: return dispatch_group<8>(static_cast<int>(group), tm, a, grid, st);
+    case 1: return dispatch_group<1, 128>(g, tm, a, grid, st);
+    case 2: return dispatch_group<2, 128>(g, tm, a, grid, st);
+    case 4: return dispatch_group<4, 128>(g, tm, a, grid, st);
+    case 8: return dispatch_group<8, 128>(g, tm, a, grid, st);
     default: return fail(MVB_ERR_UNSUPPORTED, "mvb_paged_attention_decode: %lld KV heads", (long long)num_kv_heads);
   }
+}
+
+extern "C" int mvb_paged_attention_decode(void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                                          const void* kv_cache, const int32_t* block_tables, int64_t max_blocks,
+                                          const int32_t* ctx_lens, int64_t batch, int64_t num_q_heads,
+                                          int64_t num_kv_heads, int64_t head_dim, int64_t num_layers, int64_t layer,
+                                          int64_t num_blocks, int64_t block_size, float scale, void* workspace,
+                                          int64_t workspace_bytes, mvb_stream_t stream) {
+  return mvb_paged_attention_decode_ex(out, out_stride, q, q_stride, kv_cache, block_tables, max_blocks, ctx_lens,
+                                       batch, num_q_heads, num_kv_heads, head_dim, num_layers, layer, num_blocks,
+                                       block_size, scale, 0.0f, 0, workspace, workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------------------------
@@ -766,9 +927,9 @@ extern "C" int mvb_paged_attention_decode_noalloc(void* out, int64_t out_stride,
   }
   const int sms = current_sm_count();
   MVB_REQUIRE(sms > 0, "mvb_paged_attention_decode_noalloc: no device");
-  MVB_REQUIRE(num_q_heads > 0 && head_dim > 0 && batch >= 0 && batch <= 4096,
+  MVB_REQUIRE(num_q_heads > 0 && num_kv_heads > 0 && head_dim > 0 && batch >= 0 && batch <= 4096,
               "mvb_paged_attention_decode_noalloc: bad shape");
-  const int64_t cbytes = attn_counters_bytes(batch);
+  const int64_t cbytes = attn_counters_bytes(batch * (num_kv_heads / attn_heads_per_group(num_kv_heads, head_dim)));
   const int64_t need = cbytes + 2LL * sms * num_q_heads * 8 + 2LL * sms * num_q_heads * head_dim * 4;
   if (need > kNoAllocScratchBytes)
     return fail(MVB_ERR_UNSUPPORTED,

@@ -56,13 +56,14 @@ __global__ void fused_mlp_kernel(T* __restrict__ out, const T* __restrict__ gate
   }
 }
 
-// SiLU(gate) * up of a SwiGLU-paired GEMM still in split-K partial form
+// act(gate) * up of a SwiGLU-paired GEMM still in split-K partial form
 // (MVB_EPI_SWIGLU_PARTIALS): tile t = j / 64 holds gate feature j in row j % 64 and up feature
 // j in row 64 + j % 64 of each contributor slot.  Both sums run in contributor order; the
-// rounding sequence is that of the GEMM's SWIGLU epilogue.  Thread = 4 consecutive features
-// of one batch row (blockIdx.y).
+// rounding sequence is that of the GEMM's SWIGLU epilogue.  act: SiLU (SwiGLU) or tanh-GELU
+// (GeGLU, models/gemma3_model.py:104-105).  Thread = 4 consecutive features of one batch row
+// (blockIdx.y).
 __global__ void swiglu_gemm_kernel(__nv_bfloat16* __restrict__ out, int64_t out_stride,
-                                   const float* __restrict__ partials, SplitKPlan p, int inter) {
+                                   const float* __restrict__ partials, SplitKPlan p, int inter, int act) {
   pdl_launch_dependents();
   pdl_wait();
   const int b = blockIdx.y;
@@ -84,13 +85,25 @@ __global__ void swiglu_gemm_kernel(__nv_bfloat16* __restrict__ out, int64_t out_
     u.z += pu.z;
     u.w += pu.w;
   }
-  auto h = [](float gv, float uv) { return bf16_round(silu_f(bf16_round(gv))) * bf16_round(uv); };
+  auto h = [act](float gv, float uv) { return bf16_round(act_f(bf16_round(gv), act)) * bf16_round(uv); };
   __nv_bfloat162 o01 = __floats2bfloat162_rn(h(g.x, u.x), h(g.y, u.y));
   __nv_bfloat162 o23 = __floats2bfloat162_rn(h(g.z, u.z), h(g.w, u.w));
   uint2 ov;
   ov.x = *reinterpret_cast<uint32_t*>(&o01);
   ov.y = *reinterpret_cast<uint32_t*>(&o23);
   *reinterpret_cast<uint2*>(out + static_cast<int64_t>(b) * out_stride + j) = ov;
+}
+
+// Gemma-2 final-logit soft-capping, x = T(T(tanh(T(x / cap))) * cap) (the three PyTorch ops
+// `x / cap`, `tanh`, `* cap` in the logits' dtype).
+template <typename T>
+__global__ void softcap_kernel(T* __restrict__ x, int64_t n, float cap) {
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float t = rnd<T>(tanhf(rnd<T>(to_f<T>(x[i]) / cap)));
+    x[i] = from_f<T>(t * cap);
+  }
 }
 
 template <typename T, typename I>
@@ -251,8 +264,29 @@ extern "C" int mvb_rotary_pos_emb(void* out, const void* in, const void* cos, co
                                    st, (T*)out, (const T*)in, (const T*)cos, (const T*)sin, rows, (int)head_dim));
 }
 
-extern "C" int mvb_swiglu_gemm(void* out, int64_t out_stride, const void* gemm_workspace, int64_t rows, int64_t inter,
-                               int64_t gemm_k, mvb_stream_t stream) {
+extern "C" int mvb_softcap(void* x, int64_t n, float cap, int dtype, mvb_stream_t stream) {
+  MVB_REQUIRE(x && n >= 0 && cap > 0.0f, "mvb_softcap: bad arguments");
+  if (n == 0) return MVB_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int sms = current_sm_count();
+  MVB_REQUIRE(sms > 0, "mvb_softcap: no device");
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 8LL * sms) blocks = 8LL * sms;
+  switch (dtype) {
+    case MVB_BF16:
+      return launch("softcap", softcap_kernel<__nv_bfloat16>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st,
+                    (__nv_bfloat16*)x, n, cap);
+    case MVB_F32:
+      return launch("softcap", softcap_kernel<float>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st,
+                    (float*)x, n, cap);
+    default:
+      return fail(MVB_ERR_INVALID_ARG, "mvb_softcap: unsupported dtype %d", dtype);
+  }
+}
+
+extern "C" int mvb_gated_gemm(void* out, int64_t out_stride, const void* gemm_workspace, int64_t rows, int64_t inter,
+                              int64_t gemm_k, int act, mvb_stream_t stream) {
+  MVB_REQUIRE(act == MVB_ACT_SILU || act == MVB_ACT_GELU_TANH, "mvb_gated_gemm: activation %d", act);
   MVB_REQUIRE(out && gemm_workspace, "mvb_swiglu_gemm: null pointer");
   MVB_REQUIRE(rows > 0 && rows <= 256 && inter > 0 && inter % 4 == 0 && inter < (1LL << 30) && gemm_k > 0 &&
                   gemm_k % kSplitBK == 0,
@@ -266,5 +300,10 @@ extern "C" int mvb_swiglu_gemm(void* out, int64_t out_stride, const void* gemm_w
   const unsigned bx = static_cast<unsigned>((inter / 4 + 255) / 256);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return launch("swiglu_gemm", swiglu_gemm_kernel, dim3(bx, static_cast<unsigned>(rows)), dim3(256), 0, st,
-                (__nv_bfloat16*)out, out_stride, (const float*)gemm_workspace, p, (int)inter);
+                (__nv_bfloat16*)out, out_stride, (const float*)gemm_workspace, p, (int)inter, act);
+}
+
+extern "C" int mvb_swiglu_gemm(void* out, int64_t out_stride, const void* gemm_workspace, int64_t rows, int64_t inter,
+                               int64_t gemm_k, mvb_stream_t stream) {
+  return mvb_gated_gemm(out, out_stride, gemm_workspace, rows, inter, gemm_k, MVB_ACT_SILU, stream);
 }

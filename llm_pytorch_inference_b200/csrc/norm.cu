@@ -113,10 +113,26 @@ struct TpFadd {
   const int32_t* epoch;
 };
 
-template <bool TP>
+// Sum over the cluster's CTAs (in CTA order) of each CTA's share `ss` of a row's sum of squares.
+__device__ __forceinline__ float cluster_row_sum(float ss, float* red, float* cta_ss) {
+  ss = block_sum(ss, red);
+  if (threadIdx.x == 0) *cta_ss = ss;
+  cluster_sync();
+  float total = 0.0f;
+  for (unsigned c = 0; c < gridDim.x; ++c) total += dsmem_ld_f32(cta_ss, c);
+  cluster_sync();  // no CTA leaves (or rewrites its share) while another may still read it
+  return total;
+}
+
+// POST (Gemma's sandwich norms, models/gemma3_model.py:270-283): the linear layer's output is
+// itself normalised with the post weight `pw` before the residual add,
+//   residual += T((y * r_y) * (1 + pw)),  out = T((residual * r) * (1 + w))   (plus_one form),
+// which takes a second cluster-wide sum of squares (over y) first.
+template <bool TP, bool POST>
 __global__ void fused_add_rmsnorm_gemm_kernel(__nv_bfloat16* __restrict__ out, __nv_bfloat16* __restrict__ residual,
                                               const float* __restrict__ partials, SplitKPlan p,
-                                              const __nv_bfloat16* __restrict__ w, int hidden, int runs_per_cta,
+                                              const __nv_bfloat16* __restrict__ w,
+                                              const __nv_bfloat16* __restrict__ pw, int hidden, int runs_per_cta,
                                               float eps, int plus_one, const __grid_constant__ TpFadd tp,
                                               unsigned* err) {
   __shared__ float red[32];
@@ -155,28 +171,63 @@ __global__ void fused_add_rmsnorm_gemm_kernel(__nv_bfloat16* __restrict__ out, _
           acc.w += qv.w;
         }
       }
-      const uint2 rr = *reinterpret_cast<const uint2*>(res + i);
-      const __nv_bfloat162 r01 = *reinterpret_cast<const __nv_bfloat162*>(&rr.x);
-      const __nv_bfloat162 r23 = *reinterpret_cast<const __nv_bfloat162*>(&rr.y);
-      v[k][0] = bf16_round(__low2float(r01) + bf16_round(acc.x));
-      v[k][1] = bf16_round(__high2float(r01) + bf16_round(acc.y));
-      v[k][2] = bf16_round(__low2float(r23) + bf16_round(acc.z));
-      v[k][3] = bf16_round(__high2float(r23) + bf16_round(acc.w));
-      __nv_bfloat162 o01 = __floats2bfloat162_rn(v[k][0], v[k][1]);
-      __nv_bfloat162 o23 = __floats2bfloat162_rn(v[k][2], v[k][3]);
-      uint2 ov;
-      ov.x = *reinterpret_cast<uint32_t*>(&o01);
-      ov.y = *reinterpret_cast<uint32_t*>(&o23);
-      *reinterpret_cast<uint2*>(res + i) = ov;
-      ss += v[k][0] * v[k][0] + v[k][1] * v[k][1] + v[k][2] * v[k][2] + v[k][3] * v[k][3];
+      v[k][0] = bf16_round(acc.x);  // the linear layer's bf16 output
+      v[k][1] = bf16_round(acc.y);
+      v[k][2] = bf16_round(acc.z);
+      v[k][3] = bf16_round(acc.w);
+      if constexpr (POST) {
+        ss += v[k][0] * v[k][0] + v[k][1] * v[k][1] + v[k][2] * v[k][2] + v[k][3] * v[k][3];
+      } else {
+        const uint2 rr = *reinterpret_cast<const uint2*>(res + i);
+        const __nv_bfloat162 r01 = *reinterpret_cast<const __nv_bfloat162*>(&rr.x);
+        const __nv_bfloat162 r23 = *reinterpret_cast<const __nv_bfloat162*>(&rr.y);
+        v[k][0] = bf16_round(__low2float(r01) + v[k][0]);
+        v[k][1] = bf16_round(__high2float(r01) + v[k][1]);
+        v[k][2] = bf16_round(__low2float(r23) + v[k][2]);
+        v[k][3] = bf16_round(__high2float(r23) + v[k][3]);
+        __nv_bfloat162 o01 = __floats2bfloat162_rn(v[k][0], v[k][1]);
+        __nv_bfloat162 o23 = __floats2bfloat162_rn(v[k][2], v[k][3]);
+        uint2 ov;
+        ov.x = *reinterpret_cast<uint32_t*>(&o01);
+        ov.y = *reinterpret_cast<uint32_t*>(&o23);
+        *reinterpret_cast<uint2*>(res + i) = ov;
+        ss += v[k][0] * v[k][0] + v[k][1] * v[k][1] + v[k][2] * v[k][2] + v[k][3] * v[k][3];
+      }
     }
   }
-  ss = block_sum(ss, red);
-  if (threadIdx.x == 0) cta_ss = ss;
-  cluster_sync();
-  float total = 0.0f;
-  for (unsigned c = 0; c < gridDim.x; ++c) total += dsmem_ld_f32(&cta_ss, c);
-  cluster_sync();  // no CTA leaves while another may still read its share
+  if constexpr (POST) {
+    // y -> post-norm(y) -> residual add; the sum of squares of the new residual follows.
+    const float ry = 1.0f / sqrtf(cluster_row_sum(ss, red, &cta_ss) / static_cast<float>(hidden) + eps);
+    ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kFaddMaxRuns; ++k) {
+      const int run = run0 + threadIdx.x + k * blockDim.x;
+      if (run < run_end) {
+        const int i = run * 4;
+        const uint2 wr = *reinterpret_cast<const uint2*>(pw + i);
+        const __nv_bfloat162 w01 = *reinterpret_cast<const __nv_bfloat162*>(&wr.x);
+        const __nv_bfloat162 w23 = *reinterpret_cast<const __nv_bfloat162*>(&wr.y);
+        const float wf[4] = {__low2float(w01), __high2float(w01), __low2float(w23), __high2float(w23)};
+        const uint2 rr = *reinterpret_cast<const uint2*>(res + i);
+        const __nv_bfloat162 r01 = *reinterpret_cast<const __nv_bfloat162*>(&rr.x);
+        const __nv_bfloat162 r23 = *reinterpret_cast<const __nv_bfloat162*>(&rr.y);
+        const float rf[4] = {__low2float(r01), __high2float(r01), __low2float(r23), __high2float(r23)};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float z = norm_out<__nv_bfloat16>(v[k][e], wf[e], ry, plus_one, MVB_NORM_MODEL, true);
+          v[k][e] = bf16_round(rf[e] + z);
+          ss += v[k][e] * v[k][e];
+        }
+        __nv_bfloat162 o01 = __floats2bfloat162_rn(v[k][0], v[k][1]);
+        __nv_bfloat162 o23 = __floats2bfloat162_rn(v[k][2], v[k][3]);
+        uint2 ov;
+        ov.x = *reinterpret_cast<uint32_t*>(&o01);
+        ov.y = *reinterpret_cast<uint32_t*>(&o23);
+        *reinterpret_cast<uint2*>(res + i) = ov;
+      }
+    }
+  }
+  const float total = cluster_row_sum(ss, red, &cta_ss);
   const float rr = 1.0f / sqrtf(total / static_cast<float>(hidden) + eps);
 #pragma unroll
   for (int k = 0; k < kFaddMaxRuns; ++k) {
@@ -305,11 +356,36 @@ extern "C" int mvb_fused_add_rmsnorm_gemm(void* out, void* residual, const void*
   const FaddSplit sp = fadd_split(hidden);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const TpFadd none{};
-  return launch_cluster("fused_add_rmsnorm_gemm", fused_add_rmsnorm_gemm_kernel<false>,
+  return launch_cluster("fused_add_rmsnorm_gemm", fused_add_rmsnorm_gemm_kernel<false, false>,
                         dim3(static_cast<unsigned>(sp.ctas), static_cast<unsigned>(rows)), dim3(sp.threads),
                         static_cast<unsigned>(sp.ctas), 0, st, (__nv_bfloat16*)out, (__nv_bfloat16*)residual,
-                        (const float*)gemm_workspace, p, (const __nv_bfloat16*)weight, (int)hidden,
-                        sp.runs_per_cta, eps, plus_one, none, device_status_ptr());
+                        (const float*)gemm_workspace, p, (const __nv_bfloat16*)weight, (const __nv_bfloat16*)nullptr,
+                        (int)hidden, sp.runs_per_cta, eps, plus_one, none, device_status_ptr());
+}
+
+extern "C" int mvb_fused_norm_add_rmsnorm_gemm(void* out, void* residual, const void* gemm_workspace, int64_t rows,
+                                               int64_t hidden, int64_t gemm_k, const void* post_weight,
+                                               const void* weight, float eps, int plus_one, mvb_stream_t stream) {
+  MVB_REQUIRE(out && residual && gemm_workspace && post_weight && weight,
+              "mvb_fused_norm_add_rmsnorm_gemm: null pointer");
+  MVB_REQUIRE(rows > 0 && rows <= 256 && hidden > 0 && gemm_k > 0 && gemm_k % kSplitBK == 0,
+              "mvb_fused_norm_add_rmsnorm_gemm: bad shape");
+  const int sms = current_sm_count();
+  MVB_REQUIRE(sms > 0, "mvb_fused_norm_add_rmsnorm_gemm: no device");
+  MVB_REQUIRE(hidden % 4 == 0 && hidden <= 16384,
+              "mvb_fused_norm_add_rmsnorm_gemm: hidden %lld must be a multiple of 4 and <= 16384", (long long)hidden);
+  MVB_REQUIRE(aligned(residual, 8) && aligned(out, 8) && aligned(weight, 8) && aligned(post_weight, 8),
+              "mvb_fused_norm_add_rmsnorm_gemm: 8-byte alignment");
+  const SplitKPlan p = splitk_plan(rows, hidden, gemm_k, sms);
+  const FaddSplit sp = fadd_split(hidden);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const TpFadd none{};
+  return launch_cluster("fused_norm_add_rmsnorm_gemm", fused_add_rmsnorm_gemm_kernel<false, true>,
+                        dim3(static_cast<unsigned>(sp.ctas), static_cast<unsigned>(rows)), dim3(sp.threads),
+                        static_cast<unsigned>(sp.ctas), 0, st, (__nv_bfloat16*)out, (__nv_bfloat16*)residual,
+                        (const float*)gemm_workspace, p, (const __nv_bfloat16*)weight,
+                        (const __nv_bfloat16*)post_weight, (int)hidden, sp.runs_per_cta, eps, plus_one, none,
+                        device_status_ptr());
 }
 
 extern "C" int mvb_tp_fused_add_rmsnorm_gemm(mvb_tp_comm* comm, void* residual, int64_t rows, int64_t hidden,
@@ -354,11 +430,11 @@ extern "C" int mvb_tp_fused_add_rmsnorm_gemm(mvb_tp_comm* comm, void* residual, 
   tp.epoch = comm->epoch;
   const FaddSplit sp = fadd_split(hidden);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  MVB_TRY(launch_cluster("tp_fused_add_rmsnorm_gemm", fused_add_rmsnorm_gemm_kernel<true>,
+  MVB_TRY(launch_cluster("tp_fused_add_rmsnorm_gemm", fused_add_rmsnorm_gemm_kernel<true, false>,
                          dim3(static_cast<unsigned>(sp.ctas), static_cast<unsigned>(rpr)), dim3(sp.threads),
                          static_cast<unsigned>(sp.ctas), 0, st, (__nv_bfloat16*)nullptr, (__nv_bfloat16*)residual,
-                         (const float*)nullptr, p, (const __nv_bfloat16*)weight, (int)hidden, sp.runs_per_cta, eps,
-                         plus_one, tp, device_status_ptr()));
+                         (const float*)nullptr, p, (const __nv_bfloat16*)weight, (const __nv_bfloat16*)nullptr,
+                         (int)hidden, sp.runs_per_cta, eps, plus_one, tp, device_status_ptr()));
   comm->point_count[signal_point] = 1;
   return MVB_OK;
 }

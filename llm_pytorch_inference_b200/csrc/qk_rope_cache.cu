@@ -22,7 +22,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     int64_t qkv_stride, const __nv_bfloat16* __restrict__ qnw, const __nv_bfloat16* __restrict__ knw,
     const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t, int64_t table_len,
     const int32_t* __restrict__ positions, const int32_t* __restrict__ block_tables, int64_t max_blocks, int batch,
-    int nq, int nkv, int64_t layer, int64_t num_blocks, int bs, float eps, unsigned* err,
+    int nq, int nkv, int64_t layer, int64_t num_blocks, int bs, float eps, int plus_one, unsigned* err,
     const float* __restrict__ partials, SplitKPlan plan) {
   constexpr int E = D / 32;
   pdl_launch_dependents();
@@ -100,7 +100,8 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     return;
   }
 
-  // Per-head RMSNorm (model semantics: T(w * (x * r))).
+  // Per-head RMSNorm (model semantics: T(w * (x * r)); Gemma's plus-one form T((x * r) * (1 + w)),
+  // models/gemma3_model.py:21-25).
   const __nv_bfloat16* nw = is_q ? qnw : knw;
   if (nw != nullptr) {
     float ss = 0.0f;
@@ -109,7 +110,10 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     ss = warp_sum(ss);
     const float r = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
 #pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = bf16_round(__bfloat162float(nw[d0 + e]) * (x[e] * r));
+    for (int e = 0; e < E; ++e) {
+      const float wv = __bfloat162float(nw[d0 + e]);
+      x[e] = plus_one ? bf16_round((x[e] * r) * (1.0f + wv)) : bf16_round(wv * (x[e] * r));
+    }
   }
 
   // RoPE with the model's bf16 cos/sin rows: T(T(x*cos) + T(rot(x)*sin)).
@@ -152,8 +156,8 @@ static int qk_norm_rope_kv_write_impl(void* q_out, void* kv_cache, const void* q
                                       int64_t table_len, const int32_t* positions, const int32_t* block_tables,
                                       int64_t max_blocks, int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
                                       int64_t head_dim, int64_t num_layers, int64_t layer, int64_t num_blocks,
-                                      int64_t block_size, float eps, const float* partials, SplitKPlan plan,
-                                      mvb_stream_t stream) {
+                                      int64_t block_size, float eps, int plus_one, const float* partials,
+                                      SplitKPlan plan, mvb_stream_t stream) {
   MVB_REQUIRE(q_out && kv_cache && (qkv || partials) && cos && sin && positions && block_tables,
               "mvb_qk_norm_rope_kv_write: null pointer");
   MVB_REQUIRE((q_norm_w == nullptr) == (k_norm_w == nullptr),
@@ -174,7 +178,7 @@ static int qk_norm_rope_kv_write_impl(void* q_out, void* kv_cache, const void* q
                 (__nv_bfloat16*)kv_cache, (const __nv_bfloat16*)qkv, qkv_stride, (const __nv_bfloat16*)q_norm_w, \
                 (const __nv_bfloat16*)k_norm_w, (const __nv_bfloat16*)cos, (const __nv_bfloat16*)sin, table_len,  \
                 positions, block_tables, max_blocks, (int)batch, (int)num_q_heads, (int)num_kv_heads, layer,     \
-                num_blocks, (int)block_size, eps, err, partials, plan)
+                num_blocks, (int)block_size, eps, plus_one, err, partials, plan)
   switch (head_dim) {
     case 64: MVB_QKR_LAUNCH(64);
     case 128: MVB_QKR_LAUNCH(128);
@@ -190,10 +194,11 @@ extern "C" int mvb_qk_norm_rope_kv_write(void* q_out, void* kv_cache, const void
                                          const int32_t* block_tables, int64_t max_blocks, int64_t batch,
                                          int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
                                          int64_t num_layers, int64_t layer, int64_t num_blocks, int64_t block_size,
-                                         float eps, mvb_stream_t stream) {
+                                         float eps, int plus_one, mvb_stream_t stream) {
   return qk_norm_rope_kv_write_impl(q_out, kv_cache, qkv, qkv_stride, q_norm_w, k_norm_w, cos, sin, table_len,
                                     positions, block_tables, max_blocks, batch, num_q_heads, num_kv_heads, head_dim,
-                                    num_layers, layer, num_blocks, block_size, eps, nullptr, SplitKPlan{}, stream);
+                                    num_layers, layer, num_blocks, block_size, eps, plus_one, nullptr, SplitKPlan{},
+                                    stream);
 }
 
 extern "C" int mvb_qk_norm_rope_kv_write_gemm(void* q_out, void* kv_cache, const void* gemm_workspace,
@@ -203,7 +208,7 @@ extern "C" int mvb_qk_norm_rope_kv_write_gemm(void* q_out, void* kv_cache, const
                                               int64_t max_blocks, int64_t batch, int64_t num_q_heads,
                                               int64_t num_kv_heads, int64_t head_dim, int64_t num_layers,
                                               int64_t layer, int64_t num_blocks, int64_t block_size, float eps,
-                                              mvb_stream_t stream) {
+                                              int plus_one, mvb_stream_t stream) {
   MVB_REQUIRE(gemm_workspace && batch > 0 && batch <= 256 && gemm_k > 0 && gemm_k % kSplitBK == 0,
               "mvb_qk_norm_rope_kv_write_gemm: bad arguments");
   const int sms = current_sm_count();
@@ -211,6 +216,6 @@ extern "C" int mvb_qk_norm_rope_kv_write_gemm(void* q_out, void* kv_cache, const
   const SplitKPlan plan = splitk_plan(batch, (num_q_heads + 2 * num_kv_heads) * head_dim, gemm_k, sms);
   return qk_norm_rope_kv_write_impl(q_out, kv_cache, nullptr, 0, q_norm_w, k_norm_w, cos, sin, table_len,
                                     positions, block_tables, max_blocks, batch, num_q_heads, num_kv_heads, head_dim,
-                                    num_layers, layer, num_blocks, block_size, eps,
+                                    num_layers, layer, num_blocks, block_size, eps, plus_one,
                                     static_cast<const float*>(gemm_workspace), plan, stream);
 }

@@ -412,9 +412,10 @@ def qk_norm_rope_kv_write(qkv: torch.Tensor, kv_cache: torch.Tensor, layer: int,
                           block_tables: torch.Tensor, cos_table: torch.Tensor, sin_table: torch.Tensor,
                           num_q_heads: int, num_kv_heads: int, q_norm_w: torch.Tensor | None = None,
                           k_norm_w: torch.Tensor | None = None, eps: float = 1e-6,
-                          q_out: torch.Tensor | None = None) -> torch.Tensor:
+                          q_out: torch.Tensor | None = None, plus_one: bool = False) -> torch.Tensor:
     """Per-head QK-norm + RoPE of one new token per sequence and its K/V written into
-    ``kv_cache[layer, 0|1, block_tables[b][pos // bs], pos % bs]``; returns q ``[B, Hq, D]``."""
+    ``kv_cache[layer, 0|1, block_tables[b][pos // bs], pos % bs]``; returns q ``[B, Hq, D]``.
+    ``plus_one`` selects Gemma's ``(1 + w)`` norm scale."""
     N.require_cuda(qkv, kv_cache, positions, block_tables, cos_table, sin_table)
     L, _, P, bs, nkv, D = kv_cache.shape
     B = qkv.shape[0]
@@ -425,15 +426,18 @@ def qk_norm_rope_kv_write(qkv: torch.Tensor, kv_cache: torch.Tensor, layer: int,
             q_out.data_ptr(), kv_cache.data_ptr(), qkv.data_ptr(), qkv.stride(0), N.ptr(q_norm_w), N.ptr(k_norm_w),
             cos_table.data_ptr(), sin_table.data_ptr(), cos_table.shape[0], positions.data_ptr(),
             block_tables.data_ptr(), block_tables.shape[1], B, num_q_heads, num_kv_heads, D, L, layer, P, bs,
-            float(eps), _st(qkv)), "qk_norm_rope_kv_write")
+            float(eps), int(plus_one), _st(qkv)), "qk_norm_rope_kv_write")
     return q_out
 
 
 def paged_attention_decode(q: torch.Tensor, kv_cache: torch.Tensor, layer: int, block_tables: torch.Tensor,
                            ctx_lens: torch.Tensor, scale: float, out: torch.Tensor | None = None,
-                           workspace: torch.Tensor | None = None) -> torch.Tensor:
+                           workspace: torch.Tensor | None = None, softcap: float = 0.0,
+                           window: int = 0) -> torch.Tensor:
     """Decode attention of q ``[B, Hq, D]`` over each sequence's first ``ctx_lens[b]`` cached
-    tokens of ``layer`` (read through ``block_tables``); returns ``[B, Hq, D]``."""
+    tokens of ``layer`` (read through ``block_tables``); returns ``[B, Hq, D]``.  ``softcap`` > 0
+    soft-caps the scaled scores (``softcap * tanh(s / softcap)``); ``window`` > 0 keeps only the
+    newest ``window`` keys of each sequence."""
     N.require_cuda(q, kv_cache, block_tables, ctx_lens)
     L, _, P, bs, nkv, D = kv_cache.shape
     B, Hq, _ = q.shape
@@ -443,8 +447,8 @@ def paged_attention_decode(q: torch.Tensor, kv_cache: torch.Tensor, layer: int, 
     with torch.cuda.device(dev):
         need = N.lib().mvb_paged_attention_workspace_bytes(B, Hq, D, dev.index if dev.index is not None else 0) + (1 << 16)
         ws = workspace if workspace is not None else WORKSPACES.get(dev, "attention", need)
-        N.check(N.lib().mvb_paged_attention_decode(
+        N.check(N.lib().mvb_paged_attention_decode_ex(
             out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), kv_cache.data_ptr(), block_tables.data_ptr(),
-            block_tables.shape[1], ctx_lens.data_ptr(), B, Hq, nkv, D, L, layer, P, bs, float(scale), ws.data_ptr(),
-            ws.numel(), _st(q)), "paged_attention_decode")
+            block_tables.shape[1], ctx_lens.data_ptr(), B, Hq, nkv, D, L, layer, P, bs, float(scale), float(softcap),
+            int(window), ws.data_ptr(), ws.numel(), _st(q)), "paged_attention_decode")
     return out

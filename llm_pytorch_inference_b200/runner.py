@@ -31,7 +31,7 @@ import math
 import torch
 
 from . import _native as N
-from .configs import head_dim, num_kv_heads
+from .configs import embed_scale, head_dim, is_gemma, layer_rope_theta, layer_window, num_kv_heads
 from .kv_cache import KVCacheManager
 from . import tensor_parallel as tpm
 from .tensor_parallel import TensorParallelConfig
@@ -72,6 +72,7 @@ class DecodeWeights:
         self.final_norm = get("model.norm.weight")
         self.qk_norm = cfg.get("_qk_norm", False)
         self.wqkv, self.wo, self.wgu, self.wdown, self.ln1, self.ln2, self.qn, self.kn = ([] for _ in range(8))
+        self.pre_ff, self.post_ff = [], []   # Gemma: pre/post feed-forward norms (gemma3_model.py:265-268)
         self.moe = bool(cfg.get("num_experts"))
         self.router, self.egu, self.edown = [], [], []    # MoE: [E, H], [E, 2I, H], [E, H, I]
         for i in range(L):
@@ -97,13 +98,16 @@ class DecodeWeights:
                 self.wdown.append(get(p + "mlp.down_proj.weight"))
             self.ln1.append(get(p + "input_layernorm.weight"))
             self.ln2.append(get(p + "post_attention_layernorm.weight"))
+            if cfg.get("_has_feedforward_layernorms"):
+                self.pre_ff.append(get(p + "pre_feedforward_layernorm.weight"))
+                self.post_ff.append(get(p + "post_feedforward_layernorm.weight"))
             if self.qk_norm:
                 self.qn.append(get(a + "q_norm.weight"))
                 self.kn.append(get(a + "k_norm.weight"))
 
     def nbytes(self) -> int:
         ts = [self.embed, self.final_norm, *self.wqkv, *self.wo, *self.wgu, *self.wdown, *self.ln1, *self.ln2,
-              *self.qn, *self.kn, *self.router, *self.egu, *self.edown]
+              *self.qn, *self.kn, *self.router, *self.egu, *self.edown, *self.pre_ff, *self.post_ff]
         if self.lm_head is not self.embed:
             ts.append(self.lm_head)
         return sum(t.numel() * t.element_size() for t in ts)
@@ -112,7 +116,7 @@ class DecodeWeights:
         """Weight bytes one decode step must read: every layer's matrices and norms, the final norm
         and lm_head (the embedding table is only gathered, one row per sequence)."""
         ts = [self.final_norm, self.lm_head, *self.wqkv, *self.wo, *self.wgu, *self.wdown, *self.ln1, *self.ln2,
-              *self.qn, *self.kn, *self.router, *self.egu, *self.edown]
+              *self.qn, *self.kn, *self.router, *self.egu, *self.edown, *self.pre_ff, *self.post_ff]
         return sum(t.numel() * t.element_size() for t in ts)
 
 
@@ -146,9 +150,25 @@ class DecodeRunner:
         self.max_blocks = (max_model_len + kv.block_size - 1) // kv.block_size
         self.P = kv.kv_cache.shape[2]  # includes the scratch block
         rope_len = rope_len or max(max_model_len, 256)
-        self.cos, self.sin = rope_tables(self.D, float(cfg.get("rope_theta", 10000.0)), rope_len, torch.bfloat16,
-                                         self.dev)
+        # Gemma: sandwich (1 + w) norms, GeGLU, scaled embedding, per-layer RoPE theta and window,
+        # soft-capped attention / final logits (0 = off).
+        self.gemma = is_gemma(cfg)
+        self.plus_one = 1 if (self.gemma or cfg.get("_rms_norm_plus_one")) else 0
+        self.act = N.ACT_GELU_TANH if cfg.get("hidden_act") in ("gelu_new", "gelu_pytorch_tanh") else N.ACT_SILU
+        self.embed_scale = embed_scale(cfg)
+        self.softcap = float(cfg.get("attn_logit_softcapping") or 0.0)
+        self.final_softcap = float(cfg.get("final_logit_softcapping") or 0.0)
+        self.windows = [layer_window(cfg, i) for i in range(self.L)]
+        self.tables = {}
+        for i in range(self.L):
+            th = layer_rope_theta(cfg, i)
+            if th not in self.tables:
+                self.tables[th] = rope_tables(self.D, th, rope_len, torch.bfloat16, self.dev)
+        self.layer_tables = [self.tables[layer_rope_theta(cfg, i)] for i in range(self.L)]
+        self.cos, self.sin = self.layer_tables[0]
 
+        if self.gemma and self.tp.enabled:
+            raise NotImplementedError("tensor parallelism of the Gemma decode step is not built")
         B, H, dev, bf = self.B, self.H, self.dev, torch.bfloat16
         qkv_n = (self.Hq + 2 * self.Hkv) * self.D
         didx = dev.index if dev.index is not None else torch.cuda.current_device()
@@ -266,6 +286,58 @@ class DecodeRunner:
                                   w.shape[0], w.shape[1], epilogue, N.ptr(aux), 0 if aux is None else aux.stride(0),
                                   self.gemm_ws.data_ptr(), self.gemm_ws.numel(), self._st), "gemm_bf16")
 
+    def _qk(self, i) -> None:
+        """QK-norm + RoPE + KV write of layer i from the q|k|v projection's split-K partials."""
+        w, D = self.w, self.D
+        cos, sin = self.layer_tables[i]
+        N.check(N.lib().mvb_qk_norm_rope_kv_write_gemm(
+            self.q.data_ptr(), self.kv.kv_cache.data_ptr(), self.gemm_ws.data_ptr(), self.H,
+            w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
+            cos.data_ptr(), sin.data_ptr(), cos.shape[0], self.pos.data_ptr(), self.block_tables.data_ptr(),
+            self.max_blocks, self.B, self.Hq, self.Hkv, D, self.L, i, self.P, self.kv.block_size, self.eps,
+            self.plus_one, self._st), "qk_norm_rope_kv_write_gemm")
+
+    def _attention(self, i) -> None:
+        """Paged decode attention of layer i (soft-capping and sliding window as configured)."""
+        D = self.D
+        N.check(N.lib().mvb_paged_attention_decode_ex(
+            self.attn.data_ptr(), self.attn.stride(0), self.q.data_ptr(), self.Hq * D, self.kv.kv_cache.data_ptr(),
+            self.block_tables.data_ptr(), self.max_blocks, self.ctx.data_ptr(), self.B, self.Hq, self.Hkv, D,
+            self.L, i, self.P, self.kv.block_size, self.scale, self.softcap, self.windows[i],
+            self.attn_ws.data_ptr(), self.attn_ws.numel(), self._st), "paged_attention_decode")
+
+    def _add_norm(self, gemm_k, weight, post_weight=None) -> None:
+        """residual += the preceding GEMM's output (Gemma: post-normalised first), xn = norm(residual)."""
+        lib, B, H = N.lib(), self.B, self.H
+        if post_weight is not None:
+            N.check(lib.mvb_fused_norm_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(),
+                                                        self.gemm_ws.data_ptr(), B, H, gemm_k,
+                                                        post_weight.data_ptr(), weight.data_ptr(), self.eps,
+                                                        self.plus_one, self._st), "fused_norm_add_rmsnorm_gemm")
+        else:
+            N.check(lib.mvb_fused_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(),
+                                                   self.gemm_ws.data_ptr(), B, H, gemm_k, weight.data_ptr(),
+                                                   self.eps, self.plus_one, self._st), "fused_add_rmsnorm_gemm")
+
+    def _embed(self) -> None:
+        """Token embedding (times sqrt(hidden) for Gemma) and the first layer's input norm."""
+        lib, w, B, H = N.lib(), self.w, self.B, self.H
+        N.check(lib.mvb_embedding(self.residual.data_ptr(), self.ids.data_ptr(), N.I32, w.embed.data_ptr(), B, H,
+                                  self.V, self.embed_scale, N.BF16, self._st), "embedding")
+        N.check(lib.mvb_rmsnorm(self.xn.data_ptr(), H, self.residual.data_ptr(), H, w.ln1[0].data_ptr(), B, H,
+                                self.eps, self.plus_one, N.NORM_MODEL, N.BF16, self._st), "rmsnorm")
+
+    def _logits_and_sample(self) -> None:
+        """lm_head into the logits buffer, the final soft-capping (Gemma-2), sampling."""
+        lib, B = N.lib(), self.B
+        self._gemm(self.logits, self.xn, self.w.lm_head)
+        if self.final_softcap:
+            N.check(lib.mvb_softcap(self.logits.data_ptr(), B * self.V, self.final_softcap, N.BF16, self._st),
+                    "softcap")
+        N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
+                               self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
+                               0, self.offset.data_ptr(), N.BF16, self._st), "sample")
+
     def forward(self) -> None:
         """Launches one decode step on the current stream (metadata must be on the device)."""
         if self.tp.enabled:
@@ -276,43 +348,26 @@ class DecodeRunner:
             return
         lib, w, B, H = N.lib(), self.w, self.B, self.H
         self._st = N.stream_handle(self.dev)
-        st, eps, bf = self._st, self.eps, N.BF16
-        kvc = self.kv.kv_cache
-        N.check(lib.mvb_embedding(self.residual.data_ptr(), self.ids.data_ptr(), N.I32, w.embed.data_ptr(), B, H,
-                                  self.V, 1.0, bf, st), "embedding")
-        N.check(lib.mvb_rmsnorm(self.xn.data_ptr(), H, self.residual.data_ptr(), H, w.ln1[0].data_ptr(), B, H, eps, 0,
-                                N.NORM_MODEL, bf, st), "rmsnorm")
-        ws = self.gemm_ws.data_ptr()
+        st = self._st
+        g = self.gemma   # Gemma: post-norms of the attention and MLP outputs before each residual add
+        self._embed()
         for i in range(self.L):
             if i > 0:   # residual += down_proj output (split-K partials), then input_layernorm
-                N.check(lib.mvb_fused_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(), ws, B, H,
-                                                       self.I, w.ln1[i].data_ptr(), eps, 0, st),
-                        "fused_add_rmsnorm_gemm")
+                self._add_norm(self.I, w.ln1[i], w.post_ff[i - 1] if g else None)
             self._gemm(None, self.xn, w.wqkv[i], N.EPI_PARTIALS)
-            N.check(lib.mvb_qk_norm_rope_kv_write_gemm(
-                self.q.data_ptr(), kvc.data_ptr(), ws, H,
-                w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
-                self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0], self.pos.data_ptr(),
-                self.block_tables.data_ptr(), self.max_blocks, B, self.Hq, self.Hkv, self.D, self.L, i, self.P,
-                self.kv.block_size, eps, st), "qk_norm_rope_kv_write_gemm")
-            N.check(lib.mvb_paged_attention_decode(
-                self.attn.data_ptr(), self.attn.stride(0), self.q.data_ptr(), self.Hq * self.D, kvc.data_ptr(),
-                self.block_tables.data_ptr(), self.max_blocks, self.ctx.data_ptr(), B, self.Hq, self.Hkv, self.D,
-                self.L, i, self.P, self.kv.block_size, self.scale, self.attn_ws.data_ptr(), self.attn_ws.numel(), st),
-                "paged_attention_decode")
+            self._qk(i)
+            self._attention(i)
             self._gemm(None, self.attn, w.wo[i], N.EPI_PARTIALS)
-            N.check(lib.mvb_fused_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(), ws, B, H,
-                                                   self.Hq * self.D, w.ln2[i].data_ptr(), eps, 0, st),
-                    "fused_add_rmsnorm_gemm")
+            if g:   # residual += post_attention_layernorm(o_proj), then pre_feedforward_layernorm
+                self._add_norm(self.Hq * self.D, w.pre_ff[i], w.ln2[i])
+            else:
+                self._add_norm(self.Hq * self.D, w.ln2[i])
             self._gemm(None, self.xn, w.wgu[i], N.EPI_SWIGLU_PARTIALS)
-            N.check(lib.mvb_swiglu_gemm(self.h.data_ptr(), self.h.stride(0), ws, B, self.I, H, st), "swiglu_gemm")
+            N.check(lib.mvb_gated_gemm(self.h.data_ptr(), self.h.stride(0), self.gemm_ws.data_ptr(), B, self.I, H,
+                                       self.act, st), "gated_gemm")
             self._gemm(None, self.h, w.wdown[i], N.EPI_PARTIALS)
-        N.check(lib.mvb_fused_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(), ws, B, H, self.I,
-                                               w.final_norm.data_ptr(), eps, 0, st), "fused_add_rmsnorm_gemm")
-        self._gemm(self.logits, self.xn, w.lm_head)
-        N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
-                               self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
-                               0, self.offset.data_ptr(), bf, st), "sample")
+        self._add_norm(self.I, w.final_norm, w.post_ff[self.L - 1] if g else None)
+        self._logits_and_sample()
 
     def _moe_mlp(self, i) -> None:
         """The sparse MoE block on ``self.xn`` into ``self.mlp_out`` (``qwen3_moe_model.py:39-65``):
@@ -343,7 +398,6 @@ class DecodeRunner:
         lib, w, B, H, D = N.lib(), self.w, self.B, self.H, self.D
         self._st = N.stream_handle(self.dev)
         st, eps, bf = self._st, self.eps, N.BF16
-        kvc = self.kv.kv_cache
         ws = self.gemm_ws.data_ptr()
         N.check(lib.mvb_embedding(self.residual.data_ptr(), self.ids.data_ptr(), N.I32, w.embed.data_ptr(), B, H,
                                   self.V, 1.0, bf, st), "embedding")
@@ -355,17 +409,8 @@ class DecodeRunner:
                                                   w.ln1[i].data_ptr(), B, H, eps, 0, N.NORM_MODEL, bf, st),
                         "fused_add_rmsnorm")
             self._gemm(None, self.xn, w.wqkv[i], N.EPI_PARTIALS)
-            N.check(lib.mvb_qk_norm_rope_kv_write_gemm(
-                self.q.data_ptr(), kvc.data_ptr(), ws, H,
-                w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
-                self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0], self.pos.data_ptr(),
-                self.block_tables.data_ptr(), self.max_blocks, B, self.Hq, self.Hkv, D, self.L, i, self.P,
-                self.kv.block_size, eps, st), "qk_norm_rope_kv_write_gemm")
-            N.check(lib.mvb_paged_attention_decode(
-                self.attn.data_ptr(), self.attn.stride(0), self.q.data_ptr(), self.Hq * D, kvc.data_ptr(),
-                self.block_tables.data_ptr(), self.max_blocks, self.ctx.data_ptr(), B, self.Hq, self.Hkv, D,
-                self.L, i, self.P, self.kv.block_size, self.scale, self.attn_ws.data_ptr(), self.attn_ws.numel(), st),
-                "paged_attention_decode")
+            self._qk(i)
+            self._attention(i)
             self._gemm(None, self.attn, w.wo[i], N.EPI_PARTIALS)
             N.check(lib.mvb_fused_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(), ws, B, H,
                                                    self.Hq * D, w.ln2[i].data_ptr(), eps, 0, st),
@@ -398,7 +443,6 @@ class DecodeRunner:
         self._st = N.stream_handle(self.dev)
         st, eps, bf, lay = self._st, self.eps, N.BF16, self.layout
         comm = self.heap.comm
-        kvc = self.kv.kv_cache
         ws = self.gemm_ws.data_ptr()
         N.check(lib.mvb_tp_begin_step(comm, st), "tp_begin_step")
         N.check(lib.mvb_embedding(self.residual.data_ptr(), self.ids.data_ptr(), N.I32, w.embed.data_ptr(), B, H,
@@ -409,17 +453,8 @@ class DecodeRunner:
             if i > 0:
                 self._tp_add_norm(self.I, w.ln1[i], lay.recv_down, tpm.point_down(i - 1), tpm.point_mlp_norm(i - 1))
             self._tp_gemm(self.xn, w.wqkv[i], N.EPI_PARTIALS, wait=-1 if i == 0 else tpm.point_mlp_norm(i - 1))
-            N.check(lib.mvb_qk_norm_rope_kv_write_gemm(
-                self.q.data_ptr(), kvc.data_ptr(), ws, H,
-                w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
-                self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0], self.pos.data_ptr(),
-                self.block_tables.data_ptr(), self.max_blocks, B, self.Hq, self.Hkv, D, self.L, i, self.P,
-                self.kv.block_size, eps, st), "qk_norm_rope_kv_write_gemm")
-            N.check(lib.mvb_paged_attention_decode(
-                self.attn.data_ptr(), self.attn.stride(0), self.q.data_ptr(), self.Hq * D, kvc.data_ptr(),
-                self.block_tables.data_ptr(), self.max_blocks, self.ctx.data_ptr(), B, self.Hq, self.Hkv, D,
-                self.L, i, self.P, self.kv.block_size, self.scale, self.attn_ws.data_ptr(), self.attn_ws.numel(), st),
-                "paged_attention_decode")
+            self._qk(i)
+            self._attention(i)
             self._tp_gemm(self.attn, w.wo[i], N.EPI_PARTIALS, out_offset=lay.recv_o, signal=tpm.point_o_proj(i))
             self._tp_add_norm(self.Hq * D, w.ln2[i], lay.recv_o, tpm.point_o_proj(i), tpm.point_attn_norm(i))
             self._tp_gemm(self.xn, w.wgu[i], N.EPI_SWIGLU_PARTIALS, wait=tpm.point_attn_norm(i))
@@ -438,61 +473,65 @@ class DecodeRunner:
     def kernel_kinds(self) -> dict:
         """kind -> (launch(layer), launches per step, algorithmic bytes per launch, flops per launch)."""
         lib, w, B, H, D = N.lib(), self.w, self.B, self.H, self.D
-        st, eps, bf = self._st, self.eps, N.BF16
-        kvc = self.kv.kv_cache
-        ctx = self.ctx.cpu()
-        kv_bytes = int(ctx.sum()) * self.Hkv * D * 2 * 2          # K and V of every attended token
+        self._st = N.stream_handle(self.dev)
+        st = self._st
+        ctx = self.ctx.cpu().tolist()
         qkv_n = (self.Hq + 2 * self.Hkv) * D
+        glob = [i for i in range(self.L) if not self.windows[i]]
+        slid = [i for i in range(self.L) if self.windows[i]]
+
+        def attn_kind(layers):   # launches over the given layers, bytes and flops of one launch
+            wnd = self.windows[layers[0]]
+            keys = sum(min(c, wnd) if wnd else c for c in ctx)
+            return ((lambda i: self._attention(layers[i % len(layers)])), len(layers),
+                    keys * self.Hkv * D * 2 * 2 + 2 * B * self.Hq * D * 2, 4 * keys * self.Hq * D)
+        g = self.gemma
 
         def gemm_bytes(n, k, out_cols):
             return n * k * 2 + B * k * 2 + B * out_cols * 2
 
-        def qk(i):
-            N.check(lib.mvb_qk_norm_rope_kv_write_gemm(
-                self.q.data_ptr(), kvc.data_ptr(), self.gemm_ws.data_ptr(), H,
-                w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
-                self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0], self.pos.data_ptr(),
-                self.block_tables.data_ptr(), self.max_blocks, B, self.Hq, self.Hkv, D, self.L, i, self.P,
-                self.kv.block_size, eps, st), "qk_norm_rope_kv_write")
-
-        def attn(i):
-            N.check(lib.mvb_paged_attention_decode(
-                self.attn.data_ptr(), self.attn.stride(0), self.q.data_ptr(), self.Hq * D, kvc.data_ptr(),
-                self.block_tables.data_ptr(), self.max_blocks, self.ctx.data_ptr(), B, self.Hq, self.Hkv, D,
-                self.L, i, self.P, self.kv.block_size, self.scale, self.attn_ws.data_ptr(), self.attn_ws.numel(),
-                st), "paged_attention_decode")
-
         def fadd(i):
-            N.check(lib.mvb_fused_add_rmsnorm_gemm(self.xn.data_ptr(), self.residual.data_ptr(),
-                                                   self.gemm_ws.data_ptr(), B, H, self.Hq * D, w.ln2[i].data_ptr(),
-                                                   eps, 0, st), "fused_add_rmsnorm_gemm")
+            if g:
+                self._add_norm(self.Hq * D, w.pre_ff[i], w.ln2[i])
+            else:
+                self._add_norm(self.Hq * D, w.ln2[i])
 
-        def swiglu(i):
-            N.check(lib.mvb_swiglu_gemm(self.h.data_ptr(), self.h.stride(0), self.gemm_ws.data_ptr(), B, self.I, H,
-                                        st), "swiglu_gemm")
+        def gated(i):
+            N.check(lib.mvb_gated_gemm(self.h.data_ptr(), self.h.stride(0), self.gemm_ws.data_ptr(), B, self.I, H,
+                                       self.act, st), "gated_gemm")
 
         def samp(i):
             N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
                                    self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(),
-                                   self.seed, 0, self.offset.data_ptr(), bf, st), "sample")
+                                   self.seed, 0, self.offset.data_ptr(), N.BF16, st), "sample")
 
-        return {
-            "paged_attention_decode": (attn, self.L, kv_bytes + 2 * B * self.Hq * D * 2, 4 * int(ctx.sum()) * self.Hq * D),
+        kinds = {}
+        if glob:
+            kinds["paged_attention_decode"] = attn_kind(glob)
+        if slid:   # sliding-window layers: the newest `window` keys of each sequence
+            kinds["paged_attention_decode_window"] = attn_kind(slid)
+        kinds.update({
             "gemm_qkv": (lambda i: self._gemm(None, self.xn, w.wqkv[i], N.EPI_PARTIALS), self.L,
                          gemm_bytes(qkv_n, H, 0), 2 * B * qkv_n * H),
             "gemm_o_proj": (lambda i: self._gemm(None, self.attn, w.wo[i], N.EPI_PARTIALS), self.L,
                             gemm_bytes(H, self.Hq * D, 0), 2 * B * H * self.Hq * D),
             "gemm_gate_up": (lambda i: self._gemm(None, self.xn, w.wgu[i], N.EPI_SWIGLU_PARTIALS), self.L,
                              gemm_bytes(2 * self.I, H, 0), 2 * B * 2 * self.I * H),
-            "swiglu_gemm": (swiglu, self.L, B * 2 * self.I * 4 + B * self.I * 2, 0),
+            "swiglu_gemm": (gated, self.L, B * 2 * self.I * 4 + B * self.I * 2, 0),
             "gemm_down": (lambda i: self._gemm(None, self.h, w.wdown[i], N.EPI_PARTIALS), self.L,
                           gemm_bytes(H, self.I, 0), 2 * B * H * self.I),
             "gemm_lm_head": (lambda i: self._gemm(self.logits, self.xn, w.lm_head), 1,
                              gemm_bytes(self.Vl, H, self.Vl), 2 * B * self.Vl * H),
-            "qk_norm_rope_kv_write": (qk, self.L, B * qkv_n * 2 + B * self.Hq * D * 2 + 2 * B * self.Hkv * D * 2, 0),
+            "qk_norm_rope_kv_write": (self._qk, self.L, B * qkv_n * 2 + B * self.Hq * D * 2 + 2 * B * self.Hkv * D * 2,
+                                      0),
             "fused_add_rmsnorm": (fadd, 2 * self.L, 5 * B * H * 2, 0),
             "sample": (samp, 1, B * self.V * 2, 0),
-        }
+        })
+        if self.final_softcap:
+            kinds["softcap"] = (lambda i: N.check(lib.mvb_softcap(self.logits.data_ptr(), B * self.V,
+                                                                  self.final_softcap, N.BF16, st), "softcap"),
+                                1, 2 * B * self.V * 2, 0)
+        return kinds
 
     def time_kernels(self, iters: int = 36) -> dict[str, dict]:
         """Average device time of each kernel kind: every launch bracketed by CUDA events on
@@ -518,10 +557,12 @@ class DecodeRunner:
 
     def algorithmic_step_bytes(self) -> int:
         """HBM bytes a decode step cannot avoid at the current context lengths: streamed weights,
-        K and V of every attended token in every layer, and the new token's K and V."""
-        ctx = int(self.ctx.cpu().sum())
-        kv_token = self.L * self.Hkv * self.D * 2 * 2
-        return self.w.streamed_bytes() + ctx * kv_token + self.B * kv_token
+        K and V of every attended token in every layer (a sliding-window layer attends to at most
+        its window), and the new token's K and V."""
+        ctx = self.ctx.cpu().tolist()
+        per_layer = self.Hkv * self.D * 2 * 2
+        attended = sum(sum(min(c, wnd) if wnd else c for c in ctx) for wnd in self.windows)
+        return self.w.streamed_bytes() + attended * per_layer + self.B * self.L * per_layer
 
     def launches_per_step(self) -> int:
         """Kernels one step launches: embedding, rmsnorm, 8 per layer (qkv, qk-norm/rope/kv, attention,
@@ -531,7 +572,7 @@ class DecodeRunner:
             return 2 + self.L * 11 + (self.L - 1) + 3
         if self.tp.enabled:   # + the step-counter kernel and the wait before sampling
             return 2 + self.L * 8 + (self.L - 1) + 3 + 2
-        return 2 + self.L * 8 + (self.L - 1) + 3
+        return 2 + self.L * 8 + (self.L - 1) + 3 + (1 if self.final_softcap else 0)
 
     # ------------------------------------------------------------------ graphs
     def capture(self) -> None:

@@ -51,7 +51,22 @@ def weight_shapes(cfg: dict) -> dict[str, tuple[int, ...]]:
             shapes[p + "mlp.down_proj.weight"] = (H, inter)
         shapes[p + "input_layernorm.weight"] = (H,)
         shapes[p + "post_attention_layernorm.weight"] = (H,)
+        if cfg.get("_has_feedforward_layernorms"):   # Gemma sandwich norms (gemma3_model.py:265-268)
+            shapes[p + "pre_feedforward_layernorm.weight"] = (H,)
+            shapes[p + "post_feedforward_layernorm.weight"] = (H,)
     return shapes
+
+
+def jitter_norms(sd: dict[str, torch.Tensor], seed: int = 1, std: float = 0.1) -> dict[str, torch.Tensor]:
+    """Adds seeded N(0, std) noise to every norm weight (in place of their constant init) so that
+    parity tests exercise the norm scales; same seed, same values on every side."""
+    gen = torch.Generator().manual_seed(seed)
+    out = dict(sd)
+    for key in sorted(sd):
+        if _is_norm(key):
+            t = sd[key]
+            out[key] = (t.float().cpu() + torch.randn(t.shape, generator=gen) * std).to(t.dtype).to(t.device)
+    return out
 
 
 def _is_norm(key: str) -> bool:

@@ -68,11 +68,14 @@ class OracleEngine:
 
     def __init__(self, cfg: dict, state_dict: dict, dtype: torch.dtype, num_blocks: int = 256,
                  block_size: int = 16, free_order: list[int] | None = None, device="cpu",
-                 sdpa_backend=None, prefill_last_only: bool = False):
+                 sdpa_backend=None, prefill_last_only: bool = False, capped_rounding: str = "fp32"):
         """``sdpa_backend`` (a ``torch.nn.attention.SDPBackend``) pins PyTorch's attention
         implementation -- the reference leaves the choice to PyTorch, so two backends are two
-        equally valid executions of the reference (used to measure its own rounding noise)."""
+        equally valid executions of the reference (used to measure its own rounding noise).
+        ``capped_rounding`` chooses how Gemma-2's soft-capped attention rounds (``OracleDecoder``):
+        "fp32" (one rounding) or "eager" (transformers' eager attention in the model dtype)."""
         self.model = OracleDecoder(cfg, state_dict, dtype, device)
+        self.model.capped_rounding = capped_rounding
         self.sdpa_backend = sdpa_backend
         self.prefill_last_only = prefill_last_only
         self.dtype = dtype

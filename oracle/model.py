@@ -3,7 +3,12 @@
 Follows ``mini_vllm/models/model.py`` (the PyTorch-path model the reference runs
 with ``MINI_VLLM_BACKEND=pytorch``) operation by operation, in the same dtype and
 with the same intermediate roundings, so that the CUDA path can be compared with
-it at bf16 tolerance and its KV-cache indexing bit for bit.
+it at bf16 tolerance and its KV-cache indexing bit for bit.  Gemma models follow
+``mini_vllm/models/gemma3_model.py`` (sandwich (1 + w) norms, GeGLU, sqrt(hidden)
+embedding scale, per-layer RoPE theta); the Gemma-2 features the reference does not
+have (attention / final logit soft-capping, sliding-window layers) are restated from
+Gemma-2's published definition and pinned to the transformers implementation
+(``tests/golden/make_gemma2_golden.py``).
 
 Weights come in as an HF-keyed state dict; ``gate_proj``/``up_proj`` stay separate
 as in ``model.py:106-117``.
@@ -14,6 +19,30 @@ import math
 
 import torch
 import torch.nn.functional as F
+
+
+def is_gemma(cfg: dict) -> bool:
+    """``loader.py:70``: model_type gemma3_text selects ``Gemma3ForCausalLM``; Gemma-2 shares its
+    layer structure (sandwich norms, GeGLU, embedding scale)."""
+    return cfg.get("model_type") in ("gemma2", "gemma3_text")
+
+
+def layer_rope_theta(cfg: dict, i: int) -> float:
+    """``gemma3_model.py:307-320``: layer i uses the global ``rope_theta`` when
+    ``i % pattern == pattern - 1`` and ``rope_local_base_freq`` otherwise; other models one theta."""
+    if cfg.get("model_type") == "gemma3_text":
+        pattern = cfg.get("sliding_window_pattern", 6)
+        return cfg.get("rope_theta", 1000000.0) if i % pattern == pattern - 1 else cfg.get("rope_local_base_freq",
+                                                                                            10000.0)
+    return cfg.get("rope_theta", 10000.0)
+
+
+def layer_window(cfg: dict, i: int) -> int:
+    """Gemma-2: even layers attend through a ``sliding_window``, odd layers globally (the
+    reference's Gemma 3 applies no window)."""
+    if cfg.get("model_type") == "gemma2" and cfg.get("sliding_window"):
+        return int(cfg["sliding_window"]) if i % 2 == 0 else 0
+    return 0
 
 
 # ----------------------------------------------------------------- primitives
@@ -142,17 +171,31 @@ class OracleDecoder:
         self.w = {k: v.to(device=self.device, dtype=dtype) for k, v in state_dict.items()}
         if "lm_head.weight" not in self.w:                                # tied (model.py:417-418)
             self.w["lm_head.weight"] = self.w["model.embed_tokens.weight"]
-        self._cos = self._sin = None
-        self._cache_len = 0
+        self.gemma = is_gemma(cfg)
+        if self.gemma:
+            self.plus_one = True
+        self.softcap = float(cfg.get("attn_logit_softcapping") or 0.0)
+        self.final_softcap = float(cfg.get("final_logit_softcapping") or 0.0)
+        self.thetas = [layer_rope_theta(cfg, i) for i in range(self.L)]
+        self.windows = [layer_window(cfg, i) for i in range(self.L)]
+        self._tables: dict[float, tuple[torch.Tensor, torch.Tensor, int]] = {}
+        # Gemma-2 soft-capped attention: "fp32" computes scores, softmax and p.v in fp32 and rounds
+        # once; "eager" rounds as transformers' eager attention does in the model dtype (scores and
+        # each soft-capping op in the dtype, fp32 softmax rounded to the dtype, p.v in the dtype).
+        # Both are executions of the same definition; their spread measures its rounding noise.
+        self.capped_rounding = "fp32"
 
-    # model.py:60-81 -- grow like the reference: max(seq_len, 2*cache_len, 256)
-    def rope(self, positions: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    # model.py:60-81 (gemma3_model.py:60-81, one cache per theta) -- grow like the reference:
+    # max(seq_len, 2*cache_len, 256)
+    def rope(self, positions: torch.Tensor, theta: float | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        theta = self.theta if theta is None else theta
         seq_len = int(positions.max().item()) + 1
-        if self._cos is None or self._cache_len < seq_len:
-            grow_to = max(seq_len, self._cache_len * 2, 256)
-            self._cos, self._sin = rope_tables(self.hd, self.theta, grow_to, self.dtype, self.device)
-            self._cache_len = grow_to
-        return self._cos[:seq_len], self._sin[:seq_len]
+        cos, sin, n = self._tables.get(theta, (None, None, 0))
+        if cos is None or n < seq_len:
+            grow_to = max(seq_len, n * 2, 256)
+            cos, sin = rope_tables(self.hd, theta, grow_to, self.dtype, self.device)
+            self._tables[theta] = (cos, sin, grow_to)
+        return cos[:seq_len], sin[:seq_len]
 
     # model.py:226-243
     @staticmethod
@@ -195,9 +238,9 @@ class OracleDecoder:
         k = F.linear(x, w[p + "k_proj.weight"], w.get(p + "k_proj.bias")).view(B, S, self.nkv, self.hd)
         v = F.linear(x, w[p + "v_proj.weight"], w.get(p + "v_proj.bias")).view(B, S, self.nkv, self.hd)
         v = v.transpose(1, 2)
-        if self.qk_norm:
-            q = rms_norm(q, w[p + "q_norm.weight"], self.eps)
-            k = rms_norm(k, w[p + "k_norm.weight"], self.eps)
+        if self.qk_norm:   # Gemma: the (1 + w) form (gemma3_model.py:135-136, :159-160)
+            q = rms_norm(q, w[p + "q_norm.weight"], self.eps, self.gemma)
+            k = rms_norm(k, w[p + "k_norm.weight"], self.eps, self.gemma)
         q, k = q.transpose(1, 2), k.transpose(1, 2)
         q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
         if kv_pool is not None and block_tables is not None and slot_idx is not None:
@@ -209,6 +252,10 @@ class OracleDecoder:
             k = k.repeat_interleave(g, dim=1)
             v = v.repeat_interleave(g, dim=1)
         sc = 1.0 / math.sqrt(self.scale)
+        if self.softcap or self.windows[i]:
+            o = self.capped_attention(q, k, v, sc, self.windows[i], num_cached if use_cache else None)
+            o = o.transpose(1, 2).contiguous().view(B, S, -1)
+            return F.linear(o, w[p + "o_proj.weight"], w.get(p + "o_proj.bias"))
         if attn_mask is not None:
             o = F.scaled_dot_product_attention(q, k, v, scale=sc, attn_mask=attn_mask)
         elif use_cache:
@@ -217,6 +264,40 @@ class OracleDecoder:
             o = F.scaled_dot_product_attention(q, k, v, scale=sc, is_causal=True)
         o = o.transpose(1, 2).contiguous().view(B, S, -1)
         return F.linear(o, w[p + "o_proj.weight"], w.get(p + "o_proj.bias"))
+
+    def capped_attention(self, q, k, v, scale, window, num_cached):
+        """Gemma-2 attention: scores ``q k^T * scale`` soft-capped (``cap * tanh(s / cap)``) before
+        the mask, then softmax and ``p v``; computed in fp32 and rounded once to the model dtype.
+        The mask keeps key j for query position t when j <= t and, in a sliding-window layer,
+        t - j < window.  Decode (``num_cached`` given): query b sits at position num_cached[b]
+        with keys 0..num_cached[b] valid; prefill: query i at position i (causal)."""
+        B, Hq, S, D = q.shape
+        T = k.shape[2]
+        eager = self.capped_rounding == "eager"
+        if eager:
+            s = torch.matmul(q, k.transpose(-1, -2)) * scale
+            if self.softcap:
+                s = torch.tanh(s / self.softcap) * self.softcap
+        else:   # fp32 throughout: autocast would otherwise run both products in the model dtype
+            with torch.autocast(device_type=q.device.type, enabled=False):
+                s = torch.matmul(q.float(), k.float().transpose(-1, -2)) * scale
+            if self.softcap:
+                s = self.softcap * torch.tanh(s / self.softcap)
+        j = torch.arange(T, device=s.device)
+        if num_cached is not None:
+            t = torch.tensor(num_cached, device=s.device).view(B, 1, 1, 1)     # query positions
+        else:
+            t = torch.arange(S, device=s.device).view(1, 1, S, 1)
+        keep = j.view(1, 1, 1, T) <= t
+        if window:
+            keep = keep & (t - j.view(1, 1, 1, T) < window)
+        s = s.masked_fill(~keep, float("-inf"))
+        if eager:
+            p = torch.softmax(s, dim=-1, dtype=torch.float32).to(q.dtype)
+            return torch.matmul(p, v)
+        with torch.autocast(device_type=q.device.type, enabled=False):
+            p = torch.softmax(s, dim=-1)
+            return torch.matmul(p, v.float()).to(q.dtype)
 
     def mlp(self, i, x):
         """``MLP.forward`` (``model.py:116-117``): ``down(act(gate(x)) * up(x))``."""
@@ -265,12 +346,22 @@ class OracleDecoder:
         (rows are independent there; it saves the ``S x V`` prefill projection)."""
         w = self.w
         h = F.embedding(input_ids, w["model.embed_tokens.weight"])
-        cos, sin = self.rope(positions)
-        cos, sin = cos[positions], sin[positions]
-        if cos.dim() == 3:
-            cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
-        else:
-            cos, sin = cos.unsqueeze(0).unsqueeze(0), sin.unsqueeze(0).unsqueeze(0)
+        if self.gemma:   # gemma3_model.py:295-299, :330: times the sqrt(hidden) buffer, which
+            # model.to(dtype) (loader.py:297) has cast to the model dtype
+            h = h * torch.tensor(math.sqrt(self.H), dtype=torch.float32).to(self.dtype)
+        tables = {}
+        for theta in dict.fromkeys(self.thetas):
+            cos, sin = self.rope(positions, theta)
+            cos, sin = cos[positions], sin[positions]
+            if cos.dim() == 3:
+                cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
+            else:
+                cos, sin = cos.unsqueeze(0).unsqueeze(0), sin.unsqueeze(0).unsqueeze(0)
+            tables[theta] = (cos, sin)
+        if self.gemma:
+            return self._forward_gemma(h, tables, kv_pool, block_tables, slot_idx, use_cache, num_cached, attn_mask,
+                                       return_hidden, last_only)
+        cos, sin = tables[self.theta]
         for i in range(self.L):
             p = f"model.layers.{i}."
             r = h
@@ -285,4 +376,31 @@ class OracleDecoder:
             h = h[:, -1:]
         h = rms_norm(h, w["model.norm.weight"], self.eps, self.plus_one)
         logits = F.linear(h, w["lm_head.weight"])
+        return (logits, h) if return_hidden else logits
+
+    def _forward_gemma(self, h, tables, kv_pool, block_tables, slot_idx, use_cache, num_cached, attn_mask,
+                       return_hidden, last_only):
+        """``Gemma3DecoderLayer.forward`` (gemma3_model.py:270-283) for every layer, the final norm
+        and lm_head (``:345-372``), then Gemma-2's final soft-capping ``cap * tanh(x / cap)`` as
+        the three ops ``x / cap``, ``tanh``, ``* cap`` in the logits' dtype."""
+        w = self.w
+        for i in range(self.L):
+            p = f"model.layers.{i}."
+            cos, sin = tables[self.thetas[i]]
+            r = h
+            x = rms_norm(h, w[p + "input_layernorm.weight"], self.eps, True)
+            x = self.attention(i, x, cos, sin, kv_pool, block_tables, slot_idx, use_cache, num_cached, attn_mask)
+            x = rms_norm(x, w[p + "post_attention_layernorm.weight"], self.eps, True)
+            h = r + x
+            r = h
+            x = rms_norm(h, w[p + "pre_feedforward_layernorm.weight"], self.eps, True)
+            x = self.mlp(i, x)
+            x = rms_norm(x, w[p + "post_feedforward_layernorm.weight"], self.eps, True)
+            h = r + x
+        if last_only:
+            h = h[:, -1:]
+        h = rms_norm(h, w["model.norm.weight"], self.eps, True)
+        logits = F.linear(h, w["lm_head.weight"])
+        if self.final_softcap:
+            logits = torch.tanh(logits / self.final_softcap) * self.final_softcap
         return (logits, h) if return_hidden else logits

@@ -15,6 +15,9 @@ PyTorch path (``MINI_VLLM_BACKEND=pytorch``, ``mini_vllm/ops/_utils.py:74``):
   greedy 24 tokens, full per-step logits.
 * ``decode_moe_tiny_f32.pt`` -- a 2-layer Qwen3-MoE model (``models/qwen3_moe_model.py``,
   16 experts, top-4) in fp32: its MoE block alone, and greedy decoding with full logits.
+* ``decode_gemma3_tiny.pt`` -- the reference's Gemma 3 model (``models/gemma3_model.py``, head
+  dim 256, QK-norm, local/global RoPE theta) with seeded non-trivial norm weights: greedy
+  decoding in fp32 and in bf16, full logits.
 
 Usage (only where the reference is mounted):
     python tests/golden/make_golden.py [--reference /root/reference]
@@ -40,7 +43,7 @@ REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO))
 
 from llm_pytorch_inference_b200.configs import get_config, head_dim, num_kv_heads  # noqa: E402
-from llm_pytorch_inference_b200.weights import canonical_state_dict  # noqa: E402
+from llm_pytorch_inference_b200.weights import canonical_state_dict, jitter_norms  # noqa: E402
 
 
 def _import_reference(path: str):
@@ -160,7 +163,8 @@ def make_kv_golden() -> dict:
 
 
 # ------------------------------------------------------------------------- decode
-def _build_reference_engine(cfg: dict, dtype: torch.dtype, num_blocks: int, pool_seed: int = 0):
+def _build_reference_engine(cfg: dict, dtype: torch.dtype, num_blocks: int, pool_seed: int = 0,
+                            norm_jitter: int | None = None):
     from mini_vllm.models.loader import _ensure_builtin_models, _BUILTIN_MODELS
     from mini_vllm.engine.engine import LLMEngine
     from mini_vllm.engine.kv_cache import KVCacheManager
@@ -171,6 +175,8 @@ def _build_reference_engine(cfg: dict, dtype: torch.dtype, num_blocks: int, pool
     _ensure_builtin_models()
     model = _BUILTIN_MODELS[cfg["model_type"]](dict(cfg))
     sd = canonical_state_dict(cfg, seed=0, dtype=torch.float32)
+    if norm_jitter is not None:
+        sd = jitter_norms(sd, norm_jitter)
     missing, unexpected = model.load_state_dict(sd, strict=False)
     assert not unexpected, unexpected
     assert all(k == "lm_head.weight" for k in missing), missing
@@ -209,11 +215,11 @@ class _Recorder(torch.nn.Module):
         return logits
 
 
-def run_reference_decode(cfg, dtype, prompts, max_tokens, num_blocks=256):
+def run_reference_decode(cfg, dtype, prompts, max_tokens, num_blocks=256, norm_jitter=None):
     from mini_vllm.engine.sequence import Sequence
     from mini_vllm.utils.config import SamplingParams
 
-    eng = _build_reference_engine(cfg, dtype, num_blocks)
+    eng = _build_reference_engine(cfg, dtype, num_blocks, norm_jitter=norm_jitter)
     rec = _Recorder(eng.model)
     eng.model = rec
     seqs = []
@@ -229,8 +235,8 @@ def run_reference_decode(cfg, dtype, prompts, max_tokens, num_blocks=256):
     return seqs, rec.calls
 
 
-def _decode_fixture(cfg, dtype, prompts, max_tokens, keep_full_logits):
-    seqs, calls = run_reference_decode(cfg, dtype, prompts, max_tokens)
+def _decode_fixture(cfg, dtype, prompts, max_tokens, keep_full_logits, norm_jitter=None):
+    seqs, calls = run_reference_decode(cfg, dtype, prompts, max_tokens, norm_jitter=norm_jitter)
     prefill = [c for c in calls if not c["use_cache"]]
     decode = [c for c in calls if c["use_cache"]]
     fx: dict = {
@@ -279,6 +285,22 @@ def make_moe_golden() -> dict:
     return fx
 
 
+def make_gemma3_golden() -> dict:
+    """The reference's Gemma 3 model (``model_type`` gemma3_text, ``loader.py:70``) through
+    ``LLMEngine._step``, in fp32 and bf16, with norm weights jittered (seed 1) so that every
+    (1 + w) scale matters."""
+    cfg = get_config("gemma3-tiny")
+    g = torch.Generator().manual_seed(17)
+    lens = [37, 50, 16, 64]
+    prompts = [torch.randint(0, cfg["vocab_size"], (n,), generator=g).tolist() for n in lens]
+    out = {"arch": "gemma3-tiny", "norm_jitter": 1}
+    for dt, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
+        fx = _decode_fixture(cfg, dt, prompts, 16, keep_full_logits=True, norm_jitter=1)
+        out.update({f"{k}_{tag}": v for k, v in fx.items()})
+    out["prompts"] = out["prompts_f32"]
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -309,6 +331,9 @@ def main() -> None:
     if want("moe"):
         torch.save(make_moe_golden(), HERE / "decode_moe_tiny_f32.pt")
         print("decode_moe_tiny_f32.pt written")
+    if want("gemma3"):
+        torch.save(make_gemma3_golden(), HERE / "decode_gemma3_tiny.pt")
+        print("decode_gemma3_tiny.pt written")
     if want("cfg1"):
         cfg = get_config("qwen3-0.6b")
         g = torch.Generator().manual_seed(0)

@@ -29,14 +29,18 @@ pytestmark = pytest.mark.gpu
 MAX_ABS, MEAN_ABS = 2e-2, 2e-3
 
 
-def _setup(arch, prompts, num_blocks, seed=0):
+def _setup(arch, prompts, num_blocks, seed=0, norm_jitter=None):
     cfg = get_config(arch)
     sd = canonical_state_dict(cfg, seed, torch.float32)
+    if norm_jitter is not None:
+        from llm_pytorch_inference_b200.weights import jitter_norms
+
+        sd = jitter_norms(sd, norm_jitter)
     order = list(range(num_blocks))
     random.Random(seed).shuffle(order)
     oracle = OracleEngine(cfg, sd, torch.bfloat16, num_blocks, 16, list(order), prefill_last_only=True)
     alt = OracleEngine(cfg, sd, torch.bfloat16, num_blocks, 16, list(order), sdpa_backend=SDPBackend.MATH,
-                       prefill_last_only=True)
+                       prefill_last_only=True, capped_rounding="eager")
     first = []
     for i, p in enumerate(prompts):
         first.append(int(osamp.greedy(oracle.prefill(i, p)[None])[0]))

@@ -275,7 +275,7 @@ def test_qk_norm_rope_kv_write_from_split_k_partials_bit_exact():
     q_b = torch.empty_like(q_a)
     N.check(N.lib().mvb_qk_norm_rope_kv_write_gemm(
         q_b.data_ptr(), pool_b.data_ptr(), ws.data_ptr(), H, qn.data_ptr(), kn.data_ptr(), cos.data_ptr(),
-        sin.data_ptr(), cos.shape[0], pos.data_ptr(), bt.data_ptr(), 4, B, Hq, Hkv, D, L, 1, P + 1, 16, 1e-6,
+        sin.data_ptr(), cos.shape[0], pos.data_ptr(), bt.data_ptr(), 4, B, Hq, Hkv, D, L, 1, P + 1, 16, 1e-6, 0,
         N.stream_handle()), "qk gemm")
     assert torch.equal(q_a, q_b) and torch.equal(pool_a, pool_b)
 
@@ -293,17 +293,22 @@ def test_kv_write_bad_block_is_reported_not_faulted():
 
 
 # ------------------------------------------------------------ paged attention
-def _attention_ref(q, pool, layer, bts, ctx, scale):
-    """fp32 restatement of _read_kv_cache_batch + SDPA (model.py:191-221)."""
+def _attention_ref(q, pool, layer, bts, ctx, scale, softcap=0.0, window=0):
+    """fp32 restatement of _read_kv_cache_batch + SDPA (model.py:191-221); ``softcap`` and
+    ``window`` as Gemma-2 applies them (scores soft-capped before the mask; a sliding window
+    keeps the newest ``window`` keys)."""
     B, Hq, D = q.shape
     Hkv = pool.shape[4]
     out = torch.empty(B, Hq, D)
     for b in range(B):
         k = torch.cat([pool[layer, 0, blk] for blk in bts[b]], 0)[:ctx[b]].float()   # [ctx, Hkv, D]
         v = torch.cat([pool[layer, 1, blk] for blk in bts[b]], 0)[:ctx[b]].float()
-        k = k.repeat_interleave(Hq // Hkv, dim=1)
-        v = v.repeat_interleave(Hq // Hkv, dim=1)
+        lo = max(0, ctx[b] - window) if window else 0
+        k = k[lo:].repeat_interleave(Hq // Hkv, dim=1)
+        v = v[lo:].repeat_interleave(Hq // Hkv, dim=1)
         s = torch.einsum("hd,thd->ht", q[b].float(), k) * scale
+        if softcap:
+            s = softcap * torch.tanh(s / softcap)
         p = torch.softmax(s, -1)
         out[b] = torch.einsum("ht,thd->hd", p, v)
     return out
@@ -343,6 +348,46 @@ def test_paged_attention_matches_fp32_reference(Hq, Hkv, lens):
     out2 = ops.paged_attention_decode(q.to(DEV), pool.to(DEV), layer, bt.to(DEV),
                                       torch.tensor(lens, dtype=torch.int32, device=DEV), scale)
     assert torch.equal(out, out2)  # deterministic split-KV merge
+
+
+@pytest.mark.parametrize("D,Hq,Hkv,lens,softcap,window", [
+    (256, 16, 8, [8193] * 4 + [1, 16, 17, 300], 50.0, 0),     # Gemma-2-9B heads: global layer
+    (256, 16, 8, [8193] * 4 + [1, 16, 17, 300], 50.0, 4096),  # ... sliding-window layer
+    (256, 16, 8, [4096, 4097, 4111, 4112, 4113], 0.0, 4096),  # window edges around block bounds
+    (256, 4, 2, [37, 50, 16, 64], 0.0, 0),                    # Gemma-3 test model heads
+    (256, 2, 1, [2049] * 6 + [5], 50.0, 1000),                # one KV head (TP=8 shard), odd window
+    (256, 32, 4, [700, 33], 30.0, 0),                         # group 8
+    (128, 32, 8, [2049] * 3 + [1, 300], 50.0, 1024),          # head_dim 128 with both options
+    (128, 8, 2, [1200] * 4, 0.0, 17),
+])
+def test_paged_attention_softcap_window_head_dim_256(D, Hq, Hkv, lens, softcap, window):
+    L, layer = 2, 1
+    total_blocks = sum((n + 15) // 16 for n in lens)
+    P = total_blocks + 7
+    order = list(range(P))
+    random.Random(6).shuffle(order)
+    it = iter(order)
+    bts = [[next(it) for _ in range((n + 15) // 16)] for n in lens]
+    mb = max(len(b) for b in bts)
+    bt = torch.full((len(lens), mb), P, dtype=torch.int32)
+    for i, b in enumerate(bts):
+        bt[i, :len(b)] = torch.tensor(b)
+    pool = _pool(L, P, Hkv, D, 10)
+    g = torch.Generator().manual_seed(8)
+    q = (torch.randn(len(lens), Hq, D, generator=g) * (6 if softcap else 1)).to(torch.bfloat16)  # scores ~ +-20
+    scale = 1.0 / math.sqrt(D)
+    ctx = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    out = ops.paged_attention_decode(q.to(DEV), pool.to(DEV), layer, bt.to(DEV), ctx, scale, softcap=softcap,
+                                     window=window)
+    assert N.device_status(clear=True) == 0
+    ref = _attention_ref(q, pool, layer, bts, lens, scale, softcap, window)
+    torch.testing.assert_close(out.cpu().float(), ref, rtol=2e-2, atol=1e-2)
+    if softcap or (window and 2 * window <= max(lens)):   # the options change the result
+        plain = _attention_ref(q, pool, layer, bts, lens, scale)
+        assert (plain - ref).abs().max() > 5e-2
+    out2 = ops.paged_attention_decode(q.to(DEV), pool.to(DEV), layer, bt.to(DEV), ctx, scale, softcap=softcap,
+                                      window=window)
+    assert torch.equal(out, out2)
 
 
 # --------------------------------------------------------------------- sampling

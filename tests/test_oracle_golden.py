@@ -148,3 +148,53 @@ def test_decode_moe_tiny_fp32_matches_reference(golden_dir):
     torch.testing.assert_close(torch.stack(step_logits), fx["decode_logits"], rtol=1e-5, atol=1e-5)
     bts = json.loads(fx["decode_block_tables"])
     assert [eng.blocks.get_block_table(s) for s in range(4)] == bts[-1]
+
+
+@pytest.mark.parametrize("tag,dtype", [("f32", torch.float32), ("bf16", torch.bfloat16)])
+def test_decode_gemma3_tiny_matches_reference(golden_dir, tag, dtype):
+    """Greedy decoding of the reference's own Gemma 3 model (``models/gemma3_model.py``: head dim
+    256, QK-norm and sandwich norms in the (1 + w) form, local/global RoPE theta, sqrt(hidden)
+    embedding scale, GeGLU) through ``LLMEngine._step``, with jittered norm weights."""
+    from llm_pytorch_inference_b200.weights import jitter_norms
+
+    fx = torch.load(golden_dir / "decode_gemma3_tiny.pt")
+    cfg = get_config(fx["arch"])
+    order = list(range(256))
+    random.Random(0).shuffle(order)
+    sd = jitter_norms(canonical_state_dict(cfg, 0, torch.float32), fx["norm_jitter"])
+    eng = OracleEngine(cfg, sd, dtype, 256, 16, order)
+    prompts = [p.tolist() for p in fx["prompts"]]
+    out, step_logits = eng.generate_greedy(prompts, 16)
+    assert torch.equal(torch.tensor(out), fx[f"output_tokens_{tag}"])
+    L = torch.stack(step_logits)
+    ref = fx[f"decode_logits_{tag}"].float()
+    if dtype == torch.float32:
+        torch.testing.assert_close(L, ref, rtol=1e-5, atol=1e-5)
+    else:   # host-dependent CPU bf16 GEMM rounding, as for the Qwen3 bf16 fixture
+        d = (L.to(torch.bfloat16).float() - ref).abs()
+        assert float(d.max()) <= 2e-2 and float(d.mean()) <= 2.5e-3, (float(d.max()), float(d.mean()))
+    bts = json.loads(fx[f"decode_block_tables_{tag}"])
+    assert [eng.blocks.get_block_table(s) for s in range(4)] == bts[-1]
+
+
+def test_gemma2_features_match_transformers(golden_dir):
+    """Soft-capping (attention 50, final 30), alternating 32-token sliding-window layers, sandwich
+    norms and GeGLU of the oracle's Gemma-2 path against transformers' ``Gemma2ForCausalLM``
+    (fp32, eager attention; tests/golden/make_gemma2_golden.py): greedy tokens and every step's
+    logits, prefill included, with prompts longer than the window."""
+    from llm_pytorch_inference_b200.weights import jitter_norms
+
+    fx = torch.load(golden_dir / "gemma2_tiny_hf_f32.pt")
+    cfg = get_config(fx["arch"])
+    eng = OracleEngine(cfg, jitter_norms(canonical_state_dict(cfg, 0, torch.float32)), torch.float32, 128)
+    prompts = [p.tolist() for p in fx["prompts"]]
+    first = [eng.prefill(s, p) for s, p in enumerate(prompts)]
+    torch.testing.assert_close(torch.stack(first), fx["logits"][:, 0], rtol=1e-5, atol=1e-5)
+    for s in range(len(prompts)):
+        eng.append(s, int(fx["tokens"][s, 0]))
+    for step in range(1, fx["tokens"].shape[1]):
+        lg = eng.decode(list(range(len(prompts))))
+        torch.testing.assert_close(lg, fx["logits"][:, step], rtol=1e-5, atol=1e-5)
+        assert torch.equal(torch.argmax(lg, -1), fx["tokens"][:, step])
+        for s in range(len(prompts)):
+            eng.append(s, int(fx["tokens"][s, step]))
