@@ -57,7 +57,11 @@ def parse_args(argv=None):
     ap.add_argument("--case", default=None, choices=["kernels", "moe", "gemma2"],
                     help="kernels: small profiling case (2 layers of the workload's dims), each kernel kind "
                          "launched a few times; prints per-kernel timings only.  moe: the sparse-MoE decode "
-                         "workload (Qwen3-30B-A3B arch, batch 32, prompt 4096, greedy), 1 GPU")
+                         "workload (Qwen3-30B-A3B arch, batch 32, prompt 4096, greedy), 1 GPU.  gemma2: the "
+                         "Gemma-2-9B-arch decode workload (batch 16, prompt 8192, greedy), 1 GPU")
+    ap.add_argument("--arch", default=None, choices=["qwen3-8b", "gemma2-9b"],
+                    help="--case kernels: the layer dims (qwen3-8b: batch 64, prompt 2048; gemma2-9b: batch 16, "
+                         "prompt 8192)")
     return ap.parse_args(argv)
 
 
@@ -380,9 +384,10 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
 
 def run_kernel_case(args) -> None:
     """Profiling case: Qwen3-8B layer dims with 2 layers, batch 64, context 2048 (537 MB of KV per
-    layer, above the 126 MB L2), ~4.5 GB on the device.  One full decode step runs first (2 attention
-    and 9 GEMM launches), then every kernel kind of the step is launched 1 + 3 times (first launch
-    = warm-up), in the order of DecodeRunner.kernel_kinds()."""
+    layer, above the 126 MB L2), ~4.5 GB on the device; or (``--arch gemma2-9b``) Gemma-2-9B layer
+    dims with 2 layers (one sliding-window, one global), batch 16, context 8192 (1.07 GB of KV per
+    layer), ~4.5 GB.  One full decode step runs first, then every kernel kind of the step is launched
+    1 + 3 times (first launch = warm-up), in the order of DecodeRunner.kernel_kinds()."""
     from llm_pytorch_inference_b200 import _native as N
     from llm_pytorch_inference_b200.configs import get_config
     from llm_pytorch_inference_b200.engine import DecodeEngine
@@ -391,14 +396,16 @@ def run_kernel_case(args) -> None:
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     N.set_pdl(bool(args.pdl))
-    cfg = get_config(ARCH, num_hidden_layers=2)
+    arch = args.arch or ARCH
+    batch, prompt = (BATCH, PROMPT) if arch == ARCH else (16, 8192)
+    cfg = get_config(arch, num_hidden_layers=2)
     sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev)
-    nblk = BATCH * ((PROMPT + 2 + 15) // 16) + 64
-    eng = DecodeEngine(cfg, sd, max_batch=BATCH, max_model_len=PROMPT + 64, num_blocks=nblk, device=dev)
+    nblk = batch * ((prompt + 2 + 15) // 16) + 64
+    eng = DecodeEngine(cfg, sd, max_batch=batch, max_model_len=prompt + 64, num_blocks=nblk, device=dev)
     del sd
     g = torch.Generator().manual_seed(1)
-    for s in range(BATCH):
-        eng.add_sequence(s, torch.randint(0, cfg["vocab_size"], (PROMPT,), generator=g).tolist())
+    for s in range(batch):
+        eng.add_sequence(s, torch.randint(0, cfg["vocab_size"], (prompt,), generator=g).tolist())
         eng.append_first_token(s, 1)
     eng.prefill_synthetic(seed=0)
     eng.set_sampling(*SAMPLING, seed=1234)

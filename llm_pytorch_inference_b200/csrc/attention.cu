@@ -176,13 +176,12 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, 1)
   uint64_t* empty = full + STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + STAGES);
   volatile int* last_flag = abort_flag + 1;
-  int* cu = const_cast<int*>(abort_flag + 2);  // [batch + 1] block prefix sums
+  const int nv = a.batch * a.nhg;  // virtual sequences: (sequence, head group), head groups adjacent
+  int* cu = const_cast<int*>(abort_flag + 2);  // [nv + 1] block prefix sums
   // split-sequence merge scratch and per-head combine (W > 1), each 16-byte aligned (float2 use)
-  float* merge_smem =
-      reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(cu + a.batch + 1) + 15) & ~uintptr_t(15));
+  float* merge_smem = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(cu + nv + 1) + 15) & ~uintptr_t(15));
   float* combine_smem = reinterpret_cast<float*>(
       (reinterpret_cast<uintptr_t>(merge_smem + attn_merge_floats<GROUP, HKV>()) + 15) & ~uintptr_t(15));
-  const int nv = a.batch * a.nhg;  // virtual sequences: (sequence, head group), head groups adjacent
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
