@@ -15,13 +15,13 @@
 // the GPU).  A sequence that spans several CTAs is merged by the last CTA to finish it,
 // combining the partial (max, sum, output) triples in CTA order, so results are deterministic.
 //
-// CTA = 8 consumer warps (4 at D = 256) + 1 producer warp.  The producer streams each block's
+// CTA = 8 consumer warps (4 at D = 256 and for D = 128 groups of <= 2 heads) + 1 producer warp.  The producer streams each block's
 // K and V (the head group's heads) through TMA into a 128-byte-swizzled image of 128-byte lines
 // (head_dim split into parts of 64).  It issues one copy per (K|V, part), image
 // [kv][part][head][token][64]; only for D = 128 blocks of one or two heads (tensor-parallel
 // shards, 4-8 KB) is the per-copy cost worth saving, with one 5-D copy per block, image
 // [kv][token][head, part][64].  Consumer warp (h, w) serves KV head h -- its GROUP query heads
-// are the columns of an m16n8 tile -- and with W = 8 / HKV (4 / HKV) warps per head takes every
+// are the columns of an m16n8 tile -- and with W = (consumer warps) / HKV warps per head takes every
 // W-th block of the CTA's range, so a GPU holding few KV heads (tensor parallelism) still runs
 // every consumer warp; the W partial softmax states of a head are combined in shared memory at
 // each sequence boundary.
@@ -125,10 +125,13 @@ __host__ __device__ constexpr int attn_consumer_warps() {
 }
 
 // Consumer warps per KV head: all consumer warps of the CTA shared by its HKV heads, as long as
-// the merge's per-thread share (GROUP * D / (W * 32) outputs) stays whole.
+// the merge's per-thread share (GROUP * D / (W * 32) outputs) stays whole.  Blocks of one or two
+// D = 128 heads (4-8 KB) take 4 consumer warps instead of 8: each warp then owns twice as many
+// stages ahead of it (25.7 instead of 27.4 us at one KV head, batch 64, context 2049).
 template <int GROUP, int HKV, int D>
 __host__ __device__ constexpr int attn_wph() {
-  return (attn_consumer_warps<D>() / HKV) < GROUP * (D / 32) ? (attn_consumer_warps<D>() / HKV) : GROUP * (D / 32);
+  constexpr int cw = (D == 128 && HKV <= 2) ? 4 : attn_consumer_warps<D>();
+  return (cw / HKV) < GROUP * (D / 32) ? (cw / HKV) : GROUP * (D / 32);
 }
 
 // One TMA copy per block (D = 128 blocks of <= 2 heads) or one per (K|V, part).  Several small
@@ -161,7 +164,9 @@ __host__ __device__ constexpr int attn_combine_bytes() {
   return attn_wph<GROUP, HKV, D>() > 1 ? HKV * attn_wph<GROUP, HKV, D>() * GROUP * (D + 2) * 4 : 0;
 }
 
-template <int GROUP, int HKV, int STAGES, int D>
+// CAP: soft-capped scores (a compile-time switch: the tanh would otherwise be evaluated for
+// every score of every launch).
+template <int GROUP, int HKV, int STAGES, int D, bool CAP>
 __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, 1)
     paged_attention_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs a) {
   constexpr int NP = D / 64;                                      // 64-dim parts of a head
@@ -274,7 +279,8 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, 1)
         for (int i = 0; i < n; ++i) {
           const int bi = __shfl_sync(0xffffffffu, blk, i);
           const int li = __shfl_sync(0xffffffffu, last, i);
-          const int hg = __shfl_sync(0xffffffffu, b_lane, i) % a.nhg;  // head group of the block
+          // head group of the block (at D = 128 a stage holds all KV heads: one group)
+          const int hg = D == 128 ? 0 : __shfl_sync(0xffffffffu, b_lane, i) % a.nhg;
           int good = 1;
           if (lane == 0) {
             if (li && !waited) {  // this block holds the token the previous kernel wrote
@@ -390,7 +396,12 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const float raw = sacc[0][c] + sacc[1][c] + sacc[2][c] + sacc[3][c];
-          const float sc = a.cap_log2 > 0.0f ? a.cap_log2 * tanhf(raw * a.cap_scale) : raw * a.scale_log2;
+          float sc;
+          if constexpr (CAP) {
+            sc = a.cap_log2 * tanhf(raw * a.cap_scale);
+          } else {
+            sc = raw * a.scale_log2;
+          }
           x[c] = (c < 2 ? ka : kb) ? sc : -INFINITY;
         }
         // Column (head) maxima over the 16 tokens: this thread's two rows, then the 8 g lanes.
@@ -454,8 +465,8 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, 1)
       float ma = m_a, la = l_a, mb = m_b, lb = l_b;
       if constexpr (W > 1) {
         // Combine the W warps of head h: each publishes (m, l, o) of its GROUP heads as rows of
-        // D + 2 floats; warp w == 0 merges them (a warp that had no block in the segment
-        // contributes m = -inf, l = 0, o = 0).
+        // D + 2 floats (a warp that had no block in the segment contributes m = -inf, l = 0,
+        // o = 0), then each merges a share of the dims.
         constexpr int RS = D + 2;
         float* mine = combine_smem + static_cast<int64_t>(warp) * GROUP * RS;
         if (g == 0) {
@@ -481,87 +492,92 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, 1)
           }
         }
         head_bar<W>(h);
-        if (w == 0) {
-          const float* base = combine_smem + static_cast<int64_t>(h * W) * GROUP * RS;
-          float Ma = -INFINITY, Mb = -INFINITY;
+        // Every warp merges the dims it owns (m-tiles n with n % W == w) for the head's GROUP query
+        // heads; the per-head max and denominator are formed redundantly by all W warps.
+        const float* base = combine_smem + static_cast<int64_t>(h * W) * GROUP * RS;
+        float Ma = -INFINITY, Mb = -INFINITY;
 #pragma unroll
-          for (int ww = 0; ww < W; ++ww) {
-            if (va) Ma = fmaxf(Ma, base[ww * GROUP * RS + ha * RS]);
-            if (vb) Mb = fmaxf(Mb, base[ww * GROUP * RS + hb * RS]);
-          }
-          float La = 0.0f, Lb = 0.0f;
+        for (int ww = 0; ww < W; ++ww) {
+          if (va) Ma = fmaxf(Ma, base[ww * GROUP * RS + ha * RS]);
+          if (vb) Mb = fmaxf(Mb, base[ww * GROUP * RS + hb * RS]);
+        }
+        float La = 0.0f, Lb = 0.0f;
+#pragma unroll 1
+        for (int ww = 0; ww < W; ++ww) {
+          const float* r = base + ww * GROUP * RS;
+          if (va && r[ha * RS] != -INFINITY) La += r[ha * RS + 1] * exp2f(r[ha * RS] - Ma);
+          if (vb && r[hb * RS] != -INFINITY) Lb += r[hb * RS + 1] * exp2f(r[hb * RS] - Mb);
+        }
 #pragma unroll
-          for (int n = 0; n < D / 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
-#pragma unroll
+        for (int n = 0; n < D / 16; ++n) {
+          if (n % W != w) continue;
+          float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+#pragma unroll 1
           for (int ww = 0; ww < W; ++ww) {
             const float* r = base + ww * GROUP * RS;
-            if (va) {
-              const float sc = r[ha * RS] == -INFINITY ? 0.0f : exp2f(r[ha * RS] - Ma);
-              La += r[ha * RS + 1] * sc;
-#pragma unroll
-              for (int n = 0; n < D / 16; ++n) {
-                o[n][0] += r[ha * RS + 2 + 16 * n + g] * sc;
-                o[n][2] += r[ha * RS + 2 + 16 * n + g + 8] * sc;
-              }
+            if (va && r[ha * RS] != -INFINITY) {
+              const float sc = exp2f(r[ha * RS] - Ma);
+              s0 += r[ha * RS + 2 + 16 * n + g] * sc;
+              s2 += r[ha * RS + 2 + 16 * n + g + 8] * sc;
             }
-            if (vb) {
-              const float sc = r[hb * RS] == -INFINITY ? 0.0f : exp2f(r[hb * RS] - Mb);
-              Lb += r[hb * RS + 1] * sc;
-#pragma unroll
-              for (int n = 0; n < D / 16; ++n) {
-                o[n][1] += r[hb * RS + 2 + 16 * n + g] * sc;
-                o[n][3] += r[hb * RS + 2 + 16 * n + g + 8] * sc;
-              }
+            if (vb && r[hb * RS] != -INFINITY) {
+              const float sc = exp2f(r[hb * RS] - Mb);
+              s1 += r[hb * RS + 2 + 16 * n + g] * sc;
+              s3 += r[hb * RS + 2 + 16 * n + g + 8] * sc;
             }
           }
-          ma = Ma;
-          la = La;
-          mb = Mb;
-          lb = Lb;
+          o[n][0] = s0;
+          o[n][1] = s1;
+          o[n][2] = s2;
+          o[n][3] = s3;
         }
+        ma = Ma;
+        la = La;
+        mb = Mb;
+        lb = Lb;
         head_bar<W>(h);  // the area is rewritten by the next segment
       }
+      // m-tiles this warp writes: all of them, or after a W-warp combine those with n % W == w.
+      auto owns = [&](int n) { return W == 1 || n % W == w; };
       const bool whole = (gpos == seq_lo) && (seg_end == seq_hi);
       if (whole) {
-        if (w == 0) {
-          __nv_bfloat16* op = a.out + static_cast<int64_t>(b) * a.out_stride + static_cast<int64_t>(hq0) * D;
-          const float ia = va ? 1.0f / la : 0.0f, ib = vb ? 1.0f / lb : 0.0f;
+        __nv_bfloat16* op = a.out + static_cast<int64_t>(b) * a.out_stride + static_cast<int64_t>(hq0) * D;
+        const float ia = va ? 1.0f / la : 0.0f, ib = vb ? 1.0f / lb : 0.0f;
 #pragma unroll
-          for (int n = 0; n < D / 16; ++n) {
-            const int d0 = 16 * n + g;
-            if (va) {
-              op[ha * D + d0] = __float2bfloat16_rn(o[n][0] * ia);
-              op[ha * D + d0 + 8] = __float2bfloat16_rn(o[n][2] * ia);
-            }
-            if (vb) {
-              op[hb * D + d0] = __float2bfloat16_rn(o[n][1] * ib);
-              op[hb * D + d0 + 8] = __float2bfloat16_rn(o[n][3] * ib);
-            }
+        for (int n = 0; n < D / 16; ++n) {
+          if (!owns(n)) continue;
+          const int d0 = 16 * n + g;
+          if (va) {
+            op[ha * D + d0] = __float2bfloat16_rn(o[n][0] * ia);
+            op[ha * D + d0 + 8] = __float2bfloat16_rn(o[n][2] * ia);
+          }
+          if (vb) {
+            op[hb * D + d0] = __float2bfloat16_rn(o[n][1] * ib);
+            op[hb * D + d0 + 8] = __float2bfloat16_rn(o[n][3] * ib);
           }
         }
       } else {
         const int slot = (g_begin >= seq_lo) ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
-        if (w == 0) {
-          // query heads h*GROUP + ha / hb within the head group
-          float* po = a.partial_o + (static_cast<int64_t>(slot) * HQ + h * GROUP) * D;
-          const float ia = va ? 1.0f / la : 0.0f, ib = vb ? 1.0f / lb : 0.0f;
+        // query heads h*GROUP + ha / hb within the head group
+        float* po = a.partial_o + (static_cast<int64_t>(slot) * HQ + h * GROUP) * D;
+        const float ia = va ? 1.0f / la : 0.0f, ib = vb ? 1.0f / lb : 0.0f;
 #pragma unroll
-          for (int n = 0; n < D / 16; ++n) {
-            const int d0 = 16 * n + g;
-            if (va) {
-              __stcg(po + ha * D + d0, o[n][0] * ia);
-              __stcg(po + ha * D + d0 + 8, o[n][2] * ia);
-            }
-            if (vb) {
-              __stcg(po + hb * D + d0, o[n][1] * ib);
-              __stcg(po + hb * D + d0 + 8, o[n][3] * ib);
-            }
+        for (int n = 0; n < D / 16; ++n) {
+          if (!owns(n)) continue;
+          const int d0 = 16 * n + g;
+          if (va) {
+            __stcg(po + ha * D + d0, o[n][0] * ia);
+            __stcg(po + ha * D + d0 + 8, o[n][2] * ia);
           }
-          float2* pml = a.partial_ml + static_cast<int64_t>(slot) * HQ + h * GROUP;
-          if (g == 0) {
-            if (va) __stcg(pml + ha, make_float2(ma, la));
-            if (vb) __stcg(pml + hb, make_float2(mb, lb));
+          if (vb) {
+            __stcg(po + hb * D + d0, o[n][1] * ib);
+            __stcg(po + hb * D + d0 + 8, o[n][3] * ib);
           }
+        }
+        float2* pml = a.partial_ml + static_cast<int64_t>(slot) * HQ + h * GROUP;
+        if (w == 0 && g == 0) {
+          if (va) __stcg(pml + ha, make_float2(ma, la));
+          if (vb) __stcg(pml + hb, make_float2(mb, lb));
         }
         __threadfence();
         consumer_bar<NCW>();
@@ -716,24 +732,30 @@ size_t attn_smem(int nv) {
          1024;
 }
 
-template <int GROUP, int HKV, int D>
-int launch_attn(const CUtensorMap& tm, const AttnArgs& a, int grid, cudaStream_t st) {
+template <int GROUP, int HKV, int D, bool CAP>
+int launch_attn_cap(const CUtensorMap& tm, const AttnArgs& a, int grid, cudaStream_t st) {
   constexpr int S = attn_stages<GROUP, HKV, D>();
   static_assert(S >= 2, "two stages must fit");
   constexpr int NT = (HKV * attn_wph<GROUP, HKV, D>() + 1) * 32;
   const size_t smem = attn_smem<GROUP, HKV, D>(a.batch * a.nhg);
-  // Raise the kernel's dynamic-smem limit once per device (to the 4096-sequence maximum),
-  // so no attribute call happens while a stream is being captured into a graph.
+  // Raise the kernel's dynamic-smem limit once per device (to the largest pair count), so no
+  // attribute call happens while a stream is being captured into a graph.
   static unsigned long long done_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !(done_mask & (1ull << dev))) {
-    MVB_TRY(set_smem(paged_attention_kernel<GROUP, HKV, S, D>, attn_smem<GROUP, HKV, D>(attn_max_pairs<D>()),
-                     "paged_attention: smem attribute"));
+    MVB_TRY(set_smem(paged_attention_kernel<GROUP, HKV, S, D, CAP>,
+                     attn_smem<GROUP, HKV, D>(attn_max_pairs<D>()), "paged_attention: smem attribute"));
     if (dev < 64) done_mask |= 1ull << dev;
   }
-  return launch("paged_attention_decode", paged_attention_kernel<GROUP, HKV, S, D>, dim3(grid), dim3(NT), smem, st,
-                tm, a);
+  return launch("paged_attention_decode", paged_attention_kernel<GROUP, HKV, S, D, CAP>, dim3(grid), dim3(NT), smem,
+                st, tm, a);
+}
+
+template <int GROUP, int HKV, int D>
+int launch_attn(const CUtensorMap& tm, const AttnArgs& a, int grid, cudaStream_t st) {
+  return a.cap_log2 > 0.0f ? launch_attn_cap<GROUP, HKV, D, true>(tm, a, grid, st)
+                           : launch_attn_cap<GROUP, HKV, D, false>(tm, a, grid, st);
 }
 
 template <int HKV, int D>
