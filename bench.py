@@ -54,11 +54,12 @@ def parse_args(argv=None):
     ap.add_argument("--layers", type=int, default=None, help="override layer count (debug only; invalid bench)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pdl", type=int, default=1)
-    ap.add_argument("--case", default=None, choices=["kernels", "moe", "gemma2"],
+    ap.add_argument("--case", default=None, choices=["kernels", "moe", "gemma2", "prefill"],
                     help="kernels: small profiling case (2 layers of the workload's dims), each kernel kind "
                          "launched a few times; prints per-kernel timings only.  moe: the sparse-MoE decode "
                          "workload (Qwen3-30B-A3B arch, batch 32, prompt 4096, greedy), 1 GPU.  gemma2: the "
-                         "Gemma-2-9B-arch decode workload (batch 16, prompt 8192, greedy), 1 GPU")
+                         "Gemma-2-9B-arch decode workload (batch 16, prompt 8192, greedy), 1 GPU.  prefill: "
+                         "batched prefill of the headline's 64 x 2048-token prompts (Qwen3-8B arch), 1 GPU")
     ap.add_argument("--arch", default=None, choices=["qwen3-8b", "gemma2-9b"],
                     help="--case kernels: the layer dims (qwen3-8b: batch 64, prompt 2048; gemma2-9b: batch 16, "
                          "prompt 8192)")
@@ -145,8 +146,9 @@ def peaks() -> dict:
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 def ncu_traffic() -> dict:
@@ -569,6 +571,64 @@ def run_gemma2_case(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_prefill_case(args) -> None:
+    """Batched prefill (``DecodeEngine.prefill``) of the headline workload's prompts: Qwen3-8B
+    architecture, 64 sequences of 2048 uniform-random tokens, into a shuffled paged pool.  One
+    warm-up prefill of 2 sequences, then the 64-sequence prefill timed with CUDA events (chunks of
+    16384 tokens).  GEMM FLOPs are 2 x tokens x the layers' parameters (plus the last tokens' lm_head);
+    attention reads each token's prefix once (the decode kernel, one query per token)."""
+    from llm_pytorch_inference_b200 import _native as N
+    from llm_pytorch_inference_b200.configs import get_config
+    from llm_pytorch_inference_b200.engine import DecodeEngine
+    from llm_pytorch_inference_b200.weights import canonical_state_dict
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    N.set_pdl(bool(args.pdl))
+    cfg = get_config(ARCH)
+    B, prompt = BATCH, PROMPT
+    sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev)
+    eng = DecodeEngine(cfg, sd, max_batch=B + 2, max_model_len=prompt + 64, device=dev)
+    del sd
+    order = list(range(eng.kv.num_blocks))
+    random.Random(0).shuffle(order)
+    from collections import deque
+
+    eng.kv.free_blocks = deque(order)
+    g = torch.Generator().manual_seed(0)
+    prompts = {s: torch.randint(0, cfg["vocab_size"], (prompt,), generator=g).tolist() for s in range(B)}
+    eng.prefill({B: prompts[0][:300], B + 1: prompts[1][:700]})          # warm-up (modules, buffers)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    clocks = ClockSampler(0)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    eng.prefill(prompts)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    r = eng.runner
+    T = B * prompt
+    layer_params = sum(t.numel() for t in [*r.w.wqkv, *r.w.wo, *r.w.wgu, *r.w.wdown])
+    gemm_flops = 2 * T * layer_params + 2 * B * r.w.lm_head.numel()
+    # attention, one query per token: K and V of every block of the token's prefix, all KV heads
+    blocks = B * sum((i + 16) // 16 for i in range(prompt))
+    attn_bytes = r.L * blocks * 16 * r.Hkv * r.D * 2 * 2
+    attn_flops = r.L * B * sum(i + 1 for i in range(prompt)) * r.Hq * r.D * 4
+    pk = peaks()
+    line = {"case": "prefill", "metric": "prefill prompt tokens/s Qwen3-8B-arch bf16, 64 x 2048-token prompts",
+            "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "ms": round(ms, 1), "tokens": T,
+            "gemm_tflop": round(gemm_flops / 1e12, 1), "attention_tflop": round(attn_flops / 1e12, 1),
+            "attention_bytes_gb": round(attn_bytes / 1e9, 1),
+            "gemm_time_at_peak_ms": round(gemm_flops / (pk["bf16_tflops_sustained"] * 1e12) * 1e3, 1),
+            "attention_time_at_hbm_peak_ms": round(attn_bytes / (pk["hbm_gbs"] * 1e9) * 1e3, 1),
+            "peaks": {"bf16_tflops_sustained": pk["bf16_tflops_sustained"], "hbm_gbs": pk["hbm_gbs"]},
+            "clocks": clk, "device_status": N.device_status(clear=True)}
+    print(json.dumps(line), flush=True)
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
     if args.case == "kernels":
@@ -576,6 +636,9 @@ def main(argv=None) -> int:
         return 0
     if args.case == "gemma2":
         run_gemma2_case(args)
+        return 0
+    if args.case == "prefill":
+        run_prefill_case(args)
         return 0
     if args.case == "moe":
         run_moe_case(args)

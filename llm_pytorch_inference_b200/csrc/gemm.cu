@@ -1,6 +1,6 @@
 // Dense bf16 GEMM for the decode-step projections on 5th-generation tensor cores.
 //
-//   Y[m, n] = sum_k X[m, k] * W[n, k]      (X: activations, m = batch <= 256; W: nn.Linear weight)
+//   Y[m, n] = sum_k X[m, k] * W[n, k]      (X: activations, m = batch; W: nn.Linear weight)
 //
 // Replaces the nn.Linear / cuBLAS calls of the reference decode step: q/k/v
 // (models/model_cuda.py:124-126), o_proj (:180), gate_up / down (ops/mlp.py:66, :84)
@@ -13,6 +13,10 @@
 // <= 64, see splitk_ctas) by stream-K: CTA c owns k-blocks [c*T/G, (c+1)*T/G) of the linearised (tile, k-block)
 // space.  A tile covered by several CTAs is merged by the last CTA to finish it,
 // summing the fp32 partials in CTA order (deterministic).
+//
+// More than 256 rows (a prefill's tokens) are cut into row tiles of 256: the output tiles are the
+// (weight tile, row tile) pairs, weight-major, so consecutive tiles of a CTA reuse one weight slab
+// from L2.
 //
 // Warp roles (192 threads):  warp 0 TMA producer, warp 1 TMEM alloc + MMA issue,
 // warps 2-5 epilogue (TMEM -> registers -> global).  Accumulators are double
@@ -36,7 +40,8 @@ struct GemmArgs {
   const __nv_bfloat16* aux;
   int64_t ld_aux;
   int m, n, k;
-  int tiles;     // output tiles
+  int tiles;     // output tiles: weight tiles x row tiles
+  int mt;        // row tiles (ceil(m / BN)); 1 for decode batches
   int kblocks;   // k / BK
   int epilogue;  // MVB_EPI_*
   int inter;     // SWIGLU: rows of the gate half of W
@@ -58,10 +63,11 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: 
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
-// Final epilogue for 32 batch columns [c0, c0+32) of feature `row` of tile t.
+// Final epilogue for 32 batch columns [c0, c0+32) of feature `row` of weight tile t, rows
+// r0 + c0 .. of Y.
 template <int BN>
 __device__ __forceinline__ void epilogue_store(const GemmArgs& a, const TpGemm& tp, const float (&v)[32], int t,
-                                               int row, int c0, float* xbuf) {
+                                               int row, int c0, float* xbuf, int r0) {
   if (a.epilogue == MVB_EPI_SWIGLU) {
     // TMEM lanes 0-63 hold gate features 64t + r, lanes 64-127 the matching up features.
     const bool is_up = row >= 64;
@@ -76,7 +82,7 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs& a, const TpGemm& 
       if (f < a.inter) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const int b = c0 + j;
+          const int b = r0 + c0 + j;
           if (b < a.m) {
             const float g = bf16_round(v[j]);
             const float s = bf16_round(silu_f(g));
@@ -93,7 +99,7 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs& a, const TpGemm& 
   if (a.epilogue == MVB_EPI_RESADD) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const int b = c0 + j;
+      const int b = r0 + c0 + j;
       if (b < a.m) {
         const float r = __bfloat162float(a.aux[static_cast<int64_t>(b) * a.ld_aux + nn]);
         a.y[static_cast<int64_t>(b) * a.ldy + nn] = __float2bfloat16_rn(r + bf16_round(v[j]));
@@ -115,7 +121,7 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs& a, const TpGemm& 
   }
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    const int b = c0 + j;
+    const int b = r0 + c0 + j;
     if (b < a.m) a.y[static_cast<int64_t>(b) * a.ldy + nn] = __float2bfloat16_rn(v[j]);
   }
 }
@@ -187,8 +193,9 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
       auto load_w = [&](int it) {
         const int s = it % STAGES;
         const int64_t g = kb_begin + it;
-        const int t = static_cast<int>(g / a.kblocks);
-        const int kb = static_cast<int>(g - static_cast<int64_t>(t) * a.kblocks);
+        const int lt = static_cast<int>(g / a.kblocks);  // linear tile
+        const int kb = static_cast<int>(g - static_cast<int64_t>(lt) * a.kblocks);
+        const int t = lt / a.mt;  // weight tile
         if (swiglu) {
           tma_load_2d(sA + s * A_STAGE, &tmW, &full[s], kb * BK, 64 * t, pol_w);
           tma_load_2d(sA + s * A_STAGE + A_STAGE / 2, &tmW, &full[s], kb * BK, a.inter + 64 * t, pol_w);
@@ -201,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
         const int64_t g = kb_begin + it;
         const int t = static_cast<int>(g / a.kblocks);
         const int kb = static_cast<int>(g - static_cast<int64_t>(t) * a.kblocks);
-        tma_load_2d(sB + s * B_STAGE, &tmX, &full[s], kb * BK, 0, pol_x);
+        tma_load_2d(sB + s * B_STAGE, &tmX, &full[s], kb * BK, (t % a.mt) * BN, pol_x);  // row tile
       };
       // Weights do not depend on the previous kernel: start streaming them before the
       // grid-dependency wait, then add the activation tiles to the same stages.
@@ -321,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          epilogue_store<BN>(a, tp, v, t, row, c0, xbuf);
+          epilogue_store<BN>(a, tp, v, t / a.mt, row, c0, xbuf, (t % a.mt) * BN);
         }
       } else {
         const int slot = seg == 0 ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
@@ -357,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] += __ldcg(p + (c0 + j) * BM + row);
             }
-            epilogue_store<BN>(a, tp, v, t, row, c0, xbuf);
+            epilogue_store<BN>(a, tp, v, t / a.mt, row, c0, xbuf, (t % a.mt) * BN);
           }
           if (e == 0) a.counters[t] = 0;
         }
@@ -432,8 +439,8 @@ extern "C" int64_t mvb_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int
   int sms = mvb_num_sms(device);
   if (sms <= 0) sms = 148;
   const int64_t bn = bn_for(m);
-  // Counters sized for the larger of the two tilings (plain / SWIGLU pairs).
-  const int64_t tiles = (n + 63) / 64;
+  // Counters sized for the larger of the two tilings (plain / SWIGLU pairs), times the row tiles.
+  const int64_t tiles = (n + 63) / 64 * ((m + bn - 1) / bn);
   const int64_t merge = counters_bytes(tiles) + 2LL * splitk_ctas(m, sms) * bn * BM * 4 + 256;
   int64_t part = splitk_partials_bytes(splitk_plan(m, n, k, sms)) + 256;
   if (n % 2 == 0) {
@@ -452,7 +459,9 @@ int gemm_launch(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
                 const TpGemm& tp, int64_t max_ctas, int* grid_out, mvb_stream_t stream) {
   MVB_REQUIRE(x && w && workspace && (y || partials_out(epilogue) || (tp.nranks > 0 && tp.y[0])),
               "mvb_gemm_bf16: null pointer");
-  MVB_REQUIRE(m > 0 && m <= 256, "mvb_gemm_bf16: m=%lld outside [1, 256]", (long long)m);
+  MVB_REQUIRE(m > 0 && m < (1LL << 24), "mvb_gemm_bf16: m=%lld", (long long)m);
+  MVB_REQUIRE(m <= 256 || (!partials_out(epilogue) && tp.nranks == 0),
+              "mvb_gemm_bf16: m=%lld > 256 needs a STORE, SWIGLU or RESADD epilogue on one GPU", (long long)m);
   MVB_REQUIRE(n > 0 && n < (1LL << 31) && k > 0 && k % BK == 0, "mvb_gemm_bf16: need k %% 64 == 0 (k=%lld)",
               (long long)k);
   MVB_REQUIRE(ldx >= k && ldw >= k && ldx % 8 == 0 && ldw % 8 == 0, "mvb_gemm_bf16: ldx/ldw must be >= k, %% 8");
@@ -467,7 +476,8 @@ int gemm_launch(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
   const int sms = current_sm_count();
   MVB_REQUIRE(sms > 0, "mvb_gemm_bf16: no device");
   const int bn = bn_for(m);
-  const int64_t tiles = tiles_for(n, epilogue);
+  const int64_t mt = (m + bn - 1) / bn;  // row tiles
+  const int64_t tiles = tiles_for(n, epilogue) * mt;
   const int64_t kblocks = k / BK;
   const int64_t total = tiles * kblocks;
   int64_t ctas = splitk_ctas(m, sms);
@@ -481,7 +491,7 @@ int gemm_launch(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
   // that share one buffer then use nested suffixes of the same (self-zeroing) counter area,
   // never bytes that another call used for partials.
   const int64_t ws_end = workspace_bytes / 256 * 256;
-  const int64_t cbytes = counters_bytes((n + 63) / 64);
+  const int64_t cbytes = counters_bytes((n + 63) / 64 * mt);
   SplitKPlan plan{};
   if (partials_out(epilogue)) plan = splitk_plan_ctas(m, static_cast<int>(tiles), k, ctas);
   const int64_t need = partials_out(epilogue) ? splitk_partials_bytes(plan) : cbytes + 2LL * grid * bn * BM * 4;
@@ -513,6 +523,7 @@ int gemm_launch(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
   a.n = static_cast<int>(n);
   a.k = static_cast<int>(k);
   a.tiles = static_cast<int>(tiles);
+  a.mt = static_cast<int>(mt);
   a.kblocks = static_cast<int>(kblocks);
   a.epilogue = epilogue;
   a.inter = static_cast<int>(n / 2);

@@ -23,6 +23,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
+from . import _native as N
 from .configs import head_dim, num_kv_heads
 from .kv_cache import KVCacheManager, num_blocks_for_budget
 from .runner import DecodeRunner, DecodeWeights, resolve_device
@@ -62,6 +63,8 @@ class DecodeEngine:
         self.tokens: dict[int, list[int]] = {}
         self.prompt_len: dict[int, int] = {}
         self.step_count = 0
+        self._prefill = None
+        self.last_prefill_logits = None
         m = self.runner.meta_host.numpy()
         r = self.runner
         self._ids = m[0:r.B]
@@ -87,6 +90,35 @@ class DecodeEngine:
     def append_first_token(self, seq_id: int, token: int) -> None:
         """The token the prefill sampled (``engine.py:288-290``)."""
         self.tokens[seq_id].append(int(token))
+
+    def prefill(self, prompts: dict[int, list[int]], temperature: float = 0.0, top_k: int = -1, top_p: float = 1.0,
+                seed: int = 0, max_tokens: int = 16384) -> dict[int, int]:
+        """``engine.py:253-290`` for a batch of new sequences on the GPU: registers each (blocks for
+        ``len(prompt) + 1`` tokens), prefills all of them in one packed token batch
+        (``prefill.BatchedPrefill``), samples each first token from its last position's logits and
+        appends it.  Returns seq_id -> first token; ``last_prefill_logits`` keeps the logits."""
+        from .prefill import BatchedPrefill
+
+        if self._prefill is None or self._prefill.max_tokens < max_tokens:
+            self._prefill = BatchedPrefill(self.runner, max_tokens)
+        sids = list(prompts)
+        tables = [self.add_sequence(s, prompts[s]) for s in sids]
+        logits = self._prefill.run([prompts[s] for s in sids], tables)
+        n = len(sids)
+        lib = N.lib()
+        out = torch.zeros(n, dtype=torch.int64, device=self.dev)
+        temp = torch.full((n,), float(temperature), dtype=torch.float32, device=self.dev)
+        tk = torch.full((n,), int(top_k), dtype=torch.int32, device=self.dev)
+        tp = torch.full((n,), float(top_p), dtype=torch.float32, device=self.dev)
+        N.check(lib.mvb_sample(out.data_ptr(), None, logits.data_ptr(), n, logits.shape[1], logits.stride(0),
+                               temp.data_ptr(), tk.data_ptr(), tp.data_ptr(), int(seed), 0, None, N.BF16,
+                               N.stream_handle(self.dev)), "sample")
+        first = out.cpu().tolist()
+        self.last_prefill_logits = logits
+        for s, t in zip(sids, first):
+            self.append_first_token(s, t)
+        self._refresh_rows()   # ready for the first decode step
+        return dict(zip(sids, first))
 
     def load_prefilled(self, kv_pool: torch.Tensor) -> None:
         """Copies a prefilled pool ``[L, 2, P, 16, Hkv, D]`` (same block ids) into the device pool."""

@@ -353,17 +353,14 @@ def linear(x: torch.Tensor, weight: torch.Tensor, epilogue: int = N.EPI_STORE, a
     auxf = None if aux is None else aux.reshape(-1, cols)
     dev = x.device
     with torch.cuda.device(dev):
-        for m0 in range(0, M, 256):
-            m = min(256, M - m0)
-            # + a fixed 1 MiB counter reserve: shapes sharing the cached buffer keep their
-            # partials clear of every other shape's counters (up to 256K output tiles)
-            need = N.lib().mvb_gemm_workspace_bytes(m, Nn, K, dev.index if dev.index is not None else 0) + (1 << 20)
-            ws = workspace if workspace is not None else WORKSPACES.get(dev, "gemm", need)
-            N.check(N.lib().mvb_gemm_bf16(out[m0:].data_ptr(), out.stride(0), xf[m0:].data_ptr(), xf.stride(0),
-                                          w.data_ptr(), w.stride(0), m, Nn, K, epilogue,
-                                          None if auxf is None else auxf[m0:].data_ptr(),
-                                          0 if auxf is None else auxf.stride(0), ws.data_ptr(), ws.numel(),
-                                          _st(x)), "gemm_bf16")
+        # + a fixed 1 MiB counter reserve: shapes sharing the cached buffer keep their partials
+        # clear of every other shape's counters (up to 256K output tiles)
+        need = N.lib().mvb_gemm_workspace_bytes(M, Nn, K, dev.index if dev.index is not None else 0) + (1 << 20)
+        ws = workspace if workspace is not None else WORKSPACES.get(dev, "gemm", need)
+        N.check(N.lib().mvb_gemm_bf16(out.data_ptr(), out.stride(0), xf.data_ptr(), xf.stride(0), w.data_ptr(),
+                                      w.stride(0), M, Nn, K, epilogue, None if auxf is None else auxf.data_ptr(),
+                                      0 if auxf is None else auxf.stride(0), ws.data_ptr(), ws.numel(), _st(x)),
+                "gemm_bf16")
     return out.reshape(*x.shape[:-1], cols)
 
 

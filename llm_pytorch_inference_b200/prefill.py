@@ -1,0 +1,136 @@
+"""Batched varlen prefill over the paged KV pool, on the decode path's kernels.
+
+Replaces ``LLMEngine._run_prefill`` (``mini_vllm/engine/engine.py:253-295``), which runs the model
+once per sequence (``ForCausalLM.forward`` with ``use_cache=False``: causal SDPA over the prompt,
+``Attention._write_kv_cache`` for every position, ``models/model.py:154-243``) and samples the first
+token from the last position's logits.  Here all prompts of a call are packed into one token batch
+(row r = token i of sequence s) and every layer runs once over all of them:
+
+* RMSNorm, the q|k|v GEMM over all rows (tcgen05, row tiles of 256), per-head QK-norm + RoPE and the
+  paged KV write of every token (one row per token: its sequence's block table, its position);
+* attention: the decode kernel with one query per token row, over that token's first ``pos + 1``
+  keys of its sequence, read back from the pool the KV write just filled (causal by construction);
+* o_proj GEMM with the residual add in its epilogue, RMSNorm, gate_up GEMM with the SwiGLU epilogue,
+  down GEMM with the residual add;
+* the final RMSNorm and lm_head on each sequence's last row only, then the sampler.
+
+The attention form is exact but reads each sequence's prefix once per query token (quadratic in
+the prompt length); a tiled causal kernel that reuses each K/V tile for many queries is the
+next step for long prompts.  Rows are processed in chunks of whole sequences so the activations
+stay within a fixed budget next to the KV pool.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as N
+
+_ATTN_ROWS = 4096   # query rows per attention launch (the kernel's limit on sequences)
+
+
+class BatchedPrefill:
+    """Prefill of dense (Qwen3 / Llama-family) models through a ``DecodeRunner``'s weights, tables
+    and KV pool."""
+
+    def __init__(self, runner, max_tokens: int = 16384):
+        if runner.moe or runner.gemma or runner.tp.enabled:
+            raise NotImplementedError("batched prefill covers dense single-GPU models")
+        self.r = runner
+        self.max_tokens = max_tokens
+        r, dev, bf = runner, runner.dev, torch.bfloat16
+        T = max_tokens
+        self.h = torch.zeros(T, r.H, dtype=bf, device=dev)           # residual stream
+        self.xn = torch.zeros(T, r.H, dtype=bf, device=dev)
+        self.qkv = torch.zeros(T, (r.Hq + 2 * r.Hkv) * r.D, dtype=bf, device=dev)
+        self.q = torch.zeros(T, r.Hq, r.D, dtype=bf, device=dev)
+        self.attn = torch.zeros(T, r.Hq * r.D, dtype=bf, device=dev)
+        self.act = torch.zeros(T, r.I, dtype=bf, device=dev)
+        self.gemm_ws = None
+        ws = N.lib().mvb_paged_attention_workspace_bytes(min(T, _ATTN_ROWS), r.Hq, r.D, dev.index)
+        self.attn_ws = torch.zeros(ws, dtype=torch.uint8, device=dev)
+
+    def _gemm(self, y, x, w, epilogue=N.EPI_STORE, aux=None):
+        lib, dev = N.lib(), self.r.dev
+        need = lib.mvb_gemm_workspace_bytes(x.shape[0], w.shape[0], w.shape[1], dev.index)
+        if self.gemm_ws is None or self.gemm_ws.numel() < need:
+            self.gemm_ws = torch.zeros(need + (1 << 20), dtype=torch.uint8, device=dev)
+        N.check(lib.mvb_gemm_bf16(y.data_ptr(), y.stride(0), x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0),
+                                  x.shape[0], w.shape[0], w.shape[1], epilogue, N.ptr(aux),
+                                  0 if aux is None else aux.stride(0), self.gemm_ws.data_ptr(),
+                                  self.gemm_ws.numel(), N.stream_handle(dev)), "gemm_bf16")
+
+    def run(self, ids: list[list[int]], tables: list[list[int]]) -> torch.Tensor:
+        """Prefills the sequences whose prompts are ``ids`` into the blocks ``tables`` (each holding
+        at least ``len(prompt)`` tokens); returns the bf16 logits ``[n, V]`` of each last token."""
+        out = []
+        i = 0
+        while i < len(ids):
+            j, n = i, 0
+            while j < len(ids) and n + len(ids[j]) <= self.max_tokens:
+                n += len(ids[j])
+                j += 1
+            if j == i:
+                raise ValueError(f"prompt of {len(ids[i])} tokens exceeds the prefill budget {self.max_tokens}")
+            out.append(self._chunk(ids[i:j], tables[i:j]))
+            i = j
+        return torch.cat(out)
+
+    def _chunk(self, ids: list[list[int]], tables: list[list[int]]) -> torch.Tensor:
+        r, lib = self.r, N.lib()
+        dev, w, H, D, L = r.dev, r.w, r.H, r.D, r.L
+        lens = [len(p) for p in ids]
+        T = sum(lens)
+        mb = r.max_blocks
+        # one int32 buffer: token ids | positions | per-row context | per-row block tables
+        host = torch.zeros(3 * T + T * mb, dtype=torch.int32)
+        tok, pos, ctx = host[:T], host[T:2 * T], host[2 * T:3 * T]
+        bt = host[3 * T:].view(T, mb)
+        bt.fill_(r.kv.scratch_block)
+        row = 0
+        for p, t in zip(ids, tables):
+            n = len(p)
+            if len(t) > mb:
+                raise ValueError(f"sequence needs {len(t)} blocks > max_blocks {mb}")
+            tok[row:row + n] = torch.tensor(p, dtype=torch.int32)
+            pos[row:row + n] = torch.arange(n, dtype=torch.int32)
+            ctx[row:row + n] = torch.arange(1, n + 1, dtype=torch.int32)
+            bt[row:row + n, :len(t)] = torch.tensor(t, dtype=torch.int32)
+            row += n
+        meta = host.to(dev, non_blocking=False)
+        tok_d, pos_d, ctx_d = meta[:T], meta[T:2 * T], meta[2 * T:3 * T]
+        bt_d = meta[3 * T:].view(T, mb)
+        st, eps, bf = N.stream_handle(dev), r.eps, N.BF16
+        h, xn, qkv, q, attn, act = (t_[:T] for t_ in (self.h, self.xn, self.qkv, self.q, self.attn, self.act))
+        kvc = r.kv.kv_cache
+        N.check(lib.mvb_embedding(h.data_ptr(), tok_d.data_ptr(), N.I32, w.embed.data_ptr(), T, H, r.V,
+                                  r.embed_scale, bf, st), "embedding")
+        for i in range(L):
+            N.check(lib.mvb_rmsnorm(xn.data_ptr(), H, h.data_ptr(), H, w.ln1[i].data_ptr(), T, H, eps, r.plus_one,
+                                    N.NORM_MODEL, bf, st), "rmsnorm")
+            self._gemm(qkv, xn, w.wqkv[i])
+            cos, sin = r.layer_tables[i]
+            N.check(lib.mvb_qk_norm_rope_kv_write(
+                q.data_ptr(), kvc.data_ptr(), qkv.data_ptr(), qkv.stride(0),
+                w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
+                cos.data_ptr(), sin.data_ptr(), cos.shape[0], pos_d.data_ptr(), bt_d.data_ptr(), mb, T, r.Hq, r.Hkv,
+                D, L, i, r.P, r.kv.block_size, eps, r.plus_one, st), "qk_norm_rope_kv_write")
+            for a0 in range(0, T, _ATTN_ROWS):
+                n = min(_ATTN_ROWS, T - a0)
+                N.check(lib.mvb_paged_attention_decode_ex(
+                    attn[a0:].data_ptr(), attn.stride(0), q[a0:].data_ptr(), r.Hq * D, kvc.data_ptr(),
+                    bt_d[a0:].data_ptr(), mb, ctx_d[a0:].data_ptr(), n, r.Hq, r.Hkv, D, L, i, r.P,
+                    r.kv.block_size, r.scale, r.softcap, r.windows[i], self.attn_ws.data_ptr(),
+                    self.attn_ws.numel(), st), "paged_attention_decode")
+            self._gemm(h, attn, w.wo[i], N.EPI_RESADD, aux=h)          # h = h + o_proj(attn)
+            N.check(lib.mvb_rmsnorm(xn.data_ptr(), H, h.data_ptr(), H, w.ln2[i].data_ptr(), T, H, eps, r.plus_one,
+                                    N.NORM_MODEL, bf, st), "rmsnorm")
+            self._gemm(act, xn, w.wgu[i], N.EPI_SWIGLU)
+            self._gemm(h, act, w.wdown[i], N.EPI_RESADD, aux=h)        # h = h + down(swiglu)
+        last = torch.tensor([sum(lens[:k + 1]) - 1 for k in range(len(lens))], device=dev)
+        hl = h.index_select(0, last).contiguous()
+        xl = torch.empty_like(hl)
+        N.check(lib.mvb_rmsnorm(xl.data_ptr(), H, hl.data_ptr(), H, w.final_norm.data_ptr(), len(lens), H, eps,
+                                r.plus_one, N.NORM_MODEL, bf, st), "rmsnorm")
+        logits = torch.empty(len(lens), r.V, dtype=torch.bfloat16, device=dev)
+        self._gemm(logits, xl, w.lm_head)
+        return logits

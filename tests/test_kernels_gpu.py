@@ -125,6 +125,27 @@ def test_gemm_store_matches_fp32(m, n, k):
     assert torch.equal(ops.linear(x, w), y)  # deterministic split-K merge
 
 
+@pytest.mark.parametrize("m,n,k", [(257, 1024, 512), (700, 4096, 4096), (2049, 6144, 4096), (4096, 512, 12288)])
+def test_gemm_row_tiles_for_prefill(m, n, k):
+    """More than 256 rows (a prefill's tokens): row tiles of 256, ragged last tile; the three
+    epilogues a prefill uses (store, SwiGLU, residual add)."""
+    g = torch.Generator(device=DEV).manual_seed(m + n + k)
+    x = (torch.randn(m, k, device=DEV, generator=g) / math.sqrt(k)).to(torch.bfloat16)
+    w = torch.randn(n, k, device=DEV, generator=g).to(torch.bfloat16)
+    y = ops.linear(x, w)
+    ref = x.float() @ w.float().T
+    torch.testing.assert_close(y.float(), ref, rtol=1e-2, atol=1e-2)
+    assert torch.equal(ops.linear(x, w), y)
+    h = ops.linear(x, w, N.EPI_SWIGLU)
+    gu = ref.to(torch.bfloat16)
+    sw = torch.nn.functional.silu(gu[:, :n // 2].float()).to(torch.bfloat16).float() * gu[:, n // 2:].float()
+    torch.testing.assert_close(h.float(), sw, rtol=2e-2, atol=2e-2)
+    aux = torch.randn(m, n, device=DEV, generator=g).to(torch.bfloat16)
+    r = ops.linear(x, w, N.EPI_RESADD, aux=aux)
+    torch.testing.assert_close(r.float(), aux.float() + gu.float(), rtol=1e-2, atol=2e-2)
+    assert N.device_status(clear=True) == 0
+
+
 def test_gemm_shapes_sharing_one_workspace():
     # the decode step's five GEMM shapes back to back on one buffer, twice, as the runner does
     from llm_pytorch_inference_b200 import _native

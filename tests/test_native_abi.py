@@ -44,8 +44,8 @@ def test_calls_that_need_no_gpu(lib):
     # argument validation fails before any CUDA call and sets the message
     rc = lib.mvb_rmsnorm(None, 0, None, 0, None, 1, 1, 1e-6, 0, 0, N.BF16, None)
     assert rc == 1 and b"null pointer" in lib.mvb_last_error()
-    rc = lib.mvb_gemm_bf16(1, 64, 1, 64, 1, 64, 300, 64, 64, 0, None, 0, 1, 0, None)
-    assert rc == 1 and b"m=300" in lib.mvb_last_error()
+    rc = lib.mvb_gemm_bf16(1, 64, 1, 64, 1, 64, 300, 64, 64, N.EPI_PARTIALS, None, 0, 1, 0, None)
+    assert rc == 1 and b"m=300" in lib.mvb_last_error()   # > 256 rows: not in split-K partial form
 
 
 def test_check_raises_with_library_message(lib):

@@ -1,0 +1,86 @@
+"""Batched varlen prefill on the GPU (``DecodeEngine.prefill``) against the oracle's per-sequence
+prefill (the reference's ``LLMEngine._run_prefill``, ``engine.py:253-295``, restated): the
+block ids, the KV state it leaves in the pool, each sequence's last-position logits, and the
+decode steps that continue from that state.  Bars as in tests/test_decode_gpu.py: the
+reference's own spread between two SDPA backends sets the noise allowance."""
+import random
+
+import pytest
+import torch
+from torch.nn.attention import SDPBackend
+
+from llm_pytorch_inference_b200.configs import get_config
+from llm_pytorch_inference_b200.engine import DecodeEngine
+from llm_pytorch_inference_b200.weights import canonical_state_dict
+from oracle import sampling as osamp
+from oracle.engine import OracleEngine
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(arch, lens, num_blocks, max_tokens=16384, seed=3):
+    cfg = get_config(arch)
+    sd = canonical_state_dict(cfg, 0, torch.float32)
+    order = list(range(num_blocks))
+    random.Random(0).shuffle(order)
+    g = torch.Generator().manual_seed(seed)
+    prompts = [torch.randint(0, cfg["vocab_size"], (n,), generator=g).tolist() for n in lens]
+    oracle = OracleEngine(cfg, sd, torch.bfloat16, num_blocks, 16, list(order), prefill_last_only=True)
+    alt = OracleEngine(cfg, sd, torch.bfloat16, num_blocks, 16, list(order), sdpa_backend=SDPBackend.MATH,
+                       prefill_last_only=True, capped_rounding="eager")
+    ref = torch.stack([oracle.prefill(i, p) for i, p in enumerate(prompts)])
+    ref_alt = torch.stack([alt.prefill(i, p) for i, p in enumerate(prompts)])
+    eng = DecodeEngine(cfg, {k: v.to(torch.bfloat16) for k, v in sd.items()}, max_batch=len(prompts),
+                       max_model_len=max(lens) + 64, num_blocks=num_blocks, device="cuda", free_order=list(order))
+    first = eng.prefill(dict(enumerate(prompts)), max_tokens=max_tokens)
+    for i in range(len(prompts)):
+        assert eng.kv.get_block_table(i) == oracle.blocks.get_block_table(i)   # same FIFO block ids
+    return cfg, prompts, oracle, alt, eng, ref, ref_alt, first
+
+
+def _check_logits(got, ref, ref_alt):
+    d, n = (got - ref).abs(), (ref_alt - ref).abs()
+    assert float(d.max()) <= max(2e-2, 1.5 * float(n.max())), (float(d.max()), float(n.max()))
+    assert float(d.mean()) <= max(2e-3, 1.25 * float(n.mean())), (float(d.mean()), float(n.mean()))
+
+
+def _check_kv(eng, oracle, alt, prompts):
+    """Every prompt position's K and V in every layer, against the oracle's pool."""
+    got_pool = eng.kv.kv_cache[:, :, :oracle.kv_pool.shape[2]].float().cpu()
+    for s, p in enumerate(prompts):
+        bt = oracle.blocks.get_block_table(s)
+        rows = torch.tensor([bt[t // 16] for t in range(len(p))])
+        offs = torch.tensor([t % 16 for t in range(len(p))])
+        got = got_pool[:, :, rows, offs]
+        ref = oracle.kv_pool[:, :, rows, offs].float()
+        spread = (alt.kv_pool[:, :, rows, offs].float() - ref).abs()
+        d = (got - ref).abs()
+        assert float(d.max()) <= max(6e-2, 1.5 * float(spread.max())), (s, float(d.max()), float(spread.max()))
+        assert float(d.mean()) <= max(4e-3, 1.25 * float(spread.mean())), (s, float(d.mean()))
+
+
+def test_prefill_tiny_matches_oracle_and_decodes_on():
+    from test_decode_gpu import _compare_teacher_forced
+
+    cfg, prompts, oracle, alt, eng, ref, ref_alt, first = _run("qwen3-tiny", [37, 50, 16, 64, 5, 300], 256)
+    _check_logits(eng.last_prefill_logits.float().cpu(), ref, ref_alt)
+    _check_kv(eng, oracle, alt, prompts)
+    ref_tok = osamp.greedy(ref).tolist()
+    for i in range(len(prompts)):   # greedy first tokens equal unless the oracle's top-2 is a near tie
+        if first[i] != ref_tok[i]:
+            top2 = torch.topk(ref[i], 2).values
+            assert float(top2[0] - top2[1]) <= 4e-2, i
+        oracle.append(i, ref_tok[i])
+        alt.append(i, ref_tok[i])
+    eng.force_last_tokens(ref_tok)
+    alt.kv_pool.copy_(oracle.kv_pool)
+    _compare_teacher_forced(oracle, alt, eng, 6)
+
+
+def test_prefill_chunks_and_row_tiles_at_qwen3_8b_dims():
+    """Qwen3-8B layer dims (2 layers): > 256 rows per GEMM, several attention launches of 4096
+    query rows, and a token budget that splits the batch into chunks of whole sequences."""
+    cfg, prompts, oracle, alt, eng, ref, ref_alt, first = _run("qwen3-8b-2l", [1500, 2049, 700, 1200], 512,
+                                                               max_tokens=4096)
+    _check_logits(eng.last_prefill_logits.float().cpu(), ref, ref_alt)
+    _check_kv(eng, oracle, alt, prompts)
