@@ -202,6 +202,22 @@ int mvb_paged_attention_decode_ex(void* out, int64_t out_stride, const void* q, 
                                   int64_t block_size, float scale, float softcap, int64_t window, void* workspace,
                                   int64_t workspace_bytes, mvb_stream_t stream);
 
+/* Causal attention of a batched prefill over the paged pool (the prefill's SDPA with
+ * is_causal=True, models/model.py:206-221, after Attention._write_kv_cache, :226-243): for every
+ * prompt token t of every sequence, out[t, h] = softmax_{k <= t}(q[t, h] . K[k]^T * scale) V[k].
+ * q/out: [tokens, Hq, D] bf16 rows (row stride q_stride / out_stride), sequence s occupying rows
+ * seq_start[s] .. seq_start[s] + seq_len[s] - 1.  block_tables: int32 [num_seqs, max_blocks].
+ * The work is num_tiles (sequence, 16-token query tile) pairs: tile i is query tokens
+ * 16 tile_idx[i] .. of sequence tile_seq[i] (tile_idx < ceil(seq_len / 16)); order them longest
+ * first.  The tile's K/V prefix is read once for its 16 queries.  head_dim 128, 1, 2 or 4 query
+ * heads per KV head, block_size 16. */
+int mvb_prefill_attention(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* kv_cache,
+                          const int32_t* block_tables, int64_t max_blocks, const int32_t* seq_start,
+                          const int32_t* seq_len, const int32_t* tile_seq, const int32_t* tile_idx,
+                          int64_t num_tiles, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                          int64_t num_layers, int64_t layer, int64_t num_blocks, int64_t block_size, float scale,
+                          mvb_stream_t stream);
+
 /* Allocation-free paged attention (no counterpart in the reference).  Same arguments and
  * result as mvb_paged_attention_decode, minus the workspace: the split-KV scratch is a
  * 6 MiB area built into the library, for callers that cannot allocate device memory (a host

@@ -52,6 +52,8 @@ SIGNATURES: dict[str, tuple] = {
     "mvb_paged_attention_workspace_bytes": (_i64, [_i64, _i64, _i64, _i32]),
     "mvb_paged_attention_decode": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64,
                                           _i64, _i64, _i64, _i64, _f32, _vp, _i64, _vp]),
+    "mvb_prefill_attention": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+                                     _i64, _i64, _i64, _i64, _i64, _f32, _vp]),
     "mvb_paged_attention_decode_ex": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64,
                                              _i64, _i64, _i64, _i64, _f32, _f32, _i64, _vp, _i64, _vp]),
     "mvb_paged_attention_decode_noalloc": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64,

@@ -8,16 +8,16 @@ token from the last position's logits.  Here all prompts of a call are packed in
 
 * RMSNorm, the q|k|v GEMM over all rows (tcgen05, row tiles of 256), per-head QK-norm + RoPE and the
   paged KV write of every token (one row per token: its sequence's block table, its position);
-* attention: the decode kernel with one query per token row, over that token's first ``pos + 1``
-  keys of its sequence, read back from the pool the KV write just filled (causal by construction);
+* causal attention over the pool the KV write just filled: ``mvb_prefill_attention``, one CTA per
+  (sequence, 16-token query tile, KV head) reading the tile's K/V prefix once for its 16 queries
+  (head dim 128, up to 4 query heads per KV head); other shapes take the decode kernel with one
+  query per token row over its first ``pos + 1`` keys;
 * o_proj GEMM with the residual add in its epilogue, RMSNorm, gate_up GEMM with the SwiGLU epilogue,
   down GEMM with the residual add;
 * the final RMSNorm and lm_head on each sequence's last row only, then the sampler.
 
-The attention form is exact but reads each sequence's prefix once per query token (quadratic in
-the prompt length); a tiled causal kernel that reuses each K/V tile for many queries is the
-next step for long prompts.  Rows are processed in chunks of whole sequences so the activations
-stay within a fixed budget next to the KV pool.
+Rows are processed in chunks of whole sequences so the activations stay within a fixed budget
+next to the KV pool.
 """
 from __future__ import annotations
 
@@ -46,10 +46,26 @@ class BatchedPrefill:
         self.attn = torch.zeros(T, r.Hq * r.D, dtype=bf, device=dev)
         self.act = torch.zeros(T, r.I, dtype=bf, device=dev)
         self.gemm_ws = None
+        self.timing: dict[str, list] | None = None   # kind -> [(start, end) CUDA events] when profiling
         ws = N.lib().mvb_paged_attention_workspace_bytes(min(T, _ATTN_ROWS), r.Hq, r.D, dev.index)
         self.attn_ws = torch.zeros(ws, dtype=torch.uint8, device=dev)
 
+    def _mark(self, kind: str):
+        """Start/stop CUDA-event pair around one launch when ``timing`` is on (else a no-op)."""
+        if self.timing is None:
+            return None
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        ev[0].record()
+        self.timing.setdefault(kind, []).append(ev)
+        return ev[1]
+
     def _gemm(self, y, x, w, epilogue=N.EPI_STORE, aux=None):
+        end = self._mark("gemm")
+        self._gemm_launch(y, x, w, epilogue, aux)
+        if end is not None:
+            end.record()
+
+    def _gemm_launch(self, y, x, w, epilogue, aux):
         lib, dev = N.lib(), self.r.dev
         need = lib.mvb_gemm_workspace_bytes(x.shape[0], w.shape[0], w.shape[1], dev.index)
         if self.gemm_ws is None or self.gemm_ws.numel() < need:
@@ -81,13 +97,22 @@ class BatchedPrefill:
         lens = [len(p) for p in ids]
         T = sum(lens)
         mb = r.max_blocks
-        # one int32 buffer: token ids | positions | per-row context | per-row block tables
-        host = torch.zeros(3 * T + T * mb, dtype=torch.int32)
+        S = len(ids)
+        tiles = sorted(((s, qt) for s in range(S) for qt in range((lens[s] + 15) // 16)), key=lambda x: -x[1])
+        nt = len(tiles)
+        # one int32 buffer: token ids | positions | per-row context | per-row block tables |
+        # per-sequence start, length, block tables | tiles (sequence, index)
+        o_seq = 3 * T + T * mb
+        o_tile = o_seq + 2 * S + S * mb
+        host = torch.zeros(o_tile + 2 * nt, dtype=torch.int32)
         tok, pos, ctx = host[:T], host[T:2 * T], host[2 * T:3 * T]
-        bt = host[3 * T:].view(T, mb)
+        bt = host[3 * T:o_seq].view(T, mb)
         bt.fill_(r.kv.scratch_block)
+        seq_start, seq_len = host[o_seq:o_seq + S], host[o_seq + S:o_seq + 2 * S]
+        seq_bt = host[o_seq + 2 * S:o_tile].view(S, mb)
+        seq_bt.fill_(r.kv.scratch_block)
         row = 0
-        for p, t in zip(ids, tables):
+        for k, (p, t) in enumerate(zip(ids, tables)):
             n = len(p)
             if len(t) > mb:
                 raise ValueError(f"sequence needs {len(t)} blocks > max_blocks {mb}")
@@ -95,10 +120,18 @@ class BatchedPrefill:
             pos[row:row + n] = torch.arange(n, dtype=torch.int32)
             ctx[row:row + n] = torch.arange(1, n + 1, dtype=torch.int32)
             bt[row:row + n, :len(t)] = torch.tensor(t, dtype=torch.int32)
+            seq_start[k], seq_len[k] = row, n
+            seq_bt[k, :len(t)] = torch.tensor(t, dtype=torch.int32)
             row += n
+        host[o_tile:o_tile + nt] = torch.tensor([x[0] for x in tiles], dtype=torch.int32)
+        host[o_tile + nt:] = torch.tensor([x[1] for x in tiles], dtype=torch.int32)
         meta = host.to(dev, non_blocking=False)
         tok_d, pos_d, ctx_d = meta[:T], meta[T:2 * T], meta[2 * T:3 * T]
-        bt_d = meta[3 * T:].view(T, mb)
+        bt_d = meta[3 * T:o_seq].view(T, mb)
+        seq_start_d, seq_len_d = meta[o_seq:o_seq + S], meta[o_seq + S:o_seq + 2 * S]
+        seq_bt_d = meta[o_seq + 2 * S:o_tile]
+        tile_seq_d, tile_idx_d = meta[o_tile:o_tile + nt], meta[o_tile + nt:]
+        tiled = D == 128 and (r.Hq // r.Hkv) in (1, 2, 4) and not r.softcap and not any(r.windows)
         st, eps, bf = N.stream_handle(dev), r.eps, N.BF16
         h, xn, qkv, q, attn, act = (t_[:T] for t_ in (self.h, self.xn, self.qkv, self.q, self.attn, self.act))
         kvc = r.kv.kv_cache
@@ -114,13 +147,21 @@ class BatchedPrefill:
                 w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
                 cos.data_ptr(), sin.data_ptr(), cos.shape[0], pos_d.data_ptr(), bt_d.data_ptr(), mb, T, r.Hq, r.Hkv,
                 D, L, i, r.P, r.kv.block_size, eps, r.plus_one, st), "qk_norm_rope_kv_write")
-            for a0 in range(0, T, _ATTN_ROWS):
+            end = self._mark("attention")
+            if tiled:
+                N.check(lib.mvb_prefill_attention(
+                    attn.data_ptr(), attn.stride(0), q.data_ptr(), r.Hq * D, kvc.data_ptr(), seq_bt_d.data_ptr(), mb,
+                    seq_start_d.data_ptr(), seq_len_d.data_ptr(), tile_seq_d.data_ptr(), tile_idx_d.data_ptr(), nt,
+                    r.Hq, r.Hkv, D, L, i, r.P, r.kv.block_size, r.scale, st), "prefill_attention")
+            for a0 in range(0, 0 if tiled else T, _ATTN_ROWS):
                 n = min(_ATTN_ROWS, T - a0)
                 N.check(lib.mvb_paged_attention_decode_ex(
                     attn[a0:].data_ptr(), attn.stride(0), q[a0:].data_ptr(), r.Hq * D, kvc.data_ptr(),
                     bt_d[a0:].data_ptr(), mb, ctx_d[a0:].data_ptr(), n, r.Hq, r.Hkv, D, L, i, r.P,
                     r.kv.block_size, r.scale, r.softcap, r.windows[i], self.attn_ws.data_ptr(),
                     self.attn_ws.numel(), st), "paged_attention_decode")
+            if end is not None:
+                end.record()
             self._gemm(h, attn, w.wo[i], N.EPI_RESADD, aux=h)          # h = h + o_proj(attn)
             N.check(lib.mvb_rmsnorm(xn.data_ptr(), H, h.data_ptr(), H, w.ln2[i].data_ptr(), T, H, eps, r.plus_one,
                                     N.NORM_MODEL, bf, st), "rmsnorm")

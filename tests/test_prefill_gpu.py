@@ -84,3 +84,58 @@ def test_prefill_chunks_and_row_tiles_at_qwen3_8b_dims():
                                                                max_tokens=4096)
     _check_logits(eng.last_prefill_logits.float().cpu(), ref, ref_alt)
     _check_kv(eng, oracle, alt, prompts)
+
+
+@pytest.mark.parametrize("Hq,Hkv,lens", [
+    (32, 8, [2049, 1, 16, 17, 300]),     # Qwen3-8B heads: group 4, tiles ending inside a block
+    (8, 4, [37, 50, 16, 64, 5]),          # group 2
+    (4, 4, [129, 33]),                    # group 1
+])
+def test_prefill_attention_kernel_matches_causal_fp32(Hq, Hkv, lens):
+    """``mvb_prefill_attention`` against causal softmax attention in fp32 over the same pool;
+    rows of other sequences and padding untouched."""
+    import math
+
+    from llm_pytorch_inference_b200 import _native as N
+
+    D, L, layer = 128, 2, 1
+    nblk = [(n + 15) // 16 for n in lens]
+    P = sum(nblk) + 5
+    order = list(range(P))
+    random.Random(9).shuffle(order)
+    it = iter(order)
+    tables = [[next(it) for _ in range(nb)] for nb in nblk]
+    g = torch.Generator().manual_seed(Hq + len(lens))
+    pool = torch.randn(L, 2, P + 1, 16, Hkv, D, generator=g).to(torch.bfloat16)
+    T = sum(lens)
+    q = torch.randn(T, Hq, D, generator=g).to(torch.bfloat16)
+    mb = max(nblk)
+    bt = torch.full((len(lens), mb), P, dtype=torch.int32)
+    for k, t in enumerate(tables):
+        bt[k, :len(t)] = torch.tensor(t)
+    starts = [sum(lens[:k]) for k in range(len(lens))]
+    tiles = sorted(((s, qt) for s in range(len(lens)) for qt in range(nblk[s])), key=lambda x: -x[1])
+    dev = "cuda"
+    out = torch.full((T + 3, Hq, D), float("nan"), dtype=torch.bfloat16, device=dev)
+    ts = torch.tensor([x[0] for x in tiles], dtype=torch.int32, device=dev)
+    ti = torch.tensor([x[1] for x in tiles], dtype=torch.int32, device=dev)
+    pool_d, q_d, bt_d = pool.to(dev), q.to(dev), bt.to(dev)
+    st_d = torch.tensor(starts, dtype=torch.int32, device=dev)
+    ln_d = torch.tensor(lens, dtype=torch.int32, device=dev)
+    scale = 1.0 / math.sqrt(D)
+    N.check(N.lib().mvb_prefill_attention(out.data_ptr(), Hq * D, q_d.data_ptr(), Hq * D, pool_d.data_ptr(),
+                                          bt_d.data_ptr(), mb, st_d.data_ptr(), ln_d.data_ptr(), ts.data_ptr(),
+                                          ti.data_ptr(), len(tiles), Hq, Hkv, D, L, layer, P + 1, 16, scale,
+                                          N.stream_handle()), "prefill_attention")
+    torch.cuda.synchronize()
+    assert N.device_status(clear=True) == 0
+    got = out.cpu()
+    assert bool(got[T:].isnan().all())
+    for s, n in enumerate(lens):
+        k = torch.cat([pool[layer, 0, b] for b in tables[s]], 0)[:n].float().repeat_interleave(Hq // Hkv, dim=1)
+        v = torch.cat([pool[layer, 1, b] for b in tables[s]], 0)[:n].float().repeat_interleave(Hq // Hkv, dim=1)
+        qs = q[starts[s]:starts[s] + n].float()
+        sc = torch.einsum("thd,khd->htk", qs, k) * scale
+        sc = sc.masked_fill(torch.ones(n, n, dtype=torch.bool).triu(1), float("-inf"))
+        ref = torch.einsum("htk,khd->thd", torch.softmax(sc, -1), v)
+        torch.testing.assert_close(got[starts[s]:starts[s] + n].float(), ref, rtol=2e-2, atol=1e-2)
