@@ -372,6 +372,12 @@ int mvb_tp_gemm_bf16(mvb_tp_comm* comm, const void* x, int64_t ldx, const void* 
 int mvb_tp_fused_add_rmsnorm_gemm(mvb_tp_comm* comm, void* residual, int64_t rows, int64_t hidden, int64_t gemm_k,
                                   const void* weight, float eps, int plus_one, int64_t recv_offset, int wait_point,
                                   int64_t out_offset, int signal_point, mvb_stream_t stream);
+/* The same with Gemma's post-norm (mvb_fused_norm_add_rmsnorm_gemm): the row's summed output is
+ * normalised with post_weight before the residual add. */
+int mvb_tp_fused_norm_add_rmsnorm_gemm(mvb_tp_comm* comm, void* residual, int64_t rows, int64_t hidden,
+                                       int64_t gemm_k, const void* post_weight, const void* weight, float eps,
+                                       int plus_one, int64_t recv_offset, int wait_point, int64_t out_offset,
+                                       int signal_point, mvb_stream_t stream);
 /* Stream-ordered wait (one tiny kernel) until every rank signalled `point` this step. */
 int mvb_tp_wait(mvb_tp_comm* comm, int point, mvb_stream_t stream);
 

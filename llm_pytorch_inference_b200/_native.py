@@ -78,6 +78,8 @@ SIGNATURES: dict[str, tuple] = {
                                 _vp]),
     "mvb_tp_fused_add_rmsnorm_gemm": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _f32, _i32, _i64, _i32, _i64, _i32,
                                              _vp]),
+    "mvb_tp_fused_norm_add_rmsnorm_gemm": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _f32, _i32, _i64, _i32,
+                                                  _i64, _i32, _vp]),
     "mvb_tp_wait": (_i32, [_vp, _i32, _vp]),
 }
 

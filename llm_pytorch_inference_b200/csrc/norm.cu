@@ -388,10 +388,10 @@ extern "C" int mvb_fused_norm_add_rmsnorm_gemm(void* out, void* residual, const 
                         device_status_ptr());
 }
 
-extern "C" int mvb_tp_fused_add_rmsnorm_gemm(mvb_tp_comm* comm, void* residual, int64_t rows, int64_t hidden,
-                                             int64_t gemm_k, const void* weight, float eps, int plus_one,
-                                             int64_t recv_offset, int wait_point, int64_t out_offset,
-                                             int signal_point, mvb_stream_t stream) {
+static int tp_fused_add_rmsnorm_gemm_impl(mvb_tp_comm* comm, void* residual, int64_t rows, int64_t hidden,
+                                          int64_t gemm_k, const void* post_weight, const void* weight, float eps,
+                                          int plus_one, int64_t recv_offset, int wait_point, int64_t out_offset,
+                                          int signal_point, mvb_stream_t stream) {
   MVB_REQUIRE(comm && residual && weight, "mvb_tp_fused_add_rmsnorm_gemm: null pointer");
   const int nr = comm->nranks;
   MVB_REQUIRE(rows > 0 && rows <= 256 && rows % nr == 0 && gemm_k > 0 && gemm_k % kSplitBK == 0,
@@ -430,11 +430,38 @@ extern "C" int mvb_tp_fused_add_rmsnorm_gemm(mvb_tp_comm* comm, void* residual, 
   tp.epoch = comm->epoch;
   const FaddSplit sp = fadd_split(hidden);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  MVB_TRY(launch_cluster("tp_fused_add_rmsnorm_gemm", fused_add_rmsnorm_gemm_kernel<true, false>,
-                         dim3(static_cast<unsigned>(sp.ctas), static_cast<unsigned>(rpr)), dim3(sp.threads),
-                         static_cast<unsigned>(sp.ctas), 0, st, (__nv_bfloat16*)nullptr, (__nv_bfloat16*)residual,
-                         (const float*)nullptr, p, (const __nv_bfloat16*)weight, (const __nv_bfloat16*)nullptr,
-                         (int)hidden, sp.runs_per_cta, eps, plus_one, tp, device_status_ptr()));
+  MVB_REQUIRE(post_weight == nullptr || aligned(post_weight, 8), "mvb_tp_fused_add_rmsnorm_gemm: 8-byte alignment");
+  if (post_weight != nullptr) {
+    MVB_TRY(launch_cluster("tp_fused_norm_add_rmsnorm_gemm", fused_add_rmsnorm_gemm_kernel<true, true>,
+                           dim3(static_cast<unsigned>(sp.ctas), static_cast<unsigned>(rpr)), dim3(sp.threads),
+                           static_cast<unsigned>(sp.ctas), 0, st, (__nv_bfloat16*)nullptr, (__nv_bfloat16*)residual,
+                           (const float*)nullptr, p, (const __nv_bfloat16*)weight,
+                           (const __nv_bfloat16*)post_weight, (int)hidden, sp.runs_per_cta, eps, plus_one, tp,
+                           device_status_ptr()));
+  } else {
+    MVB_TRY(launch_cluster("tp_fused_add_rmsnorm_gemm", fused_add_rmsnorm_gemm_kernel<true, false>,
+                           dim3(static_cast<unsigned>(sp.ctas), static_cast<unsigned>(rpr)), dim3(sp.threads),
+                           static_cast<unsigned>(sp.ctas), 0, st, (__nv_bfloat16*)nullptr, (__nv_bfloat16*)residual,
+                           (const float*)nullptr, p, (const __nv_bfloat16*)weight, (const __nv_bfloat16*)nullptr,
+                           (int)hidden, sp.runs_per_cta, eps, plus_one, tp, device_status_ptr()));
+  }
   comm->point_count[signal_point] = 1;
   return MVB_OK;
+}
+
+extern "C" int mvb_tp_fused_add_rmsnorm_gemm(mvb_tp_comm* comm, void* residual, int64_t rows, int64_t hidden,
+                                             int64_t gemm_k, const void* weight, float eps, int plus_one,
+                                             int64_t recv_offset, int wait_point, int64_t out_offset,
+                                             int signal_point, mvb_stream_t stream) {
+  return tp_fused_add_rmsnorm_gemm_impl(comm, residual, rows, hidden, gemm_k, nullptr, weight, eps, plus_one,
+                                        recv_offset, wait_point, out_offset, signal_point, stream);
+}
+
+extern "C" int mvb_tp_fused_norm_add_rmsnorm_gemm(mvb_tp_comm* comm, void* residual, int64_t rows, int64_t hidden,
+                                                  int64_t gemm_k, const void* post_weight, const void* weight,
+                                                  float eps, int plus_one, int64_t recv_offset, int wait_point,
+                                                  int64_t out_offset, int signal_point, mvb_stream_t stream) {
+  MVB_REQUIRE(post_weight != nullptr, "mvb_tp_fused_norm_add_rmsnorm_gemm: null post weight");
+  return tp_fused_add_rmsnorm_gemm_impl(comm, residual, rows, hidden, gemm_k, post_weight, weight, eps, plus_one,
+                                        recv_offset, wait_point, out_offset, signal_point, stream);
 }

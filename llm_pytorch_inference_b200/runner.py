@@ -167,8 +167,6 @@ class DecodeRunner:
         self.layer_tables = [self.tables[layer_rope_theta(cfg, i)] for i in range(self.L)]
         self.cos, self.sin = self.layer_tables[0]
 
-        if self.gemma and self.tp.enabled:
-            raise NotImplementedError("tensor parallelism of the Gemma decode step is not built")
         B, H, dev, bf = self.B, self.H, self.dev, torch.bfloat16
         qkv_n = (self.Hq + 2 * self.Hkv) * self.D
         didx = dev.index if dev.index is not None else torch.cuda.current_device()
@@ -430,10 +428,15 @@ class DecodeRunner:
                                          self.gemm_ws.numel(), out_offset, ldy, wait, signal, self._st),
                 "tp_gemm_bf16")
 
-    def _tp_add_norm(self, gemm_k, weight, recv, wait, signal):
+    def _tp_add_norm(self, gemm_k, weight, recv, wait, signal, post=None):
+        if post is not None:   # Gemma: the summed output is post-normalised before the residual add
+            N.check(N.lib().mvb_tp_fused_norm_add_rmsnorm_gemm(
+                self.heap.comm, self.residual.data_ptr(), self.B, self.H, gemm_k, post.data_ptr(), weight.data_ptr(),
+                self.eps, self.plus_one, recv, wait, self.layout.xn, signal, self._st), "tp_fused_norm_add_rmsnorm_gemm")
+            return
         N.check(N.lib().mvb_tp_fused_add_rmsnorm_gemm(self.heap.comm, self.residual.data_ptr(), self.B, self.H, gemm_k,
-                                                      weight.data_ptr(), self.eps, 0, recv, wait, self.layout.xn,
-                                                      signal, self._st), "tp_fused_add_rmsnorm_gemm")
+                                                      weight.data_ptr(), self.eps, self.plus_one, recv, wait,
+                                                      self.layout.xn, signal, self._st), "tp_fused_add_rmsnorm_gemm")
 
     def _forward_tp(self) -> None:
         """The step on one rank of a tensor-parallel group (see tensor_parallel): same kernels,
@@ -445,27 +448,31 @@ class DecodeRunner:
         comm = self.heap.comm
         ws = self.gemm_ws.data_ptr()
         N.check(lib.mvb_tp_begin_step(comm, st), "tp_begin_step")
-        N.check(lib.mvb_embedding(self.residual.data_ptr(), self.ids.data_ptr(), N.I32, w.embed.data_ptr(), B, H,
-                                  self.V, 1.0, bf, st), "embedding")
-        N.check(lib.mvb_rmsnorm(self.xn.data_ptr(), H, self.residual.data_ptr(), H, w.ln1[0].data_ptr(), B, H, eps, 0,
-                                N.NORM_MODEL, bf, st), "rmsnorm")
+        self._embed()
+        g = self.gemma   # Gemma: post-norms of the attention and MLP outputs before each residual add
         for i in range(self.L):
             if i > 0:
-                self._tp_add_norm(self.I, w.ln1[i], lay.recv_down, tpm.point_down(i - 1), tpm.point_mlp_norm(i - 1))
+                self._tp_add_norm(self.I, w.ln1[i], lay.recv_down, tpm.point_down(i - 1), tpm.point_mlp_norm(i - 1),
+                                  post=w.post_ff[i - 1] if g else None)
             self._tp_gemm(self.xn, w.wqkv[i], N.EPI_PARTIALS, wait=-1 if i == 0 else tpm.point_mlp_norm(i - 1))
             self._qk(i)
             self._attention(i)
             self._tp_gemm(self.attn, w.wo[i], N.EPI_PARTIALS, out_offset=lay.recv_o, signal=tpm.point_o_proj(i))
-            self._tp_add_norm(self.Hq * D, w.ln2[i], lay.recv_o, tpm.point_o_proj(i), tpm.point_attn_norm(i))
+            self._tp_add_norm(self.Hq * D, w.pre_ff[i] if g else w.ln2[i], lay.recv_o, tpm.point_o_proj(i),
+                              tpm.point_attn_norm(i), post=w.ln2[i] if g else None)
             self._tp_gemm(self.xn, w.wgu[i], N.EPI_SWIGLU_PARTIALS, wait=tpm.point_attn_norm(i))
-            N.check(lib.mvb_swiglu_gemm(self.h.data_ptr(), self.h.stride(0), ws, B, self.I, H, st), "swiglu_gemm")
+            N.check(lib.mvb_gated_gemm(self.h.data_ptr(), self.h.stride(0), ws, B, self.I, H, self.act, st),
+                    "gated_gemm")
             self._tp_gemm(self.h, w.wdown[i], N.EPI_PARTIALS, out_offset=lay.recv_down, signal=tpm.point_down(i))
         last = self.L - 1
-        self._tp_add_norm(self.I, w.final_norm, lay.recv_down, tpm.point_down(last), tpm.point_mlp_norm(last))
+        self._tp_add_norm(self.I, w.final_norm, lay.recv_down, tpm.point_down(last), tpm.point_mlp_norm(last),
+                          post=w.post_ff[last] if g else None)
         # vocab-parallel lm_head: this rank's columns into every rank's full logits
         self._tp_gemm(self.xn, w.lm_head, N.EPI_STORE, out_offset=lay.logits + self.tp.rank * self.Vl * 2,
                       ldy=self.V, wait=tpm.point_mlp_norm(last), signal=tpm.point_logits(self.L))
         N.check(lib.mvb_tp_wait(comm, tpm.point_logits(self.L), st), "tp_wait")
+        if self.final_softcap:   # every rank soft-caps its copy of the gathered logits
+            N.check(lib.mvb_softcap(self.logits.data_ptr(), B * self.V, self.final_softcap, N.BF16, st), "softcap")
         N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
                                self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
                                0, self.offset.data_ptr(), bf, st), "sample")
@@ -571,7 +578,7 @@ class DecodeRunner:
         if self.moe:   # 11 per layer: qkv, qk, attention, o_proj, add+norm, router, route, gather, 2 GEMMs, combine
             return 2 + self.L * 11 + (self.L - 1) + 3
         if self.tp.enabled:   # + the step-counter kernel and the wait before sampling
-            return 2 + self.L * 8 + (self.L - 1) + 3 + 2
+            return 2 + self.L * 8 + (self.L - 1) + 3 + 2 + (1 if self.final_softcap else 0)
         return 2 + self.L * 8 + (self.L - 1) + 3 + (1 if self.final_softcap else 0)
 
     # ------------------------------------------------------------------ graphs

@@ -52,8 +52,9 @@ def _engine(cfg, sd, tp, batch, lens, num_blocks):
     return eng
 
 
-def test_exchange_path_on_one_gpu_is_bit_identical():
-    cfg = get_config("qwen3-8b", num_hidden_layers=2)
+@pytest.mark.parametrize("arch", ["qwen3-8b", "gemma2-9b"])
+def test_exchange_path_on_one_gpu_is_bit_identical(arch):
+    cfg = get_config(arch, num_hidden_layers=2)
     sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device="cuda")
     batch, lens = 16, [40 + 31 * i for i in range(16)]
     plain = _engine(cfg, sd, TensorParallelConfig(1, 0), batch, lens, 512)
@@ -102,12 +103,13 @@ def test_wait_for_a_missing_signal_times_out_with_status():
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_tp1_teacher_forced(tmp_path):
+@pytest.mark.parametrize("arch", ["qwen3-8b", "gemma2-9b"])
+def test_tp2_matches_tp1_teacher_forced(tmp_path, arch):
     out = tmp_path / "tp2.json"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533", str(REPO / "tests" / "tp_worker.py"),
-           "--out", str(out), "--steps", "4"]
+           "--out", str(out), "--steps", "4", "--arch", arch]
     r = subprocess.run(cmd, env=env, cwd=REPO, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     rep = json.loads(out.read_text())

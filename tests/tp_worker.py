@@ -1,7 +1,8 @@
 """One rank of the tensor-parallel parity run (launched by tests/test_tensor_parallel_gpu.py via
 torch.distributed.run, one process per GPU).
 
-Every rank builds the same 2-layer model at Qwen3-8B layer dims and the same batch of sequences
+Every rank builds the same 2-layer model (Qwen3-8B or, with --arch gemma2-9b, Gemma-2-9B layer
+dims) and the same batch of sequences
 on a shuffled block pool, and decodes with the tensor-parallel engine.  Rank 0 also decodes the
 same workload on one GPU (TP=1) and compares, step by step under teacher forcing, the full
 logits and the greedy tokens; it writes a JSON report to --out.
@@ -56,6 +57,7 @@ def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", required=True)
     ap.add_argument("--steps", type=int, default=4)
+    ap.add_argument("--arch", default="qwen3-8b", choices=["qwen3-8b", "gemma2-9b"])
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -63,7 +65,7 @@ def main() -> int:
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     N.set_pdl(True)
-    cfg = get_config("qwen3-8b", num_hidden_layers=2)
+    cfg = get_config(args.arch, num_hidden_layers=2)
     batch = 16
     lens = [37 + 29 * i for i in range(batch)]          # ragged contexts, blocks cross boundaries
     num_blocks = 512
