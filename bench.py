@@ -502,20 +502,34 @@ def run_gemma2_case(args) -> None:
     """Gemma-2-9B-architecture decode (42 layers, hidden 3584, 16/8 heads of 256, GeGLU 14336,
     vocab 256000, alternating 4096-token sliding-window / global layers, soft-capping 50 / 30,
     tied embeddings), batch 16, 8192-token prompts with seeded synthetic K/V, greedy.  Same
-    timing rules as the headline line; per-kind kernel times as in the headline's `kernels`."""
+    timing rules as the headline line; per-kind kernel times as in the headline's `kernels`.  Under
+    torchrun, the N ranks form one tensor-parallel group over the same workload (strong scaling),
+    times are maxima over ranks and rank 0 prints."""
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        _gemma2_case(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+def _gemma2_case(args, rank: int, world: int, local: int) -> None:
     from llm_pytorch_inference_b200 import _native as N
     from llm_pytorch_inference_b200.configs import get_config
     from llm_pytorch_inference_b200.engine import DecodeEngine
+    from llm_pytorch_inference_b200.tensor_parallel import TensorParallelConfig
     from llm_pytorch_inference_b200.weights import canonical_state_dict
 
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
+    dev = torch.device("cuda", local)
     N.set_pdl(bool(args.pdl))
     cfg = get_config("gemma2-9b")
     B, prompt = 16, 8192
     W, K = args.warmup, args.steps
     sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev)
-    eng = DecodeEngine(cfg, sd, max_batch=B, max_model_len=prompt + 2 * (W + 2 * K) + 32, device=dev)
+    eng = DecodeEngine(cfg, sd, max_batch=B, max_model_len=prompt + 2 * (W + 2 * K) + 32, device=dev,
+                       tp=TensorParallelConfig(world, rank))
     del sd
     order = list(range(eng.kv.num_blocks))
     random.Random(0).shuffle(order)
@@ -526,7 +540,7 @@ def run_gemma2_case(args) -> None:
     for s in range(B):
         eng.add_sequence(s, torch.randint(0, cfg["vocab_size"], (prompt,), generator=g).tolist())
         eng.append_first_token(s, int(torch.randint(0, cfg["vocab_size"], (1,), generator=g)))
-    eng.prefill_synthetic(seed=0)
+    eng.prefill_synthetic(seed=rank)   # each rank fills its own KV heads
     eng.set_sampling(0.0, -1, 1.0)
     eng.prepare_first_step()
     r = eng.runner
@@ -535,8 +549,10 @@ def run_gemma2_case(args) -> None:
         eng.step()
     torch.cuda.synchronize(dev)
     metas = torch.stack([eng.plan_step(eng.runner.tokens_host[:B].tolist()) for _ in range(K)]).to(dev)
-    clocks = ClockSampler(0)
+    clocks = ClockSampler(local)
     clocks.start()
+    barrier(world)
+    torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for k in range(K):
@@ -544,19 +560,27 @@ def run_gemma2_case(args) -> None:
         r.replay()
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1) / K
+    ms = max_over_ranks(e0.elapsed_time(e1), world) / K
     step_bytes = r.algorithmic_step_bytes()
+    barrier(world)
+    torch.cuda.synchronize(dev)
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
     for _ in range(K):
         eng.step()
     e3.record(stream)
     torch.cuda.synchronize(dev)
-    e2e_ms = e2.elapsed_time(e3) / K
+    e2e_ms = max_over_ranks(e2.elapsed_time(e3), world) / K
     clk = clocks.stop()
     kinds = r.time_kernels(iters=max(8, r.L))
+    status = N.device_status(clear=True)
+    barrier(world)
+    r.close()
+    if rank != 0:
+        return
     pk = peaks()
     line = {"case": "gemma2", "metric": "decode tokens/s Gemma-2-9B-arch bf16 batch 16 ctx 8192 greedy",
+            "n_gpus": world, "parallelism": f"tp{world}",
             "value": round(B / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 4), "steps": K,
             "warmup": W, "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tokens/s"},
             "step_bytes": step_bytes,
@@ -566,8 +590,7 @@ def run_gemma2_case(args) -> None:
                             "gbs": round(v["gbs"], 1), "frac": round(v["gbs"] / pk["hbm_gbs"], 4),
                             "share_of_step": round(v["avg_ms"] * v["launches_per_step"] / ms, 4)}
                         for k, v in kinds.items()},
-            "launches_per_step": r.launches_per_step(), "clocks": clk,
-            "device_status": N.device_status(clear=True)}
+            "launches_per_step": r.launches_per_step(), "clocks": clk, "device_status": status}
     print(json.dumps(line), flush=True)
 
 
