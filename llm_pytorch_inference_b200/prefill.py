@@ -16,6 +16,12 @@ token from the last position's logits.  Here all prompts of a call are packed in
   down GEMM with the residual add;
 * the final RMSNorm and lm_head on each sequence's last row only, then the sampler.
 
+Gemma models (``models/gemma3_model.py:270-283``) take the same pass with their own layer: the
+embedding times its scale, (1 + w) norms, the o_proj and down outputs each post-normalised before
+the residual add (``mvb_rmsnorm`` in place, then ``mvb_fused_add_rmsnorm`` into the next norm),
+GeGLU on the stored gate_up product (``mvb_fused_mlp``), attention with the layer's soft-capping and
+window (one query per token row, head dim 256), and the final logits soft-capped.
+
 Rows are processed in chunks of whole sequences so the activations stay within a fixed budget
 next to the KV pool.
 """
@@ -25,7 +31,16 @@ import torch
 
 from . import _native as N
 
-_ATTN_ROWS = 4096   # query rows per attention launch (the kernel's limit on sequences)
+_ATTN_ROWS = 4096   # query rows per attention launch at head dim 128 (the kernel's limit on sequences)
+
+
+def _attention_rows(runner) -> int:
+    """Query rows per launch of the decode kernel: it takes up to 4096 (row, head group) pairs at
+    head dim 128, where one group holds all KV heads, and 1024 at head dim 256 (groups of 2 heads)."""
+    if runner.D == 128:
+        return _ATTN_ROWS
+    groups = runner.Hkv // (2 if runner.Hkv % 2 == 0 else 1)
+    return max(1, 1024 // groups)
 
 
 class BatchedPrefill:
@@ -33,7 +48,7 @@ class BatchedPrefill:
     and KV pool."""
 
     def __init__(self, runner, max_tokens: int = 16384):
-        if runner.moe or runner.gemma or runner.tp.enabled:
+        if runner.moe or runner.tp.enabled:
             raise NotImplementedError("batched prefill covers dense single-GPU models")
         self.r = runner
         self.max_tokens = max_tokens
@@ -45,9 +60,13 @@ class BatchedPrefill:
         self.q = torch.zeros(T, r.Hq, r.D, dtype=bf, device=dev)
         self.attn = torch.zeros(T, r.Hq * r.D, dtype=bf, device=dev)
         self.act = torch.zeros(T, r.I, dtype=bf, device=dev)
+        if r.gemma:   # the stored gate_up product (GeGLU is applied after it) and a post-norm buffer
+            self.gu = torch.zeros(T, 2 * r.I, dtype=bf, device=dev)
+            self.z = torch.zeros(T, r.H, dtype=bf, device=dev)
         self.gemm_ws = None
         self.timing: dict[str, list] | None = None   # kind -> [(start, end) CUDA events] when profiling
-        ws = N.lib().mvb_paged_attention_workspace_bytes(min(T, _ATTN_ROWS), r.Hq, r.D, dev.index)
+        self.attn_rows = _attention_rows(r)
+        ws = N.lib().mvb_paged_attention_workspace_bytes(min(T, self.attn_rows), r.Hq, r.D, dev.index)
         self.attn_ws = torch.zeros(ws, dtype=torch.uint8, device=dev)
 
     def _mark(self, kind: str):
@@ -137,9 +156,11 @@ class BatchedPrefill:
         kvc = r.kv.kv_cache
         N.check(lib.mvb_embedding(h.data_ptr(), tok_d.data_ptr(), N.I32, w.embed.data_ptr(), T, H, r.V,
                                   r.embed_scale, bf, st), "embedding")
+        g = r.gemma
         for i in range(L):
-            N.check(lib.mvb_rmsnorm(xn.data_ptr(), H, h.data_ptr(), H, w.ln1[i].data_ptr(), T, H, eps, r.plus_one,
-                                    N.NORM_MODEL, bf, st), "rmsnorm")
+            if not g or i == 0:   # a Gemma layer's input norm was formed by the previous layer's add
+                N.check(lib.mvb_rmsnorm(xn.data_ptr(), H, h.data_ptr(), H, w.ln1[i].data_ptr(), T, H, eps,
+                                        r.plus_one, N.NORM_MODEL, bf, st), "rmsnorm")
             self._gemm(qkv, xn, w.wqkv[i])
             cos, sin = r.layer_tables[i]
             N.check(lib.mvb_qk_norm_rope_kv_write(
@@ -153,8 +174,8 @@ class BatchedPrefill:
                     attn.data_ptr(), attn.stride(0), q.data_ptr(), r.Hq * D, kvc.data_ptr(), seq_bt_d.data_ptr(), mb,
                     seq_start_d.data_ptr(), seq_len_d.data_ptr(), tile_seq_d.data_ptr(), tile_idx_d.data_ptr(), nt,
                     r.Hq, r.Hkv, D, L, i, r.P, r.kv.block_size, r.scale, st), "prefill_attention")
-            for a0 in range(0, 0 if tiled else T, _ATTN_ROWS):
-                n = min(_ATTN_ROWS, T - a0)
+            for a0 in range(0, 0 if tiled else T, self.attn_rows):
+                n = min(self.attn_rows, T - a0)
                 N.check(lib.mvb_paged_attention_decode_ex(
                     attn[a0:].data_ptr(), attn.stride(0), q[a0:].data_ptr(), r.Hq * D, kvc.data_ptr(),
                     bt_d[a0:].data_ptr(), mb, ctx_d[a0:].data_ptr(), n, r.Hq, r.Hkv, D, L, i, r.P,
@@ -162,16 +183,46 @@ class BatchedPrefill:
                     self.attn_ws.numel(), st), "paged_attention_decode")
             if end is not None:
                 end.record()
+            if g:
+                self._gemma_mlp_block(i, T, h, xn, attn, act)
+                continue
             self._gemm(h, attn, w.wo[i], N.EPI_RESADD, aux=h)          # h = h + o_proj(attn)
             N.check(lib.mvb_rmsnorm(xn.data_ptr(), H, h.data_ptr(), H, w.ln2[i].data_ptr(), T, H, eps, r.plus_one,
                                     N.NORM_MODEL, bf, st), "rmsnorm")
             self._gemm(act, xn, w.wgu[i], N.EPI_SWIGLU)
             self._gemm(h, act, w.wdown[i], N.EPI_RESADD, aux=h)        # h = h + down(swiglu)
         last = torch.tensor([sum(lens[:k + 1]) - 1 for k in range(len(lens))], device=dev)
-        hl = h.index_select(0, last).contiguous()
-        xl = torch.empty_like(hl)
-        N.check(lib.mvb_rmsnorm(xl.data_ptr(), H, hl.data_ptr(), H, w.final_norm.data_ptr(), len(lens), H, eps,
-                                r.plus_one, N.NORM_MODEL, bf, st), "rmsnorm")
+        if g:   # xn already holds the final norm of every row
+            xl = xn.index_select(0, last).contiguous()
+        else:
+            hl = h.index_select(0, last).contiguous()
+            xl = torch.empty_like(hl)
+            N.check(lib.mvb_rmsnorm(xl.data_ptr(), H, hl.data_ptr(), H, w.final_norm.data_ptr(), len(lens), H, eps,
+                                    r.plus_one, N.NORM_MODEL, bf, st), "rmsnorm")
         logits = torch.empty(len(lens), r.V, dtype=torch.bfloat16, device=dev)
         self._gemm(logits, xl, w.lm_head)
+        if r.final_softcap:
+            N.check(lib.mvb_softcap(logits.data_ptr(), logits.numel(), r.final_softcap, bf, st), "softcap")
         return logits
+
+    def _gemma_mlp_block(self, i, T, h, xn, attn, act) -> None:
+        """The rest of Gemma layer i after attention (gemma3_model.py:274-281): o_proj, its post-norm,
+        residual add + pre-feed-forward norm, gate_up, GeGLU, down, its post-norm, residual add + the
+        next layer's input norm (the final norm after the last layer)."""
+        r, lib, w = self.r, N.lib(), self.r.w
+        H, eps, bf, st = r.H, r.eps, N.BF16, N.stream_handle(r.dev)
+        z, gu = self.z[:T], self.gu[:T]
+
+        def post_add_norm(post_w, next_w):
+            # z = RMSNorm(z; post_w) in place, then h += z, xn = RMSNorm(h; next_w)
+            N.check(lib.mvb_rmsnorm(z.data_ptr(), H, z.data_ptr(), H, post_w.data_ptr(), T, H, eps, r.plus_one,
+                                    N.NORM_MODEL, bf, st), "rmsnorm")
+            N.check(lib.mvb_fused_add_rmsnorm(xn.data_ptr(), h.data_ptr(), z.data_ptr(), next_w.data_ptr(), T, H,
+                                              eps, r.plus_one, N.NORM_MODEL, bf, st), "fused_add_rmsnorm")
+
+        self._gemm(z, attn, w.wo[i])
+        post_add_norm(w.ln2[i], w.pre_ff[i])
+        self._gemm(gu, xn, w.wgu[i])
+        N.check(lib.mvb_fused_mlp(act.data_ptr(), gu.data_ptr(), T, r.I, r.act, bf, st), "fused_mlp")
+        self._gemm(z, act, w.wdown[i])
+        post_add_norm(w.post_ff[i], w.ln1[i + 1] if i + 1 < r.L else w.final_norm)

@@ -18,9 +18,13 @@ from oracle.engine import OracleEngine
 pytestmark = pytest.mark.gpu
 
 
-def _run(arch, lens, num_blocks, max_tokens=16384, seed=3):
+def _run(arch, lens, num_blocks, max_tokens=16384, seed=3, norm_jitter=None):
     cfg = get_config(arch)
     sd = canonical_state_dict(cfg, 0, torch.float32)
+    if norm_jitter is not None:
+        from llm_pytorch_inference_b200.weights import jitter_norms
+
+        sd = jitter_norms(sd, norm_jitter)
     order = list(range(num_blocks))
     random.Random(0).shuffle(order)
     g = torch.Generator().manual_seed(seed)
@@ -75,6 +79,27 @@ def test_prefill_tiny_matches_oracle_and_decodes_on():
     eng.force_last_tokens(ref_tok)
     alt.kv_pool.copy_(oracle.kv_pool)
     _compare_teacher_forced(oracle, alt, eng, 6)
+
+
+@pytest.mark.parametrize("arch,lens", [
+    ("gemma3-tiny", [37, 50, 16, 64, 5]),         # the reference's Gemma 3: QK-norm, local/global theta
+    ("gemma2-tiny", [40, 51, 9, 70, 33, 300]),     # softcaps, 32-token sliding window, prompts past it
+])
+def test_gemma_prefill_matches_oracle_and_decodes_on(arch, lens):
+    """The Gemma layer in the batched prefill (sandwich norms, GeGLU, head dim 256 attention with
+    soft-capping and the window, final soft-capping) against the oracle's per-sequence prefill."""
+    from test_decode_gpu import _compare_teacher_forced
+
+    cfg, prompts, oracle, alt, eng, ref, ref_alt, first = _run(arch, lens, 256, norm_jitter=1)
+    _check_logits(eng.last_prefill_logits.float().cpu(), ref, ref_alt)
+    _check_kv(eng, oracle, alt, prompts)
+    ref_tok = osamp.greedy(ref).tolist()
+    for i in range(len(prompts)):
+        oracle.append(i, ref_tok[i])
+        alt.append(i, ref_tok[i])
+    eng.force_last_tokens(ref_tok)
+    alt.kv_pool.copy_(oracle.kv_pool)
+    _compare_teacher_forced(oracle, alt, eng, 4)
 
 
 def test_prefill_chunks_and_row_tiles_at_qwen3_8b_dims():
