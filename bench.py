@@ -54,12 +54,14 @@ def parse_args(argv=None):
     ap.add_argument("--layers", type=int, default=None, help="override layer count (debug only; invalid bench)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pdl", type=int, default=1)
-    ap.add_argument("--case", default=None, choices=["kernels", "moe", "gemma2", "prefill"],
+    ap.add_argument("--case", default=None, choices=["kernels", "moe", "gemma2", "prefill", "prefill-kernels"],
                     help="kernels: small profiling case (2 layers of the workload's dims), each kernel kind "
                          "launched a few times; prints per-kernel timings only.  moe: the sparse-MoE decode "
                          "workload (Qwen3-30B-A3B arch, batch 32, prompt 4096, greedy), 1 GPU.  gemma2: the "
                          "Gemma-2-9B-arch decode workload (batch 16, prompt 8192, greedy), 1 GPU.  prefill: "
-                         "batched prefill of the headline's 64 x 2048-token prompts (Qwen3-8B arch), 1 GPU")
+                         "batched prefill of the headline's 64 x 2048-token prompts (Qwen3-8B arch), 1 GPU.  "
+                         "prefill-kernels: small profiling case of the prefill (2 layers at Qwen3-8B dims, "
+                         "8 x 2048-token prompts, ~5 GB on the device)")
     ap.add_argument("--arch", default=None, choices=["qwen3-8b", "gemma2-9b"],
                     help="--case kernels: the layer dims (qwen3-8b: batch 64, prompt 2048; gemma2-9b: batch 16, "
                          "prompt 8192)")
@@ -663,6 +665,35 @@ def run_prefill_case(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_prefill_kernel_case(args) -> None:
+    """Profiling case of the prefill: 2 layers at Qwen3-8B dims, a pool sized to its prompts.  One
+    warm-up prefill of a 300-token prompt (2 attention and 9 GEMM launches), then one prefill of 8
+    prompts of 2048 tokens (16384 rows: one chunk); prints the per-kind device times of the second."""
+    from llm_pytorch_inference_b200 import _native as N
+    from llm_pytorch_inference_b200.configs import get_config
+    from llm_pytorch_inference_b200.engine import DecodeEngine
+    from llm_pytorch_inference_b200.weights import canonical_state_dict
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    N.set_pdl(bool(args.pdl))
+    cfg = get_config(ARCH, num_hidden_layers=2)
+    B, prompt = 8, PROMPT
+    sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev)
+    nblk = (B + 1) * ((prompt + 16) // 16) + 16
+    eng = DecodeEngine(cfg, sd, max_batch=B + 1, max_model_len=prompt + 64, num_blocks=nblk, device=dev)
+    del sd
+    g = torch.Generator().manual_seed(0)
+    eng.prefill({B: torch.randint(0, cfg["vocab_size"], (300,), generator=g).tolist()})   # warm-up
+    torch.cuda.synchronize(dev)
+    eng._prefill.timing = {}
+    eng.prefill({s: torch.randint(0, cfg["vocab_size"], (prompt,), generator=g).tolist() for s in range(B)})
+    torch.cuda.synchronize(dev)
+    kind_ms = {k: round(sum(a.elapsed_time(b) for a, b in v), 3) for k, v in eng._prefill.timing.items()}
+    print(json.dumps({"case": "prefill-kernels", "tokens": B * prompt, "kind_ms": kind_ms,
+                      "device_status": N.device_status(clear=True)}), flush=True)
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
     if args.case == "kernels":
@@ -673,6 +704,9 @@ def main(argv=None) -> int:
         return 0
     if args.case == "prefill":
         run_prefill_case(args)
+        return 0
+    if args.case == "prefill-kernels":
+        run_prefill_kernel_case(args)
         return 0
     if args.case == "moe":
         run_moe_case(args)
