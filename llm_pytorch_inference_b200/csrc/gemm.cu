@@ -16,7 +16,7 @@
 //
 // More than 256 rows (a prefill's tokens) are cut into row tiles of 256: the output tiles are the
 // (weight tile, row tile) pairs, weight-major, so consecutive tiles of a CTA reuse one weight slab
-// from L2.
+// from L2.  With an even number of weight tiles they go to gemm_rows_kernel (256 x 256 tiles, below).
 //
 // Warp roles (192 threads):  warp 0 TMA producer, warp 1 TMEM alloc + MMA issue,
 // warps 2-5 epilogue (TMEM -> registers -> global).  Accumulators are double
@@ -59,13 +59,17 @@ __device__ __forceinline__ int cta_of(int64_t x, int64_t total, int grid) {
   return static_cast<int>(((x + 1) * grid + total - 1) / total - 1);
 }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier of the 128 threads (4 warps) that share one accumulator's epilogue.
+template <int BAR = 1>
+__device__ __forceinline__ void epi_bar() {
+  asm volatile("bar.sync %0, 128;" ::"n"(BAR) : "memory");
+}
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
 // Final epilogue for 32 batch columns [c0, c0+32) of feature `row` of weight tile t, rows
 // r0 + c0 .. of Y.
-template <int BN>
+template <int BN, int BAR = 1>
 __device__ __forceinline__ void epilogue_store(const GemmArgs& a, const TpGemm& tp, const float (&v)[32], int t,
                                                int row, int c0, float* xbuf, int r0) {
   if (a.epilogue == MVB_EPI_SWIGLU) {
@@ -76,7 +80,7 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs& a, const TpGemm& 
 #pragma unroll
       for (int j = 0; j < 32; ++j) xbuf[r * 33 + j] = bf16_round(v[j]);
     }
-    epi_bar();
+    epi_bar<BAR>();
     if (!is_up) {
       const int f = 64 * t + r;
       if (f < a.inter) {
@@ -91,7 +95,7 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs& a, const TpGemm& 
         }
       }
     }
-    epi_bar();
+    epi_bar<BAR>();
     return;
   }
   const int nn = t * BM + row;
@@ -394,6 +398,212 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
   }
 }
 
+// Prefill GEMMs (more than 256 rows, an even number of weight tiles): 256 x 256 output tiles, two
+// weight tiles (UMMA M = 128 each) against one 256-row activation box.  Per k-block a CTA loads
+// 64 KB for 2 x 128 x 256 x 64 multiply-adds, two thirds of the bytes per product of the 128 x 256
+// tile, whose operand traffic from L2 holds the tensor pipe near 55 %.  The two accumulators fill
+// TMEM (512 columns), so a tile's epilogue does not overlap the next tile's MMAs; eight epilogue
+// warps (a TMEM lane quarter of one accumulator each) keep it short.  Tiles are whole and
+// weight-major, a contiguous range per CTA: no split-K, no merge, the same sums on any grid.
+constexpr int kRowsThreads = 320;  // warp 0 TMA, warp 1 TMEM + MMA, warps 2-9 epilogue
+constexpr int kRowsStages = 3;
+
+template <int STAGES>
+__global__ void __launch_bounds__(kRowsThreads, 1)
+    gemm_rows_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                     const GemmArgs a, const __grid_constant__ TpGemm tp) {
+  constexpr int BN = 256;
+  constexpr int B_STAGE = BN * BK * 2;                     // 32 KB
+  constexpr uint32_t STAGE_BYTES = 2 * A_STAGE + B_STAGE;  // 64 KB
+  constexpr uint32_t TMEM_COLS = 2 * BN;                   // accumulators of weight tiles 2tw, 2tw + 1
+  constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;                    // [stage][half] 16 KB weight boxes
+  uint8_t* sB = sA + STAGES * 2 * A_STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;  // accumulators full (MMA -> epilogue)
+  uint64_t* acce = accf + 1;        // accumulators drained (epilogue -> MMA)
+  uint64_t* drain = acce + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* xbuf = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 256);  // 2 x 64 x 33 floats (SWIGLU)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t_begin = static_cast<int>(range_start(blockIdx.x, a.tiles, gridDim.x));
+  const int t_end = static_cast<int>(range_start(blockIdx.x + 1, a.tiles, gridDim.x));
+  const int my_kb = (t_end - t_begin) * a.kblocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accf, 1);
+    mbar_init(acce, kRowsThreads - 64);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
+  int issued = 0;  // producer: loads issued
+  if (warp == 0) {
+    if (lane == 0 && my_kb > 0) {
+      prefetch_tmap(&tmW);
+      prefetch_tmap(&tmX);
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      const bool swiglu = a.epilogue == MVB_EPI_SWIGLU;
+      auto load_w = [&](int it) {
+        const int s = it % STAGES;
+        const int lt = t_begin + it / a.kblocks;
+        const int kb = it % a.kblocks;
+        const int tw = lt / a.mt;  // weight tiles 2tw, 2tw + 1
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint8_t* dst = sA + (s * 2 + h) * A_STAGE;
+          const int t = 2 * tw + h;
+          if (swiglu) {
+            tma_load_2d(dst, &tmW, &full[s], kb * BK, 64 * t, pol_w);
+            tma_load_2d(dst + A_STAGE / 2, &tmW, &full[s], kb * BK, a.inter + 64 * t, pol_w);
+          } else {
+            tma_load_2d(dst, &tmW, &full[s], kb * BK, BM * t, pol_w);
+          }
+        }
+      };
+      auto load_x = [&](int it) {
+        const int s = it % STAGES;
+        const int lt = t_begin + it / a.kblocks;
+        const int kb = it % a.kblocks;
+        tma_load_2d(sB + s * B_STAGE, &tmX, &full[s], kb * BK, (lt % a.mt) * BN, pol_x);  // row tile
+      };
+      // Weights do not depend on the previous kernel: start streaming them before the
+      // grid-dependency wait, then add the activation boxes to the same stages.
+      const int pro = my_kb < STAGES ? my_kb : STAGES;
+      for (int it = 0; it < pro; ++it) {
+        mbar_arrive_expect_tx(&full[it], STAGE_BYTES);
+        load_w(it);
+      }
+      pdl_wait();
+      for (int it = 0; it < pro; ++it) load_x(it);
+      issued = pro;
+      for (int it = pro; it < my_kb; ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err)) break;
+        mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+        load_w(it);
+        load_x(it);
+        issued = it + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && my_kb > 0) {
+      int it = 0;
+      bool ok = true;
+      for (int lt = t_begin; ok && lt < t_end; ++lt) {
+        const int seg = lt - t_begin;
+        if (!mbar_wait(acce, (seg & 1) ^ 1, abort_flag, a.err)) break;
+        tc_fence_after();
+        for (int kb = 0; kb < a.kblocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag, a.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t a0 = umma_desc_sw128(smem_u32(sA + (s * 2) * A_STAGE));
+          const uint64_t a1 = umma_desc_sw128(smem_u32(sA + (s * 2 + 1) * A_STAGE));
+          const uint64_t bd = umma_desc_sw128(smem_u32(sB + s * B_STAGE));
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+            umma_bf16(tmem_base, a0 + 2 * kk, bd + 2 * kk, IDESC, acc);
+            umma_bf16(tmem_base + BN, a1 + 2 * kk, bd + 2 * kk, IDESC, acc);
+          }
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(accf);
+      }
+      // Drain: every MMA issued above has completed before TMEM is released.
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, a.err);
+    }
+  } else {
+    // Epilogue warps 2..9: warp w reads TMEM lanes 32*(w%4) .. +31 of accumulator h = (w-2)/4.
+    pdl_wait();
+    const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
+    const int row = q * 32 + lane;
+    float* xb = xbuf + h * 64 * 33;
+    for (int lt = t_begin; lt < t_end; ++lt) {
+      const int seg = lt - t_begin;
+      if (!mbar_wait(accf, seg & 1, abort_flag, a.err)) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(h * BN);
+      const int t = 2 * (lt / a.mt) + h;
+      const int r0 = (lt % a.mt) * BN;
+      for (int c0 = 0; c0 < BN && r0 + c0 < a.m; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld_x32(tb + c0, r);
+        tmem_ld_wait();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (h == 0)
+          epilogue_store<BN, 1>(a, tp, v, t, row, c0, xb, r0);
+        else
+          epilogue_store<BN, 2>(a, tp, v, t, row, c0, xb, r0);
+      }
+      tc_fence_before();
+      mbar_arrive(acce);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 0 && lane == 0) {
+    // Wait (bounded) for the copies still in flight when a wait gave up.
+    const int first = issued > STAGES ? issued - STAGES : 0;
+    for (int it = first; it < issued; ++it) mbar_wait(&full[it % STAGES], (it / STAGES) & 1, nullptr, a.err);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+size_t rows_smem() {
+  return static_cast<size_t>(kRowsStages) * (2 * A_STAGE + 256 * BK * 2) + 256 + 2 * 64 * 33 * 4 + 1024;
+}
+
+int launch_gemm_rows(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, const TpGemm& tp, int grid,
+                     cudaStream_t st) {
+  const size_t smem = rows_smem();
+  static unsigned long long done_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !(done_mask & (1ull << dev))) {
+    MVB_TRY(set_smem(gemm_rows_kernel<kRowsStages>, smem, "gemm: smem attribute"));
+    if (dev < 64) done_mask |= 1ull << dev;
+  }
+  return launch("gemm_bf16_rows", gemm_rows_kernel<kRowsStages>, dim3(grid), dim3(kRowsThreads), smem, st, tw, tx,
+                a, tp);
+}
+
 template <int BN>
 constexpr int stages_for() {
   return BN == 64 ? 4 : (BN == 128 ? 6 : 4);
@@ -531,8 +741,16 @@ int gemm_launch(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
   a.partials = static_cast<float*>(workspace);
   a.counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + ws_end - cbytes);
   a.err = device_status_ptr();
-  if (grid_out) *grid_out = grid;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t wtiles = tiles_for(n, epilogue);
+  if (mt > 1 && wtiles % 2 == 0) {
+    // Prefill rows: 256 x 256 tiles (weight tiles 2tw, 2tw + 1 against one row tile), whole.
+    a.tiles = static_cast<int>(wtiles / 2 * mt);
+    const int rgrid = a.tiles < sms ? a.tiles : sms;
+    if (grid_out) *grid_out = rgrid;
+    return launch_gemm_rows(tw, tx, a, tp, rgrid, st);
+  }
+  if (grid_out) *grid_out = grid;
   switch (bn) {
     case 64: return launch_gemm<64>(tw, tx, a, tp, grid, st);
     case 128: return launch_gemm<128>(tw, tx, a, tp, grid, st);

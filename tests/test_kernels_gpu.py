@@ -125,10 +125,12 @@ def test_gemm_store_matches_fp32(m, n, k):
     assert torch.equal(ops.linear(x, w), y)  # deterministic split-K merge
 
 
-@pytest.mark.parametrize("m,n,k", [(257, 1024, 512), (700, 4096, 4096), (2049, 6144, 4096), (4096, 512, 12288)])
+@pytest.mark.parametrize("m,n,k", [(257, 1024, 512), (700, 4096, 4096), (2049, 6144, 4096), (4096, 512, 12288),
+                                   (300, 384, 256)])
 def test_gemm_row_tiles_for_prefill(m, n, k):
     """More than 256 rows (a prefill's tokens): row tiles of 256, ragged last tile; the three
-    epilogues a prefill uses (store, SwiGLU, residual add)."""
+    epilogues a prefill uses (store, SwiGLU, residual add).  An even number of weight tiles takes
+    the 256 x 256 tile kernel; n = 384 (3 weight tiles, 3 SwiGLU pairs) the 128 x 256 one."""
     g = torch.Generator(device=DEV).manual_seed(m + n + k)
     x = (torch.randn(m, k, device=DEV, generator=g) / math.sqrt(k)).to(torch.bfloat16)
     w = torch.randn(n, k, device=DEV, generator=g).to(torch.bfloat16)
