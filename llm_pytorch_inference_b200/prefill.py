@@ -22,6 +22,12 @@ the residual add (``mvb_rmsnorm`` in place, then ``mvb_fused_add_rmsnorm`` into 
 GeGLU on the stored gate_up product (``mvb_fused_mlp``), attention with the layer's soft-capping and
 window (one query per token row, head dim 256), and the final logits soft-capped.
 
+Sparse-MoE models (``models/qwen3_moe_model.py:39-66``, every layer sparse) replace the MLP with the
+decode step's MoE kernels: the router GEMM over all rows, then per 256-row chunk (the routing
+kernel's limit) routing + dispatch order, gather, the grouped gate/up (SwiGLU) and down GEMMs over
+the active experts and the expert-ordered combine; the residual add is fused with the next layer's
+input norm (``mvb_fused_add_rmsnorm``), as in the decode step.
+
 Rows are processed in chunks of whole sequences so the activations stay within a fixed budget
 next to the KV pool.
 """
@@ -32,6 +38,7 @@ import torch
 from . import _native as N
 
 _ATTN_ROWS = 4096   # query rows per attention launch at head dim 128 (the kernel's limit on sequences)
+_MOE_ROWS = 256     # token rows per MoE routing / dispatch launch (mvb_moe_route's limit)
 
 
 def _attention_rows(runner) -> int:
@@ -44,12 +51,12 @@ def _attention_rows(runner) -> int:
 
 
 class BatchedPrefill:
-    """Prefill of dense (Qwen3 / Llama-family) models through a ``DecodeRunner``'s weights, tables
-    and KV pool."""
+    """Prefill of dense (Qwen3 / Llama-family), Gemma and sparse-MoE models through a
+    ``DecodeRunner``'s weights, tables and KV pool, on one GPU."""
 
     def __init__(self, runner, max_tokens: int = 16384):
-        if runner.moe or runner.tp.enabled:
-            raise NotImplementedError("batched prefill covers dense single-GPU models")
+        if runner.tp.enabled:
+            raise NotImplementedError("batched prefill covers single-GPU models")
         self.r = runner
         self.max_tokens = max_tokens
         r, dev, bf = runner, runner.dev, torch.bfloat16
@@ -59,7 +66,20 @@ class BatchedPrefill:
         self.qkv = torch.zeros(T, (r.Hq + 2 * r.Hkv) * r.D, dtype=bf, device=dev)
         self.q = torch.zeros(T, r.Hq, r.D, dtype=bf, device=dev)
         self.attn = torch.zeros(T, r.Hq * r.D, dtype=bf, device=dev)
-        self.act = torch.zeros(T, r.I, dtype=bf, device=dev)
+        self.act = torch.zeros(0 if r.moe else T, r.I, dtype=bf, device=dev)
+        if r.moe:   # routing / dispatch state of one 256-row chunk; the router logits of all rows
+            C, E, K, i32 = _MOE_ROWS, r.E, r.K, torch.int32
+            self.router_logits = torch.zeros(T, E, dtype=bf, device=dev)
+            self.topk_ids = torch.zeros(C, K, dtype=i32, device=dev)
+            self.topk_w = torch.zeros(C, K, dtype=torch.float32, device=dev)
+            self.pair_row = torch.zeros(C, K, dtype=i32, device=dev)
+            self.row_token = torch.zeros(C * K, dtype=i32, device=dev)
+            self.expert_off = torch.zeros(E + 1, dtype=i32, device=dev)
+            self.active = torch.zeros(E + 1, dtype=i32, device=dev)
+            self.x_sorted = torch.zeros(C * K, r.H, dtype=bf, device=dev)
+            self.h_sorted = torch.zeros(C * K, r.Im, dtype=bf, device=dev)
+            self.y_sorted = torch.zeros(C * K, r.H, dtype=bf, device=dev)
+            self.moe_out = torch.zeros(T, r.H, dtype=bf, device=dev)
         if r.gemma:   # the stored gate_up product (GeGLU is applied after it) and a post-norm buffer
             self.gu = torch.zeros(T, 2 * r.I, dtype=bf, device=dev)
             self.z = torch.zeros(T, r.H, dtype=bf, device=dev)
@@ -156,9 +176,9 @@ class BatchedPrefill:
         kvc = r.kv.kv_cache
         N.check(lib.mvb_embedding(h.data_ptr(), tok_d.data_ptr(), N.I32, w.embed.data_ptr(), T, H, r.V,
                                   r.embed_scale, bf, st), "embedding")
-        g = r.gemma
+        g, moe = r.gemma, r.moe
         for i in range(L):
-            if not g or i == 0:   # a Gemma layer's input norm was formed by the previous layer's add
+            if not (g or moe) or i == 0:   # else the previous layer's add formed this layer's input norm
                 N.check(lib.mvb_rmsnorm(xn.data_ptr(), H, h.data_ptr(), H, w.ln1[i].data_ptr(), T, H, eps,
                                         r.plus_one, N.NORM_MODEL, bf, st), "rmsnorm")
             self._gemm(qkv, xn, w.wqkv[i])
@@ -189,10 +209,17 @@ class BatchedPrefill:
             self._gemm(h, attn, w.wo[i], N.EPI_RESADD, aux=h)          # h = h + o_proj(attn)
             N.check(lib.mvb_rmsnorm(xn.data_ptr(), H, h.data_ptr(), H, w.ln2[i].data_ptr(), T, H, eps, r.plus_one,
                                     N.NORM_MODEL, bf, st), "rmsnorm")
+            if moe:   # h = h + moe(xn), xn = the next layer's input norm (the final norm after the last)
+                out = self.moe_out[:T]
+                self._moe_block(i, T, xn, out)
+                nw = w.ln1[i + 1] if i + 1 < L else w.final_norm
+                N.check(lib.mvb_fused_add_rmsnorm(xn.data_ptr(), h.data_ptr(), out.data_ptr(), nw.data_ptr(), T, H,
+                                                  eps, r.plus_one, N.NORM_MODEL, bf, st), "fused_add_rmsnorm")
+                continue
             self._gemm(act, xn, w.wgu[i], N.EPI_SWIGLU)
             self._gemm(h, act, w.wdown[i], N.EPI_RESADD, aux=h)        # h = h + down(swiglu)
         last = torch.tensor([sum(lens[:k + 1]) - 1 for k in range(len(lens))], device=dev)
-        if g:   # xn already holds the final norm of every row
+        if g or moe:   # xn already holds the final norm of every row
             xl = xn.index_select(0, last).contiguous()
         else:
             hl = h.index_select(0, last).contiguous()
@@ -204,6 +231,34 @@ class BatchedPrefill:
         if r.final_softcap:
             N.check(lib.mvb_softcap(logits.data_ptr(), logits.numel(), r.final_softcap, bf, st), "softcap")
         return logits
+
+    def _moe_block(self, i, T, xn, out) -> None:
+        """The sparse MoE block of layer i on ``xn`` into ``out`` (``qwen3_moe_model.py:39-65``): the
+        router GEMM over all T rows, then per chunk of up to 256 rows the decode step's routing,
+        gather, grouped SwiGLU and down GEMMs over the chunk's active experts, and combine."""
+        r, lib, w = self.r, N.lib(), self.r.w
+        H, E, K, st = r.H, r.E, r.K, N.stream_handle(r.dev)
+        rl = self.router_logits[:T]
+        self._gemm(rl, xn, w.router[i])
+        end = self._mark("moe")
+        for c0 in range(0, T, _MOE_ROWS):
+            n = min(_MOE_ROWS, T - c0)
+            N.check(lib.mvb_moe_route(rl[c0:].data_ptr(), n, E, K, r.norm_topk, self.topk_ids.data_ptr(),
+                                      self.topk_w.data_ptr(), self.pair_row.data_ptr(), self.row_token.data_ptr(),
+                                      self.expert_off.data_ptr(), self.active.data_ptr(), st), "moe_route")
+            N.check(lib.mvb_moe_gather(self.x_sorted.data_ptr(), xn[c0:].data_ptr(), H, self.row_token.data_ptr(),
+                                       n * K, st), "moe_gather")
+            N.check(lib.mvb_moe_gemm_bf16(self.h_sorted.data_ptr(), r.Im, self.x_sorted.data_ptr(), H,
+                                          w.egu[i].data_ptr(), 2 * r.Im, H, E, n * K, n, N.EPI_SWIGLU,
+                                          self.expert_off.data_ptr(), self.active.data_ptr(), st), "moe_gemm gate_up")
+            N.check(lib.mvb_moe_gemm_bf16(self.y_sorted.data_ptr(), H, self.h_sorted.data_ptr(), r.Im,
+                                          w.edown[i].data_ptr(), H, r.Im, E, n * K, n, N.EPI_STORE,
+                                          self.expert_off.data_ptr(), self.active.data_ptr(), st), "moe_gemm down")
+            N.check(lib.mvb_moe_combine(out[c0:].data_ptr(), self.y_sorted.data_ptr(), self.topk_w.data_ptr(),
+                                        self.topk_ids.data_ptr(), self.pair_row.data_ptr(), n, K, H, st),
+                    "moe_combine")
+        if end is not None:
+            end.record()
 
     def _gemma_mlp_block(self, i, T, h, xn, attn, act) -> None:
         """The rest of Gemma layer i after attention (gemma3_model.py:274-281): o_proj, its post-norm,

@@ -55,7 +55,9 @@ def test_route_matches_oracle_and_dispatch_is_consistent(B, E, K):
         assert toks == sorted(toks)
 
 
-@pytest.mark.parametrize("B,E,K,H,I", [(32, 128, 8, 2048, 768), (5, 16, 4, 512, 128), (64, 32, 4, 256, 192)])
+@pytest.mark.parametrize("B,E,K,H,I", [(32, 128, 8, 2048, 768), (5, 16, 4, 512, 128), (64, 32, 4, 256, 192),
+                                       (128, 8, 2, 256, 128),     # 128-row tiles (up to 128 rows per expert)
+                                       (256, 16, 4, 512, 128)])   # 256-row tiles: a prefill chunk's expert groups
 def test_grouped_expert_gemms_match_fp32(B, E, K, H, I):
     g = torch.Generator().manual_seed(E + H + I)
     logits = torch.randn(B, E, generator=g).to(torch.bfloat16)

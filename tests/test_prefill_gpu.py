@@ -18,7 +18,7 @@ from oracle.engine import OracleEngine
 pytestmark = pytest.mark.gpu
 
 
-def _run(arch, lens, num_blocks, max_tokens=16384, seed=3, norm_jitter=None):
+def _run(arch, lens, num_blocks, max_tokens=16384, seed=3, norm_jitter=None, on_oracle=None):
     cfg = get_config(arch)
     sd = canonical_state_dict(cfg, 0, torch.float32)
     if norm_jitter is not None:
@@ -32,6 +32,8 @@ def _run(arch, lens, num_blocks, max_tokens=16384, seed=3, norm_jitter=None):
     oracle = OracleEngine(cfg, sd, torch.bfloat16, num_blocks, 16, list(order), prefill_last_only=True)
     alt = OracleEngine(cfg, sd, torch.bfloat16, num_blocks, 16, list(order), sdpa_backend=SDPBackend.MATH,
                        prefill_last_only=True, capped_rounding="eager")
+    if on_oracle is not None:
+        on_oracle(oracle)
     ref = torch.stack([oracle.prefill(i, p) for i, p in enumerate(prompts)])
     ref_alt = torch.stack([alt.prefill(i, p) for i, p in enumerate(prompts)])
     eng = DecodeEngine(cfg, {k: v.to(torch.bfloat16) for k, v in sd.items()}, max_batch=len(prompts),
@@ -48,8 +50,10 @@ def _check_logits(got, ref, ref_alt):
     assert float(d.mean()) <= max(2e-3, 1.25 * float(n.mean())), (float(d.mean()), float(n.mean()))
 
 
-def _check_kv(eng, oracle, alt, prompts):
-    """Every prompt position's K and V in every layer, against the oracle's pool."""
+def _check_kv(eng, oracle, alt, prompts, skip=None):
+    """Every prompt position's K and V in every layer, against the oracle's pool.  ``skip`` maps a
+    sequence to (layer, position): its K/V from that layer on, at that position and after, are left
+    out (a routing flip upstream of them, see the MoE test)."""
     got_pool = eng.kv.kv_cache[:, :, :oracle.kv_pool.shape[2]].float().cpu()
     for s, p in enumerate(prompts):
         bt = oracle.blocks.get_block_table(s)
@@ -59,6 +63,9 @@ def _check_kv(eng, oracle, alt, prompts):
         ref = oracle.kv_pool[:, :, rows, offs].float()
         spread = (alt.kv_pool[:, :, rows, offs].float() - ref).abs()
         d = (got - ref).abs()
+        if skip and s in skip:
+            layer, t0 = skip[s]
+            d[layer:, :, t0:] = 0
         assert float(d.max()) <= max(6e-2, 1.5 * float(spread.max())), (s, float(d.max()), float(spread.max()))
         assert float(d.mean()) <= max(4e-3, 1.25 * float(spread.mean())), (s, float(d.mean()))
 
@@ -93,6 +100,78 @@ def test_gemma_prefill_matches_oracle_and_decodes_on(arch, lens):
     cfg, prompts, oracle, alt, eng, ref, ref_alt, first = _run(arch, lens, 256, norm_jitter=1)
     _check_logits(eng.last_prefill_logits.float().cpu(), ref, ref_alt)
     _check_kv(eng, oracle, alt, prompts)
+    ref_tok = osamp.greedy(ref).tolist()
+    for i in range(len(prompts)):
+        oracle.append(i, ref_tok[i])
+        alt.append(i, ref_tok[i])
+    eng.force_last_tokens(ref_tok)
+    alt.kv_pool.copy_(oracle.kv_pool)
+    _compare_teacher_forced(oracle, alt, eng, 4)
+
+
+def test_moe_prefill_matches_oracle_and_decodes_on(monkeypatch):
+    """Sparse-MoE prefill (router GEMM over all rows; routing, expert GEMMs and combine per chunk of
+    256 rows, which the 200-token prompt straddles) against the oracle's per-sequence prefill (the
+    reference's Qwen3-MoE model), then teacher-forced decode steps.
+
+    Routing is discrete: where a token's K-th and (K+1)-th router logits lie closer than the bf16
+    noise of the logits (the attention output feeding the router differs in its last bits), the two
+    computations may pick different expert sets.  Both sides' router logits are recorded; a token
+    whose top-k set differs must be such a near tie, few tokens may be, and what such a flip feeds
+    (its sequence's K/V in later layers, from that token on; its sequence's logits) is left out of
+    the comparison.  Everything else meets the dense bars."""
+    from test_decode_gpu import _compare_teacher_forced
+    from llm_pytorch_inference_b200 import prefill as pf
+    from oracle.model import moe_route
+
+    got_logits, ref_logits = {}, {}
+    orig_block = pf.BatchedPrefill._moe_block
+
+    def gpu_block(self, i, T, xn, out):
+        orig_block(self, i, T, xn, out)
+        got_logits[i] = self.router_logits[:T].float().cpu()
+
+    monkeypatch.setattr(pf.BatchedPrefill, "_moe_block", gpu_block)
+
+    def hook(oracle):
+        m, orig_route = oracle.model, oracle.model.route
+
+        def route(i, flat):
+            ref_logits.setdefault(i, []).append(
+                torch.nn.functional.linear(flat, m.w[f"model.layers.{i}.mlp.gate.weight"]).float())
+            return orig_route(i, flat)
+
+        m.route = route
+
+    lens = [21, 40, 9, 33, 17, 200]
+    cfg, prompts, oracle, alt, eng, ref, ref_alt, first = _run("qwen3-moe-tiny", lens, 256, on_oracle=hook)
+    K, L = cfg["num_experts_per_tok"], cfg["num_hidden_layers"]
+    starts = [sum(lens[:s]) for s in range(len(lens))]
+    skip, flips = {}, 0
+    for i in range(L):
+        r, g = torch.cat(ref_logits[i]), got_logits[i]
+        assert r.shape == g.shape
+        dl = (g - r).abs()
+        assert float(dl.mean()) <= 2e-2 * float(r.abs().mean()), (i, float(dl.mean()))
+        rs = torch.sort(r, dim=-1, descending=True).values
+        for t in range(r.shape[0]):
+            a = sorted(moe_route(r[t:t + 1], K)[1][0].tolist())
+            b = sorted(moe_route(g[t:t + 1], K)[1][0].tolist())
+            if a == b:
+                continue
+            flips += 1
+            margin = float(rs[t, K - 1] - rs[t, K])   # the oracle's gap at the top-k boundary
+            assert margin <= 2 * float(dl[t].max()) + 1e-6, (i, t, margin, float(dl[t].max()))
+            s = max(k for k in range(len(lens)) if starts[k] <= t)
+            layer, pos = skip.get(s, (L, lens[s]))
+            skip[s] = (min(layer, i + 1), min(pos, t - starts[s]))
+    assert flips <= max(2, sum(lens) * L // 50), flips
+    print(f"routing flips: {flips}; sequences with a flip: {sorted(skip)}")
+    keep = [s for s in range(len(lens)) if s not in skip]
+    _check_logits(eng.last_prefill_logits.float().cpu()[keep], ref[keep], ref_alt[keep])
+    _check_kv(eng, oracle, alt, prompts, skip)
+    if skip:   # the decode continuation starts from the oracle's state
+        eng.load_prefilled(oracle.kv_pool)
     ref_tok = osamp.greedy(ref).tolist()
     for i in range(len(prompts)):
         oracle.append(i, ref_tok[i])
