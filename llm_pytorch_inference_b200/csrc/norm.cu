@@ -82,6 +82,73 @@ __global__ void fused_add_rmsnorm_kernel(T* __restrict__ out, T* __restrict__ re
     y[i] = from_f<T>(norm_out<T>(to_f<T>(res[i]), to_f<T>(w[i]), r, plus_one, semantics, true));
 }
 
+// Many rows (a prefill's tokens, more than 256), bf16: one warp per row, 8 rows per 256-thread CTA.
+// The row stays in registers as 16-byte vectors of 8 values (vector j * 32 + lane) between the
+// sum-of-squares pass and the output pass, so it is read from HBM once, with 512-byte warp accesses.
+// One CTA per row (the kernels above) keeps too few bytes in flight for HBM at this row count.  The
+// per-element rounding is the kernels' above; only the order of the fp32 sum of squares differs.
+// ADD: residual += in (rounded to bf16, written back), then the norm of the sum.  `out` may be `in`.
+template <int MAXV, bool ADD>
+__global__ void __launch_bounds__(256) norm_rows_kernel(__nv_bfloat16* out, int64_t out_stride,
+                                                        __nv_bfloat16* residual, const __nv_bfloat16* in,
+                                                        int64_t in_stride, const __nv_bfloat16* __restrict__ w,
+                                                        int64_t rows, int hidden, float eps, int plus_one,
+                                                        int semantics) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nv = hidden >> 8;  // vectors per lane
+  const uint4* x = reinterpret_cast<const uint4*>(in + row * in_stride);
+  uint4* res = ADD ? reinterpret_cast<uint4*>(residual + row * hidden) : nullptr;
+  uint4 v[MAXV];
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) {
+    if (j < nv) {
+      uint4 a = x[j * 32 + lane];
+      __nv_bfloat162* pa = reinterpret_cast<__nv_bfloat162*>(&a);
+      if (ADD) {
+        const uint4 b = res[j * 32 + lane];
+        const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 fa = __bfloat1622float2(pa[k]), fb = __bfloat1622float2(pb[k]);
+          pa[k] = __floats2bfloat162_rn(fb.x + fa.x, fb.y + fa.y);
+        }
+        res[j * 32 + lane] = a;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(pa[k]);
+        ss += f.x * f.x;
+        ss += f.y * f.y;
+      }
+      v[j] = a;
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(hidden) + eps);
+  const uint4* wv = reinterpret_cast<const uint4*>(w);
+  uint4* y = reinterpret_cast<uint4*>(out + row * out_stride);
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) {
+    if (j < nv) {
+      const uint4 wq = wv[j * 32 + lane];
+      const __nv_bfloat162* pw = reinterpret_cast<const __nv_bfloat162*>(&wq);
+      __nv_bfloat162* px = reinterpret_cast<__nv_bfloat162*>(&v[j]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 fx = __bfloat1622float2(px[k]), fw = __bfloat1622float2(pw[k]);
+        px[k] = __floats2bfloat162_rn(norm_out<__nv_bfloat16>(fx.x, fw.x, r, plus_one, semantics, ADD),
+                                      norm_out<__nv_bfloat16>(fx.y, fw.y, r, plus_one, semantics, ADD));
+      }
+      y[j * 32 + lane] = v[j];
+    }
+  }
+}
+
 // Residual add + RMSNorm whose input is a GEMM's output still in split-K partial form: the
 // linear layer's bf16 output is formed here as bf16(sum of the tile's partial slots, contributor
 // order), then residual += it and out = RMSNorm(residual) (model semantics, models/model.py:19-25,
@@ -282,6 +349,37 @@ int threads_for(int64_t hidden) {
   return t < 64 ? 64 : (t > 1024 ? 1024 : t);
 }
 
+// norm_rows_kernel covers bf16 calls of more than 256 rows with hidden a multiple of 256 up to
+// 8192 and 16-byte aligned rows; every other call (decode batches among them) takes the CTA-per-row
+// kernels.
+bool rows_form(int dtype, int64_t rows, int64_t hidden, const void* out, int64_t out_stride, const void* in,
+               int64_t in_stride, const void* w, const void* residual) {
+  return dtype == MVB_BF16 && rows > 256 && hidden % 256 == 0 && hidden <= 8192 && aligned(out, 16) &&
+         aligned(in, 16) && aligned(w, 16) && (residual == nullptr || aligned(residual, 16)) && out_stride % 8 == 0 &&
+         in_stride % 8 == 0;
+}
+
+template <bool ADD>
+int launch_norm_rows(void* out, int64_t out_stride, void* residual, const void* in, int64_t in_stride,
+                     const void* w, int64_t rows, int64_t hidden, float eps, int plus_one, int semantics,
+                     cudaStream_t st) {
+  const char* name = ADD ? "fused_add_rmsnorm_rows" : "rmsnorm_rows";
+  const dim3 grid(static_cast<unsigned>((rows + 7) / 8)), block(256);
+  auto* o = static_cast<__nv_bfloat16*>(out);
+  auto* r = static_cast<__nv_bfloat16*>(residual);
+  auto* x = static_cast<const __nv_bfloat16*>(in);
+  auto* wt = static_cast<const __nv_bfloat16*>(w);
+  const int h = static_cast<int>(hidden);
+  if (hidden <= 2048)
+    return launch(name, norm_rows_kernel<8, ADD>, grid, block, 0, st, o, out_stride, r, x, in_stride, wt, rows, h,
+                  eps, plus_one, semantics);
+  if (hidden <= 4096)
+    return launch(name, norm_rows_kernel<16, ADD>, grid, block, 0, st, o, out_stride, r, x, in_stride, wt, rows, h,
+                  eps, plus_one, semantics);
+  return launch(name, norm_rows_kernel<32, ADD>, grid, block, 0, st, o, out_stride, r, x, in_stride, wt, rows, h,
+                eps, plus_one, semantics);
+}
+
 }  // namespace
 }  // namespace mvb
 
@@ -297,6 +395,9 @@ extern "C" int mvb_rmsnorm(void* out, int64_t out_stride, const void* in, int64_
   MVB_REQUIRE(semantics == MVB_NORM_OPS || semantics == MVB_NORM_MODEL, "mvb_rmsnorm: bad semantics %d", semantics);
   if (rows == 0) return MVB_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (rows_form(dtype, rows, hidden, out, out_stride, in, in_stride, weight, nullptr))
+    return launch_norm_rows<false>(out, out_stride, nullptr, in, in_stride, weight, rows, hidden, eps, plus_one,
+                                   semantics, st);
   dim3 grid(static_cast<unsigned>(rows)), block(threads_for(hidden));
   switch (dtype) {
     case MVB_F32:
@@ -322,6 +423,9 @@ extern "C" int mvb_fused_add_rmsnorm(void* out, void* residual, const void* in, 
   MVB_REQUIRE(semantics == MVB_NORM_OPS || semantics == MVB_NORM_MODEL, "mvb_fused_add_rmsnorm: bad semantics");
   if (rows == 0) return MVB_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (rows_form(dtype, rows, hidden, out, hidden, in, hidden, weight, residual))
+    return launch_norm_rows<true>(out, hidden, residual, in, hidden, weight, rows, hidden, eps, plus_one, semantics,
+                                  st);
   dim3 grid(static_cast<unsigned>(rows)), block(threads_for(hidden));
   switch (dtype) {
     case MVB_F32:

@@ -33,6 +33,8 @@ next to the KV pool.
 """
 from __future__ import annotations
 
+from contextlib import contextmanager
+
 import torch
 
 from . import _native as N
@@ -97,6 +99,14 @@ class BatchedPrefill:
         ev[0].record()
         self.timing.setdefault(kind, []).append(ev)
         return ev[1]
+
+    @contextmanager
+    def _timed(self, kind: str):
+        """CUDA-event pair around the launches in the block when ``timing`` is on."""
+        end = self._mark(kind)
+        yield
+        if end is not None:
+            end.record()
 
     def _gemm(self, y, x, w, epilogue=N.EPI_STORE, aux=None):
         end = self._mark("gemm")
@@ -174,20 +184,23 @@ class BatchedPrefill:
         st, eps, bf = N.stream_handle(dev), r.eps, N.BF16
         h, xn, qkv, q, attn, act = (t_[:T] for t_ in (self.h, self.xn, self.qkv, self.q, self.attn, self.act))
         kvc = r.kv.kv_cache
-        N.check(lib.mvb_embedding(h.data_ptr(), tok_d.data_ptr(), N.I32, w.embed.data_ptr(), T, H, r.V,
-                                  r.embed_scale, bf, st), "embedding")
+        with self._timed("embedding"):
+            N.check(lib.mvb_embedding(h.data_ptr(), tok_d.data_ptr(), N.I32, w.embed.data_ptr(), T, H, r.V,
+                                      r.embed_scale, bf, st), "embedding")
         g, moe = r.gemma, r.moe
         for i in range(L):
             if not (g or moe) or i == 0:   # else the previous layer's add formed this layer's input norm
-                N.check(lib.mvb_rmsnorm(xn.data_ptr(), H, h.data_ptr(), H, w.ln1[i].data_ptr(), T, H, eps,
-                                        r.plus_one, N.NORM_MODEL, bf, st), "rmsnorm")
+                with self._timed("norm"):
+                    N.check(lib.mvb_rmsnorm(xn.data_ptr(), H, h.data_ptr(), H, w.ln1[i].data_ptr(), T, H, eps,
+                                            r.plus_one, N.NORM_MODEL, bf, st), "rmsnorm")
             self._gemm(qkv, xn, w.wqkv[i])
             cos, sin = r.layer_tables[i]
-            N.check(lib.mvb_qk_norm_rope_kv_write(
-                q.data_ptr(), kvc.data_ptr(), qkv.data_ptr(), qkv.stride(0),
-                w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
-                cos.data_ptr(), sin.data_ptr(), cos.shape[0], pos_d.data_ptr(), bt_d.data_ptr(), mb, T, r.Hq, r.Hkv,
-                D, L, i, r.P, r.kv.block_size, eps, r.plus_one, st), "qk_norm_rope_kv_write")
+            with self._timed("qk_rope_kv"):
+                N.check(lib.mvb_qk_norm_rope_kv_write(
+                    q.data_ptr(), kvc.data_ptr(), qkv.data_ptr(), qkv.stride(0),
+                    w.qn[i].data_ptr() if w.qk_norm else None, w.kn[i].data_ptr() if w.qk_norm else None,
+                    cos.data_ptr(), sin.data_ptr(), cos.shape[0], pos_d.data_ptr(), bt_d.data_ptr(), mb, T, r.Hq,
+                    r.Hkv, D, L, i, r.P, r.kv.block_size, eps, r.plus_one, st), "qk_norm_rope_kv_write")
             end = self._mark("attention")
             if tiled:
                 N.check(lib.mvb_prefill_attention(
@@ -207,14 +220,16 @@ class BatchedPrefill:
                 self._gemma_mlp_block(i, T, h, xn, attn, act)
                 continue
             self._gemm(h, attn, w.wo[i], N.EPI_RESADD, aux=h)          # h = h + o_proj(attn)
-            N.check(lib.mvb_rmsnorm(xn.data_ptr(), H, h.data_ptr(), H, w.ln2[i].data_ptr(), T, H, eps, r.plus_one,
-                                    N.NORM_MODEL, bf, st), "rmsnorm")
+            with self._timed("norm"):
+                N.check(lib.mvb_rmsnorm(xn.data_ptr(), H, h.data_ptr(), H, w.ln2[i].data_ptr(), T, H, eps,
+                                        r.plus_one, N.NORM_MODEL, bf, st), "rmsnorm")
             if moe:   # h = h + moe(xn), xn = the next layer's input norm (the final norm after the last)
                 out = self.moe_out[:T]
                 self._moe_block(i, T, xn, out)
                 nw = w.ln1[i + 1] if i + 1 < L else w.final_norm
-                N.check(lib.mvb_fused_add_rmsnorm(xn.data_ptr(), h.data_ptr(), out.data_ptr(), nw.data_ptr(), T, H,
-                                                  eps, r.plus_one, N.NORM_MODEL, bf, st), "fused_add_rmsnorm")
+                with self._timed("norm"):
+                    N.check(lib.mvb_fused_add_rmsnorm(xn.data_ptr(), h.data_ptr(), out.data_ptr(), nw.data_ptr(), T,
+                                                      H, eps, r.plus_one, N.NORM_MODEL, bf, st), "fused_add_rmsnorm")
                 continue
             self._gemm(act, xn, w.wgu[i], N.EPI_SWIGLU)
             self._gemm(h, act, w.wdown[i], N.EPI_RESADD, aux=h)        # h = h + down(swiglu)

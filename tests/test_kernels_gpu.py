@@ -67,6 +67,49 @@ def test_rmsnorm_model_semantics_match_oracle():
     assert bf16_ulps(out.cpu(), om.rms_norm(x, w, 1e-6)) <= 1
 
 
+@pytest.mark.parametrize("rows,hidden", [(1000, 4096), (300, 512), (777, 3584), (2049, 2048)])
+def test_norms_over_many_rows_match_the_row_kernels(rows, hidden):
+    """More than 256 rows (a prefill) take the warp-per-row kernels: the per-element rounding of the
+    CTA-per-row kernels that decode batches use (run here 256 rows at a time), the fp32 sum of
+    squares in another order (at most 1 bf16 ulp apart), the residual sum bit-exact; strided input
+    rows, in place."""
+    bf = torch.bfloat16
+    g = torch.Generator(device=DEV).manual_seed(rows + hidden)
+    x = torch.randn(rows, hidden + 64, device=DEV, generator=g).to(bf)   # row stride hidden + 64
+    w = (1 + 0.1 * torch.randn(hidden, device=DEV, generator=g)).to(bf)
+    lib, st = N.lib(), N.stream_handle()
+
+    def norm(out, inp, n, plus_one, sem):
+        N.check(lib.mvb_rmsnorm(out.data_ptr(), out.stride(0), inp.data_ptr(), inp.stride(0), w.data_ptr(), n,
+                                hidden, 1e-6, plus_one, sem, N.BF16, st), "rmsnorm")
+
+    for plus_one, sem in [(0, N.NORM_MODEL), (1, N.NORM_MODEL), (0, N.NORM_OPS), (1, N.NORM_OPS)]:
+        out = torch.empty(rows, hidden, dtype=bf, device=DEV)
+        norm(out, x, rows, plus_one, sem)
+        ref = torch.empty_like(out)
+        for r0 in range(0, rows, 256):
+            norm(ref[r0:], x[r0:], min(256, rows - r0), plus_one, sem)
+        assert bf16_ulps(out.cpu(), ref.cpu()) <= 1, (plus_one, sem)
+    z = x[:, :hidden].contiguous()
+    zz = z.clone()
+    norm(zz, zz, rows, 0, N.NORM_MODEL)                      # in place
+    out = torch.empty_like(z)
+    norm(out, z, rows, 0, N.NORM_MODEL)
+    assert torch.equal(zz, out)
+    res = torch.randn(rows, hidden, device=DEV, generator=g).to(bf)
+    r_a, r_b = res.clone(), res.clone()
+    y_a, y_b = torch.empty_like(z), torch.empty_like(z)
+    N.check(lib.mvb_fused_add_rmsnorm(y_a.data_ptr(), r_a.data_ptr(), z.data_ptr(), w.data_ptr(), rows, hidden, 1e-6,
+                                      0, N.NORM_MODEL, N.BF16, st), "fused_add_rmsnorm")
+    for r0 in range(0, rows, 256):
+        N.check(lib.mvb_fused_add_rmsnorm(y_b[r0:].data_ptr(), r_b[r0:].data_ptr(), z[r0:].data_ptr(), w.data_ptr(),
+                                          min(256, rows - r0), hidden, 1e-6, 0, N.NORM_MODEL, N.BF16, st),
+                "fused_add_rmsnorm")
+    assert torch.equal(r_a, r_b)
+    assert torch.equal(r_a, (res.float() + z.float()).to(bf))
+    assert bf16_ulps(y_a.cpu(), y_b.cpu()) <= 1
+
+
 # ------------------------------------------------------------------ elementwise
 def test_rope_op_matches_reference(golden):
     q, k = golden["rope_q"], golden["rope_k"]
