@@ -65,7 +65,9 @@ int mvb_device_status(unsigned int* status, int clear, mvb_stream_t stream);
  * semantics: MVB_NORM_OPS reproduces the ops-API formula of ops/rmsnorm.py:12-31
  * (w*x rounded to the dtype before the 1/rms scale); MVB_NORM_MODEL reproduces
  * RMSNorm.forward of models/model.py:19-25 (x*(1/rms) in fp32, then w*, one rounding).
- * in_stride / out_stride: elements between rows (>= hidden). */
+ * in_stride / out_stride: elements between rows (>= hidden); out may be in.  bf16 calls of more
+ * than 256 rows (hidden % 256 == 0, <= 8192, 16-byte aligned rows) run one warp per row: the same
+ * per-element rounding, the fp32 sum of squares in another order. */
 #define MVB_NORM_OPS 0
 #define MVB_NORM_MODEL 1
 int mvb_rmsnorm(void* out, int64_t out_stride, const void* in, int64_t in_stride, const void* weight, int64_t rows,
@@ -248,7 +250,10 @@ int mvb_paged_attention_decode_noalloc(void* out, int64_t out_stride, const void
  *                          mvb_qk_norm_rope_kv_write_gemm); the GEMM then ends without a merge
  *           MVB_EPI_SWIGLU_PARTIALS  the SWIGLU pairing of W's rows with MVB_EPI_PARTIALS' output:
  *                          fp32 partials of gate and up features, finished by mvb_swiglu_gemm
- * Requires k % 64 == 0, ldx/ldw/ldy multiples of 8, 16-byte aligned pointers, m <= 256.
+ * Requires k % 64 == 0, ldx/ldw/ldy multiples of 8, 16-byte aligned pointers, m < 2^24.  More
+ * than 256 rows (a prefill's tokens) take STORE, SWIGLU or RESADD on one GPU: 256-row tiles, and
+ * whole 256 x 256 output tiles (two 128-row weight tiles per activation tile) when the 128-row
+ * weight tiles (64-row gate/up pairs for SWIGLU) are even in number.
  * workspace: >= mvb_gemm_workspace_bytes(m, n, k, device); zero before the first call.  fp32
  * partials use its head, per-tile counters its tail; the kernel leaves the counters zero, so
  * one buffer serves any number of calls on one stream.  Calls of different shapes may share
