@@ -43,6 +43,65 @@ _ATTN_ROWS = 4096   # query rows per attention launch at head dim 128 (the kerne
 _MOE_ROWS = 256     # token rows per MoE routing / dispatch launch (mvb_moe_route's limit)
 
 
+def split_chunks(lens: list[int], max_tokens: int) -> list[tuple[int, int]]:
+    """Consecutive runs ``[i, j)`` of whole sequences of at most ``max_tokens`` tokens each, taken
+    greedily in order; a prompt longer than the budget raises ``ValueError``."""
+    out, i = [], 0
+    while i < len(lens):
+        j, n = i, 0
+        while j < len(lens) and n + lens[j] <= max_tokens:
+            n += lens[j]
+            j += 1
+        if j == i:
+            raise ValueError(f"prompt of {lens[i]} tokens exceeds the prefill budget {max_tokens}")
+        out.append((i, j))
+        i = j
+    return out
+
+
+def pack_chunk_metadata(ids: list[list[int]], tables: list[list[int]], max_blocks: int,
+                        scratch_block: int) -> tuple[torch.Tensor, tuple[int, int, int, int, int]]:
+    """The host side of one chunk's metadata, one int32 buffer uploaded with one copy:
+
+    ``token ids [T] | positions [T] | context lengths [T] | block table per row [T, max_blocks] |
+    sequence start [S] | sequence length [S] | block table per sequence [S, max_blocks] |
+    tile sequence [nt] | tile index [nt]``
+
+    Row r is token i of sequence s (prompts packed in order): position i, context i + 1, its
+    sequence's block table (unused entries the scratch block).  The attention tiles are the
+    (sequence, 16-token query tile) pairs, the tiles with the longest prefixes first (stable
+    within an index).  Returns the buffer and (T, S, nt, offset of the sequence part, offset of
+    the tile part)."""
+    lens = [len(p) for p in ids]
+    T, S, mb = sum(lens), len(ids), max_blocks
+    tiles = sorted(((s, qt) for s in range(S) for qt in range((lens[s] + 15) // 16)), key=lambda x: -x[1])
+    nt = len(tiles)
+    o_seq = 3 * T + T * mb
+    o_tile = o_seq + 2 * S + S * mb
+    host = torch.zeros(o_tile + 2 * nt, dtype=torch.int32)
+    tok, pos, ctx = host[:T], host[T:2 * T], host[2 * T:3 * T]
+    bt = host[3 * T:o_seq].view(T, mb)
+    bt.fill_(scratch_block)
+    seq_start, seq_len = host[o_seq:o_seq + S], host[o_seq + S:o_seq + 2 * S]
+    seq_bt = host[o_seq + 2 * S:o_tile].view(S, mb)
+    seq_bt.fill_(scratch_block)
+    row = 0
+    for k, (p, t) in enumerate(zip(ids, tables)):
+        n = len(p)
+        if len(t) > mb:
+            raise ValueError(f"sequence needs {len(t)} blocks > max_blocks {mb}")
+        tok[row:row + n] = torch.tensor(p, dtype=torch.int32)
+        pos[row:row + n] = torch.arange(n, dtype=torch.int32)
+        ctx[row:row + n] = torch.arange(1, n + 1, dtype=torch.int32)
+        bt[row:row + n, :len(t)] = torch.tensor(t, dtype=torch.int32)
+        seq_start[k], seq_len[k] = row, n
+        seq_bt[k, :len(t)] = torch.tensor(t, dtype=torch.int32)
+        row += n
+    host[o_tile:o_tile + nt] = torch.tensor([x[0] for x in tiles], dtype=torch.int32)
+    host[o_tile + nt:] = torch.tensor([x[1] for x in tiles], dtype=torch.int32)
+    return host, (T, S, nt, o_seq, o_tile)
+
+
 def _attention_rows(runner) -> int:
     """Query rows per launch of the decode kernel: it takes up to 4096 (row, head group) pairs at
     head dim 128, where one group holds all KV heads, and 1024 at head dim 256 (groups of 2 heads)."""
@@ -127,53 +186,15 @@ class BatchedPrefill:
     def run(self, ids: list[list[int]], tables: list[list[int]]) -> torch.Tensor:
         """Prefills the sequences whose prompts are ``ids`` into the blocks ``tables`` (each holding
         at least ``len(prompt)`` tokens); returns the bf16 logits ``[n, V]`` of each last token."""
-        out = []
-        i = 0
-        while i < len(ids):
-            j, n = i, 0
-            while j < len(ids) and n + len(ids[j]) <= self.max_tokens:
-                n += len(ids[j])
-                j += 1
-            if j == i:
-                raise ValueError(f"prompt of {len(ids[i])} tokens exceeds the prefill budget {self.max_tokens}")
-            out.append(self._chunk(ids[i:j], tables[i:j]))
-            i = j
+        out = [self._chunk(ids[i:j], tables[i:j]) for i, j in split_chunks([len(p) for p in ids], self.max_tokens)]
         return torch.cat(out)
 
     def _chunk(self, ids: list[list[int]], tables: list[list[int]]) -> torch.Tensor:
         r, lib = self.r, N.lib()
         dev, w, H, D, L = r.dev, r.w, r.H, r.D, r.L
         lens = [len(p) for p in ids]
-        T = sum(lens)
         mb = r.max_blocks
-        S = len(ids)
-        tiles = sorted(((s, qt) for s in range(S) for qt in range((lens[s] + 15) // 16)), key=lambda x: -x[1])
-        nt = len(tiles)
-        # one int32 buffer: token ids | positions | per-row context | per-row block tables |
-        # per-sequence start, length, block tables | tiles (sequence, index)
-        o_seq = 3 * T + T * mb
-        o_tile = o_seq + 2 * S + S * mb
-        host = torch.zeros(o_tile + 2 * nt, dtype=torch.int32)
-        tok, pos, ctx = host[:T], host[T:2 * T], host[2 * T:3 * T]
-        bt = host[3 * T:o_seq].view(T, mb)
-        bt.fill_(r.kv.scratch_block)
-        seq_start, seq_len = host[o_seq:o_seq + S], host[o_seq + S:o_seq + 2 * S]
-        seq_bt = host[o_seq + 2 * S:o_tile].view(S, mb)
-        seq_bt.fill_(r.kv.scratch_block)
-        row = 0
-        for k, (p, t) in enumerate(zip(ids, tables)):
-            n = len(p)
-            if len(t) > mb:
-                raise ValueError(f"sequence needs {len(t)} blocks > max_blocks {mb}")
-            tok[row:row + n] = torch.tensor(p, dtype=torch.int32)
-            pos[row:row + n] = torch.arange(n, dtype=torch.int32)
-            ctx[row:row + n] = torch.arange(1, n + 1, dtype=torch.int32)
-            bt[row:row + n, :len(t)] = torch.tensor(t, dtype=torch.int32)
-            seq_start[k], seq_len[k] = row, n
-            seq_bt[k, :len(t)] = torch.tensor(t, dtype=torch.int32)
-            row += n
-        host[o_tile:o_tile + nt] = torch.tensor([x[0] for x in tiles], dtype=torch.int32)
-        host[o_tile + nt:] = torch.tensor([x[1] for x in tiles], dtype=torch.int32)
+        host, (T, S, nt, o_seq, o_tile) = pack_chunk_metadata(ids, tables, mb, r.kv.scratch_block)
         meta = host.to(dev, non_blocking=False)
         tok_d, pos_d, ctx_d = meta[:T], meta[T:2 * T], meta[2 * T:3 * T]
         bt_d = meta[3 * T:o_seq].view(T, mb)
