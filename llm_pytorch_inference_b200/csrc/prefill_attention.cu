@@ -65,7 +65,13 @@ __global__ void __launch_bounds__((kPfWarps + 1) * 32, 2)
   const int h = blockIdx.y;  // KV head
   const int len = a.seq_len[s];
   const int q0 = qt * PBS;
-  const int nb = qt + 1;  // key blocks 0 .. qt (the tile's last token sits in block qt)
+  // Key blocks 0 .. qt (the tile's last token sits in block qt), never past the table's width: a
+  // tile index the block table cannot hold sets the status word, as the decode kernel does.
+  int nb = qt + 1;
+  if (qt < 0 || nb > a.max_blocks) {
+    if (threadIdx.x == 0) report(a.err, kDevBadPosition);
+    nb = qt < 0 ? 0 : static_cast<int>(a.max_blocks);
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kPfStages; ++i) {
