@@ -9,7 +9,7 @@ PyTorch path (``MINI_VLLM_BACKEND=pytorch``, ``mini_vllm/ops/_utils.py:74``):
   FusedMLP fallback, greedy / top-k / top-p / softmax sampling ``ops/sampling.py``).
 * ``kv_golden.json``   -- KVCacheManager traces (``engine/kv_cache.py:6-81``):
   block tables under a shuffled pool, exhaustion, growth.
-* ``decode_cfg1.pt``   -- Qwen3-0.6B-architecture fp32 greedy generation through
+* ``decode_qwen3_0.6b_f32.pt`` -- Qwen3-0.6B-architecture fp32 greedy generation through
   ``LLMEngine._step`` (``engine/engine.py:241-360``): 4 prompts x 128 ids, 64 tokens.
 * ``decode_tiny_bf16.pt`` -- a 2-layer Qwen3-family bf16 model, ragged prompts,
   greedy 24 tokens, full per-step logits.
@@ -334,14 +334,14 @@ def main() -> None:
     if want("gemma3"):
         torch.save(make_gemma3_golden(), HERE / "decode_gemma3_tiny.pt")
         print("decode_gemma3_tiny.pt written")
-    if want("cfg1"):
+    if want("qwen3-0.6b"):
         cfg = get_config("qwen3-0.6b")
         g = torch.Generator().manual_seed(0)
         prompts = [torch.randint(0, cfg["vocab_size"], (128,), generator=g).tolist() for _ in range(4)]
         fx = _decode_fixture(cfg, torch.float32, prompts, 64, keep_full_logits=False)
         fx["arch"] = "qwen3-0.6b"
-        torch.save(fx, HERE / "decode_cfg1.pt")
-        print("decode_cfg1.pt written")
+        torch.save(fx, HERE / "decode_qwen3_0.6b_f32.pt")
+        print("decode_qwen3_0.6b_f32.pt written")
 
 
 if __name__ == "__main__":

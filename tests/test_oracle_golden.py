@@ -113,8 +113,8 @@ def test_decode_tiny_bf16_matches_reference(golden_dir):
 
 
 @pytest.mark.slow
-def test_decode_cfg1_fp32_matches_reference(golden_dir):
-    fx = torch.load(golden_dir / "decode_cfg1.pt")
+def test_decode_qwen3_0_6b_fp32_matches_reference(golden_dir):
+    fx = torch.load(golden_dir / "decode_qwen3_0.6b_f32.pt")
     eng = _engine_for(fx, torch.float32)
     prompts = [p.tolist() for p in fx["prompts"]]
     out, step_logits = eng.generate_greedy(prompts, 64)
