@@ -117,7 +117,8 @@ def test_moe_prefill_matches_oracle_and_decodes_on(monkeypatch):
     Routing is discrete: where a token's K-th and (K+1)-th router logits lie closer than the bf16
     noise of the logits (the attention output feeding the router differs in its last bits), the two
     computations may pick different expert sets.  Both sides' router logits are recorded; a token
-    whose top-k set differs must be such a near tie, few tokens may be, and what such a flip feeds
+    whose top-k set differs must be such a near tie, at most 3 % of the routings may flip (the oracle's
+bf16 CPU GEMMs round differently on different host ISAs, so the count varies), and what a flip feeds
     (its sequence's K/V in later layers, from that token on; its sequence's logits) is left out of
     the comparison.  Everything else meets the dense bars."""
     from test_decode_gpu import _compare_teacher_forced
@@ -165,7 +166,7 @@ def test_moe_prefill_matches_oracle_and_decodes_on(monkeypatch):
             s = max(k for k in range(len(lens)) if starts[k] <= t)
             layer, pos = skip.get(s, (L, lens[s]))
             skip[s] = (min(layer, i + 1), min(pos, t - starts[s]))
-    assert flips <= max(2, sum(lens) * L // 50), flips
+    assert flips <= max(2, sum(lens) * L * 3 // 100), flips   # 8 of 640 routings flipped on a B200
     print(f"routing flips: {flips}; sequences with a flip: {sorted(skip)}")
     keep = [s for s in range(len(lens)) if s not in skip]
     _check_logits(eng.last_prefill_logits.float().cpu()[keep], ref[keep], ref_alt[keep])
