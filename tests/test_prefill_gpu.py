@@ -117,10 +117,10 @@ def test_moe_prefill_matches_oracle_and_decodes_on(monkeypatch):
     Routing is discrete: where a token's K-th and (K+1)-th router logits lie closer than the bf16
     noise of the logits (the attention output feeding the router differs in its last bits), the two
     computations may pick different expert sets.  Both sides' router logits are recorded; a token
-    whose top-k set differs must be such a near tie, at most 3 % of the routings may flip (the oracle's
-bf16 CPU GEMMs round differently on different host ISAs, so the count varies), and what a flip feeds
-    (its sequence's K/V in later layers, from that token on; its sequence's logits) is left out of
-    the comparison.  Everything else meets the dense bars."""
+    whose top-k set differs must be such a near tie, at most 3 % of the routings may flip (the
+    oracle's bf16 CPU GEMMs round differently on different host ISAs, so the count varies), and what
+    a flip feeds (its sequence's K/V in later layers, from that token on; its sequence's logits) is
+    left out of the comparison.  Everything else meets the dense bars."""
     from test_decode_gpu import _compare_teacher_forced
     from llm_pytorch_inference_b200 import prefill as pf
     from oracle.model import moe_route
