@@ -1,6 +1,7 @@
 """Per-layer architecture facts on the CPU: the product's helpers (which pick each layer's RoPE
 table, attention window and embedding scale on the GPU path) agree with the oracle's own
-restatement of the reference (``models/gemma3_model.py:295-320``) for every named architecture."""
+restatement of the reference (``models/gemma3_model.py:295-320``) for every named architecture,
+and the RoPE tables (``models/model.py:28-81``)."""
 import math
 
 import pytest
@@ -42,3 +43,14 @@ def test_overrides_do_not_leak_between_calls():
     assert a["num_hidden_layers"] == 2 and b["num_hidden_layers"] != 2
     with pytest.raises(KeyError):
         C.get_config("no-such-arch")
+
+
+@pytest.mark.parametrize("head_dim,theta,length", [(128, 1e6, 4200), (256, 10000.0, 9000), (128, 10000.0, 64)])
+def test_rope_tables_match_the_oracle(head_dim, theta, length):
+    """The cos/sin tables the GPU path uploads (bf16, positions rounded to bf16 as the reference's
+    ``model.to(dtype)`` leaves them) equal the oracle's, which the golden fixtures pin."""
+    from llm_pytorch_inference_b200.runner import rope_tables
+
+    cos, sin = rope_tables(head_dim, theta, length, torch.bfloat16, "cpu")
+    ocos, osin = om.rope_tables(head_dim, theta, length, torch.bfloat16)
+    assert torch.equal(cos, ocos) and torch.equal(sin, osin)
