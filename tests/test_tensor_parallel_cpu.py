@@ -158,3 +158,28 @@ def test_shard_shapes_and_divisibility():
     assert tpm.local_config(cfg, 8)["num_key_value_heads"] == 1
     with pytest.raises(ValueError):
         tpm.check_divisible(cfg, 3)
+
+
+def test_gemma2_shard_shapes():
+    """Gemma-2-9B at TP=2: head dim 256, query heads and o_proj columns split, KV heads split, the
+    sandwich norms replicated, vocab-parallel lm_head (tied to the embedding, which stays whole)."""
+    from llm_pytorch_inference_b200.weights import weight_shapes
+
+    cfg = get_config("gemma2-9b", num_hidden_layers=1)
+    sd = {k: torch.empty(s, dtype=torch.bfloat16, device="meta") for k, s in weight_shapes(cfg).items()}
+    out = tpm.shard_state_dict(cfg, sd, 2, 1)
+    H, D, V = cfg["hidden_size"], head_dim(cfg), cfg["vocab_size"]
+    nq, nkv, inter = cfg["num_attention_heads"], num_kv_heads(cfg), cfg["intermediate_size"]
+    p = "model.layers.0."
+    assert out[p + "self_attn.q_proj.weight"].shape == (nq // 2 * D, H)
+    assert out[p + "self_attn.k_proj.weight"].shape == (nkv // 2 * D, H)
+    assert out[p + "self_attn.v_proj.weight"].shape == (nkv // 2 * D, H)
+    assert out[p + "self_attn.o_proj.weight"].shape == (H, nq // 2 * D)
+    assert out[p + "mlp.gate_proj.weight"].shape == (inter // 2, H)
+    assert out[p + "mlp.down_proj.weight"].shape == (H, inter // 2)
+    for norm in ("input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
+                 "post_feedforward_layernorm"):
+        assert out[p + norm + ".weight"].shape == (H,)
+    assert out["model.embed_tokens.weight"].shape == (V, H)
+    assert "lm_head.weight" not in sd and out["lm_head.weight"].shape == (V // 2, H)   # cut from the tied table
+    assert tpm.local_config(cfg, 2)["num_key_value_heads"] == nkv // 2
