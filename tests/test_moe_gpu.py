@@ -7,8 +7,6 @@ reference's ``Qwen3MoeSparseMoe.forward`` restated, pinned to fixtures the refer
 * the whole decode step of a 2-layer MoE model, teacher-forced, within the noise-aware bars of
   the dense decode tests.
 """
-import random
-
 import pytest
 import torch
 
