@@ -674,7 +674,6 @@ template <int D>
 constexpr int attn_max_pairs() {
   return D == 128 ? 4096 : 1024;
 }
-constexpr int kAttnMaxBatch = 4096;
 
 // Shared memory other than the stages, at the largest batch: barriers, the block prefix sums,
 // the merge scratch, the per-head combine and the 1 KB alignment slack.
