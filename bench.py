@@ -637,8 +637,7 @@ def run_prefill_case(args) -> None:
     r = eng.runner
     # per-kind device time: the same prefill again (new sequence ids) with events around each launch
     for s in range(B):
-        eng.kv.free(s)
-    eng.seqs = [x for x in eng.seqs if x >= B]
+        eng.finish(s)
     eng._prefill.timing = {}
     eng.prefill({B + 2 + s: p for s, p in prompts.items()})
     torch.cuda.synchronize(dev)

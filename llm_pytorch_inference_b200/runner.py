@@ -57,6 +57,20 @@ def rope_tables(head_dim_: int, theta: float, length: int, dtype: torch.dtype, d
     return emb.cos().to(device).contiguous(), emb.sin().to(device).contiguous()
 
 
+def meta_layout(batch: int, max_blocks: int) -> dict[str, int]:
+    """Offsets (in int32 words) of the per-step metadata buffer, one upload per step:
+    token ids | positions | context lengths | sampling offset (int64, 8-byte aligned) |
+    temperature (fp32) | top-k (int32) | top-p (fp32) | block tables ``[batch, max_blocks]``."""
+    B = batch
+    o_off = (3 * B + 1) // 2 * 2
+    o_temp = o_off + 2
+    o_topk = o_temp + B
+    o_topp = o_topk + B
+    o_bt = o_topp + B
+    return {"ids": 0, "pos": B, "ctx": 2 * B, "off": o_off, "temp": o_temp, "topk": o_topk, "topp": o_topp,
+            "bt": o_bt, "total": o_bt + B * max_blocks}
+
+
 class DecodeWeights:
     """Per-layer device weights in the layout the decode kernels read."""
 
@@ -206,26 +220,27 @@ class DecodeRunner:
             self.y_sorted = torch.zeros(B * self.K, H, dtype=bf, device=dev)
             self.mlp_out = torch.zeros(B, H, dtype=bf, device=dev)
         self.tokens = torch.zeros(B, dtype=torch.int64, device=dev)
-        # per-row sampling parameters (greedy by default)
-        self.temperature = torch.zeros(B, dtype=torch.float32, device=dev)
-        self.top_k = torch.full((B,), -1, dtype=torch.int32, device=dev)
-        self.top_p = torch.ones(B, dtype=torch.float32, device=dev)
         self.seed = 0
+        self.probs = None   # [B, V] fp32 filtered / tempered probabilities, when requested (set_probs_out)
 
-        # metadata: ids | pos | ctx | offset(int64) | block tables
-        self._o_pos = B
-        self._o_ctx = 2 * B
-        self._o_off = (3 * B + 1) // 2 * 2
-        self._o_bt = self._o_off + 2
-        n_meta = self._o_bt + B * self.max_blocks
-        self.meta = torch.zeros(n_meta, dtype=torch.int32, device=dev)
-        self.meta_host = torch.zeros(n_meta, dtype=torch.int32, pin_memory=True)
+        # metadata: ids | pos | ctx | offset(int64) | temperature | top-k | top-p | block tables
+        lay = meta_layout(B, self.max_blocks)
+        self.meta_offsets = lay
+        self._o_pos, self._o_ctx, self._o_off, self._o_bt = lay["pos"], lay["ctx"], lay["off"], lay["bt"]
+        self.meta = torch.zeros(lay["total"], dtype=torch.int32, device=dev)
+        self.meta_host = torch.zeros(lay["total"], dtype=torch.int32, pin_memory=True)
         self.ids = self.meta[0:B]
         self.pos = self.meta[self._o_pos:self._o_pos + B]
         self.ctx = self.meta[self._o_ctx:self._o_ctx + B]
         self.offset = self.meta[self._o_off:self._o_off + 2].view(torch.int64)
+        # per-row sampling parameters travel with the step's metadata (greedy by default)
+        self.temperature = self.meta[lay["temp"]:lay["temp"] + B].view(torch.float32)
+        self.top_k = self.meta[lay["topk"]:lay["topk"] + B]
+        self.top_p = self.meta[lay["topp"]:lay["topp"] + B].view(torch.float32)
         self.block_tables = self.meta[self._o_bt:].view(B, self.max_blocks)
         self.tokens_host = torch.zeros(B, dtype=torch.int64, pin_memory=True)
+        self._host_sampling(0.0, -1, 1.0)
+        self.upload_metadata()
 
         gemm_shapes = [(qkv_n, H), (H, self.Hq * self.D), (2 * self.I, H), (H, self.I), (self.Vl, H)]
         if self.moe:
@@ -246,8 +261,8 @@ class DecodeRunner:
         if n > self.B:
             raise ValueError(f"batch {n} exceeds the runner's max_batch {self.B}")
         m = self.meta_host
-        m.zero_()
         B, mb = self.B, self.max_blocks
+        m[:self._o_off + 2].zero_()
         m[0:n] = torch.tensor(ids, dtype=torch.int32)
         m[self._o_pos:self._o_pos + n] = torch.tensor(positions, dtype=torch.int32)
         ctx = ctx_lens if ctx_lens is not None else [p + 1 for p in positions]
@@ -265,13 +280,31 @@ class DecodeRunner:
     def upload_metadata(self) -> None:
         self.meta.copy_(self.meta_host, non_blocking=True)
 
+    def _host_sampling(self, temperature, top_k, top_p) -> None:
+        lay, B, m = self.meta_offsets, self.B, self.meta_host
+        m[lay["temp"]:lay["temp"] + B].view(torch.float32).copy_(
+            torch.as_tensor(temperature, dtype=torch.float32).expand(B))
+        m[lay["topk"]:lay["topk"] + B].copy_(torch.as_tensor(top_k, dtype=torch.int32).expand(B))
+        m[lay["topp"]:lay["topp"] + B].view(torch.float32).copy_(torch.as_tensor(top_p, dtype=torch.float32).expand(B))
+
     def set_sampling(self, temperature, top_k, top_p, seed: int = 0) -> None:
-        """Per-row (or scalar) sampling parameters; T == 0 rows decode greedily."""
-        self.temperature.copy_(torch.as_tensor(temperature, dtype=torch.float32).expand(self.B))
-        self.top_k.copy_(torch.as_tensor(top_k, dtype=torch.int32).expand(self.B))
-        self.top_p.copy_(torch.as_tensor(top_p, dtype=torch.float32).expand(self.B))
-        self.seed = int(seed)
-        self.graph = None  # the seed is a kernel argument: re-capture
+        """Per-row (or scalar) sampling parameters; T == 0 rows decode greedily.  They sit in the
+        step metadata (host mirror and device copy are both updated here)."""
+        self._host_sampling(temperature, top_k, top_p)
+        lay, B = self.meta_offsets, self.B
+        self.meta[lay["temp"]:lay["topp"] + B].copy_(self.meta_host[lay["temp"]:lay["topp"] + B])
+        if int(seed) != self.seed:
+            self.seed = int(seed)
+            self.graph = None  # the seed is a kernel argument: re-capture
+
+    def set_probs_out(self, enabled: bool) -> None:
+        """With ``enabled`` the step's sampler also writes each row's filtered, tempered
+        probabilities to ``self.probs`` ``[B, V]`` fp32 (the distribution a parity-mode draw uses)."""
+        want = bool(enabled)
+        if want == (self.probs is not None):
+            return
+        self.probs = torch.zeros(self.B, self.V, dtype=torch.float32, device=self.dev) if want else None
+        self.graph = None
 
     # ------------------------------------------------------------------- step
     def _gemm(self, y, x, w, epilogue=N.EPI_STORE, aux=None):
@@ -332,7 +365,7 @@ class DecodeRunner:
         if self.final_softcap:
             N.check(lib.mvb_softcap(self.logits.data_ptr(), B * self.V, self.final_softcap, N.BF16, self._st),
                     "softcap")
-        N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
+        N.check(lib.mvb_sample(self.tokens.data_ptr(), N.ptr(self.probs), self.logits.data_ptr(), B, self.V, self.V,
                                self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
                                0, self.offset.data_ptr(), N.BF16, self._st), "sample")
 
@@ -418,7 +451,7 @@ class DecodeRunner:
                                           w.final_norm.data_ptr(), B, H, eps, 0, N.NORM_MODEL, bf, st),
                 "fused_add_rmsnorm")
         self._gemm(self.logits, self.xn, w.lm_head)
-        N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
+        N.check(lib.mvb_sample(self.tokens.data_ptr(), N.ptr(self.probs), self.logits.data_ptr(), B, self.V, self.V,
                                self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
                                0, self.offset.data_ptr(), bf, st), "sample")
 
@@ -473,7 +506,7 @@ class DecodeRunner:
         N.check(lib.mvb_tp_wait(comm, tpm.point_logits(self.L), st), "tp_wait")
         if self.final_softcap:   # every rank soft-caps its copy of the gathered logits
             N.check(lib.mvb_softcap(self.logits.data_ptr(), B * self.V, self.final_softcap, N.BF16, st), "softcap")
-        N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
+        N.check(lib.mvb_sample(self.tokens.data_ptr(), N.ptr(self.probs), self.logits.data_ptr(), B, self.V, self.V,
                                self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
                                0, self.offset.data_ptr(), bf, st), "sample")
 
@@ -508,7 +541,7 @@ class DecodeRunner:
                                        self.act, st), "gated_gemm")
 
         def samp(i):
-            N.check(lib.mvb_sample(self.tokens.data_ptr(), None, self.logits.data_ptr(), B, self.V, self.V,
+            N.check(lib.mvb_sample(self.tokens.data_ptr(), N.ptr(self.probs), self.logits.data_ptr(), B, self.V, self.V,
                                    self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(),
                                    self.seed, 0, self.offset.data_ptr(), N.BF16, st), "sample")
 

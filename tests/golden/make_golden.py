@@ -11,16 +11,22 @@ PyTorch path (``MINI_VLLM_BACKEND=pytorch``, ``mini_vllm/ops/_utils.py:74``):
   block tables under a shuffled pool, exhaustion, growth.
 * ``decode_qwen3_0.6b_f32.pt`` -- Qwen3-0.6B-architecture fp32 greedy generation through
   ``LLMEngine._step`` (``engine/engine.py:241-360``): 4 prompts x 128 ids, 64 tokens.
+* ``decode_qwen3_0.6b_bf16.pt`` -- the same model, prompts and engine path in bf16: greedy,
+  33 tokens (the prefill's token and 32 decode steps), top-16 logits of every step.
 * ``decode_tiny_bf16.pt`` -- a 2-layer Qwen3-family bf16 model, ragged prompts,
   greedy 24 tokens, full per-step logits.
+* ``engine_trace.json`` -- continuous batching through ``LLMEngine._step``: sequences finishing
+  at different steps (max_tokens, a stop id), joining mid-run, one that cannot be allocated;
+  per-step decoded rows, tokens, block tables, free list and finished set.
 * ``decode_moe_tiny_f32.pt`` -- a 2-layer Qwen3-MoE model (``models/qwen3_moe_model.py``,
   16 experts, top-4) in fp32: its MoE block alone, and greedy decoding with full logits.
 * ``decode_gemma3_tiny.pt`` -- the reference's Gemma 3 model (``models/gemma3_model.py``, head
   dim 256, QK-norm, local/global RoPE theta) with seeded non-trivial norm weights: greedy
   decoding in fp32 and in bf16, full logits.
 
-Usage (only where the reference is mounted):
-    python tests/golden/make_golden.py [--reference /root/reference]
+Usage (only where the reference is mounted; its checkout path is required):
+    python tests/golden/make_golden.py --reference <path to the reference checkout> [--only name,...]
+    (or set MINI_VLLM_REFERENCE to that path)
 
 The reference cannot travel with the repository; the fixtures it produced are
 committed, and this script is how they were made.
@@ -260,6 +266,78 @@ def _decode_fixture(cfg, dtype, prompts, max_tokens, keep_full_logits, norm_jitt
     return fx
 
 
+def make_engine_trace_golden() -> dict:
+    """Continuous batching through the reference's ``LLMEngine._step`` (``engine/engine.py:241-360``,
+    ``engine/scheduler.py:27-57``): qwen3-tiny in fp32 on a shuffled 20-block pool, sequences
+    finishing at different steps (each its own ``max_tokens``, one with a stop id that it
+    generates), two sequences joining while others run, one whose prompt does not fit.  After
+    every ``_step`` the trace records the prefilled sequences with their first tokens, the decoded
+    sequences in batch order with their tokens and block tables, the free list and the finished
+    set."""
+    from mini_vllm.engine.sequence import Sequence
+    from mini_vllm.utils.config import SamplingParams
+
+    cfg = get_config("qwen3-tiny")
+    g = torch.Generator().manual_seed(23)
+    lens = [37, 50, 16, 64, 20, 33, 400]
+    prompts = [torch.randint(0, cfg["vocab_size"], (n,), generator=g).tolist() for n in lens]
+    max_toks = [3, 9, 5, 14, 6, 8, 4]
+    joins = {0: [0, 1, 2, 3], 4: [4, 5, 6]}      # _step index -> sequences added before it
+
+    def run(stop: dict[int, list[int]]):
+        eng = _build_reference_engine(cfg, torch.float32, num_blocks=20, pool_seed=3)
+        seqs = {}
+        trace = []
+        cur = {}
+        orig_prefill, orig_decode = eng._run_prefill, eng._run_decode
+
+        def rec_prefill(seq):
+            orig_prefill(seq)
+            cur["prefill"].append([seq.seq_id, seq.token_ids[-1] if seq.output_len else None])
+
+        model = eng.model
+
+        def forward(input_ids, positions, **kw):      # the tables the decode forward is given
+            if kw.get("use_cache"):
+                cur["block_tables"] = [list(t) for t in kw["block_tables"]]
+                cur["slot_idx"] = list(kw["slot_idx"])
+            return model(input_ids, positions, **kw)
+
+        def rec_decode(batch):
+            before = {q.seq_id: q.output_len for q in batch}
+            orig_decode(batch)
+            cur["decode"] = [q.seq_id for q in batch if q.output_len > before[q.seq_id]]
+            cur["decode_tokens"] = {str(q.seq_id): q.token_ids[-1] for q in batch if q.output_len > before[q.seq_id]}
+
+        eng.model = forward
+
+        eng._run_prefill, eng._run_decode = rec_prefill, rec_decode
+        step = 0
+        with torch.no_grad():
+            while step == 0 or eng.scheduler.has_unfinished or step in joins:
+                for i in joins.get(step, []):
+                    q = Sequence(prompt_token_ids=prompts[i], seq_id=i,
+                                 sampling_params=SamplingParams(temperature=0.0, max_tokens=max_toks[i]))
+                    q.set_stop_conditions(stop.get(i, []))
+                    eng.scheduler.add_sequence(q)
+                    seqs[i] = q
+                cur.clear()
+                cur.update(prefill=[], decode=[], block_tables=[], slot_idx=[], decode_tokens={})
+                eng._step()
+                cur["free_after"] = list(eng.kv_cache.free_blocks)
+                cur["finished_after"] = sorted(i for i, q in seqs.items() if q.is_finished())
+                trace.append(dict(cur))
+                step += 1
+        return trace, {i: q.token_ids[q.prompt_len:] for i, q in seqs.items()}
+
+    _, dry = run({})
+    stop_tok = dry[3][5]            # sequence 3 stops at its first occurrence of its 6th token
+    trace, outs = run({3: [stop_tok]})
+    return {"arch": "qwen3-tiny", "num_blocks": 20, "pool_seed": 3, "prompts": prompts, "max_tokens": max_toks,
+            "stop": {"3": [stop_tok]}, "joins": {str(k): v for k, v in joins.items()}, "trace": trace,
+            "outputs": {str(k): v for k, v in outs.items()}}
+
+
 def make_moe_golden() -> dict:
     """The reference's sparse-MoE model (``models/qwen3_moe_model.py``) in fp32: the MoE block of
     layer 0 on seeded hidden states, and greedy decoding through ``LLMEngine._step`` (the engine
@@ -303,9 +381,12 @@ def make_gemma3_golden() -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("MINI_VLLM_REFERENCE"),
+                    help="path of the reference checkout (default: $MINI_VLLM_REFERENCE)")
     ap.add_argument("--only", default="", help="comma list of fixtures to (re)make")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or MINI_VLLM_REFERENCE) must name the reference checkout")
     _import_reference(args.reference)
     torch.set_num_threads(os.cpu_count() or 8)
     only = set(filter(None, args.only.split(",")))
@@ -328,6 +409,9 @@ def main() -> None:
         fx["arch"] = "qwen3-tiny"
         torch.save(fx, HERE / "decode_tiny_bf16.pt")
         print("decode_tiny_bf16.pt written")
+    if want("engine-trace"):
+        (HERE / "engine_trace.json").write_text(json.dumps(make_engine_trace_golden()))
+        print("engine_trace.json written")
     if want("moe"):
         torch.save(make_moe_golden(), HERE / "decode_moe_tiny_f32.pt")
         print("decode_moe_tiny_f32.pt written")
@@ -342,6 +426,15 @@ def main() -> None:
         fx["arch"] = "qwen3-0.6b"
         torch.save(fx, HERE / "decode_qwen3_0.6b_f32.pt")
         print("decode_qwen3_0.6b_f32.pt written")
+    if want("qwen3-0.6b-bf16"):
+        # the same architecture, weights and prompts in bf16: greedy, the prefill's token + 32 decode steps
+        cfg = get_config("qwen3-0.6b")
+        g = torch.Generator().manual_seed(0)
+        prompts = [torch.randint(0, cfg["vocab_size"], (128,), generator=g).tolist() for _ in range(4)]
+        fx = _decode_fixture(cfg, torch.bfloat16, prompts, 33, keep_full_logits=False)
+        fx["arch"] = "qwen3-0.6b"
+        torch.save(fx, HERE / "decode_qwen3_0.6b_bf16.pt")
+        print("decode_qwen3_0.6b_bf16.pt written")
 
 
 if __name__ == "__main__":
