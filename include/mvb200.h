@@ -229,7 +229,9 @@ int mvb_prefill_attention(void* out, int64_t out_stride, const void* q, int64_t 
  * sequences; larger shapes return MVB_ERR_UNSUPPORTED.  The first call on a device looks up
  * the area's device address (cudaGetSymbolAddress), so make that first call before any
  * stream capture.  All calls on a device share the area: each call clears its counters
- * itself, and calls that overlap on the GPU (e.g. on two streams) race. */
+ * itself, and calls that overlap on the GPU (e.g. on two streams) race.  The looked-up address
+ * is kept until the process exits: do not reset a device (cudaDeviceReset) after using this
+ * entry point on it. */
 int mvb_paged_attention_decode_noalloc(void* out, int64_t out_stride, const void* q, int64_t q_stride,
                                        const void* kv_cache, const int32_t* block_tables, int64_t max_blocks,
                                        const int32_t* ctx_lens, int64_t batch, int64_t num_q_heads,

@@ -908,7 +908,10 @@ extern "C" int mvb_paged_attention_decode_noalloc(void* out, int64_t out_stride,
   void* scratch = nullptr;
   {
     // Set-up on the first call on each device (the current one): host code cannot use the
-    // array's name as a device address, so look the address up and keep it.
+    // array's name as a device address, so look the address up and keep it.  The address is
+    // kept for the life of the process: a device reset (cudaDeviceReset) after the first call
+    // reloads the module, and the kept address would then be stale, so resetting a device that
+    // this entry point has used is not supported.
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     if (g_scratch_ptr[dev] == nullptr) {
       void* p = nullptr;
@@ -930,8 +933,9 @@ extern "C" int mvb_paged_attention_decode_noalloc(void* out, int64_t out_stride,
                 "scratch; the built-in area holds %lld (use mvb_paged_attention_decode with a workspace)",
                 (long long)num_q_heads, (long long)head_dim, sms, (long long)need, (long long)kNoAllocScratchBytes);
   if (batch == 0) return MVB_OK;
-  // The area keeps whatever the previous call left; the per-sequence counters must start at
-  // zero, so clear them (they sit at the tail) in stream order before the kernel.
+  // The area keeps whatever the previous call left.  A call that completes leaves its counters
+  // at zero, but one whose kernel gave up on a bounded wait may not; the per-sequence counters
+  // must start at zero, so clear them (they sit at the tail) in stream order before the kernel.
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   MVB_TRY(cuda_status(cudaMemsetAsync(static_cast<char*>(scratch) + kNoAllocScratchBytes - cbytes, 0, cbytes, st),
                       "mvb_paged_attention_decode_noalloc: clear counters"));

@@ -48,13 +48,15 @@ def resolve_device(device) -> torch.device:
 def rope_tables(head_dim_: int, theta: float, length: int, dtype: torch.dtype, device) -> tuple[torch.Tensor, torch.Tensor]:
     """cos/sin ``[length, D]`` as the reference's ``RotaryEmbedding`` holds them after
     ``model.to(dtype)``: fp32 ``inv_freq`` rounded to ``dtype``, position ramp in ``dtype``
-    (``models/model.py:31``, ``:75-80``).  Built on the host, then copied."""
+    (``models/model.py:31``, ``:75-80``).  Built on ``device``, as the reference builds them on the
+    device of the positions: a bf16 ramp rounds differently on the CPU and on the GPU past
+    position 4112, and a bf16 model decodes on the GPU."""
     inv = 1.0 / (theta ** (torch.arange(0, head_dim_, 2).float() / head_dim_))
-    inv = inv.to(dtype)
-    t = torch.arange(length, dtype=inv.dtype)
+    inv = inv.to(dtype).to(device)
+    t = torch.arange(length, dtype=inv.dtype, device=device)
     freqs = torch.outer(t, inv)
     emb = torch.cat((freqs, freqs), dim=-1)
-    return emb.cos().to(device).contiguous(), emb.sin().to(device).contiguous()
+    return emb.cos().contiguous(), emb.sin().contiguous()
 
 
 def meta_layout(batch: int, max_blocks: int) -> dict[str, int]:
@@ -106,6 +108,9 @@ class DecodeWeights:
                     self.egu.append(torch.stack([torch.cat([get(f"{e}{j}.gate_proj.weight"), get(f"{e}{j}.up_proj.weight")],
                                                            0) for j in range(E)]).contiguous())
                     self.edown.append(torch.stack([get(f"{e}{j}.down_proj.weight") for j in range(E)]).contiguous())
+            elif p + "mlp.gate_up_proj.weight" in sd:   # already fused (ops/mlp.py:87-121)
+                self.wgu.append(get(p + "mlp.gate_up_proj.weight"))
+                self.wdown.append(get(p + "mlp.down_proj.weight"))
             else:
                 self.wgu.append(torch.cat([get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight")],
                                           0).contiguous())

@@ -121,6 +121,18 @@ def test_rope_op_matches_reference(golden):
     assert torch.equal(ke.cpu(), golden["rope_k_out"])
 
 
+def test_rope_tables_are_built_where_the_reference_builds_them():
+    """The reference builds its cos/sin cache on the device of the positions (``model.py:74-80``),
+    and a bf16 position ramp rounds differently on the CPU and on the GPU past position 4112.  The
+    decode path's tables equal the oracle's built on the same GPU, at every position up to 9000."""
+    from llm_pytorch_inference_b200.runner import rope_tables
+
+    for theta in (1e6, 5e5):
+        cos, sin = rope_tables(128, theta, 9000, torch.bfloat16, DEV)
+        ocos, osin = om.rope_tables(128, theta, 9000, torch.bfloat16, DEV)
+        assert torch.equal(cos, ocos) and torch.equal(sin, osin)
+
+
 def test_activations_embedding_softmax(golden):
     ax, ay = golden["act_x"].to(DEV), golden["act_y"].to(DEV)
     for fn, key in ((ops.silu, "silu"), (ops.gelu, "gelu")):
@@ -229,7 +241,8 @@ def _gemm_partials(x, w, ws, epilogue=N.EPI_PARTIALS):
                                   N.stream_handle()), "gemm partials")
 
 
-@pytest.mark.parametrize("m,inter,k", [(64, 12288, 4096), (64, 3072, 1024), (5, 1536, 2048), (200, 256, 512)])
+@pytest.mark.parametrize("m,inter,k", [(64, 12288, 4096), (64, 3072, 1024), (5, 1536, 2048), (200, 256, 512),
+                                        (128, 14336, 4096), (128, 12288, 4096), (256, 12288, 4096)])
 def test_swiglu_from_split_k_partials_bit_exact(m, inter, k):
     """GEMM(MVB_EPI_SWIGLU_PARTIALS) + mvb_swiglu_gemm == GEMM(MVB_EPI_SWIGLU): same contributor-order
     sums, same rounding sequence.  Runs twice on one workspace (the finalize leaves nothing behind)."""
@@ -247,7 +260,8 @@ def test_swiglu_from_split_k_partials_bit_exact(m, inter, k):
         assert bool(got[:, inter:].isnan().all())   # nothing written past inter
 
 
-@pytest.mark.parametrize("m,n,k", [(64, 4096, 4096), (64, 4096, 12288), (13, 1024, 512)])
+@pytest.mark.parametrize("m,n,k", [(64, 4096, 4096), (64, 4096, 12288), (13, 1024, 512), (128, 4096, 14336),
+                                   (128, 4096, 4096), (256, 4096, 4096)])
 def test_split_k_partials_feed_fused_add_rmsnorm_bit_exactly(m, n, k):
     """GEMM(MVB_EPI_PARTIALS) + mvb_fused_add_rmsnorm_gemm == GEMM(STORE) + fused_add_rmsnorm (model
     semantics): the consumer sums the same partials in the same order, so the updated residual is
@@ -321,8 +335,10 @@ def test_qk_norm_rope_kv_write_indexing_is_bit_exact():
     assert bf16_ulps(q.cpu(), qo[:, :, 0]) <= 1
 
 
-def test_qk_norm_rope_kv_write_from_split_k_partials_bit_exact():
-    B, Hq, Hkv, D, L, P, H = 64, 32, 8, 128, 2, 300, 4096
+@pytest.mark.parametrize("B,qk_norm", [(64, True), (128, True), (128, False), (256, False)])
+def test_qk_norm_rope_kv_write_from_split_k_partials_bit_exact(B, qk_norm):
+    Hq, Hkv, D, L, H = 32, 8, 128, 2, 4096
+    P = 5 * B
     g = torch.Generator(device=DEV).manual_seed(5)
     x = (torch.randn(B, H, device=DEV, generator=g) / math.sqrt(H)).to(torch.bfloat16)
     wqkv = torch.randn((Hq + 2 * Hkv) * D, H, device=DEV, generator=g).to(torch.bfloat16)
@@ -332,6 +348,8 @@ def test_qk_norm_rope_kv_write_from_split_k_partials_bit_exact():
     cos, sin = cos.to(DEV), sin.to(DEV)
     pos = torch.randint(0, 64, (B,), device=DEV, dtype=torch.int32)
     bt = torch.randperm(P, device=DEV)[:B * 4].to(torch.int32).view(B, 4)
+    if not qk_norm:   # Llama-family: no per-head norm
+        qn = kn = None
     pool_a = torch.zeros(L, 2, P + 1, 16, Hkv, D, dtype=torch.bfloat16, device=DEV)
     pool_b = pool_a.clone()
     qkv = ops.linear(x, wqkv)
@@ -340,7 +358,7 @@ def test_qk_norm_rope_kv_write_from_split_k_partials_bit_exact():
     _gemm_partials(x, wqkv, ws)
     q_b = torch.empty_like(q_a)
     N.check(N.lib().mvb_qk_norm_rope_kv_write_gemm(
-        q_b.data_ptr(), pool_b.data_ptr(), ws.data_ptr(), H, qn.data_ptr(), kn.data_ptr(), cos.data_ptr(),
+        q_b.data_ptr(), pool_b.data_ptr(), ws.data_ptr(), H, N.ptr(qn), N.ptr(kn), cos.data_ptr(),
         sin.data_ptr(), cos.shape[0], pos.data_ptr(), bt.data_ptr(), 4, B, Hq, Hkv, D, L, 1, P + 1, 16, 1e-6, 0,
         N.stream_handle()), "qk gemm")
     assert torch.equal(q_a, q_b) and torch.equal(pool_a, pool_b)
@@ -390,6 +408,8 @@ def _attention_ref(q, pool, layer, bts, ctx, scale, softcap=0.0, window=0):
     (16, 4, [2049] * 12 + [7, 300]),            # TP=2 shard of Qwen3-8B
     (8, 2, [1200] * 16),                        # TP=4 shard
     (4, 1, [2049] * 16),                        # TP=8 shard
+    # Llama-3-8B heads, a batch of 128 with contexts drawn from 128-8192 (up to 513 blocks each)
+    (32, 8, [128 + (7919 * i) % 8065 for i in range(128)]),
 ])
 def test_paged_attention_matches_fp32_reference(Hq, Hkv, lens):
     D, L, layer = 128, 2, 1

@@ -71,8 +71,10 @@ def test_no_alloc_attention_matches_workspace_version_on_two_calls():
     ref_a = _with_workspace(a)
     torch.testing.assert_close(got_a.float(), ref_a.float(), rtol=2e-2, atol=1e-2)
     # second call straight after, different shape and batch: the area still holds the first
-    # call's partials, and its counters sit at a different offset
-    b = _case(16, 8, [129, 5, 64, 4000, 2], seed=2)
+    # call's partials; 100 sequences need 400 bytes of per-sequence counters, so the counter area
+    # (at the tail) is twice the first call's 256 bytes and starts 256 bytes lower
+    lens = [129, 5, 64, 4000, 2] + [1 + (37 * i) % 300 for i in range(95)]
+    b = _case(16, 8, lens, seed=2)
     got_b = _no_alloc(b)
     ref_b = _with_workspace(b)
     torch.testing.assert_close(got_b.float(), ref_b.float(), rtol=2e-2, atol=1e-2)
