@@ -56,7 +56,7 @@ def parse_args(argv=None):
     ap.add_argument("--layers", type=int, default=None, help="override layer count (debug only; invalid bench)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pdl", type=int, default=1)
-    ap.add_argument("--case", default=None, choices=["kernels", "moe", "gemma2", "prefill", "prefill-kernels"],
+    ap.add_argument("--case", default=None, choices=["kernels", "moe", "gemma2", "llama3", "prefill", "prefill-kernels"],
                     help="kernels: small profiling case (2 layers of the workload's dims), each kernel kind "
                          "launched a few times; prints per-kernel timings only.  moe: the sparse-MoE decode "
                          "workload (Qwen3-30B-A3B arch, batch 32, prompt 4096, greedy), 1 GPU.  gemma2: the "
@@ -512,6 +512,86 @@ def run_moe_case(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_llama3_case(args) -> None:
+    """Llama-3-8B-architecture decode (32 layers, hidden 4096, 32/8 heads, SwiGLU 14336, vocab 128256,
+    theta 5e5, no QK-norm), a mixed batch of 128 sequences whose contexts are drawn uniformly from
+    128-8192 (seeded), K/V filled with seeded synthetic values in a shuffled pool, greedy.  Same
+    timing rules as the headline line; the e2e figure goes through ``DecodeEngine.step()``."""
+    from llm_pytorch_inference_b200 import _native as N
+    from llm_pytorch_inference_b200.configs import get_config
+    from llm_pytorch_inference_b200.engine import DecodeEngine
+    from llm_pytorch_inference_b200.weights import canonical_state_dict
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    N.set_pdl(bool(args.pdl))
+    cfg = get_config("llama3-8b")
+    B = 128
+    W, K = args.warmup, args.steps
+    g = torch.Generator().manual_seed(42)
+    lens = torch.randint(128, 8193, (B,), generator=g).tolist()
+    sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev)
+    eng = DecodeEngine(cfg, sd, max_batch=B, max_model_len=max(lens) + 2 * (W + 2 * K) + 32, device=dev)
+    del sd
+    order = list(range(eng.kv.num_blocks))
+    random.Random(0).shuffle(order)
+    from collections import deque
+
+    eng.kv.free_blocks = deque(order)
+    for s, n in enumerate(lens):
+        eng.add_sequence(s, torch.randint(0, cfg["vocab_size"], (n,), generator=g).tolist())
+        eng.append_first_token(s, int(torch.randint(0, cfg["vocab_size"], (1,), generator=g)))
+    eng.prefill_synthetic(seed=0)
+    eng.set_sampling(0.0, -1, 1.0)
+    eng.prepare_first_step()
+    r = eng.runner
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(W):
+        eng.step()
+    torch.cuda.synchronize(dev)
+    metas = torch.stack([eng.plan_step(eng.runner.tokens_host[:B].tolist()) for _ in range(K)]).to(dev)
+    clocks = ClockSampler(0)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(K):
+        r.meta.copy_(metas[k], non_blocking=True)
+        r.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / K
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(K):
+        eng.step()
+    e3.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e2.elapsed_time(e3) / K
+    clk = clocks.stop()
+    step_bytes = r.algorithmic_step_bytes()
+    kinds = r.time_kernels(iters=32)
+    top = max(kinds, key=lambda k: kinds[k]["avg_ms"] * kinds[k]["launches_per_step"])
+    pk = peaks()
+    line = {"case": "llama3", "metric": "decode tokens/s Llama-3-8B-arch bf16 batch 128 ctx U[128,8192] greedy",
+            "value": round(B / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 4), "steps": K,
+            "warmup": W, "config": {"workload": "llama3-8b decode, batch 128, contexts U[128,8192] (seeded), greedy",
+                                     "layers": cfg["num_hidden_layers"], "mean_context": round(sum(lens) / B, 1),
+                                     "parallelism": "tp1"},
+            "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": r.meta_host.numel() * 4, "d2h_bytes_per_step": B * 8},
+            "step_bytes": step_bytes,
+            "step_roofline": {"achieved_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),
+                              "frac": round(step_bytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)},
+            "roofline": {"kernel": top, "bound": "hbm", "achieved": round(kinds[top]["gbs"], 1), "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(kinds[top]["gbs"] / pk["hbm_gbs"], 3),
+                         "peak_source": pk["source"]},
+            "kernels": {k: {"avg_us": round(v["avg_ms"] * 1e3, 2), "per_step": v["launches_per_step"],
+                            "gbs": round(v["gbs"], 1)} for k, v in kinds.items()},
+            "launches_per_step": r.launches_per_step(), "clocks": clk,
+            "device_status": N.device_status(clear=True)}
+    print(json.dumps(line), flush=True)
+
+
 def run_gemma2_case(args) -> None:
     """Gemma-2-9B-architecture decode (42 layers, hidden 3584, 16/8 heads of 256, GeGLU 14336,
     vocab 256000, alternating 4096-token sliding-window / global layers, soft-capping 50 / 30,
@@ -718,6 +798,9 @@ def main(argv=None) -> int:
         return 0
     if args.case == "prefill-kernels":
         run_prefill_kernel_case(args)
+        return 0
+    if args.case == "llama3":
+        run_llama3_case(args)
         return 0
     if args.case == "moe":
         run_moe_case(args)
