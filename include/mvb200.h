@@ -293,6 +293,37 @@ int mvb_fused_norm_add_rmsnorm_gemm(void* out, void* residual, const void* gemm_
                                     int64_t hidden, int64_t gemm_k, const void* post_weight, const void* weight,
                                     float eps, int plus_one, mvb_stream_t stream);
 
+/* ---- fused decoder layer --------------------------------------------------------------
+ * Everything of one dense decode layer after its attention, and the next layer's projection,
+ * in one persistent launch (DecoderLayer.forward after self_attn, models/model.py:315-328,
+ * model_cuda.py:306-321; then Attention.forward's q/k/v projections, QK-norm, RoPE and
+ * _write_kv_cache of the next layer, model.py:154-243):
+ *   residual += o_proj(attn);  xn = RMSNorm(residual; ln2)
+ *   h = silu(gate(xn)) * up(xn)             (wgu = cat([gate, up]), ops/mlp.py:87-121)
+ *   residual += down(h);       xn = RMSNorm(residual; ln_next)   (next input norm | final norm)
+ *   if wqkv_next: q|k|v = xn W^T, QK-norm (q_norm_next / k_norm_next, or none), RoPE at
+ *                 positions, K/V written to (next_layer, block_tables[b][pos/bs], pos%bs), q -> q_out
+ * The GEMMs run on tcgen05 with a stream-K split over two CTAs per SM (fp32 partials summed in a
+ * fixed order: deterministic); results agree with the unfused kernels to bf16 rounding.  All CTAs
+ * are resident and meet at grid barriers; every wait is bounded (MVB_DEV_WAIT_TIMEOUT).
+ * Shapes: batch m <= 64, head_dim 128, hidden a multiple of 64 and <= 4096, intermediate a
+ * multiple of 64; weights contiguous [n, k] bf16; attn [m, Hq*D] (row stride attn_stride),
+ * residual / xn [m, hidden], h [m, inter], q_out [m, Hq, D].
+ * workspace: >= mvb_decoder_layer_workspace_bytes(), 256-byte aligned (fp32 partials and
+ * per-tile flags).  barrier: 256 bytes, 128-byte aligned.  Zero both before the first call; the
+ * calls leave them ready for the next one; calls that share them must be stream-ordered.  After a
+ * call that reported MVB_DEV_WAIT_TIMEOUT, zero both again. */
+int64_t mvb_decoder_layer_workspace_bytes(int64_t m, int64_t hidden, int64_t q_dim, int64_t inter, int64_t qkv_dim,
+                                          int device);
+int mvb_decoder_layer_tail(const void* attn, int64_t attn_stride, const void* wo, const void* ln2, const void* wgu,
+                           const void* wdown, const void* ln_next, const void* wqkv_next, const void* q_norm_next,
+                           const void* k_norm_next, void* residual, void* xn, void* h, void* q_out, void* kv_cache,
+                           const void* cos, const void* sin, int64_t table_len, const int32_t* positions,
+                           const int32_t* block_tables, int64_t max_blocks, int64_t m, int64_t hidden,
+                           int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t inter,
+                           int64_t num_layers, int64_t next_layer, int64_t num_blocks, int64_t block_size, float eps,
+                           void* workspace, int64_t workspace_bytes, void* barrier, mvb_stream_t stream);
+
 /* Logit soft-capping in place (Gemma-2's final_logit_softcapping): x = T(T(tanh(T(x / cap))) * cap),
  * the rounding sequence of `logits / cap; tanh; * cap` in the logits' dtype.  n elements of
  * dtype MVB_BF16 or MVB_F32; cap > 0. */

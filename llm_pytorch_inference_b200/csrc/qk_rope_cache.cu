@@ -11,6 +11,7 @@
 // the device status word and nothing is written for that token.
 #include "common.cuh"
 #include "host.h"
+#include "qk_rope.cuh"
 #include "splitk.cuh"
 
 namespace mvb {
@@ -24,126 +25,17 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     const int32_t* __restrict__ positions, const int32_t* __restrict__ block_tables, int64_t max_blocks, int batch,
     int nq, int nkv, int64_t layer, int64_t num_blocks, int bs, float eps, int plus_one, unsigned* err,
     const float* __restrict__ partials, SplitKPlan plan) {
-  constexpr int E = D / 32;
   pdl_launch_dependents();
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int heads = nq + 2 * nkv;
-  if (warp_global >= batch * heads) {
-    pdl_wait();
-    return;
-  }
+  pdl_wait();
+  if (warp_global >= batch * heads) return;
   const int b = warp_global / heads;
   const int h = warp_global - b * heads;
-  const int d0 = lane * E;
-
-  pdl_wait();
-  const __nv_bfloat16* src =
-      partials ? nullptr : qkv + static_cast<int64_t>(b) * qkv_stride + static_cast<int64_t>(h) * D + d0;
-  float x[E];
-  if (partials == nullptr) {
-#pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = __bfloat162float(src[e]);
-  } else {
-    // The projection's bf16 output, formed from the GEMM's split-K partial slots: the lane's E
-    // consecutive features sit in one 128-feature tile, read as float4 per contributor.
-    const int n0 = h * D + d0;
-    const int t = n0 / kSplitBM, r = n0 - t * kSplitBM;
-    const int nc = sk_count(plan, t);
-    float acc[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e) acc[e] = 0.0f;
-    for (int j = 0; j < nc; ++j) {
-      const float* src_p = partials + sk_offset(plan, t, j, b, r);
-      if constexpr (E % 4 == 0) {
-#pragma unroll
-        for (int e4 = 0; e4 < E; e4 += 4) {
-          const float4 q = __ldcg(reinterpret_cast<const float4*>(src_p + e4));
-          acc[e4] += q.x;
-          acc[e4 + 1] += q.y;
-          acc[e4 + 2] += q.z;
-          acc[e4 + 3] += q.w;
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < E; ++e) acc[e] += __ldcg(src_p + e);
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = bf16_round(acc[e]);
-  }
-
-  const int pos = positions[b];
-  const bool is_q = h < nq, is_k = !is_q && h < nq + nkv;
-
-  // Slot of this token in the paged pool (only K/V heads need it).
-  int64_t dst_off = -1;
-  if (!is_q) {
-    const int64_t bidx = pos / bs;
-    if (pos < 0 || bidx >= max_blocks) {
-      if (lane == 0) report(err, kDevBadPosition);
-      return;
-    }
-    const int64_t blk = block_tables[static_cast<int64_t>(b) * max_blocks + bidx];
-    if (blk < 0 || blk >= num_blocks) {
-      if (lane == 0) report(err, kDevBadBlock);
-      return;
-    }
-    const int kvh = is_k ? h - nq : h - nq - nkv;
-    const int64_t which = is_k ? 0 : 1;
-    dst_off = ((((layer * 2 + which) * num_blocks + blk) * bs + (pos % bs)) * nkv + kvh) * D + d0;
-  }
-
-  if (!is_q && !is_k) {  // V: plain copy into the cache
-#pragma unroll
-    for (int e = 0; e < E; ++e) kv[dst_off + e] = __float2bfloat16_rn(x[e]);
-    return;
-  }
-
-  // Per-head RMSNorm (model semantics: T(w * (x * r)); Gemma's plus-one form T((x * r) * (1 + w)),
-  // models/gemma3_model.py:21-25).
-  const __nv_bfloat16* nw = is_q ? qnw : knw;
-  if (nw != nullptr) {
-    float ss = 0.0f;
-#pragma unroll
-    for (int e = 0; e < E; ++e) ss += x[e] * x[e];
-    ss = warp_sum(ss);
-    const float r = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const float wv = __bfloat162float(nw[d0 + e]);
-      x[e] = plus_one ? bf16_round((x[e] * r) * (1.0f + wv)) : bf16_round(wv * (x[e] * r));
-    }
-  }
-
-  // RoPE with the model's bf16 cos/sin rows: T(T(x*cos) + T(rot(x)*sin)).
-  float out[E];
-  if (pos < 0 || pos >= table_len) {
-    if (lane == 0) report(err, kDevBadPosition);
-#pragma unroll
-    for (int e = 0; e < E; ++e) out[e] = 0.0f;
-  } else {
-    const __nv_bfloat16* c = cos_t + static_cast<int64_t>(pos) * D + d0;
-    const __nv_bfloat16* s = sin_t + static_cast<int64_t>(pos) * D + d0;
-    const bool low = lane < 16;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
-      const float rot = low ? -partner : partner;
-      const float a = bf16_round(x[e] * __bfloat162float(c[e]));
-      const float bb = bf16_round(rot * __bfloat162float(s[e]));
-      out[e] = a + bb;
-    }
-  }
-
-  if (is_q) {
-    __nv_bfloat16* q = q_out + (static_cast<int64_t>(b) * nq + h) * D + d0;
-#pragma unroll
-    for (int e = 0; e < E; ++e) q[e] = __float2bfloat16_rn(out[e]);
-  } else if (dst_off >= 0) {
-#pragma unroll
-    for (int e = 0; e < E; ++e) kv[dst_off + e] = __float2bfloat16_rn(out[e]);
-  }
+  qk_norm_rope_kv_one<D>(b, h, lane, q_out, kv, qkv, qkv_stride, qnw, knw, cos_t, sin_t, table_len, positions,
+                         block_tables, max_blocks, nq, nkv, layer, num_blocks, bs, eps, plus_one, err, partials,
+                         plan);
 }
 
 }  // namespace

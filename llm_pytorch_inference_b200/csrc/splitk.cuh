@@ -47,6 +47,101 @@ __host__ __device__ __forceinline__ int64_t sk_offset(const SplitKPlan& p, int t
   return ((static_cast<int64_t>(t) * p.maxc + j) * p.bn + b) * kSplitBM + r;
 }
 
+// Sum, in contributor order, of the float4 at (column b, rows r..r+3) over the contributors of
+// tile t.  The loads of up to 8 contributors are issued together: one L2 round trip per 8
+// contributors instead of one per contributor (the order of the additions is unchanged).
+__device__ __forceinline__ float4 sk_sum4(const float* partials, const SplitKPlan& p, int t, int b, int r) {
+  const int nc = sk_count(p, t);
+  const float* base = partials + sk_offset(p, t, 0, b, r);
+  const int64_t stride = static_cast<int64_t>(p.bn) * kSplitBM;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j0 = 0; j0 < nc; j0 += 8) {
+    float4 q[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j0 + j < nc) q[j] = __ldcg(reinterpret_cast<const float4*>(base + (j0 + j) * stride));
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j0 + j < nc) {
+        acc.x += q[j].x;
+        acc.y += q[j].y;
+        acc.z += q[j].z;
+        acc.w += q[j].w;
+      }
+  }
+  return acc;
+}
+
+// sk_sum4 of two elements at once, 4 contributors of each in flight together; `second` false
+// skips the second one.
+__device__ __forceinline__ void sk_sum4_x2(const float* partials, const SplitKPlan& p, int t1, int b1, int r1,
+                                           int t2, int b2, int r2, bool second, float4& o1, float4& o2) {
+  const int n1 = sk_count(p, t1), n2 = second ? sk_count(p, t2) : 0;
+  const float* base1 = partials + sk_offset(p, t1, 0, b1, r1);
+  const float* base2 = partials + sk_offset(p, t2, 0, b2, r2);
+  const int64_t stride = static_cast<int64_t>(p.bn) * kSplitBM;
+  o1 = make_float4(0.f, 0.f, 0.f, 0.f);
+  o2 = o1;
+  for (int j0 = 0; j0 < n1 || j0 < n2; j0 += 4) {
+    float4 q1[4], q2[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j0 + j < n1) q1[j] = __ldcg(reinterpret_cast<const float4*>(base1 + (j0 + j) * stride));
+      if (j0 + j < n2) q2[j] = __ldcg(reinterpret_cast<const float4*>(base2 + (j0 + j) * stride));
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j0 + j < n1) {
+        o1.x += q1[j].x;
+        o1.y += q1[j].y;
+        o1.z += q1[j].z;
+        o1.w += q1[j].w;
+      }
+      if (j0 + j < n2) {
+        o2.x += q2[j].x;
+        o2.y += q2[j].y;
+        o2.z += q2[j].z;
+        o2.w += q2[j].w;
+      }
+    }
+  }
+}
+
+// sk_sum4 of N elements at once (element i valid when i < nvalid), 4 contributors of each in
+// flight together.
+template <int N>
+__device__ __forceinline__ void sk_sum4_n(const float* partials, const SplitKPlan& p, const int (&t)[N],
+                                          const int (&b)[N], const int (&r)[N], int nvalid, float4 (&o)[N]) {
+  const int64_t stride = static_cast<int64_t>(p.bn) * kSplitBM;
+  int n[N];
+  int nmax = 0;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    n[i] = i < nvalid ? sk_count(p, t[i]) : 0;
+    nmax = n[i] > nmax ? n[i] : nmax;
+    o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int j0 = 0; j0 < nmax; j0 += 4) {
+    float4 q[N][4];
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (j0 + j < n[i])
+          q[i][j] = __ldcg(reinterpret_cast<const float4*>(partials + sk_offset(p, t[i], j0 + j, b[i], r[i])));
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (j0 + j < n[i]) {
+          o[i].x += q[i][j].x;
+          o[i].y += q[i][j].y;
+          o[i].z += q[i][j].z;
+          o[i].w += q[i][j].w;
+        }
+  }
+}
+
 inline int sk_bn_for(int64_t m) { return m <= 64 ? 64 : (m <= 128 ? 128 : 256); }
 
 // CTAs a decode GEMM of m batch rows may use on `sms` SMs.  At BN = 64 a CTA holds 4 x 24 KB

@@ -297,7 +297,10 @@ class DecodeEngine(RunningBatch):
 
     def __init__(self, cfg: dict, state_dict: dict[str, torch.Tensor], max_batch: int, max_model_len: int,
                  num_blocks: int | None = None, device="cuda", free_order: list[int] | None = None,
-                 hbm_budget_bytes: int | None = None, tp: TensorParallelConfig | None = None):
+                 hbm_budget_bytes: int | None = None, tp: TensorParallelConfig | None = None,
+                 fused_layers: bool = False):
+        """``fused_layers``: the dense step's layers as one persistent launch each after attention
+        (``DecodeRunner``); off by default."""
         self.cfg = cfg
         self.dev = resolve_device(device)
         self.tp = tp or TensorParallelConfig()
@@ -318,7 +321,8 @@ class DecodeEngine(RunningBatch):
                 dist.all_reduce(t, op=dist.ReduceOp.MIN)
                 num_blocks = int(t.item())
         kv = KVCacheManager(num_blocks, 16, L, nkv, D, device=self.dev, dtype=torch.bfloat16, free_order=free_order)
-        self.runner = DecodeRunner(cfg, self.weights, kv, max_batch, max_model_len, self.dev, tp=self.tp)
+        self.runner = DecodeRunner(cfg, self.weights, kv, max_batch, max_model_len, self.dev, tp=self.tp,
+                                   fused_layers=fused_layers)
         super().__init__(kv, self.runner.B, self.runner.max_blocks, self.runner.meta_host.numpy())
         self._prefill = None
         self.last_prefill_logits = None

@@ -141,7 +141,12 @@ class DecodeWeights:
 
 class DecodeRunner:
     def __init__(self, cfg: dict, weights: DecodeWeights, kv: KVCacheManager, max_batch: int, max_model_len: int,
-                 device="cuda", rope_len: int | None = None, tp: TensorParallelConfig | None = None):
+                 device="cuda", rope_len: int | None = None, tp: TensorParallelConfig | None = None,
+                 fused_layers: bool = False):
+        """``fused_layers``: run each layer after its attention as one persistent launch
+        (``mvb_decoder_layer_tail``; dense, one GPU, batch <= 64, head dim 128, hidden <= 4096)
+        instead of the per-kernel step.  Off by default: on B200 the per-kernel step with
+        programmatic dependent launch is the faster of the two at Qwen3-8B dims."""
         self.cfg = cfg
         self.w = weights
         self.kv = kv
@@ -256,6 +261,17 @@ class DecodeRunner:
         self.attn_ws = torch.zeros(attn_ws, dtype=torch.uint8, device=dev)
         self.graph: torch.cuda.CUDAGraph | None = None
         self.graph_stream: torch.cuda.Stream | None = None
+        eligible = (not self.gemma and not self.moe and not self.tp.enabled and B <= 64 and self.D == 128 and
+                    H % 64 == 0 and H <= 4096 and self.I % 64 == 0 and not cfg.get("_rms_norm_plus_one"))
+        if fused_layers and not eligible:
+            raise ValueError("the fused layer kernel needs a dense one-GPU model, batch <= 64, head dim 128, "
+                             "hidden <= 4096")
+        self.fused = bool(fused_layers)
+        if self.fused:
+            lib = N.lib()
+            self.layer_ws = torch.zeros(lib.mvb_decoder_layer_workspace_bytes(B, H, self.Hq * self.D, self.I, qkv_n,
+                                                                              didx), dtype=torch.uint8, device=dev)
+            self.layer_bar = torch.zeros(256, dtype=torch.uint8, device=dev)
 
     # ----------------------------------------------------------------- metadata
     def set_metadata(self, ids: list[int], positions: list[int], block_tables: list[list[int]], offset: int = 0,
@@ -374,6 +390,36 @@ class DecodeRunner:
                                self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
                                0, self.offset.data_ptr(), N.BF16, self._st), "sample")
 
+    def _layer_tail(self, i) -> None:
+        """Layer i after its attention, and the next layer's q|k|v projection, QK-norm, RoPE and KV
+        write: one fused launch (``mvb_decoder_layer_tail``)."""
+        w, B, H, D = self.w, self.B, self.H, self.D
+        nxt = i + 1 < self.L
+        cos, sin = self.layer_tables[i + 1] if nxt else self.layer_tables[i]
+        N.check(N.lib().mvb_decoder_layer_tail(
+            self.attn.data_ptr(), self.attn.stride(0), w.wo[i].data_ptr(), w.ln2[i].data_ptr(), w.wgu[i].data_ptr(),
+            w.wdown[i].data_ptr(), (w.ln1[i + 1] if nxt else w.final_norm).data_ptr(),
+            w.wqkv[i + 1].data_ptr() if nxt else None,
+            w.qn[i + 1].data_ptr() if nxt and w.qk_norm else None, w.kn[i + 1].data_ptr() if nxt and w.qk_norm else None,
+            self.residual.data_ptr(), self.xn.data_ptr(), self.h.data_ptr(), self.q.data_ptr(),
+            self.kv.kv_cache.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.shape[0], self.pos.data_ptr(),
+            self.block_tables.data_ptr(), self.max_blocks, B, H, self.Hq, self.Hkv, D, self.I, self.L,
+            i + 1 if nxt else 0, self.P, self.kv.block_size, self.eps, self.layer_ws.data_ptr(), self.layer_ws.numel(),
+            self.layer_bar.data_ptr(), self._st), "decoder_layer_tail")
+
+    def _forward_fused(self) -> None:
+        """The dense step with fused layers: embedding, input norm, layer 0's q|k|v GEMM and
+        QK-norm/RoPE/KV write, then per layer its attention and one fused launch for the rest (and
+        the next layer's projection), lm_head and sampling: 2L + 6 launches."""
+        self._st = N.stream_handle(self.dev)
+        self._embed()
+        self._gemm(None, self.xn, self.w.wqkv[0], N.EPI_PARTIALS)
+        self._qk(0)
+        for i in range(self.L):
+            self._attention(i)
+            self._layer_tail(i)
+        self._logits_and_sample()
+
     def forward(self) -> None:
         """Launches one decode step on the current stream (metadata must be on the device)."""
         if self.tp.enabled:
@@ -381,6 +427,9 @@ class DecodeRunner:
             return
         if self.moe:
             self._forward_moe()
+            return
+        if self.fused:
+            self._forward_fused()
             return
         lib, w, B, H = N.lib(), self.w, self.B, self.H
         self._st = N.stream_handle(self.dev)
@@ -576,6 +625,16 @@ class DecodeRunner:
             kinds["softcap"] = (lambda i: N.check(lib.mvb_softcap(self.logits.data_ptr(), B * self.V,
                                                                   self.final_softcap, N.BF16, st), "softcap"),
                                 1, 2 * B * self.V * 2, 0)
+        if self.fused:   # the kinds the fused step launches
+            tail_w = (H * self.Hq * D + 2 * self.I * H + H * self.I + qkv_n * H) * 2 + 3 * H * 2 + 2 * D * 2
+            tail_act = (B * self.Hq * D + 4 * B * H + 2 * B * self.I + B * self.Hq * D) * 2 + 2 * B * self.Hkv * D * 2
+            tail_flops = 2 * B * (H * self.Hq * D + 2 * self.I * H + H * self.I + qkv_n * H)
+            keep = {k: kinds[k] for k in ("paged_attention_decode", "gemm_lm_head", "sample") if k in kinds}
+            keep["gemm_qkv"] = (kinds["gemm_qkv"][0], 1, kinds["gemm_qkv"][2], kinds["gemm_qkv"][3])
+            keep["qk_norm_rope_kv_write"] = (self._qk, 1, kinds["qk_norm_rope_kv_write"][2], 0)
+            keep["decoder_layer_tail"] = (lambda i: self._layer_tail(i % max(self.L - 1, 1)), self.L, tail_w + tail_act,
+                                          tail_flops)
+            return keep
         return kinds
 
     def time_kernels(self, iters: int = 36) -> dict[str, dict]:
@@ -615,6 +674,8 @@ class DecodeRunner:
         sample."""
         if self.moe:   # 11 per layer: qkv, qk, attention, o_proj, add+norm, router, route, gather, 2 GEMMs, combine
             return 2 + self.L * 11 + (self.L - 1) + 3
+        if self.fused:   # embedding, rmsnorm, qkv, qk, then attention + fused tail per layer, lm_head, sample
+            return 4 + 2 * self.L + 2
         if self.tp.enabled:   # + the step-counter kernel and the wait before sampling
             return 2 + self.L * 8 + (self.L - 1) + 3 + 2 + (1 if self.final_softcap else 0)
         return 2 + self.L * 8 + (self.L - 1) + 3 + (1 if self.final_softcap else 0)

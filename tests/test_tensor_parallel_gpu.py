@@ -37,11 +37,11 @@ pytestmark = pytest.mark.gpu
 REPO = Path(__file__).resolve().parent.parent
 
 
-def _engine(cfg, sd, tp, batch, lens, num_blocks):
+def _engine(cfg, sd, tp, batch, lens, num_blocks, fused_layers=None):
     order = list(range(num_blocks))
     random.Random(0).shuffle(order)
     eng = DecodeEngine(cfg, sd, max_batch=batch, max_model_len=max(lens) + 64, num_blocks=num_blocks,
-                       device="cuda", free_order=order, tp=tp)
+                       device="cuda", free_order=order, tp=tp, fused_layers=fused_layers)
     g = torch.Generator().manual_seed(1)
     for s, n in enumerate(lens):
         eng.add_sequence(s, torch.randint(0, cfg["vocab_size"], (n,), generator=g).tolist())
@@ -57,7 +57,8 @@ def test_exchange_path_on_one_gpu_is_bit_identical(arch):
     cfg = get_config(arch, num_hidden_layers=2)
     sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device="cuda")
     batch, lens = 16, [40 + 31 * i for i in range(16)]
-    plain = _engine(cfg, sd, TensorParallelConfig(1, 0), batch, lens, 512)
+    # the per-kernel plain step: the exchange kernels share its kernels and sums
+    plain = _engine(cfg, sd, TensorParallelConfig(1, 0), batch, lens, 512, fused_layers=False)
     xchg = _engine(cfg, sd, TensorParallelConfig(1, 0, exchange=True), batch, lens, 512)
     del sd
     N.device_status(clear=True)
