@@ -56,6 +56,8 @@ def parse_args(argv=None):
     ap.add_argument("--layers", type=int, default=None, help="override layer count (debug only; invalid bench)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pdl", type=int, default=1)
+    ap.add_argument("--fused-layers", type=int, default=0,
+                    help="1: one persistent launch per layer tail (mvb_decoder_layer_tail / its tensor-parallel form)")
     ap.add_argument("--case", default=None, choices=["kernels", "moe", "gemma2", "llama3", "prefill", "prefill-kernels"],
                     help="kernels: small profiling case (2 layers of the workload's dims), each kernel kind "
                          "launched a few times; prints per-kernel timings only.  moe: the sparse-MoE decode "
@@ -296,7 +298,8 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
     W, K = args.warmup, args.steps
     max_len = PROMPT + 1 + W + 2 * K + 16
     free_order_seed = 0
-    eng = DecodeEngine(cfg, sd, max_batch=BATCH, max_model_len=max_len, device=dev, tp=tp)
+    eng = DecodeEngine(cfg, sd, max_batch=BATCH, max_model_len=max_len, device=dev, tp=tp,
+                       fused_layers=bool(args.fused_layers))
     del sd
     order = list(range(eng.kv.num_blocks))
     random.Random(free_order_seed).shuffle(order)
@@ -385,7 +388,8 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
                    "seq_len": PROMPT, "context_during_timing": [PROMPT + 1 + W, PROMPT + 1 + W + 2 * K],
                    "parallelism": f"tp{world}",
                    "l2": "inputs larger than L2: 15.1 GB weights + ~20 GB KV read per step",
-                   "kv_pool_blocks": eng.kv.num_blocks, "pdl": bool(args.pdl)},
+                   "kv_pool_blocks": eng.kv.num_blocks, "pdl": bool(args.pdl),
+                   "layer_tail": "one persistent launch" if r.fused else "per-kernel"},
         "roofline": roof, "step_roofline": step_roof,
         "kernels": {k: {"avg_us": round(v["avg_ms"] * 1e3, 2), "per_step": v["launches_per_step"],
                         "share": round(v["share"], 3), "gbs": round(v["gbs"], 1)} for k, v in kinds.items()},

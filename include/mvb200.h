@@ -386,6 +386,30 @@ int mvb_tp_comm_init(int rank, int nranks, void* local_base, const void* ipc_han
                      mvb_tp_comm** comm);
 int mvb_tp_comm_destroy(mvb_tp_comm* comm);
 int mvb_tp_begin_step(mvb_tp_comm* comm, mvb_stream_t stream);
+
+/* Tensor-parallel form of mvb_decoder_layer_tail, one call per rank of the group: the local
+ * shards (num_q_heads, num_kv_heads and inter are this rank's; o_proj / down_proj row-parallel,
+ * the rest column-parallel) and the exchanges of the per-kernel tensor-parallel step inside the
+ * launch -- replaces, per layer, mvb_tp_gemm_bf16 (o_proj push) -> mvb_tp_fused_add_rmsnorm_gemm
+ * -> mvb_tp_gemm_bf16 (gate_up) -> mvb_gated_gemm -> mvb_tp_gemm_bf16 (down push) ->
+ * mvb_tp_fused_add_rmsnorm_gemm -> mvb_tp_gemm_bf16 (next q|k|v) -> QK-norm/RoPE/KV write.
+ *   o_proj and down_proj push their fp32 partials into the receive areas (heap offsets
+ *   recv_o_offset / recv_down_offset, sized by mvb_tp_recv_bytes) of the ranks that own the batch
+ *   rows (m / nranks each); each owner adds them to its residual rows, normalises them and writes
+ *   them into every rank's xn (heap offset xn_offset); signal points 4 * layer .. 4 * layer + 3
+ *   (o_proj pushed, rows gathered, down_proj pushed, rows gathered), as the per-kernel step uses
+ *   them.  mvb_tp_begin_step must have started the step.  Waits for other ranks give up after
+ *   their time limit with MVB_DEV_WAIT_TIMEOUT. */
+int mvb_tp_decoder_layer_tail(mvb_tp_comm* comm, int layer, const void* attn, int64_t attn_stride, const void* wo,
+                              const void* ln2, const void* wgu, const void* wdown, const void* ln_next,
+                              const void* wqkv_next, const void* q_norm_next, const void* k_norm_next, void* residual,
+                              int64_t xn_offset, void* h, void* q_out, void* kv_cache, const void* cos,
+                              const void* sin, int64_t table_len, const int32_t* positions,
+                              const int32_t* block_tables, int64_t max_blocks, int64_t m, int64_t hidden,
+                              int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t inter,
+                              int64_t num_layers, int64_t next_layer, int64_t num_blocks, int64_t block_size,
+                              float eps, int64_t recv_o_offset, int64_t recv_down_offset, void* workspace,
+                              int64_t workspace_bytes, void* barrier, mvb_stream_t stream);
 /* Bytes of the receive area of a row-parallel (push) GEMM of shape [m, n, k_local]. */
 int64_t mvb_tp_recv_bytes(int64_t m, int64_t n, int64_t k, int nranks, int device);
 /* The tcgen05 GEMM of mvb_gemm_bf16 with the exchanges of a tensor-parallel step:

@@ -67,6 +67,8 @@ SIGNATURES: dict[str, tuple] = {
     "mvb_decoder_layer_tail": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                       _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                       _i64, _i64, _f32, _vp, _i64, _vp, _vp]),
+    "mvb_tp_decoder_layer_tail": (_i32, [_vp, _i32, _vp, _i64] + [_vp] * 9 + [_i64] + [_vp] * 5 +
+                                  [_i64, _vp, _vp, _i64] + [_i64] * 10 + [_f32, _i64, _i64, _vp, _i64, _vp, _vp]),
     "mvb_moe_route": (_i32, [_vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mvb_moe_gather": (_i32, [_vp, _vp, _i64, _vp, _i64, _vp]),
     "mvb_moe_gemm_bf16": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _vp, _vp]),

@@ -32,6 +32,7 @@
 #include "host.h"
 #include "qk_rope.cuh"
 #include "splitk.cuh"
+#include "tp.cuh"
 
 namespace mvb {
 namespace {
@@ -48,8 +49,10 @@ constexpr int kMaxPhases = 4;
 constexpr int kLayerMaxHidden = 4096;  // add+norm rows held in the 128 epilogue threads' registers
 
 // What follows a GEMM phase: residual add + RMSNorm over the grid; SwiGLU in the epilogue of each
-// tile's contributor 0 (no consumer pass); QK-norm + RoPE + KV write over the grid.
-enum : int { kConsAddNorm = 0, kConsSwiglu = 1, kConsQk = 2 };
+// tile's contributor 0 (no consumer pass); QK-norm + RoPE + KV write over the grid; tensor
+// parallel: partials pushed to the ranks that own the batch rows, the owners' residual add +
+// RMSNorm of their rows written into every rank's activations.
+enum : int { kConsAddNorm = 0, kConsSwiglu = 1, kConsQk = 2, kConsTpAddNorm = 3 };
 
 struct LayerPhase {
   SplitKPlan plan;   // stream-K split over the launch's grid (plan.grid <= gridDim.x)
@@ -92,6 +95,17 @@ struct LayerArgs {
   // 128-byte lines)
   unsigned* bar;
   unsigned* err;
+  // tensor parallel (nranks > 0): row-parallel o_proj / down_proj push their partials to the
+  // owners of the batch rows (rows_per_rank each); each owner adds and normalises its rows and
+  // writes them into every rank's xn; four signal points per launch (0: o_proj pushed, 1: rows
+  // gathered, 2: down_proj pushed, 3: rows gathered), each signalled once per rank per step.
+  int nranks, rank, rpr;
+  const float* recv[2];                   // this rank's receive areas (o_proj, down_proj)
+  float* push[2][kTpMaxRanks];            // every rank's receive area of the two pushes
+  __nv_bfloat16* xn_all[kTpMaxRanks];     // every rank's xn
+  uint32_t* signal[4][kTpMaxRanks];       // rank q's counter [point][this rank]
+  const uint32_t* wait[4];                // this rank's counters [point][0..nranks)
+  const int32_t* epoch;                   // the step counter (signals per point so far)
 };
 
 struct LayerMaps {
@@ -275,6 +289,113 @@ __device__ __forceinline__ bool wait_passed(volatile uint32_t* nbar_s, uint32_t 
   return true;
 }
 
+// Bounded wait until every rank's counter counters[0..n) reaches `target` (signals from other
+// GPUs: system-scope acquire polls; a system-scope fence here would cost microseconds per CTA).
+__device__ __forceinline__ bool wait_ranks(const uint32_t* counters, int n, uint32_t target, volatile int* abort_flag,
+                                           unsigned* err) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (int s = 0; s < n; ++s) {
+    unsigned polls = 0;
+    while (static_cast<int32_t>(ld_acquire_sys(counters + s) - target) < 0) {
+      __nanosleep(64);
+      if ((++polls & 15u) == 0) {
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          report(err, kDevWaitTimeout);
+          *abort_flag = 1;
+          return false;
+        }
+      }
+    }
+  }
+  return true;
+}
+
+// Tensor parallel: the owner's residual add + RMSNorm of its owned row `bl` (batch row
+// rank * rpr + bl), one CTA's 128 epilogue threads per row: the pushed partials summed over
+// source ranks, then contributors (the order of norm.cu's tensor-parallel fused_add_rmsnorm),
+// residual += bf16(sum), out = bf16(w * (residual * r)) stored into every rank's xn.  The new
+// residual row waits in shared memory (vs, bf16 [hidden]) for the row's 1 / rms.
+constexpr int kTpNormRuns = kLayerMaxHidden / (4 * 128);
+
+__device__ void tp_add_norm_row(const LayerArgs& a, const SplitKPlan& p, const float* __restrict__ recv,
+                                const __nv_bfloat16* __restrict__ w, int bl, int e, float* red,
+                                __nv_bfloat16* vs) {
+  const int b = a.rank * a.rpr + bl;
+  __nv_bfloat16* res = a.residual + static_cast<int64_t>(b) * a.hidden;
+  const int runs = a.hidden / 4;
+  float ss = 0.0f;
+  for (int k0 = 0; k0 < kTpNormRuns; k0 += 2) {
+    float4 acc[2];
+    uint2 rv[2];
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      const int run = e + 128 * (k0 + kk);
+      acc[kk] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (run < runs) {
+        const int i = run * 4;
+        const int t = i / kSplitBM, r = i - t * kSplitBM;
+        const int nc = sk_count(p, t);
+        rv[kk] = __ldcg(reinterpret_cast<const uint2*>(res + i));
+        for (int src = 0; src < a.nranks; ++src)
+          for (int j = 0; j < nc; ++j) {
+            const float4 q =
+                __ldcg(reinterpret_cast<const float4*>(recv + sk_push_offset(p, src, t, j, a.rpr, bl, r)));
+            acc[kk].x += q.x;
+            acc[kk].y += q.y;
+            acc[kk].z += q.z;
+            acc[kk].w += q.w;
+          }
+      }
+    }
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      const int run = e + 128 * (k0 + kk);
+      if (run < runs) {
+        const int i = run * 4;
+        const __nv_bfloat162 r01 = *reinterpret_cast<const __nv_bfloat162*>(&rv[kk].x);
+        const __nv_bfloat162 r23 = *reinterpret_cast<const __nv_bfloat162*>(&rv[kk].y);
+        const float v0 = bf16_round(__low2float(r01) + bf16_round(acc[kk].x));
+        const float v1 = bf16_round(__high2float(r01) + bf16_round(acc[kk].y));
+        const float v2 = bf16_round(__low2float(r23) + bf16_round(acc[kk].z));
+        const float v3 = bf16_round(__high2float(r23) + bf16_round(acc[kk].w));
+        __nv_bfloat162 o01 = __floats2bfloat162_rn(v0, v1);
+        __nv_bfloat162 o23 = __floats2bfloat162_rn(v2, v3);
+        uint2 ov;
+        ov.x = *reinterpret_cast<uint32_t*>(&o01);
+        ov.y = *reinterpret_cast<uint32_t*>(&o23);
+        __stcg(reinterpret_cast<uint2*>(res + i), ov);
+        *reinterpret_cast<uint2*>(vs + i) = ov;
+        ss += v0 * v0 + v1 * v1 + v2 * v2 + v3 * v3;
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  if ((e & 31) == 0) red[e >> 5] = ss;
+  epi_sync();
+  const float total = red[0] + red[1] + red[2] + red[3];
+  const float rs = 1.0f / sqrtf(total / static_cast<float>(a.hidden) + a.eps);
+  for (int run = e; run < runs; run += 128) {
+    const int i = run * 4;
+    const uint2 vv = *reinterpret_cast<const uint2*>(vs + i);
+    const uint2 wv = *reinterpret_cast<const uint2*>(w + i);
+    const __nv_bfloat162 v01 = *reinterpret_cast<const __nv_bfloat162*>(&vv.x);
+    const __nv_bfloat162 v23 = *reinterpret_cast<const __nv_bfloat162*>(&vv.y);
+    const __nv_bfloat162 w01 = *reinterpret_cast<const __nv_bfloat162*>(&wv.x);
+    const __nv_bfloat162 w23 = *reinterpret_cast<const __nv_bfloat162*>(&wv.y);
+    __nv_bfloat162 o01 = __floats2bfloat162_rn(bf16_round(__low2float(w01) * (__low2float(v01) * rs)),
+                                               bf16_round(__high2float(w01) * (__high2float(v01) * rs)));
+    __nv_bfloat162 o23 = __floats2bfloat162_rn(bf16_round(__low2float(w23) * (__low2float(v23) * rs)),
+                                               bf16_round(__high2float(w23) * (__high2float(v23) * rs)));
+    uint2 ov;
+    ov.x = *reinterpret_cast<uint32_t*>(&o01);
+    ov.y = *reinterpret_cast<uint32_t*>(&o23);
+    const int64_t off = static_cast<int64_t>(b) * a.hidden + i;
+    for (int q = 0; q < a.nranks; ++q) *reinterpret_cast<uint2*>(a.xn_all[q] + off) = ov;
+  }
+  epi_sync();   // red and vs are reused by the next row
+}
+
 // SwiGLU of one gate_up tile (64 gate rows | the 64 matching up rows, 64 batch columns) by the
 // tile's contributor 0 in its epilogue: each epilogue thread holds one tile row, sums its
 // accumulator (TMEM) and the other contributors' partials in contributor order (the order of
@@ -348,12 +469,26 @@ __device__ __forceinline__ void phase_range(const SplitKPlan& p, int cta, int64_
 // add+norm consumer, its first pass is complete; except after the last phase, the phase's output
 // is complete.
 __device__ __forceinline__ uint32_t phase_bars(const LayerArgs& a, int p) {
-  return (a.ph[p].consumer == kConsSwiglu ? 0u : 1u) + (a.ph[p].consumer == kConsAddNorm ? 1u : 0u) +
-         (p + 1 < a.nphase ? 1u : 0u);
+  const int c = a.ph[p].consumer;
+  const bool last = p + 1 == a.nphase;
+  if (c == kConsSwiglu) return last ? 0u : 1u;
+  if (c == kConsTpAddNorm) return 2u;   // pushes issued; gathered rows written
+  return 1u + (c == kConsAddNorm ? 1u : 0u) + (last ? 0u : 1u);
+}
+// Synchronisation points of phase p: its grid barriers, and for a tensor-parallel add+norm the
+// waits for every rank's signal (pushed; unless last, gathered).  The producer loads a phase's
+// activations once the epilogue has passed every point before it.
+__device__ __forceinline__ uint32_t phase_syncs(const LayerArgs& a, int p) {
+  return phase_bars(a, p) + (a.ph[p].consumer == kConsTpAddNorm ? (p + 1 == a.nphase ? 1u : 2u) : 0u);
 }
 __device__ __forceinline__ uint32_t bars_before(const LayerArgs& a, int p) {
   uint32_t n = 0;
   for (int q = 0; q < p; ++q) n += phase_bars(a, q);
+  return n;
+}
+__device__ __forceinline__ uint32_t syncs_before(const LayerArgs& a, int p) {
+  uint32_t n = 0;
+  for (int q = 0; q < p; ++q) n += phase_syncs(a, q);
   return n;
 }
 
@@ -371,14 +506,15 @@ __global__ void __launch_bounds__(kLayerThreads, 2)
   uint64_t* drain = acce + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  // grid barriers the epilogue has passed (written by its thread 0 after a CTA-scope fence; the
-  // producer polls it instead of the global count)
+  // synchronisation points the epilogue has passed (written by its thread 0 after a CTA-scope
+  // fence; the producer polls it instead of the global count)
   volatile uint32_t* nbar_s = reinterpret_cast<volatile uint32_t*>(abort_flag + 1);
   volatile int* leave = reinterpret_cast<volatile int*>(nbar_s + 1);   // thread 0's decision, read after a barrier
   volatile int* go_s = leave + 1;                                      // SwiGLU reducer: partials seen
   float* red = reinterpret_cast<float*>(smem + LSTAGES * LSTAGE + 256);   // [4]
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(red + 4);           // [32][64] SwiGLU bf16(up)
-  __nv_bfloat16* hs = xs + 32 * 64;                                         // [64][64] SwiGLU output tile
+  __nv_bfloat16* hs = xs + 32 * 64;   // [64][64] SwiGLU output tile; tensor parallel: a residual row
+  static_assert(64 * 64 >= kLayerMaxHidden, "a residual row fits in hs");
   static_assert((2 * LSTAGES + 5) * 8 + 5 * 4 <= 256, "barrier area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -472,7 +608,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2)
           if (!ok) break;
           if (ready < 0) pdl_wait();   // phase 0's activations come from the previous kernel
           if (p > 0) {
-            if (!wait_passed(nbar_s, bars_before(a, p), abort_flag, a.err)) break;
+            if (!wait_passed(nbar_s, syncs_before(a, p), abort_flag, a.err)) break;
             fence_proxy_async_global();   // the consumer's generic stores, read by TMA below
           }
           ready = p;
@@ -540,12 +676,14 @@ __global__ void __launch_bounds__(kLayerThreads, 2)
     const int e = threadIdx.x - 64;
     const int row = (warp & 3) * 32 + lane;
     pdl_wait();
-    uint32_t gen0 = 0;
+    uint32_t gen0 = 0, tp_target = 0;
     if (e == 0) {
       gen0 = ld_acquire_gpu(epoch);   // published by the previous launch, which has ended
+      if (a.nranks > 0) tp_target = static_cast<uint32_t>(*a.epoch);
     }
     int seg = 0;
     uint32_t nbar = 0;   // grid barriers passed (thread 0)
+    uint32_t nsync = 0;  // synchronisation points passed (thread 0)
     bool dead = false;   // warp-uniform
     for (int p = 0; p < a.nphase; ++p) {
       const LayerPhase& ph = a.ph[p];
@@ -579,7 +717,23 @@ __global__ void __launch_bounds__(kLayerThreads, 2)
           epi_sync();
           swiglu_tile(a, ph, t, n, tb, row, e, *go_s && !dead, xs, hs);
         } else {
-          if (!dead) {
+          if (!dead && ph.consumer == kConsTpAddNorm) {
+            // push: batch row b's partial to its owner's receive area
+            float* const* dst = a.push[p == 0 ? 0 : 1];
+            for (int c0 = 0; c0 < LBN; c0 += 32) {
+              uint32_t r[32];
+              tmem_ld_x32(tb + c0, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) {
+                const int b = c0 + jj;
+                if (b < a.m) {
+                  const int q = b / a.rpr, bl = b - q * a.rpr;
+                  dst[q][sk_push_offset(ph.plan, a.rank, t, j, a.rpr, bl, row)] = __uint_as_float(r[jj]);
+                }
+              }
+            }
+          } else if (!dead) {
             float* part = ph.partials + (static_cast<int64_t>(t) * ph.plan.maxc + j) * LBN * LBM;
             for (int c0 = 0; c0 < LBN; c0 += 32) {
               uint32_t r[32];
@@ -609,18 +763,53 @@ __global__ void __launch_bounds__(kLayerThreads, 2)
         epi_sync();
         if (e == 0) {
           ++nbar;
+          ++nsync;
           if (!*abort_flag && !grid_barrier(count, gen0 + nbar * G, abort_flag, a.err)) *abort_flag = 1;
           if (cta == 0 && nbar == bars_before(a, a.nphase) && !*abort_flag)
             st_release_gpu(epoch, gen0 + nbar * G);   // every arrival of this launch is in
           if (!*abort_flag) {
             __threadfence_block();   // the acquire above, then the count the producer reads
-            *nbar_s = nbar;
+            *nbar_s = nsync;
           }
           *leave = *abort_flag;
         }
         epi_sync();
         return !*leave;
       };
+      // Tensor parallel, right after a grid barrier: CTA 0 signals point k to every rank (one
+      // system-scope release fence, cumulative over every CTA's stores that the barrier ordered
+      // before it, then a relaxed increment per rank); with `wait`, every CTA then waits for
+      // point k's signal from every rank.
+      auto xrank = [&](int k, bool wait) -> bool {
+        epi_sync();   // every thread has read the last decision before thread 0 writes the next
+        if (e == 0) {
+          if (cta == 0 && !*abort_flag) {
+            fence_acq_rel_sys();
+            for (int q = 0; q < a.nranks; ++q) signal_add_relaxed_sys(a.signal[k][q]);
+          }
+          if (wait && !*abort_flag) {
+            if (wait_ranks(a.wait[k], a.nranks, tp_target, abort_flag, a.err)) {
+              ++nsync;
+              __threadfence_block();
+              *nbar_s = nsync;
+            }
+          }
+          *leave = *abort_flag;
+        }
+        epi_sync();
+        return !*leave;
+      };
+      if (ph.consumer == kConsTpAddNorm) {
+        const int k0 = p == 0 ? 0 : 2;
+        if (!meet(false)) break;          // every CTA's pushes issued
+        if (!xrank(k0, true)) break;      // ... and every rank's arrived
+        if (p == 0 && e == 0) pdl_launch_dependents();
+        for (int bl = cta; bl < a.rpr; bl += G)
+          tp_add_norm_row(a, ph.plan, a.recv[p == 0 ? 0 : 1], a.norm_w[p == 0 ? 0 : 1], bl, e, red, hs);
+        if (!meet(true)) break;           // this rank's owned rows written into every rank's xn
+        if (!xrank(k0 + 1, p + 1 < a.nphase)) break;   // ... and every owner's (read by TMA next)
+        continue;
+      }
       if (!fix && !meet(false)) break;
       if (p == 0 && e == 0) pdl_launch_dependents();   // every CTA is resident: the next kernel may queue
       const int warp4 = warp - 2;
@@ -723,15 +912,23 @@ extern "C" int64_t mvb_decoder_layer_workspace_bytes(int64_t m, int64_t hidden, 
          (static_cast<int64_t>(plans[1].tiles) * plans[1].maxc * 4 + 255) / 256 * 256;
 }
 
-extern "C" int mvb_decoder_layer_tail(const void* attn, int64_t attn_stride, const void* wo, const void* ln2,
-                                      const void* wgu, const void* wdown, const void* ln_next, const void* wqkv_next,
-                                      const void* q_norm_next, const void* k_norm_next, void* residual, void* xn,
-                                      void* h, void* q_out, void* kv_cache, const void* cos, const void* sin,
-                                      int64_t table_len, const int32_t* positions, const int32_t* block_tables,
-                                      int64_t max_blocks, int64_t m, int64_t hidden, int64_t num_q_heads,
-                                      int64_t num_kv_heads, int64_t head_dim, int64_t inter, int64_t num_layers,
-                                      int64_t next_layer, int64_t num_blocks, int64_t block_size, float eps,
-                                      void* workspace, int64_t workspace_bytes, void* barrier, mvb_stream_t stream) {
+namespace {
+
+// Tensor-parallel arguments of a launch (null: one GPU).
+struct TpLayerCall {
+  mvb_tp_comm* comm;
+  int64_t recv_o, recv_down, xn;   // heap offsets
+  int layer;                       // signal points 4 * layer .. 4 * layer + 3
+};
+
+int layer_tail_impl(const TpLayerCall* tp, const void* attn, int64_t attn_stride, const void* wo, const void* ln2,
+                    const void* wgu, const void* wdown, const void* ln_next, const void* wqkv_next,
+                    const void* q_norm_next, const void* k_norm_next, void* residual, void* xn, void* h,
+                    void* q_out, void* kv_cache, const void* cos, const void* sin, int64_t table_len,
+                    const int32_t* positions, const int32_t* block_tables, int64_t max_blocks, int64_t m,
+                    int64_t hidden, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t inter,
+                    int64_t num_layers, int64_t next_layer, int64_t num_blocks, int64_t block_size, float eps,
+                    void* workspace, int64_t workspace_bytes, void* barrier, mvb_stream_t stream) {
   MVB_REQUIRE(attn && wo && ln2 && wgu && wdown && ln_next && residual && xn && h && workspace && barrier,
               "mvb_decoder_layer_tail: null pointer");
   MVB_REQUIRE(m > 0 && m <= LBN, "mvb_decoder_layer_tail: batch %lld must be in [1, %d]", (long long)m, LBN);
@@ -777,10 +974,45 @@ extern "C" int mvb_decoder_layer_tail(const void* attn, int64_t attn_stride, con
     a.ph[3].plan = splitk_plan_ctas(m, static_cast<int>(qkv_dim / LBM), hidden, G);
     a.ph[3].consumer = kConsQk;
   }
+  int points[4] = {0, 0, 0, 0};
+  if (tp) {
+    // row-parallel o_proj / down_proj: the push split of the per-kernel path (the receive areas
+    // are sized by mvb_tp_recv_bytes for it)
+    mvb_tp_comm* c = tp->comm;
+    const int nr = c->nranks;
+    MVB_REQUIRE(m % nr == 0, "mvb_tp_decoder_layer_tail: batch %lld not a multiple of %d ranks", (long long)m, nr);
+    a.nranks = nr;
+    a.rank = c->rank;
+    a.rpr = static_cast<int>(m / nr);
+    a.ph[0].plan = splitk_plan_push(m, hidden, q_dim, sms, nr);
+    a.ph[0].consumer = kConsTpAddNorm;
+    a.ph[2].plan = splitk_plan_push(m, hidden, inter, sms, nr);
+    a.ph[2].consumer = kConsTpAddNorm;
+    MVB_REQUIRE(a.ph[0].plan.grid <= G && a.ph[2].plan.grid <= G, "mvb_tp_decoder_layer_tail: push split");
+    const int64_t off[2] = {tp->recv_o, tp->recv_down};
+    for (int k = 0; k < 2; ++k) {
+      const int64_t bytes = splitk_push_bytes(a.ph[k == 0 ? 0 : 2].plan, nr, a.rpr);
+      MVB_REQUIRE(off[k] >= kTpSignalBytes && off[k] % 16 == 0 && off[k] + bytes <= c->heap_bytes,
+                  "mvb_tp_decoder_layer_tail: receive area outside the heap");
+      a.recv[k] = reinterpret_cast<const float*>(c->base[c->rank] + off[k]);
+      for (int q = 0; q < nr; ++q) a.push[k][q] = reinterpret_cast<float*>(c->base[q] + off[k]);
+    }
+    MVB_REQUIRE(tp->xn >= kTpSignalBytes && tp->xn % 16 == 0 && tp->xn + m * hidden * 2 <= c->heap_bytes,
+                "mvb_tp_decoder_layer_tail: xn outside the heap");
+    for (int q = 0; q < nr; ++q) a.xn_all[q] = reinterpret_cast<__nv_bfloat16*>(c->base[q] + tp->xn);
+    MVB_REQUIRE(tp->layer >= 0 && 4 * tp->layer + 3 < kTpMaxPoints, "mvb_tp_decoder_layer_tail: layer %d",
+                tp->layer);
+    for (int k = 0; k < 4; ++k) {
+      points[k] = 4 * tp->layer + k;
+      for (int q = 0; q < nr; ++q) a.signal[k][q] = c->signal_slot(q, points[k]);
+      a.wait[k] = c->wait_row(points[k]);
+    }
+    a.epoch = c->epoch;
+  }
   int64_t need = 0;
   for (int p = 0; p < a.nphase; ++p) {
     a.ph[p].partials = static_cast<float*>(workspace);
-    need = std::max(need, splitk_partials_bytes(a.ph[p].plan));
+    if (a.ph[p].consumer != kConsTpAddNorm) need = std::max(need, splitk_partials_bytes(a.ph[p].plan));
   }
   const int64_t ss_off = (need + 255) / 256 * 256;
   const int64_t flags_off = ss_off + (m * kNormChunks * 4 + 255) / 256 * 256;
@@ -825,6 +1057,47 @@ extern "C" int mvb_decoder_layer_tail(const void* attn, int64_t attn_stride, con
   a.bar = static_cast<unsigned*>(barrier);
   a.err = device_status_ptr();
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  return launch("decoder_layer_tail", layer_kernel, dim3(static_cast<unsigned>(G)), dim3(kLayerThreads), layer_smem(),
-                st, maps, a);
+  MVB_TRY(launch(tp ? "tp_decoder_layer_tail" : "decoder_layer_tail", layer_kernel, dim3(static_cast<unsigned>(G)),
+                 dim3(kLayerThreads), layer_smem(), st, maps, a));
+  if (tp)
+    for (int k = 0; k < 4; ++k) tp->comm->point_count[points[k]] = 1;   // one signal per rank per step
+  return MVB_OK;
+}
+
+}  // namespace
+
+extern "C" int mvb_decoder_layer_tail(const void* attn, int64_t attn_stride, const void* wo, const void* ln2,
+                                      const void* wgu, const void* wdown, const void* ln_next, const void* wqkv_next,
+                                      const void* q_norm_next, const void* k_norm_next, void* residual, void* xn,
+                                      void* h, void* q_out, void* kv_cache, const void* cos, const void* sin,
+                                      int64_t table_len, const int32_t* positions, const int32_t* block_tables,
+                                      int64_t max_blocks, int64_t m, int64_t hidden, int64_t num_q_heads,
+                                      int64_t num_kv_heads, int64_t head_dim, int64_t inter, int64_t num_layers,
+                                      int64_t next_layer, int64_t num_blocks, int64_t block_size, float eps,
+                                      void* workspace, int64_t workspace_bytes, void* barrier, mvb_stream_t stream) {
+  return layer_tail_impl(nullptr, attn, attn_stride, wo, ln2, wgu, wdown, ln_next, wqkv_next, q_norm_next,
+                         k_norm_next, residual, xn, h, q_out, kv_cache, cos, sin, table_len, positions, block_tables,
+                         max_blocks, m, hidden, num_q_heads, num_kv_heads, head_dim, inter, num_layers, next_layer,
+                         num_blocks, block_size, eps, workspace, workspace_bytes, barrier, stream);
+}
+
+extern "C" int mvb_tp_decoder_layer_tail(mvb_tp_comm* comm, int layer, const void* attn, int64_t attn_stride,
+                                         const void* wo, const void* ln2, const void* wgu, const void* wdown,
+                                         const void* ln_next, const void* wqkv_next, const void* q_norm_next,
+                                         const void* k_norm_next, void* residual, int64_t xn_offset, void* h,
+                                         void* q_out, void* kv_cache, const void* cos, const void* sin,
+                                         int64_t table_len, const int32_t* positions, const int32_t* block_tables,
+                                         int64_t max_blocks, int64_t m, int64_t hidden, int64_t num_q_heads,
+                                         int64_t num_kv_heads, int64_t head_dim, int64_t inter, int64_t num_layers,
+                                         int64_t next_layer, int64_t num_blocks, int64_t block_size, float eps,
+                                         int64_t recv_o_offset, int64_t recv_down_offset, void* workspace,
+                                         int64_t workspace_bytes, void* barrier, mvb_stream_t stream) {
+  MVB_REQUIRE(comm, "mvb_tp_decoder_layer_tail: null communicator");
+  MVB_REQUIRE(xn_offset >= 0 && xn_offset < comm->heap_bytes, "mvb_tp_decoder_layer_tail: xn offset");
+  const TpLayerCall tp{comm, recv_o_offset, recv_down_offset, xn_offset, layer};
+  return layer_tail_impl(&tp, attn, attn_stride, wo, ln2, wgu, wdown, ln_next, wqkv_next, q_norm_next, k_norm_next,
+                         residual, comm->base[comm->rank] + xn_offset, h, q_out, kv_cache, cos, sin, table_len,
+                         positions, block_tables, max_blocks, m, hidden, num_q_heads, num_kv_heads, head_dim, inter,
+                         num_layers, next_layer, num_blocks, block_size, eps, workspace, workspace_bytes, barrier,
+                         stream);
 }

@@ -261,11 +261,11 @@ class DecodeRunner:
         self.attn_ws = torch.zeros(attn_ws, dtype=torch.uint8, device=dev)
         self.graph: torch.cuda.CUDAGraph | None = None
         self.graph_stream: torch.cuda.Stream | None = None
-        eligible = (not self.gemma and not self.moe and not self.tp.enabled and B <= 64 and self.D == 128 and
-                    H % 64 == 0 and H <= 4096 and self.I % 64 == 0 and not cfg.get("_rms_norm_plus_one"))
+        eligible = (not self.gemma and not self.moe and B <= 64 and self.D == 128 and H % 64 == 0 and H <= 4096 and
+                    self.I % 64 == 0 and not cfg.get("_rms_norm_plus_one"))
         if fused_layers and not eligible:
-            raise ValueError("the fused layer kernel needs a dense one-GPU model, batch <= 64, head dim 128, "
-                             "hidden <= 4096")
+            raise ValueError("the fused layer kernel needs a dense model, batch <= 64, head dim 128, hidden <= 4096 "
+                             "and a per-rank intermediate size that is a multiple of 64")
         self.fused = bool(fused_layers)
         if self.fused:
             lib = N.lib()
@@ -525,10 +525,29 @@ class DecodeRunner:
                                                       weight.data_ptr(), self.eps, self.plus_one, recv, wait,
                                                       self.layout.xn, signal, self._st), "tp_fused_add_rmsnorm_gemm")
 
+    def _tp_layer_tail(self, i) -> None:
+        """Tensor parallel: layer i after its attention and the next layer's projection as one
+        launch (``mvb_tp_decoder_layer_tail``), the exchanges of the row-parallel o_proj and
+        down_proj inside it (signal points 4i .. 4i + 3, as the per-kernel step uses them)."""
+        w, B, H, D = self.w, self.B, self.H, self.D
+        nxt = i + 1 < self.L
+        cos, sin = self.layer_tables[i + 1] if nxt else self.layer_tables[i]
+        N.check(N.lib().mvb_tp_decoder_layer_tail(
+            self.heap.comm, i, self.attn.data_ptr(), self.attn.stride(0), w.wo[i].data_ptr(), w.ln2[i].data_ptr(),
+            w.wgu[i].data_ptr(), w.wdown[i].data_ptr(), (w.ln1[i + 1] if nxt else w.final_norm).data_ptr(),
+            w.wqkv[i + 1].data_ptr() if nxt else None,
+            w.qn[i + 1].data_ptr() if nxt and w.qk_norm else None, w.kn[i + 1].data_ptr() if nxt and w.qk_norm else None,
+            self.residual.data_ptr(), self.layout.xn, self.h.data_ptr(), self.q.data_ptr(), self.kv.kv_cache.data_ptr(),
+            cos.data_ptr(), sin.data_ptr(), cos.shape[0], self.pos.data_ptr(), self.block_tables.data_ptr(),
+            self.max_blocks, B, H, self.Hq, self.Hkv, D, self.I, self.L, i + 1 if nxt else 0, self.P,
+            self.kv.block_size, self.eps, self.layout.recv_o, self.layout.recv_down, self.layer_ws.data_ptr(),
+            self.layer_ws.numel(), self.layer_bar.data_ptr(), self._st), "tp_decoder_layer_tail")
+
     def _forward_tp(self) -> None:
         """The step on one rank of a tensor-parallel group (see tensor_parallel): same kernels,
         local head / feature counts, and the cross-GPU exchanges inside the row-parallel GEMMs,
-        the add+norm kernels, the lm_head GEMM and one wait before sampling."""
+        the add+norm kernels, the lm_head GEMM and one wait before sampling.  With fused layers,
+        one launch per layer after its attention holds the layer's exchanges."""
         lib, w, B, H, D = N.lib(), self.w, self.B, self.H, self.D
         self._st = N.stream_handle(self.dev)
         st, eps, bf, lay = self._st, self.eps, N.BF16, self.layout
@@ -536,6 +555,30 @@ class DecodeRunner:
         ws = self.gemm_ws.data_ptr()
         N.check(lib.mvb_tp_begin_step(comm, st), "tp_begin_step")
         self._embed()
+        if self.fused:
+            self._tp_gemm(self.xn, w.wqkv[0], N.EPI_PARTIALS)
+            self._qk(0)
+            for i in range(self.L):
+                self._attention(i)
+                self._tp_layer_tail(i)   # the last one applies the final norm
+        else:
+            self._tp_layers()
+        last = self.L - 1
+        # vocab-parallel lm_head: this rank's columns into every rank's full logits
+        self._tp_gemm(self.xn, w.lm_head, N.EPI_STORE, out_offset=lay.logits + self.tp.rank * self.Vl * 2,
+                      ldy=self.V, wait=tpm.point_mlp_norm(last), signal=tpm.point_logits(self.L))
+        N.check(lib.mvb_tp_wait(comm, tpm.point_logits(self.L), st), "tp_wait")
+        if self.final_softcap:   # every rank soft-caps its copy of the gathered logits
+            N.check(lib.mvb_softcap(self.logits.data_ptr(), B * self.V, self.final_softcap, N.BF16, st), "softcap")
+        N.check(lib.mvb_sample(self.tokens.data_ptr(), N.ptr(self.probs), self.logits.data_ptr(), B, self.V, self.V,
+                               self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
+                               0, self.offset.data_ptr(), bf, st), "sample")
+
+    def _tp_layers(self) -> None:
+        """The per-kernel tensor-parallel layers, through the final norm."""
+        lib, w, B, H, D = N.lib(), self.w, self.B, self.H, self.D
+        st, lay = self._st, self.layout
+        ws = self.gemm_ws.data_ptr()
         g = self.gemma   # Gemma: post-norms of the attention and MLP outputs before each residual add
         for i in range(self.L):
             if i > 0:
@@ -554,15 +597,6 @@ class DecodeRunner:
         last = self.L - 1
         self._tp_add_norm(self.I, w.final_norm, lay.recv_down, tpm.point_down(last), tpm.point_mlp_norm(last),
                           post=w.post_ff[last] if g else None)
-        # vocab-parallel lm_head: this rank's columns into every rank's full logits
-        self._tp_gemm(self.xn, w.lm_head, N.EPI_STORE, out_offset=lay.logits + self.tp.rank * self.Vl * 2,
-                      ldy=self.V, wait=tpm.point_mlp_norm(last), signal=tpm.point_logits(self.L))
-        N.check(lib.mvb_tp_wait(comm, tpm.point_logits(self.L), st), "tp_wait")
-        if self.final_softcap:   # every rank soft-caps its copy of the gathered logits
-            N.check(lib.mvb_softcap(self.logits.data_ptr(), B * self.V, self.final_softcap, N.BF16, st), "softcap")
-        N.check(lib.mvb_sample(self.tokens.data_ptr(), N.ptr(self.probs), self.logits.data_ptr(), B, self.V, self.V,
-                               self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
-                               0, self.offset.data_ptr(), bf, st), "sample")
 
     def kernel_kinds(self) -> dict:
         """kind -> (launch(layer), launches per step, algorithmic bytes per launch, flops per launch)."""
@@ -675,7 +709,8 @@ class DecodeRunner:
         if self.moe:   # 11 per layer: qkv, qk, attention, o_proj, add+norm, router, route, gather, 2 GEMMs, combine
             return 2 + self.L * 11 + (self.L - 1) + 3
         if self.fused:   # embedding, rmsnorm, qkv, qk, then attention + fused tail per layer, lm_head, sample
-            return 4 + 2 * self.L + 2
+            # (tensor parallel: + the step-counter kernel and the wait before sampling)
+            return 4 + 2 * self.L + 2 + (2 + (1 if self.final_softcap else 0) if self.tp.enabled else 0)
         if self.tp.enabled:   # + the step-counter kernel and the wait before sampling
             return 2 + self.L * 8 + (self.L - 1) + 3 + 2 + (1 if self.final_softcap else 0)
         return 2 + self.L * 8 + (self.L - 1) + 3 + (1 if self.final_softcap else 0)

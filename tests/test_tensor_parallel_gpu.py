@@ -37,7 +37,7 @@ pytestmark = pytest.mark.gpu
 REPO = Path(__file__).resolve().parent.parent
 
 
-def _engine(cfg, sd, tp, batch, lens, num_blocks, fused_layers=None):
+def _engine(cfg, sd, tp, batch, lens, num_blocks, fused_layers=False):
     order = list(range(num_blocks))
     random.Random(0).shuffle(order)
     eng = DecodeEngine(cfg, sd, max_batch=batch, max_model_len=max(lens) + 64, num_blocks=num_blocks,
@@ -103,14 +103,49 @@ def test_wait_for_a_missing_signal_times_out_with_status():
         heap.close()
 
 
+def test_fused_layer_exchange_path_on_one_gpu_matches_per_kernel_exchange_path():
+    """The tensor-parallel step with one launch per layer tail (mvb_tp_decoder_layer_tail: pushes,
+    owner add+norm, all-gather and the signal points inside the launch), one rank, against the
+    per-kernel exchange step: same partial sums and summation order, the owner's sum of squares
+    in another order (bf16 rounding of the normalised rows), greedy tokens equal wherever the
+    margin is not a near tie, and the residual stream close."""
+    cfg = get_config("qwen3-8b", num_hidden_layers=2)
+    sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device="cuda")
+    batch, lens = 16, [40 + 31 * i for i in range(16)]
+    plain = _engine(cfg, sd, TensorParallelConfig(1, 0, exchange=True), batch, lens, 512, fused_layers=False)
+    fused = _engine(cfg, sd, TensorParallelConfig(1, 0, exchange=True), batch, lens, 512, fused_layers=True)
+    assert fused.runner.fused and not plain.runner.fused
+    del sd
+    N.device_status(clear=True)
+    for e in (plain, fused):
+        e.set_sampling(0.0, -1, 1.0)
+    for step in range(4):
+        a = plain.step(use_graph=step > 0)
+        b = fused.step(use_graph=step > 0)
+        la, lb = plain.runner.logits[:batch].float(), fused.runner.logits[:batch].float()
+        d = (la - lb).abs()
+        assert float(d.max()) <= 0.02 * float(la.abs().max()) + 1e-3, (step, float(d.max()))
+        assert float(d.mean()) <= 2e-3 * float(la.abs().mean()) + 1e-4, (step, float(d.mean()))
+        top2 = la.topk(2, dim=-1).values
+        for r in range(batch):
+            if float(top2[r, 0] - top2[r, 1]) > 2 * float(d[r].max()):
+                assert a[r] == b[r], (step, r)
+        rd = (plain.runner.residual.float() - fused.runner.residual.float()).abs()
+        assert float(rd.max()) <= 0.02 * float(plain.runner.residual.float().abs().max()) + 1e-2
+        fused.force_last_tokens(a)
+    assert N.device_status(clear=True) == 0
+    plain.runner.close()
+    fused.runner.close()
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("arch", ["qwen3-8b", "gemma2-9b"])
-def test_tp2_matches_tp1_teacher_forced(tmp_path, arch):
+@pytest.mark.parametrize("arch,fused", [("qwen3-8b", False), ("gemma2-9b", False), ("qwen3-8b", True)])
+def test_tp2_matches_tp1_teacher_forced(tmp_path, arch, fused):
     out = tmp_path / "tp2.json"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533", str(REPO / "tests" / "tp_worker.py"),
-           "--out", str(out), "--steps", "4", "--arch", arch]
+           "--out", str(out), "--steps", "4", "--arch", arch] + (["--fused"] if fused else [])
     r = subprocess.run(cmd, env=env, cwd=REPO, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     rep = json.loads(out.read_text())

@@ -2,8 +2,8 @@
 torch.distributed.run, one process per GPU).
 
 Every rank builds the same 2-layer model (Qwen3-8B or, with --arch gemma2-9b, Gemma-2-9B layer
-dims) and the same batch of sequences
-on a shuffled block pool, and decodes with the tensor-parallel engine.  Rank 0 also decodes the
+dims) and the same batch of sequences on a shuffled block pool, and decodes with the
+tensor-parallel engine (with --fused, its one-launch-per-layer-tail step).  Rank 0 also decodes the
 same workload on one GPU (TP=1) and compares, step by step under teacher forcing, the full
 logits and the greedy tokens; it writes a JSON report to --out.
 """
@@ -29,12 +29,12 @@ from llm_pytorch_inference_b200.tensor_parallel import TensorParallelConfig  # n
 from llm_pytorch_inference_b200.weights import canonical_state_dict  # noqa: E402
 
 
-def build(cfg, tp, dev, batch, lens, num_blocks):
+def build(cfg, tp, dev, batch, lens, num_blocks, fused=False):
     sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev)
     order = list(range(num_blocks))
     random.Random(0).shuffle(order)
     eng = DecodeEngine(cfg, sd, max_batch=batch, max_model_len=max(lens) + 64, num_blocks=num_blocks, device=dev,
-                       free_order=order, tp=tp)
+                       free_order=order, tp=tp, fused_layers=fused)
     del sd
     g = torch.Generator().manual_seed(1)
     for s, n in enumerate(lens):
@@ -58,6 +58,7 @@ def main() -> int:
     ap.add_argument("--out", required=True)
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--arch", default="qwen3-8b", choices=["qwen3-8b", "gemma2-9b"])
+    ap.add_argument("--fused", action="store_true", help="the tensor-parallel step with one launch per layer tail")
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -69,7 +70,7 @@ def main() -> int:
     batch = 16
     lens = [37 + 29 * i for i in range(batch)]          # ragged contexts, blocks cross boundaries
     num_blocks = 512
-    eng = build(cfg, TensorParallelConfig(world, rank), dev, batch, lens, num_blocks)
+    eng = build(cfg, TensorParallelConfig(world, rank), dev, batch, lens, num_blocks, fused=args.fused)
     ref = None
     if rank == 0:
         ref = build(cfg, TensorParallelConfig(1, 0), dev, batch, lens, num_blocks)
