@@ -58,14 +58,16 @@ def parse_args(argv=None):
     ap.add_argument("--pdl", type=int, default=1)
     ap.add_argument("--fused-layers", type=int, default=0,
                     help="1: one persistent launch per layer tail (mvb_decoder_layer_tail / its tensor-parallel form)")
-    ap.add_argument("--case", default=None, choices=["kernels", "moe", "gemma2", "llama3", "prefill", "prefill-kernels"],
+    ap.add_argument("--case", default=None, choices=["kernels", "moe", "gemma2", "llama3", "prefill", "prefill-kernels",
+                                                     "reference-gpu"],
                     help="kernels: small profiling case (2 layers of the workload's dims), each kernel kind "
                          "launched a few times; prints per-kernel timings only.  moe: the sparse-MoE decode "
                          "workload (Qwen3-30B-A3B arch, batch 32, prompt 4096, greedy), 1 GPU.  gemma2: the "
                          "Gemma-2-9B-arch decode workload (batch 16, prompt 8192, greedy), 1 GPU.  prefill: "
                          "batched prefill of the headline's 64 x 2048-token prompts (Qwen3-8B arch), 1 GPU.  "
                          "prefill-kernels: small profiling case of the prefill (2 layers at Qwen3-8B dims, "
-                         "8 x 2048-token prompts, ~5 GB on the device)")
+                         "8 x 2048-token prompts, ~5 GB on the device).  reference-gpu (with --impl reference): "
+                         "the secondary baseline, the reference's PyTorch decode step and GPU sampling on cuda:0")
     ap.add_argument("--arch", default=None, choices=["qwen3-8b", "gemma2-9b"],
                     help="--case kernels: the layer dims (qwen3-8b: batch 64, prompt 2048; gemma2-9b: batch 16, "
                          "prompt 8192)")
@@ -276,6 +278,95 @@ def run_reference(args, rank: int, world: int) -> None:
                        "parallelism": "cpu"},
             "cpu_baseline": {k: last[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_gpu(args) -> None:
+    """Secondary baseline: the reference's own GPU path on this B200, restated by the oracle --
+    the PyTorch decode step of models/model.py as engine.py:339-349 runs it (bf16 autocast, cuBLAS
+    projections, SDPA over the pages gathered through the block tables) on the headline workload
+    (36 layers, batch 64, 2048-token contexts, zero-filled KV pages: the values do not change the
+    work), and the reference's GPU sampling (sampler.py:40-48 filter + ops/sampling.py:69-73
+    tempered softmax, torch.multinomial draw) against mvb_sample on the same bf16 logits.  The
+    reference's CUDA extension needs libtorch's ATen headers and libraries to build, so it is not
+    built here; its sampling kernel is the path this replaces."""
+    from llm_pytorch_inference_b200 import ops
+    from llm_pytorch_inference_b200.configs import get_config
+    from llm_pytorch_inference_b200.weights import canonical_state_dict
+    from oracle import sampling as osamp
+    from oracle.engine import OracleEngine
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = get_config(ARCH)
+    sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev)
+    K = max(1, min(args.steps, 3))
+    per_seq = (PROMPT + 1 + 2 + K + 15) // 16 + 1
+    blocks = BATCH * per_seq + 8
+    order = list(range(blocks))
+    random.Random(0).shuffle(order)
+    o = OracleEngine(cfg, sd, torch.bfloat16, blocks, 16, order, device=dev)
+    g = torch.Generator().manual_seed(1)
+    for s in range(BATCH):
+        prompt = torch.randint(0, cfg["vocab_size"], (PROMPT,), generator=g).tolist()
+        assert o.blocks.allocate(s, PROMPT + 1) is not None
+        o.tokens[s] = prompt + [int(torch.randint(0, cfg["vocab_size"], (1,), generator=g))]
+        o.prompt_len[s] = PROMPT
+    seqs = list(range(BATCH))
+    T, top_k, top_p = SAMPLING
+    gen = torch.Generator(device=dev).manual_seed(1234)
+
+    def step():
+        logits = o.decode(seqs)
+        probs = osamp.gpu_semantics_probs(logits, T, top_k, top_p)
+        toks = torch.multinomial(probs, 1, generator=gen).view(-1).tolist()
+        for s, t in zip(seqs, toks):
+            o.append(s, t)
+        return logits
+
+    logits = step()   # warm-up
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    for _ in range(K):
+        logits = step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    step_ms = e0.elapsed_time(e1) / K
+    wall_ms = (time.perf_counter() - t0) * 1e3 / K
+
+    # sampling alone, on the last step's logits (bf16, as the model emits them)
+    lb = logits.to(torch.bfloat16)
+
+    def timed(fn, iters=20):
+        fn()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(iters):
+            fn()
+        b.record()
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) / iters * 1e3
+
+    ref_us = timed(lambda: torch.multinomial(osamp.gpu_semantics_probs(lb.float(), T, top_k, top_p), 1,
+                                             generator=gen))
+    out = torch.empty(BATCH, dtype=torch.int64, device=dev)
+    ours_us = timed(lambda: ops.sample(lb, T, top_k, top_p, 1234, 0, out=out))
+    v = BATCH / (step_ms * 1e-3)
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 2), "unit": "tokens/s", "n_gpus": 1,
+            "steps": K, "warmup": 1, "ms_per_step": round(step_ms, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{ARCH} decode, batch {BATCH}, prompt {PROMPT}, T/top-k/top-p "
+                                   f"{SAMPLING[0]}/{SAMPLING[1]}/{SAMPLING[2]}",
+                       "model": ARCH, "layers": cfg["num_hidden_layers"], "global_batch": BATCH, "seq_len": PROMPT,
+                       "parallelism": "tp1", "path": "reference PyTorch path (oracle restatement) on cuda:0"},
+            "secondary_baseline": {"decode_step_ms": round(step_ms, 3), "decode_step_wall_ms": round(wall_ms, 3),
+                                   "sampling_reference_us": round(ref_us, 2), "sampling_mvb_sample_us": round(ours_us, 2),
+                                   "sampling_rows": BATCH, "vocab": int(lb.shape[-1])},
+            "e2e": {"value": round(BATCH / (wall_ms * 1e-3), 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": BATCH * 8}}
     print(json.dumps(line), flush=True)
 
 
@@ -808,6 +899,11 @@ def main(argv=None) -> int:
         return 0
     if args.case == "moe":
         run_moe_case(args)
+        return 0
+    if args.case == "reference-gpu":
+        if args.impl != "reference":
+            raise SystemExit("--case reference-gpu times the reference's path: pass --impl reference")
+        run_reference_gpu(args)
         return 0
     rank, world, local = (0, 1, 0)
     if args.impl == "reference":
