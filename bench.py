@@ -534,20 +534,24 @@ def run_kernel_case(args) -> None:
 def run_moe_case(args) -> None:
     """Sparse-MoE decode (Qwen3-30B-A3B architecture: 48 layers, hidden 2048, 32/4 heads, 128
     experts of 768, top-8), batch 32, 4096-token prompts with seeded synthetic K/V, greedy.  Same
-    timing rules as the headline line (CUDA events over K graph replays, inputs far above L2)."""
+    timing rules as the headline line (CUDA events over K graph replays, inputs far above L2).
+    Under torchrun with N GPUs: attention split by heads and the experts split whole over the
+    ranks (expert parallel), one group over the same batch (strong scaling), max over ranks."""
     from llm_pytorch_inference_b200 import _native as N
     from llm_pytorch_inference_b200.configs import get_config
     from llm_pytorch_inference_b200.engine import DecodeEngine
+    from llm_pytorch_inference_b200.tensor_parallel import TensorParallelConfig
     from llm_pytorch_inference_b200.weights import canonical_state_dict
 
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
     N.set_pdl(bool(args.pdl))
     cfg = get_config("qwen3-30b-a3b")
     B, prompt = 32, 4096
     W, K = args.warmup, args.steps
     sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev, stacked_experts=True)
-    eng = DecodeEngine(cfg, sd, max_batch=B, max_model_len=prompt + 2 * (W + 2 * K) + 32, device=dev)
+    eng = DecodeEngine(cfg, sd, max_batch=B, max_model_len=prompt + 2 * (W + 2 * K) + 32, device=dev,
+                       tp=TensorParallelConfig(world, rank))
     del sd
     order = list(range(eng.kv.num_blocks))
     random.Random(0).shuffle(order)
@@ -558,7 +562,7 @@ def run_moe_case(args) -> None:
     for s in range(B):
         eng.add_sequence(s, torch.randint(0, cfg["vocab_size"], (prompt,), generator=g).tolist())
         eng.append_first_token(s, int(torch.randint(0, cfg["vocab_size"], (1,), generator=g)))
-    eng.prefill_synthetic(seed=0)
+    eng.prefill_synthetic(seed=rank)   # each rank fills its own KV heads
     eng.set_sampling(0.0, -1, 1.0)
     eng.prepare_first_step()
     r = eng.runner
@@ -567,8 +571,10 @@ def run_moe_case(args) -> None:
         eng.step()
     torch.cuda.synchronize(dev)
     metas = torch.stack([eng.plan_step(eng.runner.tokens_host[:B].tolist()) for _ in range(K)]).to(dev)
-    clocks = ClockSampler(0)
+    clocks = ClockSampler(local)
     clocks.start()
+    barrier(world)
+    torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for k in range(K):
@@ -576,18 +582,21 @@ def run_moe_case(args) -> None:
         r.replay()
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1) / K
+    ms = max_over_ranks(e0.elapsed_time(e1) / K, world)
+    barrier(world)
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
     for _ in range(K):
         eng.step()
     e3.record(stream)
     torch.cuda.synchronize(dev)
-    e2e_ms = e2.elapsed_time(e3) / K
+    e2e_ms = max_over_ranks(e2.elapsed_time(e3) / K, world)
     clk = clocks.stop()
-    # algorithmic bytes: attention/norm/lm_head weights, the experts the step's routing touched in
-    # each layer (counted on the device after the last step), K/V of every attended token
-    act = int(r.active[0])
+    # algorithmic bytes per GPU: attention/norm/lm_head weights, the rank's experts the step's
+    # routing touched in each layer (counted on the device after the last step), K/V of every
+    # attended token of the rank's KV heads
+    ids = r.active[1:1 + int(r.active[0])].tolist()
+    act = sum(1 for e in ids if r.e_first <= e < r.e_first + r.e_local)
     L, H, E, Im = cfg["num_hidden_layers"], cfg["hidden_size"], cfg["num_experts"], cfg["moe_intermediate_size"]
     w = r.w
     dense = sum(t.numel() * 2 for t in [w.final_norm, w.lm_head, *w.wqkv, *w.wo, *w.ln1, *w.ln2, *w.qn, *w.kn,
@@ -596,14 +605,26 @@ def run_moe_case(args) -> None:
     kv_token = L * r.Hkv * r.D * 2 * 2
     step_bytes = dense + L * act * expert_bytes + int(r.ctx.cpu().sum()) * kv_token
     pk = peaks()
+    status = N.device_status(clear=True)
+    statuses = [status]
+    if world > 1:
+        import torch.distributed as dist
+
+        statuses = [None] * world
+        dist.all_gather_object(statuses, status)
+        r.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
     line = {"case": "moe", "metric": "decode tokens/s Qwen3-30B-A3B-arch bf16 batch 32 ctx 4096 greedy",
-            "value": round(B / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 4), "steps": K,
-            "warmup": W, "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tokens/s"},
-            "active_experts_last_layer": act, "step_bytes": step_bytes,
+            "value": round(B / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world, "ms_per_step": round(ms, 4),
+            "steps": K, "warmup": W, "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tokens/s"},
+            "parallelism": f"tp{world} (attention heads) / ep{world} (experts)" if world > 1 else "1 GPU",
+            "active_experts_last_layer_this_gpu": act, "step_bytes_per_gpu": step_bytes,
             "step_roofline": {"achieved_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),
                               "frac": round(step_bytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)},
-            "launches_per_step": r.launches_per_step(), "clocks": clk,
-            "device_status": N.device_status(clear=True)}
+            "launches_per_step": r.launches_per_step(), "clocks": clk, "device_status": statuses}
     print(json.dumps(line), flush=True)
 
 

@@ -355,6 +355,13 @@ int mvb_moe_gather(void* out, const void* x, int64_t hidden, const int32_t* row_
 int mvb_moe_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t n_per_expert,
                       int64_t k, int64_t num_experts, int64_t nrows, int64_t max_rows_per_expert, int epilogue,
                       const int32_t* expert_off, const int32_t* active, mvb_stream_t stream);
+/* Expert-parallel form: w holds only experts first_expert .. first_expert + local_experts - 1
+ * ([local_experts, n_per_expert, k]); the routing (expert_off, active) still covers all
+ * num_experts, and only the dispatched rows of the local experts are computed and stored. */
+int mvb_moe_gemm_bf16_experts(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t n_per_expert,
+                              int64_t k, int64_t num_experts, int64_t first_expert, int64_t local_experts,
+                              int64_t nrows, int64_t max_rows_per_expert, int epilogue, const int32_t* expert_off,
+                              const int32_t* active, mvb_stream_t stream);
 /* out[row] = the reference's accumulation of the row's expert outputs y[pair_row] (bf16 rows of
  * `hidden`): experts in ascending index, acc = bf16(acc + w * y) from acc = 0. */
 int mvb_moe_combine(void* out, const void* y, const float* topk_w, const int32_t* topk_ids, const int32_t* pair_row,
@@ -410,6 +417,18 @@ int mvb_tp_decoder_layer_tail(mvb_tp_comm* comm, int layer, const void* attn, in
                               int64_t num_layers, int64_t next_layer, int64_t num_blocks, int64_t block_size,
                               float eps, int64_t recv_o_offset, int64_t recv_down_offset, void* workspace,
                               int64_t workspace_bytes, void* barrier, mvb_stream_t stream);
+
+/* Expert parallelism of the sparse MoE block over the group (Qwen3MoeSparseMoe.forward,
+ * models/qwen3_moe_model.py:39-65, with its experts split evenly over the ranks): each rank
+ * combines the slots of its experts first_expert .. first_expert + local_experts - 1 for every
+ * row (as mvb_moe_combine, ascending expert index, acc = bf16(acc + w * y)) and pushes the fp32
+ * partial into the receive area (heap offset recv_offset, mvb_tp_recv_bytes(rows, hidden, 64,
+ * nranks) bytes) of the rank that owns the row; then signals `signal_point` once per rank.  The
+ * owner's mvb_tp_fused_add_rmsnorm_gemm with gemm_k = 64 adds the ranks' partials.
+ * rows % nranks == 0, hidden % 128 == 0. */
+int mvb_tp_moe_combine(mvb_tp_comm* comm, const void* y, const float* topk_w, const int32_t* topk_ids,
+                       const int32_t* pair_row, int64_t rows, int64_t top_k, int64_t hidden, int64_t first_expert,
+                       int64_t local_experts, int64_t recv_offset, int signal_point, mvb_stream_t stream);
 /* Bytes of the receive area of a row-parallel (push) GEMM of shape [m, n, k_local]. */
 int64_t mvb_tp_recv_bytes(int64_t m, int64_t n, int64_t k, int nranks, int device);
 /* The tcgen05 GEMM of mvb_gemm_bf16 with the exchanges of a tensor-parallel step:

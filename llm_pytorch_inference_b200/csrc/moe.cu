@@ -18,8 +18,17 @@
 //    are the UMMA N operand (swap-AB, as in the dense decode GEMM).  SWIGLU epilogue for
 //    gate/up, plain store for down.
 //  * mvb_moe_combine: per token, its experts in ascending index, acc = bf16(acc + w * out).
+//
+// Expert parallelism across the GPUs of a tensor-parallel group: every rank routes all tokens
+// (the same router weights and the all-gathered activations give the same routing everywhere),
+// runs the grouped GEMMs over its own experts only (mvb_moe_gemm_bf16_experts), and
+// mvb_tp_moe_combine sums each token's slots on its experts and pushes the partial sum to the rank
+// that owns the token's row, whose add+norm (mvb_tp_fused_add_rmsnorm_gemm) adds the ranks'
+// partials.  No activation rows cross GPUs before the experts.
 #include "common.cuh"
 #include "host.h"
+#include "splitk.cuh"
+#include "tp.cuh"
 
 namespace mvb {
 namespace {
@@ -42,8 +51,29 @@ struct MoeGemmArgs {
   int swiglu;
   const int32_t* expert_off;  // [E + 1] first dispatched row of each expert
   const int32_t* active;      // [1 + E]: count, then the active experts ascending
+  int first_expert;           // expert parallel: this GPU holds experts first_expert ..
+  int local_experts;          //   first_expert + local_experts - 1 (weights indexed from first_expert)
   unsigned* err;
 };
+
+// Index range [i0, i1) of the ascending active list (active[1 .. n]) holding the experts
+// first .. first + count - 1 (binary searches: the list is sorted).
+__device__ __forceinline__ void local_active_range(const int32_t* active, int n, int first, int count, int& i0,
+                                                   int& i1) {
+  auto lower = [&](int v) {
+    int lo = 0, hi = n;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (active[1 + mid] < v)
+        lo = mid + 1;
+      else
+        hi = mid;
+    }
+    return lo;
+  };
+  i0 = lower(first);
+  i1 = lower(first + count);
+}
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
@@ -95,8 +125,9 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
   const uint32_t tmem_base = *tmem_slot;
   if (threadIdx.x == 0) pdl_launch_dependents();
   pdl_wait();  // the routing (active experts, dispatch offsets) and x come from earlier kernels
-  const int n_active = a.active[0];
-  const int total = n_active * a.tiles_pe;
+  int i0 = 0, i1 = 0;
+  local_active_range(a.active, a.active[0], a.first_expert, a.local_experts, i0, i1);
+  const int total = (i1 - i0) * a.tiles_pe;
   const int G = gridDim.x;
 
   int issued = 0;
@@ -109,10 +140,10 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
       int it = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < total; u += G) {
-        const int e = a.active[1 + u / a.tiles_pe];
+        const int e = a.active[1 + i0 + u / a.tiles_pe];
         const int t = u % a.tiles_pe;
         const int xrow = a.expert_off[e];
-        const int wrow = e * a.rows_per_expert;
+        const int wrow = (e - a.first_expert) * a.rows_per_expert;
         for (int kb = 0; kb < a.kblocks; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -167,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, BN == 64 ? 2 : 1)
     const int row = q * 32 + lane;
     int seg = 0;
     for (int u = blockIdx.x; u < total; u += G, ++seg) {
-      const int e = a.active[1 + u / a.tiles_pe];
+      const int e = a.active[1 + i0 + u / a.tiles_pe];
       const int t = u % a.tiles_pe;
       const int xrow = a.expert_off[e];
       const int n_e = a.expert_off[e + 1] - xrow;  // dispatched rows of this expert (<= BN)
@@ -409,6 +440,61 @@ __global__ void moe_combine_kernel(__nv_bfloat16* __restrict__ out, const __nv_b
   }
 }
 
+// Expert parallel combine: a token's slots on this GPU's experts only (ascending expert index, the
+// same rounding as moe_combine_kernel), pushed as fp32 into the receive area of the row's owner
+// (sk_push_offset of a one-contributor plan: tiles of 128 features, contributor 0); then every
+// rank is signalled once.  A token none of whose experts live here pushes zeros.
+struct MoePush {
+  int nranks, rank, rpr;
+  SplitKPlan plan;
+  float* recv[kTpMaxRanks];
+  uint32_t* signal[kTpMaxRanks];
+  uint32_t* arrive;
+  int first_expert, local_experts;
+};
+
+__global__ void moe_combine_push_kernel(const __nv_bfloat16* __restrict__ y, const float* __restrict__ topk_w,
+                                        const int32_t* __restrict__ topk_ids, const int32_t* __restrict__ pair_row,
+                                        int K, int hidden, const __grid_constant__ MoePush mp) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.x;
+  int ord[kMaxTopK];
+  for (int k = 0; k < K; ++k) ord[k] = k;
+  for (int i = 1; i < K; ++i) {  // insertion sort of the slots by expert index
+    const int v = ord[i];
+    int j = i - 1;
+    while (j >= 0 && topk_ids[b * K + ord[j]] > topk_ids[b * K + v]) {
+      ord[j + 1] = ord[j];
+      --j;
+    }
+    ord[j + 1] = v;
+  }
+  const int q = b / mp.rpr, bl = b - q * mp.rpr;
+  float* dst = mp.recv[q];
+  for (int i = threadIdx.x * 8; i < hidden; i += blockDim.x * 8) {
+    float acc[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
+    for (int kk = 0; kk < K; ++kk) {
+      const int k = ord[kk];
+      const int e = topk_ids[b * K + k];
+      if (e < mp.first_expert || e >= mp.first_expert + mp.local_experts) continue;
+      const float w = topk_w[b * K + k];
+      const uint4 v = *reinterpret_cast<const uint4*>(y + static_cast<int64_t>(pair_row[b * K + k]) * hidden + i);
+      const __nv_bfloat16* ve = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[c] = bf16_round(__fadd_rn(acc[c], __fmul_rn(w, __bfloat162float(ve[c]))));
+    }
+    const int t = i / kSplitBM, r = i - t * kSplitBM;
+    float4* o = reinterpret_cast<float4*>(dst + sk_push_offset(mp.plan, mp.rank, t, 0, mp.rpr, bl, r));
+    o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) signal_ranks_once(mp.arrive, gridDim.x, mp.signal, mp.nranks);
+}
+
 template <int BN>
 constexpr int moe_stages() {
   return BN == 64 ? 4 : (BN == 128 ? 6 : 4);
@@ -463,11 +549,15 @@ extern "C" int mvb_moe_gather(void* out, const void* x, int64_t hidden, const in
                 (__nv_bfloat16*)out, (const __nv_bfloat16*)x, (int)hidden, row_token);
 }
 
-extern "C" int mvb_moe_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t n_per_expert,
-                                 int64_t k, int64_t num_experts, int64_t nrows, int64_t max_rows_per_expert,
-                                 int epilogue, const int32_t* expert_off, const int32_t* active,
-                                 mvb_stream_t stream) {
+extern "C" int mvb_moe_gemm_bf16_experts(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
+                                         int64_t n_per_expert, int64_t k, int64_t num_experts, int64_t first_expert,
+                                         int64_t local_experts, int64_t nrows, int64_t max_rows_per_expert,
+                                         int epilogue, const int32_t* expert_off, const int32_t* active,
+                                         mvb_stream_t stream) {
   MVB_REQUIRE(y && x && w && expert_off && active, "mvb_moe_gemm_bf16: null pointer");
+  MVB_REQUIRE(first_expert >= 0 && local_experts > 0 && first_expert + local_experts <= num_experts,
+              "mvb_moe_gemm_bf16: experts %lld + %lld of %lld", (long long)first_expert, (long long)local_experts,
+              (long long)num_experts);
   MVB_REQUIRE(epilogue == MVB_EPI_STORE || epilogue == MVB_EPI_SWIGLU, "mvb_moe_gemm_bf16: epilogue %d", epilogue);
   MVB_REQUIRE(k > 0 && k % BK == 0 && n_per_expert > 0 && num_experts > 0 && num_experts <= kMaxExperts && nrows > 0,
               "mvb_moe_gemm_bf16: bad shape");
@@ -482,7 +572,7 @@ extern "C" int mvb_moe_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ld
   const int bn = max_rows_per_expert <= 64 ? 64 : (max_rows_per_expert <= 128 ? 128 : 256);
   CUtensorMap tw, tx;
   {
-    const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(num_experts * n_per_expert)};
+    const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(local_experts * n_per_expert)};
     const uint64_t strides[1] = {static_cast<uint64_t>(k) * 2};
     const uint32_t box[2] = {BK, static_cast<uint32_t>(swiglu ? 64 : BM)};
     MVB_TRY(encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B));
@@ -503,10 +593,12 @@ extern "C" int mvb_moe_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ld
   a.swiglu = swiglu ? 1 : 0;
   a.expert_off = expert_off;
   a.active = active;
+  a.first_expert = static_cast<int>(first_expert);
+  a.local_experts = static_cast<int>(local_experts);
   a.err = device_status_ptr();
   // The active-expert count is known on the device only: enough CTAs for every unit of all
   // experts, two per SM at BN = 64; CTAs without a unit exit after the prologue.
-  const int64_t max_units = num_experts * a.tiles_pe;
+  const int64_t max_units = local_experts * a.tiles_pe;
   const int64_t ctas = bn == 64 ? 2LL * sms : sms;
   const int grid = static_cast<int>(max_units < ctas ? max_units : ctas);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -515,6 +607,14 @@ extern "C" int mvb_moe_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ld
     case 128: return launch_moe_gemm<128>(tw, tx, a, grid, st);
     default: return launch_moe_gemm<256>(tw, tx, a, grid, st);
   }
+}
+
+extern "C" int mvb_moe_gemm_bf16(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t n_per_expert,
+                                 int64_t k, int64_t num_experts, int64_t nrows, int64_t max_rows_per_expert,
+                                 int epilogue, const int32_t* expert_off, const int32_t* active,
+                                 mvb_stream_t stream) {
+  return mvb_moe_gemm_bf16_experts(y, ldy, x, ldx, w, n_per_expert, k, num_experts, 0, num_experts, nrows,
+                                   max_rows_per_expert, epilogue, expert_off, active, stream);
 }
 
 extern "C" int mvb_moe_combine(void* out, const void* y, const float* topk_w, const int32_t* topk_ids,
@@ -527,4 +627,40 @@ extern "C" int mvb_moe_combine(void* out, const void* y, const float* topk_w, co
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return launch("moe_combine", moe_combine_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, st,
                 (__nv_bfloat16*)out, (const __nv_bfloat16*)y, topk_w, topk_ids, pair_row, (int)top_k, (int)hidden);
+}
+
+extern "C" int mvb_tp_moe_combine(mvb_tp_comm* comm, const void* y, const float* topk_w, const int32_t* topk_ids,
+                                  const int32_t* pair_row, int64_t rows, int64_t top_k, int64_t hidden,
+                                  int64_t first_expert, int64_t local_experts, int64_t recv_offset, int signal_point,
+                                  mvb_stream_t stream) {
+  MVB_REQUIRE(comm && y && topk_w && topk_ids && pair_row, "mvb_tp_moe_combine: null pointer");
+  const int nr = comm->nranks;
+  MVB_REQUIRE(rows > 0 && rows <= kMaxRows && rows % nr == 0 && top_k > 0 && top_k <= kMaxTopK && hidden > 0 &&
+                  hidden % kSplitBM == 0 && aligned(y, 16),
+              "mvb_tp_moe_combine: rows %lld (a multiple of %d ranks), hidden %lld (a multiple of %d)",
+              (long long)rows, nr, (long long)hidden, kSplitBM);
+  MVB_REQUIRE(first_expert >= 0 && local_experts > 0, "mvb_tp_moe_combine: expert range");
+  MVB_REQUIRE(signal_point >= 0 && signal_point < kTpMaxPoints, "mvb_tp_moe_combine: signal point");
+  const int sms = current_sm_count();
+  MVB_REQUIRE(sms > 0, "mvb_tp_moe_combine: no device");
+  MoePush mp{};
+  mp.nranks = nr;
+  mp.rank = comm->rank;
+  mp.rpr = static_cast<int>(rows / nr);
+  mp.plan = splitk_plan_push(rows, hidden, kSplitBK, sms, nr);   // one k-block: one contributor per tile
+  MVB_REQUIRE(recv_offset >= kTpSignalBytes && recv_offset % 16 == 0 &&
+                  recv_offset + splitk_push_bytes(mp.plan, nr, mp.rpr) <= comm->heap_bytes,
+              "mvb_tp_moe_combine: receive area outside the heap");
+  for (int q = 0; q < nr; ++q) {
+    mp.recv[q] = reinterpret_cast<float*>(comm->base[q] + recv_offset);
+    mp.signal[q] = comm->signal_slot(q, signal_point);
+  }
+  mp.arrive = comm->arrive_slot(signal_point);
+  mp.first_expert = static_cast<int>(first_expert);
+  mp.local_experts = static_cast<int>(local_experts);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  MVB_TRY(launch("tp_moe_combine", moe_combine_push_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, st,
+                 (const __nv_bfloat16*)y, topk_w, topk_ids, pair_row, (int)top_k, (int)hidden, mp));
+  comm->point_count[signal_point] = 1;   // one signal per rank per step
+  return MVB_OK;
 }

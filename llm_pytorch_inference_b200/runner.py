@@ -104,7 +104,9 @@ class DecodeWeights:
                     self.egu.append(get(e + "gate_up_proj.weight"))
                     self.edown.append(get(e + "down_proj.weight"))
                 else:
-                    E = cfg["num_experts"]
+                    E = 0   # the experts this GPU holds (all, or a tensor-parallel rank's share)
+                    while f"{e}{E}.gate_proj.weight" in sd:
+                        E += 1
                     self.egu.append(torch.stack([torch.cat([get(f"{e}{j}.gate_proj.weight"), get(f"{e}{j}.up_proj.weight")],
                                                            0) for j in range(E)]).contiguous())
                     self.edown.append(torch.stack([get(f"{e}{j}.down_proj.weight") for j in range(E)]).contiguous())
@@ -199,7 +201,8 @@ class DecodeRunner:
         if self.tp.enabled:
             lib = N.lib()
             recv_o = lib.mvb_tp_recv_bytes(B, H, self.Hq * self.D, T, didx)
-            recv_d = lib.mvb_tp_recv_bytes(B, H, self.I, T, didx)
+            # down_proj partials; a sparse MoE block pushes one combined partial per rank (one k-block plan)
+            recv_d = lib.mvb_tp_recv_bytes(B, H, 64 if cfg.get("num_experts") else self.I, T, didx)
             self.layout = tpm.plan_heap(lib.mvb_tp_signal_bytes(), B, H, self.V, recv_o, recv_d)
             self.heap = tpm.SymmetricHeap(self.layout.total, self.tp.rank, T)
             self.xn = self.heap.tensor(self.layout.xn, (B, H), bf, dev)
@@ -212,9 +215,9 @@ class DecodeRunner:
         self.h = torch.zeros(B, self.I, dtype=bf, device=dev)
         self.moe = bool(cfg.get("num_experts"))
         if self.moe:
-            if self.tp.enabled:
-                raise NotImplementedError("tensor parallelism of the MoE layers is not built")
             self.E, self.K = cfg["num_experts"], cfg["num_experts_per_tok"]
+            # expert parallel under tensor parallelism: this rank's experts (all of them on one GPU)
+            self.e_first, self.e_local = (tpm.expert_range(cfg, T, self.tp.rank) if self.tp.enabled else (0, self.E))
             self.Im = cfg["moe_intermediate_size"]
             self.norm_topk = 1 if cfg.get("norm_topk_prob", True) else 0
             i32 = torch.int32
@@ -457,8 +460,31 @@ class DecodeRunner:
     def _moe_mlp(self, i) -> None:
         """The sparse MoE block on ``self.xn`` into ``self.mlp_out`` (``qwen3_moe_model.py:39-65``):
         router GEMM, routing + dispatch order, gather, grouped gate/up (SwiGLU) and down GEMMs over
-        the active experts, expert-ordered weighted combine."""
+        the active experts, expert-ordered weighted combine.  Tensor parallel: every rank routes
+        every row, computes its own experts only, and pushes its combined partial to the row's
+        owner (``mvb_tp_moe_combine``, signal point ``point_down(i)``)."""
         lib, w, B, H, st = N.lib(), self.w, self.B, self.H, self._st
+        if self.tp.enabled:
+            self._gemm(self.router_logits, self.xn, w.router[i])
+            N.check(lib.mvb_moe_route(self.router_logits.data_ptr(), B, self.E, self.K, self.norm_topk,
+                                      self.topk_ids.data_ptr(), self.topk_w.data_ptr(), self.pair_row.data_ptr(),
+                                      self.row_token.data_ptr(), self.expert_off.data_ptr(), self.active.data_ptr(),
+                                      st), "moe_route")
+            n = B * self.K
+            N.check(lib.mvb_moe_gather(self.x_sorted.data_ptr(), self.xn.data_ptr(), H, self.row_token.data_ptr(), n,
+                                       st), "moe_gather")
+            for y, ldy, x, ldx, wt, nn, k, epi in (
+                    (self.h_sorted, self.Im, self.x_sorted, H, w.egu[i], 2 * self.Im, H, N.EPI_SWIGLU),
+                    (self.y_sorted, H, self.h_sorted, self.Im, w.edown[i], H, self.Im, N.EPI_STORE)):
+                N.check(lib.mvb_moe_gemm_bf16_experts(y.data_ptr(), ldy, x.data_ptr(), ldx, wt.data_ptr(), nn, k,
+                                                      self.E, self.e_first, self.e_local, n, B, epi,
+                                                      self.expert_off.data_ptr(), self.active.data_ptr(), st),
+                        "moe_gemm_experts")
+            N.check(lib.mvb_tp_moe_combine(self.heap.comm, self.y_sorted.data_ptr(), self.topk_w.data_ptr(),
+                                           self.topk_ids.data_ptr(), self.pair_row.data_ptr(), B, self.K, H,
+                                           self.e_first, self.e_local, self.layout.recv_down, tpm.point_down(i), st),
+                    "tp_moe_combine")
+            return
         self._gemm(self.router_logits, self.xn, w.router[i])
         N.check(lib.mvb_moe_route(self.router_logits.data_ptr(), B, self.E, self.K, self.norm_topk,
                                   self.topk_ids.data_ptr(), self.topk_w.data_ptr(), self.pair_row.data_ptr(),
@@ -561,6 +587,8 @@ class DecodeRunner:
             for i in range(self.L):
                 self._attention(i)
                 self._tp_layer_tail(i)   # the last one applies the final norm
+        elif self.moe:
+            self._tp_layers_moe()
         else:
             self._tp_layers()
         last = self.L - 1
@@ -573,6 +601,24 @@ class DecodeRunner:
         N.check(lib.mvb_sample(self.tokens.data_ptr(), N.ptr(self.probs), self.logits.data_ptr(), B, self.V, self.V,
                                self.temperature.data_ptr(), self.top_k.data_ptr(), self.top_p.data_ptr(), self.seed,
                                0, self.offset.data_ptr(), bf, st), "sample")
+
+    def _tp_layers_moe(self) -> None:
+        """Tensor-parallel attention and expert-parallel MoE blocks, through the final norm: the
+        owners' add+norm sums one pushed partial per rank (a one-k-block plan, ``gemm_k`` 64)."""
+        lib, w, D, st, lay = N.lib(), self.w, self.D, self._st, self.layout
+        comm = self.heap.comm
+        for i in range(self.L):
+            if i > 0:
+                self._tp_add_norm(64, w.ln1[i], lay.recv_down, tpm.point_down(i - 1), tpm.point_mlp_norm(i - 1))
+            self._tp_gemm(self.xn, w.wqkv[i], N.EPI_PARTIALS, wait=-1 if i == 0 else tpm.point_mlp_norm(i - 1))
+            self._qk(i)
+            self._attention(i)
+            self._tp_gemm(self.attn, w.wo[i], N.EPI_PARTIALS, out_offset=lay.recv_o, signal=tpm.point_o_proj(i))
+            self._tp_add_norm(self.Hq * D, w.ln2[i], lay.recv_o, tpm.point_o_proj(i), tpm.point_attn_norm(i))
+            N.check(lib.mvb_tp_wait(comm, tpm.point_attn_norm(i), st), "tp_wait")   # the router reads every row
+            self._moe_mlp(i)
+        last = self.L - 1
+        self._tp_add_norm(64, w.final_norm, lay.recv_down, tpm.point_down(last), tpm.point_mlp_norm(last))
 
     def _tp_layers(self) -> None:
         """The per-kernel tensor-parallel layers, through the final norm."""
@@ -707,7 +753,8 @@ class DecodeRunner:
         o_proj, add+norm, gate_up, swiglu, down), an add+norm between layers, final add+norm, lm_head,
         sample."""
         if self.moe:   # 11 per layer: qkv, qk, attention, o_proj, add+norm, router, route, gather, 2 GEMMs, combine
-            return 2 + self.L * 11 + (self.L - 1) + 3
+            # (tensor parallel: + a wait before each router, the step-counter kernel, the wait before sampling)
+            return 2 + self.L * 11 + (self.L - 1) + 3 + (self.L + 2 if self.tp.enabled else 0)
         if self.fused:   # embedding, rmsnorm, qkv, qk, then attention + fused tail per layer, lm_head, sample
             # (tensor parallel: + the step-counter kernel and the wait before sampling)
             return 4 + 2 * self.L + 2 + (2 + (1 if self.final_softcap else 0) if self.tp.enabled else 0)

@@ -66,19 +66,28 @@ def init_distributed(backend: str = "nccl", timeout_s: float = 60.0) -> TensorPa
 
 # ------------------------------------------------------------------------ weights
 def check_divisible(cfg: dict, tp_size: int) -> None:
-    """The split needs whole heads, whole intermediate slices and whole vocab slices per rank."""
+    """The split needs whole heads, whole intermediate slices (whole experts for a sparse MoE
+    model) and whole vocab slices per rank."""
     hq, hkv, inter, vocab = (cfg["num_attention_heads"], num_kv_heads(cfg), cfg["intermediate_size"],
                              cfg["vocab_size"])
-    for name, v in (("num_attention_heads", hq), ("num_key_value_heads", hkv), ("intermediate_size", inter),
-                    ("vocab_size", vocab)):
+    checks = [("num_attention_heads", hq), ("num_key_value_heads", hkv), ("vocab_size", vocab)]
+    checks.append(("num_experts", cfg["num_experts"]) if cfg.get("num_experts") else ("intermediate_size", inter))
+    for name, v in checks:
         if v % tp_size:
             raise ValueError(f"{name}={v} is not divisible by tp_size={tp_size}")
+
+
+def expert_range(cfg: dict, tp_size: int, rank: int) -> tuple[int, int]:
+    """Expert parallelism of a sparse MoE block: rank r holds experts [r E / T, (r + 1) E / T)."""
+    per = cfg["num_experts"] // tp_size
+    return rank * per, per
 
 
 def shard_state_dict(cfg: dict, sd: dict[str, torch.Tensor], tp_size: int, rank: int) -> dict[str, torch.Tensor]:
     """Rank ``rank``'s part of a HuggingFace-keyed state dict (tensors are views or copies of
     ``sd``'s, on the same device).  Norm weights, the embedding and q_norm/k_norm (per head
-    dimension) are replicated."""
+    dimension) are replicated; a sparse MoE block's router is replicated and its experts are
+    split whole over the ranks (``expert_range``)."""
     check_divisible(cfg, tp_size)
     if tp_size == 1:
         return dict(sd)
@@ -94,7 +103,17 @@ def shard_state_dict(cfg: dict, sd: dict[str, torch.Tensor], tp_size: int, rank:
     def cols(t, n):
         return t[:, rank * n:(rank + 1) * n].contiguous()
 
+    first, per = expert_range(cfg, tp_size, rank) if cfg.get("num_experts") else (0, 0)
     for k, t in sd.items():
+        if ".mlp.experts." in k:   # expert parallel: this rank's experts, renumbered from 0
+            head, tail = k.split(".mlp.experts.")
+            if tail in ("gate_up_proj.weight", "down_proj.weight"):   # stacked [E, ...]
+                out[k] = t[first:first + per].contiguous()
+            else:
+                j, rest = tail.split(".", 1)
+                if first <= int(j) < first + per:
+                    out[f"{head}.mlp.experts.{int(j) - first}.{rest}"] = t
+            continue
         if k.endswith("self_attn.q_proj.weight"):
             out[k] = rows(t, hq * D)
         elif k.endswith("self_attn.k_proj.weight") or k.endswith("self_attn.v_proj.weight"):
@@ -117,10 +136,13 @@ def shard_state_dict(cfg: dict, sd: dict[str, torch.Tensor], tp_size: int, rank:
 def local_config(cfg: dict, tp_size: int) -> dict:
     """Per-rank head / feature counts (the model dims a rank's kernels see)."""
     check_divisible(cfg, tp_size)
-    return {"num_attention_heads": cfg["num_attention_heads"] // tp_size,
-            "num_key_value_heads": num_kv_heads(cfg) // tp_size,
-            "intermediate_size": cfg["intermediate_size"] // tp_size,
-            "vocab_size": cfg["vocab_size"] // tp_size}
+    out = {"num_attention_heads": cfg["num_attention_heads"] // tp_size,
+           "num_key_value_heads": num_kv_heads(cfg) // tp_size,
+           "intermediate_size": cfg["intermediate_size"] // tp_size,
+           "vocab_size": cfg["vocab_size"] // tp_size}
+    if cfg.get("num_experts"):
+        out["num_experts"] = cfg["num_experts"] // tp_size
+    return out
 
 
 # ------------------------------------------------------------------- signal points

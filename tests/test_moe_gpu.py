@@ -114,3 +114,68 @@ def test_moe_decode_teacher_forced_matches_oracle():
     cfg, oracle, alt, eng = _setup("qwen3-moe-tiny", prompts, 256)
     _compare_teacher_forced(oracle, alt, eng, 10)
     assert N.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("first,count", [(0, 32), (32, 32), (96, 32), (64, 16)])
+def test_expert_range_gemms_equal_the_full_grouped_gemm_on_their_rows(first, count):
+    """Expert parallelism: with only experts first .. first+count-1 in the weight tensor, the
+    grouped GEMMs compute exactly the full grouped GEMM's rows of those experts and leave every
+    other dispatched row untouched."""
+    B, E, K, H, I = 32, 128, 8, 2048, 768
+    g = torch.Generator().manual_seed(first + count)
+    r = _route(torch.randn(B, E, generator=g).to(torch.bfloat16).to(DEV), K)
+    x = (torch.randn(B * K, H, generator=g) / H ** 0.5).to(torch.bfloat16).to(DEV)
+    wgu = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    lib, st, n = N.lib(), N.stream_handle(), B * K
+    full = torch.zeros(n, I, dtype=torch.bfloat16, device=DEV)
+    part = torch.full((n, I), 7.0, dtype=torch.bfloat16, device=DEV)
+    N.check(lib.mvb_moe_gemm_bf16(full.data_ptr(), I, x.data_ptr(), H, wgu.data_ptr(), 2 * I, H, E, n, B,
+                                  N.EPI_SWIGLU, r["off"].data_ptr(), r["active"].data_ptr(), st), "full")
+    local = wgu[first:first + count].contiguous()
+    N.check(lib.mvb_moe_gemm_bf16_experts(part.data_ptr(), I, x.data_ptr(), H, local.data_ptr(), 2 * I, H, E, first,
+                                          count, n, B, N.EPI_SWIGLU, r["off"].data_ptr(), r["active"].data_ptr(), st),
+            "experts")
+    torch.cuda.synchronize()
+    assert N.device_status(clear=True) == 0
+    off = r["off"].cpu()
+    a, b = int(off[first]), int(off[first + count])
+    assert torch.equal(part[a:b], full[a:b])
+    assert bool((part[:a] == 7.0).all()) and bool((part[b:] == 7.0).all())
+
+
+def test_tp_moe_combine_pushes_each_ranks_partial():
+    """mvb_tp_moe_combine on one rank: the combined rows (all experts local) land in the receive
+    area's layout bit-exact against the reference accumulation; with half the experts, the
+    partial is the reference accumulation over those experts' slots only."""
+    from llm_pytorch_inference_b200 import tensor_parallel as tpm
+
+    B, E, K, H = 16, 16, 4, 512
+    g = torch.Generator().manual_seed(9)
+    r = _route(torch.randn(B, E, generator=g).to(torch.bfloat16).to(DEV), K)
+    y = torch.randn(B * K, H, generator=g).to(torch.bfloat16)
+    yd = y.to(DEV)
+    lib = N.lib()
+    recv_bytes = lib.mvb_tp_recv_bytes(B, H, 64, 1, 0)
+    assert recv_bytes == B * H * 4
+    heap = tpm.SymmetricHeap(lib.mvb_tp_signal_bytes() + recv_bytes + 4096, 0, 1)
+    try:
+        off = (lib.mvb_tp_signal_bytes() + 255) // 256 * 256
+        recv = heap.tensor(off, (H // 128, B, 128), torch.float32, DEV)   # [tile][row][128] for one rank
+        pr = r["pair_row"].cpu().long()
+        for first, count in ((0, E), (8, 8)):
+            N.check(lib.mvb_tp_begin_step(heap.comm, N.stream_handle()), "begin")
+            N.check(lib.mvb_tp_moe_combine(heap.comm, yd.data_ptr(), r["w"].data_ptr(), r["ids"].data_ptr(),
+                                           r["pair_row"].data_ptr(), B, K, H, first, count, off, 5,
+                                           N.stream_handle()), "tp_moe_combine")
+            N.check(lib.mvb_tp_wait(heap.comm, 5, N.stream_handle()), "wait")
+            torch.cuda.synchronize()
+            got = recv.permute(1, 0, 2).reshape(B, H).cpu()
+            ids, w = r["ids"].cpu(), r["w"].cpu().clone()
+            mine = (ids >= first) & (ids < first + count)
+            w[~mine] = 0.0          # a zero weight adds exactly nothing to the bf16 chain
+            want = om.moe_combine(y[pr], w, ids, torch.bfloat16).float()
+            assert torch.equal(got, want), (first, count)
+        assert N.device_status(clear=True) == 0
+    finally:
+        torch.cuda.synchronize()
+        heap.close()

@@ -183,3 +183,78 @@ def test_gemma2_shard_shapes():
     assert out["model.embed_tokens.weight"].shape == (V, H)
     assert "lm_head.weight" not in sd and out["lm_head.weight"].shape == (V // 2, H)   # cut from the tied table
     assert tpm.local_config(cfg, 2)["num_key_value_heads"] == nkv // 2
+
+
+def _moe_block(sd, p, xn, top_k, first, count):
+    """The sparse MoE block of layer prefix ``p`` in fp32 over the experts ``first .. first+count-1``
+    only (the state dict holds them as local experts 0 .. count-1); routing over all experts."""
+    from oracle.model import moe_route
+
+    topw, topi = moe_route(xn @ sd[p + "mlp.gate.weight"].T, top_k)
+    out = torch.zeros_like(xn)
+    for b in range(xn.shape[0]):
+        for k in range(top_k):
+            e = int(topi[b, k])
+            if not first <= e < first + count:
+                continue
+            q = f"{p}mlp.experts.{e - first}."
+            h = torch.nn.functional.silu(xn[b] @ sd[q + "gate_proj.weight"].T) * (xn[b] @ sd[q + "up_proj.weight"].T)
+            out[b] += topw[b, k] * (h @ sd[q + "down_proj.weight"].T)
+    return out
+
+
+def _moe_worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = get_config("qwen3-moe-tiny", num_hidden_layers=1)
+        sd = canonical_state_dict(cfg, seed=0, dtype=torch.float32)
+        xn = torch.randn(8, cfg["hidden_size"], generator=torch.Generator().manual_seed(5))
+        E, K = cfg["num_experts"], cfg["num_experts_per_tok"]
+        first, count = tpm.expert_range(cfg, world, rank)
+        shard = tpm.shard_state_dict(cfg, sd, world, rank)
+        p = "model.layers.0."
+        same = all(torch.equal(shard[f"{p}mlp.experts.{j}.{w}_proj.weight"], sd[f"{p}mlp.experts.{first + j}.{w}_proj.weight"])
+                   for j in range(count) for w in ("gate", "up", "down"))
+        extra = any(f"{p}mlp.experts.{j}.gate_proj.weight" in shard for j in range(count, E))
+        part = _moe_block(shard, p, xn, K, first, count)   # this rank's experts only
+        dist.all_reduce(part)                               # the owners' sum of the pushed partials
+        want = _moe_block(sd, p, xn, K, 0, E)
+        results[rank] = {"err": float((part - want).abs().max()), "scale": float(want.abs().max()),
+                         "same": same, "extra": extra, "router": torch.equal(shard[p + "mlp.gate.weight"],
+                                                                              sd[p + "mlp.gate.weight"])}
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_moe_block_reproduces_the_unsharded_block_on_two_gloo_ranks():
+    """Expert parallelism of the sparse MoE block: each rank keeps the router and its contiguous
+    share of the experts (renumbered from 0); the sum over ranks of each rank's experts'
+    contributions is the unsharded block (fp32, up to summation order)."""
+    world = 2
+    with mp.get_context("spawn").Manager() as m:
+        results = m.dict()
+        mp.spawn(_moe_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+        res = dict(results)
+    for r in range(world):
+        assert res[r]["same"] and not res[r]["extra"] and res[r]["router"], res[r]
+        assert res[r]["err"] <= 1e-5 * max(1.0, res[r]["scale"]), res[r]
+
+
+def test_moe_shard_shapes():
+    """Qwen3-30B-A3B-arch experts at TP=4: 32 whole experts per rank (stacked and per-expert keys),
+    the router replicated, attention split by heads; a split that cuts experts is refused."""
+    from llm_pytorch_inference_b200.weights import stacked_expert_shapes
+
+    cfg = get_config("qwen3-30b-a3b", num_hidden_layers=1)
+    sd = {k: torch.empty(s, dtype=torch.bfloat16, device="meta") for k, s in stacked_expert_shapes(cfg).items()}
+    out = tpm.shard_state_dict(cfg, sd, 4, 2)
+    p = "model.layers.0."
+    assert out[p + "mlp.experts.gate_up_proj.weight"].shape == (32, 2 * 768, 2048)
+    assert out[p + "mlp.experts.down_proj.weight"].shape == (32, 2048, 768)
+    assert out[p + "mlp.gate.weight"].shape == (128, 2048)
+    assert out[p + "self_attn.q_proj.weight"].shape == (8 * 128, 2048)
+    assert tpm.expert_range(cfg, 4, 2) == (64, 32)
+    assert tpm.local_config(cfg, 4)["num_experts"] == 32
+    with pytest.raises(ValueError):
+        tpm.check_divisible(dict(cfg, num_experts=130), 4)

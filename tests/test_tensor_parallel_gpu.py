@@ -138,8 +138,42 @@ def test_fused_layer_exchange_path_on_one_gpu_matches_per_kernel_exchange_path()
     fused.runner.close()
 
 
+def test_expert_parallel_moe_exchange_path_on_one_gpu_matches_plain_moe_step():
+    """The tensor-parallel step of a sparse MoE model (heads split for attention, experts split
+    for the MoE block, each rank's combined partial pushed to the row's owner) with one rank,
+    against the one-GPU MoE step: the same routing, expert GEMMs and combine chain; the owner's
+    add+norm sums its square in another order than the plain add+norm kernel, so the bar is bf16
+    rounding of the normalised rows carried through the model, and greedy tokens equal wherever
+    the margin is not a near tie."""
+    cfg = get_config("qwen3-moe-tiny")
+    sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device="cuda")
+    batch, lens = 8, [20 + 23 * i for i in range(8)]
+    plain = _engine(cfg, sd, TensorParallelConfig(1, 0), batch, lens, 128)
+    xchg = _engine(cfg, sd, TensorParallelConfig(1, 0, exchange=True), batch, lens, 128)
+    del sd
+    N.device_status(clear=True)
+    for e in (plain, xchg):
+        e.set_sampling(0.0, -1, 1.0)
+    for step in range(4):
+        a = plain.step(use_graph=step > 0)
+        b = xchg.step(use_graph=step > 0)
+        la, lb = plain.runner.logits[:batch].float(), xchg.runner.logits[:batch].float()
+        d = (la - lb).abs()
+        assert float(d.max()) <= 0.02 * float(la.abs().max()) + 1e-3, (step, float(d.max()))
+        assert float(d.mean()) <= 2e-3 * float(la.abs().mean()) + 1e-4, (step, float(d.mean()))
+        top2 = la.topk(2, dim=-1).values
+        for r in range(batch):
+            if float(top2[r, 0] - top2[r, 1]) > 2 * float(d[r].max()):
+                assert a[r] == b[r], (step, r)
+        xchg.force_last_tokens(a)
+    assert N.device_status(clear=True) == 0
+    plain.runner.close()
+    xchg.runner.close()
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("arch,fused", [("qwen3-8b", False), ("gemma2-9b", False), ("qwen3-8b", True)])
+@pytest.mark.parametrize("arch,fused", [("qwen3-8b", False), ("gemma2-9b", False), ("qwen3-8b", True),
+                                        ("qwen3-30b-a3b", False)])
 def test_tp2_matches_tp1_teacher_forced(tmp_path, arch, fused):
     out = tmp_path / "tp2.json"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
@@ -153,6 +187,14 @@ def test_tp2_matches_tp1_teacher_forced(tmp_path, arch, fused):
     assert rep["tables_equal"] and all(s["tables_ref_equal"] for s in rep["steps"])
     assert rep["all_status"] == [0, 0]
     for s in rep["steps"]:
-        print(s["max_abs"], s["mean_abs"])
-        assert s["max_abs"] <= 1e-1 and s["mean_abs"] <= 1.25e-2
+        print(s["max_abs"], s["mean_abs"], s["row_max_abs"])
+        if arch == "qwen3-30b-a3b":
+            # Sparse MoE: a row whose top-8 of 128 experts sits on a near tie may take another
+            # expert under the split's fp32 reordering (the order of router logits is what flips,
+            # whatever their scale), which changes that row's logits wholesale: at most one such
+            # row per step, every other row within the dense bar.
+            over = [r for r, v in enumerate(s["row_max_abs"]) if v > 1e-1]
+            assert len(over) <= 1 and s["mean_abs"] <= 1.25e-2, (over, s["mean_abs"])
+        else:
+            assert s["max_abs"] <= 1e-1 and s["mean_abs"] <= 1.25e-2
         assert not s["bad_token_rows"], s

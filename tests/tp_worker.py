@@ -1,8 +1,8 @@
 """One rank of the tensor-parallel parity run (launched by tests/test_tensor_parallel_gpu.py via
 torch.distributed.run, one process per GPU).
 
-Every rank builds the same 2-layer model (Qwen3-8B or, with --arch gemma2-9b, Gemma-2-9B layer
-dims) and the same batch of sequences on a shuffled block pool, and decodes with the
+Every rank builds the same 2-layer model (Qwen3-8B, or with --arch the Gemma-2-9B or the sparse-MoE
+Qwen3-30B-A3B layer dims, experts split over the ranks) and the same batch of sequences on a shuffled block pool, and decodes with the
 tensor-parallel engine (with --fused, its one-launch-per-layer-tail step).  Rank 0 also decodes the
 same workload on one GPU (TP=1) and compares, step by step under teacher forcing, the full
 logits and the greedy tokens; it writes a JSON report to --out.
@@ -31,6 +31,13 @@ from llm_pytorch_inference_b200.weights import canonical_state_dict  # noqa: E40
 
 def build(cfg, tp, dev, batch, lens, num_blocks, fused=False):
     sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev)
+    if cfg.get("num_experts"):
+        # Sparse MoE: router weights at 30x the init scale, so that a row's top-8 weights are
+        # spread out (a trained router's are; at N(0, 0.02) they are all ~1/8).  An expert that a
+        # near tie swaps at the 8th place then moves the row by its small weight only.
+        for k in sd:
+            if k.endswith("mlp.gate.weight"):
+                sd[k] = sd[k] * 30
     order = list(range(num_blocks))
     random.Random(0).shuffle(order)
     eng = DecodeEngine(cfg, sd, max_batch=batch, max_model_len=max(lens) + 64, num_blocks=num_blocks, device=dev,
@@ -57,7 +64,7 @@ def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", required=True)
     ap.add_argument("--steps", type=int, default=4)
-    ap.add_argument("--arch", default="qwen3-8b", choices=["qwen3-8b", "gemma2-9b"])
+    ap.add_argument("--arch", default="qwen3-8b", choices=["qwen3-8b", "gemma2-9b", "qwen3-30b-a3b"])
     ap.add_argument("--fused", action="store_true", help="the tensor-parallel step with one launch per layer tail")
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -91,6 +98,7 @@ def main() -> int:
             # a greedy token may only differ where TP=1's own top-2 margin is within the logit noise
             bad = [i for i in range(batch) if toks[i] != want[i] and margin[i] > 2 * float(d[i].max())]
             report["steps"].append({"max_abs": float(d.max()), "mean_abs": float(d.mean()),
+                                    "row_max_abs": [round(float(x), 4) for x in d[:batch].amax(-1)],
                                     "tokens_tp": toks, "tokens_ref": want, "bad_token_rows": bad,
                                     "tables_ref_equal": tabs == [ref.kv.get_block_table(s) for s in range(batch)]})
             forced = want
