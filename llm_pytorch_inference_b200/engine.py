@@ -32,10 +32,10 @@ import numpy as np
 import torch
 
 from . import _native as N
-from .configs import head_dim, num_kv_heads
+from .configs import head_dim
 from .kv_cache import KVCacheManager, num_blocks_for_budget
 from .runner import DecodeRunner, DecodeWeights, meta_layout, resolve_device
-from .tensor_parallel import TensorParallelConfig, shard_state_dict
+from .tensor_parallel import TensorParallelConfig, local_kv_heads, shard_state_dict
 
 
 @dataclass
@@ -308,7 +308,7 @@ class DecodeEngine(RunningBatch):
         sd = shard_state_dict(cfg, state_dict, T, self.tp.rank) if T > 1 else state_dict
         self.weights = DecodeWeights(cfg, sd, self.dev)
         del sd
-        L, nkv, D = cfg["num_hidden_layers"], num_kv_heads(cfg) // T, head_dim(cfg)
+        L, nkv, D = cfg["num_hidden_layers"], local_kv_heads(cfg, T), head_dim(cfg)
         if num_blocks is None:
             free, _ = torch.cuda.mem_get_info(self.dev)
             kw = {} if hbm_budget_bytes is None else {"budget_bytes": hbm_budget_bytes}

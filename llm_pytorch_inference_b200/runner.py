@@ -162,7 +162,7 @@ class DecodeRunner:
         self.L = cfg["num_hidden_layers"]
         self.H = cfg["hidden_size"]
         self.Hq = cfg["num_attention_heads"] // T       # this rank's heads / features
-        self.Hkv = num_kv_heads(cfg) // T
+        self.Hkv = tpm.local_kv_heads(cfg, T)   # one replicated head when there are fewer than ranks
         self.D = head_dim(cfg)
         self.I = cfg["intermediate_size"] // T
         self.V = cfg["vocab_size"]                       # full vocabulary (logits are all-gathered)

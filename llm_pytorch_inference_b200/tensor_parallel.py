@@ -70,11 +70,29 @@ def check_divisible(cfg: dict, tp_size: int) -> None:
     model) and whole vocab slices per rank."""
     hq, hkv, inter, vocab = (cfg["num_attention_heads"], num_kv_heads(cfg), cfg["intermediate_size"],
                              cfg["vocab_size"])
-    checks = [("num_attention_heads", hq), ("num_key_value_heads", hkv), ("vocab_size", vocab)]
+    checks = [("num_attention_heads", hq), ("vocab_size", vocab)]
+    if hkv >= tp_size or tp_size % hkv:   # fewer KV heads than ranks: each is replicated on tp_size / hkv ranks
+        checks.append(("num_key_value_heads", hkv))
     checks.append(("num_experts", cfg["num_experts"]) if cfg.get("num_experts") else ("intermediate_size", inter))
     for name, v in checks:
         if v % tp_size:
             raise ValueError(f"{name}={v} is not divisible by tp_size={tp_size}")
+
+
+def local_kv_heads(cfg: dict, tp_size: int) -> int:
+    """KV heads a rank holds: its share, or one replicated head when there are fewer KV heads than
+    ranks (the query heads of a rank always sit in one GQA group then)."""
+    return max(num_kv_heads(cfg) // tp_size, 1)
+
+
+def kv_head_range(cfg: dict, tp_size: int, rank: int) -> tuple[int, int]:
+    """The first KV head of rank ``rank`` and how many: heads [r n, (r + 1) n) when they split, else
+    the one head whose GQA group holds the rank's query heads (head r / (tp_size / n_kv))."""
+    hkv = num_kv_heads(cfg)
+    if hkv >= tp_size:
+        per = hkv // tp_size
+        return rank * per, per
+    return rank // (tp_size // hkv), 1
 
 
 def expert_range(cfg: dict, tp_size: int, rank: int) -> tuple[int, int]:
@@ -92,7 +110,8 @@ def shard_state_dict(cfg: dict, sd: dict[str, torch.Tensor], tp_size: int, rank:
     if tp_size == 1:
         return dict(sd)
     D = head_dim(cfg)
-    hq, hkv = cfg["num_attention_heads"] // tp_size, num_kv_heads(cfg) // tp_size
+    hq = cfg["num_attention_heads"] // tp_size
+    kv0, hkv = kv_head_range(cfg, tp_size, rank)
     inter = cfg["intermediate_size"] // tp_size
     vocab = cfg["vocab_size"] // tp_size
     out: dict[str, torch.Tensor] = {}
@@ -117,7 +136,7 @@ def shard_state_dict(cfg: dict, sd: dict[str, torch.Tensor], tp_size: int, rank:
         if k.endswith("self_attn.q_proj.weight"):
             out[k] = rows(t, hq * D)
         elif k.endswith("self_attn.k_proj.weight") or k.endswith("self_attn.v_proj.weight"):
-            out[k] = rows(t, hkv * D)
+            out[k] = t[kv0 * D:(kv0 + hkv) * D].contiguous()
         elif k.endswith("self_attn.o_proj.weight"):
             out[k] = cols(t, hq * D)
         elif k.endswith("mlp.gate_proj.weight") or k.endswith("mlp.up_proj.weight"):
@@ -137,7 +156,7 @@ def local_config(cfg: dict, tp_size: int) -> dict:
     """Per-rank head / feature counts (the model dims a rank's kernels see)."""
     check_divisible(cfg, tp_size)
     out = {"num_attention_heads": cfg["num_attention_heads"] // tp_size,
-           "num_key_value_heads": num_kv_heads(cfg) // tp_size,
+           "num_key_value_heads": local_kv_heads(cfg, tp_size),
            "intermediate_size": cfg["intermediate_size"] // tp_size,
            "vocab_size": cfg["vocab_size"] // tp_size}
     if cfg.get("num_experts"):

@@ -68,11 +68,11 @@ def _free_port() -> int:
     return port
 
 
-def _worker(rank, world, port, results):
+def _worker(rank, world, port, results, nkv=4):
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        cfg = get_config("qwen3-tiny", **CFG)
+        cfg = get_config("qwen3-tiny", **dict(CFG, num_key_value_heads=nkv))
         sd = canonical_state_dict(cfg, seed=0, dtype=torch.float32)
         for k in sd:
             if k.endswith("norm.weight"):   # non-trivial norm weights
@@ -86,7 +86,7 @@ def _worker(rank, world, port, results):
         vc = torch.randn(L, B, T, hkv, D, generator=g)
 
         shard = tpm.shard_state_dict(cfg, sd, world, rank)
-        lh = hkv // world
+        kv0, lh = tpm.kv_head_range(cfg, world, rank)   # one replicated head when hkv < world
 
         def reduce(t):
             t = t.clone()
@@ -98,7 +98,7 @@ def _worker(rank, world, port, results):
             dist.all_gather(parts, t.contiguous())
             return torch.cat(parts, -1)
 
-        got = _step(cfg, shard, ids, kc[:, :, :, rank * lh:(rank + 1) * lh], vc[:, :, :, rank * lh:(rank + 1) * lh],
+        got = _step(cfg, shard, ids, kc[:, :, :, kv0:kv0 + lh], vc[:, :, :, kv0:kv0 + lh],
                     T, reduce, gather, lh, hq // world)
         want = _step(cfg, sd, ids, kc, vc, T, lambda t: t, lambda t: t, hkv, hq)
         err = float((got - want).abs().max())
@@ -127,11 +127,14 @@ def _worker(rank, world, port, results):
         dist.destroy_process_group()
 
 
-def test_sharded_step_reproduces_the_unsharded_step_on_two_gloo_ranks():
+@pytest.mark.parametrize("nkv", [4, 1])
+def test_sharded_step_reproduces_the_unsharded_step_on_two_gloo_ranks(nkv):
+    """nkv = 1: fewer KV heads than ranks, the head is replicated and each rank keeps the query
+    heads of its half of the GQA group."""
     world = 2
     with mp.get_context("spawn").Manager() as m:
         results = m.dict()
-        mp.spawn(_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+        mp.spawn(_worker, args=(world, _free_port(), results, nkv), nprocs=world, join=True)
         res = dict(results)
     for r in range(world):
         assert res[r]["err"] <= 1e-4 * max(1.0, res[r]["scale"]), res[r]
@@ -258,3 +261,24 @@ def test_moe_shard_shapes():
     assert tpm.local_config(cfg, 4)["num_experts"] == 32
     with pytest.raises(ValueError):
         tpm.check_divisible(dict(cfg, num_experts=130), 4)
+
+
+def test_kv_heads_replicate_when_fewer_than_ranks():
+    """Qwen3-30B-A3B-arch at TP=8: 4 KV heads, each on two ranks; rank r keeps query heads
+    4r .. 4r+3 and KV head r // 2, whose GQA group (8 query heads) holds them."""
+    from llm_pytorch_inference_b200.weights import stacked_expert_shapes
+
+    cfg = get_config("qwen3-30b-a3b", num_hidden_layers=1)
+    sd = {k: torch.arange(s[0], dtype=torch.float32).view(-1, *([1] * (len(s) - 1))).expand(s)
+          for k, s in stacked_expert_shapes(cfg).items() if "self_attn" in k or k == "lm_head.weight"}
+    for r in range(8):
+        out = tpm.shard_state_dict(cfg, sd, 8, r)
+        k = out["model.layers.0.self_attn.k_proj.weight"]
+        assert k.shape == (128, 2048) and int(k[0, 0]) == (r // 2) * 128
+        q = out["model.layers.0.self_attn.q_proj.weight"]
+        assert q.shape == (512, 2048) and int(q[0, 0]) == r * 512
+        assert (r * 4) // 8 == r // 2       # the rank's first query head is in KV head r // 2's group
+    assert tpm.local_kv_heads(cfg, 8) == 1 and tpm.kv_head_range(cfg, 8, 5) == (2, 1)
+    assert tpm.kv_head_range(cfg, 2, 1) == (2, 2)
+    with pytest.raises(ValueError):
+        tpm.check_divisible(dict(cfg, num_key_value_heads=3, num_attention_heads=24), 8)

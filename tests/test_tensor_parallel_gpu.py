@@ -172,14 +172,17 @@ def test_expert_parallel_moe_exchange_path_on_one_gpu_matches_plain_moe_step():
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("arch,fused", [("qwen3-8b", False), ("gemma2-9b", False), ("qwen3-8b", True),
-                                        ("qwen3-30b-a3b", False)])
-def test_tp2_matches_tp1_teacher_forced(tmp_path, arch, fused):
+@pytest.mark.parametrize("arch,fused,kv", [("qwen3-8b", False, None), ("gemma2-9b", False, None),
+                                           ("qwen3-8b", True, None), ("qwen3-30b-a3b", False, None),
+                                           ("qwen3-8b", False, 1)])
+def test_tp2_matches_tp1_teacher_forced(tmp_path, arch, fused, kv):
+    """kv = 1: one KV head for two ranks (replicated on both; each keeps half its query heads)."""
     out = tmp_path / "tp2.json"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533", str(REPO / "tests" / "tp_worker.py"),
-           "--out", str(out), "--steps", "4", "--arch", arch] + (["--fused"] if fused else [])
+           "--out", str(out), "--steps", "4", "--arch", arch] + (["--fused"] if fused else []) + \
+        ([] if kv is None else ["--kv-heads", str(kv)])
     r = subprocess.run(cmd, env=env, cwd=REPO, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     rep = json.loads(out.read_text())

@@ -23,7 +23,8 @@ import torch.distributed as dist
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
 from llm_pytorch_inference_b200 import _native as N  # noqa: E402
-from llm_pytorch_inference_b200.configs import get_config  # noqa: E402
+from llm_pytorch_inference_b200 import tensor_parallel as tpm  # noqa: E402
+from llm_pytorch_inference_b200.configs import get_config, num_kv_heads  # noqa: E402
 from llm_pytorch_inference_b200.engine import DecodeEngine  # noqa: E402
 from llm_pytorch_inference_b200.tensor_parallel import TensorParallelConfig  # noqa: E402
 from llm_pytorch_inference_b200.weights import canonical_state_dict  # noqa: E402
@@ -49,12 +50,12 @@ def build(cfg, tp, dev, batch, lens, num_blocks, fused=False):
         eng.append_first_token(s, int(torch.randint(0, cfg["vocab_size"], (1,), generator=g)))
     # identical prompt K/V on every configuration: fill the full-head pool on the CPU, slice heads
     T, r = tp.tp_size, tp.rank
-    hkv = eng.kv.num_heads
+    kv0, hkv = tpm.kv_head_range(cfg, T, r)
     gk = torch.Generator().manual_seed(2)
     for s in range(len(lens)):
         for blk in eng.kv.get_block_table(s):
-            full = torch.randn(cfg["num_hidden_layers"], 2, 16, hkv * T, eng.kv.head_dim, generator=gk)
-            eng.kv.kv_cache[:, :, blk] = full[:, :, :, r * hkv:(r + 1) * hkv].to(dev, torch.bfloat16)
+            full = torch.randn(cfg["num_hidden_layers"], 2, 16, num_kv_heads(cfg), eng.kv.head_dim, generator=gk)
+            eng.kv.kv_cache[:, :, blk] = full[:, :, :, kv0:kv0 + hkv].to(dev, torch.bfloat16)
     eng.set_sampling(0.0, -1, 1.0)
     eng.prepare_first_step()
     return eng
@@ -66,6 +67,8 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--arch", default="qwen3-8b", choices=["qwen3-8b", "gemma2-9b", "qwen3-30b-a3b"])
     ap.add_argument("--fused", action="store_true", help="the tensor-parallel step with one launch per layer tail")
+    ap.add_argument("--kv-heads", type=int, default=None,
+                    help="override the KV head count (1: fewer KV heads than ranks, each replicated)")
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -73,7 +76,8 @@ def main() -> int:
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     N.set_pdl(True)
-    cfg = get_config(args.arch, num_hidden_layers=2)
+    over = {} if args.kv_heads is None else {"num_key_value_heads": args.kv_heads}
+    cfg = get_config(args.arch, num_hidden_layers=2, **over)
     batch = 16
     lens = [37 + 29 * i for i in range(batch)]          # ragged contexts, blocks cross boundaries
     num_blocks = 512
