@@ -113,12 +113,22 @@ def _attention_rows(runner) -> int:
 
 class BatchedPrefill:
     """Prefill of dense (Qwen3 / Llama-family), Gemma and sparse-MoE models through a
-    ``DecodeRunner``'s weights, tables and KV pool, on one GPU."""
+    ``DecodeRunner``'s weights, tables and KV pool, on one GPU; dense Qwen3 / Llama-family models
+    also on a tensor-parallel group.
+
+    Tensor parallel (``engine.py:253-295`` with the decode step's Megatron split): each rank runs
+    its column-parallel q|k|v (writing its own KV heads into its pool), its heads' attention and
+    its gate/up slice; the row-parallel o_proj and down_proj outputs are summed over the ranks
+    with an NCCL all-reduce in fp32 (a prefill chunk moves [tokens, hidden] per layer, bandwidth
+    work that NCCL's ring / NVLS algorithms do well; the decode step's in-kernel exchanges are
+    sized for 64 rows), then residual add + RMSNorm on every rank; the vocab-parallel logits of
+    the last tokens are all-gathered, so every rank samples the same first tokens."""
 
     def __init__(self, runner, max_tokens: int = 16384):
-        if runner.tp.enabled:
-            raise NotImplementedError("batched prefill covers single-GPU models")
+        if runner.tp.enabled and (runner.gemma or runner.moe):
+            raise NotImplementedError("tensor-parallel prefill covers dense Qwen3 / Llama-family models")
         self.r = runner
+        self.tp = runner.tp
         self.max_tokens = max_tokens
         r, dev, bf = runner, runner.dev, torch.bfloat16
         T = max_tokens
@@ -144,6 +154,9 @@ class BatchedPrefill:
         if r.gemma:   # the stored gate_up product (GeGLU is applied after it) and a post-norm buffer
             self.gu = torch.zeros(T, 2 * r.I, dtype=bf, device=dev)
             self.z = torch.zeros(T, r.H, dtype=bf, device=dev)
+        if self.tp.enabled:   # a rank's row-parallel partial, and its fp32 copy for the all-reduce
+            self.y = torch.zeros(T, r.H, dtype=bf, device=dev)
+            self.y32 = torch.zeros(T, r.H, dtype=torch.float32, device=dev)
         self.gemm_ws = None
         self.timing: dict[str, list] | None = None   # kind -> [(start, end) CUDA events] when profiling
         self.attn_rows = _attention_rows(r)
@@ -183,6 +196,19 @@ class BatchedPrefill:
                                   0 if aux is None else aux.stride(0), self.gemm_ws.data_ptr(),
                                   self.gemm_ws.numel(), N.stream_handle(dev)), "gemm_bf16")
 
+    def _all_reduce(self, y: torch.Tensor) -> None:
+        """Sums the ranks' partials of a row-parallel product in fp32, then rounds to bf16 (the
+        reference's linear-layer output dtype)."""
+        if self.tp.tp_size == 1:
+            return
+        import torch.distributed as dist
+
+        y32 = self.y32[:y.shape[0]]
+        y32.copy_(y)
+        with self._timed("all_reduce"):
+            dist.all_reduce(y32)
+        y.copy_(y32)
+
     def run(self, ids: list[list[int]], tables: list[list[int]]) -> torch.Tensor:
         """Prefills the sequences whose prompts are ``ids`` into the blocks ``tables`` (each holding
         at least ``len(prompt)`` tokens); returns the bf16 logits ``[n, V]`` of each last token."""
@@ -208,9 +234,9 @@ class BatchedPrefill:
         with self._timed("embedding"):
             N.check(lib.mvb_embedding(h.data_ptr(), tok_d.data_ptr(), N.I32, w.embed.data_ptr(), T, H, r.V,
                                       r.embed_scale, bf, st), "embedding")
-        g, moe = r.gemma, r.moe
+        g, moe, tpx = r.gemma, r.moe, self.tp.enabled
         for i in range(L):
-            if not (g or moe) or i == 0:   # else the previous layer's add formed this layer's input norm
+            if not (g or moe or tpx) or i == 0:   # else the previous layer's add formed this layer's input norm
                 with self._timed("norm"):
                     N.check(lib.mvb_rmsnorm(xn.data_ptr(), H, h.data_ptr(), H, w.ln1[i].data_ptr(), T, H, eps,
                                             r.plus_one, N.NORM_MODEL, bf, st), "rmsnorm")
@@ -240,6 +266,21 @@ class BatchedPrefill:
             if g:
                 self._gemma_mlp_block(i, T, h, xn, attn, act)
                 continue
+            if tpx:   # row-parallel o_proj / down_proj: this rank's partials, summed over the ranks
+                y = self.y[:T]
+                self._gemm(y, attn, w.wo[i])
+                self._all_reduce(y)
+                with self._timed("norm"):
+                    N.check(lib.mvb_fused_add_rmsnorm(xn.data_ptr(), h.data_ptr(), y.data_ptr(), w.ln2[i].data_ptr(),
+                                                      T, H, eps, r.plus_one, N.NORM_MODEL, bf, st), "fused_add_rmsnorm")
+                self._gemm(act, xn, w.wgu[i], N.EPI_SWIGLU)
+                self._gemm(y, act, w.wdown[i])
+                self._all_reduce(y)
+                nw = w.ln1[i + 1] if i + 1 < L else w.final_norm
+                with self._timed("norm"):
+                    N.check(lib.mvb_fused_add_rmsnorm(xn.data_ptr(), h.data_ptr(), y.data_ptr(), nw.data_ptr(), T, H,
+                                                      eps, r.plus_one, N.NORM_MODEL, bf, st), "fused_add_rmsnorm")
+                continue
             self._gemm(h, attn, w.wo[i], N.EPI_RESADD, aux=h)          # h = h + o_proj(attn)
             with self._timed("norm"):
                 N.check(lib.mvb_rmsnorm(xn.data_ptr(), H, h.data_ptr(), H, w.ln2[i].data_ptr(), T, H, eps,
@@ -255,7 +296,7 @@ class BatchedPrefill:
             self._gemm(act, xn, w.wgu[i], N.EPI_SWIGLU)
             self._gemm(h, act, w.wdown[i], N.EPI_RESADD, aux=h)        # h = h + down(swiglu)
         last = torch.tensor([sum(lens[:k + 1]) - 1 for k in range(len(lens))], device=dev)
-        if g or moe:   # xn already holds the final norm of every row
+        if g or moe or tpx:   # xn already holds the final norm of every row
             xl = xn.index_select(0, last).contiguous()
         else:
             hl = h.index_select(0, last).contiguous()
@@ -263,7 +304,16 @@ class BatchedPrefill:
             N.check(lib.mvb_rmsnorm(xl.data_ptr(), H, hl.data_ptr(), H, w.final_norm.data_ptr(), len(lens), H, eps,
                                     r.plus_one, N.NORM_MODEL, bf, st), "rmsnorm")
         logits = torch.empty(len(lens), r.V, dtype=torch.bfloat16, device=dev)
-        self._gemm(logits, xl, w.lm_head)
+        if tpx and self.tp.tp_size > 1:   # vocab-parallel lm_head: every rank's columns, gathered in rank order
+            import torch.distributed as dist
+
+            part = torch.empty(len(lens), r.Vl, dtype=torch.bfloat16, device=dev)
+            self._gemm(part, xl, w.lm_head)
+            parts = [torch.empty_like(part) for _ in range(self.tp.tp_size)]
+            dist.all_gather(parts, part)
+            torch.cat(parts, dim=1, out=logits)
+        else:
+            self._gemm(logits, xl, w.lm_head)
         if r.final_softcap:
             N.check(lib.mvb_softcap(logits.data_ptr(), logits.numel(), r.final_softcap, bf, st), "softcap")
         return logits

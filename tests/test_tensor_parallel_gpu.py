@@ -138,6 +138,39 @@ def test_fused_layer_exchange_path_on_one_gpu_matches_per_kernel_exchange_path()
     fused.runner.close()
 
 
+def test_tensor_parallel_prefill_on_one_gpu_matches_plain_prefill():
+    """The tensor-parallel batched prefill with one rank (row-parallel outputs summed over one
+    rank, then residual add + RMSNorm in one kernel) against the one-GPU prefill (residual added
+    in the GEMM epilogue): last-token logits to bf16 rounding, first tokens equal wherever the
+    margin is not a near tie, and the pools' prompt K/V equal to bf16 rounding."""
+    cfg = get_config("qwen3-8b", num_hidden_layers=2)
+    sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device="cuda")
+    g = torch.Generator().manual_seed(4)
+    lens = [40 + 57 * i for i in range(8)]
+    prompts = {s: torch.randint(0, cfg["vocab_size"], (n,), generator=g).tolist() for s, n in enumerate(lens)}
+    order = list(range(256))
+    random.Random(1).shuffle(order)
+    engs = [DecodeEngine(cfg, sd, max_batch=8, max_model_len=max(lens) + 32, num_blocks=256, device="cuda",
+                         free_order=list(order), tp=t) for t in (TensorParallelConfig(1, 0),
+                                                                 TensorParallelConfig(1, 0, exchange=True))]
+    del sd
+    N.device_status(clear=True)
+    firsts = [e.prefill(prompts) for e in engs]
+    la, lb = (e.last_prefill_logits.float() for e in engs)
+    d = (la - lb).abs()
+    assert float(d.max()) <= 0.02 * float(la.abs().max()) + 1e-3, float(d.max())
+    assert float(d.mean()) <= 2e-3 * float(la.abs().mean()) + 1e-4, float(d.mean())
+    top2 = la.topk(2, dim=-1).values
+    for r in range(8):
+        if float(top2[r, 0] - top2[r, 1]) > 2 * float(d[r].max()):
+            assert firsts[0][r] == firsts[1][r], r
+    ka, kb = (e.kv.kv_cache.float() for e in engs)
+    assert float((ka - kb).abs().max()) <= 0.05 * float(ka.abs().max()) + 1e-2
+    assert N.device_status(clear=True) == 0
+    for e in engs:
+        e.runner.close()
+
+
 def test_expert_parallel_moe_exchange_path_on_one_gpu_matches_plain_moe_step():
     """The tensor-parallel step of a sparse MoE model (heads split for attention, experts split
     for the MoE block, each rank's combined partial pushed to the row's owner) with one rank,
@@ -172,10 +205,11 @@ def test_expert_parallel_moe_exchange_path_on_one_gpu_matches_plain_moe_step():
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("arch,fused,kv", [("qwen3-8b", False, None), ("gemma2-9b", False, None),
-                                           ("qwen3-8b", True, None), ("qwen3-30b-a3b", False, None),
-                                           ("qwen3-8b", False, 1)])
-def test_tp2_matches_tp1_teacher_forced(tmp_path, arch, fused, kv):
+@pytest.mark.parametrize("arch,fused,kv,prefill", [("qwen3-8b", False, None, False), ("gemma2-9b", False, None, False),
+                                                   ("qwen3-8b", True, None, False),
+                                                   ("qwen3-30b-a3b", False, None, False),
+                                                   ("qwen3-8b", False, 1, False), ("qwen3-8b", False, None, True)])
+def test_tp2_matches_tp1_teacher_forced(tmp_path, arch, fused, kv, prefill):
     """kv = 1: one KV head for two ranks (replicated on both; each keeps half of its GQA group of
     8 query heads)."""
     out = tmp_path / "tp2.json"
@@ -183,13 +217,17 @@ def test_tp2_matches_tp1_teacher_forced(tmp_path, arch, fused, kv):
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533", str(REPO / "tests" / "tp_worker.py"),
            "--out", str(out), "--steps", "4", "--arch", arch] + (["--fused"] if fused else []) + \
-        ([] if kv is None else ["--kv-heads", str(kv), "--q-heads", "8"])
+        ([] if kv is None else ["--kv-heads", str(kv), "--q-heads", "8"]) + (["--prefill"] if prefill else [])
     r = subprocess.run(cmd, env=env, cwd=REPO, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     rep = json.loads(out.read_text())
     print(json.dumps({k: v for k, v in rep.items() if k != "steps"}))
     assert rep["tables_equal"] and all(s["tables_ref_equal"] for s in rep["steps"])
     assert rep["all_status"] == [0, 0]
+    if prefill:   # the tensor-parallel batched prefill: last-token logits and first tokens
+        pf = rep["prefill"]
+        print("prefill", pf["max_abs"], pf["mean_abs"])
+        assert pf["max_abs"] <= 1e-1 and pf["mean_abs"] <= 1.25e-2 and not pf["bad_token_rows"], pf
     for s in rep["steps"]:
         print(s["max_abs"], s["mean_abs"], s["row_max_abs"])
         if arch == "qwen3-30b-a3b":

@@ -30,7 +30,10 @@ from llm_pytorch_inference_b200.tensor_parallel import TensorParallelConfig  # n
 from llm_pytorch_inference_b200.weights import canonical_state_dict  # noqa: E402
 
 
-def build(cfg, tp, dev, batch, lens, num_blocks, fused=False):
+def build(cfg, tp, dev, batch, lens, num_blocks, fused=False, prefill=False):
+    """The engine with its sequences' prompts in the KV pool: synthetic K/V (the same on every
+    configuration), or with ``prefill`` the engine's own batched prefill of the prompts, whose
+    last-token logits are kept in ``eng.last_prefill_logits``."""
     sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device=dev)
     order = list(range(num_blocks))
     random.Random(0).shuffle(order)
@@ -38,6 +41,12 @@ def build(cfg, tp, dev, batch, lens, num_blocks, fused=False):
                        free_order=order, tp=tp, fused_layers=fused)
     del sd
     g = torch.Generator().manual_seed(1)
+    if prefill:
+        prompts = {s: torch.randint(0, cfg["vocab_size"], (n,), generator=g).tolist() for s, n in enumerate(lens)}
+        eng.prefill(prompts)
+        eng.set_sampling(0.0, -1, 1.0)
+        eng.prepare_first_step()
+        return eng
     for s, n in enumerate(lens):
         eng.add_sequence(s, torch.randint(0, cfg["vocab_size"], (n,), generator=g).tolist())
         eng.append_first_token(s, int(torch.randint(0, cfg["vocab_size"], (1,), generator=g)))
@@ -63,6 +72,7 @@ def main() -> int:
     ap.add_argument("--kv-heads", type=int, default=None,
                     help="override the KV head count (1: fewer KV heads than ranks, each replicated)")
     ap.add_argument("--q-heads", type=int, default=None, help="override the query head count")
+    ap.add_argument("--prefill", action="store_true", help="prompts through the batched prefill, compared too")
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -77,11 +87,28 @@ def main() -> int:
     batch = 16
     lens = [37 + 29 * i for i in range(batch)]          # ragged contexts, blocks cross boundaries
     num_blocks = 512
-    eng = build(cfg, TensorParallelConfig(world, rank), dev, batch, lens, num_blocks, fused=args.fused)
+    eng = build(cfg, TensorParallelConfig(world, rank), dev, batch, lens, num_blocks, fused=args.fused,
+                prefill=args.prefill)
     ref = None
     if rank == 0:
-        ref = build(cfg, TensorParallelConfig(1, 0), dev, batch, lens, num_blocks)
+        ref = build(cfg, TensorParallelConfig(1, 0), dev, batch, lens, num_blocks, prefill=args.prefill)
     report = {"steps": [], "tables_equal": True}
+    if args.prefill and rank == 0:
+        a, b = eng.last_prefill_logits.float(), ref.last_prefill_logits.float()
+        d = (a - b).abs()
+        top2 = b.topk(2, dim=-1).values
+        ta, tb = [eng.output_tokens(s)[0] for s in range(batch)], [ref.output_tokens(s)[0] for s in range(batch)]
+        report["prefill"] = {"max_abs": float(d.max()), "mean_abs": float(d.mean()),
+                             "bad_token_rows": [i for i in range(batch) if ta[i] != tb[i] and
+                                                float(top2[i, 0] - top2[i, 1]) > 2 * float(d[i].max())]}
+        obj = [tb]
+    else:
+        obj = [None]
+    if args.prefill:   # both continue from TP=1's first tokens
+        dist.broadcast_object_list(obj, src=0)
+        eng.force_last_tokens(obj[0])
+        if ref is not None:
+            ref.force_last_tokens(obj[0])
     for step in range(args.steps):
         moe = bool(cfg.get("num_experts"))
         if moe:   # every layer's routing, to tell a near-tie expert swap from an error
