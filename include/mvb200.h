@@ -366,6 +366,11 @@ int mvb_moe_gemm_bf16_experts(void* y, int64_t ldy, const void* x, int64_t ldx, 
  * `hidden`): experts in ascending index, acc = bf16(acc + w * y) from acc = 0. */
 int mvb_moe_combine(void* out, const void* y, const float* topk_w, const int32_t* topk_ids, const int32_t* pair_row,
                     int64_t rows, int64_t top_k, int64_t hidden, mvb_stream_t stream);
+/* Expert-parallel form: only the slots on experts first_expert .. first_expert + local_experts - 1
+ * (the ranks' outputs are then summed across the group). */
+int mvb_moe_combine_experts(void* out, const void* y, const float* topk_w, const int32_t* topk_ids,
+                            const int32_t* pair_row, int64_t rows, int64_t top_k, int64_t hidden,
+                            int64_t first_expert, int64_t local_experts, mvb_stream_t stream);
 
 /* ---- tensor parallelism (one process per GPU, NVLink peer memory) ----------------------
  * No counterpart in the reference beyond its stub (distributed/tensor_parallel.py:14-35,

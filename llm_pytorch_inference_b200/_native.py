@@ -73,6 +73,7 @@ SIGNATURES: dict[str, tuple] = {
     "mvb_moe_gather": (_i32, [_vp, _vp, _i64, _vp, _i64, _vp]),
     "mvb_moe_gemm_bf16": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _vp, _vp]),
     "mvb_moe_combine": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "mvb_moe_combine_experts": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
     "mvb_moe_gemm_bf16_experts": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32,
                                          _vp, _vp, _vp]),
     "mvb_tp_moe_combine": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp]),

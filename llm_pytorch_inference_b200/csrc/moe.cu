@@ -404,7 +404,8 @@ __global__ void moe_gather_kernel(__nv_bfloat16* __restrict__ out, const __nv_bf
 // the reference's final[token] += w * out with fp32 routing weights).  8 features per thread.
 __global__ void moe_combine_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ y,
                                    const float* __restrict__ topk_w, const int32_t* __restrict__ topk_ids,
-                                   const int32_t* __restrict__ pair_row, int K, int hidden) {
+                                   const int32_t* __restrict__ pair_row, int K, int hidden, int first_expert,
+                                   int local_experts) {
   pdl_launch_dependents();
   pdl_wait();
   const int b = blockIdx.x;
@@ -425,6 +426,8 @@ __global__ void moe_combine_kernel(__nv_bfloat16* __restrict__ out, const __nv_b
     for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
     for (int kk = 0; kk < K; ++kk) {
       const int k = ord[kk];
+      const int e = topk_ids[b * K + k];
+      if (e < first_expert || e - first_expert >= local_experts) continue;   // another GPU's expert
       const float w = topk_w[b * K + k];
       const uint4 v = *reinterpret_cast<const uint4*>(y + static_cast<int64_t>(pair_row[b * K + k]) * hidden + i);
       const __nv_bfloat16* ve = reinterpret_cast<const __nv_bfloat16*>(&v);
@@ -626,7 +629,21 @@ extern "C" int mvb_moe_combine(void* out, const void* y, const float* topk_w, co
               "mvb_moe_combine: bad shape or alignment");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return launch("moe_combine", moe_combine_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, st,
-                (__nv_bfloat16*)out, (const __nv_bfloat16*)y, topk_w, topk_ids, pair_row, (int)top_k, (int)hidden);
+                (__nv_bfloat16*)out, (const __nv_bfloat16*)y, topk_w, topk_ids, pair_row, (int)top_k, (int)hidden, 0,
+                kMaxExperts);
+}
+
+extern "C" int mvb_moe_combine_experts(void* out, const void* y, const float* topk_w, const int32_t* topk_ids,
+                                       const int32_t* pair_row, int64_t rows, int64_t top_k, int64_t hidden,
+                                       int64_t first_expert, int64_t local_experts, mvb_stream_t stream) {
+  MVB_REQUIRE(out && y && topk_w && topk_ids && pair_row, "mvb_moe_combine_experts: null pointer");
+  MVB_REQUIRE(rows > 0 && top_k > 0 && top_k <= kMaxTopK && hidden > 0 && hidden % 8 == 0 && aligned(out, 16) &&
+                  aligned(y, 16) && first_expert >= 0 && local_experts > 0,
+              "mvb_moe_combine_experts: bad shape, alignment or expert range");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return launch("moe_combine", moe_combine_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, st,
+                (__nv_bfloat16*)out, (const __nv_bfloat16*)y, topk_w, topk_ids, pair_row, (int)top_k, (int)hidden,
+                (int)first_expert, (int)local_experts);
 }
 
 extern "C" int mvb_tp_moe_combine(mvb_tp_comm* comm, const void* y, const float* topk_w, const int32_t* topk_ids,

@@ -113,20 +113,19 @@ def _attention_rows(runner) -> int:
 
 class BatchedPrefill:
     """Prefill of dense (Qwen3 / Llama-family), Gemma and sparse-MoE models through a
-    ``DecodeRunner``'s weights, tables and KV pool, on one GPU; dense Qwen3 / Llama-family models
-    also on a tensor-parallel group.
+    ``DecodeRunner``'s weights, tables and KV pool, on one GPU or on a tensor-parallel group.
 
     Tensor parallel (``engine.py:253-295`` with the decode step's Megatron split): each rank runs
     its column-parallel q|k|v (writing its own KV heads into its pool), its heads' attention and
     its gate/up slice; the row-parallel o_proj and down_proj outputs are summed over the ranks
     with an NCCL all-reduce in fp32 (a prefill chunk moves [tokens, hidden] per layer, bandwidth
     work that NCCL's ring / NVLS algorithms do well; the decode step's in-kernel exchanges are
-    sized for 64 rows), then residual add + RMSNorm on every rank; the vocab-parallel logits of
-    the last tokens are all-gathered, so every rank samples the same first tokens."""
+    sized for 64 rows), then residual add + RMSNorm on every rank (Gemma: the post-norm of the
+    summed output first); a sparse MoE block runs the rank's experts only and its combined
+    partial is summed the same way; the vocab-parallel logits of the last tokens are
+    all-gathered, so every rank samples the same first tokens."""
 
     def __init__(self, runner, max_tokens: int = 16384):
-        if runner.tp.enabled and (runner.gemma or runner.moe):
-            raise NotImplementedError("tensor-parallel prefill covers dense Qwen3 / Llama-family models")
         self.r = runner
         self.tp = runner.tp
         self.max_tokens = max_tokens
@@ -199,7 +198,7 @@ class BatchedPrefill:
     def _all_reduce(self, y: torch.Tensor) -> None:
         """Sums the ranks' partials of a row-parallel product in fp32, then rounds to bf16 (the
         reference's linear-layer output dtype)."""
-        if self.tp.tp_size == 1:
+        if not self.tp.enabled or self.tp.tp_size == 1:
             return
         import torch.distributed as dist
 
@@ -273,6 +272,15 @@ class BatchedPrefill:
                 with self._timed("norm"):
                     N.check(lib.mvb_fused_add_rmsnorm(xn.data_ptr(), h.data_ptr(), y.data_ptr(), w.ln2[i].data_ptr(),
                                                       T, H, eps, r.plus_one, N.NORM_MODEL, bf, st), "fused_add_rmsnorm")
+                if moe:   # this rank's experts, their combined partial summed over the ranks
+                    self._moe_block(i, T, xn, y)
+                    self._all_reduce(y)
+                    nw = w.ln1[i + 1] if i + 1 < L else w.final_norm
+                    with self._timed("norm"):
+                        N.check(lib.mvb_fused_add_rmsnorm(xn.data_ptr(), h.data_ptr(), y.data_ptr(), nw.data_ptr(), T,
+                                                          H, eps, r.plus_one, N.NORM_MODEL, bf, st),
+                                "fused_add_rmsnorm")
+                    continue
                 self._gemm(act, xn, w.wgu[i], N.EPI_SWIGLU)
                 self._gemm(y, act, w.wdown[i])
                 self._all_reduce(y)
@@ -334,15 +342,18 @@ class BatchedPrefill:
                                       self.expert_off.data_ptr(), self.active.data_ptr(), st), "moe_route")
             N.check(lib.mvb_moe_gather(self.x_sorted.data_ptr(), xn[c0:].data_ptr(), H, self.row_token.data_ptr(),
                                        n * K, st), "moe_gather")
-            N.check(lib.mvb_moe_gemm_bf16(self.h_sorted.data_ptr(), r.Im, self.x_sorted.data_ptr(), H,
-                                          w.egu[i].data_ptr(), 2 * r.Im, H, E, n * K, n, N.EPI_SWIGLU,
-                                          self.expert_off.data_ptr(), self.active.data_ptr(), st), "moe_gemm gate_up")
-            N.check(lib.mvb_moe_gemm_bf16(self.y_sorted.data_ptr(), H, self.h_sorted.data_ptr(), r.Im,
-                                          w.edown[i].data_ptr(), H, r.Im, E, n * K, n, N.EPI_STORE,
-                                          self.expert_off.data_ptr(), self.active.data_ptr(), st), "moe_gemm down")
-            N.check(lib.mvb_moe_combine(out[c0:].data_ptr(), self.y_sorted.data_ptr(), self.topk_w.data_ptr(),
-                                        self.topk_ids.data_ptr(), self.pair_row.data_ptr(), n, K, H, st),
-                    "moe_combine")
+            e0, ne = r.e_first, r.e_local   # all experts on one GPU; this rank's under tensor parallelism
+            N.check(lib.mvb_moe_gemm_bf16_experts(self.h_sorted.data_ptr(), r.Im, self.x_sorted.data_ptr(), H,
+                                                  w.egu[i].data_ptr(), 2 * r.Im, H, E, e0, ne, n * K, n,
+                                                  N.EPI_SWIGLU, self.expert_off.data_ptr(), self.active.data_ptr(),
+                                                  st), "moe_gemm gate_up")
+            N.check(lib.mvb_moe_gemm_bf16_experts(self.y_sorted.data_ptr(), H, self.h_sorted.data_ptr(), r.Im,
+                                                  w.edown[i].data_ptr(), H, r.Im, E, e0, ne, n * K, n, N.EPI_STORE,
+                                                  self.expert_off.data_ptr(), self.active.data_ptr(), st),
+                    "moe_gemm down")
+            N.check(lib.mvb_moe_combine_experts(out[c0:].data_ptr(), self.y_sorted.data_ptr(), self.topk_w.data_ptr(),
+                                                self.topk_ids.data_ptr(), self.pair_row.data_ptr(), n, K, H, e0, ne,
+                                                st), "moe_combine")
         if end is not None:
             end.record()
 
@@ -362,8 +373,10 @@ class BatchedPrefill:
                                               eps, r.plus_one, N.NORM_MODEL, bf, st), "fused_add_rmsnorm")
 
         self._gemm(z, attn, w.wo[i])
+        self._all_reduce(z)   # tensor parallel: the ranks' row-parallel partials (no-op on one GPU)
         post_add_norm(w.ln2[i], w.pre_ff[i])
         self._gemm(gu, xn, w.wgu[i])
         N.check(lib.mvb_fused_mlp(act.data_ptr(), gu.data_ptr(), T, r.I, r.act, bf, st), "fused_mlp")
         self._gemm(z, act, w.wdown[i])
+        self._all_reduce(z)
         post_add_norm(w.post_ff[i], w.ln1[i + 1] if i + 1 < r.L else w.final_norm)

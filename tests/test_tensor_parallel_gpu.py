@@ -138,12 +138,14 @@ def test_fused_layer_exchange_path_on_one_gpu_matches_per_kernel_exchange_path()
     fused.runner.close()
 
 
-def test_tensor_parallel_prefill_on_one_gpu_matches_plain_prefill():
+@pytest.mark.parametrize("arch", ["qwen3-8b", "gemma2-9b", "qwen3-moe-tiny"])
+def test_tensor_parallel_prefill_on_one_gpu_matches_plain_prefill(arch):
     """The tensor-parallel batched prefill with one rank (row-parallel outputs summed over one
-    rank, then residual add + RMSNorm in one kernel) against the one-GPU prefill (residual added
-    in the GEMM epilogue): last-token logits to bf16 rounding, first tokens equal wherever the
-    margin is not a near tie, and the pools' prompt K/V equal to bf16 rounding."""
-    cfg = get_config("qwen3-8b", num_hidden_layers=2)
+    rank, then residual add + RMSNorm in one kernel; the MoE block over the rank's expert range)
+    against the one-GPU prefill (residual added in the GEMM epilogue): last-token logits to bf16
+    rounding, first tokens equal wherever the margin is not a near tie, and the pools' prompt
+    K/V equal to bf16 rounding."""
+    cfg = get_config(arch, num_hidden_layers=2)
     sd = canonical_state_dict(cfg, seed=0, dtype=torch.bfloat16, device="cuda")
     g = torch.Generator().manual_seed(4)
     lens = [40 + 57 * i for i in range(8)]
@@ -208,7 +210,8 @@ def test_expert_parallel_moe_exchange_path_on_one_gpu_matches_plain_moe_step():
 @pytest.mark.parametrize("arch,fused,kv,prefill", [("qwen3-8b", False, None, False), ("gemma2-9b", False, None, False),
                                                    ("qwen3-8b", True, None, False),
                                                    ("qwen3-30b-a3b", False, None, False),
-                                                   ("qwen3-8b", False, 1, False), ("qwen3-8b", False, None, True)])
+                                                   ("qwen3-8b", False, 1, False), ("qwen3-8b", False, None, True),
+                                                   ("gemma2-9b", False, None, True)])
 def test_tp2_matches_tp1_teacher_forced(tmp_path, arch, fused, kv, prefill):
     """kv = 1: one KV head for two ranks (replicated on both; each keeps half of its GQA group of
     8 query heads)."""
