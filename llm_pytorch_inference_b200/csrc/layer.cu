@@ -102,6 +102,7 @@ struct LayerArgs {
   int nranks, rank, rpr;
   const float* recv[2];                   // this rank's receive areas (o_proj, down_proj)
   float* push[2][kTpMaxRanks];            // every rank's receive area of the two pushes
+  SplitKPlan push_plan[2];                // their layout: one (summed) contribution per rank and tile
   __nv_bfloat16* xn_all[kTpMaxRanks];     // every rank's xn
   uint32_t* signal[4][kTpMaxRanks];       // rank q's counter [point][this rank]
   const uint32_t* wait[4];                // this rank's counters [point][0..nranks)
@@ -404,27 +405,50 @@ __device__ void tp_add_norm_row(const LayerArgs& a, const SplitKPlan& p, const f
 // (elementwise.cu's swiglu_gemm_kernel) into a [64 batch rows][64 features] tile (hs), and all
 // 128 threads store it as 16-byte row pieces.  Every thread runs the four epi_sync calls whatever
 // `go` is.
+// Contributor 0's sum of tile row `row`, batch columns c0 .. c0 + 15: its own accumulator (TMEM)
+// first, then contributors 1 .. n-1 in order (the order of sk_sum4), two contributors' loads in
+// flight together.  Sixteen columns at a time keep the sum and the loads in registers.
+__device__ __forceinline__ void reduce_chunk16(const LayerPhase& ph, int t, int n, int c0, int row, uint32_t tb,
+                                               float* v) {
+  uint32_t r[16];
+  tmem_ld_x16(tb + c0, r);
+  tmem_ld_wait();
+#pragma unroll
+  for (int jj = 0; jj < 16; ++jj) {
+    v[jj] = 0.0f;
+    v[jj] += __uint_as_float(r[jj]);
+  }
+  const float* base = ph.partials + (static_cast<int64_t>(t) * ph.plan.maxc * LBN + c0) * LBM + row;
+  constexpr int64_t kContrib = static_cast<int64_t>(LBN) * LBM;
+  for (int q = 1; q < n; q += 2) {
+    const bool two = q + 1 < n;
+    float x0[16], x1[16];
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) x0[jj] = __ldcg(base + q * kContrib + jj * LBM);
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) x1[jj] = two ? __ldcg(base + (q + 1) * kContrib + jj * LBM) : 0.0f;
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) v[jj] += x0[jj];
+    if (two) {
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) v[jj] += x1[jj];
+    }
+  }
+}
+
+// Columns c0 .. c0 + 31 (two 16-column sums).
+__device__ __forceinline__ void reduce_chunk(const LayerPhase& ph, int t, int n, int c0, int row, uint32_t tb,
+                                             float (&v)[32]) {
+  reduce_chunk16(ph, t, n, c0, row, tb, v);
+  reduce_chunk16(ph, t, n, c0 + 16, row, tb, v + 16);
+}
+
 __device__ __forceinline__ void swiglu_tile(const LayerArgs& a, const LayerPhase& ph, int t, int n, uint32_t tb,
                                             int row, int e, bool go, __nv_bfloat16* xs, __nv_bfloat16* hs) {
   for (int c0 = 0; c0 < LBN; c0 += 32) {
     float v[32];
     if (go) {
-      uint32_t r[32];
-      tmem_ld_x32(tb + c0, r);
-      tmem_ld_wait();
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        v[jj] = 0.0f;
-        v[jj] += __uint_as_float(r[jj]);
-      }
-      for (int q = 1; q < n; ++q) {
-        const float* src = ph.partials + ((static_cast<int64_t>(t) * ph.plan.maxc + q) * LBN + c0) * LBM + row;
-        float x[32];
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) x[jj] = __ldcg(src + jj * LBM);
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) v[jj] += x[jj];
-      }
+      reduce_chunk(ph, t, n, c0, row, tb, v);
       if (row >= 64) {
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) xs[jj * 64 + row - 64] = __float2bfloat16_rn(v[jj]);
@@ -448,6 +472,25 @@ __device__ __forceinline__ void swiglu_tile(const LayerArgs& a, const LayerPhase
       if (b < a.m)
         *reinterpret_cast<uint4*>(a.h + static_cast<int64_t>(b) * a.inter + t * 64 + piece * 8) =
             reinterpret_cast<const uint4*>(hs)[idx];
+    }
+  }
+}
+
+// Tensor parallel: contributor 0 of a row-parallel tile sums the tile over this rank's
+// contributors and pushes the sum of every batch row to the receive area of the row's owner
+// (one-contributor layout `pp`), so NVLink carries one tile per rank, not one per contributor.
+__device__ __forceinline__ void push_tile(const LayerArgs& a, const LayerPhase& ph, const SplitKPlan& pp,
+                                          float* const* dst, int t, int n, uint32_t tb, int row) {
+  for (int c0 = 0; c0 < LBN; c0 += 16) {
+    float v[16];
+    reduce_chunk16(ph, t, n, c0, row, tb, v);
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) {
+      const int b = c0 + jj;
+      if (b < a.m) {
+        const int q = b / a.rpr, bl = b - q * a.rpr;
+        dst[q][sk_push_offset(pp, a.rank, t, 0, a.rpr, bl, row)] = v[jj];
+      }
     }
   }
 }
@@ -691,7 +734,10 @@ __global__ void __launch_bounds__(kLayerThreads, 2)
       const int64_t total = static_cast<int64_t>(ph.plan.tiles) * kbl;
       int64_t kb = kb0[p];
       const int64_t kb_end = kb0[p] + nkb[p];
-      const bool fix = ph.consumer == kConsSwiglu;   // tiles finished in contributor 0's epilogue
+      // tiles finished in contributor 0's epilogue: SwiGLU, or (tensor parallel) the push of the
+      // rank's sum of a row-parallel tile
+      const bool fix = ph.consumer == kConsSwiglu || ph.consumer == kConsTpAddNorm;
+      const uint32_t stamp = gen0 + 1 + static_cast<uint32_t>(p);   // this launch's, this phase's flags
       while (kb < kb_end) {
         // A warp whose wait gave up (dead) skips the work of the remaining segments but still
         // takes part in their epi_sync calls, which every thread of the 128 must reach.
@@ -706,34 +752,23 @@ __global__ void __launch_bounds__(kLayerThreads, 2)
         const uint32_t tb = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + static_cast<uint32_t>(ab * LBN);
         const int j = cta - sk_cta_of(static_cast<int64_t>(t) * kbl, total, ph.plan.grid);
         if (fix && j == 0) {
-          // the other contributors' partials of tile t, then SwiGLU
+          // the other contributors' partials of tile t, then SwiGLU or the push
           const int n = sk_count(ph.plan, t);
           if (e == 0) {
             bool ok = !*abort_flag;
             for (int q = 1; ok && q < n; ++q)
-              ok = wait_flag(a.flags + static_cast<int64_t>(t) * ph.plan.maxc + q, gen0 + 1, abort_flag, a.err);
+              ok = wait_flag(a.flags + static_cast<int64_t>(t) * ph.plan.maxc + q, stamp, abort_flag, a.err);
             *go_s = ok;
           }
           epi_sync();
-          swiglu_tile(a, ph, t, n, tb, row, e, *go_s && !dead, xs, hs);
+          if (ph.consumer == kConsSwiglu) {
+            swiglu_tile(a, ph, t, n, tb, row, e, *go_s && !dead, xs, hs);
+          } else if (*go_s && !dead) {
+            const int pi = p == 0 ? 0 : 1;
+            push_tile(a, ph, a.push_plan[pi], a.push[pi], t, n, tb, row);
+          }
         } else {
-          if (!dead && ph.consumer == kConsTpAddNorm) {
-            // push: batch row b's partial to its owner's receive area
-            float* const* dst = a.push[p == 0 ? 0 : 1];
-            for (int c0 = 0; c0 < LBN; c0 += 32) {
-              uint32_t r[32];
-              tmem_ld_x32(tb + c0, r);
-              tmem_ld_wait();
-#pragma unroll
-              for (int jj = 0; jj < 32; ++jj) {
-                const int b = c0 + jj;
-                if (b < a.m) {
-                  const int q = b / a.rpr, bl = b - q * a.rpr;
-                  dst[q][sk_push_offset(ph.plan, a.rank, t, j, a.rpr, bl, row)] = __uint_as_float(r[jj]);
-                }
-              }
-            }
-          } else if (!dead) {
+          if (!dead) {
             float* part = ph.partials + (static_cast<int64_t>(t) * ph.plan.maxc + j) * LBN * LBM;
             for (int c0 = 0; c0 < LBN; c0 += 32) {
               uint32_t r[32];
@@ -747,7 +782,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2)
             // the tile's reducer may read this partial once the flag holds the launch's stamp
             epi_sync();
             if (e == 0 && !*abort_flag)
-              st_release_gpu(a.flags + static_cast<int64_t>(t) * ph.plan.maxc + j, gen0 + 1);
+              st_release_gpu(a.flags + static_cast<int64_t>(t) * ph.plan.maxc + j, stamp);
           }
         }
         if (!dead) {
@@ -805,7 +840,8 @@ __global__ void __launch_bounds__(kLayerThreads, 2)
         if (!xrank(k0, true)) break;      // ... and every rank's arrived
         if (p == 0 && e == 0) pdl_launch_dependents();
         for (int bl = cta; bl < a.rpr; bl += G)
-          tp_add_norm_row(a, ph.plan, a.recv[p == 0 ? 0 : 1], a.norm_w[p == 0 ? 0 : 1], bl, e, red, hs);
+          tp_add_norm_row(a, a.push_plan[p == 0 ? 0 : 1], a.recv[p == 0 ? 0 : 1], a.norm_w[p == 0 ? 0 : 1], bl, e,
+                          red, hs);
         if (!meet(true)) break;           // this rank's owned rows written into every rank's xn
         if (!xrank(k0 + 1, p + 1 < a.nphase)) break;   // ... and every owner's (read by TMA next)
         continue;
@@ -907,9 +943,12 @@ extern "C" int64_t mvb_decoder_layer_workspace_bytes(int64_t m, int64_t hidden, 
       splitk_plan_ctas(m, static_cast<int>((inter + 63) / 64), hidden, G),
       splitk_plan_ctas(m, static_cast<int>((hidden + LBM - 1) / LBM), inter, G),
       splitk_plan_ctas(m, static_cast<int>((qkv_dim + LBM - 1) / LBM), hidden, G)};
-  for (const SplitKPlan& p : plans) best = std::max(best, splitk_partials_bytes(p));
-  return (best + 255) / 256 * 256 + (m * kNormChunks * 4 + 255) / 256 * 256 +
-         (static_cast<int64_t>(plans[1].tiles) * plans[1].maxc * 4 + 255) / 256 * 256;
+  int64_t nflags = 0;
+  for (const SplitKPlan& p : plans) {
+    best = std::max(best, splitk_partials_bytes(p));
+    nflags = std::max(nflags, static_cast<int64_t>(p.tiles) * p.maxc);
+  }
+  return (best + 255) / 256 * 256 + (m * kNormChunks * 4 + 255) / 256 * 256 + (nflags * 4 + 255) / 256 * 256;
 }
 
 namespace {
@@ -976,22 +1015,23 @@ int layer_tail_impl(const TpLayerCall* tp, const void* attn, int64_t attn_stride
   }
   int points[4] = {0, 0, 0, 0};
   if (tp) {
-    // row-parallel o_proj / down_proj: the push split of the per-kernel path (the receive areas
-    // are sized by mvb_tp_recv_bytes for it)
+    // row-parallel o_proj / down_proj: the whole grid's stream-K split (as one GPU), each tile
+    // summed over this rank's contributors by its contributor 0, which pushes one fp32 tile per
+    // rank (a one-k-block plan's layout, which fits the receive areas mvb_tp_recv_bytes sizes for
+    // the per-kernel path's push split)
     mvb_tp_comm* c = tp->comm;
     const int nr = c->nranks;
     MVB_REQUIRE(m % nr == 0, "mvb_tp_decoder_layer_tail: batch %lld not a multiple of %d ranks", (long long)m, nr);
     a.nranks = nr;
     a.rank = c->rank;
     a.rpr = static_cast<int>(m / nr);
-    a.ph[0].plan = splitk_plan_push(m, hidden, q_dim, sms, nr);
     a.ph[0].consumer = kConsTpAddNorm;
-    a.ph[2].plan = splitk_plan_push(m, hidden, inter, sms, nr);
     a.ph[2].consumer = kConsTpAddNorm;
-    MVB_REQUIRE(a.ph[0].plan.grid <= G && a.ph[2].plan.grid <= G, "mvb_tp_decoder_layer_tail: push split");
     const int64_t off[2] = {tp->recv_o, tp->recv_down};
     for (int k = 0; k < 2; ++k) {
-      const int64_t bytes = splitk_push_bytes(a.ph[k == 0 ? 0 : 2].plan, nr, a.rpr);
+      a.push_plan[k] = splitk_plan_push(m, hidden, kSplitBK, sms, nr);
+      MVB_REQUIRE(a.push_plan[k].maxc == 1, "mvb_tp_decoder_layer_tail: push layout");
+      const int64_t bytes = splitk_push_bytes(a.push_plan[k], nr, a.rpr);
       MVB_REQUIRE(off[k] >= kTpSignalBytes && off[k] % 16 == 0 && off[k] + bytes <= c->heap_bytes,
                   "mvb_tp_decoder_layer_tail: receive area outside the heap");
       a.recv[k] = reinterpret_cast<const float*>(c->base[c->rank] + off[k]);
@@ -1009,14 +1049,15 @@ int layer_tail_impl(const TpLayerCall* tp, const void* attn, int64_t attn_stride
     }
     a.epoch = c->epoch;
   }
-  int64_t need = 0;
+  int64_t need = 0, nflags = 0;
   for (int p = 0; p < a.nphase; ++p) {
     a.ph[p].partials = static_cast<float*>(workspace);
-    if (a.ph[p].consumer != kConsTpAddNorm) need = std::max(need, splitk_partials_bytes(a.ph[p].plan));
+    need = std::max(need, splitk_partials_bytes(a.ph[p].plan));
+    nflags = std::max(nflags, static_cast<int64_t>(a.ph[p].plan.tiles) * a.ph[p].plan.maxc);
   }
   const int64_t ss_off = (need + 255) / 256 * 256;
   const int64_t flags_off = ss_off + (m * kNormChunks * 4 + 255) / 256 * 256;
-  need = flags_off + static_cast<int64_t>(a.ph[1].plan.tiles) * a.ph[1].plan.maxc * 4;
+  need = flags_off + nflags * 4;
   MVB_REQUIRE(workspace_bytes >= need, "mvb_decoder_layer_tail: workspace %lld < %lld bytes",
               (long long)workspace_bytes, (long long)need);
   a.ss = reinterpret_cast<float*>(static_cast<char*>(workspace) + ss_off);
