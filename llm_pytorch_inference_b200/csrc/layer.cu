@@ -9,8 +9,8 @@
 //
 //   GEMM phase  o_proj  (X = attention output)      -> fp32 split-K partials
 //   consumer    residual += o_proj; xn = RMSNorm(residual; post_attention_layernorm)
-//   GEMM phase  gate_up (X = xn, SwiGLU-paired rows) -> partials
-//   consumer    h = silu(gate) * up
+//   GEMM phase  gate_up (X = xn, SwiGLU-paired rows) -> h = silu(gate) * up, by each tile's
+//               contributor 0 in its epilogue (no separate pass)
 //   GEMM phase  down    (X = h)                     -> partials
 //   consumer    residual += down;  xn = RMSNorm(residual; next input_layernorm | final norm)
 //   GEMM phase  q|k|v of the next layer (X = xn)    -> partials      (absent after the last layer)
@@ -24,8 +24,14 @@
 // consumers in contributor order (deterministic); the results agree with the unfused kernels to
 // bf16 rounding (a different split and a different order of the sum of squares).
 //
-// Every wait is bounded (mbarrier waits, grid barriers): a wait that runs out sets the
-// kDevWaitTimeout status bit, the CTA unwinds, waits for its copies in flight and frees its TMEM.
+// Tensor parallel (mvb_tp_decoder_layer_tail): the same phases on a rank's shards; o_proj and
+// down_proj are row-parallel, so each tile's contributor 0 pushes the rank's sum of the tile to
+// the owners of its batch rows, the owners add and normalise their rows and write them into
+// every rank's xn, and signal points (system-scope release / acquire) order the ranks.
+//
+// Every wait is bounded (mbarrier waits, grid barriers, contributor flags, other ranks' signals):
+// a wait that runs out sets the kDevWaitTimeout status bit, the CTA unwinds, waits for its copies
+// in flight and frees its TMEM.
 #include <algorithm>
 
 #include "common.cuh"
@@ -75,7 +81,7 @@ struct LayerArgs {
   const __nv_bfloat16* norm_w[2]; // RMSNorm weights of the two add+norm consumers
   float eps;
   float* ss;                      // [m * kNormChunks] per-chunk sums of squares
-  unsigned* flags;                // [tiles][maxc] of the SwiGLU phase: partial written (launch stamp)
+  unsigned* flags;                // [tiles][maxc] of a reduced phase: partial written (launch + phase stamp)
   // QK-norm + RoPE + KV write of the next layer
   __nv_bfloat16* q_out;
   __nv_bfloat16* kv;
