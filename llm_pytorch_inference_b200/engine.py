@@ -191,6 +191,10 @@ class RunningBatch:
         """``engine.py:299-309``: one more token per decoded sequence, a new block when needed;
         a sequence the pool cannot grow is freed and leaves the batch before the step runs.
         Held rows (sequences that joined in this step) are written as padding rows."""
+        if not self.held and self._grow_fast():
+            self.last_step_seqs = list(self.seqs)
+            self._off[0] = self.step_count
+            return
         dropped = False
         for row, s in enumerate(list(self.seqs)):
             if s in self.held:
@@ -215,17 +219,49 @@ class RunningBatch:
         # the sampling offset of this step (fresh Philox uniforms every step)
         self._off[0] = self.step_count
 
+    def _grow_fast(self) -> bool:
+        """The common step (no held rows): ``KVCacheManager.append_token`` for every row in row
+        order, with its bookkeeping inlined.  Gives up (returns False, nothing changed) when some
+        row would need a block beyond the pool or the block table, where the general path frees
+        and drops sequences in the reference's order."""
+        kv, bs, mb = self.kv, self.kv.block_size, self.max_blocks
+        tables, ntok = kv.block_tables, kv.seq_num_tokens
+        need_blocks = 0
+        for s in self.seqs:
+            n = ntok[s] + 1
+            if n > len(tables[s]) * bs:
+                if len(tables[s]) + 1 > mb:
+                    return False
+                need_blocks += 1
+        if need_blocks > len(kv.free_blocks):
+            return False
+        free = kv.free_blocks
+        for row, s in enumerate(self.seqs):
+            n = ntok[s] + 1
+            bt = tables[s]
+            if n > len(bt) * bs:
+                bt.append(free.popleft())
+                self._bt[row, len(bt) - 1] = bt[-1]
+            ntok[s] = n
+        return True
+
     def _commit(self, out: list[int]) -> None:
         """The sampled tokens (one per row of the step) become each decoded row's last token
         and positions advance by one; then every sequence this step finished is freed in row
         order and its row removed (``engine.py:352-359``)."""
         rows = list(self.seqs)
-        for row, s in enumerate(rows):
-            if s in self.held:
-                continue
-            self.tokens[s].append(int(out[row]))
-            self._ids[row] = int(out[row])
         n = len(rows)
+        if self.held:
+            for row, s in enumerate(rows):
+                if s in self.held:
+                    continue
+                self.tokens[s].append(int(out[row]))
+                self._ids[row] = int(out[row])
+        else:
+            toks = [int(t) for t in out[:n]]
+            for s, t in zip(rows, toks):
+                self.tokens[s].append(t)
+            self._ids[:n] = toks
         self._pos[:n] += 1
         self._ctx[:n] += 1
         self.step_count += 1
