@@ -108,3 +108,35 @@ def test_pool_exhaustion_during_growth_drops_the_sequence():
     rb.plan_step([5, 6])
     assert rb.finish_reason == {0: "abort"} and rb.seqs == [1] and rb.last_step_seqs == [1]
     assert kv.get_block_table(1)[-1] == table0[0]
+
+
+@pytest.mark.parametrize("num_blocks,seed", [(40, 0), (29, 3), (200, 1)])
+def test_step_fast_path_equals_the_general_path(num_blocks, seed):
+    """The common step's bookkeeping fast path (no held rows, every block growth fits) against
+    the general per-row path on the same steps: identical metadata, free list, block tables and
+    finish reasons, including steps where the pool runs dry and sequences are dropped."""
+    runs = []
+    for fast in (True, False):
+        kv, rb = _batch(num_blocks, seed)
+        if not fast:
+            rb._grow_fast = lambda: False
+        r2 = random.Random(seed)
+        for s in range(B):
+            rb.add_sequence(s, [r2.randrange(1000) for _ in range(r2.randrange(5, 60))],
+                            max_tokens=r2.choice([None, 20, 45]), stop_token_ids=[7] if s % 3 == 0 else ())
+        rb.start()
+        snaps = []
+        r3 = random.Random(seed + 100)
+        for _ in range(70):
+            if not rb.seqs:
+                break
+            toks = [r3.randrange(50) for _ in range(B)]
+            snaps.append(rb.plan_step(toks).copy())
+        runs.append((snaps, list(kv.free_blocks), dict(kv.block_tables), dict(rb.finish_reason)))
+    (sa, fa, ta, ra), (sb, fb, tb, rb_) = runs
+    assert len(sa) == len(sb)
+    for a, b in zip(sa, sb):
+        assert np.array_equal(a, b)
+    assert fa == fb and ta == tb and ra == rb_
+    if num_blocks < 100:   # the tight pools run dry: some sequences are dropped while growing
+        assert "abort" in ra.values(), ra
