@@ -107,6 +107,12 @@ __host__ __device__ constexpr int attn_wph() {
   return (cw / HKV) < GROUP * (D / 32) ? (cw / HKV) : GROUP * (D / 32);
 }
 
+// CTAs per SM: two for D = 128 groups of one or two KV heads (tensor-parallel shards), each with
+// half the stage memory; the bytes in flight per SM stay the same, but two producers and two
+// consumer sets overlap one CTA's ramp, merges and tail with the other's streaming, and the
+// finer split of the block ranges evens out when the CTAs finish.  One for the rest.
+__host__ __device__ constexpr int attn_ctas_per_sm(int hkv, int d) { return (d == 128 && hkv <= 2) ? 2 : 1; }
+
 // One TMA copy per block (D = 128 blocks of <= 2 heads) or one per (K|V, part).  Several small
 // copies keep more requests in flight than one large multi-dimensional box: at D = 256 the split
 // form streams at 6.7 TB/s where one 32 KB box per stage reached 3.9 TB/s.
@@ -140,7 +146,7 @@ __host__ __device__ constexpr int attn_combine_bytes() {
 // CAP: soft-capped scores (a compile-time switch: the tanh would otherwise be evaluated for
 // every score of every launch).
 template <int GROUP, int HKV, int STAGES, int D, bool CAP>
-__global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, 1)
+__global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, attn_ctas_per_sm(HKV, D))
     paged_attention_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs a) {
   constexpr int NP = D / 64;                                      // 64-dim parts of a head
   constexpr int STAGE_BYTES = 2 * NP * HKV * HALF_BYTES_PER_HEAD;  // K and V parts of HKV heads
@@ -683,7 +689,8 @@ constexpr int attn_fixed_smem() {
          attn_combine_bytes<GROUP, HKV, D>() + 1024;
 }
 
-// As many stages as fit in 227 KB next to the rest (at most 24), rounded down to a multiple of
+// As many stages as fit next to the rest (at most 24) in 227 KB, or in 112 KB when two CTAs share
+// an SM (attn_ctas_per_sm), rounded down to a multiple of
 // the warps per head: iteration `it` uses stage it % STAGES and warp it % W of each head, so with
 // STAGES % W == 0 a stage only ever serves the same warp of each head, in iteration order.  A warp
 // therefore never waits on a stage more than one phase ahead of its last use, where the
@@ -692,7 +699,8 @@ template <int GROUP, int HKV, int D>
 constexpr int attn_stages() {
   constexpr int stage = 2 * (D / 64) * HKV * HALF_BYTES_PER_HEAD;
   constexpr int W = attn_wph<GROUP, HKV, D>();
-  constexpr int n = (227 * 1024 - attn_fixed_smem<GROUP, HKV, D>()) / stage;
+  constexpr int budget = attn_ctas_per_sm(HKV, D) == 2 ? 112 * 1024 : 227 * 1024;
+  constexpr int n = (budget - attn_fixed_smem<GROUP, HKV, D>()) / stage;
   constexpr int c = n > 24 ? 24 : n;
   return c / W * W;
 }
@@ -778,9 +786,11 @@ extern "C" int64_t mvb_paged_attention_workspace_bytes(int64_t batch, int64_t nu
                                                        int device) {
   int sms = mvb_num_sms(device);
   if (sms <= 0) sms = 148;
-  // counters: one per (sequence, head group); head groups <= KV heads <= query heads
-  return attn_counters_bytes(batch * num_q_heads) + 2LL * sms * num_q_heads * 8 +
-         2LL * sms * num_q_heads * head_dim * 4 + 256;
+  // counters: one per (sequence, head group); head groups <= KV heads <= query heads; partials
+  // for two slots per CTA, up to two CTAs per SM
+  const int64_t grid = 2LL * sms;
+  return attn_counters_bytes(batch * num_q_heads) + 2LL * grid * num_q_heads * 8 +
+         2LL * grid * num_q_heads * head_dim * 4 + 256;
 }
 
 extern "C" int mvb_paged_attention_decode_ex(void* out, int64_t out_stride, const void* q, int64_t q_stride,
@@ -818,7 +828,8 @@ extern "C" int mvb_paged_attention_decode_ex(void* out, int64_t out_stride, cons
   // across calls of different batch sizes sharing one buffer; the kernel leaves them zero).
   const int64_t ws_end = workspace_bytes / 256 * 256;
   const int64_t cbytes = attn_counters_bytes(batch * nhg);
-  const int64_t need = cbytes + 2LL * sms * num_q_heads * 8 + 2LL * sms * num_q_heads * head_dim * 4;
+  const int grid = sms * attn_ctas_per_sm(static_cast<int>(hs), static_cast<int>(head_dim));
+  const int64_t need = cbytes + 2LL * grid * num_q_heads * 8 + 2LL * grid * num_q_heads * head_dim * 4;
   MVB_REQUIRE(ws_end >= need, "mvb_paged_attention_decode: workspace %lld < %lld", (long long)workspace_bytes,
               (long long)need);
 
@@ -844,13 +855,12 @@ extern "C" int mvb_paged_attention_decode_ex(void* out, int64_t out_stride, cons
   a.cap_log2 = softcap > 0.0f ? softcap * kLog2e : 0.0f;
   char* ws = static_cast<char*>(workspace);
   a.partial_ml = reinterpret_cast<float2*>(ws);
-  a.partial_o = reinterpret_cast<float*>(ws + 2LL * sms * num_q_heads * 8);
+  a.partial_o = reinterpret_cast<float*>(ws + 2LL * grid * num_q_heads * 8);
   a.counters = reinterpret_cast<int*>(ws + ws_end - cbytes);
   a.err = device_status_ptr();
-  // Grid: one persistent CTA per SM (192 KB of stages each); never more CTAs than blocks.
-  // The block total is only known on the device, so the grid is the SM count and CTAs
-  // with an empty range exit after the prologue.
-  const int grid = sms;
+  // Grid: persistent CTAs, one per SM (192 KB of stages each) or two (attn_ctas_per_sm); never
+  // more CTAs than blocks.  The block total is only known on the device, so the grid is fixed
+  // and CTAs with an empty range exit after the prologue.
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int g = static_cast<int>(group);
   if (head_dim == 256) {
@@ -925,8 +935,10 @@ extern "C" int mvb_paged_attention_decode_noalloc(void* out, int64_t out_stride,
   MVB_REQUIRE(sms > 0, "mvb_paged_attention_decode_noalloc: no device");
   MVB_REQUIRE(num_q_heads > 0 && num_kv_heads > 0 && head_dim > 0 && batch >= 0 && batch <= 4096,
               "mvb_paged_attention_decode_noalloc: bad shape");
-  const int64_t cbytes = attn_counters_bytes(batch * (num_kv_heads / attn_heads_per_group(num_kv_heads, head_dim)));
-  const int64_t need = cbytes + 2LL * sms * num_q_heads * 8 + 2LL * sms * num_q_heads * head_dim * 4;
+  const int64_t hs = attn_heads_per_group(num_kv_heads, head_dim);
+  const int64_t cbytes = attn_counters_bytes(batch * (num_kv_heads / hs));
+  const int64_t grid = static_cast<int64_t>(sms) * attn_ctas_per_sm(static_cast<int>(hs), static_cast<int>(head_dim));
+  const int64_t need = cbytes + 2LL * grid * num_q_heads * 8 + 2LL * grid * num_q_heads * head_dim * 4;
   if (need > kNoAllocScratchBytes)
     return fail(MVB_ERR_UNSUPPORTED,
                 "mvb_paged_attention_decode_noalloc: %lld query heads x %lld dims on %d SMs need %lld bytes of "
