@@ -107,11 +107,13 @@ __host__ __device__ constexpr int attn_wph() {
   return (cw / HKV) < GROUP * (D / 32) ? (cw / HKV) : GROUP * (D / 32);
 }
 
-// CTAs per SM: two for D = 128 groups of one or two KV heads (tensor-parallel shards), each with
-// half the stage memory; the bytes in flight per SM stay the same, but two producers and two
-// consumer sets overlap one CTA's ramp, merges and tail with the other's streaming, and the
-// finer split of the block ranges evens out when the CTAs finish.  One for the rest.
-__host__ __device__ constexpr int attn_ctas_per_sm(int hkv, int d) { return (d == 128 && hkv <= 2) ? 2 : 1; }
+// CTAs per SM: two for D = 128 groups of one or two KV heads (tensor-parallel shards) when the
+// launch has at most kDualMaxPairs (sequence, head group) pairs, each CTA with about half the
+// stage memory; two producers and two consumer sets per SM overlap one CTA's ramp, merges and
+// tail with the other's streaming, and the finer split of the block ranges evens out when the
+// CTAs finish.  One for the rest.
+constexpr int kDualMaxPairs = 512;
+__host__ __device__ constexpr bool attn_dual_for(int hkv, int d) { return d == 128 && hkv <= 2; }
 
 // One TMA copy per block (D = 128 blocks of <= 2 heads) or one per (K|V, part).  Several small
 // copies keep more requests in flight than one large multi-dimensional box: at D = 256 the split
@@ -145,8 +147,8 @@ __host__ __device__ constexpr int attn_combine_bytes() {
 
 // CAP: soft-capped scores (a compile-time switch: the tanh would otherwise be evaluated for
 // every score of every launch).
-template <int GROUP, int HKV, int STAGES, int D, bool CAP>
-__global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, attn_ctas_per_sm(HKV, D))
+template <int GROUP, int HKV, int STAGES, int D, bool CAP, int CPS>
+__global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, CPS)
     paged_attention_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs a) {
   constexpr int NP = D / 64;                                      // 64-dim parts of a head
   constexpr int STAGE_BYTES = 2 * NP * HKV * HALF_BYTES_PER_HEAD;  // K and V parts of HKV heads
@@ -675,76 +677,85 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, at
 }
 
 // Most (sequence, head group) pairs one launch takes: their block prefix sums live in shared
-// memory, so at D = 256 (32 KB stages) the bound is lower to leave room for a sixth stage.
-template <int D>
+// memory, so at D = 256 (32 KB stages) the bound is lower to leave room for a sixth stage, and
+// the two-CTA form (CPS = 2) keeps kDualMaxPairs.
+template <int D, int CPS>
 constexpr int attn_max_pairs() {
-  return D == 128 ? 4096 : 1024;
+  return CPS == 2 ? kDualMaxPairs : (D == 128 ? 4096 : 1024);
 }
 
 // Shared memory other than the stages, at the largest batch: barriers, the block prefix sums,
 // the merge scratch, the per-head combine and the 1 KB alignment slack.
-template <int GROUP, int HKV, int D>
+template <int GROUP, int HKV, int D, int CPS>
 constexpr int attn_fixed_smem() {
-  return 2 * 8 * 32 + 16 + 4 * (attn_max_pairs<D>() + 1) + 16 + 4 * attn_merge_floats<GROUP, HKV>() + 16 +
+  return 2 * 8 * 32 + 16 + 4 * (attn_max_pairs<D, CPS>() + 1) + 16 + 4 * attn_merge_floats<GROUP, HKV>() + 16 +
          attn_combine_bytes<GROUP, HKV, D>() + 1024;
 }
 
 // As many stages as fit next to the rest (at most 24) in 227 KB, or in 112 KB when two CTAs share
-// an SM (attn_ctas_per_sm), rounded down to a multiple of
+// an SM (CPS = 2), rounded down to a multiple of
 // the warps per head: iteration `it` uses stage it % STAGES and warp it % W of each head, so with
 // STAGES % W == 0 a stage only ever serves the same warp of each head, in iteration order.  A warp
 // therefore never waits on a stage more than one phase ahead of its last use, where the
 // mbarrier's parity would alias a stale phase as complete.
-template <int GROUP, int HKV, int D>
+template <int GROUP, int HKV, int D, int CPS>
 constexpr int attn_stages() {
   constexpr int stage = 2 * (D / 64) * HKV * HALF_BYTES_PER_HEAD;
   constexpr int W = attn_wph<GROUP, HKV, D>();
-  constexpr int budget = attn_ctas_per_sm(HKV, D) == 2 ? 112 * 1024 : 227 * 1024;
-  constexpr int n = (budget - attn_fixed_smem<GROUP, HKV, D>()) / stage;
+  constexpr int budget = CPS == 2 ? 112 * 1024 : 227 * 1024;
+  constexpr int n = (budget - attn_fixed_smem<GROUP, HKV, D, CPS>()) / stage;
   constexpr int c = n > 24 ? 24 : n;
   return c / W * W;
 }
 
-template <int GROUP, int HKV, int D>
+template <int GROUP, int HKV, int D, int CPS>
 size_t attn_smem(int nv) {
-  return static_cast<size_t>(attn_stages<GROUP, HKV, D>()) * 2 * (D / 64) * HKV * HALF_BYTES_PER_HEAD + 2 * 8 * 32 +
-         16 + 4 * (nv + 1) + 16 + 4 * attn_merge_floats<GROUP, HKV>() + 16 + attn_combine_bytes<GROUP, HKV, D>() +
-         1024;
+  return static_cast<size_t>(attn_stages<GROUP, HKV, D, CPS>()) * 2 * (D / 64) * HKV * HALF_BYTES_PER_HEAD +
+         2 * 8 * 32 + 16 + 4 * (nv + 1) + 16 + 4 * attn_merge_floats<GROUP, HKV>() + 16 +
+         attn_combine_bytes<GROUP, HKV, D>() + 1024;
 }
 
-template <int GROUP, int HKV, int D, bool CAP>
-int launch_attn_cap(const CUtensorMap& tm, const AttnArgs& a, int grid, cudaStream_t st) {
-  constexpr int S = attn_stages<GROUP, HKV, D>();
+template <int GROUP, int HKV, int D, bool CAP, int CPS>
+int launch_attn_cps(const CUtensorMap& tm, const AttnArgs& a, int grid, cudaStream_t st) {
+  constexpr int S = attn_stages<GROUP, HKV, D, CPS>();
   static_assert(S >= 2, "two stages must fit");
   constexpr int NT = (HKV * attn_wph<GROUP, HKV, D>() + 1) * 32;
-  const size_t smem = attn_smem<GROUP, HKV, D>(a.batch * a.nhg);
+  const size_t smem = attn_smem<GROUP, HKV, D, CPS>(a.batch * a.nhg);
   // Raise the kernel's dynamic-smem limit once per device (to the largest pair count), so no
   // attribute call happens while a stream is being captured into a graph.
   static unsigned long long done_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !(done_mask & (1ull << dev))) {
-    MVB_TRY(set_smem(paged_attention_kernel<GROUP, HKV, S, D, CAP>,
-                     attn_smem<GROUP, HKV, D>(attn_max_pairs<D>()), "paged_attention: smem attribute"));
+    MVB_TRY(set_smem(paged_attention_kernel<GROUP, HKV, S, D, CAP, CPS>,
+                     attn_smem<GROUP, HKV, D, CPS>(attn_max_pairs<D, CPS>()), "paged_attention: smem attribute"));
     if (dev < 64) done_mask |= 1ull << dev;
   }
-  return launch("paged_attention_decode", paged_attention_kernel<GROUP, HKV, S, D, CAP>, dim3(grid), dim3(NT), smem,
-                st, tm, a);
+  return launch("paged_attention_decode", paged_attention_kernel<GROUP, HKV, S, D, CAP, CPS>, dim3(grid), dim3(NT),
+                smem, st, tm, a);
+}
+
+template <int GROUP, int HKV, int D, bool CAP>
+int launch_attn_cap(const CUtensorMap& tm, const AttnArgs& a, int grid, bool dual, cudaStream_t st) {
+  if constexpr (attn_dual_for(HKV, D)) {
+    if (dual) return launch_attn_cps<GROUP, HKV, D, CAP, 2>(tm, a, grid, st);
+  }
+  return launch_attn_cps<GROUP, HKV, D, CAP, 1>(tm, a, grid, st);
 }
 
 template <int GROUP, int HKV, int D>
-int launch_attn(const CUtensorMap& tm, const AttnArgs& a, int grid, cudaStream_t st) {
-  return a.cap_log2 > 0.0f ? launch_attn_cap<GROUP, HKV, D, true>(tm, a, grid, st)
-                           : launch_attn_cap<GROUP, HKV, D, false>(tm, a, grid, st);
+int launch_attn(const CUtensorMap& tm, const AttnArgs& a, int grid, bool dual, cudaStream_t st) {
+  return a.cap_log2 > 0.0f ? launch_attn_cap<GROUP, HKV, D, true>(tm, a, grid, dual, st)
+                           : launch_attn_cap<GROUP, HKV, D, false>(tm, a, grid, dual, st);
 }
 
 template <int HKV, int D>
-int dispatch_group(int group, const CUtensorMap& tm, const AttnArgs& a, int grid, cudaStream_t st) {
+int dispatch_group(int group, const CUtensorMap& tm, const AttnArgs& a, int grid, bool dual, cudaStream_t st) {
   switch (group) {
-    case 1: return launch_attn<1, HKV, D>(tm, a, grid, st);
-    case 2: return launch_attn<2, HKV, D>(tm, a, grid, st);
-    case 4: return launch_attn<4, HKV, D>(tm, a, grid, st);
-    case 8: return launch_attn<8, HKV, D>(tm, a, grid, st);
+    case 1: return launch_attn<1, HKV, D>(tm, a, grid, dual, st);
+    case 2: return launch_attn<2, HKV, D>(tm, a, grid, dual, st);
+    case 4: return launch_attn<4, HKV, D>(tm, a, grid, dual, st);
+    case 8: return launch_attn<8, HKV, D>(tm, a, grid, dual, st);
     default: return fail(MVB_ERR_UNSUPPORTED, "paged attention: %d query heads per KV head", group);
   }
 }
@@ -811,7 +822,7 @@ extern "C" int mvb_paged_attention_decode_ex(void* out, int64_t out_stride, cons
               "mvb_paged_attention_decode: softcap and window must be >= 0");
   const int64_t hs = attn_heads_per_group(num_kv_heads, head_dim);
   const int64_t nhg = num_kv_heads / hs;
-  const int max_pairs = head_dim == 128 ? attn_max_pairs<128>() : attn_max_pairs<256>();
+  const int max_pairs = head_dim == 128 ? attn_max_pairs<128, 1>() : attn_max_pairs<256, 1>();
   MVB_REQUIRE(batch >= 0 && batch * nhg <= max_pairs,
               "mvb_paged_attention_decode: batch %lld x %lld head groups > %d", (long long)batch, (long long)nhg,
               max_pairs);
@@ -828,7 +839,8 @@ extern "C" int mvb_paged_attention_decode_ex(void* out, int64_t out_stride, cons
   // across calls of different batch sizes sharing one buffer; the kernel leaves them zero).
   const int64_t ws_end = workspace_bytes / 256 * 256;
   const int64_t cbytes = attn_counters_bytes(batch * nhg);
-  const int grid = sms * attn_ctas_per_sm(static_cast<int>(hs), static_cast<int>(head_dim));
+  const bool dual = attn_dual_for(static_cast<int>(hs), static_cast<int>(head_dim)) && batch * nhg <= kDualMaxPairs;
+  const int grid = sms * (dual ? 2 : 1);
   const int64_t need = cbytes + 2LL * grid * num_q_heads * 8 + 2LL * grid * num_q_heads * head_dim * 4;
   MVB_REQUIRE(ws_end >= need, "mvb_paged_attention_decode: workspace %lld < %lld", (long long)workspace_bytes,
               (long long)need);
@@ -858,20 +870,20 @@ extern "C" int mvb_paged_attention_decode_ex(void* out, int64_t out_stride, cons
   a.partial_o = reinterpret_cast<float*>(ws + 2LL * grid * num_q_heads * 8);
   a.counters = reinterpret_cast<int*>(ws + ws_end - cbytes);
   a.err = device_status_ptr();
-  // Grid: persistent CTAs, one per SM (192 KB of stages each) or two (attn_ctas_per_sm); never
+  // Grid: persistent CTAs, one per SM (192 KB of stages each) or two (the dual form); never
   // more CTAs than blocks.  The block total is only known on the device, so the grid is fixed
   // and CTAs with an empty range exit after the prologue.
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int g = static_cast<int>(group);
   if (head_dim == 256) {
-    if (hs == 2) return dispatch_group<2, 256>(g, tm, a, grid, st);
-    return dispatch_group<1, 256>(g, tm, a, grid, st);
+    if (hs == 2) return dispatch_group<2, 256>(g, tm, a, grid, dual, st);
+    return dispatch_group<1, 256>(g, tm, a, grid, dual, st);
   }
   switch (num_kv_heads) {
-    case 1: return dispatch_group<1, 128>(g, tm, a, grid, st);
-    case 2: return dispatch_group<2, 128>(g, tm, a, grid, st);
-    case 4: return dispatch_group<4, 128>(g, tm, a, grid, st);
-    case 8: return dispatch_group<8, 128>(g, tm, a, grid, st);
+    case 1: return dispatch_group<1, 128>(g, tm, a, grid, dual, st);
+    case 2: return dispatch_group<2, 128>(g, tm, a, grid, dual, st);
+    case 4: return dispatch_group<4, 128>(g, tm, a, grid, dual, st);
+    case 8: return dispatch_group<8, 128>(g, tm, a, grid, dual, st);
     default: return fail(MVB_ERR_UNSUPPORTED, "mvb_paged_attention_decode: %lld KV heads", (long long)num_kv_heads);
   }
 }
@@ -937,7 +949,9 @@ extern "C" int mvb_paged_attention_decode_noalloc(void* out, int64_t out_stride,
               "mvb_paged_attention_decode_noalloc: bad shape");
   const int64_t hs = attn_heads_per_group(num_kv_heads, head_dim);
   const int64_t cbytes = attn_counters_bytes(batch * (num_kv_heads / hs));
-  const int64_t grid = static_cast<int64_t>(sms) * attn_ctas_per_sm(static_cast<int>(hs), static_cast<int>(head_dim));
+  const bool dual = attn_dual_for(static_cast<int>(hs), static_cast<int>(head_dim)) && batch * (num_kv_heads / hs) <=
+                    kDualMaxPairs;
+  const int64_t grid = static_cast<int64_t>(sms) * (dual ? 2 : 1);
   const int64_t need = cbytes + 2LL * grid * num_q_heads * 8 + 2LL * grid * num_q_heads * head_dim * 4;
   if (need > kNoAllocScratchBytes)
     return fail(MVB_ERR_UNSUPPORTED,
