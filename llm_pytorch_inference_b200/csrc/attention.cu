@@ -42,7 +42,7 @@ namespace {
 constexpr int BS = 16;       // tokens per block (the reference's block_size)
 constexpr int HALF_BYTES_PER_HEAD = BS * 64 * 2;  // 2 KB: 16 tokens x 64 dims (one part of a head)
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kMergeC = 32;  // contributors merged per round
+constexpr int kEarlyBlocks = 4;  // see the early arrival-count read in the consumer loop
 
 struct AttnArgs {
   __nv_bfloat16* out;
@@ -132,13 +132,6 @@ __device__ __forceinline__ int attn_line(int kv, int part, int h, int tok) {
   return ((kv * NP + part) * HKV + h) * BS + tok;
 }
 
-// Floats of the split-sequence merge scratch: (m, l) pairs, weights, per-head max and
-// denominator, contributor slots.
-template <int GROUP, int HKV>
-__host__ __device__ constexpr int attn_merge_floats() {
-  return (3 * kMergeC + 2) * GROUP * HKV + kMergeC;
-}
-
 // Shared memory of the per-head combine: every consumer warp's (m, l, o) for its GROUP rows.
 template <int GROUP, int HKV, int D>
 __host__ __device__ constexpr int attn_combine_bytes() {
@@ -164,10 +157,8 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, CP
   volatile int* last_flag = abort_flag + 1;
   const int nv = a.batch * a.nhg;  // virtual sequences: (sequence, head group), head groups adjacent
   int* cu = const_cast<int*>(abort_flag + 2);  // [nv + 1] block prefix sums
-  // split-sequence merge scratch and per-head combine (W > 1), each 16-byte aligned (float2 use)
-  float* merge_smem = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(cu + nv + 1) + 15) & ~uintptr_t(15));
-  float* combine_smem = reinterpret_cast<float*>(
-      (reinterpret_cast<uintptr_t>(merge_smem + attn_merge_floats<GROUP, HKV>()) + 15) & ~uintptr_t(15));
+  // per-head combine (W > 1), 16-byte aligned
+  float* combine_smem = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(cu + nv + 1) + 15) & ~uintptr_t(15));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -310,6 +301,14 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, CP
       const int b = vs / a.nhg, hg = vs - (vs / a.nhg) * a.nhg;
       const int64_t seq_lo = cu[vs], seq_hi = cu[vs + 1];
       const int64_t seg_end = min(g_end, seq_hi);
+      const bool whole = (gpos == seq_lo) && (seg_end == seq_hi);
+      // Thread 0 of a split segment reads the sequence's arrival count a few blocks before the
+      // segment ends (kEarlyBlocks per consumer warp of a head): if every other contributor has
+      // already arrived, this CTA is the last one and merges without the fence and the atomic.
+      // The CTA whose range begins a sequence is its usual last arriver, long after the CTAs that
+      // took the sequence's later blocks at the start of their ranges.
+      bool early_read = false;
+      uint32_t early_count = 0;
       const int ctx = a.ctx_lens[b];
       const int blk0 = window_first_block(ctx, a.window);
       const int lo_tok = a.window > 0 ? ctx - a.window : 0;
@@ -346,6 +345,10 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, CP
         // A wait that gives up has reported the timeout and raised the abort flag; the warp
         // carries on (on stale data) so that every warp still meets every barrier below.
         mbar_wait(&full[s], ph, abort_flag, a.err);
+        if (threadIdx.x == 0 && !whole && !early_read && seg_end - gg <= kEarlyBlocks * W) {
+          early_count = ld_relaxed_gpu(reinterpret_cast<const unsigned*>(a.counters + vs));
+          early_read = true;
+        }
         const int j = blk0 + static_cast<int>(gg - seq_lo);  // block index within the sequence
         // 128-byte lines of the stage image (attn_line); 16-byte chunks are XOR-swizzled with the
         // line index mod 8 (the stage is 1024-byte aligned).
@@ -520,7 +523,6 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, CP
       }
       // m-tiles this warp writes: all of them, or after a W-warp combine those with n % W == w.
       auto owns = [&](int n) { return W == 1 || n % W == w; };
-      const bool whole = (gpos == seq_lo) && (seg_end == seq_hi);
       if (whole) {
         __nv_bfloat16* op = a.out + static_cast<int64_t>(b) * a.out_stride + static_cast<int64_t>(hq0) * D;
         const float ia = va ? 1.0f / la : 0.0f, ib = vb ? 1.0f / lb : 0.0f;
@@ -539,6 +541,13 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, CP
         }
       } else {
         const int slot = (g_begin >= seq_lo) ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
+        const int c_first = cta_of(seq_lo, total, G);
+        const int nc = cta_of(seq_hi - 1, total, G) - c_first + 1;  // contributors of the sequence
+        // Thread 0 only: every other contributor had arrived when the count was read, so this
+        // CTA is the last one.  The fence turns that relaxed read into an acquire of their
+        // partials; it comes before this thread's own stores, so it has nothing to wait for.
+        const bool known_last = early_read && early_count == static_cast<uint32_t>(nc - 1);
+        if (known_last) fence_acq_rel_gpu();
         // query heads h*GROUP + ha / hb within the head group
         float* po = a.partial_o + (static_cast<int64_t>(slot) * HQ + h * GROUP) * D;
         const float ia = va ? 1.0f / la : 0.0f, ib = vb ? 1.0f / lb : 0.0f;
@@ -560,107 +569,93 @@ __global__ void __launch_bounds__((HKV * attn_wph<GROUP, HKV, D>() + 1) * 32, CP
           if (va) __stcg(pml + ha, make_float2(ma, la));
           if (vb) __stcg(pml + hb, make_float2(mb, lb));
         }
-        __threadfence();
+        // Arrival: after the barrier, thread 0's fence orders the whole CTA's partial stores before
+        // its relaxed increment (a release), and a last arriver's second fence acquires the other
+        // contributors' partials.  A known last arriver neither increments nor fences again (the
+        // merge below reads this CTA's own partial after the CTA barriers).
         consumer_bar<NCW>();
         if (threadIdx.x == 0) {
-          const int c_first = cta_of(seq_lo, total, G);
-          const int c_last = cta_of(seq_hi - 1, total, G);
-          const int old = atomicAdd(&a.counters[vs], 1);
-          const int last = old == c_last - c_first;
-          if (last) __threadfence();
+          int last = 1;
+          if (!known_last) {
+            fence_acq_rel_gpu();
+            const int old = atomicAdd(&a.counters[vs], 1);
+            last = old == nc - 1;
+            if (last) fence_acq_rel_gpu();
+          }
           *last_flag = last;
         }
         consumer_bar<NCW>();
         if (*last_flag) {
-          // Merge the sequence's partials (deterministic, contributor order): per-head max and
-          // denominator, normalised weights staged in shared memory, then every thread accumulates
-          // its GROUP*4 outputs.  Up to kMergeC contributors (the usual case) take two rounds of
-          // global loads; more are merged kMergeC at a time.
+          // Merge the sequence's nc partials in contributor order (deterministic).  Thread t owns
+          // PER consecutive dims of query head t / TPH and folds the contributors in with an online
+          // softmax (running max, denominator and weighted sum of the normalised partials), loading
+          // JB contributors' (m, l) pairs and dims at a time: one round of global loads per JB
+          // contributors, no shared memory and no barrier.
           constexpr int NT = NCW * 32;
           constexpr int PER = HQ * D / NT;
-          static_assert(PER * NT == HQ * D, "merge share must be whole");
-          float2* s_ml = reinterpret_cast<float2*>(merge_smem);  // [kMergeC][HQ]
-          float* s_w = merge_smem + 2 * kMergeC * HQ;            // [kMergeC][HQ]
-          float* s_M = s_w + kMergeC * HQ;                       // [HQ]
-          float* s_den = s_M + HQ;                               // [HQ]
-          int* s_slot = reinterpret_cast<int*>(s_den + HQ);      // [kMergeC]
-          const int c_first = cta_of(seq_lo, total, G);
-          const int nc = cta_of(seq_hi - 1, total, G) - c_first + 1;
+          constexpr int TPH = D / PER;  // threads per query head
+          static_assert(PER * NT == HQ * D && TPH * PER == D, "merge share must be whole");
+          // Contributors per round of loads, as many as the registers allow without spilling.
+          constexpr int JB = (PER >= 32 || (CPS == 2 && PER >= 16)) ? 1
+                             : (PER >= 16 ? 2 : (16 / PER > 4 ? 4 : 16 / PER));
+          const int hh = threadIdx.x / TPH;
+          const int d0 = (threadIdx.x - hh * TPH) * PER;
           auto slot_of = [&](int j) {
             const int c = c_first + j;
             return range_start(c, total, G) >= seq_lo ? 2 * c : 2 * c + 1;
           };
+          float M = -INFINITY, den = 0.0f;
           float acc[PER];
 #pragma unroll
           for (int k = 0; k < PER; ++k) acc[k] = 0.0f;
-          if (nc <= kMergeC) {
-            for (int e = threadIdx.x; e < nc * HQ; e += NT) {
-              const int j = e / HQ, hh = e - j * HQ;
-              const int sl = slot_of(j);
-              s_ml[e] = __ldcg(a.partial_ml + static_cast<int64_t>(sl) * HQ + hh);
-              if (hh == 0) s_slot[j] = sl;
-            }
-            consumer_bar<NCW>();
-            for (int hh = threadIdx.x; hh < HQ; hh += NT) {
-              float M = -INFINITY;
-              for (int j = 0; j < nc; ++j) M = fmaxf(M, s_ml[j * HQ + hh].x);
-              float den = 0.0f;
-              for (int j = 0; j < nc; ++j) den += s_ml[j * HQ + hh].y * exp2f(s_ml[j * HQ + hh].x - M);
-              s_M[hh] = M;
-              s_den[hh] = den;
-            }
-            consumer_bar<NCW>();
-            for (int e = threadIdx.x; e < nc * HQ; e += NT) {
-              const int hh = e % HQ;
-              s_w[e] = s_ml[e].y * exp2f(s_ml[e].x - s_M[hh]) / s_den[hh];
-            }
-            consumer_bar<NCW>();
-#pragma unroll 4
-            for (int j = 0; j < nc; ++j) {
-              const float* po = a.partial_o + static_cast<int64_t>(s_slot[j]) * HQ * D;
+          for (int j0 = 0; j0 < nc; j0 += JB) {
+            float2 ml[JB];
+            float ov[JB][PER];
 #pragma unroll
-              for (int k = 0; k < PER; ++k) {
-                const int i = threadIdx.x + k * NT;
-                acc[k] += s_w[j * HQ + i / D] * __ldcg(po + i);
-              }
-            }
-          } else {
-            for (int hh = threadIdx.x; hh < HQ; hh += NT) {
-              float M = -INFINITY;
-              for (int j = 0; j < nc; ++j)
-                M = fmaxf(M, __ldcg(a.partial_ml + static_cast<int64_t>(slot_of(j)) * HQ + hh).x);
-              float den = 0.0f;
-              for (int j = 0; j < nc; ++j) {
-                const float2 ml = __ldcg(a.partial_ml + static_cast<int64_t>(slot_of(j)) * HQ + hh);
-                den += ml.y * exp2f(ml.x - M);
-              }
-              s_M[hh] = M;
-              s_den[hh] = den;
-            }
-            for (int j0 = 0; j0 < nc; j0 += kMergeC) {
-              const int cn = nc - j0 < kMergeC ? nc - j0 : kMergeC;
-              consumer_bar<NCW>();
-              for (int e = threadIdx.x; e < cn * HQ; e += NT) {
-                const int j = e / HQ, hh = e - j * HQ;
-                const int sl = slot_of(j0 + j);
-                const float2 ml = __ldcg(a.partial_ml + static_cast<int64_t>(sl) * HQ + hh);
-                s_w[j * HQ + hh] = ml.y * exp2f(ml.x - s_M[hh]) / s_den[hh];
-                if (hh == 0) s_slot[j] = sl;
-              }
-              consumer_bar<NCW>();
-              for (int j = 0; j < cn; ++j) {
-                const float* po = a.partial_o + static_cast<int64_t>(s_slot[j]) * HQ * D;
+            for (int jj = 0; jj < JB; ++jj) {
+              if (j0 + jj < nc) {
+                const int64_t sl = slot_of(j0 + jj);
+                ml[jj] = __ldcg(a.partial_ml + sl * HQ + hh);
+                const float* po = a.partial_o + (sl * HQ + hh) * D + d0;
+                if constexpr (PER % 4 == 0) {
 #pragma unroll
-                for (int k = 0; k < PER; ++k) {
-                  const int i = threadIdx.x + k * NT;
-                  acc[k] += s_w[j * HQ + i / D] * __ldcg(po + i);
+                  for (int k = 0; k < PER; k += 4) {
+                    const float4 v = __ldcg(reinterpret_cast<const float4*>(po + k));
+                    ov[jj][k] = v.x;
+                    ov[jj][k + 1] = v.y;
+                    ov[jj][k + 2] = v.z;
+                    ov[jj][k + 3] = v.w;
+                  }
+                } else {
+#pragma unroll
+                  for (int k = 0; k < PER; ++k) ov[jj][k] = __ldcg(po + k);
                 }
               }
             }
-          }
-          __nv_bfloat16* og = a.out + static_cast<int64_t>(b) * a.out_stride + static_cast<int64_t>(hg) * HQ * D;
 #pragma unroll
-          for (int k = 0; k < PER; ++k) og[threadIdx.x + k * NT] = __float2bfloat16_rn(acc[k]);
+            for (int jj = 0; jj < JB; ++jj) {
+              if (j0 + jj < nc) {
+                const float Mn = fmaxf(M, ml[jj].x);
+                const float keep = exp2f(M - Mn);  // 0 for the first contributor
+                const float wj = ml[jj].y * exp2f(ml[jj].x - Mn);
+                den = den * keep + wj;
+#pragma unroll
+                for (int k = 0; k < PER; ++k) acc[k] = acc[k] * keep + wj * ov[jj][k];
+                M = Mn;
+              }
+            }
+          }
+          const float inv = 1.0f / den;
+          __nv_bfloat16* og = a.out + static_cast<int64_t>(b) * a.out_stride +
+                              static_cast<int64_t>(hg) * HQ * D + hh * D + d0;
+          if constexpr (PER % 2 == 0) {
+#pragma unroll
+            for (int k = 0; k < PER; k += 2)
+              *reinterpret_cast<__nv_bfloat162*>(og + k) = __floats2bfloat162_rn(acc[k] * inv, acc[k + 1] * inv);
+          } else {
+#pragma unroll
+            for (int k = 0; k < PER; ++k) og[k] = __float2bfloat16_rn(acc[k] * inv);
+          }
           if (threadIdx.x == 0) a.counters[vs] = 0;
         }
         consumer_bar<NCW>();
@@ -685,11 +680,10 @@ constexpr int attn_max_pairs() {
 }
 
 // Shared memory other than the stages, at the largest batch: barriers, the block prefix sums,
-// the merge scratch, the per-head combine and the 1 KB alignment slack.
+// the per-head combine and the 1 KB alignment slack.
 template <int GROUP, int HKV, int D, int CPS>
 constexpr int attn_fixed_smem() {
-  return 2 * 8 * 32 + 16 + 4 * (attn_max_pairs<D, CPS>() + 1) + 16 + 4 * attn_merge_floats<GROUP, HKV>() + 16 +
-         attn_combine_bytes<GROUP, HKV, D>() + 1024;
+  return 2 * 8 * 32 + 16 + 4 * (attn_max_pairs<D, CPS>() + 1) + 16 + attn_combine_bytes<GROUP, HKV, D>() + 1024;
 }
 
 // As many stages as fit next to the rest (at most 24) in 227 KB, or in 112 KB when two CTAs share
@@ -711,8 +705,7 @@ constexpr int attn_stages() {
 template <int GROUP, int HKV, int D, int CPS>
 size_t attn_smem(int nv) {
   return static_cast<size_t>(attn_stages<GROUP, HKV, D, CPS>()) * 2 * (D / 64) * HKV * HALF_BYTES_PER_HEAD +
-         2 * 8 * 32 + 16 + 4 * (nv + 1) + 16 + 4 * attn_merge_floats<GROUP, HKV>() + 16 +
-         attn_combine_bytes<GROUP, HKV, D>() + 1024;
+         2 * 8 * 32 + 16 + 4 * (nv + 1) + 16 + attn_combine_bytes<GROUP, HKV, D>() + 1024;
 }
 
 template <int GROUP, int HKV, int D, bool CAP, int CPS>

@@ -261,6 +261,16 @@ __device__ __forceinline__ void signal_add_relaxed_sys(uint32_t* counter) {
   asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
 }
 
+// GPU scope: a relaxed load (it orders nothing, so its latency overlaps the work after it), and
+// the fence that turns a value observed by relaxed loads into an acquire (and orders the CTA's
+// earlier stores, after a CTA barrier, before a following relaxed signal).
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const unsigned* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

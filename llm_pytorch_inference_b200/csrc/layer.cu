@@ -126,14 +126,6 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const unsigned* p) {
   return v;
 }
 
-__device__ __forceinline__ uint32_t ld_relaxed_gpu(const unsigned* p) {
-  uint32_t v;
-  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
-
 __device__ __forceinline__ void st_release_gpu(unsigned* p, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }

@@ -410,6 +410,9 @@ def _attention_ref(q, pool, layer, bts, ctx, scale, softcap=0.0, window=0):
     (4, 1, [2049] * 16),                        # TP=8 shard
     # Llama-3-8B heads, a batch of 128 with contexts drawn from 128-8192 (up to 513 blocks each)
     (32, 8, [128 + (7919 * i) % 8065 for i in range(128)]),
+    # one long sequence: every CTA of the launch is a contributor to the same merge
+    (32, 8, [40001]),
+    (4, 1, [40001]),                            # two CTAs per SM: twice as many contributors
 ])
 def test_paged_attention_matches_fp32_reference(Hq, Hkv, lens):
     D, L, layer = 128, 2, 1
