@@ -56,6 +56,62 @@ struct KeyOf<__half> {
   }
 };
 
+// Element t of a 16-byte vector of T.
+template <typename T>
+__device__ __forceinline__ T vec_elem(const uint4& w, int t);
+template <>
+__device__ __forceinline__ float vec_elem<float>(const uint4& w, int t) {
+  return __uint_as_float(t == 0 ? w.x : t == 1 ? w.y : t == 2 ? w.z : w.w);
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 vec_elem<__nv_bfloat16>(const uint4& w, int t) {
+  const uint32_t u = (t >> 1) == 0 ? w.x : (t >> 1) == 1 ? w.y : (t >> 1) == 2 ? w.z : w.w;
+  return __ushort_as_bfloat16(static_cast<unsigned short>((t & 1) ? (u >> 16) : (u & 0xFFFFu)));
+}
+template <>
+__device__ __forceinline__ __half vec_elem<__half>(const uint4& w, int t) {
+  const uint32_t u = (t >> 1) == 0 ? w.x : (t >> 1) == 1 ? w.y : (t >> 1) == 2 ? w.z : w.w;
+  return __ushort_as_half(static_cast<unsigned short>((t & 1) ? (u >> 16) : (u & 0xFFFFu)));
+}
+
+// Visits a row of n elements: as 16-byte vectors (thread t takes vectors t, t + blockDim, ...;
+// four loads in flight per thread) when the row is 16-byte aligned, then the ragged tail element
+// by element.  Each thread sees its elements in ascending index order.  Every lane of a warp
+// calls f(value, index, valid) the same number of times (the trip counts are uniform over the
+// block), so f may use warp collectives; `valid` is false on lanes past the end.
+template <typename T, typename F>
+__device__ __forceinline__ void for_each_elem(const T* x, int64_t n, F&& f) {
+  constexpr int V = 16 / static_cast<int>(sizeof(T));
+  constexpr int U = 4;
+  int64_t nv = 0;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    nv = n / V;
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    const int64_t trips = (nv + blockDim.x - 1) / blockDim.x;
+    for (int64_t r = 0; r < trips; r += U) {
+      uint4 w[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t j = (r + u) * blockDim.x + threadIdx.x;
+        w[u] = j < nv ? __ldg(xv + j) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t j = (r + u) * blockDim.x + threadIdx.x;
+#pragma unroll
+        for (int t = 0; t < V; ++t) f(vec_elem<T>(w[u], t), j * V + t, j < nv);
+      }
+    }
+  }
+  const int64_t rest = n - nv * V;
+  const int64_t trips = (rest + blockDim.x - 1) / blockDim.x;
+  for (int64_t r = 0; r < trips; ++r) {
+    const int64_t i = nv * V + r * blockDim.x + threadIdx.x;
+    const bool ok = i < n;
+    f(ok ? x[i] : x[0], i, ok);
+  }
+}
+
 // ------------------------------------------------------------------ Philox4x32-10
 __device__ __forceinline__ uint32_t philox_u32(uint64_t seed, uint32_t row, uint64_t offset) {
   uint32_t c0 = row, c1 = static_cast<uint32_t>(offset), c2 = static_cast<uint32_t>(offset >> 32),
@@ -115,21 +171,19 @@ __device__ float block_sum_f(float v, Shared& s) {
   return v;
 }
 
-// Argmax with the lowest index among equal maxima.  Threads scan contiguous chunks, so
-// a strict '>' keeps each thread's earliest maximum.
+// Argmax with the lowest index among equal maxima.  Each thread sees its elements in
+// ascending index order, so a strict '>' keeps its earliest maximum.
 template <typename T>
 __device__ int block_argmax(const T* x, int64_t n, Shared& s) {
-  const int64_t chunk = (n + blockDim.x - 1) / blockDim.x;
-  const int64_t lo = threadIdx.x * chunk, hi = min(n, lo + chunk);
   float best = -INFINITY;
   int bi = static_cast<int>(n);  // sentinel
-  for (int64_t i = lo; i < hi; ++i) {
-    const float v = to_f<T>(x[i]);
-    if (bi == n || v > best) {
+  for_each_elem(x, n, [&](T e, int64_t i, bool ok) {
+    const float v = to_f<T>(e);
+    if (ok && (bi == n || v > best)) {
       best = v;
       bi = static_cast<int>(i);
     }
-  }
+  });
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ob = __shfl_xor_sync(0xffffffffu, best, o);
@@ -179,10 +233,10 @@ __device__ uint32_t radix_kth_key(const T* x, int64_t n, int k, Shared& s) {
     __syncthreads();
     const uint32_t prefix = s.prefix;
     const uint32_t mask_hi = shift + 8 >= 32 ? 0u : (0xFFFFFFFFu << (shift + 8));
-    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-      const uint32_t key = KeyOf<T>::key(x[i]);
-      if ((key & mask_hi) == (prefix & mask_hi)) atomicAdd(&s.hist[(key >> shift) & 0xFF], 1u);
-    }
+    for_each_elem(x, n, [&](T e, int64_t, bool ok) {
+      const uint32_t key = KeyOf<T>::key(e);
+      if (ok && (key & mask_hi) == (prefix & mask_hi)) atomicAdd(&s.hist[(key >> shift) & 0xFFu], 1u);
+    });
     __syncthreads();
     if (threadIdx.x == 0) {
       int rem = s.remaining;
@@ -276,14 +330,14 @@ template <typename T>
 __device__ int gather_sorted_candidates(const T* x, int64_t n, uint32_t kth, Shared& s, unsigned* err) {
   if (threadIdx.x == 0) s.ncand = 0;
   __syncthreads();
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    const uint32_t key = KeyOf<T>::key(x[i]);
-    if (key >= kth) {
+  for_each_elem(x, n, [&](T e, int64_t i, bool ok) {
+    const uint32_t key = KeyOf<T>::key(e);
+    if (ok && key >= kth) {
       const int slot = atomicAdd(&s.ncand, 1);
       if (slot < kCandMax)
         s.cand[slot] = (static_cast<unsigned long long>(key) << 32) | (0xFFFFFFFFull - static_cast<uint32_t>(i));
     }
-  }
+  });
   __syncthreads();
   int nc = s.ncand;
   if (nc > kCandMax) {

@@ -486,6 +486,30 @@ def test_greedy_matches_torch_argmax(golden):
         assert torch.equal(ops.greedy_sample(t.to(DEV)).cpu(), golden["greedy"])
 
 
+def test_sampling_row_layouts_and_ties():
+    """The sampler reads a row as 16-byte vectors when the row is 16-byte aligned and element by
+    element otherwise, with a ragged tail when the vocabulary is not a multiple of the vector
+    width.  An odd vocabulary, column-sliced views (rows at every alignment) and maxima tied far
+    apart (the lowest index wins) give the oracle's tokens in every layout."""
+    g = torch.Generator().manual_seed(3)
+    V = 151937
+    base = torch.randn(4, V + 1, generator=g)
+    base[0, 100] = base[0, 150001] = 9.0  # tied maxima in vectors far apart
+    base[1, V - 1] = 9.0                  # the maximum in the ragged tail of the first view
+    base[2, V] = 9.0                      # the last element of the second view
+    for dt in (torch.bfloat16, torch.float32):
+        xd = base.to(dt).to(DEV)
+        for view in (xd[:, :V], xd[:, 1:]):
+            host = view.float().cpu()
+            assert torch.equal(ops.greedy_sample(view).cpu(), host.argmax(-1))
+            for (T, k, p) in ((0.8, 50, 0.95), (1.3, 5, 1.0), (0.0, 50, 0.95)):
+                tok = ops.sample(view, T, k, p, 7, 17).cpu()
+                for r in range(4):
+                    exp, margin = osamp.sample_row(host[r], T, k, p, 7, r, 17)
+                    assert int(tok[r]) == exp or margin < 1e-5, (dt, T, k, p, r, int(tok[r]), exp, margin)
+    assert N.device_status(clear=True) == 0
+
+
 def _exact_nucleus_count(row: torch.Tensor, top_p: float) -> tuple[int, torch.Tensor]:
     """Tokens kept by top-p in exact (fp64) arithmetic, and the stable (value desc, index asc) order."""
     sv, si = torch.sort(row.double(), descending=True, stable=True)
