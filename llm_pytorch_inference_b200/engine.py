@@ -83,6 +83,11 @@ class RunningBatch:
         self.last_step_seqs: list[int] = []          # the sequences the last step decoded, in row order
         self.held: set[int] = set()                  # rows that sit out the next decode (joined in it)
         self.step_count = 0
+        # Per-row mirrors for the vectorised common step (see _mirrors), valid while the running
+        # rows are exactly _mir_seqs; every general path drops them.
+        self._mir_seqs: list[int] | None = None
+        self._mir_ntok = self._mir_nblk = self._mir_left = None
+        self._mir_stop_rows: list[int] = []
 
     # ------------------------------------------------------------------ sequences
     def add_sequence(self, seq_id: int, prompt: list[int], max_tokens: int | None = None,
@@ -159,6 +164,7 @@ class RunningBatch:
 
     def _refresh_rows(self) -> None:
         """Full rewrite of the metadata rows (after sequences were added or removed)."""
+        self._mir_seqs = None
         self._bt.fill(self.kv.scratch_block)
         self._ids.fill(0)
         self._pos.fill(0)
@@ -195,6 +201,7 @@ class RunningBatch:
             self.last_step_seqs = list(self.seqs)
             self._off[0] = self.step_count
             return
+        self._mir_seqs = None
         dropped = False
         for row, s in enumerate(list(self.seqs)):
             if s in self.held:
@@ -219,30 +226,42 @@ class RunningBatch:
         # the sampling offset of this step (fresh Philox uniforms every step)
         self._off[0] = self.step_count
 
+    def _mirrors(self) -> None:
+        """Builds the per-row mirrors of the running rows unless they are current: tokens and
+        blocks held (``KVCacheManager.seq_num_tokens`` / block-table lengths), output tokens left
+        before "length", and the rows that have stop ids."""
+        if self._mir_seqs is not None and self._mir_seqs == self.seqs:
+            return
+        seqs, kv = self.seqs, self.kv
+        self._mir_ntok = np.array([kv.seq_num_tokens[q] for q in seqs], dtype=np.int64)
+        self._mir_nblk = np.array([len(kv.block_tables[q]) for q in seqs], dtype=np.int64)
+        big = 1 << 62
+        self._mir_left = np.array([big if self.max_tokens[q] is None else self.max_tokens[q] - self.output_len(q)
+                                   for q in seqs], dtype=np.int64)
+        self._mir_stop_rows = [row for row, q in enumerate(seqs) if self.stop_ids[q]]
+        self._mir_seqs = list(seqs)
+
     def _grow_fast(self) -> bool:
         """The common step (no held rows): ``KVCacheManager.append_token`` for every row in row
-        order, with its bookkeeping inlined.  Gives up (returns False, nothing changed) when some
-        row would need a block beyond the pool or the block table, where the general path frees
-        and drops sequences in the reference's order."""
-        kv, bs, mb = self.kv, self.kv.block_size, self.max_blocks
-        tables, ntok = kv.block_tables, kv.seq_num_tokens
-        need_blocks = 0
-        for s in self.seqs:
-            n = ntok[s] + 1
-            if n > len(tables[s]) * bs:
-                if len(tables[s]) + 1 > mb:
-                    return False
-                need_blocks += 1
-        if need_blocks > len(kv.free_blocks):
-            return False
-        free = kv.free_blocks
-        for row, s in enumerate(self.seqs):
-            n = ntok[s] + 1
-            bt = tables[s]
-            if n > len(bt) * bs:
+        order, vectorised over the row mirrors; only the rows that cross a block boundary take a
+        block from the free list (in row order).  Gives up (returns False, nothing changed) when
+        some row would need a block beyond the pool or the block table, where the general path
+        frees and drops sequences in the reference's order."""
+        kv = self.kv
+        self._mirrors()
+        ntok = self._mir_ntok + 1
+        grow = np.flatnonzero(ntok > self._mir_nblk * kv.block_size)
+        if grow.size:
+            if int(self._mir_nblk[grow].max()) + 1 > self.max_blocks or grow.size > len(kv.free_blocks):
+                return False
+            free, tables, seqs = kv.free_blocks, kv.block_tables, self.seqs
+            for row in grow.tolist():
+                bt = tables[seqs[row]]
                 bt.append(free.popleft())
                 self._bt[row, len(bt) - 1] = bt[-1]
-            ntok[s] = n
+            self._mir_nblk[grow] += 1
+        self._mir_ntok = ntok
+        kv.seq_num_tokens.update(zip(self.seqs, ntok.tolist()))
         return True
 
     def _commit(self, out: list[int]) -> None:
@@ -251,7 +270,9 @@ class RunningBatch:
         order and its row removed (``engine.py:352-359``)."""
         rows = list(self.seqs)
         n = len(rows)
+        fast = not self.held and self._mir_seqs is not None and self._mir_seqs == rows
         if self.held:
+            self._mir_seqs = None
             for row, s in enumerate(rows):
                 if s in self.held:
                     continue
@@ -265,7 +286,15 @@ class RunningBatch:
         self._pos[:n] += 1
         self._ctx[:n] += 1
         self.step_count += 1
-        done = [s for s in rows if s not in self.held and self.is_finished(s)]
+        if fast:
+            # Sequence.is_finished over the row mirrors: the length limit for every row, the stop
+            # ids only for the rows that have some.
+            self._mir_left -= 1
+            fin = set(np.flatnonzero(self._mir_left <= 0).tolist())
+            fin.update(row for row in self._mir_stop_rows if toks[row] in self.stop_ids[rows[row]])
+            done = [rows[row] for row in sorted(fin)]
+        else:
+            done = [s for s in rows if s not in self.held and self.is_finished(s)]
         for s in done:
             self._release(s, self._reason(s))
         if done or self.held:

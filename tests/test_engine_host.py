@@ -112,14 +112,15 @@ def test_pool_exhaustion_during_growth_drops_the_sequence():
 
 @pytest.mark.parametrize("num_blocks,seed", [(32, 0), (30, 3), (200, 1)])
 def test_step_fast_path_equals_the_general_path(num_blocks, seed):
-    """The common step's bookkeeping fast path (no held rows, every block growth fits) against
-    the general per-row path on the same steps: identical metadata, free list, block tables and
-    finish reasons, including steps where the pool runs dry and sequences are dropped."""
+    """The common step's bookkeeping fast path (no held rows, every block growth fits; the row
+    mirrors for growth and the finish rules) against the general per-row path on the same steps:
+    identical metadata, free list, block tables, outputs and finish reasons in finish order,
+    including steps where the pool runs dry and sequences are dropped."""
     runs = []
     for fast in (True, False):
         kv, rb = _batch(num_blocks, seed)
         if not fast:
-            rb._grow_fast = lambda: False
+            rb._grow_fast = lambda: False   # the general path, which also drops the row mirrors
         r2 = random.Random(seed)
         for s in range(B):
             rb.add_sequence(s, [r2.randrange(1000) for _ in range(r2.randrange(5, 60))],
@@ -133,11 +134,13 @@ def test_step_fast_path_equals_the_general_path(num_blocks, seed):
                 break
             toks = [r3.randrange(50) for _ in range(B)]
             snaps.append(rb.plan_step(toks).copy())
-        runs.append((snaps, list(kv.free_blocks), dict(kv.block_tables), dict(rb.finish_reason)))
-    (sa, fa, ta, ra), (sb, fb, tb, rb_) = runs
+        runs.append((snaps, list(kv.free_blocks), dict(kv.block_tables), list(rb.finish_reason.items()),
+                     {s: list(t) for s, t in rb.tokens.items()}))
+    (sa, fa, ta, ra, oa), (sb, fb, tb, rb_, ob) = runs
     assert len(sa) == len(sb)
     for a, b in zip(sa, sb):
         assert np.array_equal(a, b)
-    assert fa == fb and ta == tb and ra == rb_
+    assert fa == fb and ta == tb and ra == rb_ and oa == ob   # finish order too
+    ra = dict(ra)
     if num_blocks < 100:   # the tight pools run dry: some sequences are dropped while growing
         assert "abort" in ra.values(), ra
