@@ -11,8 +11,10 @@ Reported (one JSON line from rank 0):
   value     tokens/s of the whole job: K graph replays of the full step (forward + sampling),
             the per-step metadata already resident in HBM, CUDA events on the launching stream,
             max over ranks.  Weights (15.1 GB) + KV (~20 GB) per step >> L2 (126 MB).
-  e2e       the same through DecodeEngine.step(): per step one host->device copy of the
-            step's metadata from pinned memory and one device->host read of the 64 sampled tokens.
+  e2e       the same through DecodeEngine.run_steps(K): per step one host->device copy of the
+            step's metadata from pinned memory and one device->host read of the 64 sampled tokens
+            (with no sequence able to finish, each step is launched before the previous step's
+            tokens are read back, and the host's bookkeeping overlaps the GPU).
   roofline  the kernel with the largest share of the step, its algorithmic bytes / average
             launch duration (CUDA events, launching stream) against the measured HBM peak.
   cpu_baseline  the oracle (the reference's PyTorch decode path restated on the CPU) on this
@@ -428,12 +430,11 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
     dev_ms = max_over_ranks(e0.elapsed_time(e1), world)
     barrier(world)
 
-    # ---- e2e: K steps through DecodeEngine.step() (H2D metadata, replay, D2H tokens)
+    # ---- e2e: K steps through DecodeEngine.run_steps() (per step: H2D metadata, replay, D2H tokens)
     torch.cuda.synchronize(dev)
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
-    for _ in range(K):
-        eng.step()
+    eng.run_steps(K)
     e3.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(e2.elapsed_time(e3), world)
@@ -586,8 +587,7 @@ def run_moe_case(args) -> None:
     barrier(world)
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
-    for _ in range(K):
-        eng.step()
+    eng.run_steps(K)
     e3.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(e2.elapsed_time(e3) / K, world)
@@ -632,7 +632,7 @@ def run_llama3_case(args) -> None:
     """Llama-3-8B-architecture decode (32 layers, hidden 4096, 32/8 heads, SwiGLU 14336, vocab 128256,
     theta 5e5, no QK-norm), a mixed batch of 128 sequences whose contexts are drawn uniformly from
     128-8192 (seeded), K/V filled with seeded synthetic values in a shuffled pool, greedy.  Same
-    timing rules as the headline line; the e2e figure goes through ``DecodeEngine.step()``."""
+    timing rules as the headline line; the e2e figure goes through ``DecodeEngine.run_steps()``."""
     from llm_pytorch_inference_b200 import _native as N
     from llm_pytorch_inference_b200.configs import get_config
     from llm_pytorch_inference_b200.engine import DecodeEngine
@@ -678,8 +678,7 @@ def run_llama3_case(args) -> None:
     ms = e0.elapsed_time(e1) / K
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
-    for _ in range(K):
-        eng.step()
+    eng.run_steps(K)
     e3.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = e2.elapsed_time(e3) / K
@@ -776,8 +775,7 @@ def _gemma2_case(args, rank: int, world: int, local: int) -> None:
     torch.cuda.synchronize(dev)
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
-    for _ in range(K):
-        eng.step()
+    eng.run_steps(K)
     e3.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(e2.elapsed_time(e3), world) / K

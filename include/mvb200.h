@@ -329,6 +329,14 @@ int mvb_decoder_layer_tail(const void* attn, int64_t attn_stride, const void* wo
  * dtype MVB_BF16 or MVB_F32; cap > 0. */
 int mvb_softcap(void* x, int64_t n, float cap, int dtype, mvb_stream_t stream);
 
+/* Input ids of a decode step from the previous step's sampled tokens: ids[i] = tokens[i] for
+ * i < n when *feed != 0, nothing otherwise.  ids: int32 [n] (the step metadata's id words),
+ * tokens: int64 [n] (the sampler's output), feed: one int32 of the same metadata, read on the
+ * device, so a captured step can take either its uploaded ids or the tokens the previous step
+ * sampled.  Replaces the host round trip of engine.py:315-317 (the next step's input_ids built
+ * from the tokens the last step appended) when the caller runs a step ahead of reading them. */
+int mvb_feed_ids(int32_t* ids, const int64_t* tokens, const int32_t* feed, int64_t n, mvb_stream_t stream);
+
 /* ---- sparse mixture of experts (Qwen3-MoE) ---------------------------------------------
  * Replace Qwen3MoeSparseMoe.forward (models/qwen3_moe_model.py:39-65) for one decode step.
  *

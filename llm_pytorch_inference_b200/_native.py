@@ -63,6 +63,7 @@ SIGNATURES: dict[str, tuple] = {
     "mvb_swiglu_gemm": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _vp]),
     "mvb_gated_gemm": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _i32, _vp]),
     "mvb_softcap": (_i32, [_vp, _i64, _f32, _i32, _vp]),
+    "mvb_feed_ids": (_i32, [_vp, _vp, _vp, _i64, _vp]),
     "mvb_decoder_layer_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64, _i64, _i32]),
     "mvb_decoder_layer_tail": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                       _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,

@@ -106,6 +106,17 @@ __global__ void softcap_kernel(T* __restrict__ x, int64_t n, float cap) {
   }
 }
 
+// Input ids of a step from the previous step's sampled tokens when *feed is nonzero (the engine
+// launched the step before reading those tokens back); otherwise the ids stay as uploaded.
+__global__ void feed_ids_kernel(int32_t* __restrict__ ids, const int64_t* __restrict__ tokens,
+                                const int32_t* __restrict__ feed, int64_t n) {
+  pdl_launch_dependents();
+  pdl_wait();
+  if (*feed == 0) return;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    ids[i] = static_cast<int32_t>(tokens[i]);
+}
+
 template <typename T, typename I>
 __global__ void embedding_kernel(T* __restrict__ out, const I* __restrict__ ids, const T* __restrict__ w,
                                  int64_t hidden, int64_t vocab, float scale, unsigned* err) {
@@ -282,6 +293,14 @@ extern "C" int mvb_softcap(void* x, int64_t n, float cap, int dtype, mvb_stream_
     default:
       return fail(MVB_ERR_INVALID_ARG, "mvb_softcap: unsupported dtype %d", dtype);
   }
+}
+
+extern "C" int mvb_feed_ids(int32_t* ids, const int64_t* tokens, const int32_t* feed, int64_t n, mvb_stream_t stream) {
+  MVB_REQUIRE(ids && tokens && feed && n >= 0 && n <= (1LL << 20), "mvb_feed_ids: bad arguments");
+  if (n == 0) return MVB_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return launch("feed_ids", feed_ids_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, st, ids,
+                tokens, feed, n);
 }
 
 extern "C" int mvb_gated_gemm(void* out, int64_t out_stride, const void* gemm_workspace, int64_t rows, int64_t inter,

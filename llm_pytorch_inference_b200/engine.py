@@ -393,6 +393,7 @@ class DecodeEngine(RunningBatch):
         self.last_prefill_logits = None
         self.parity = False
         self.parity_generator: torch.Generator | None = None
+        self.steps_run_ahead = 0   # steps run_steps launched before reading the previous step's tokens
 
     def prefill(self, prompts: dict[int, list[int]], temperature: float = 0.0, top_k: int = -1, top_p: float = 1.0,
                 seed: int = 0, max_tokens: int = 16384, gen_max_tokens: dict[int, int | None] | None = None,
@@ -504,6 +505,75 @@ class DecodeEngine(RunningBatch):
         order); the sequences that finished are in ``finished_last``."""
         self.finished_last = []
         return self._decode(use_graph)
+
+    def run_steps(self, n: int) -> list[list[int]]:
+        """``n`` decode steps, each exactly as ``step()`` would take it (same tokens, block
+        tables, free list and finishes); returns each step's tokens.  While step k runs, the host
+        already launches step k+1 when no running sequence can finish at step k (no length limit
+        reached, no stop ids), no row joins and the growth of step k+1 fits: step k+1 then takes
+        its input ids from step k's sampled tokens on the device (``mvb_feed_ids``), and the
+        token read-back and the bookkeeping of step k overlap step k+1 instead of leaving the GPU
+        idle.  Otherwise step k's tokens are read and committed first, as ``step()`` does.
+        ``finished_last`` lists the sequences that finished in any of the ``n`` steps."""
+        finished = []
+        out: list[list[int]] = []
+        pending = None   # (rows, decoded rows, token buffer) of the step on the device
+        for k in range(n):
+            self.finished_last = []
+            if pending is None:
+                if self.parity:   # the reference's host-side draw needs each step's probabilities
+                    out.append(self._decode(True))
+                    finished += self.finished_last
+                    continue
+                self._grow_blocks()
+                rows = list(self.seqs)
+                decoded = set(self.last_step_seqs)
+                if not decoded:
+                    if rows:
+                        self.held = set()
+                        self._refresh_rows()
+                    out.append([])
+                    continue
+                pending = (rows, decoded, self.runner.launch_staged(feed=False))
+            rows, decoded, buf = pending
+            pending = None
+            if k + 1 < n and self._can_run_ahead():
+                # Step k's position advance and step k+1's growth, without step k's tokens.
+                m = len(rows)
+                self._pos[:m] += 1
+                self._ctx[:m] += 1
+                self.step_count += 1
+                self._mir_left -= 1
+                self._grow_blocks()
+                pending = (list(self.seqs), set(self.last_step_seqs), self.runner.launch_staged(feed=True))
+                self.steps_run_ahead += 1
+                toks = self.runner.tokens_of(buf)[:m].tolist()
+                for s, t in zip(rows, toks):
+                    self.tokens[s].append(t)
+                self._ids[:m] = toks
+            else:
+                toks = self.runner.tokens_of(buf)[:len(rows)].tolist()
+                self._commit(toks)
+            out.append([toks[i] for i, s in enumerate(rows) if s in decoded])
+            finished += self.finished_last
+        self.finished_last = finished
+        return out
+
+    def _can_run_ahead(self) -> bool:
+        """Whether the next step can be launched before this step's tokens are read: the rows are
+        the ones of the row mirrors, none joins, none can finish with this step's token (no
+        length limit reached, no stop ids) and the next step's block growth takes the fast path."""
+        if self.held or self.parity or not self.seqs or self._mir_seqs is None or self._mir_seqs != self.seqs:
+            return False
+        if self.runner.graph is None:   # a capture replays the step eagerly first: never with fed ids
+            return False
+        if self._mir_stop_rows or int(self._mir_left.min()) <= 1:
+            return False
+        ntok = self._mir_ntok + 1
+        grow = np.flatnonzero(ntok > self._mir_nblk * self.kv.block_size)
+        if grow.size and (int(self._mir_nblk[grow].max()) + 1 > self.max_blocks or grow.size > len(self.kv.free_blocks)):
+            return False
+        return True
 
     def schedule_step(self, new_prompts: dict[int, list[int]] | None = None, use_graph: bool = True,
                       gen_max_tokens: dict[int, int | None] | None = None, stop_token_ids=()) -> dict[int, int]:

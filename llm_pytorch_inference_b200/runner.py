@@ -62,15 +62,17 @@ def rope_tables(head_dim_: int, theta: float, length: int, dtype: torch.dtype, d
 def meta_layout(batch: int, max_blocks: int) -> dict[str, int]:
     """Offsets (in int32 words) of the per-step metadata buffer, one upload per step:
     token ids | positions | context lengths | sampling offset (int64, 8-byte aligned) |
-    temperature (fp32) | top-k (int32) | top-p (fp32) | block tables ``[batch, max_blocks]``."""
+    temperature (fp32) | top-k (int32) | top-p (fp32) | feed (int32: nonzero = take the ids from
+    the previous step's sampled tokens on the device) | block tables ``[batch, max_blocks]``."""
     B = batch
     o_off = (3 * B + 1) // 2 * 2
     o_temp = o_off + 2
     o_topk = o_temp + B
     o_topp = o_topk + B
-    o_bt = o_topp + B
+    o_feed = o_topp + B
+    o_bt = o_feed + 1
     return {"ids": 0, "pos": B, "ctx": 2 * B, "off": o_off, "temp": o_temp, "topk": o_topk, "topp": o_topp,
-            "bt": o_bt, "total": o_bt + B * max_blocks}
+            "feed": o_feed, "bt": o_bt, "total": o_bt + B * max_blocks}
 
 
 class DecodeWeights:
@@ -251,7 +253,15 @@ class DecodeRunner:
         self.top_k = self.meta[lay["topk"]:lay["topk"] + B]
         self.top_p = self.meta[lay["topp"]:lay["topp"] + B].view(torch.float32)
         self.block_tables = self.meta[self._o_bt:].view(B, self.max_blocks)
+        self.feed = self.meta[lay["feed"]:lay["feed"] + 1]
         self.tokens_host = torch.zeros(B, dtype=torch.int64, pin_memory=True)
+        # Staged uploads and token read-backs of steps run ahead (``DecodeEngine.run_steps``): two
+        # pinned copies of the metadata and of the tokens, used by alternate steps, so the host
+        # never rewrites a buffer a queued copy may still read.
+        self._meta_stage = [torch.zeros(lay["total"], dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self._tok_stage = [torch.zeros(B, dtype=torch.int64, pin_memory=True) for _ in range(2)]
+        self._stage_i = 0
+        self._tok_event: list[torch.cuda.Event | None] = [None, None]
         self._host_sampling(0.0, -1, 1.0)
         self.upload_metadata()
 
@@ -303,6 +313,28 @@ class DecodeRunner:
 
     def upload_metadata(self) -> None:
         self.meta.copy_(self.meta_host, non_blocking=True)
+
+    def launch_staged(self, feed: bool) -> int:
+        """Copies the host metadata into the next staging buffer (``feed`` set or not), uploads
+        it and replays the step, then queues the read-back of the step's tokens into the matching
+        token buffer.  Returns the buffer index for ``tokens_of``.  Nothing waits on the host."""
+        i = self._stage_i
+        self._stage_i ^= 1
+        m = self._meta_stage[i]
+        m.copy_(self.meta_host)
+        m[self.meta_offsets["feed"]] = 1 if feed else 0
+        self.meta.copy_(m, non_blocking=True)
+        self.replay()
+        self._tok_stage[i].copy_(self.tokens, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.dev))
+        self._tok_event[i] = ev
+        return i
+
+    def tokens_of(self, i: int) -> torch.Tensor:
+        """The tokens of the step launched by ``launch_staged`` into buffer ``i`` (waits for them)."""
+        self._tok_event[i].synchronize()
+        return self._tok_stage[i]
 
     def _host_sampling(self, temperature, top_k, top_p) -> None:
         lay, B, m = self.meta_offsets, self.B, self.meta_host
@@ -425,6 +457,9 @@ class DecodeRunner:
 
     def forward(self) -> None:
         """Launches one decode step on the current stream (metadata must be on the device)."""
+        self._st = N.stream_handle(self.dev)
+        N.check(N.lib().mvb_feed_ids(self.ids.data_ptr(), self.tokens.data_ptr(), self.feed.data_ptr(), self.B,
+                                     self._st), "feed_ids")
         if self.tp.enabled:
             self._forward_tp()
             return
@@ -749,9 +784,12 @@ class DecodeRunner:
         return self.w.streamed_bytes() + attended * per_layer + self.B * self.L * per_layer
 
     def launches_per_step(self) -> int:
-        """Kernels one step launches: embedding, rmsnorm, 8 per layer (qkv, qk-norm/rope/kv, attention,
-        o_proj, add+norm, gate_up, swiglu, down), an add+norm between layers, final add+norm, lm_head,
-        sample."""
+        """Kernels one step launches: the id feed, embedding, rmsnorm, 8 per layer (qkv,
+        qk-norm/rope/kv, attention, o_proj, add+norm, gate_up, swiglu, down), an add+norm between
+        layers, final add+norm, lm_head, sample."""
+        return 1 + self._launches_after_feed()
+
+    def _launches_after_feed(self) -> int:
         if self.moe:   # 11 per layer: qkv, qk, attention, o_proj, add+norm, router, route, gather, 2 GEMMs, combine
             # (tensor parallel: + a wait before each router, the step-counter kernel, the wait before sampling)
             return 2 + self.L * 11 + (self.L - 1) + 3 + (self.L + 2 if self.tp.enabled else 0)
