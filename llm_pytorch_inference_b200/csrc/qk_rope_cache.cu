@@ -29,13 +29,19 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int heads = nq + 2 * nkv;
-  pdl_wait();
   if (warp_global >= batch * heads) return;
   const int b = warp_global / heads;
   const int h = warp_global - b * heads;
-  qk_norm_rope_kv_one<D>(b, h, lane, q_out, kv, qkv, qkv_stride, qnw, knw, cos_t, sin_t, table_len, positions,
-                         block_tables, max_blocks, nq, nkv, layer, num_blocks, bs, eps, plus_one, err, partials,
-                         plan);
+  // Programmatic dependent launch: the position, block table, norm weights and cos/sin are step
+  // metadata or constant tables, loaded while the GEMM before this kernel still runs; only the
+  // projection itself waits for it.
+  QkMeta<D> m;
+  qk_meta_load<D>(m, b, h, lane, qnw, knw, cos_t, sin_t, table_len, positions, block_tables, max_blocks, nq, nkv,
+                  layer, num_blocks, bs, err);
+  pdl_wait();
+  float x[D / 32];
+  qk_load_x<D>(b, h, lane, x, qkv, qkv_stride, partials, plan);
+  qk_apply<D>(m, b, h, lane, x, q_out, kv, nq, nkv, eps, plus_one);
 }
 
 }  // namespace
