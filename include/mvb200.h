@@ -480,10 +480,10 @@ int mvb_tp_wait(mvb_tp_comm* comm, int point, mvb_stream_t stream);
  * attribute so that, inside a stream or CUDA graph, a kernel's prologue overlaps the
  * tail of the previous one.  A kernel then reads its step metadata (positions, context
  * lengths, block tables) and constant tables (weights, cos/sin) before it waits for the
- * previous kernel, so with PDL enabled those inputs must not be written by the kernel of
- * this library launched just before it (host copies and other libraries' kernels are
- * fine: the wait is only relaxed against this library's own kernels).  Returns the
- * previous setting. */
+ * previous kernel.  With PDL enabled, those inputs must therefore not be written by the
+ * kernel launched just before it in the stream when that kernel lets its dependents start
+ * early, as every kernel of this library does.  Host copies, and kernels that let
+ * dependents start only at their end, are fine.  Returns the previous setting. */
 int mvb_set_pdl(int enable);
 
 #ifdef __cplusplus
