@@ -509,8 +509,9 @@ class DecodeEngine(RunningBatch):
     def run_steps(self, n: int) -> list[list[int]]:
         """``n`` decode steps, each exactly as ``step()`` would take it (same tokens, block
         tables, free list and finishes); returns each step's tokens.  While step k runs, the host
-        already launches step k+1 when no running sequence can finish at step k (no length limit
-        reached, no stop ids), no row joins and the growth of step k+1 fits: step k+1 then takes
+        already launches step k+1 when every row of the batch is a running sequence, none can
+        finish at step k (no length limit reached, no stop ids), no row joins and the growth of
+        step k+1 fits: step k+1 then takes
         its input ids from step k's sampled tokens on the device (``mvb_feed_ids``), and the
         token read-back and the bookkeeping of step k overlap step k+1 instead of leaving the GPU
         idle.  Otherwise step k's tokens are read and committed first, as ``step()`` does.
@@ -560,10 +561,14 @@ class DecodeEngine(RunningBatch):
         return out
 
     def _can_run_ahead(self) -> bool:
-        """Whether the next step can be launched before this step's tokens are read: the rows are
-        the ones of the row mirrors, none joins, none can finish with this step's token (no
-        length limit reached, no stop ids) and the next step's block growth takes the fast path."""
-        if self.held or self.parity or not self.seqs or self._mir_seqs is None or self._mir_seqs != self.seqs:
+        """Whether the next step can be launched before this step's tokens are read: every row
+        of the batch is a running sequence (the id feed copies all rows, and a padding row must
+        keep its id 0: in a sparse-MoE step its routing would otherwise change how the experts'
+        rows are split), the rows are the ones of the row mirrors, none joins, none can finish
+        with this step's token (no length limit reached, no stop ids) and the next step's block
+        growth takes the fast path."""
+        if self.held or self.parity or len(self.seqs) != self.B or self._mir_seqs is None \
+                or self._mir_seqs != self.seqs:
             return False
         if self.runner.graph is None:   # a capture replays the step eagerly first: never with fed ids
             return False

@@ -2,8 +2,9 @@
 the same tokens, outputs, block tables, free list and finishes in finish order.  Three regimes:
 every step after the first launched ahead of the previous step's token read-back (no limits,
 greedy); rows that reach their length limits mid-run, sampled at T 0.8 / top-k 50 / top-p 0.95
-(a step where a row can finish is read back before the next launch, and the rows compact); and
-stop ids (a row could stop at any step, so no step runs ahead)."""
+(a step where a row can finish is read back before the next launch; once rows have finished the
+batch has padding rows and is no longer run ahead); and stop ids (a row could stop at any step,
+so no step runs ahead)."""
 import random
 
 import pytest
